@@ -1,0 +1,49 @@
+// Python bindings of the verl_omni_b200 sm_100a kernels (module verl_omni_b200._C).
+#include <torch/extension.h>
+
+#include <vector>
+
+namespace vo {
+std::vector<torch::Tensor> sde_step_fwd(torch::Tensor x, torch::Tensor v, torch::Tensor sigma, torch::Tensor sigma_prev,
+                                        c10::optional<torch::Tensor> prev, c10::optional<torch::Tensor> noise,
+                                        double sigma_max, double eta, int64_t type, int64_t seed, int64_t offset,
+                                        bool want_logp, bool norm);
+torch::Tensor sde_step_bwd(torch::Tensor x, torch::Tensor prev, torch::Tensor mean, torch::Tensor sigma,
+                           torch::Tensor sigma_prev, torch::Tensor g_logp, torch::Tensor g_mean, double sigma_max,
+                           double eta, int64_t type);
+std::vector<torch::Tensor> ppo_clip_fwd(torch::Tensor logp, torch::Tensor old, torch::Tensor adv,
+                                        c10::optional<torch::Tensor> w, double clip);
+torch::Tensor ppo_clip_bwd(torch::Tensor logp, torch::Tensor old, torch::Tensor adv, c10::optional<torch::Tensor> w,
+                           double clip, torch::Tensor g_loss);
+std::vector<torch::Tensor> adaln_ln_fwd(torch::Tensor x, c10::optional<torch::Tensor> mod, int64_t shift_off,
+                                        int64_t scale_off, c10::optional<torch::Tensor> w,
+                                        c10::optional<torch::Tensor> bias, int64_t S, double eps);
+std::vector<torch::Tensor> adaln_ln_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor mean, torch::Tensor rstd,
+                                        torch::Tensor mod, int64_t shift_off, int64_t scale_off, int64_t S);
+std::vector<torch::Tensor> qk_rmsnorm_fwd(torch::Tensor qkv, torch::Tensor wq, torch::Tensor wk, torch::Tensor q,
+                                          torch::Tensor k, torch::Tensor v, int64_t S_seg, int64_t seg_off,
+                                          c10::optional<torch::Tensor> rope_cos, c10::optional<torch::Tensor> rope_sin,
+                                          double eps, std::vector<int64_t> part_off);
+std::vector<torch::Tensor> qk_rmsnorm_bwd(torch::Tensor qkv, torch::Tensor wq, torch::Tensor wk, torch::Tensor dq,
+                                          torch::Tensor dk, torch::Tensor dv, torch::Tensor rq, torch::Tensor rk,
+                                          int64_t S_seg, int64_t seg_off, c10::optional<torch::Tensor> rope_cos,
+                                          c10::optional<torch::Tensor> rope_sin, std::vector<int64_t> part_off);
+torch::Tensor sq_norm(torch::Tensor g);
+void adamw_flat(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, c10::optional<torch::Tensor> p16,
+                double lr, double b1, double b2, double eps, double wd, int64_t step, double max_norm,
+                c10::optional<torch::Tensor> sq_norm_t, double grad_scale);
+}  // namespace vo
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "verl_omni_b200 sm_100a kernels";
+  m.def("sde_step_fwd", &vo::sde_step_fwd);
+  m.def("sde_step_bwd", &vo::sde_step_bwd);
+  m.def("ppo_clip_fwd", &vo::ppo_clip_fwd);
+  m.def("ppo_clip_bwd", &vo::ppo_clip_bwd);
+  m.def("adaln_ln_fwd", &vo::adaln_ln_fwd);
+  m.def("adaln_ln_bwd", &vo::adaln_ln_bwd);
+  m.def("qk_rmsnorm_fwd", &vo::qk_rmsnorm_fwd);
+  m.def("qk_rmsnorm_bwd", &vo::qk_rmsnorm_bwd);
+  m.def("sq_norm", &vo::sq_norm);
+  m.def("adamw_flat", &vo::adamw_flat);
+}

@@ -1,0 +1,265 @@
+// Fused flow-matching reverse-SDE step with per-sample log-probability.
+//
+// One pass over the latents computes, per element,
+//   mean = ca[b]*x + cb[b]*v          (x = sample, v = model output; the three SDE variants
+//                                      sde / cps / dance_sde are all affine in (x, v))
+//   prev = mean + scale[b]*z          (z ~ N(0,1) from Philox4x32-10 keyed by seed, unless
+//                                      prev or an explicit noise tensor is given)
+//   d2  += (prev - mean)^2            (block partial sums, reduced in fixed order)
+// and a second tiny kernel turns the per-row sums into the mean log-prob with the Gaussian
+// normaliser.  The backward is elementwise: dL/dv = cb*(g_mean + g_logp*dlogp/dmean).
+// Math restates verl_omni/pipelines/schedulers/flow_match_sde.py:214-313.
+#include "common.cuh"
+
+namespace vo {
+namespace {
+
+struct RowCoef {
+  float ca, cb, scale, std, lp_coef, lp_const;  // logp = lp_coef*sum(d2)/N + lp_const
+};
+
+__device__ RowCoef row_coef(float sigma_f, float sigma_prev_f, float sigma_max, float eta, int type, bool norm) {
+  // Per-row scalars in double, rounded once.
+  double s = sigma_f, sp = sigma_prev_f, dt = sp - s;
+  RowCoef c;
+  if (type == 0) {  // FlowGRPO "sde"
+    double den = 1.0 - (s == 1.0 ? (double)sigma_max : s);
+    double std = sqrt(s / den) * eta;
+    double ca = 1.0 + std * std / (2.0 * s) * dt;
+    double cb = (1.0 + std * std * (1.0 - s) / (2.0 * s)) * dt;
+    double scale = std * sqrt(-dt);
+    c.ca = (float)ca;
+    c.cb = (float)cb;
+    c.scale = (float)scale;
+    c.std = (float)std;
+    c.lp_coef = (float)(-1.0 / (2.0 * scale * scale));
+    c.lp_const = norm ? (float)(-log(scale) - 0.5 * log(2.0 * M_PI)) : 0.f;
+  } else if (type == 1) {  // "cps"
+    double std = sp * sin(eta * M_PI / 2.0);
+    double sq = sqrt(fmax(sp * sp - std * std, 0.0));
+    c.ca = (float)((1.0 - sp) + sq);
+    c.cb = (float)(-s * (1.0 - sp) + (1.0 - s) * sq);
+    c.scale = (float)std;
+    c.std = (float)std;
+    c.lp_coef = -1.f;
+    c.lp_const = 0.f;
+  } else {  // "dance_sde"
+    double half = 0.5 * eta * eta;
+    double std = eta * sqrt(s - sp);
+    c.ca = (float)(1.0 + half * dt / s);
+    c.cb = (float)(dt + half * (1.0 - s) * dt / s);
+    c.scale = (float)std;
+    c.std = (float)std;
+    c.lp_coef = (float)(-1.0 / (2.0 * std * std));
+    c.lp_const = norm ? (float)(-log(std) - 0.5 * log(2.0 * M_PI)) : 0.f;
+  }
+  return c;
+}
+
+// Philox4x32-10 (Salmon, Moraes, Dror, Shaw: "Parallel random numbers: as easy as 1, 2, 3", SC'11).
+__device__ __forceinline__ uint4 philox(uint4 c, uint2 k) {
+  const uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u, W0 = 0x9E3779B9u, W1 = 0xBB67AE85u;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    if (r) {
+      k.x += W0;
+      k.y += W1;
+    }
+    uint32_t hi0 = __umulhi(M0, c.x), lo0 = M0 * c.x;
+    uint32_t hi1 = __umulhi(M1, c.z), lo1 = M1 * c.z;
+    c = make_uint4(hi1 ^ c.y ^ k.x, lo1, hi0 ^ c.w ^ k.y, lo0);
+  }
+  return c;
+}
+
+__device__ __forceinline__ float2 box_muller(uint32_t a, uint32_t b) {
+  const double inv = 2.3283064365386963e-10;  // 2^-32
+  float u1 = (float)(((double)a + 1.0) * inv);
+  float u2 = (float)((double)b * inv);
+  float r = sqrtf(-2.f * logf(u1));
+  float ang = 6.2831855f * u2;
+  return make_float2(r * cosf(ang), r * sinf(ang));
+}
+
+template <bool kHasPrev, bool kHasNoise>
+__global__ void sde_fwd_kernel(const float* __restrict__ x, const float* __restrict__ v,
+                               const float* __restrict__ sigma, const float* __restrict__ sigma_prev,
+                               const float* __restrict__ prev_in, const float* __restrict__ noise,
+                               float* __restrict__ prev_out, float* __restrict__ mean_out,
+                               float* __restrict__ partial, int64_t n, int64_t chunk, int nchunks,
+                               float sigma_max, float eta, int type, bool norm, uint64_t seed, uint32_t offset) {
+  __shared__ float red[32];
+  const int b = blockIdx.y;
+  const RowCoef c = row_coef(sigma[b], sigma_prev[b], sigma_max, eta, type, norm);
+  const int64_t base = (int64_t)b * n;
+  const int64_t lo = (int64_t)blockIdx.x * chunk;
+  const int64_t hi = min(lo + chunk, n);
+  const uint2 key = make_uint2((uint32_t)seed, (uint32_t)(seed >> 32));
+  float acc = 0.f;
+  for (int64_t i = lo + 4 * (int64_t)threadIdx.x; i < hi; i += 4 * (int64_t)blockDim.x) {
+    float xs[4], vs[4], ps[4], ms[4];
+    const bool full = (i + 4 <= hi) && (((base + i) & 3) == 0);
+    if (full) {
+      float4 a = *reinterpret_cast<const float4*>(x + base + i);
+      float4 bb = *reinterpret_cast<const float4*>(v + base + i);
+      xs[0] = a.x; xs[1] = a.y; xs[2] = a.z; xs[3] = a.w;
+      vs[0] = bb.x; vs[1] = bb.y; vs[2] = bb.z; vs[3] = bb.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        xs[j] = (i + j < hi) ? x[base + i + j] : 0.f;
+        vs[j] = (i + j < hi) ? v[base + i + j] : 0.f;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ms[j] = xs[j] * c.ca + vs[j] * c.cb;
+    if (kHasPrev) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ps[j] = (i + j < hi) ? prev_in[base + i + j] : ms[j];
+    } else if (kHasNoise) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ps[j] = (i + j < hi) ? ms[j] + c.scale * noise[base + i + j] : ms[j];
+    } else {
+      uint4 r = philox(make_uint4((uint32_t)(i >> 2), (uint32_t)b, offset, 0u), key);
+      float2 z01 = box_muller(r.x, r.y), z23 = box_muller(r.z, r.w);
+      ps[0] = ms[0] + c.scale * z01.x;
+      ps[1] = ms[1] + c.scale * z01.y;
+      ps[2] = ms[2] + c.scale * z23.x;
+      ps[3] = ms[3] + c.scale * z23.y;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (i + j < hi) {
+        float d = ps[j] - ms[j];
+        acc += d * d;
+      }
+    }
+    if (full) {
+      *reinterpret_cast<float4*>(mean_out + base + i) = make_float4(ms[0], ms[1], ms[2], ms[3]);
+      if (!kHasPrev) *reinterpret_cast<float4*>(prev_out + base + i) = make_float4(ps[0], ps[1], ps[2], ps[3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (i + j < hi) {
+          mean_out[base + i + j] = ms[j];
+          if (!kHasPrev) prev_out[base + i + j] = ps[j];
+        }
+      }
+    }
+  }
+  acc = block_sum(acc, red);
+  if (threadIdx.x == 0) partial[(int64_t)b * nchunks + blockIdx.x] = acc;
+}
+
+// One warp per row: fixed-order reduction of the chunk partials, then the log-prob.
+__global__ void sde_finalize_kernel(const float* __restrict__ partial, const float* __restrict__ sigma,
+                                    const float* __restrict__ sigma_prev, float* __restrict__ logp,
+                                    float* __restrict__ std_out, int B, int nchunks, int64_t n, float sigma_max,
+                                    float eta, int type, bool norm) {
+  const int b = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (b >= B) return;
+  float s = 0.f;
+  for (int i = lane; i < nchunks; i += 32) s += partial[(int64_t)b * nchunks + i];
+  s = warp_sum(s);
+  if (lane == 0) {
+    RowCoef c = row_coef(sigma[b], sigma_prev[b], sigma_max, eta, type, norm);
+    if (logp) logp[b] = c.lp_coef * (s / (float)n) + c.lp_const;
+    std_out[b] = c.std;
+  }
+}
+
+__global__ void sde_bwd_kernel(const float* __restrict__ prev, const float* __restrict__ mean,
+                               const float* __restrict__ sigma, const float* __restrict__ sigma_prev,
+                               const float* __restrict__ g_logp, const float* __restrict__ g_mean,
+                               float* __restrict__ g_v, int64_t n, float sigma_max, float eta, int type) {
+  const int b = blockIdx.y;
+  const RowCoef c = row_coef(sigma[b], sigma_prev[b], sigma_max, eta, type, true);
+  // d logp / d mean_i = -2*lp_coef*(prev_i - mean_i)/N   (lp_coef = -1/(2 var) or -1 for cps)
+  const float k = g_logp[b] * (-2.f * c.lp_coef) / (float)n;
+  const int64_t base = (int64_t)b * n;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float d = prev[base + i] - mean[base + i];
+    g_v[base + i] = c.cb * (g_mean[base + i] + k * d);
+  }
+}
+
+}  // namespace
+
+std::vector<torch::Tensor> sde_step_fwd(torch::Tensor x, torch::Tensor v, torch::Tensor sigma,
+                                        torch::Tensor sigma_prev, c10::optional<torch::Tensor> prev,
+                                        c10::optional<torch::Tensor> noise, double sigma_max, double eta, int64_t type,
+                                        int64_t seed, int64_t offset, bool want_logp, bool norm) {
+  VO_CHECK_INPUT(x);
+  VO_CHECK_INPUT(v);
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 && v.scalar_type() == torch::kFloat32, "fp32 inputs required");
+  TORCH_CHECK(x.sizes() == v.sizes(), "sample/model_output shape mismatch");
+  c10::cuda::CUDAGuard g(x.device());
+  const int B = x.size(0);
+  const int64_t n = x.numel() / B;
+  auto mean = torch::empty_like(x);
+  torch::Tensor prev_out;
+  const bool has_prev = prev.has_value() && prev->defined();
+  const bool has_noise = !has_prev && noise.has_value() && noise->defined();
+  if (has_prev) {
+    VO_CHECK_INPUT((*prev));
+    prev_out = *prev;
+  } else {
+    prev_out = torch::empty_like(x);
+  }
+  if (has_noise) VO_CHECK_INPUT((*noise));
+  // ~4 blocks per SM across the batch, chunks in multiples of 1024 elements
+  int target = 4 * num_sms();
+  int nchunks = std::max(1, std::min<int>((int)((n + 1023) / 1024), (target + B - 1) / B));
+  int64_t chunk = ((n + nchunks - 1) / nchunks + 1023) / 1024 * 1024;
+  nchunks = (int)((n + chunk - 1) / chunk);
+  auto opts = x.options();
+  auto partial = torch::empty({B, nchunks}, opts);
+  auto logp = torch::empty({B}, opts);
+  auto stdv = torch::empty({B}, opts);
+  dim3 grid(nchunks, B);
+  auto st = stream();
+  const float* pp = has_prev ? prev->data_ptr<float>() : nullptr;
+  const float* np_ = has_noise ? noise->data_ptr<float>() : nullptr;
+#define VO_SDE_LAUNCH(HP, HN)                                                                               \
+  sde_fwd_kernel<HP, HN><<<grid, 256, 0, st>>>(x.data_ptr<float>(), v.data_ptr<float>(),                   \
+                                               sigma.data_ptr<float>(), sigma_prev.data_ptr<float>(), pp, np_, \
+                                               prev_out.data_ptr<float>(), mean.data_ptr<float>(),          \
+                                               partial.data_ptr<float>(), n, chunk, nchunks, (float)sigma_max, \
+                                               (float)eta, (int)type, norm, (uint64_t)seed, (uint32_t)offset)
+  if (has_prev)
+    VO_SDE_LAUNCH(true, false);
+  else if (has_noise)
+    VO_SDE_LAUNCH(false, true);
+  else
+    VO_SDE_LAUNCH(false, false);
+#undef VO_SDE_LAUNCH
+  sde_finalize_kernel<<<(B + 7) / 8, 256, 0, st>>>(partial.data_ptr<float>(), sigma.data_ptr<float>(),
+                                                   sigma_prev.data_ptr<float>(),
+                                                   want_logp ? logp.data_ptr<float>() : nullptr,
+                                                   stdv.data_ptr<float>(), B, nchunks, n, (float)sigma_max,
+                                                   (float)eta, (int)type, norm);
+  VO_CUDA_OK(cudaGetLastError());
+  return {prev_out, logp, mean, stdv};
+}
+
+torch::Tensor sde_step_bwd(torch::Tensor x, torch::Tensor prev, torch::Tensor mean, torch::Tensor sigma,
+                           torch::Tensor sigma_prev, torch::Tensor g_logp, torch::Tensor g_mean, double sigma_max,
+                           double eta, int64_t type) {
+  VO_CHECK_INPUT(prev);
+  VO_CHECK_INPUT(mean);
+  VO_CHECK_INPUT(g_mean);
+  c10::cuda::CUDAGuard g(x.device());
+  const int B = x.size(0);
+  const int64_t n = x.numel() / B;
+  auto gv = torch::empty_like(x);
+  int bx = std::max(1, std::min<int>((int)((n + 255) / 256), (4 * num_sms() + B - 1) / B));
+  sde_bwd_kernel<<<dim3(bx, B), 256, 0, stream()>>>(prev.data_ptr<float>(), mean.data_ptr<float>(),
+                                                     sigma.data_ptr<float>(), sigma_prev.data_ptr<float>(),
+                                                     g_logp.data_ptr<float>(), g_mean.data_ptr<float>(),
+                                                     gv.data_ptr<float>(), n, (float)sigma_max, (float)eta, (int)type);
+  VO_CUDA_OK(cudaGetLastError());
+  return gv;
+}
+
+}  // namespace vo

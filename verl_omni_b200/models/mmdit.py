@@ -1,0 +1,185 @@
+"""SD3 / SD3.5-shaped MMDiT (joint text+image attention transformer) built on the sm_100a ops.
+
+Shape family of diffusers' ``SD3Transformer2DModel`` as used by the reference SD3.5 FlowGRPO
+adapter (``verl_omni/pipelines/sd3_flow_grpo/diffusers_training_adapter.py:48-181``):
+
+* patch embed (p=2) + fixed 2D sin-cos positions; timestep (256-d sinusoid) + pooled-text MLPs
+  summed into ``temb``; ``context_embedder`` maps the joint CLIP+T5 token sequence to the width;
+* ``depth`` joint blocks: per-stream AdaLN-Zero modulation, per-head RMS qk-norm, one joint
+  attention over ``[image ; text]`` tokens, gated residual out-projections and GELU(tanh) MLPs.
+  The first ``dual_attention_layers`` blocks add an image-only self-attention branch
+  (SD3.5 "MMDiT-X"); the last block is ``context_pre_only`` (text stream feeds k/v only);
+* AdaLN-continuous output norm + linear to ``p*p*C`` and unpatchify.
+
+Every linear runs on the tcgen05 GEMM (gated residuals and GELU fused into the epilogue), the
+AdaLN norms and the qk-norm/QKV split are fused kernels, and attention is the tcgen05 FMHA.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from verl_omni_b200.models.layers import Linear, RMSWeight, TimestepMLP, patchify, sincos_2d, timestep_embedding, unpatchify
+from verl_omni_b200.ops.attention import attention
+from verl_omni_b200.ops.norm import adaln_layernorm, qk_norm_split_into
+
+
+@dataclass
+class MMDiTConfig:
+    in_channels: int = 16
+    out_channels: int = 16
+    patch_size: int = 2
+    hidden: int = 1536
+    heads: int = 24
+    depth: int = 24
+    mlp_ratio: float = 4.0
+    joint_attention_dim: int = 4096
+    pooled_projection_dim: int = 2048
+    pos_embed_max_size: int = 384
+    sample_size: int = 64
+    dual_attention_layers: int = 13
+    qk_norm: bool = True
+    eps: float = 1e-6
+
+    @staticmethod
+    def sd35_medium() -> "MMDiTConfig":
+        return MMDiTConfig()
+
+    @staticmethod
+    def tiny(hidden: int = 64, heads: int = 2, depth: int = 2) -> "MMDiTConfig":
+        return MMDiTConfig(hidden=hidden, heads=heads, depth=depth, joint_attention_dim=48,
+                           pooled_projection_dim=32, dual_attention_layers=1, sample_size=8, in_channels=4,
+                           out_channels=4, pos_embed_max_size=16)
+
+
+class JointBlock(nn.Module):
+    def __init__(self, cfg: MMDiTConfig, context_pre_only: bool, dual: bool):
+        super().__init__()
+        D = cfg.hidden
+        self.D, self.H = D, cfg.heads
+        self.dh = D // cfg.heads
+        self.cpo = context_pre_only
+        self.dual = dual
+        self.n_mod = 9 if dual else 6
+        self.n_mod_c = 2 if context_pre_only else 6
+        self.norm1_linear = Linear(D, self.n_mod * D)
+        self.norm1_context_linear = Linear(D, self.n_mod_c * D)
+        self.to_qkv = Linear(D, 3 * D)
+        self.add_qkv = Linear(D, 3 * D)
+        self.norm_q, self.norm_k = RMSWeight(self.dh), RMSWeight(self.dh)
+        self.norm_added_q, self.norm_added_k = RMSWeight(self.dh), RMSWeight(self.dh)
+        self.to_out = Linear(D, D)
+        hid = int(D * cfg.mlp_ratio)
+        self.ff_1, self.ff_2 = Linear(D, hid), Linear(hid, D)
+        if not context_pre_only:
+            self.to_add_out = Linear(D, D)
+            self.ff_context_1, self.ff_context_2 = Linear(D, hid), Linear(hid, D)
+        if dual:
+            self.attn2_qkv = Linear(D, 3 * D)
+            self.attn2_out = Linear(D, D)
+            self.norm2_q, self.norm2_k = RMSWeight(self.dh), RMSWeight(self.dh)
+        self.eps = cfg.eps
+
+    def forward(self, x: torch.Tensor, c: torch.Tensor, temb_act: torch.Tensor):
+        B, Si, D = x.shape
+        St = c.shape[1]
+        H, dh = self.H, self.dh
+        mod = self.norm1_linear(temb_act)  # [B, n_mod*D]
+        modc = self.norm1_context_linear(temb_act)
+        # chunk order: 0 shift_msa, 1 scale_msa, 2 gate_msa, 3 shift_mlp, 4 scale_mlp, 5 gate_mlp,
+        #              6 shift_msa2, 7 scale_msa2, 8 gate_msa2
+        h = adaln_layernorm(x, mod, 0, 1, self.n_mod, self.eps)
+        hc = adaln_layernorm(c, modc, 0, 1, self.n_mod_c, self.eps)
+        qkv = self.to_qkv(h).reshape(B * Si, 3 * D)
+        qkvc = self.add_qkv(hc).reshape(B * St, 3 * D)
+        S = Si + St
+        dev, dt = x.device, x.dtype
+        q = torch.empty(B, H, S, dh, device=dev, dtype=dt)
+        k = torch.empty(B, H, S, dh, device=dev, dtype=dt)
+        v = torch.empty(B, H, S, dh, device=dev, dtype=dt)
+        q, k, v = qk_norm_split_into(q, k, v, qkv, self.norm_q.weight, self.norm_k.weight, Si, 0, eps=self.eps)
+        q, k, v = qk_norm_split_into(q, k, v, qkvc, self.norm_added_q.weight, self.norm_added_k.weight, St, Si,
+                                     eps=self.eps)
+        o = attention(q, k, v)  # [B, S, D]
+        o_img = o[:, :Si].contiguous()
+        gate_msa = mod.view(B, self.n_mod, D)[:, 2]
+        x_new = self.to_out(o_img, epilogue="gate_res", gate=gate_msa, res=x, S=Si)
+        if self.dual:
+            h2 = adaln_layernorm(x, mod, 6, 7, self.n_mod, self.eps)
+            qkv2 = self.attn2_qkv(h2).reshape(B * Si, 3 * D)
+            q2 = torch.empty(B, H, Si, dh, device=dev, dtype=dt)
+            k2 = torch.empty_like(q2)
+            v2 = torch.empty_like(q2)
+            q2, k2, v2 = qk_norm_split_into(q2, k2, v2, qkv2, self.norm2_q.weight, self.norm2_k.weight, Si, 0,
+                                            eps=self.eps)
+            o2 = attention(q2, k2, v2)
+            x_new = self.attn2_out(o2, epilogue="gate_res", gate=mod.view(B, self.n_mod, D)[:, 8], res=x_new, S=Si)
+        x = x_new
+        hm = adaln_layernorm(x, mod, 3, 4, self.n_mod, self.eps)
+        u = self.ff_1(hm, epilogue="gelu")
+        x = self.ff_2(u, epilogue="gate_res", gate=mod.view(B, self.n_mod, D)[:, 5], res=x, S=Si)
+        if self.cpo:
+            return x, None
+        o_txt = o[:, Si:].contiguous()
+        mc = modc.view(B, self.n_mod_c, D)
+        c = self.to_add_out(o_txt, epilogue="gate_res", gate=mc[:, 2], res=c, S=St)
+        hcm = adaln_layernorm(c, modc, 3, 4, self.n_mod_c, self.eps)
+        uc = self.ff_context_1(hcm, epilogue="gelu")
+        c = self.ff_context_2(uc, epilogue="gate_res", gate=mc[:, 5], res=c, S=St)
+        return x, c
+
+
+class MMDiT(nn.Module):
+    """Input latents ``[B, C, H, W]`` (fp32 or bf16), timesteps ``[B]`` in [0, 1000],
+    ``encoder_hidden_states [B, St, joint_attention_dim]``, ``pooled_projections [B, pooled_dim]``.
+    Returns the velocity prediction ``[B, C, H, W]`` in fp32."""
+
+    family = "sd3"
+
+    def __init__(self, cfg: MMDiTConfig):
+        super().__init__()
+        self.cfg = cfg
+        D, p = cfg.hidden, cfg.patch_size
+        self.pos_embed_proj = Linear(cfg.in_channels * p * p, D)
+        grid = cfg.pos_embed_max_size
+        self.register_buffer("pos_table", sincos_2d(D, grid, grid, base_size=cfg.sample_size // p), persistent=False)
+        self.time_embed = TimestepMLP(256, D)
+        self.text_embed = TimestepMLP(cfg.pooled_projection_dim, D)
+        self.context_embedder = Linear(cfg.joint_attention_dim, D)
+        self.transformer_blocks = nn.ModuleList([
+            JointBlock(cfg, context_pre_only=(i == cfg.depth - 1), dual=(i < cfg.dual_attention_layers))
+            for i in range(cfg.depth)])
+        self.norm_out_linear = Linear(D, 2 * D)
+        self.proj_out = Linear(D, p * p * cfg.out_channels)
+        self.gradient_checkpointing = False
+
+    def _pos(self, h: int, w: int) -> torch.Tensor:
+        g = self.cfg.pos_embed_max_size
+        top, left = (g - h) // 2, (g - w) // 2
+        t = self.pos_table.view(g, g, -1)[top:top + h, left:left + w]
+        return t.reshape(h * w, -1)
+
+    def forward(self, hidden_states, timestep, encoder_hidden_states, pooled_projections):
+        cfg = self.cfg
+        p = cfg.patch_size
+        B, C, Hh, Ww = hidden_states.shape
+        dt = self.proj_out.weight.dtype
+        x = patchify(hidden_states.to(dt), p)
+        x = self.pos_embed_proj(x)
+        x = x + self._pos(Hh // p, Ww // p).to(dt)[None]
+        temb = self.time_embed(timestep_embedding(timestep, 256).to(dt)) + self.text_embed(pooled_projections.to(dt))
+        temb_act = F.silu(temb)
+        c = self.context_embedder(encoder_hidden_states.to(dt))
+        for blk in self.transformer_blocks:
+            if self.gradient_checkpointing and torch.is_grad_enabled():
+                x, c = torch.utils.checkpoint.checkpoint(blk, x, c, temb_act, use_reentrant=False)
+            else:
+                x, c = blk(x, c, temb_act)
+        mod = self.norm_out_linear(temb_act)
+        h = adaln_layernorm(x, mod, 1, 0, 2, cfg.eps)
+        out = self.proj_out(h)
+        return unpatchify(out, p, cfg.out_channels, Hh, Ww).float()

@@ -1,0 +1,63 @@
+"""Architecture presets: name -> (module factory, adapter arch, latent shape, conditioning spec)."""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Callable, Optional
+
+import torch
+
+from verl_omni_b200.models.dit import DiT, DiTConfig, TextEncoder
+from verl_omni_b200.models.mmdit import MMDiT, MMDiTConfig
+
+
+@dataclass
+class ArchSpec:
+    name: str
+    adapter: str
+    build: Callable[[], torch.nn.Module]
+    latent_shape: tuple
+    cond_shapes: dict  # key -> per-sample shape of random conditioning (embeddings)
+    text_encoder: Optional[Callable[[], torch.nn.Module]] = None  # token-id prompts
+    prompt_len: int = 16
+    vocab: int = 1000
+    reward: str = "vit"
+    image_size: int = 512
+    notes: str = ""
+
+
+def _flux_build():
+    from verl_omni_b200.models.flux import FluxConfig, FluxDiT
+
+    return FluxDiT(FluxConfig.flux1_dev())
+
+
+ARCHS: dict[str, ArchSpec] = {
+    "tiny_dit": ArchSpec(
+        "tiny_dit", "TinyDiT", lambda: DiT(DiTConfig.tiny_plumbing()), (4, 16, 16), {},
+        text_encoder=lambda: TextEncoder(vocab=1000, dim=256, layers=2, heads=4), prompt_len=16, vocab=1000,
+        reward="mlp", notes="4 blocks, hidden 256, 4 heads, patch 2; 2-layer text encoder (vocab 1000, hidden 256)"),
+    "sd35_medium": ArchSpec(
+        "sd35_medium", "SD3MMDiT", lambda: MMDiT(MMDiTConfig.sd35_medium()), (16, 64, 64),
+        {"prompt_embeds": (333, 4096), "pooled_prompt_embeds": (2048,)}, reward="vit", image_size=512,
+        notes="24 joint blocks, hidden 1536, 24 heads, patch 2, 16-ch latents; 256 T5 + 77 CLIP tokens"),
+    "sd35_tiny": ArchSpec(
+        "sd35_tiny", "SD3MMDiT", lambda: MMDiT(MMDiTConfig.tiny()), (4, 8, 8),
+        {"prompt_embeds": (12, 48), "pooled_prompt_embeds": (32,)}, reward="mlp", image_size=64),
+    "flux1_dev": ArchSpec(
+        "flux1_dev", "FluxDiT", _flux_build, (16, 128, 128),
+        {"prompt_embeds": (512, 4096), "pooled_prompt_embeds": (768,)}, reward="vit", image_size=1024),
+    "wan21_14b": ArchSpec(
+        "wan21_14b", "WanDiT", lambda: DiT(DiTConfig.wan21_14b()), (16, 21, 60, 104),
+        {"prompt_embeds": (512, 4096)}, reward="vit_video", image_size=480),
+}
+
+
+def get_arch(name: str) -> ArchSpec:
+    if name not in ARCHS:
+        raise KeyError(f"unknown architecture {name!r}; known: {sorted(ARCHS)}")
+    return ARCHS[name]
+
+
+def count_params(m: torch.nn.Module) -> int:
+    return sum(p.numel() for p in m.parameters())

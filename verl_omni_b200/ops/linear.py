@@ -1,0 +1,77 @@
+"""Linear layers on the tcgen05 GEMM with fused epilogues and fp32 main-grad accumulation.
+
+Forward ``y = x W^T + b`` with optional fused epilogues:
+
+* ``gelu``     : ``y = gelu_tanh(x W^T + b)`` (pre-activation kept for backward);
+* ``gate_res`` : ``y = res + gate[b] * (x W^T + b)`` -- the AdaLN-Zero gated residual of DiT blocks.
+
+Backward computes ``dX = dY W`` and accumulates ``dW = dY^T X`` straight into the fp32
+``weight.main_grad`` buffer that the sharded engine owns (no bf16 weight-grad tensor, no
+separate accumulation pass), and ``db`` into ``bias.main_grad``.  Parameters without a
+``main_grad`` get ordinary ``.grad`` tensors.  CPU tensors use ``torch.nn.functional``.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from verl_omni_b200.ops import gemm as G
+
+
+def _accum(param: torch.Tensor, grad: torch.Tensor):
+    """Returns the grad to hand back to autograd (None when accumulated into main_grad)."""
+    mg = getattr(param, "main_grad", None)
+    if mg is None:
+        return grad.to(param.dtype)
+    mg.add_(grad.view_as(mg))
+    return None
+
+
+class _LinearFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, b, epilogue, gate, res, S):
+        x2 = x.reshape(-1, x.shape[-1])
+        out, pre = G.linear_fwd(x2, w, b, epilogue=epilogue, gate=gate, res=res.reshape(-1, w.shape[0]) if res is not None else None, S=S)
+        ctx.save_for_backward(x2, w, pre if pre is not None else torch.empty(0, device=x.device), gate if gate is not None else torch.empty(0, device=x.device))
+        ctx.meta = (epilogue, S, x.shape, b is not None, b)
+        return out.view(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w, pre, gate = ctx.saved_tensors
+        epilogue, S, xshape, has_b, b = ctx.meta
+        dy2 = dy.reshape(-1, w.shape[0]).contiguous()
+        d_gate = d_res = None
+        if epilogue == "gate_res":
+            d_res = dy  # residual passes through
+            # y_lin = pre (saved linear output); dgate[b, n] = sum_s dy * y_lin
+            B = dy2.shape[0] // S
+            d_gate = (dy2.float().view(B, S, -1) * pre.float().view(B, S, -1)).sum(1).to(gate.dtype)
+            dy2 = (dy2.view(B, S, -1) * gate.view(B, 1, -1)).reshape(dy2.shape).contiguous()
+        elif epilogue == "gelu":
+            dy2 = G.gelu_bwd(dy2, pre)
+        dx = G.matmul_nn(dy2, w)  # [M, N] x [N, K] -> [M, K]
+        dw = G.wgrad(dy2, x2, getattr(w, "main_grad", None))
+        gw = None if dw is None else dw.to(w.dtype)
+        gb = None
+        if has_b:
+            db = dy2.float().sum(0)
+            gb = _accum(b, db)
+        return dx.view(xshape), gw, gb, None, d_gate, d_res, None
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None, *, epilogue: str = "none",
+           gate: Optional[torch.Tensor] = None, res: Optional[torch.Tensor] = None, S: int = 1) -> torch.Tensor:
+    """``gate`` is [B, N] (per-sample), ``res`` has the output's shape; ``S`` = rows per sample."""
+    if not x.is_cuda:
+        y = F.linear(x, w, b)
+        if epilogue == "gelu":
+            return F.gelu(y, approximate="tanh")
+        if epilogue == "gate_res":
+            B = gate.shape[0]
+            return res + (y.view(B, -1, y.shape[-1]) * gate[:, None]).view_as(res)
+        return y
+    return _LinearFn.apply(x, w, b, epilogue, gate, res, S)

@@ -1,0 +1,143 @@
+"""Model adapters: (architecture, algorithm) -> how a DiT is called and stepped.
+
+Mirrors the registry/dispatch contract of ``verl_omni/pipelines/model_base.py:28-257``
+(``DiffusionModelBase.register(arch, algorithm)``, ``build_scheduler``,
+``prepare_model_inputs``, ``forward_and_sample_previous_step``, ``forward``) for the model
+families implemented in ``verl_omni_b200.models``:
+
+* ``TinyDiT``  : cross-attention DiT + 2-layer text encoder (token-id prompts)
+* ``SD3MMDiT`` : SD3.5-shaped MMDiT, prompt = (joint CLIP+T5 embeds, pooled CLIP embed)
+* ``FluxDiT``  : FLUX.1-shaped double/single-stream DiT with 2D RoPE and guidance embedding
+* ``WanDiT``   : Wan2.1-shaped video DiT with 3D RoPE
+
+The same adapter serves the rollout loop and the trainer's log-prob recompute, so both run
+identical kernels on identical inputs (bit-identical log-probs for bypass mode).
+"""
+
+from __future__ import annotations
+
+from typing import Any, Optional
+
+import torch
+
+from verl_omni_b200.pipelines.schedulers.flow_match_sde import FlowMatchSDEDiscreteScheduler, build_scheduler
+
+_REGISTRY: dict[tuple[str, str], type] = {}
+
+
+class DiffusionModelBase:
+    """Adapter base; subclasses are stateless (classmethods), selected by (architecture, algorithm)."""
+
+    scheduler_kind = "sd3"
+    latent_key = "latents"
+
+    @classmethod
+    def register(cls, arch: str, algorithm: str | tuple = "flow_grpo"):
+        algos = (algorithm,) if isinstance(algorithm, str) else tuple(algorithm)
+
+        def deco(sub):
+            for a in algos:
+                _REGISTRY[(arch, a)] = sub
+            return sub
+
+        return deco
+
+    @classmethod
+    def get(cls, arch: str, algorithm: str) -> type:
+        if (arch, algorithm) in _REGISTRY:
+            return _REGISTRY[(arch, algorithm)]
+        if (arch, "flow_grpo") in _REGISTRY and algorithm in ("dance_grpo", "mix_grpo", "flow_dppo", "grpo_guard",
+                                                             "diffusion_nft", "dpo", "distill_kl"):
+            return _REGISTRY[(arch, "flow_grpo")]
+        raise KeyError(f"no adapter registered for ({arch!r}, {algorithm!r}); known: {sorted(_REGISTRY)}")
+
+    # -------------------------------------------------------------- schedule
+    @classmethod
+    def build_scheduler(cls, num_inference_steps: int, image_seq_len: Optional[int] = None,
+                        device=None) -> FlowMatchSDEDiscreteScheduler:
+        return build_scheduler(cls.scheduler_kind, num_inference_steps, image_seq_len=image_seq_len, device=device)
+
+    # -------------------------------------------------------------- model call
+    @classmethod
+    def cond_keys(cls) -> tuple:
+        """Per-sample conditioning tensors carried from rollout to training."""
+        raise NotImplementedError
+
+    @classmethod
+    def forward(cls, module, latents: torch.Tensor, timesteps: torch.Tensor, cond: dict) -> torch.Tensor:
+        raise NotImplementedError
+
+    @classmethod
+    def predict(cls, module, latents, timesteps, cond: dict, neg_cond: Optional[dict] = None,
+                guidance_scale: Optional[float] = None) -> torch.Tensor:
+        """Velocity prediction with optional classifier-free guidance (cond+uncond batched in one forward)."""
+        if guidance_scale is not None and guidance_scale > 1.0 and neg_cond is not None:
+            both = {k: torch.cat([cond[k], neg_cond[k]], 0) for k in cond}
+            out = cls.forward(module, torch.cat([latents, latents], 0), torch.cat([timesteps, timesteps], 0), both)
+            pos, neg = out.chunk(2, 0)
+            return neg + guidance_scale * (pos - neg)
+        return cls.forward(module, latents, timesteps, cond)
+
+    @classmethod
+    def forward_and_sample_previous_step(cls, module, scheduler: FlowMatchSDEDiscreteScheduler, *,
+                                         latents: torch.Tensor, prev_latents: torch.Tensor, step_index: torch.Tensor,
+                                         cond: dict, neg_cond: Optional[dict], guidance_scale: Optional[float],
+                                         noise_level: float, sde_type: str) -> dict:
+        t = scheduler.timesteps.to(latents.device)[step_index.to(latents.device)]
+        v = cls.predict(module, latents, t, cond, neg_cond, guidance_scale)
+        out = scheduler.sample_previous_step(latents.float(), v.float(), step_index=step_index, noise_level=noise_level,
+                                             prev_sample=prev_latents.float(), sde_type=sde_type, return_sqrt_dt=True)
+        return {"log_probs": out.log_prob, "prev_sample_mean": out.prev_sample_mean, "std_dev_t": out.std_dev_t,
+                "sqrt_dt": out.sqrt_dt, "noise_pred": v}
+
+
+@DiffusionModelBase.register("TinyDiT", ("flow_grpo",))
+class TinyDiTFlowGRPO(DiffusionModelBase):
+    scheduler_kind = "tiny"
+
+    @classmethod
+    def cond_keys(cls):
+        return ("prompt_embeds",)
+
+    @classmethod
+    def forward(cls, module, latents, timesteps, cond):
+        return module(latents, timesteps, cond["prompt_embeds"])
+
+
+@DiffusionModelBase.register("SD3MMDiT", ("flow_grpo",))
+class SD3FlowGRPO(DiffusionModelBase):
+    scheduler_kind = "sd3"
+
+    @classmethod
+    def cond_keys(cls):
+        return ("prompt_embeds", "pooled_prompt_embeds")
+
+    @classmethod
+    def forward(cls, module, latents, timesteps, cond):
+        return module(latents, timesteps, cond["prompt_embeds"], cond["pooled_prompt_embeds"])
+
+
+@DiffusionModelBase.register("WanDiT", ("flow_grpo", "dance_grpo"))
+class WanFlowGRPO(DiffusionModelBase):
+    scheduler_kind = "wan"
+
+    @classmethod
+    def cond_keys(cls):
+        return ("prompt_embeds",)
+
+    @classmethod
+    def forward(cls, module, latents, timesteps, cond):
+        return module(latents, timesteps, cond["prompt_embeds"])
+
+
+@DiffusionModelBase.register("FluxDiT", ("flow_grpo",))
+class FluxFlowGRPO(DiffusionModelBase):
+    scheduler_kind = "flux"
+
+    @classmethod
+    def cond_keys(cls):
+        return ("prompt_embeds", "pooled_prompt_embeds")
+
+    @classmethod
+    def forward(cls, module, latents, timesteps, cond):
+        return module(latents, timesteps, cond["prompt_embeds"], cond["pooled_prompt_embeds"])

@@ -1,0 +1,253 @@
+"""Synchronous on-policy diffusion RL trainer (FlowGRPO / DanceGRPO / MixGRPO / GRPO-Guard / Flow-DPPO).
+
+One step, as in ``PolicyGradientRayTrainer.fit`` (``verl_omni/trainer/diffusion/ray_diffusion_trainer.py:1067-1361``):
+
+  prompts -> repeat n (uid per prompt) -> rollout (SDE trajectories + log-probs) -> decode -> reward
+  -> old log-probs (skipped in bypass mode) -> rollout correction -> reference means (KL)
+  -> group advantage -> actor update (micro-batches x SDE steps) -> checkpoint -> weight sync -> metrics
+
+Differences by design: ranks are plain processes (torchrun) instead of Ray actors; rollout runs
+in-process on the same weights (the hybrid engine is the default and weight sync is zero-copy
+when colocated); every rank owns whole prompt groups so advantages need only one all-gather of the
+scalar rewards.
+"""
+
+from __future__ import annotations
+
+import copy
+import logging
+import os
+import time
+from typing import Optional
+
+import numpy as np
+import torch
+
+from verl_omni_b200.models.registry import ArchSpec, get_arch
+from verl_omni_b200.models.reward import LatentMLPReward, VAEDecoder, ViTScorer
+from verl_omni_b200.parallel import dist as D
+from verl_omni_b200.pipelines.model_base import DiffusionModelBase
+from verl_omni_b200.trainer.config.algorithm import DiffusionAlgoConfig
+from verl_omni_b200.trainer.diffusion import diffusion_algos as algos
+from verl_omni_b200.trainer.diffusion.rollout_correction import (
+    apply_bypass_mode_to_diffusion_batch, apply_rollout_correction_to_diffusion_batch,
+    compute_rollout_corr_metrics_from_batch, rollout_correction_enabled)
+from verl_omni_b200.utils.dataproto import DataProto
+from verl_omni_b200.utils.dataset import ResumableSampler, SyntheticPromptDataset
+from verl_omni_b200.utils import metrics as M
+from verl_omni_b200.workers.config.diffusion import DiffusionActorConfig, DiffusionModelConfig, DiffusionRolloutConfig
+from verl_omni_b200.workers.engine.diffusion_engine import PPODiffusionEngine
+from verl_omni_b200.workers.reward.reward_manager import ModelScorer, VisualRewardManager
+from verl_omni_b200.workers.rollout.dit_rollout import DiTRolloutEngine
+from verl_omni_b200.workers.utils_losses import diffusion_loss
+
+_log = logging.getLogger(__name__)
+
+
+class PolicyGradientTrainer:
+    def __init__(self, config, *, arch: Optional[str] = None, device: Optional[torch.device] = None):
+        self.config = config
+        di = D.info()
+        self.device = device or di.device
+        self.rank, self.world = D.rank(), D.world_size()
+        arc = config.actor_rollout_ref
+        self.actor_cfg = DiffusionActorConfig.from_cfg(arc.actor)
+        self.rollout_cfg = DiffusionRolloutConfig.from_cfg(arc.rollout)
+        self.model_cfg = DiffusionModelConfig.from_cfg(arc.model)
+        self.algo_cfg = DiffusionAlgoConfig.from_cfg(config.algorithm)
+        self.spec: ArchSpec = get_arch(arch or self.model_cfg.architecture or "tiny_dit")
+        self.adapter = DiffusionModelBase.get(self.spec.adapter, self.model_cfg.algorithm)
+        self.n = self.rollout_cfg.n
+        gbs = int(config.data.train_batch_size)
+        if gbs % self.world:
+            raise ValueError(f"data.train_batch_size={gbs} must be divisible by the world size {self.world}")
+        self.prompts_per_rank = gbs // self.world
+        self.global_step = 0
+        self.total_steps = int(config.trainer.total_training_steps or 1)
+        seed = int(self.actor_cfg.fsdp_config.seed)
+        torch.manual_seed(seed)
+        cuda = self.device.type == "cuda"
+        # ---------------------------------------------------------------- models
+        module = self.spec.build()
+        if self.model_cfg.enable_gradient_checkpointing and hasattr(module, "gradient_checkpointing"):
+            module.gradient_checkpointing = True
+        module.to(self.device)
+        ref_module = copy.deepcopy(module) if self.actor_cfg.use_kl_loss else None
+        T = self.rollout_cfg.pipeline.num_inference_steps
+        seq = int(np.prod(self.spec.latent_shape[-2:])) // 4
+        self.scheduler = self.adapter.build_scheduler(T, image_seq_len=seq, device=self.device)
+        self.actor = PPODiffusionEngine(module, self.adapter, self.scheduler, self.actor_cfg, self.model_cfg,
+                                        device=self.device, total_steps=self.total_steps)
+        self.ref = None
+        if ref_module is not None:
+            self.ref = PPODiffusionEngine(ref_module, self.adapter, self.scheduler, self.actor_cfg, self.model_cfg,
+                                          device=self.device, trainable=False)
+        dt = self.actor.engine.dtype
+        self.text_encoder = None
+        if self.spec.text_encoder is not None:
+            torch.manual_seed(seed + 1)
+            self.text_encoder = self.spec.text_encoder().to(self.device, dt).eval()
+            for p in self.text_encoder.parameters():
+                p.requires_grad_(False)
+        # ---------------------------------------------------------------- reward + decoder
+        torch.manual_seed(seed + 2)
+        decoder = None
+        if self.spec.reward == "mlp":
+            scorer = ModelScorer(LatentMLPReward(self.spec.latent_shape[0]).to(self.device, dt), "final_latents",
+                                 self.device)
+        else:
+            vae = VAEDecoder(self.spec.latent_shape[0]).to(self.device, dt)
+            if cuda:
+                vae = vae.to(memory_format=torch.channels_last)
+            decoder = vae.decode_video if self.spec.reward == "vit_video" else vae
+            scorer = ModelScorer(ViTScorer(image_size=self.spec.image_size).to(self.device, dt), "images", self.device)
+        self.reward_fn = VisualRewardManager(scorer, name="score")
+        self.rollout = DiTRolloutEngine(module, self.adapter, self.rollout_cfg, self.model_cfg, device=self.device,
+                                        latent_shape=self.spec.latent_shape, decoder=decoder)
+        # ---------------------------------------------------------------- data
+        n_prompts = int(config.data.get("synthetic", {}).get("num_prompts", 1024))
+        self.dataset = SyntheticPromptDataset(n_prompts, seed=int(config.data.get("seed", 0) or 0),
+                                              token_len=self.spec.prompt_len if self.spec.text_encoder else 0,
+                                              vocab=self.spec.vocab, cond_shapes=self.spec.cond_shapes)
+        self.sampler = ResumableSampler(n_prompts, gbs, seed=int(config.data.get("seed", 0) or 0),
+                                        shuffle=bool(config.data.get("shuffle", True)))
+        self.loss_fn = lambda model_output, data: diffusion_loss(self.actor_cfg, model_output, data)
+        self.ckpt_dir = config.trainer.default_local_dir
+
+    # ------------------------------------------------------------------ pieces
+    @torch.no_grad()
+    def encode_prompts(self, batch: DataProto) -> DataProto:
+        dt = self.actor.engine.dtype
+        t = {}
+        if self.text_encoder is not None:
+            t["prompt_embeds"] = self.text_encoder(batch.batch["input_ids"].to(self.device))
+        for k in self.spec.cond_shapes:
+            t[k] = batch.batch[k].to(self.device, dt)
+        return DataProto(t, dict(batch.non_tensor_batch))
+
+    def local_prompt_ids(self, global_ids: list[int]) -> list[int]:
+        p = self.prompts_per_rank
+        return global_ids[self.rank * p:(self.rank + 1) * p]
+
+    def compute_advantage(self, scores: torch.Tensor, uid: np.ndarray, T: int) -> torch.Tensor:
+        """Group-normalised advantage; global std needs every rank's scores (one small all-gather)."""
+        all_scores = D.all_gather_object(scores.detach().float().cpu())
+        all_uid = D.all_gather_object(list(uid))
+        g_scores = torch.cat(all_scores)
+        g_uid = np.concatenate([np.asarray(u, dtype=object) for u in all_uid])
+        est = algos.get_diffusion_adv_estimator_fn(self.algo_cfg.adv_estimator)
+        adv, _ = est(g_scores[:, None].expand(-1, T), g_uid, norm_adv_by_std_in_grpo=self.algo_cfg.norm_adv_by_std_in_grpo,
+                     global_std=self.algo_cfg.global_std)
+        B = scores.shape[0]
+        return adv[self.rank * B:(self.rank + 1) * B]
+
+    # ------------------------------------------------------------------ one step
+    def step(self, global_ids: Optional[list[int]] = None) -> dict:
+        self.global_step += 1
+        timer = M.PhaseTimer(self.device)
+        t_start = time.perf_counter()
+        if self.device.type == "cuda":
+            torch.cuda.synchronize()
+        ids = self.local_prompt_ids(global_ids if global_ids is not None else self.sampler.next_batch())
+        with timer("gen"):
+            prompts = self.dataset.get_batch(ids)
+            cond = self.encode_prompts(prompts)
+            uid = np.array([f"{self.global_step}-{i}" for i in ids], dtype=object)
+            cond.non_tensor_batch["uid"] = uid
+            gen = cond.repeat(self.n, interleave=True)
+            base_seed = int(self.rollout_cfg.seed if self.rollout_cfg.seed is not None else 12345)
+            seed = (base_seed + self.global_step - 1) * 9973 + self.rank
+            out = self.rollout.generate(gen, seed=seed, global_step=self.global_step)
+            out.non_tensor_batch.update(gen.non_tensor_batch)
+        with timer("reward"):
+            scores, rmetrics = self.reward_fn(out)
+            scores = scores.to(self.device)
+        T = out.batch["step_index"].shape[1]
+        with timer("old_log_prob"):
+            if self.algo_cfg.rollout_correction.bypass_mode or self.actor_cfg.rollout_correction.bypass_mode:
+                apply_bypass_mode_to_diffusion_batch(out)
+            else:
+                old = self.actor.infer_batch(out, keys=("log_probs",))
+                out.batch["old_log_probs"] = old.batch["log_probs"]
+        corr_metrics = compute_rollout_corr_metrics_from_batch(out, bypass_mode=self.algo_cfg.rollout_correction.bypass_mode)
+        if rollout_correction_enabled(self.algo_cfg.rollout_correction) and not self.algo_cfg.rollout_correction.bypass_mode:
+            out, m2 = apply_rollout_correction_to_diffusion_batch(out, self.algo_cfg.rollout_correction)
+            corr_metrics.update(m2)
+        if self.ref is not None:
+            with timer("ref"):
+                r = self.ref.infer_batch(out, keys=("prev_sample_mean",))
+                out.batch["ref_prev_sample_mean"] = r.batch["prev_sample_mean"]
+        if self.actor_cfg.diffusion_loss.loss_mode in ("flow_dppo", "grpo_guard"):
+            with timer("old_mean"):
+                om = self.actor.infer_batch(out, keys=("prev_sample_mean",))
+                out.batch["old_prev_sample_mean"] = om.batch["prev_sample_mean"]
+        with timer("adv"):
+            adv = self.compute_advantage(scores, out.non_tensor_batch["uid"], T).to(self.device)
+            out.batch["advantages"] = adv
+        train_metrics = {}
+        with timer("update_actor"):
+            for _ in range(self.actor_cfg.ppo_epochs):
+                mini = max(1, int(self.actor_cfg.ppo_mini_batch_size) * self.n // self.world)
+                for s in range(0, len(out), mini):
+                    train_metrics = self.actor.train_batch(out.select_idxs(slice(s, min(len(out), s + mini))),
+                                                           self.loss_fn)
+        with timer("update_weights"):
+            self.rollout.update_weights(self.actor.engine.get_per_tensor_param())
+        save_freq = int(self.config.trainer.save_freq)
+        if save_freq > 0 and self.global_step % save_freq == 0:
+            with timer("save_checkpoint"):
+                self.save_checkpoint()
+        step_time = time.perf_counter() - t_start
+        metrics = {"training/global_step": self.global_step}
+        metrics.update(train_metrics)
+        metrics.update(rmetrics)
+        metrics.update(corr_metrics)
+        metrics.update(M.compute_data_metrics_diffusion(scores, adv[:, 0], out.non_tensor_batch["uid"]))
+        metrics.update(M.compute_timing_metrics_diffusion(timer.timing, len(out)))
+        metrics.update(M.compute_throughput_metrics_diffusion(step_time, len(out) * self.world, self.world))
+        return metrics
+
+    def fit(self, steps: Optional[int] = None, log_fn=None) -> list[dict]:
+        steps = steps or self.total_steps
+        if self.config.trainer.resume_mode == "auto":
+            self.maybe_resume()
+        hist = []
+        while self.global_step < steps:
+            m = self.step()
+            hist.append(m)
+            if log_fn is not None and self.rank == 0:
+                log_fn(m)
+        return hist
+
+    # ------------------------------------------------------------------ checkpoint / resume
+    def save_checkpoint(self) -> str:
+        """``{default_local_dir}/global_step_{N}/actor`` + ``data.pt`` + ``latest_checkpointed_iteration.txt``."""
+        root = os.path.join(self.ckpt_dir, f"global_step_{self.global_step}")
+        self.actor.engine.save_checkpoint(os.path.join(root, "actor"), self.global_step,
+                                          tuple(self.actor_cfg.checkpoint.save_contents))
+        if self.rank == 0:
+            torch.save({"sampler": self.sampler.state_dict(), "global_step": self.global_step},
+                       os.path.join(root, "data.pt"))
+            with open(os.path.join(self.ckpt_dir, "latest_checkpointed_iteration.txt"), "w") as f:
+                f.write(str(self.global_step))
+        D.barrier()
+        return root
+
+    def maybe_resume(self) -> bool:
+        mode = self.config.trainer.resume_mode
+        if mode == "disable":
+            return False
+        if mode == "resume_path" and self.config.trainer.resume_from_path:
+            root = self.config.trainer.resume_from_path
+        else:
+            marker = os.path.join(self.ckpt_dir, "latest_checkpointed_iteration.txt")
+            if not os.path.exists(marker):
+                return False
+            with open(marker) as f:
+                root = os.path.join(self.ckpt_dir, f"global_step_{int(f.read().strip())}")
+        self.actor.engine.load_checkpoint(os.path.join(root, "actor"),
+                                          tuple(self.actor_cfg.checkpoint.load_contents))
+        d = torch.load(os.path.join(root, "data.pt"), weights_only=False)
+        self.sampler.load_state_dict(d["sampler"])
+        self.global_step = int(d["global_step"])
+        return True

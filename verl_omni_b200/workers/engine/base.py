@@ -1,0 +1,337 @@
+"""Sharded training engine core: flat parameters, fp32 main grads, sharded AdamW, checkpoints.
+
+Design for B200 (180 GB HBM per GPU):
+
+* every trainable parameter lives in ONE flat compute-dtype buffer (bf16 on GPU); parameter
+  tensors are views into it, so the rollout engine and the trainer share the same weights and
+  the trainer->rollout "weight sync" within a process is free;
+* gradients accumulate in a flat fp32 ``main_grad`` buffer (the GEMM weight-gradient epilogue
+  adds into it directly) across all micro-batches and SDE timesteps of a step;
+* the fp32 master weights and AdamW moments are sharded 1/world per rank; one optimizer step is
+  reduce-scatter(main_grad) -> global-norm clip -> fused AdamW on the shard (writing the fp32
+  master and the bf16 copy in one pass) -> all-gather of the bf16 shards;
+* ``reshard_after_forward=False`` (default): the gathered bf16 weights stay resident (ZeRO-2
+  style); this removes per-block all-gathers from the hot loop for every model in scope.
+
+Engine contract and checkpoint layout follow the reference's FSDP engine
+(``verl_omni/workers/engine/fsdp/diffusers_impl.py:405-724``): AdamW with constant/cosine
+warm-up schedules, grad-clip with a skipped step on a non-finite norm, and per-rank files
+``model_world_size_{W}_rank_{r}.pt`` / ``optim_world_size_{W}_rank_{r}.pt`` /
+``extra_state_world_size_{W}_rank_{r}.pt`` + ``fsdp_config.json``.  Model files hold each
+parameter's dim-0 shard (the FSDP2 ``Shard(0)`` placement, recorded in the file), so a checkpoint
+can be re-loaded at a different world size.
+"""
+
+from __future__ import annotations
+
+import json
+import math
+import os
+from typing import Callable, Iterable, Optional
+
+import torch
+import torch.nn as nn
+
+from verl_omni_b200.parallel import dist as D
+from verl_omni_b200.ops._ext import ext
+
+_ALIGN = 128
+
+
+def _dtype(name: str) -> torch.dtype:
+    return {"bfloat16": torch.bfloat16, "bf16": torch.bfloat16, "float32": torch.float32, "fp32": torch.float32,
+            "float16": torch.float16}[name]
+
+
+class FlatParams:
+    """Packs the trainable parameters of ``module`` into one flat buffer + fp32 grad buffer."""
+
+    def __init__(self, module: nn.Module, dtype: torch.dtype, device: torch.device, world: int, rank: int,
+                 group=None):
+        self.module = module
+        self.group = group
+        self.world, self.rank = world, rank
+        self.names, self.params = [], []
+        for n, p in module.named_parameters():
+            if p.requires_grad:
+                self.names.append(n)
+                self.params.append(p)
+        self.shapes = [tuple(p.shape) for p in self.params]
+        self.numels = [p.numel() for p in self.params]
+        self.offsets = []
+        off = 0
+        for n in self.numels:
+            self.offsets.append(off)
+            off += n
+        self.numel = off
+        unit = world * _ALIGN
+        self.padded = max(unit, (off + unit - 1) // unit * unit)
+        self.shard_size = self.padded // world
+        self.shard_lo = rank * self.shard_size
+        self.device, self.dtype = device, dtype
+        self.flat = torch.zeros(self.padded, dtype=dtype, device=device)
+        self.main_grad = torch.zeros(self.padded, dtype=torch.float32, device=device)
+        master_full = torch.zeros(self.padded, dtype=torch.float32, device=device)
+        for p, o, n in zip(self.params, self.offsets, self.numels):
+            src = p.detach().reshape(-1).to(device=device, dtype=torch.float32)
+            master_full[o:o + n].copy_(src)
+        self.flat.copy_(master_full.to(dtype))
+        self.master = master_full[self.shard_lo:self.shard_lo + self.shard_size].clone()
+        del master_full
+        self.exp_avg = torch.zeros_like(self.master)
+        self.exp_avg_sq = torch.zeros_like(self.master)
+        self.grad_shard = torch.zeros_like(self.master)
+        for p, o, n, s in zip(self.params, self.offsets, self.numels, self.shapes):
+            p.data = self.flat[o:o + n].view(s)
+            p.main_grad = self.main_grad[o:o + n].view(s)
+            p.register_post_accumulate_grad_hook(self._accumulate)
+        # non-trainable parameters and buffers follow the compute dtype/device
+        for m in module.modules():
+            for k, p in list(m._parameters.items()):
+                if p is not None and not p.requires_grad:
+                    p.data = p.data.to(device=device, dtype=dtype if p.is_floating_point() else p.dtype)
+            for k, b in list(m._buffers.items()):
+                if b is not None:
+                    m._buffers[k] = b.to(device=device)
+
+    @staticmethod
+    def _accumulate(p: torch.Tensor) -> None:
+        if p.grad is not None:
+            p.main_grad.add_(p.grad.view_as(p.main_grad))
+            p.grad = None
+
+    def zero_grad(self) -> None:
+        self.main_grad.zero_()
+
+    def shard_view(self) -> torch.Tensor:
+        return self.flat[self.shard_lo:self.shard_lo + self.shard_size]
+
+    def full_master(self) -> torch.Tensor:
+        full = torch.empty(self.padded, dtype=torch.float32, device=self.device)
+        D.all_gather_into(full, self.master, self.group)
+        return full
+
+    def param_views(self, flat: torch.Tensor) -> Iterable[tuple[str, torch.Tensor]]:
+        for n, o, k, s in zip(self.names, self.offsets, self.numels, self.shapes):
+            yield n, flat[o:o + k].view(s)
+
+
+class LRSchedule:
+    """Constant or cosine schedule with linear warm-up (reference ``diffusers_impl.py:412-443``)."""
+
+    def __init__(self, optim_cfg, total_steps: int):
+        self.base = float(optim_cfg.lr)
+        self.kind = optim_cfg.lr_scheduler_type
+        total = optim_cfg.total_training_steps if optim_cfg.total_training_steps > 0 else total_steps
+        self.total = max(1, int(total))
+        warm = optim_cfg.lr_warmup_steps
+        if warm is None or warm < 0:
+            warm = int(optim_cfg.lr_warmup_steps_ratio * self.total)
+        self.warmup = warm
+        self.min_ratio = optim_cfg.min_lr_ratio
+        self.cycles = optim_cfg.num_cycles
+        self.step_count = 0
+
+    def lr(self) -> float:
+        s = self.step_count
+        if self.warmup > 0 and s < self.warmup:
+            return self.base * (s + 1) / self.warmup
+        if self.kind == "constant":
+            return self.base
+        prog = (s - self.warmup) / max(1, self.total - self.warmup)
+        cos = 0.5 * (1.0 + math.cos(math.pi * 2.0 * self.cycles * prog))
+        return self.base * (self.min_ratio + (1 - self.min_ratio) * cos)
+
+    def step(self) -> None:
+        self.step_count += 1
+
+    def state_dict(self) -> dict:
+        return {"step_count": self.step_count}
+
+    def load_state_dict(self, sd: dict) -> None:
+        self.step_count = int(sd["step_count"])
+
+
+class ShardedEngine:
+    """Owns a module, its flat parameters and the sharded AdamW state."""
+
+    def __init__(self, module: nn.Module, actor_cfg, *, device: torch.device, group=None, total_steps: int = 1,
+                 trainable: bool = True):
+        self.cfg = actor_cfg
+        self.group = group
+        self.world = D.world_size(group)
+        self.rank = D.rank(group)
+        self.device = device
+        self.dtype = _dtype(actor_cfg.fsdp_config.dtype) if device.type == "cuda" else torch.float32
+        self.module = module
+        self.trainable = trainable
+        if not trainable:
+            for p in module.parameters():
+                p.requires_grad_(False)
+            module.to(device=device, dtype=self.dtype)
+            self.flat = None
+        else:
+            self.flat = FlatParams(module, self.dtype, device, self.world, self.rank, group)
+        self.opt_step = 0
+        self.sched = LRSchedule(actor_cfg.optim, total_steps) if trainable else None
+        self.last_grad_norm = None
+
+    # ------------------------------------------------------------------ modes
+    def train_mode(self):
+        self.module.train()
+        return self
+
+    def eval_mode(self):
+        self.module.eval()
+        return self
+
+    def zero_grad(self) -> None:
+        if self.flat is not None:
+            self.flat.zero_grad()
+
+    # ------------------------------------------------------------------ optimizer
+    def optimizer_step(self) -> torch.Tensor:
+        """Reduce-scatter grads, clip by global norm, AdamW on the shard, all-gather bf16 weights.
+
+        Returns the global grad norm as a device scalar (non-finite -> the update is skipped on device).
+        """
+        fp = self.flat
+        oc = self.cfg.optim
+        D.reduce_scatter_into(fp.grad_shard, fp.main_grad, self.group)
+        if self.world > 1:
+            fp.grad_shard.mul_(1.0 / self.world)
+        self.opt_step += 1
+        lr = self.sched.lr()
+        b1, b2 = float(oc.betas[0]), float(oc.betas[1])
+        max_norm = float(self.cfg.grad_clip if self.cfg.grad_clip is not None else oc.clip_grad)
+        if fp.master.is_cuda:
+            sq = ext().sq_norm(fp.grad_shard)
+            D.all_reduce(sq, group=self.group)
+            ext().adamw_flat(fp.master, fp.grad_shard, fp.exp_avg, fp.exp_avg_sq, fp.shard_view(), lr, b1, b2,
+                             float(oc.eps), float(oc.weight_decay), self.opt_step, max_norm, sq, 1.0)
+        else:
+            sq = (fp.grad_shard.double() ** 2).sum().float().reshape(1)
+            D.all_reduce(sq, group=self.group)
+            norm = float(sq.sqrt())
+            if math.isfinite(norm):
+                coef = min(1.0, max_norm / (norm + 1e-6)) if max_norm > 0 else 1.0
+                _adamw_torch(fp.master, fp.grad_shard * coef, fp.exp_avg, fp.exp_avg_sq, lr, b1, b2, float(oc.eps),
+                             float(oc.weight_decay), self.opt_step)
+                fp.shard_view().copy_(fp.master.to(fp.dtype))
+        D.all_gather_into(fp.flat, fp.shard_view().clone() if self.world > 1 else fp.shard_view(), self.group)
+        self.sched.step()
+        fp.zero_grad()
+        self.last_grad_norm = sq.sqrt()
+        return self.last_grad_norm
+
+    def lr(self) -> float:
+        return self.sched.lr() if self.sched is not None else 0.0
+
+    # ------------------------------------------------------------------ weights
+    def get_per_tensor_param(self) -> Iterable[tuple[str, torch.Tensor]]:
+        """(name, bf16 full tensor) pairs for the rollout engine (already replicated: no gather)."""
+        return self.flat.param_views(self.flat.flat)
+
+    def load_full_state(self, state: dict) -> None:
+        """Load full fp32/bf16 tensors by name into master shards and the compute buffer."""
+        fp = self.flat
+        full = torch.zeros(fp.padded, dtype=torch.float32, device=self.device)
+        for n, o, k in zip(fp.names, fp.offsets, fp.numels):
+            if n in state:
+                full[o:o + k].copy_(state[n].reshape(-1).to(full.device, torch.float32))
+            else:
+                full[o:o + k].copy_(fp.flat[o:o + k].float())
+        fp.master.copy_(full[fp.shard_lo:fp.shard_lo + fp.shard_size])
+        fp.flat.copy_(full.to(fp.dtype))
+
+    # ------------------------------------------------------------------ checkpoints
+    def save_checkpoint(self, local_path: str, global_step: int = 0, save_contents=("model", "optimizer", "extra"),
+                        hf_export: bool = False) -> None:
+        os.makedirs(local_path, exist_ok=True)
+        W, r = self.world, self.rank
+        fp = self.flat
+        if "model" in save_contents:
+            full = fp.full_master()
+            shards = {}
+            for n, view in fp.param_views(full):
+                rows = view.shape[0] if view.ndim else 1
+                per = (rows + W - 1) // W
+                shards[n] = view[r * per:(r + 1) * per].detach().cpu().clone() if view.ndim else view.detach().cpu()
+            torch.save({"params": shards, "placements": {"type": "Shard", "dim": 0}, "world_size": W},
+                       os.path.join(local_path, f"model_world_size_{W}_rank_{r}.pt"))
+            if hf_export and r == 0:
+                from safetensors.torch import save_file
+
+                os.makedirs(os.path.join(local_path, "huggingface"), exist_ok=True)
+                save_file({n: v.to(torch.bfloat16).contiguous().cpu() for n, v in fp.param_views(full)},
+                          os.path.join(local_path, "huggingface", "diffusion_pytorch_model.safetensors"))
+            del full
+        if "optimizer" in save_contents:
+            torch.save({"exp_avg": fp.exp_avg.cpu(), "exp_avg_sq": fp.exp_avg_sq.cpu(), "step": self.opt_step,
+                        "padded": fp.padded, "world_size": W},
+                       os.path.join(local_path, f"optim_world_size_{W}_rank_{r}.pt"))
+        if "extra" in save_contents:
+            torch.save({"lr_scheduler": self.sched.state_dict(), "global_step": global_step,
+                        "rng": torch.get_rng_state(),
+                        "cuda_rng": torch.cuda.get_rng_state() if torch.cuda.is_available() else None},
+                       os.path.join(local_path, f"extra_state_world_size_{W}_rank_{r}.pt"))
+        if r == 0:
+            with open(os.path.join(local_path, "fsdp_config.json"), "w") as f:
+                json.dump({"FSDP_version": 2, "world_size": W, "layout": "flat-shard-adamw"}, f)
+        D.barrier(self.group)
+
+    def load_checkpoint(self, local_path: str, load_contents=("model", "optimizer", "extra")) -> dict:
+        with open(os.path.join(local_path, "fsdp_config.json")) as f:
+            meta = json.load(f)
+        Wsaved = int(meta["world_size"])
+        fp = self.flat
+        info: dict = {}
+        if "model" in load_contents:
+            parts = [torch.load(os.path.join(local_path, f"model_world_size_{Wsaved}_rank_{i}.pt"), map_location="cpu")
+                     for i in range(Wsaved)]
+            state = {}
+            for n in fp.names:
+                pieces = [p["params"][n] for p in parts]
+                state[n] = torch.cat(pieces, 0) if pieces[0].ndim else pieces[0]
+            self.load_full_state(state)
+        if "optimizer" in load_contents:
+            if Wsaved == self.world:
+                o = torch.load(os.path.join(local_path, f"optim_world_size_{Wsaved}_rank_{self.rank}.pt"),
+                               map_location="cpu")
+                fp.exp_avg.copy_(o["exp_avg"].to(self.device))
+                fp.exp_avg_sq.copy_(o["exp_avg_sq"].to(self.device))
+                self.opt_step = int(o["step"])
+            else:  # re-shard the moments through the full flat layout
+                full_m, full_v = [], []
+                for i in range(Wsaved):
+                    o = torch.load(os.path.join(local_path, f"optim_world_size_{Wsaved}_rank_{i}.pt"),
+                                   map_location="cpu")
+                    full_m.append(o["exp_avg"])
+                    full_v.append(o["exp_avg_sq"])
+                    self.opt_step = int(o["step"])
+                m, v = torch.cat(full_m), torch.cat(full_v)
+                lo, n = fp.shard_lo, fp.shard_size
+                fp.exp_avg.zero_()
+                fp.exp_avg_sq.zero_()
+                k = max(0, min(n, fp.numel - lo, m.numel() - lo))
+                if k > 0:
+                    fp.exp_avg[:k].copy_(m[lo:lo + k].to(self.device))
+                    fp.exp_avg_sq[:k].copy_(v[lo:lo + k].to(self.device))
+        if "extra" in load_contents:
+            r = self.rank if Wsaved == self.world else 0
+            e = torch.load(os.path.join(local_path, f"extra_state_world_size_{Wsaved}_rank_{r}.pt"),
+                           map_location="cpu", weights_only=False)
+            self.sched.load_state_dict(e["lr_scheduler"])
+            info["global_step"] = e.get("global_step", 0)
+        D.barrier(self.group)
+        return info
+
+
+def _adamw_torch(p, g, m, v, lr, b1, b2, eps, wd, step):
+    p.mul_(1 - lr * wd)
+    m.mul_(b1).add_(g, alpha=1 - b1)
+    v.mul_(b2).addcmul_(g, g, value=1 - b2)
+    bc1 = 1 - b1 ** step
+    bc2 = 1 - b2 ** step
+    denom = (v.sqrt() / math.sqrt(bc2)).add_(eps)
+    p.addcdiv_(m, denom, value=-lr / bc1)

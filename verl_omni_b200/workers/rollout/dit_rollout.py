@@ -1,0 +1,193 @@
+"""In-process DiT rollout engine (replaces the vLLM-Omni diffusion server of the reference).
+
+For a batch of requests it runs the reverse-SDE denoising loop on the current policy weights
+(shared with the trainer when colocated), recording the fp32 trajectory inside the SDE window,
+per-step log-probs and timesteps -- the ``DiffusionOutput`` contract of
+``verl_omni/workers/rollout/replica.py:20`` / ``vllm_omni_async_server.py:638-778``:
+
+* request batching: requests are packed into forward batches of at most ``max_num_seqs``
+  (cond+uncond counted twice under CFG);
+* per-request seeds: the Gaussian draw of row ``i`` at step ``t`` comes from Philox keyed by
+  ``(seed, i, t)`` inside the fused SDE kernel, so a rollout is reproducible from its seed;
+* SDE window: steps outside ``[w0, w0+W)`` take the deterministic ODE update (noise 0) and are not
+  recorded (FlowGRPO fast / MixGRPO windows, ``verl_omni/pipelines/request_batch.py:32-56``);
+* sleep / wake: activations and cached buffers are dropped between rollouts (``free_cache_engine``);
+* abort: ``abort()`` makes the running ``generate`` return the finished requests plus synthesized
+  aborted outputs (``vllm_omni_async_server.py:790-941``).
+"""
+
+from __future__ import annotations
+
+import threading
+from dataclasses import dataclass, field
+from typing import Callable, Optional
+
+import numpy as np
+import torch
+
+from verl_omni_b200.pipelines.model_base import DiffusionModelBase
+from verl_omni_b200.utils.dataproto import DataProto
+
+
+def select_sde_window(algo_cfg, T: int, global_step: int, seed: int = 0) -> tuple[int, int]:
+    """(start, size) of the SDE window; whole schedule when ``sde_window_size`` is unset.
+
+    ``random``: start drawn uniformly from ``sde_window_range`` (default ``[0, T-W]``) with a seeded
+    generator; ``progressive`` (MixGRPO): the window slides by one step every ``iters_per_group``
+    optimizer steps and wraps around.
+    """
+    W = algo_cfg.sde_window_size
+    if not W:
+        return 0, T
+    W = min(int(W), T)
+    lo, hi = 0, T - W
+    if algo_cfg.sde_window_range:
+        lo, hi = int(algo_cfg.sde_window_range[0]), min(int(algo_cfg.sde_window_range[1]), T - W)
+    if algo_cfg.sample_strategy == "progressive":
+        span = hi - lo + 1
+        return lo + (global_step // max(1, algo_cfg.iters_per_group)) % span, W
+    g = np.random.default_rng(int(algo_cfg.sde_window_seed) * 1_000_003 + int(seed) * 7919 + global_step)
+    return int(g.integers(lo, hi + 1)), W
+
+
+@dataclass
+class RolloutRequest:
+    cond: dict
+    neg_cond: Optional[dict] = None
+    seed: int = 0
+
+
+class DiTRolloutEngine:
+    def __init__(self, module, adapter: type[DiffusionModelBase], rollout_cfg, model_cfg, *, device,
+                 latent_shape: tuple, decoder: Optional[Callable] = None):
+        self.module = module
+        self.adapter = adapter
+        self.cfg = rollout_cfg
+        self.model_cfg = model_cfg
+        self.device = device
+        self.latent_shape = tuple(latent_shape)
+        self.decoder = decoder
+        T = rollout_cfg.pipeline.num_inference_steps
+        seq = int(np.prod(self.latent_shape[-2:])) // 4
+        self.scheduler = adapter.build_scheduler(T, image_seq_len=seq, device=device)
+        self._abort = threading.Event()
+        self.sleeping = False
+
+    # ------------------------------------------------------------------ lifecycle
+    def sleep(self) -> None:
+        self.sleeping = True
+        if self.cfg.free_cache_engine and torch.cuda.is_available():
+            torch.cuda.empty_cache()
+
+    def wake_up(self) -> None:
+        self.sleeping = False
+
+    def abort(self) -> None:
+        self._abort.set()
+
+    def update_weights(self, named_tensors) -> int:
+        """Load (name, tensor) pairs into the rollout module; returns bytes copied.
+
+        Colocated engines share parameter storage with the trainer, so tensors that already alias
+        the module's parameters are skipped (zero-copy)."""
+        params = dict(self.module.named_parameters())
+        n = 0
+        with torch.no_grad():
+            for name, t in named_tensors:
+                p = params.get(name)
+                if p is None or p.data_ptr() == t.data_ptr():
+                    continue
+                p.copy_(t)
+                n += t.numel() * t.element_size()
+        return n
+
+    # ------------------------------------------------------------------ generate
+    @torch.no_grad()
+    def generate(self, batch: DataProto, *, seed: int = 0, global_step: int = 0, record_logprobs: bool = True,
+                 decode: bool = True) -> DataProto:
+        """``batch`` holds the conditioning tensors (adapter ``cond_keys``, optional ``negative_*``)."""
+        if self.sleeping:
+            self.wake_up()
+        self._abort.clear()
+        cfg, algo = self.cfg, self.cfg.algo
+        T = cfg.pipeline.num_inference_steps
+        w0, W = select_sde_window(algo, T, global_step, seed)
+        B = len(batch)
+        guidance = cfg.pipeline.guidance_scale
+        cfg_mult = 2 if (guidance is not None and guidance > 1.0) else 1
+        mbs = max(1, min(B, cfg.max_num_seqs // cfg_mult))
+        sched = self.scheduler
+        sig = sched.sigmas
+        chunks = []
+        for s in range(0, B, mbs):
+            if self._abort.is_set():
+                break
+            mb = batch.select_idxs(slice(s, min(B, s + mbs)))
+            chunks.append(self._run_chunk(mb, T, w0, W, seed * 1_000_003 + s, guidance, record_logprobs))
+        done = sum(len(c) for c in chunks)
+        out = DataProto.concat(chunks) if chunks else DataProto()
+        if done < B:  # aborted: synthesize aborted outputs for the unfinished requests
+            rest = B - done
+            abort = {k: torch.zeros((rest,) + v.shape[1:], dtype=v.dtype, device=v.device)
+                     for k, v in (out.batch.items() if chunks else [])}
+            out = DataProto.concat([out, DataProto(abort)]) if chunks else DataProto()
+            out.meta_info["aborted"] = np.array([False] * done + [True] * rest)
+        if decode and self.decoder is not None and len(out):
+            out.batch["images"] = self.decode(out.batch["final_latents"])
+        out.meta_info.update({"sde_window": (w0, W), "num_inference_steps": T})
+        return out
+
+    def decode(self, latents: torch.Tensor, chunk: int = 8) -> torch.Tensor:
+        imgs = [self.decoder(latents[i:i + chunk]) for i in range(0, latents.shape[0], chunk)]
+        return torch.cat(imgs, 0)
+
+    def _run_chunk(self, mb: DataProto, T: int, w0: int, W: int, seed: int, guidance, record: bool) -> DataProto:
+        algo = self.cfg.algo
+        keys = self.adapter.cond_keys()
+        cond = {k: mb.batch[k].to(self.device) for k in keys}
+        neg = None
+        if guidance is not None and guidance > 1.0 and ("negative_" + keys[0]) in mb.batch:
+            neg = {k: mb.batch["negative_" + k].to(self.device) for k in keys}
+        b = len(mb)
+        x = self._initial_noise(b, seed)
+        sched = self.scheduler
+        traj = [x] if w0 == 0 else []
+        logps, steps = [], []
+        for t in range(T):
+            tt = sched.timesteps[t].expand(b).to(self.device)
+            v = self.adapter.predict(self.module, x, tt, cond, neg, guidance)
+            in_window = w0 <= t < w0 + W
+            nl = algo.noise_level if in_window else 0.0
+            out = sched.sample_previous_step(x.float(), v.float(), step_index=t, noise_level=nl,
+                                             sde_type=algo.sde_type if in_window else "sde",
+                                             seed=seed, noise_offset=t, return_logprobs=in_window and record)
+            if not in_window:
+                x = out.prev_sample_mean
+            else:
+                x = out.prev_sample
+            if in_window:
+                if record:
+                    logps.append(out.log_prob)
+                steps.append(t)
+                traj.append(x)
+            elif t + 1 == w0:
+                traj.append(x)
+        res = {
+            "latents": torch.stack(traj, 1),  # [b, W+1, ...] fp32
+            "step_index": torch.tensor(steps, device=self.device).expand(b, W).contiguous(),
+            "timesteps": sched.timesteps.to(self.device)[torch.tensor(steps, device=self.device)].expand(b, W).contiguous(),
+            "final_latents": x,
+        }
+        if record:
+            res["rollout_log_probs"] = torch.stack(logps, 1)
+        for k, v in cond.items():
+            res[k] = v
+        if neg is not None:
+            for k, v in neg.items():
+                res["negative_" + k] = v
+        return DataProto(res)
+
+    def _initial_noise(self, b: int, seed: int) -> torch.Tensor:
+        g = torch.Generator(device="cpu")
+        g.manual_seed(int(seed) & 0x7FFFFFFFFFFFFFFF)
+        return torch.randn((b,) + self.latent_shape, generator=g).to(self.device)
