@@ -1,0 +1,229 @@
+"""FlowGRPO step benchmark: SD3.5-Medium-shaped MMDiT, rollout + reward + train, samples/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+    torchrun --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P bench.py --gpus N ...
+
+Workload (per GPU, weak scaling -- the 8-GPU run is exactly 48 prompts x group 16):
+6 prompts x group 16 = 96 samples; 16x64x64 latents (1024 image tokens) + 333 text tokens
+(256 T5-style + 77 CLIP-style random embeddings, dim 4096) + pooled 2048-d embedding; 10 SDE
+steps (sde, noise 0.7) all trained; random-init frozen VAE decoder -> 512^2 images -> random-init
+ViT-B/16 scorer; GRPO advantages; old-log-prob recompute; full fine-tune AdamW (lr 1e-5,
+clip 1.0), one optimizer step per FlowGRPO step.  Random-init weights, synthetic data.
+
+Timing: W untimed warm-up steps; K steps bracketed by barrier + cuda.synchronize, CUDA events
+on the launching stream, max over ranks.  The end-to-end number repeats K steps through the
+public trainer API with the prompt inputs copied each step from pinned host memory and the
+step's metrics read back to the host.  Inputs (weights, activations, trajectories) are far larger
+than the 126 MB L2, so no explicit flush is used.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+METRIC = "FlowGRPO step time & samples/sec (rollout+train) at 1/2/4/8 B200, max over ranks"
+PROMPTS_PER_GPU = 6
+GROUP = 16
+
+
+def _clock_sampler(path: str):
+    try:
+        return subprocess.Popen(
+            ["nvidia-smi", "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+             "--format=csv,noheader,nounits", "-lms", "200"],
+            stdout=open(path, "w"), stderr=subprocess.DEVNULL)
+    except Exception:  # noqa: BLE001
+        return None
+
+
+def _clock_summary(path: str) -> dict:
+    sm, mx, reasons = [], [], set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    try:
+        for line in open(path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+    except OSError:
+        pass
+    if not sm:
+        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+    return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons)}
+
+
+def reference_arm(args) -> None:
+    ref = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
+    why = None
+    if not os.path.isdir(os.path.join(ref, "verl_omni")):
+        why = "reference not installed under baseline/_ref"
+    else:
+        sys.path.insert(0, ref)
+        try:
+            import verl_omni.trainer.main_diffusion  # noqa: F401
+        except Exception as e:  # noqa: BLE001
+            why = (f"reference installed (pip --no-deps) but its runtime dependencies are absent offline: "
+                   f"{type(e).__name__}: {e}".replace("\n", " "))
+    if why is None:
+        why = "reference importable but its trainer needs Ray + vLLM-Omni servers, unavailable offline"
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+
+
+class _PinnedOnce:
+    """Serves one pre-pinned host batch through the dataset interface (end-to-end input path)."""
+
+    def __init__(self, ds, host):
+        self.ds, self.host = ds, host
+
+    def get_batch(self, ids):
+        return self.host
+
+    def __getattr__(self, k):
+        return getattr(self.ds, k)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--arch", default="sd35_medium")
+    ap.add_argument("--prompts-per-gpu", type=int, default=PROMPTS_PER_GPU)
+    ap.add_argument("--group", type=int, default=GROUP)
+    ap.add_argument("--sde-steps", type=int, default=10)
+    ap.add_argument("--micro", type=int, default=16)
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from verl_omni_b200.ops._ext import ext
+    from verl_omni_b200.parallel import dist as D
+    from verl_omni_b200.trainer.diffusion.flow_grpo_trainer import PolicyGradientTrainer
+    from verl_omni_b200.utils.config import load_config
+
+    info = D.init_distributed(device="cuda", timeout_s=1800)
+    N = D.world_size()
+    assert N == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={N}"
+    prompts = args.prompts_per_gpu * N
+    ov = [
+        "trainer.device=cuda", f"actor_rollout_ref.model.architecture={args.arch}",
+        f"data.train_batch_size={prompts}", f"actor_rollout_ref.rollout.n={args.group}",
+        f"actor_rollout_ref.rollout.pipeline.num_inference_steps={args.sde_steps}",
+        "actor_rollout_ref.rollout.algo.noise_level=0.7", "actor_rollout_ref.rollout.algo.sde_type=sde",
+        "actor_rollout_ref.rollout.max_num_seqs=48",
+        f"actor_rollout_ref.actor.ppo_mini_batch_size={prompts}",
+        f"actor_rollout_ref.actor.ppo_micro_batch_size_per_gpu={args.micro}",
+        "actor_rollout_ref.actor.optim.lr=1e-5", "actor_rollout_ref.actor.optim.weight_decay=0.0",
+        "trainer.total_training_steps=1000", "trainer.resume_mode=disable", "trainer.logger=[]",
+        "trainer.save_freq=-1",
+    ]
+    cfg = load_config("diffusion_trainer", ov)
+    trainer = PolicyGradientTrainer(cfg)
+    dev = info.device
+    n_params = sum(p.numel() for p in trainer.actor.module.parameters())
+
+    def barrier_sync():
+        D.barrier()
+        torch.cuda.synchronize()
+
+    t_warm = time.perf_counter()
+    for _ in range(args.warmup):
+        m = trainer.step()
+    t_warm = time.perf_counter() - t_warm
+    if info.rank == 0:
+        print(json.dumps({"warmup_s": round(t_warm, 2), "timing": {k: round(v, 3) for k, v in m.items()
+                                                                   if k.startswith("timing_s/")}}),
+              file=sys.stderr, flush=True)
+    # ----------------------------------------------------------- device-timed region
+    clock_path = os.path.join(os.environ.get("VO_BENCH_DIR", "/tmp"), f"clocks_{info.rank}.csv")
+    sampler = _clock_sampler(clock_path) if info.local_rank == 0 else None
+    barrier_sync()
+    launches0 = ext().launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        m = trainer.step()
+    ev1.record()
+    barrier_sync()
+    launches = ext().launch_count() - launches0
+    dev_ms = ev0.elapsed_time(ev1)
+    if sampler is not None:
+        sampler.terminate()
+        sampler.wait()
+    t = torch.tensor([dev_ms], dtype=torch.float64, device=dev)
+    if N > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dev_ms = float(t.item())
+    ms_per_step = dev_ms / args.steps
+    samples_per_step = prompts * args.group
+    value = samples_per_step / (ms_per_step / 1000.0)
+    timing = {k: round(v, 3) for k, v in m.items() if k.startswith("timing_s/")}
+    # ----------------------------------------------------------- end-to-end through the public API
+    e2e = None
+    if not args.no_e2e:
+        ds = trainer.dataset
+        h2d = d2h = 0
+        barrier_sync()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            ids = trainer.sampler.next_batch()
+            host = ds.get_batch(trainer.local_prompt_ids(ids))
+            for k in list(host.batch):
+                host.batch[k] = host.batch[k].pin_memory()
+                h2d += host.batch[k].numel() * host.batch[k].element_size()
+            trainer.dataset = _PinnedOnce(ds, host)
+            m = trainer.step(ids)
+            trainer.dataset = ds
+            d2h += 4 * len([v for v in m.values() if isinstance(v, float)])
+        barrier_sync()
+        wall = time.perf_counter() - t0
+        w = torch.tensor([wall], dtype=torch.float64, device=dev)
+        if N > 1:
+            dist.all_reduce(w, op=dist.ReduceOp.MAX)
+        wall = float(w.item())
+        e2e = {"value": round(samples_per_step * args.steps / wall, 4), "unit": "samples/s",
+               "h2d_bytes_per_step": h2d // args.steps, "d2h_bytes_per_step": d2h // args.steps,
+               "ms_per_step": round(1000.0 * wall / args.steps, 2)}
+    clocks = _clock_summary(clock_path) if info.local_rank == 0 else None
+    if info.rank == 0:
+        out = {
+            "metric": METRIC, "value": round(value, 4), "unit": "samples/s", "n_gpus": N, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random prompt embeddings / latents, random-init weights)",
+            "config": {"model": f"SD3.5-Medium-shaped MMDiT ({n_params / 1e9:.2f}B params, 24 joint blocks, "
+                                "hidden 1536, 24 heads, patch 2, 16-ch latents)",
+                       "global_batch": samples_per_step, "prompts": prompts, "group": args.group,
+                       "seq_len": 1024 + 333, "sde_steps": args.sde_steps, "parallelism": f"dp{N}",
+                       "reward": "random-init VAE decoder 512^2 + ViT-B/16 scorer",
+                       "l2": "inputs larger than L2 (no flush)"},
+            "impl": "native", "gpu_launches": launches, "clocks": clocks, "e2e": e2e, "phase_s": timing,
+        }
+        print(json.dumps(out), flush=True)
+    D.destroy()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,62 @@
+"""tcgen05 flash attention against an fp32 torch reference."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+CASES = [(2, 3, 333, 333, 64, False), (1, 2, 1357, 1357, 64, False), (2, 2, 200, 200, 128, False),
+         (1, 2, 300, 300, 64, True), (2, 2, 100, 77, 64, False), (1, 1, 1024, 1024, 128, True)]
+
+
+@pytest.fixture(scope="module")
+def E():
+    from verl_omni_b200.ops._ext import ext
+
+    e = ext()
+    e.fmha_error(True)
+    yield e
+    assert e.fmha_error(True) == 0, "FMHA kernel reported a barrier timeout"
+
+
+def _ref(q, k, v, causal, scale):
+    s = (q.float() @ k.float().transpose(-1, -2)) * scale
+    if causal:
+        Sq, Sk = s.shape[-2:]
+        mask = torch.ones(Sq, Sk, dtype=torch.bool, device=s.device).tril()
+        s = s.masked_fill(~mask, float("-inf"))
+    lse = torch.logsumexp(s, -1)
+    o = torch.softmax(s, -1) @ v.float()
+    return o, lse
+
+
+@pytest.mark.parametrize("B,H,Sq,Skv,D,causal", CASES)
+def test_fmha_fwd(E, B, H, Sq, Skv, D, causal):
+    torch.manual_seed(0)
+    q = torch.randn(B, H, Sq, D, device="cuda").bfloat16()
+    k = torch.randn(B, H, Skv, D, device="cuda").bfloat16()
+    v = torch.randn(B, H, Skv, D, device="cuda").bfloat16()
+    scale = 1 / math.sqrt(D)
+    o, lse = E.fmha_fwd(q, k, v, causal, scale)
+    ro, rlse = _ref(q, k, v, causal, scale)
+    torch.testing.assert_close(o.float(), ro.transpose(1, 2), rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(lse, rlse, rtol=1e-3, atol=1e-3)
+
+
+def test_attention_op_autograd():
+    from verl_omni_b200.ops.attention import attention
+
+    torch.manual_seed(1)
+    B, H, S, D = 2, 4, 257, 64
+    q, k, v = (torch.randn(B, H, S, D, device="cuda").bfloat16().requires_grad_(True) for _ in range(3))
+    o = attention(q, k, v)
+    g = torch.randn_like(o)
+    o.backward(g)
+    qr, kr, vr = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+    orf = torch.nn.functional.scaled_dot_product_attention(qr, kr, vr).transpose(1, 2).reshape(B, S, H * D)
+    orf.backward(g.float())
+    torch.testing.assert_close(o.float(), orf, rtol=2e-2, atol=2e-2)
+    for a, b in ((q, qr), (k, kr), (v, vr)):
+        torch.testing.assert_close(a.grad.float(), b.grad, rtol=5e-2, atol=5e-2)

@@ -1,0 +1,95 @@
+"""tcgen05 GEMM (forward / dgrad / wgrad + fused epilogues) against fp32 torch references."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(128, 256, 64), (333, 776, 200), (1000, 1536, 1536), (4096, 512, 4096)]
+
+
+@pytest.fixture(scope="module")
+def E():
+    from verl_omni_b200.ops._ext import ext
+
+    e = ext()
+    e.gemm_error(True)
+    yield e
+    assert e.gemm_error(True) == 0, "GEMM kernel reported a barrier timeout"
+
+
+def _rel(a, b):
+    return float((a.float() - b.float()).norm() / (b.float().norm() + 1e-6))
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_gemm_fwd_bias(E, M, N, K):
+    torch.manual_seed(0)
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    w = (torch.randn(N, K, device="cuda") / K ** 0.5).bfloat16()
+    b = torch.randn(N, device="cuda").bfloat16()
+    out, _ = E.gemm_fwd(x, w, b, 1, None, None, 1)
+    ref = x.float() @ w.float().t() + b.float()
+    assert _rel(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES[:3])
+def test_gemm_fwd_gelu_and_gate_res(E, M, N, K):
+    torch.manual_seed(1)
+    S = M // 2 if M % 2 == 0 else M
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    w = (torch.randn(N, K, device="cuda") / K ** 0.5).bfloat16()
+    b = torch.randn(N, device="cuda").bfloat16()
+    out, pre = E.gemm_fwd(x, w, b, 2, None, None, 1)
+    lin = x.float() @ w.float().t() + b.float()
+    assert _rel(pre, lin) < 1e-2
+    assert _rel(out, torch.nn.functional.gelu(lin, approximate="tanh")) < 2e-2
+    B = M // S
+    gate = torch.randn(B, N, device="cuda").bfloat16()
+    res = torch.randn(M, N, device="cuda").bfloat16()
+    out, lin2 = E.gemm_fwd(x, w, b, 3, gate, res, S)
+    ref = res.float() + (lin.view(B, S, N) * gate.float()[:, None]).view(M, N)
+    assert _rel(lin2, lin) < 1e-2
+    assert _rel(out, ref) < 2e-2
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_gemm_dgrad(E, M, N, K):
+    torch.manual_seed(2)
+    dy = torch.randn(M, N, device="cuda").bfloat16()
+    w = (torch.randn(N, K, device="cuda") / N ** 0.5).bfloat16()
+    dx = E.gemm_dgrad(dy, w)
+    assert _rel(dx, dy.float() @ w.float()) < 1e-2
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("accumulate", [False, True])
+def test_gemm_wgrad(E, M, N, K, accumulate):
+    torch.manual_seed(3)
+    dy = torch.randn(M, N, device="cuda").bfloat16()
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    out = torch.randn(N, K, device="cuda") if accumulate else torch.empty(N, K, device="cuda")
+    base = out.clone()
+    E.gemm_wgrad(dy, x, out, accumulate)
+    ref = dy.float().t() @ x.float() + (base if accumulate else 0)
+    assert _rel(out, ref) < 1e-2
+
+
+def test_linear_layer_autograd_native_vs_torch():
+    from verl_omni_b200.ops import linear as L
+
+    torch.manual_seed(4)
+    x = torch.randn(2, 300, 512, device="cuda").bfloat16().requires_grad_(True)
+    w = (torch.randn(768, 512, device="cuda") / 512 ** 0.5).bfloat16().requires_grad_(True)
+    b = torch.zeros(768, device="cuda").bfloat16().requires_grad_(True)
+    w.main_grad = torch.zeros(768, 512, device="cuda")
+    y = L.linear(x, w, b, epilogue="gelu")
+    g = torch.randn_like(y)
+    y.backward(g)
+    xr = x.detach().float().requires_grad_(True)
+    wr = w.detach().float().requires_grad_(True)
+    yr = torch.nn.functional.gelu(xr @ wr.t(), approximate="tanh")
+    yr.backward(g.float())
+    assert _rel(y, yr) < 2e-2
+    assert _rel(x.grad, xr.grad) < 3e-2
+    assert w.grad is None and _rel(w.main_grad, wr.grad) < 3e-2

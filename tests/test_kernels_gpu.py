@@ -1,0 +1,208 @@
+"""sm_100a kernel numerics against fp32 torch references of the same op (B200 only)."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _ext():
+    from verl_omni_b200.ops._ext import ext
+
+    ext()  # fail loudly when the extension is missing on a GPU box
+
+
+@pytest.mark.parametrize("sde_type", ["sde", "cps", "dance_sde"])
+@pytest.mark.parametrize("mode", ["prev", "noise", "seed"])
+def test_sde_step_matches_reference(sde_type, mode):
+    from verl_omni_b200.ops.sde import philox_normal, sde_step, sde_step_reference
+
+    torch.manual_seed(0)
+    B, shape = 5, (16, 24, 24)
+    x = torch.randn(B, *shape, device="cuda")
+    v = torch.randn(B, *shape, device="cuda")
+    sig = torch.tensor([1.0, 0.9, 0.5, 0.3, 0.1], device="cuda")
+    sigp = torch.tensor([0.9, 0.7, 0.3, 0.1, 0.05], device="cuda")
+    kw = dict(sigma_max=0.95, noise_level=0.7, sde_type=sde_type)
+    prev = noise = None
+    if mode == "prev":
+        prev = torch.randn(B, *shape, device="cuda")
+    elif mode == "noise":
+        noise = torch.randn(B, *shape, device="cuda")
+    seed = 1234
+    p, lp, mean, std = sde_step(x, v, sig, sigp, prev_sample=prev, noise=noise, seed=seed if mode == "seed" else None,
+                                noise_offset=3, **kw)
+    ref_noise = noise
+    if mode == "seed":
+        ref_noise = philox_normal(seed, B, x[0].numel(), 3).reshape(x.shape).cuda()
+    rp, rlp, rmean, rstd = sde_step_reference(x.double(), v.double(), sig.double(), sigp.double(),
+                                              prev_sample=None if prev is None else prev.double(),
+                                              noise=None if ref_noise is None else ref_noise.double(), **kw)
+    torch.testing.assert_close(mean.double(), rmean, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(p.double(), rp, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(std.double(), rstd.double(), rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(lp.double(), rlp, rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("sde_type", ["sde", "cps", "dance_sde"])
+def test_sde_step_backward(sde_type):
+    from verl_omni_b200.ops.sde import sde_step, sde_step_reference
+
+    torch.manual_seed(1)
+    B = 3
+    x = torch.randn(B, 4, 16, 16, device="cuda")
+    v = torch.randn(B, 4, 16, 16, device="cuda", requires_grad=True)
+    prev = torch.randn(B, 4, 16, 16, device="cuda")
+    sig = torch.tensor([0.9, 0.5, 0.3], device="cuda")
+    sigp = torch.tensor([0.7, 0.3, 0.1], device="cuda")
+    kw = dict(sigma_max=0.95, noise_level=0.7, sde_type=sde_type, prev_sample=prev)
+    _, lp, mean, _ = sde_step(x, v, sig, sigp, **kw)
+    gm = torch.randn_like(mean)
+    (lp.sum() * 0.3 + (mean * gm).sum()).backward()
+    v2 = v.detach().double().requires_grad_(True)
+    _, rlp, rmean, _ = sde_step_reference(x.double(), v2, sig.double(), sigp.double(), sigma_max=0.95,
+                                          noise_level=0.7, sde_type=sde_type, prev_sample=prev.double())
+    (rlp.sum() * 0.3 + (rmean * gm.double()).sum()).backward()
+    torch.testing.assert_close(v.grad.double(), v2.grad, rtol=1e-4, atol=1e-5)
+
+
+def test_ppo_clip_fwd_bwd():
+    from verl_omni_b200.ops.losses import ppo_clip_loss, ppo_clip_reference
+
+    torch.manual_seed(0)
+    B = 300
+    lp = (torch.randn(B, device="cuda") * 0.3).requires_grad_(True)
+    old = torch.randn(B, device="cuda") * 0.3
+    adv = torch.randn(B, device="cuda")
+    w = torch.rand(B, device="cuda")
+    loss, st = ppo_clip_loss(lp, old, adv, 0.2, w)
+    loss.backward()
+    lp2 = lp.detach().clone().requires_grad_(True)
+    rl, rst = ppo_clip_reference(lp2, old, adv, 0.2, w)
+    rl.backward()
+    torch.testing.assert_close(loss, rl, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(torch.stack(list(st.values())), rst, rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(lp.grad, lp2.grad, rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("D", [256, 1536])
+def test_adaln_layernorm_fwd_bwd(D):
+    from verl_omni_b200.ops.norm import adaln_layernorm
+
+    torch.manual_seed(0)
+    B, S = 3, 77
+    x = torch.randn(B, S, D, device="cuda").bfloat16().requires_grad_(True)
+    mod = (torch.randn(B, 6 * D, device="cuda") * 0.5).bfloat16().requires_grad_(True)
+    y = adaln_layernorm(x, mod, 3, 4, 6)
+    gy = torch.randn_like(y)
+    y.backward(gy)
+    xr = x.detach().float().requires_grad_(True)
+    mr = mod.detach().float().requires_grad_(True)
+    m = mr.view(B, 6, D)
+    yr = torch.nn.functional.layer_norm(xr, (D,), eps=1e-6) * (1 + m[:, 4, None]) + m[:, 3, None]
+    yr.backward(gy.float())
+    torch.testing.assert_close(y.float(), yr, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(x.grad.float(), xr.grad, rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(mod.grad.float(), mr.grad, rtol=3e-2, atol=0.5)
+
+
+@pytest.mark.parametrize("dh", [32, 64, 128])
+@pytest.mark.parametrize("rope", [False, True])
+def test_qk_norm_split_fwd_bwd(dh, rope):
+    from verl_omni_b200.models.layers import rope_table
+    from verl_omni_b200.ops.norm import qk_norm_split_into
+
+    torch.manual_seed(0)
+    B, H, Si, St = 2, 3, 40, 13
+    D = H * dh
+    S = Si + St
+    qkv_i = torch.randn(B * Si, 3 * D, device="cuda").bfloat16().requires_grad_(True)
+    qkv_t = torch.randn(B * St, 3 * D, device="cuda").bfloat16().requires_grad_(True)
+    wq = (1 + 0.1 * torch.randn(dh, device="cuda")).bfloat16().requires_grad_(True)
+    wk = (1 + 0.1 * torch.randn(dh, device="cuda")).bfloat16().requires_grad_(True)
+    rp = None
+    if rope:
+        c, s = rope_table(torch.arange(S), dh)
+        rp = (c.cuda(), s.cuda())
+
+    def run(qi, qt, a, b, device, rope_t):
+        mk = lambda: torch.empty(B, H, S, dh, device=device, dtype=qi.dtype)  # noqa: E731
+        q, k, v = qk_norm_split_into(mk(), mk(), mk(), qi, a, b, Si, 0, rope=rope_t)
+        q, k, v = qk_norm_split_into(q, k, v, qt, a, b, St, Si, rope=rope_t)
+        return q, k, v
+
+    q, k, v = run(qkv_i, qkv_t, wq, wk, "cuda", rp)
+    g = [torch.randn_like(t) for t in (q, k, v)]
+    torch.autograd.backward([q, k, v], g)
+    leaves = [t.detach().cpu().float().requires_grad_(True) for t in (qkv_i, qkv_t, wq, wk)]
+    rq, rk, rv = run(*leaves, "cpu", (rp[0].cpu(), rp[1].cpu()) if rope else None)
+    torch.autograd.backward([rq, rk, rv], [t.cpu().float() for t in g])
+    for a, b in zip((q, k, v), (rq, rk, rv)):
+        torch.testing.assert_close(a.float().cpu(), b, rtol=2e-2, atol=2e-2)
+    for a, b in zip((qkv_i, qkv_t), leaves[:2]):
+        torch.testing.assert_close(a.grad.float().cpu(), b.grad, rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(wq.grad.float().cpu(), leaves[2].grad, rtol=3e-2, atol=0.5)
+
+
+def test_adamw_matches_torch():
+    from verl_omni_b200.ops._ext import ext
+    from verl_omni_b200.workers.engine.base import _adamw_torch
+
+    torch.manual_seed(0)
+    n = 100_003
+    p = torch.randn(n, device="cuda")
+    g = torch.randn(n, device="cuda") * 3
+    m = torch.randn(n, device="cuda").abs() * 0.1
+    v = torch.rand(n, device="cuda") * 0.1
+    p2, m2, v2 = p.clone(), m.clone(), v.clone()
+    p16 = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    sq = ext().sq_norm(g)
+    torch.testing.assert_close(sq, (g.double() ** 2).sum().float().reshape(1), rtol=1e-5, atol=1e-3)
+    ext().adamw_flat(p, g, m, v, p16, 1e-3, 0.9, 0.999, 1e-8, 0.01, 7, 1.0, sq, 1.0)
+    coef = min(1.0, 1.0 / (float(sq.sqrt()) + 1e-6))
+    _adamw_torch(p2, g * coef, m2, v2, 1e-3, 0.9, 0.999, 1e-8, 0.01, 7)
+    torch.testing.assert_close(p, p2, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(m, m2, rtol=1e-5, atol=1e-7)
+    torch.testing.assert_close(p16.float(), p2, rtol=1e-2, atol=1e-2)
+    before = p.clone()
+    bad = torch.tensor([float("inf")], device="cuda")
+    ext().adamw_flat(p, g, m, v, p16, 1e-3, 0.9, 0.999, 1e-8, 0.01, 8, 1.0, bad, 1.0)
+    assert torch.equal(p, before)
+
+
+def test_tiny_mmdit_gpu_matches_cpu():
+    from verl_omni_b200.models.mmdit import MMDiT, MMDiTConfig
+
+    torch.manual_seed(0)
+    m = MMDiT(MMDiTConfig.tiny())
+    x = torch.randn(2, 4, 8, 8)
+    t = torch.tensor([900.0, 300.0])
+    c = torch.randn(2, 12, 48)
+    pooled = torch.randn(2, 32)
+    ref = m(x, t, c, pooled)
+    mg = m.cuda().bfloat16()
+    out = mg(x.cuda(), t.cuda(), c.cuda(), pooled.cuda())
+    torch.testing.assert_close(out.cpu(), ref, rtol=5e-2, atol=5e-2)
+
+
+def test_trainer_step_gpu_sd35_tiny():
+    from verl_omni_b200.parallel import dist as D
+    from verl_omni_b200.trainer.diffusion.flow_grpo_trainer import PolicyGradientTrainer
+    from verl_omni_b200.utils.config import load_config
+
+    cfg = load_config("diffusion_trainer", [
+        "trainer.device=cuda", "actor_rollout_ref.model.architecture=sd35_tiny", "data.train_batch_size=2",
+        "actor_rollout_ref.rollout.n=4", "actor_rollout_ref.rollout.pipeline.num_inference_steps=4",
+        "actor_rollout_ref.rollout.algo.noise_level=0.7", "actor_rollout_ref.actor.ppo_mini_batch_size=2",
+        "actor_rollout_ref.actor.ppo_micro_batch_size_per_gpu=8", "actor_rollout_ref.actor.use_kl_loss=true",
+        "trainer.resume_mode=disable", "trainer.logger=[]", "trainer.total_training_steps=2"])
+    D.init_distributed(device="cuda")
+    t = PolicyGradientTrainer(cfg)
+    m1 = t.step()
+    m2 = t.step()
+    for m in (m1, m2):
+        assert math.isfinite(m["actor/grad_norm"]) and math.isfinite(m["actor/pg_loss"])
+    assert abs(m1["actor/ppo_kl"]) < 1e-4

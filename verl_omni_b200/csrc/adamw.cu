@@ -70,8 +70,8 @@ torch::Tensor sq_norm(torch::Tensor g) {
   const int nb = 2 * num_sms();
   auto part = torch::empty({nb}, g.options());
   auto out = torch::empty({1}, g.options());
-  sq_norm_partial_kernel<<<nb, 512, 0, stream()>>>(g.data_ptr<float>(), g.numel(), part.data_ptr<float>());
-  sum_partials_kernel<<<1, 512, 0, stream()>>>(part.data_ptr<float>(), nb, out.data_ptr<float>());
+  sq_norm_partial_kernel<<<nb, 512, 0, stream()>>>(g.data_ptr<float>(), g.numel(), part.data_ptr<float>()); vo::count_launch();
+  sum_partials_kernel<<<1, 512, 0, stream()>>>(part.data_ptr<float>(), nb, out.data_ptr<float>()); vo::count_launch();
   VO_CUDA_OK(cudaGetLastError());
   return out;
 }
@@ -98,7 +98,7 @@ void adamw_flat(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor
   adamw_flat_kernel<<<nb, 256, 0, stream()>>>(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(),
                                               v.data_ptr<float>(), p16p, n, (float)lr, (float)b1, (float)b2,
                                               (float)eps, (float)wd, (float)bc1, (float)std::sqrt(bc2),
-                                              (float)max_norm, sn, (float)grad_scale);
+                                              (float)max_norm, sn, (float)grad_scale); vo::count_launch();
   VO_CUDA_OK(cudaGetLastError());
 }
 

@@ -1,9 +1,13 @@
 // Python bindings of the verl_omni_b200 sm_100a kernels (module verl_omni_b200._C).
 #include <torch/extension.h>
 
+#include <atomic>
 #include <vector>
 
 namespace vo {
+static std::atomic<int64_t> g_launches{0};
+void count_launch(int64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+int64_t launch_count() { return g_launches.load(); }
 std::vector<torch::Tensor> sde_step_fwd(torch::Tensor x, torch::Tensor v, torch::Tensor sigma, torch::Tensor sigma_prev,
                                         c10::optional<torch::Tensor> prev, c10::optional<torch::Tensor> noise,
                                         double sigma_max, double eta, int64_t type, int64_t seed, int64_t offset,
@@ -32,10 +36,19 @@ torch::Tensor sq_norm(torch::Tensor g);
 void adamw_flat(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, c10::optional<torch::Tensor> p16,
                 double lr, double b1, double b2, double eps, double wd, int64_t step, double max_norm,
                 c10::optional<torch::Tensor> sq_norm_t, double grad_scale);
+std::vector<torch::Tensor> gemm_fwd(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> b, int64_t epi,
+                                    c10::optional<torch::Tensor> gate, c10::optional<torch::Tensor> res, int64_t S);
+torch::Tensor gemm_dgrad(torch::Tensor dy, torch::Tensor w);
+void gemm_wgrad(torch::Tensor dy, torch::Tensor x, torch::Tensor out, bool accumulate);
+torch::Tensor gelu_tanh_bwd(torch::Tensor dy, torch::Tensor pre);
+int64_t gemm_error(bool reset);
+std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal, double scale);
+int64_t fmha_error(bool reset);
 }  // namespace vo
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "verl_omni_b200 sm_100a kernels";
+  m.def("launch_count", &vo::launch_count);
   m.def("sde_step_fwd", &vo::sde_step_fwd);
   m.def("sde_step_bwd", &vo::sde_step_bwd);
   m.def("ppo_clip_fwd", &vo::ppo_clip_fwd);
@@ -46,4 +59,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_rmsnorm_bwd", &vo::qk_rmsnorm_bwd);
   m.def("sq_norm", &vo::sq_norm);
   m.def("adamw_flat", &vo::adamw_flat);
+  m.def("gemm_fwd", &vo::gemm_fwd);
+  m.def("gemm_dgrad", &vo::gemm_dgrad);
+  m.def("gemm_wgrad", &vo::gemm_wgrad);
+  m.def("gelu_tanh_bwd", &vo::gelu_tanh_bwd);
+  m.def("gemm_error", &vo::gemm_error);
+  m.def("fmha_fwd", &vo::fmha_fwd);
+  m.def("fmha_error", &vo::fmha_error);
 }

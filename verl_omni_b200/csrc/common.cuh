@@ -13,8 +13,10 @@
 #define VO_CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
 #define VO_CHECK_CONTIG(x) TORCH_CHECK((x).is_contiguous(), #x " must be contiguous")
 #define VO_CHECK_INPUT(x) \
-  VO_CHECK_CUDA(x);       \
-  VO_CHECK_CONTIG(x)
+  do {                    \
+    VO_CHECK_CUDA(x);     \
+    VO_CHECK_CONTIG(x);   \
+  } while (0)
 #define VO_CUDA_OK(call)                                                                      \
   do {                                                                                        \
     cudaError_t e_ = (call);                                                                  \
@@ -23,6 +25,9 @@
   } while (0)
 
 namespace vo {
+
+// Number of kernels this extension has launched (reported by the benchmark as its launch count).
+void count_launch(int64_t n = 1);
 
 constexpr int kWarp = 32;
 

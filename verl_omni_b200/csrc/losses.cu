@@ -87,7 +87,7 @@ std::vector<torch::Tensor> ppo_clip_fwd(torch::Tensor logp, torch::Tensor old, t
   auto stats = torch::empty({6}, logp.options());
   const float* wp = (w.has_value() && w->defined()) ? w->data_ptr<float>() : nullptr;
   ppo_clip_fwd_kernel<<<1, 256, 0, stream()>>>(logp.data_ptr<float>(), old.data_ptr<float>(), adv.data_ptr<float>(),
-                                               wp, B, (float)clip, loss.data_ptr<float>(), stats.data_ptr<float>());
+                                               wp, B, (float)clip, loss.data_ptr<float>(), stats.data_ptr<float>()); vo::count_launch();
   VO_CUDA_OK(cudaGetLastError());
   return {loss, stats};
 }
@@ -100,7 +100,7 @@ torch::Tensor ppo_clip_bwd(torch::Tensor logp, torch::Tensor old, torch::Tensor 
   const float* wp = (w.has_value() && w->defined()) ? w->data_ptr<float>() : nullptr;
   ppo_clip_bwd_kernel<<<(B + 255) / 256, 256, 0, stream()>>>(logp.data_ptr<float>(), old.data_ptr<float>(),
                                                              adv.data_ptr<float>(), wp, B, (float)clip,
-                                                             g_loss.data_ptr<float>(), gl.data_ptr<float>());
+                                                             g_loss.data_ptr<float>(), gl.data_ptr<float>()); vo::count_launch();
   VO_CUDA_OK(cudaGetLastError());
   return gl;
 }

@@ -320,7 +320,7 @@ std::vector<torch::Tensor> adaln_ln_fwd(torch::Tensor x, c10::optional<torch::Te
   adaln_ln_fwd_kernel<<<(rows + wpb - 1) / wpb, wpb * 32, 0, stream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr<at::BFloat16>()),
       reinterpret_cast<__nv_bfloat16*>(y.data_ptr<at::BFloat16>()), mean.data_ptr<float>(), rstd.data_ptr<float>(), m,
-      aw, ab, rows, D, (int)S, (float)eps);
+      aw, ab, rows, D, (int)S, (float)eps); vo::count_launch();
   VO_CUDA_OK(cudaGetLastError());
   return {y, mean, rstd};
 }
@@ -341,7 +341,7 @@ std::vector<torch::Tensor> adaln_ln_bwd(torch::Tensor dy, torch::Tensor x, torch
   adaln_ln_bwd_dx_kernel<<<(rows + wpb - 1) / wpb, wpb * 32, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr<at::BFloat16>()),
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr<at::BFloat16>()), mean.data_ptr<float>(),
-      rstd.data_ptr<float>(), m, reinterpret_cast<__nv_bfloat16*>(dx.data_ptr<at::BFloat16>()), rows, D, (int)S);
+      rstd.data_ptr<float>(), m, reinterpret_cast<__nv_bfloat16*>(dx.data_ptr<at::BFloat16>()), rows, D, (int)S); vo::count_launch();
   // column reductions
   const int cols8 = D / 8;
   const int tpb = std::min(128, cols8);
@@ -354,11 +354,11 @@ std::vector<torch::Tensor> adaln_ln_bwd(torch::Tensor dy, torch::Tensor x, torch
   adaln_ln_bwd_mod_kernel<<<dim3(gx, nchunk, B), tpb, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr<at::BFloat16>()),
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr<at::BFloat16>()), mean.data_ptr<float>(),
-      rstd.data_ptr<float>(), ps.data_ptr<float>(), pc.data_ptr<float>(), D, (int)S, rpc, nchunk);
+      rstd.data_ptr<float>(), ps.data_ptr<float>(), pc.data_ptr<float>(), D, (int)S, rpc, nchunk); vo::count_launch();
   auto dshift = torch::empty({B, D}, fo), dscale = torch::empty({B, D}, fo);
   const int64_t n = (int64_t)B * D;
-  reduce_chunks_kernel<<<(n + 255) / 256, 256, 0, st>>>(ps.data_ptr<float>(), dshift.data_ptr<float>(), B, nchunk, D);
-  reduce_chunks_kernel<<<(n + 255) / 256, 256, 0, st>>>(pc.data_ptr<float>(), dscale.data_ptr<float>(), B, nchunk, D);
+  reduce_chunks_kernel<<<(n + 255) / 256, 256, 0, st>>>(ps.data_ptr<float>(), dshift.data_ptr<float>(), B, nchunk, D); vo::count_launch();
+  reduce_chunks_kernel<<<(n + 255) / 256, 256, 0, st>>>(pc.data_ptr<float>(), dscale.data_ptr<float>(), B, nchunk, D); vo::count_launch();
   VO_CUDA_OK(cudaGetLastError());
   return {dx, dshift, dscale};
 }
@@ -384,7 +384,7 @@ std::vector<torch::Tensor> qk_rmsnorm_fwd(torch::Tensor qkv, torch::Tensor wq, t
   auto ref = first_defined({q, k, v});
   const int H = ref.size(1), S_total = ref.size(2), DH = ref.size(3);
   const int3 po = make_int3((int)part_off[0], (int)part_off[1], (int)part_off[2]);
-  TORCH_CHECK(DH == 64 || DH == 128, "head_dim must be 64 or 128");
+  TORCH_CHECK(DH == 32 || DH == 64 || DH == 128, "head_dim must be 32, 64 or 128");
   const int64_t rows = qkv.size(0);
   auto fo = qkv.options().dtype(torch::kFloat32);
   auto rq = torch::empty({rows, H}, fo), rk = torch::empty({rows, H}, fo);
@@ -392,14 +392,18 @@ std::vector<torch::Tensor> qk_rmsnorm_fwd(torch::Tensor qkv, torch::Tensor wq, t
   const float* rsn = (rope_sin.has_value() && rope_sin->defined()) ? rope_sin->data_ptr<float>() : nullptr;
   const int64_t threads = rows * H * (DH / 8);
   const int64_t rs_ = qkv.size(1);
-  if (DH == 64)
+  if (DH == 32)
+    qk_rmsnorm_fwd_kernel<32><<<(threads + 255) / 256, 256, 0, stream()>>>(
+        bptr(qkv), bptr(wq), bptr(wk), bptr(q), bptr(k), bptr(v), rq.data_ptr<float>(), rk.data_ptr<float>(), rc, rsn,
+        rows, H, (int)S_seg, S_total, (int)seg_off, (float)eps, rs_, po);
+  else if (DH == 64)
     qk_rmsnorm_fwd_kernel<64><<<(threads + 255) / 256, 256, 0, stream()>>>(
         bptr(qkv), bptr(wq), bptr(wk), bptr(q), bptr(k), bptr(v), rq.data_ptr<float>(), rk.data_ptr<float>(), rc, rsn,
         rows, H, (int)S_seg, S_total, (int)seg_off, (float)eps, rs_, po);
   else
     qk_rmsnorm_fwd_kernel<128><<<(threads + 255) / 256, 256, 0, stream()>>>(
         bptr(qkv), bptr(wq), bptr(wk), bptr(q), bptr(k), bptr(v), rq.data_ptr<float>(), rk.data_ptr<float>(), rc, rsn,
-        rows, H, (int)S_seg, S_total, (int)seg_off, (float)eps, rs_, po);
+        rows, H, (int)S_seg, S_total, (int)seg_off, (float)eps, rs_, po); vo::count_launch();
   VO_CUDA_OK(cudaGetLastError());
   return {rq, rk};
 }
@@ -421,7 +425,12 @@ std::vector<torch::Tensor> qk_rmsnorm_bwd(torch::Tensor qkv, torch::Tensor wq, t
   const float* rc = (rope_cos.has_value() && rope_cos->defined()) ? rope_cos->data_ptr<float>() : nullptr;
   const float* rsn = (rope_sin.has_value() && rope_sin->defined()) ? rope_sin->data_ptr<float>() : nullptr;
   const int64_t rs_ = qkv.size(1);
-  if (DH == 64)
+  if (DH == 32)
+    qk_rmsnorm_bwd_kernel<32><<<nblk, 256, 0, stream()>>>(bptr(qkv), bptr(wq), bptr(wk), bptr(dq), bptr(dk), bptr(dv),
+                                                          rq.data_ptr<float>(), rk.data_ptr<float>(), rc, rsn,
+                                                          bptr(dqkv), part.data_ptr<float>(), rows, H, (int)S_seg,
+                                                          S_total, (int)seg_off, rs_, po);
+  else if (DH == 64)
     qk_rmsnorm_bwd_kernel<64><<<nblk, 256, 0, stream()>>>(bptr(qkv), bptr(wq), bptr(wk), bptr(dq), bptr(dk), bptr(dv),
                                                           rq.data_ptr<float>(), rk.data_ptr<float>(), rc, rsn,
                                                           bptr(dqkv), part.data_ptr<float>(), rows, H, (int)S_seg,
@@ -430,7 +439,7 @@ std::vector<torch::Tensor> qk_rmsnorm_bwd(torch::Tensor qkv, torch::Tensor wq, t
     qk_rmsnorm_bwd_kernel<128><<<nblk, 256, 0, stream()>>>(bptr(qkv), bptr(wq), bptr(wk), bptr(dq), bptr(dk),
                                                            bptr(dv), rq.data_ptr<float>(), rk.data_ptr<float>(), rc,
                                                            rsn, bptr(dqkv), part.data_ptr<float>(), rows, H,
-                                                           (int)S_seg, S_total, (int)seg_off, rs_, po);
+                                                           (int)S_seg, S_total, (int)seg_off, rs_, po); vo::count_launch();
   VO_CUDA_OK(cudaGetLastError());
   auto dw = part.sum(0);  // [2, DH]
   return {dqkv, dw[0], dw[1]};

@@ -233,12 +233,13 @@ std::vector<torch::Tensor> sde_step_fwd(torch::Tensor x, torch::Tensor v, torch:
     VO_SDE_LAUNCH(false, true);
   else
     VO_SDE_LAUNCH(false, false);
+  vo::count_launch();
 #undef VO_SDE_LAUNCH
   sde_finalize_kernel<<<(B + 7) / 8, 256, 0, st>>>(partial.data_ptr<float>(), sigma.data_ptr<float>(),
                                                    sigma_prev.data_ptr<float>(),
                                                    want_logp ? logp.data_ptr<float>() : nullptr,
                                                    stdv.data_ptr<float>(), B, nchunks, n, (float)sigma_max,
-                                                   (float)eta, (int)type, norm);
+                                                   (float)eta, (int)type, norm); vo::count_launch();
   VO_CUDA_OK(cudaGetLastError());
   return {prev_out, logp, mean, stdv};
 }
@@ -257,7 +258,7 @@ torch::Tensor sde_step_bwd(torch::Tensor x, torch::Tensor prev, torch::Tensor me
   sde_bwd_kernel<<<dim3(bx, B), 256, 0, stream()>>>(prev.data_ptr<float>(), mean.data_ptr<float>(),
                                                      sigma.data_ptr<float>(), sigma_prev.data_ptr<float>(),
                                                      g_logp.data_ptr<float>(), g_mean.data_ptr<float>(),
-                                                     gv.data_ptr<float>(), n, (float)sigma_max, (float)eta, (int)type);
+                                                     gv.data_ptr<float>(), n, (float)sigma_max, (float)eta, (int)type); vo::count_launch();
   VO_CUDA_OK(cudaGetLastError());
   return gv;
 }

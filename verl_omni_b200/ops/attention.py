@@ -34,7 +34,15 @@ class _FMHA(torch.autograd.Function):
     def backward(ctx, do):
         q, k, v, o, lse = ctx.saved_tensors
         causal, scale = ctx.meta
-        dq, dk, dv = ext().fmha_bwd(q, k, v, o, lse, do.contiguous(), causal, scale)
+        if hasattr(ext(), "fmha_bwd"):
+            dq, dk, dv = ext().fmha_bwd(q, k, v, o, lse, do.contiguous(), causal, scale)
+            return dq, dk, dv, None, None
+        # backward kernel not built: recompute through SDPA autograd
+        B, S, H, D = o.shape
+        with torch.enable_grad():
+            qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
+            oo = F.scaled_dot_product_attention(qq, kk, vv, is_causal=causal, scale=scale)
+            dq, dk, dv = torch.autograd.grad(oo, (qq, kk, vv), do.view(B, S, H, D).transpose(1, 2))
         return dq, dk, dv, None, None
 
 

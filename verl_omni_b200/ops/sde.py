@@ -73,8 +73,8 @@ def _bcast(v: torch.Tensor, ref: torch.Tensor) -> torch.Tensor:
 def sde_step_reference(sample, model_output, sigma, sigma_prev, *, sigma_max, noise_level, sde_type,
                        prev_sample=None, noise=None, return_logprobs=True, include_logprob_normalizer=True):
     """fp32 torch restatement of the three reverse-step variants (the oracle)."""
-    sigma = _bcast(sigma.float(), sample)
-    sigma_prev = _bcast(sigma_prev.float(), sample)
+    sigma = _bcast(sigma.to(sample.dtype), sample)
+    sigma_prev = _bcast(sigma_prev.to(sample.dtype), sample)
     dt = sigma_prev - sigma
     if sde_type == "sde":
         denom = 1 - torch.where(sigma == 1, torch.full_like(sigma, sigma_max), sigma)
