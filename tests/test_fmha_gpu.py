@@ -60,3 +60,21 @@ def test_attention_op_autograd():
     torch.testing.assert_close(o.float(), orf, rtol=2e-2, atol=2e-2)
     for a, b in ((q, qr), (k, kr), (v, vr)):
         torch.testing.assert_close(a.grad.float(), b.grad, rtol=5e-2, atol=5e-2)
+
+
+@pytest.mark.parametrize("B,H,Sq,Skv,D,causal", CASES)
+def test_fmha_bwd(E, B, H, Sq, Skv, D, causal):
+    torch.manual_seed(2)
+    q = torch.randn(B, H, Sq, D, device="cuda").bfloat16()
+    k = torch.randn(B, H, Skv, D, device="cuda").bfloat16()
+    v = torch.randn(B, H, Skv, D, device="cuda").bfloat16()
+    scale = 1 / math.sqrt(D)
+    o, lse = E.fmha_fwd(q, k, v, causal, scale)
+    do = torch.randn(B, Sq, H, D, device="cuda").bfloat16()
+    dq, dk, dv = E.fmha_bwd(q, k, v, o, lse, do, causal, scale)
+    qr, kr, vr = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+    ro, _ = _ref(qr, kr, vr, causal, scale)
+    ro.backward(do.float().transpose(1, 2))
+    for a, b in ((dq, qr.grad), (dk, kr.grad), (dv, vr.grad)):
+        rel = float((a.float() - b).norm() / (b.norm() + 1e-6))
+        assert rel < 2e-2, rel

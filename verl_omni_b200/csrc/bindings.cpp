@@ -44,6 +44,8 @@ torch::Tensor gelu_tanh_bwd(torch::Tensor dy, torch::Tensor pre);
 int64_t gemm_error(bool reset);
 std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal, double scale);
 int64_t fmha_error(bool reset);
+std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
+                                    torch::Tensor lse, torch::Tensor dO, bool causal, double scale);
 }  // namespace vo
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -66,4 +68,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_error", &vo::gemm_error);
   m.def("fmha_fwd", &vo::fmha_fwd);
   m.def("fmha_error", &vo::fmha_error);
+  m.def("fmha_bwd", &vo::fmha_bwd);
 }

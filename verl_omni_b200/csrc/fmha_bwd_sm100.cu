@@ -1,0 +1,538 @@
+// Flash attention backward for sm_100a on tcgen05 tensor cores.
+//
+// Given Q, K, V [BH, S, D] (bf16), O and dO token-major [B, Sq, H, D], LSE [BH, Sq] (natural log):
+//   P = exp(Q K^T * scale - LSE),  dV = P^T dO,  dP = dO V^T,  dS = P * (dP - Delta),
+//   Delta = rowsum(dO * O),  dQ = scale * dS K,  dK = scale * dS^T Q.
+//
+// Kernels:
+//   delta_kernel     Delta[bh, q] in fp32 (one 8/16-lane group per row).
+//   fmha_bwd_kernel  one CTA per (128-key tile, head); loops over 128-query tiles:
+//     warp 0      TMA: K_j, V_j once; Q_i and dO_i per iteration (ring of STAGES);
+//     warp 1      MMA issuer: S^T = K Q^T and dP^T = V dO^T into TMEM (lanes = keys), then
+//                 dV += P^T dO, dK += dS^T Q (TMEM accumulators for the whole loop) and
+//                 dQ_i = dS K (TMEM, reusing the S^T columns);
+//     warps 2..5  one key row per thread: P^T and dS^T from the two TMEM rows, written bf16 into
+//                 128B-swizzled SMEM -- read as K-major A operands by the dV/dK MMAs and as an
+//                 MN-major A operand by the dQ MMA; then the dQ_i tile (one query row per thread)
+//                 is added into an fp32 dQ accumulator with vector reductions; at the end dK/dV
+//                 are scaled, rounded and stored.
+//   dq_finalize      dQ = bf16(scale * dQ_acc).
+// All operand majorness changes are expressed through smem descriptors (no transposes in memory).
+// Every mbarrier wait is bounded; a timeout records an error code and the CTA exits.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace vo_fbwd {
+
+constexpr int NUM_THREADS = 192;
+constexpr unsigned long long WAIT_BUDGET = 8ull * 1000 * 1000 * 1000;
+__device__ int g_error = 0;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t c) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(c));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t par) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(par)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t par, volatile int* abort_flag, int code) {
+  if (mbar_try_wait(b, par)) return true;
+  const unsigned long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait(b, par)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > WAIT_BUDGET) {
+      atomicCAS(&g_error, 0, code);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tma3(void* dst, const CUtensorMap* m, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(m), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void tma4(void* dst, const CUtensorMap* m, uint64_t* bar, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(m), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void commit(uint64_t* b) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(b))
+               : "memory");
+}
+__device__ __forceinline__ void ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ uint64_t desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | (2ull << 61);
+}
+__host__ __device__ constexpr uint32_t idesc(int M, int N, int a_mn, int b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+__device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n)); }
+
+struct Params {
+  int Sq, Skv, H, nkv_tiles, causal;
+  float scale, scale_log2;
+  const float* lse;    // [BH, Sq]
+  const float* delta;  // [BH, Sq]
+  float* dq_acc;       // [BH, Sq, D] fp32 (pre-zeroed)
+  __nv_bfloat16* dk;   // [BH, Skv, D]
+  __nv_bfloat16* dv;   // [BH, Skv, D]
+};
+
+template <int D>
+struct Lay {
+  static constexpr int STAGES = D == 64 ? 2 : 1;
+  static constexpr int TILE = 128 * D * 2;
+  static constexpr int K_OFF = 0;
+  static constexpr int V_OFF = TILE;
+  static constexpr int Q_OFF = 2 * TILE;
+  static constexpr int DO_OFF = Q_OFF + STAGES * TILE;
+  static constexpr int PT_OFF = DO_OFF + STAGES * TILE;
+  static constexpr int DS_OFF = PT_OFF + 32768;
+  static constexpr int LSE_OFF = DS_OFF + 32768;  // 128 floats
+  static constexpr int DEL_OFF = LSE_OFF + 512;   // 128 floats
+  static constexpr int BAR_OFF = DEL_OFF + 512;
+  static constexpr int BYTES = BAR_OFF + 256;
+};
+
+// write 32 bf16 values (one 32-column chunk of a 128-col row) into a 128B-swizzled [128 x 128] tile
+__device__ __forceinline__ void store_row_chunk(uint8_t* tile, int row, int c, const float* v) {
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    uint32_t w[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      __nv_bfloat162 b2 = __floats2bfloat162_rn(v[g * 8 + 2 * h], v[g * 8 + 2 * h + 1]);
+      w[h] = *reinterpret_cast<uint32_t*>(&b2);
+    }
+    const int col = c * 32 + g * 8;
+    const int chunk = col >> 6, unit = (col & 63) >> 3;
+    *reinterpret_cast<uint4*>(tile + chunk * 16384 + row * 128 + ((unit ^ (row & 7)) << 4)) =
+        make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    fmha_bwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+                    const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo, Params p) {
+  using L = Lay<D>;
+  constexpr int ST = L::STAGES;
+  extern __shared__ __align__(1024) uint8_t raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR_OFF);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qdo_full = bars + 1;   // [2]
+  uint64_t* qdo_empty = bars + 3;  // [2]
+  uint64_t* sp_full = bars + 5;
+  uint64_t* ds_full = bars + 6;
+  uint64_t* mma2_done = bars + 7;
+  uint64_t* dq_free = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* lse_s = reinterpret_cast<float*>(sm + L::LSE_OFF);
+  float* del_s = reinterpret_cast<float*>(sm + L::DEL_OFF);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x % p.nkv_tiles;
+  const int bh = blockIdx.x / p.nkv_tiles;
+  const int b = bh / p.H, h = bh % p.H;
+  const int kv0 = kt * 128;
+  const int i0 = p.causal ? kv0 / 128 : 0;
+  const int nq = (p.Sq + 127) / 128;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qdo_full[i], 1);
+      mbar_init(&qdo_empty[i], 1);
+    }
+    mbar_init(sp_full, 1);
+    mbar_init(ds_full, 4);
+    mbar_init(mma2_done, 1);
+    mbar_init(dq_free, 4);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+  constexpr uint32_t C_ST = 0, C_DPT = 128, C_DV = 256, C_DK = 256 + D, C_DQ = 0;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_expect_tx(kv_full, 2 * L::TILE);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        tma3(sm + L::K_OFF + c * 16384, &mk, kv_full, c * 64, kv0, bh);
+        tma3(sm + L::V_OFF + c * 16384, &mv, kv_full, c * 64, kv0, bh);
+      }
+      for (int i = i0, it = 0; i < nq; ++i, ++it) {
+        const int st = it % ST;
+        if (!mbar_wait(&qdo_empty[st], ((it / ST) & 1) ^ 1, abort_flag, 21)) break;
+        mbar_expect_tx(&qdo_full[st], 2 * L::TILE);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          tma3(sm + L::Q_OFF + st * L::TILE + c * 16384, &mq, &qdo_full[st], c * 64, i * 128, bh);
+          tma4(sm + L::DO_OFF + st * L::TILE + c * 16384, &mdo, &qdo_full[st], c * 64, h, i * 128, b);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_kk = idesc(128, 128, 0, 0);  // S^T, dP^T: A, B K-major over d
+      const uint32_t id_kn = idesc(128, D, 0, 1);    // dV, dK: A K-major over q, B MN-major (d contiguous)
+      const uint32_t id_nn = idesc(128, D, 1, 1);    // dQ: A = dS^T read MN-major, B = K MN-major
+      const uint32_t ka = smem_u32(sm + L::K_OFF), va = smem_u32(sm + L::V_OFF);
+      const uint32_t pa = smem_u32(sm + L::PT_OFF), da = smem_u32(sm + L::DS_OFF);
+      bool ok = mbar_wait(kv_full, 0, abort_flag, 22);
+      for (int i = i0, it = 0; ok && i < nq; ++i, ++it) {
+        const int st = it % ST;
+        if (!mbar_wait(&qdo_full[st], (it / ST) & 1, abort_flag, 23)) break;
+        if (it > 0 && !mbar_wait(dq_free, (it - 1) & 1, abort_flag, 24)) break;
+        fence_after();
+        const uint32_t qa = smem_u32(sm + L::Q_OFF + st * L::TILE);
+        const uint32_t oa = smem_u32(sm + L::DO_OFF + st * L::TILE);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          mma(tmem + C_ST, desc(ka + off, 16, 1024), desc(qa + off, 16, 1024), id_kk, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          mma(tmem + C_DPT, desc(va + off, 16, 1024), desc(oa + off, 16, 1024), id_kk, kk > 0);
+        }
+        commit(sp_full);
+        if (!mbar_wait(ds_full, it & 1, abort_flag, 25)) break;
+        fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // reduce over 128 queries
+          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+          mma(tmem + C_DV, desc(pa + aoff, 16, 1024), desc(oa + kk * 2048, 16384, 1024), id_kn, (it > 0 || kk > 0));
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+          mma(tmem + C_DK, desc(da + aoff, 16, 1024), desc(qa + kk * 2048, 16384, 1024), id_kn, (it > 0 || kk > 0));
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // reduce over 128 keys
+          mma(tmem + C_DQ, desc(da + kk * 2048, 16384, 1024), desc(ka + kk * 2048, 16384, 1024), id_nn, kk > 0);
+        }
+        commit(mma2_done);
+        commit(&qdo_empty[st]);
+      }
+    }
+  } else {
+    const int tid = threadIdx.x - 64;  // 0..127 over the four softmax warps
+    const int lane_base = 32 * (warp & 3);
+    const int r = lane_base + lane;  // TMEM lane = key row (S^T, dV, dK) or query row (dQ)
+    const int kv = kv0 + r;
+    const uint32_t trow = tmem + ((uint32_t)lane_base << 16);
+    uint8_t* pt = sm + L::PT_OFF;
+    uint8_t* ds = sm + L::DS_OFF;
+    bool ok = true;
+    int it = 0;
+    for (int i = i0; i < nq && ok; ++i, ++it) {
+      const int q0 = i * 128;
+      named_bar(1, 128);
+      {
+        const int q = q0 + tid;
+        lse_s[tid] = q < p.Sq ? p.lse[(int64_t)bh * p.Sq + q] * 1.4426950408889634f : INFINITY;
+        del_s[tid] = q < p.Sq ? p.delta[(int64_t)bh * p.Sq + q] : 0.f;
+      }
+      named_bar(1, 128);
+      if (!mbar_wait(sp_full, it & 1, abort_flag, 26)) {
+        ok = false;
+        break;
+      }
+      fence_after();
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float s[32], dp[32];
+        ld32(trow + C_ST + c * 32, s);
+        ld32(trow + C_DPT + c * 32, dp);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int qc = c * 32 + j;
+          const int q = q0 + qc;
+          const bool valid = kv < p.Skv && (!p.causal || kv <= q);
+          const float pv = valid ? ex2(s[j] * p.scale_log2 - lse_s[qc]) : 0.f;
+          s[j] = pv;
+          dp[j] = pv * (dp[j] - del_s[qc]);
+        }
+        store_row_chunk(pt, r, c, s);
+        store_row_chunk(ds, r, c, dp);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ds_full);
+      if (!mbar_wait(mma2_done, it & 1, abort_flag, 27)) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      {  // dQ tile: TMEM lane r = query row q0 + r
+        const int q = q0 + r;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          float v[32];
+          ld32(trow + C_DQ + c * 32, v);
+          if (q < p.Sq) {
+            float* dst = p.dq_acc + ((int64_t)bh * p.Sq + q) * D + c * 32;
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) red_add_v4(dst + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+          }
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+    }
+    if (ok && it > 0) {
+      // all MMAs of the last iteration completed (mma2_done waited) -> dV, dK final
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float vv[32], kk[32];
+        ld32(trow + C_DV + c * 32, vv);
+        ld32(trow + C_DK + c * 32, kk);
+        if (kv < p.Skv) {
+          __nv_bfloat16* dvp = p.dv + ((int64_t)bh * p.Skv + kv) * D + c * 32;
+          __nv_bfloat16* dkp = p.dk + ((int64_t)bh * p.Skv + kv) * D + c * 32;
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            uint4 a, bq;
+            __nv_bfloat162* ha = reinterpret_cast<__nv_bfloat162*>(&a);
+            __nv_bfloat162* hb = reinterpret_cast<__nv_bfloat162*>(&bq);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              ha[t] = __floats2bfloat162_rn(vv[j + 2 * t], vv[j + 2 * t + 1]);
+              hb[t] = __floats2bfloat162_rn(kk[j + 2 * t] * p.scale, kk[j + 2 * t + 1] * p.scale);
+            }
+            *reinterpret_cast<uint4*>(dvp + j) = a;
+            *reinterpret_cast<uint4*>(dkp + j) = bq;
+          }
+        }
+      }
+    } else if (ok && kv < p.Skv) {  // causal tile with no queries: zero gradients
+      for (int j = 0; j < D; ++j) {
+        p.dv[((int64_t)bh * p.Skv + kv) * D + j] = __float2bfloat16_rn(0.f);
+        p.dk[((int64_t)bh * p.Skv + kv) * D + j] = __float2bfloat16_rn(0.f);
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+  }
+}
+
+// Delta[bh, q] = sum_d dO[b, q, h, d] * O[b, q, h, d]
+template <int D>
+__global__ void delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dO,
+                             float* __restrict__ delta, int B, int Sq, int H) {
+  constexpr int LPR = D / 8;  // lanes per row
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t row = gid / LPR;  // row over (b, q, h) token-major
+  const int sub = gid % LPR;
+  const int64_t rows = (int64_t)B * Sq * H;
+  float s = 0.f;
+  if (row < rows) {
+    const uint4 a = *reinterpret_cast<const uint4*>(o + row * D + sub * 8);
+    const uint4 g = *reinterpret_cast<const uint4*>(dO + row * D + sub * 8);
+    const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&a);
+    const __nv_bfloat162* hg = reinterpret_cast<const __nv_bfloat162*>(&g);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      float2 x = __bfloat1622float2(ha[t]), y = __bfloat1622float2(hg[t]);
+      s += x.x * y.x + x.y * y.y;
+    }
+  }
+#pragma unroll
+  for (int off = LPR / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (row < rows && sub == 0) {
+    const int h = row % H;
+    const int64_t bq = row / H;
+    const int q = bq % Sq;
+    const int b = bq / Sq;
+    delta[((int64_t)b * H + h) * Sq + q] = s;
+  }
+}
+
+__global__ void dq_finalize_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq, int64_t n4,
+                                   float scale) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 v = reinterpret_cast<const float4*>(acc)[i];
+    __nv_bfloat162 a = __floats2bfloat162_rn(v.x * scale, v.y * scale);
+    __nv_bfloat162 b = __floats2bfloat162_rn(v.z * scale, v.w * scale);
+    uint2 pk;
+    pk.x = *reinterpret_cast<uint32_t*>(&a);
+    pk.y = *reinterpret_cast<uint32_t*>(&b);
+    reinterpret_cast<uint2*>(dq)[i] = pk;
+  }
+}
+
+typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                             const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                             CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeFn encode() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    fn = reinterpret_cast<EncodeFn>(ptr);
+  }
+  return fn;
+}
+static int map3(CUtensorMap* m, const void* ptr, int BH, int S, int D) {
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)BH};
+  cuuint64_t str[2] = {(cuuint64_t)D * 2, (cuuint64_t)S * D * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return (int)encode()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, str, box, es,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+// token-major [B, S, H, D] viewed as 4D {D, H, S, B}; box {64, 1, 128, 1}
+static int map4_tok(CUtensorMap* m, const void* ptr, int B, int S, int H, int D) {
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
+  cuuint64_t str[3] = {(cuuint64_t)D * 2, (cuuint64_t)H * D * 2, (cuuint64_t)S * H * D * 2};
+  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  return (int)encode()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, str, box, es,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+template <int D>
+static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
+                  Params p, int grid, cudaStream_t st) {
+  static bool set = false;
+  if (!set) {
+    cudaFuncSetAttribute(fmha_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay<D>::BYTES + 1024);
+    set = true;
+  }
+  fmha_bwd_kernel<D><<<grid, NUM_THREADS, Lay<D>::BYTES + 1024, st>>>(mq, mk, mv, mdo, p);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace vo_fbwd
+
+// q [B,H,Sq,D], k/v [B,H,Skv,D], o/do [B,Sq,H,D], lse [B,H,Sq]; outputs dq [B,H,Sq,D], dk/dv [B,H,Skv,D].
+// Scratch: delta [B*H*Sq] fp32 and dq_acc [B*H*Sq*D] fp32 (dq_acc must be zero on entry).
+extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                           const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_acc, int B, int H,
+                           int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream) {
+  using namespace vo_fbwd;
+  if (D != 64 && D != 128) return -1;
+  const int64_t rows = (int64_t)B * Sq * H;
+  const int64_t threads = rows * (D / 8);
+  if (D == 64)
+    delta_kernel<64><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
+        (const __nv_bfloat16*)o, (const __nv_bfloat16*)dO, delta, B, Sq, H);
+  else
+    delta_kernel<128><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
+        (const __nv_bfloat16*)o, (const __nv_bfloat16*)dO, delta, B, Sq, H);
+  CUtensorMap mq, mk, mv, mdo;
+  int r = map3(&mq, q, B * H, Sq, D);
+  if (!r) r = map3(&mk, k, B * H, Skv, D);
+  if (!r) r = map3(&mv, v, B * H, Skv, D);
+  if (!r) r = map4_tok(&mdo, dO, B, Sq, H, D);
+  if (r) return r;
+  Params p;
+  p.Sq = Sq;
+  p.Skv = Skv;
+  p.H = H;
+  p.nkv_tiles = (Skv + 127) / 128;
+  p.causal = causal;
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.lse = lse;
+  p.delta = delta;
+  p.dq_acc = dq_acc;
+  p.dk = (__nv_bfloat16*)dk;
+  p.dv = (__nv_bfloat16*)dv;
+  const int grid = p.nkv_tiles * B * H;
+  r = D == 64 ? launch<64>(mq, mk, mv, mdo, p, grid, stream) : launch<128>(mq, mk, mv, mdo, p, grid, stream);
+  if (r) return r;
+  const int64_t n4 = (int64_t)B * H * Sq * D / 4;
+  dq_finalize_kernel<<<(unsigned)((n4 + 255) / 256 < 4096 ? (n4 + 255) / 256 : 4096), 256, 0, stream>>>(
+      dq_acc, (__nv_bfloat16*)dq, n4, scale);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int vo_fmha_bwd_error(int reset) {
+  int e = 0;
+  cudaMemcpyFromSymbol(&e, vo_fbwd::g_error, sizeof(int));
+  if (reset) {
+    int z = 0;
+    cudaMemcpyToSymbol(vo_fbwd::g_error, &z, sizeof(int));
+  }
+  return e;
+}

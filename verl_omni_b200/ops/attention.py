@@ -34,8 +34,9 @@ class _FMHA(torch.autograd.Function):
     def backward(ctx, do):
         q, k, v, o, lse = ctx.saved_tensors
         causal, scale = ctx.meta
-        if hasattr(ext(), "fmha_bwd"):
-            dq, dk, dv = ext().fmha_bwd(q, k, v, o, lse, do.contiguous(), causal, scale)
+        if os.environ.get("VO_ATTN_BWD", "native") != "torch" and hasattr(ext(), "fmha_bwd"):
+            B, S, H, D = o.shape
+            dq, dk, dv = ext().fmha_bwd(q, k, v, o, lse, do.contiguous().view(B, S, H, D), causal, scale)
             return dq, dk, dv, None, None
         # backward kernel not built: recompute through SDPA autograd
         B, S, H, D = o.shape

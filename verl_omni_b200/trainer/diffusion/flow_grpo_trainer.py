@@ -72,7 +72,15 @@ class PolicyGradientTrainer:
         if self.model_cfg.enable_gradient_checkpointing and hasattr(module, "gradient_checkpointing"):
             module.gradient_checkpointing = True
         module.to(self.device)
-        ref_module = copy.deepcopy(module) if self.actor_cfg.use_kl_loss else None
+        self.lora = self.model_cfg.lora_rank > 0
+        if self.lora:
+            from verl_omni_b200.models.lora import inject_lora
+
+            inject_lora(module, self.model_cfg.lora_rank, self.model_cfg.lora_alpha, self.model_cfg.target_modules,
+                        self.model_cfg.exclude_modules, adapters=tuple(self.model_cfg.policy_state_adapters),
+                        init=self.model_cfg.lora_init_weights)
+        # with LoRA the reference policy is the base model (adapters disabled): no second copy
+        ref_module = copy.deepcopy(module) if (self.actor_cfg.use_kl_loss and not self.lora) else None
         T = self.rollout_cfg.pipeline.num_inference_steps
         seq = int(np.prod(self.spec.latent_shape[-2:])) // 4
         self.scheduler = self.adapter.build_scheduler(T, image_seq_len=seq, device=self.device)
@@ -173,9 +181,15 @@ class PolicyGradientTrainer:
         if rollout_correction_enabled(self.algo_cfg.rollout_correction) and not self.algo_cfg.rollout_correction.bypass_mode:
             out, m2 = apply_rollout_correction_to_diffusion_batch(out, self.algo_cfg.rollout_correction)
             corr_metrics.update(m2)
-        if self.ref is not None:
+        if self.actor_cfg.use_kl_loss:
             with timer("ref"):
-                r = self.ref.infer_batch(out, keys=("prev_sample_mean",))
+                if self.ref is not None:
+                    r = self.ref.infer_batch(out, keys=("prev_sample_mean",))
+                else:
+                    from verl_omni_b200.models.lora import use_adapter
+
+                    with use_adapter(self.actor.module, None):
+                        r = self.actor.infer_batch(out, keys=("prev_sample_mean",))
                 out.batch["ref_prev_sample_mean"] = r.batch["prev_sample_mean"]
         if self.actor_cfg.diffusion_loss.loss_mode in ("flow_dppo", "grpo_guard"):
             with timer("old_mean"):
