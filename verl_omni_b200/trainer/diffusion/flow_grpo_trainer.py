@@ -18,6 +18,7 @@ import copy
 import logging
 import os
 import time
+import zlib
 from typing import Optional
 
 import numpy as np
@@ -150,26 +151,25 @@ class PolicyGradientTrainer:
         return adv[self.rank * B:(self.rank + 1) * B]
 
     # ------------------------------------------------------------------ one step
-    def step(self, global_ids: Optional[list[int]] = None) -> dict:
-        self.global_step += 1
-        timer = M.PhaseTimer(self.device)
-        t_start = time.perf_counter()
-        if self.device.type == "cuda":
-            torch.cuda.synchronize()
-        ids = self.local_prompt_ids(global_ids if global_ids is not None else self.sampler.next_batch())
-        with timer("gen"):
-            prompts = self.dataset.get_batch(ids)
-            cond = self.encode_prompts(prompts)
-            uid = np.array([f"{self.global_step}-{i}" for i in ids], dtype=object)
-            cond.non_tensor_batch["uid"] = uid
-            gen = cond.repeat(self.n, interleave=True)
-            base_seed = int(self.rollout_cfg.seed if self.rollout_cfg.seed is not None else 12345)
-            seed = (base_seed + self.global_step - 1) * 9973 + self.rank
-            out = self.rollout.generate(gen, seed=seed, global_step=self.global_step)
-            out.non_tensor_batch.update(gen.non_tensor_batch)
-        with timer("reward"):
-            scores, rmetrics = self.reward_fn(out)
-            scores = scores.to(self.device)
+    def generate(self, ids: list[int], *, rollout=None, seed_step: Optional[int] = None,
+                 uid_prefix: Optional[str] = None) -> tuple[DataProto, torch.Tensor, dict]:
+        """Rollout + decode + reward for this rank's prompt ids (``n`` samples each)."""
+        rollout = rollout or self.rollout
+        step = self.global_step if seed_step is None else seed_step
+        prompts = self.dataset.get_batch(ids)
+        cond = self.encode_prompts(prompts)
+        pre = uid_prefix if uid_prefix is not None else str(step)
+        cond.non_tensor_batch["uid"] = np.array([f"{pre}-{i}" for i in ids], dtype=object)
+        gen = cond.repeat(self.n, interleave=True)
+        base_seed = int(self.rollout_cfg.seed if self.rollout_cfg.seed is not None else 12345)
+        seed = (base_seed + step - 1) * 9973 + self.rank * 7 + (zlib.crc32(pre.encode()) & 0xFFFF) * 131
+        out = rollout.generate(gen, seed=seed, global_step=step)
+        out.non_tensor_batch.update({k: v[: len(out)] for k, v in gen.non_tensor_batch.items()})
+        scores, rmetrics = self.reward_fn(out)
+        return out, scores.to(self.device), rmetrics
+
+    def train_on(self, out: DataProto, scores: torch.Tensor, timer: "M.PhaseTimer") -> dict:
+        """old log-probs -> rollout correction -> reference means -> advantage -> actor update."""
         T = out.batch["step_index"].shape[1]
         with timer("old_log_prob"):
             if self.algo_cfg.rollout_correction.bypass_mode or self.actor_cfg.rollout_correction.bypass_mode:
@@ -205,6 +205,23 @@ class PolicyGradientTrainer:
                 for s in range(0, len(out), mini):
                     train_metrics = self.actor.train_batch(out.select_idxs(slice(s, min(len(out), s + mini))),
                                                            self.loss_fn)
+        metrics = dict(train_metrics)
+        metrics.update(corr_metrics)
+        metrics.update(M.compute_data_metrics_diffusion(scores, adv[:, 0], out.non_tensor_batch["uid"]))
+        return metrics
+
+    # ------------------------------------------------------------------ one step
+    def step(self, global_ids: Optional[list[int]] = None) -> dict:
+        self.global_step += 1
+        timer = M.PhaseTimer(self.device)
+        t_start = time.perf_counter()
+        if self.device.type == "cuda":
+            torch.cuda.synchronize()
+        ids = self.local_prompt_ids(global_ids if global_ids is not None else self.sampler.next_batch())
+        with timer("gen"):
+            out, scores, rmetrics = self.generate(ids)
+        metrics = {"training/global_step": self.global_step}
+        metrics.update(self.train_on(out, scores, timer))
         with timer("update_weights"):
             self.rollout.update_weights(self.actor.engine.get_per_tensor_param())
         save_freq = int(self.config.trainer.save_freq)
@@ -212,11 +229,7 @@ class PolicyGradientTrainer:
             with timer("save_checkpoint"):
                 self.save_checkpoint()
         step_time = time.perf_counter() - t_start
-        metrics = {"training/global_step": self.global_step}
-        metrics.update(train_metrics)
         metrics.update(rmetrics)
-        metrics.update(corr_metrics)
-        metrics.update(M.compute_data_metrics_diffusion(scores, adv[:, 0], out.non_tensor_batch["uid"]))
         metrics.update(M.compute_timing_metrics_diffusion(timer.timing, len(out)))
         metrics.update(M.compute_throughput_metrics_diffusion(step_time, len(out) * self.world, self.world))
         return metrics
