@@ -52,7 +52,9 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = 
     """softmax(q k^T * scale) v over [B, H, S, Dh]; returns [B, S, H*Dh]."""
     B, H, S, Dh = q.shape
     scale = scale if scale is not None else 1.0 / math.sqrt(Dh)
-    if q.is_cuda and _native():
+    # the tcgen05 kernels cover head_dim 64 / 128 (every DiT, ViT and LLM head here); other widths
+    # (the VAE's single 512-wide mid-block head, miniature test models) use SDPA
+    if q.is_cuda and _native() and Dh in (64, 128) and q.dtype == torch.bfloat16:
         o = _FMHA.apply(q, k, v, causal, scale)  # [B, S, H, Dh]
         return o.view(B, S, H * Dh)
     o = F.scaled_dot_product_attention(q, k, v, is_causal=causal, scale=scale)
