@@ -1,0 +1,141 @@
+"""Kernel microbenchmarks: ``python -m verl_omni_b200.ops.bench_ops {gemm,fmha,sde,adaln} [options]``.
+
+Times each op with CUDA events on the launching stream after warm-up (synchronised on both sides),
+reports achieved TFLOP/s or GB/s and the fraction of the measured peaks (``MEASURED_PEAKS.json``:
+cuBLAS bf16 GEMM burst and STREAM-style copy bandwidth).  ``--compare`` also times the library
+equivalent (cuBLAS via ``torch.matmul`` / SDPA) on the same inputs.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+
+
+def _peaks() -> dict:
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                     "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return {"tflops": d["bf16_tflops"], "gbs": d["hbm_gbs"], "src": "measured"}
+    except OSError:
+        return {"tflops": 1590.0, "gbs": 6650.0, "src": "fallback"}
+
+
+def timeit(fn, iters: int = 10, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def bench_gemm(a) -> list[dict]:
+    from verl_omni_b200.ops._ext import ext
+
+    e = ext()
+    M, N, K = a.M, a.N, a.K
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    w = (torch.randn(N, K, device="cuda") / K ** 0.5).bfloat16()
+    dy = torch.randn(M, N, device="cuda").bfloat16()
+    gw = torch.zeros(N, K, device="cuda")
+    flops = 2.0 * M * N * K
+    cases = {
+        "fwd": lambda: e.gemm_fwd(x, w, None, 0, None, None, 1),
+        "dgrad": lambda: e.gemm_dgrad(dy, w),
+        "wgrad": lambda: e.gemm_wgrad(dy, x, gw, True),
+    }
+    if a.compare:
+        cases["cublas_fwd"] = lambda: torch.matmul(x, w.t())
+        cases["cublas_dgrad"] = lambda: torch.matmul(dy, w)
+        cases["cublas_wgrad"] = lambda: torch.matmul(dy.t(), x)
+    out = []
+    for name in a.only.split(",") if a.only else cases:
+        ms = timeit(cases[name], a.iters)
+        out.append({"op": f"gemm_{name}", "M": M, "N": N, "K": K, "ms": round(ms, 4),
+                    "tflops": round(flops / ms / 1e9, 1)})
+    return out
+
+
+def bench_fmha(a) -> list[dict]:
+    from verl_omni_b200.ops._ext import ext
+
+    e = ext()
+    B, H, S, D = a.B, a.H, a.S, a.D
+    q, k, v = (torch.randn(B, H, S, D, device="cuda").bfloat16() for _ in range(3))
+    scale = 1 / math.sqrt(D)
+    o, lse = e.fmha_fwd(q, k, v, False, scale)
+    do = torch.randn_like(o)
+    flops_f = 4.0 * B * H * S * S * D
+    cases = {"fwd": (lambda: e.fmha_fwd(q, k, v, False, scale), flops_f)}
+    if hasattr(e, "fmha_bwd"):
+        cases["bwd"] = (lambda: e.fmha_bwd(q, k, v, o, lse, do, False, scale), 2.5 * flops_f)
+    if a.compare:
+        cases["sdpa_fwd"] = (lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v), flops_f)
+    out = []
+    for name, (fn, fl) in cases.items():
+        ms = timeit(fn, a.iters)
+        out.append({"op": f"fmha_{name}", "B": B, "H": H, "S": S, "D": D, "ms": round(ms, 4),
+                    "tflops": round(fl / ms / 1e9, 1)})
+    return out
+
+
+def bench_sde(a) -> list[dict]:
+    from verl_omni_b200.ops.sde import sde_step
+
+    B = a.B
+    x = torch.randn(B, 16, 64, 64, device="cuda")
+    v = torch.randn_like(x)
+    sig = torch.full((B,), 0.6, device="cuda")
+    ms = timeit(lambda: sde_step(x, v, sig, sig - 0.1, sigma_max=0.95, noise_level=0.7, seed=1), a.iters)
+    nbytes = 4 * x.numel() * 4  # read x, v; write mean, prev
+    return [{"op": "sde_step", "B": B, "ms": round(ms, 4), "gbs": round(nbytes / ms / 1e6, 1)}]
+
+
+def bench_adaln(a) -> list[dict]:
+    from verl_omni_b200.ops._ext import ext
+
+    B, S, D = a.B, a.S, 1536
+    x = torch.randn(B, S, D, device="cuda").bfloat16()
+    mod = torch.randn(B, 6 * D, device="cuda").bfloat16()
+    ms = timeit(lambda: ext().adaln_ln_fwd(x, mod, 0, D, None, None, S, 1e-6), a.iters)
+    nbytes = 2 * 2 * x.numel()
+    return [{"op": "adaln_ln_fwd", "B": B, "S": S, "D": D, "ms": round(ms, 4), "gbs": round(nbytes / ms / 1e6, 1)}]
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("op", choices=["gemm", "fmha", "sde", "adaln"])
+    ap.add_argument("--M", type=int, default=21712)
+    ap.add_argument("--N", type=int, default=6144)
+    ap.add_argument("--K", type=int, default=1536)
+    ap.add_argument("--B", type=int, default=16)
+    ap.add_argument("--H", type=int, default=24)
+    ap.add_argument("--S", type=int, default=1357)
+    ap.add_argument("--D", type=int, default=64)
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--only", default="")
+    ap.add_argument("--compare", action="store_true")
+    a = ap.parse_args()
+    pk = _peaks()
+    rows = {"gemm": bench_gemm, "fmha": bench_fmha, "sde": bench_sde, "adaln": bench_adaln}[a.op](a)
+    for r in rows:
+        if "tflops" in r:
+            r[f"frac_of_{pk['src']}_gemm_peak"] = round(r["tflops"] / pk["tflops"], 3)
+        if "gbs" in r:
+            r[f"frac_of_{pk['src']}_hbm"] = round(r["gbs"] / pk["gbs"], 3)
+        print(json.dumps(r), flush=True)
+
+
+if __name__ == "__main__":
+    main()
