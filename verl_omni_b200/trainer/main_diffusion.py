@@ -23,6 +23,10 @@ def run_diffusion(config) -> list[dict]:
         from verl_omni_b200.trainer.diffusion.v1.trainer import build_v1_trainer
 
         trainer = build_v1_trainer(config)
+    elif config.algorithm.get("trainer_type", "policy_gradient") == "direct_preference":
+        from verl_omni_b200.trainer.diffusion.preference_trainer import DirectPreferenceTrainer
+
+        trainer = DirectPreferenceTrainer(config)
     else:
         from verl_omni_b200.trainer.diffusion.flow_grpo_trainer import PolicyGradientTrainer
 
