@@ -1,0 +1,160 @@
+"""Ulysses sequence parallelism: all-to-all between sequence-sharded and head-sharded attention layouts.
+
+Same scheme as diffusers' ``ContextParallelConfig(ulysses_degree=sp)`` used by the reference
+(``verl_omni/workers/engine/fsdp/diffusers_impl.py:175-194,458-462``): every rank holds ``S/sp`` tokens
+of each sample; before attention q/k/v go from ``[B, H, S/sp, D]`` to ``[B, H/sp, S, D]`` (all heads
+of the local sequence -> local heads of the whole sequence), attention runs on full sequences, and the
+token-major output goes back from ``[B, S, H/sp*D]`` to ``[B, S/sp, H*D]``.  The gathered sequence is
+ordered by source rank; full (non-causal) attention is invariant to key order and the inverse exchange
+restores each rank's queries.
+
+The exchanges are autograd functions (backward = the inverse exchange).  On NCCL they are
+``all_to_all_single``; gloo has no all-to-all, so CPU ranks emulate it with an all-gather.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from verl_omni_b200.parallel import dist as D
+
+
+def _all_to_all(x: torch.Tensor, group) -> torch.Tensor:
+    """x [sp, ...] (chunk r goes to rank r) -> [sp, ...] (chunk r came from rank r)."""
+    sp = D.world_size(group)
+    if sp == 1:
+        return x
+    x = x.contiguous()
+    if dist.get_backend(group) == "nccl":
+        out = torch.empty_like(x)
+        dist.all_to_all_single(out, x, group=group)
+        return out
+    parts = [torch.empty_like(x) for _ in range(sp)]
+    dist.all_gather(parts, x, group=group)
+    me = D.rank(group)
+    return torch.stack([parts[src][me] for src in range(sp)], 0)
+
+
+class _SeqToHead(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        B, H, S, Dh = x.shape
+        sp = D.world_size(group)
+        if H % sp:
+            raise ValueError(f"heads ({H}) must be divisible by the Ulysses degree ({sp})")
+        send = x.reshape(B, sp, H // sp, S, Dh).permute(1, 0, 2, 3, 4)  # [sp, B, H/sp, S, D]
+        recv = _all_to_all(send, group)  # [sp(src), B, H/sp, S, D]
+        return recv.permute(1, 2, 0, 3, 4).reshape(B, H // sp, sp * S, Dh)
+
+    @staticmethod
+    def backward(ctx, g):
+        B, Hl, St, Dh = g.shape
+        sp = D.world_size(ctx.group)
+        send = g.reshape(B, Hl, sp, St // sp, Dh).permute(2, 0, 1, 3, 4)  # [sp(dst), B, H/sp, S/sp, D]
+        recv = _all_to_all(send, ctx.group)  # [sp(src head slice), B, H/sp, S/sp, D]
+        return recv.permute(1, 0, 2, 3, 4).reshape(B, sp * Hl, St // sp, Dh), None
+
+
+class _HeadToSeq(torch.autograd.Function):
+    """token-major [B, S, Hl*D] (sequence ordered by source rank) -> [B, S/sp, H*D]."""
+
+    @staticmethod
+    def forward(ctx, o, group, Dh):
+        ctx.group, ctx.Dh = group, Dh
+        B, St, W = o.shape
+        sp = D.world_size(group)
+        send = o.reshape(B, sp, St // sp, W).permute(1, 0, 2, 3)  # [sp(dst), B, S/sp, Hl*D]
+        recv = _all_to_all(send, group)  # [sp(src head slice), B, S/sp, Hl*D]
+        return recv.permute(1, 2, 0, 3).reshape(B, St // sp, sp * W)
+
+    @staticmethod
+    def backward(ctx, g):
+        B, Sl, Wf = g.shape
+        sp = D.world_size(ctx.group)
+        W = Wf // sp
+        send = g.reshape(B, Sl, sp, W).permute(2, 0, 1, 3)  # [sp(dst head slice), B, S/sp, W]
+        recv = _all_to_all(send, ctx.group)  # [sp(src seq chunk), B, S/sp, W]
+        return recv.permute(1, 0, 2, 3).reshape(B, sp * Sl, W), None, None
+
+
+def seq_to_head(x: torch.Tensor, group) -> torch.Tensor:
+    return _SeqToHead.apply(x, group)
+
+
+def head_to_seq(o: torch.Tensor, group, head_dim: int) -> torch.Tensor:
+    return _HeadToSeq.apply(o, group, head_dim)
+
+
+def ulysses_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, group, causal: bool = False,
+                      scale: Optional[float] = None) -> torch.Tensor:
+    """q/k/v [B, H, S/sp, D] (local tokens, all heads) -> token-major output [B, S/sp, H*D]."""
+    from verl_omni_b200.ops.attention import attention
+
+    if D.world_size(group) == 1:
+        return attention(q, k, v, causal=causal, scale=scale)
+    Dh = q.shape[-1]
+    o = attention(seq_to_head(q, group), seq_to_head(k, group), seq_to_head(v, group), causal=causal, scale=scale)
+    return head_to_seq(o, group, Dh)
+
+
+class _GatherSeq(torch.autograd.Function):
+    """All-gather along dim 1 (tokens); backward keeps this rank's slice (every rank's loss is identical)."""
+
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        sp = D.world_size(group)
+        if sp == 1:
+            return x
+        parts = [torch.empty_like(x) for _ in range(sp)]
+        dist.all_gather(parts, x.contiguous(), group=group)
+        ctx.n = x.shape[1]
+        return torch.cat(parts, 1)
+
+    @staticmethod
+    def backward(ctx, g):
+        if D.world_size(ctx.group) == 1:
+            return g, None
+        r = D.rank(ctx.group)
+        return g[:, r * ctx.n:(r + 1) * ctx.n].contiguous(), None
+
+
+def gather_sequence(x: torch.Tensor, group) -> torch.Tensor:
+    return _GatherSeq.apply(x, group)
+
+
+def shard_sequence(x: torch.Tensor, group, dim: int = 1) -> torch.Tensor:
+    sp, r = D.world_size(group), D.rank(group)
+    if sp == 1:
+        return x
+    n = x.shape[dim]
+    if n % sp:
+        raise ValueError(f"sequence length {n} is not divisible by the Ulysses degree {sp}; pad first")
+    return x.narrow(dim, r * (n // sp), n // sp)
+
+
+def pad_to_multiple(x: torch.Tensor, m: int, dim: int = 1) -> torch.Tensor:
+    """Zero-pad ``dim`` to a multiple of ``m`` (the reference pads prompt embeds for SP, ``diffusers_impl.py:574-583``)."""
+    n = x.shape[dim]
+    pad = (-n) % m
+    if pad == 0:
+        return x
+    shape = list(x.shape)
+    shape[dim] = pad
+    return torch.cat([x, x.new_zeros(shape)], dim)
+
+
+def make_sp_groups(sp: int):
+    """Consecutive ranks form Ulysses groups of size ``sp``; returns (sp_group, dp_group) of this rank."""
+    ws, r = D.world_size(), D.rank()
+    if sp == 1 or ws == 1:
+        return None, None
+    if ws % sp:
+        raise ValueError(f"world size {ws} not divisible by sp {sp}")
+    sp_groups = [dist.new_group(list(range(i, i + sp))) for i in range(0, ws, sp)]
+    dp_groups = [dist.new_group(list(range(j, ws, sp))) for j in range(sp)]
+    return sp_groups[r // sp], dp_groups[r % sp]
