@@ -54,7 +54,8 @@ class DiTBlock(nn.Module):
         super().__init__()
         D = cfg.hidden
         self.D, self.H, self.dh = D, cfg.heads, D // cfg.heads
-        self.modulation = Linear(D, 6 * D)
+        # per-block learned offset added to the shared time projection (Wan2.1 layout)
+        self.modulation = nn.Parameter(torch.randn(6 * D) * 0.02)
         self.qkv = Linear(D, 3 * D)
         self.norm_q, self.norm_k = RMSWeight(self.dh), RMSWeight(self.dh)
         self.o = Linear(D, D)
@@ -67,11 +68,11 @@ class DiTBlock(nn.Module):
         self.ffn_1, self.ffn_2 = Linear(D, cfg.ffn), Linear(cfg.ffn, D)
         self.eps = cfg.eps
 
-    def forward(self, x, ctx, temb_act, rope=None):
+    def forward(self, x, ctx, temb_proj, rope=None):
         B, S, D = x.shape
         St = ctx.shape[1]
         H, dh = self.H, self.dh
-        mod = self.modulation(temb_act)
+        mod = temb_proj + self.modulation.to(temb_proj.dtype)[None]
         h = adaln_layernorm(x, mod, 0, 1, 6, self.eps)
         qkv = self.qkv(h).reshape(B * S, 3 * D)
         mk = lambda n: torch.empty(B, H, n, dh, device=x.device, dtype=x.dtype)  # noqa: E731
@@ -108,6 +109,7 @@ class DiT(nn.Module):
         self.text_embedding_1 = Linear(cfg.text_dim, D)
         self.text_embedding_2 = Linear(D, D)
         self.time_embedding = TimestepMLP(cfg.freq_dim, D)
+        self.time_projection = Linear(D, 6 * D)
         self.blocks = nn.ModuleList([DiTBlock(cfg) for _ in range(cfg.depth)])
         self.head_mod = Linear(D, 2 * D)
         self.head = Linear(D, pt * ph * pw * cfg.out_channels)
@@ -141,13 +143,14 @@ class DiT(nn.Module):
         x = self.patch_embedding(x)
         temb = self.time_embedding(timestep_embedding(timestep, cfg.freq_dim).to(dt))
         temb_act = F.silu(temb)
+        temb_proj = self.time_projection(temb_act)
         ctx = self.text_embedding_2(F.gelu(self.text_embedding_1(context.to(dt)), approximate="tanh"))
         rope = self._rope(*grid, x.device) if cfg.rope else None
         for blk in self.blocks:
             if self.gradient_checkpointing and torch.is_grad_enabled():
-                x = torch.utils.checkpoint.checkpoint(blk, x, ctx, temb_act, rope, use_reentrant=False)
+                x = torch.utils.checkpoint.checkpoint(blk, x, ctx, temb_proj, rope, use_reentrant=False)
             else:
-                x = blk(x, ctx, temb_act, rope)
+                x = blk(x, ctx, temb_proj, rope)
         mod = self.head_mod(temb_act)
         x = adaln_layernorm(x, mod, 0, 1, 2, cfg.eps)
         out = self.head(x)

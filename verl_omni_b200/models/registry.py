@@ -47,6 +47,14 @@ ARCHS: dict[str, ArchSpec] = {
     "flux1_dev": ArchSpec(
         "flux1_dev", "FluxDiT", _flux_build, (16, 128, 128),
         {"prompt_embeds": (512, 4096), "pooled_prompt_embeds": (768,)}, reward="vit", image_size=1024),
+    "flux_tiny": ArchSpec(
+        "flux_tiny", "FluxDiT", lambda: __import__("verl_omni_b200.models.flux", fromlist=["x"]).FluxDiT(
+            __import__("verl_omni_b200.models.flux", fromlist=["x"]).FluxConfig.tiny()), (4, 8, 8),
+        {"prompt_embeds": (12, 48), "pooled_prompt_embeds": (32,)}, reward="mlp", image_size=64),
+    "wan_tiny": ArchSpec(
+        "wan_tiny", "WanDiT", lambda: DiT(DiTConfig(in_channels=4, out_channels=4, hidden=128, heads=2, depth=2,
+                                                    ffn=256, text_dim=48)), (4, 3, 8, 8),
+        {"prompt_embeds": (12, 48)}, reward="mlp", image_size=64),
     "wan21_14b": ArchSpec(
         "wan21_14b", "WanDiT", lambda: DiT(DiTConfig.wan21_14b()), (16, 21, 60, 104),
         {"prompt_embeds": (512, 4096)}, reward="vit_video", image_size=480),
