@@ -10,6 +10,7 @@
 // normaliser.  The backward is elementwise: dL/dv = cb*(g_mean + g_logp*dlogp/dmean).
 // Math restates verl_omni/pipelines/schedulers/flow_match_sde.py:214-313.
 #include "common.cuh"
+#include "sde_noalloc.h"
 
 namespace vo {
 namespace {
@@ -264,3 +265,63 @@ torch::Tensor sde_step_bwd(torch::Tensor x, torch::Tensor prev, torch::Tensor me
 }
 
 }  // namespace vo
+
+// ------------------------------------------------------------------------------ allocation-free variant
+// Scratch for the per-block partial sums of vo_sde_step_fwd_noalloc (see sde_noalloc.h).  In host code
+// this name is only a stand-in for the symbol; the device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) float g_sde_noalloc_partials[VO_SDE_NOALLOC_MAX_PARTIALS];
+
+namespace {
+constexpr int kMaxDevices = 64;
+float* g_sde_noalloc_ptr[kMaxDevices] = {nullptr};
+int g_sde_noalloc_sms[kMaxDevices] = {0};
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int vo_sde_step_fwd_noalloc(
+    const float* x, const float* v, const float* sigma, const float* sigma_prev, const float* prev_in,
+    const float* noise, float* prev_out, float* mean_out, float* logp_out, float* std_out, int B, int64_t n,
+    float sigma_max, float eta, int sde_type, uint64_t seed, uint32_t offset, int want_logp, int norm,
+    cudaStream_t stream) {
+  if (!x || !v || !sigma || !sigma_prev || !mean_out || !std_out || B <= 0 || n <= 0 || sde_type < 0 ||
+      sde_type > 2 || (want_logp && !logp_out) || (!prev_in && !prev_out))
+    return -1;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= kMaxDevices) return -1;
+  if (!g_sde_noalloc_ptr[dev]) {  // one-time set-up per device, with that device current
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_sde_noalloc_partials);
+    if (e != cudaSuccess) return (int)e;
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return (int)e;
+    g_sde_noalloc_sms[dev] = sms;
+    g_sde_noalloc_ptr[dev] = static_cast<float*>(ptr);
+  }
+  float* partial = g_sde_noalloc_ptr[dev];
+  // same chunking as the allocating entry point: ~4 blocks per SM, chunks of multiples of 1024
+  const int target = 4 * g_sde_noalloc_sms[dev];
+  int nchunks = (int)std::max<int64_t>(1, std::min<int64_t>((n + 1023) / 1024, (target + B - 1) / B));
+  const int64_t chunk = ((n + nchunks - 1) / nchunks + 1023) / 1024 * 1024;
+  nchunks = (int)((n + chunk - 1) / chunk);
+  if ((int64_t)B * nchunks > VO_SDE_NOALLOC_MAX_PARTIALS) return -2;
+  float* prev_dst = prev_in ? const_cast<float*>(prev_in) : prev_out;
+  const dim3 grid(nchunks, B);
+  if (prev_in)
+    vo::sde_fwd_kernel<true, false><<<grid, 256, 0, stream>>>(x, v, sigma, sigma_prev, prev_in, nullptr, prev_dst,
+                                                             mean_out, partial, n, chunk, nchunks, sigma_max, eta,
+                                                             sde_type, norm != 0, seed, offset);
+  else if (noise)
+    vo::sde_fwd_kernel<false, true><<<grid, 256, 0, stream>>>(x, v, sigma, sigma_prev, nullptr, noise, prev_dst,
+                                                             mean_out, partial, n, chunk, nchunks, sigma_max, eta,
+                                                             sde_type, norm != 0, seed, offset);
+  else
+    vo::sde_fwd_kernel<false, false><<<grid, 256, 0, stream>>>(x, v, sigma, sigma_prev, nullptr, nullptr, prev_dst,
+                                                              mean_out, partial, n, chunk, nchunks, sigma_max, eta,
+                                                              sde_type, norm != 0, seed, offset);
+  vo::sde_finalize_kernel<<<(B + 7) / 8, 256, 0, stream>>>(partial, sigma, sigma_prev, want_logp ? logp_out : nullptr,
+                                                           std_out, B, nchunks, n, sigma_max, eta, sde_type,
+                                                           norm != 0);
+  return (int)cudaGetLastError();
+}
