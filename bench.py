@@ -110,6 +110,8 @@ def main() -> None:
     ap.add_argument("--sde-steps", type=int, default=10)
     ap.add_argument("--micro", type=int, default=16)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="after warm-up, run one step under torch.profiler and print the top CUDA kernels (no bench line)")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -156,6 +158,16 @@ def main() -> None:
         print(json.dumps({"warmup_s": round(t_warm, 2), "timing": {k: round(v, 3) for k, v in m.items()
                                                                    if k.startswith("timing_s/")}}),
               file=sys.stderr, flush=True)
+    if args.profile_step:
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            trainer.step()
+            torch.cuda.synchronize()
+        if info.rank == 0:
+            print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=40, max_name_column_width=70))
+        D.destroy()
+        return
     # ----------------------------------------------------------- device-timed region
     clock_path = os.path.join(os.environ.get("VO_BENCH_DIR", "/tmp"), f"clocks_{info.rank}.csv")
     sampler = _clock_sampler(clock_path) if info.local_rank == 0 else None

@@ -4,11 +4,11 @@
 //   Q [BH, Sq, D], K/V [BH, Skv, D] (bf16, contiguous per head); O written token-major
 //   [B, Sq, H, D]; D in {64, 128}; optional causal mask (query i sees keys <= i).
 //
-// One CTA per (128-query tile, head).  Roles (192 threads):
-//   warp 0      TMA producer: Q once, then K_j/V_j into a 2-stage ring (3D tensor maps, OOB rows
-//               zero-filled per head so ragged Sq/Skv need no padding);
-//   warp 1      TMEM allocator + MMA issuer: S_j = Q K_j^T into TMEM (double buffered), then
-//               O_j = P_j V_j into TMEM (double buffered), all tcgen05.mma kind::f16;
+// One CTA per (128-query tile, head); head_dim 64 runs two CTAs per SM.  Roles (192 threads):
+//   warp 0      TMA producer: Q once, then K_{j+1} (2-stage ring) ahead of V_j (3D tensor maps, OOB
+//               rows zero-filled per head so ragged Sq/Skv need no padding);
+//   warp 1      TMEM allocator + MMA issuer: S_j = Q K_j^T into TMEM, then O_j = P_j V_j into TMEM,
+//               all tcgen05.mma kind::f16 (S/O/P double buffered for head_dim 128);
 //   warps 2..5  softmax warpgroup, one query row per thread: row max and exp2 over S_j (two
 //               passes of tcgen05.ld), P_j written as bf16 into 128B-swizzled SMEM (the A operand
 //               of the PV MMA), online rescaling of the register-resident O accumulator with each
@@ -118,36 +118,46 @@ struct Params {
   float* lse;        // [B*H, Sq] natural log
 };
 
-template <int D>
+// NB = number of S / O / P buffers.  NB == 1 (head_dim 64): 256 TMEM columns and 112 KB of SMEM per
+// CTA so two CTAs share an SM and one CTA's softmax overlaps the other's MMAs.  NB == 2 (head_dim 128):
+// one CTA per SM with double-buffered S/O/P inside the CTA.
+// K always has a 2-stage ring (the next S MMA must not wait for a load); V has NB stages (V_j is
+// consumed late, by the PV MMA after the softmax, so one stage hides its load behind that softmax).
+template <int D, int NB>
 struct Smem {
   static constexpr int TILE = 128 * D * 2;  // one 128-row tile of Q/K/V (D/64 chunks of 16 KB)
   static constexpr int P = 128 * 128 * 2;   // P tile (two 64-column chunks of 16 KB)
+  static constexpr int VST = NB;
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = TILE;
   static constexpr int V_OFF = 3 * TILE;
-  static constexpr int P_OFF = 5 * TILE;
-  static constexpr int BAR_OFF = 5 * TILE + 2 * P;
+  static constexpr int P_OFF = (3 + VST) * TILE;
+  static constexpr int BAR_OFF = P_OFF + NB * P;
   static constexpr int BYTES = BAR_OFF + 256;
+  static constexpr int TMEM_COLS = NB == 1 ? 256 : 512;
+  static constexpr int MIN_BLOCKS = NB == 1 ? 2 : 1;
 };
 
-template <int D>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+template <int D, int NB>
+__global__ void __launch_bounds__(NUM_THREADS, Smem<D, NB>::MIN_BLOCKS)
     fmha_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                     const __grid_constant__ CUtensorMap mv, Params p) {
-  using L = Smem<D>;
+  using L = Smem<D, NB>;
   extern __shared__ __align__(1024) uint8_t raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR_OFF);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* k_empty = bars + 3;   // [2]
   uint64_t* s_full = bars + 5;    // [2]
   uint64_t* s_free = bars + 7;    // [2]
   uint64_t* p_full = bars + 9;    // [2]
   uint64_t* p_free = bars + 11;   // [2]
   uint64_t* o_full = bars + 13;   // [2]
   uint64_t* o_free = bars + 15;   // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* v_full = bars + 17;   // [2]
+  uint64_t* v_empty = bars + 19;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -161,8 +171,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 4);
       mbar_init(&p_full[i], 4);
@@ -174,30 +186,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(L::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   fence_before();
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tmem_slot;
+  // S buffers at columns [0, NB*128), O buffers after them
   const uint32_t S_COL[2] = {0u, 128u};
-  const uint32_t O_COL[2] = {256u, 256u + D};
+  const uint32_t O_COL[2] = {NB * 128u, NB * 128u + D};
 
   if (warp == 0) {
     if (lane == 0) {
       mbar_expect_tx(q_full, L::TILE);
 #pragma unroll
       for (int c = 0; c < D / 64; ++c) tma_load_3d(sm + L::Q_OFF + c * 16384, &mq, q_full, c * 64, q0, bh);
-      for (int j = 0; j < nkv; ++j) {
+      // order: K_0, then for each j: K_{j+1} (2-slot ring), V_j (VST-slot ring)
+      auto load_k = [&](int j) -> bool {
         const int s = j & 1;
-        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, 11)) break;
-        mbar_expect_tx(&kv_full[s], 2 * L::TILE);
+        if (!mbar_wait(&k_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, 11)) return false;
+        mbar_expect_tx(&k_full[s], L::TILE);
 #pragma unroll
-        for (int c = 0; c < D / 64; ++c) {
-          tma_load_3d(sm + L::K_OFF + s * L::TILE + c * 16384, &mk, &kv_full[s], c * 64, j * BKV, bh);
-          tma_load_3d(sm + L::V_OFF + s * L::TILE + c * 16384, &mv, &kv_full[s], c * 64, j * BKV, bh);
-        }
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_3d(sm + L::K_OFF + s * L::TILE + c * 16384, &mk, &k_full[s], c * 64, j * BKV, bh);
+        return true;
+      };
+      bool ok = nkv > 0 ? load_k(0) : true;
+      for (int j = 0; ok && j < nkv; ++j) {
+        if (j + 1 < nkv && !(ok = load_k(j + 1))) break;
+        const int s = j % L::VST;
+        if (!mbar_wait(&v_empty[s], ((j / L::VST) & 1) ^ 1, abort_flag, 10)) break;
+        mbar_expect_tx(&v_full[s], L::TILE);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_3d(sm + L::V_OFF + s * L::TILE + c * 16384, &mv, &v_full[s], c * 64, j * BKV, bh);
       }
     }
   } else if (warp == 1) {
@@ -208,33 +232,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t qa = smem_u32(sm + L::Q_OFF);
       for (int j = 0; ok && j <= nkv; ++j) {
         if (j < nkv) {
-          const int s = j & 1;
-          if (!mbar_wait(&kv_full[s], (j >> 1) & 1, abort_flag, 13)) break;
-          if (!mbar_wait(&s_free[s], ((j >> 1) & 1) ^ 1, abort_flag, 14)) break;
+          const int st = j & 1, b = j % NB;
+          if (!mbar_wait(&k_full[st], (j >> 1) & 1, abort_flag, 13)) break;
+          if (!mbar_wait(&s_free[b], ((j / NB) & 1) ^ 1, abort_flag, 14)) break;
           fence_after();
-          const uint32_t ka = smem_u32(sm + L::K_OFF + s * L::TILE);
+          const uint32_t ka = smem_u32(sm + L::K_OFF + st * L::TILE);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            mma(tmem + S_COL[s], desc(qa + off, 16, 1024), desc(ka + off, 16, 1024), id_s, kk > 0);
+            mma(tmem + S_COL[b], desc(qa + off, 16, 1024), desc(ka + off, 16, 1024), id_s, kk > 0);
           }
-          commit(&s_full[s]);
+          commit(&s_full[b]);
+          commit(&k_empty[st]);
         }
         if (j >= 1) {
-          const int jj = j - 1, s = jj & 1;
-          if (!mbar_wait(&p_full[s], (jj >> 1) & 1, abort_flag, 15)) break;
-          if (!mbar_wait(&o_free[s], ((jj >> 1) & 1) ^ 1, abort_flag, 16)) break;
+          const int jj = j - 1, st = jj % L::VST, b = jj % NB;
+          if (!mbar_wait(&v_full[st], (jj / L::VST) & 1, abort_flag, 20)) break;
+          if (!mbar_wait(&p_full[b], (jj / NB) & 1, abort_flag, 15)) break;
+          if (!mbar_wait(&o_free[b], ((jj / NB) & 1) ^ 1, abort_flag, 16)) break;
           fence_after();
-          const uint32_t pa = smem_u32(sm + L::P_OFF + s * L::P);
-          const uint32_t va = smem_u32(sm + L::V_OFF + s * L::TILE);
+          const uint32_t pa = smem_u32(sm + L::P_OFF + b * L::P);
+          const uint32_t va = smem_u32(sm + L::V_OFF + st * L::TILE);
 #pragma unroll
           for (int kk = 0; kk < BKV / 16; ++kk) {
             const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-            mma(tmem + O_COL[s], desc(pa + aoff, 16, 1024), desc(va + kk * 2048, 16384, 1024), id_o, kk > 0);
+            mma(tmem + O_COL[b], desc(pa + aoff, 16, 1024), desc(va + kk * 2048, 16384, 1024), id_o, kk > 0);
           }
-          commit(&o_full[s]);
-          commit(&p_free[s]);
-          commit(&kv_empty[s]);
+          commit(&o_full[b]);
+          commit(&p_free[b]);
+          commit(&v_empty[st]);
         }
       }
     }
@@ -252,28 +278,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int j = 0; j <= nkv && ok; ++j) {
       float alpha_j = 0.f;
       if (j < nkv) {
-        const int s = j & 1;
-        if (!mbar_wait(&s_full[s], (j >> 1) & 1, abort_flag, 17)) {
+        const int s = j % NB;
+        if (!mbar_wait(&s_full[s], (j / NB) & 1, abort_flag, 17)) {
           ok = false;
           break;
         }
         fence_after();
         const int kv0 = j * BKV;
+        // blocks fully inside the key range and (causal) fully below the diagonal need no masks
+        const bool full = kv0 + BKV <= p.Skv && (!p.causal || kv0 + BKV - 1 <= q0);
         float mx = -INFINITY;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           float v[32];
           ld32(trow + S_COL[s] + c * 32, v);
+          if (full) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int kv = kv0 + c * 32 + i;
-            const bool valid = kv < p.Skv && (!p.causal || kv <= q);
-            if (valid) mx = fmaxf(mx, v[i]);
+            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, v[i]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int kv = kv0 + c * 32 + i;
+              const bool valid = kv < p.Skv && (!p.causal || kv <= q);
+              if (valid) mx = fmaxf(mx, v[i]);
+            }
           }
         }
         const float m_new = fmaxf(m, mx * p.scale_log2);
-        // P buffer s must be free (PV of block j-2 done)
-        if (!mbar_wait(&p_free[s], ((j >> 1) & 1) ^ 1, abort_flag, 18)) {
+        // P buffer s must be free (its previous PV MMA done)
+        if (!mbar_wait(&p_free[s], ((j / NB) & 1) ^ 1, abort_flag, 18)) {
           ok = false;
           break;
         }
@@ -293,8 +326,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               for (int t = 0; t < 2; ++t) {
                 const int i = g * 8 + h * 2 + t;
                 const int kv = kv0 + c * 32 + i;
-                const bool valid = kv < p.Skv && (!p.causal || kv <= q);
-                e[t] = valid ? ex2(v[i] * p.scale_log2 - m_new) : 0.f;
+                const bool valid = full || (kv < p.Skv && (!p.causal || kv <= q));
+                e[t] = valid ? ex2(fmaf(v[i], p.scale_log2, -m_new)) : 0.f;
                 rs += e[t];
               }
               __nv_bfloat162 b2 = __floats2bfloat162_rn(e[0], e[1]);
@@ -319,8 +352,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         m = m_new;
       }
       if (j >= 1) {  // fold O_{j-1}
-        const int jj = j - 1, s = jj & 1;
-        if (!mbar_wait(&o_full[s], (jj >> 1) & 1, abort_flag, 19)) {
+        const int jj = j - 1, s = jj % NB;
+        if (!mbar_wait(&o_full[s], (jj / NB) & 1, abort_flag, 19)) {
           ok = false;
           break;
         }
@@ -358,7 +391,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) {
     __syncwarp();
     fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::TMEM_COLS));
   }
 }
 
@@ -411,20 +444,21 @@ extern "C" int vo_fmha_fwd(const void* q, const void* k, const void* v, void* o,
   p.lse = lse;
   const long long grid = (long long)p.nq_tiles * B * H;
   if (D == 64) {
+    using L = Smem<64, 1>;
     static bool set = false;
     if (!set) {
-      cudaFuncSetAttribute(fmha_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem<64>::BYTES + 1024);
+      cudaFuncSetAttribute(fmha_fwd_kernel<64, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES + 1024);
       set = true;
     }
-    fmha_fwd_kernel<64><<<(unsigned)grid, NUM_THREADS, Smem<64>::BYTES + 1024, stream>>>(mq, mk, mv, p);
+    fmha_fwd_kernel<64, 1><<<(unsigned)grid, NUM_THREADS, L::BYTES + 1024, stream>>>(mq, mk, mv, p);
   } else {
+    using L = Smem<128, 2>;
     static bool set = false;
     if (!set) {
-      cudaFuncSetAttribute(fmha_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           Smem<128>::BYTES + 1024);
+      cudaFuncSetAttribute(fmha_fwd_kernel<128, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES + 1024);
       set = true;
     }
-    fmha_fwd_kernel<128><<<(unsigned)grid, NUM_THREADS, Smem<128>::BYTES + 1024, stream>>>(mq, mk, mv, p);
+    fmha_fwd_kernel<128, 2><<<(unsigned)grid, NUM_THREADS, L::BYTES + 1024, stream>>>(mq, mk, mv, p);
   }
   return (int)cudaGetLastError();
 }
