@@ -1,0 +1,235 @@
+"""Qwen3-Omni-30B-A3B-shaped MoE "thinker" LLM with audio and vision encoders.
+
+Architecture (random-init): ``layers`` decoder blocks of RMSNorm -> GQA attention (``q_heads`` query
+heads, ``kv_heads`` key/value heads, per-head RMS q/k-norm, RoPE) -> RMSNorm -> sparse MoE
+(softmax router, top-``k`` of ``experts`` SwiGLU experts of width ``expert_ffn``, renormalised gates);
+tied-size LM head over ``vocab``.  Multimodal prompts carry placeholder ids (``audio_token`` /
+``image_token``) whose embeddings are replaced by the projected outputs of an audio encoder over
+128-dim log-mel frames and a ViT over image patches, as in the reference's Qwen3-Omni thinker
+adapter (``verl_omni/pipelines/qwen3_omni/thinker_training_adapter.py:34-206``).
+
+Expert computation groups tokens by expert (sort by expert id, one GEMM per non-empty expert on the
+tcgen05 GEMM; combine weighted by the gates).  ``ExpertParallel`` dispatches token groups to the
+expert-owning ranks with all-to-all and combines the results back (see ``parallel/expert_parallel.py``).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from verl_omni_b200.models.layers import Linear, rope_table
+from verl_omni_b200.ops.attention import attention
+from verl_omni_b200.ops import linear as L
+
+
+@dataclass
+class MoEConfig:
+    vocab: int = 151936
+    hidden: int = 2048
+    layers: int = 48
+    q_heads: int = 32
+    kv_heads: int = 4
+    head_dim: int = 128
+    experts: int = 128
+    top_k: int = 8
+    expert_ffn: int = 768
+    rope_theta: float = 1_000_000.0
+    audio_layers: int = 32
+    audio_dim: int = 1280
+    audio_mel: int = 128
+    vision_layers: int = 27
+    vision_dim: int = 1152
+    vision_patch_dim: int = 3 * 16 * 16
+    audio_token: int = 151646
+    image_token: int = 151655
+    eps: float = 1e-6
+
+    @staticmethod
+    def qwen3_omni_30b_a3b() -> "MoEConfig":
+        return MoEConfig()
+
+    @staticmethod
+    def tiny() -> "MoEConfig":
+        return MoEConfig(vocab=512, hidden=64, layers=2, q_heads=4, kv_heads=2, head_dim=16, experts=8, top_k=2,
+                         expert_ffn=32, audio_layers=1, audio_dim=32, audio_mel=16, vision_layers=1, vision_dim=32,
+                         vision_patch_dim=48, audio_token=510, image_token=511)
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype)
+
+
+def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """x [B, H, S, D] (rotate-half convention), cos/sin [S, D/2]."""
+    d2 = x.shape[-1] // 2
+    x1, x2 = x[..., :d2], x[..., d2:]
+    c, s = cos.to(x.dtype)[None, None], sin.to(x.dtype)[None, None]
+    return torch.cat([x1 * c - x2 * s, x1 * s + x2 * c], -1)
+
+
+class MoEBlock(nn.Module):
+    def __init__(self, cfg: MoEConfig):
+        super().__init__()
+        self.cfg = cfg
+        D, hd = cfg.hidden, cfg.head_dim
+        self.ln1 = nn.Parameter(torch.ones(D))
+        self.q_proj = Linear(D, cfg.q_heads * hd, bias=False)
+        self.kv_proj = Linear(D, 2 * cfg.kv_heads * hd, bias=False)
+        self.o_proj = Linear(cfg.q_heads * hd, D, bias=False)
+        self.q_norm = nn.Parameter(torch.ones(hd))
+        self.k_norm = nn.Parameter(torch.ones(hd))
+        self.ln2 = nn.Parameter(torch.ones(D))
+        self.router = Linear(D, cfg.experts, bias=False)
+        E, F_ = cfg.experts, cfg.expert_ffn
+        self.w_gate_up = nn.Parameter(torch.randn(E, 2 * F_, D) * 0.02)  # [E, 2F, D]
+        self.w_down = nn.Parameter(torch.randn(E, D, F_) * 0.02)  # [E, D, F]
+
+    def attn(self, x, cos, sin, cache: Optional[dict], pos0: int):
+        cfg = self.cfg
+        B, S, D = x.shape
+        hd = cfg.head_dim
+        h = rms_norm(x, self.ln1, cfg.eps)
+        q = self.q_proj(h).view(B, S, cfg.q_heads, hd).transpose(1, 2)
+        kv = self.kv_proj(h).view(B, S, 2, cfg.kv_heads, hd)
+        k, v = kv[:, :, 0].transpose(1, 2), kv[:, :, 1].transpose(1, 2)
+        q = apply_rope(rms_norm(q, self.q_norm, cfg.eps), cos, sin)
+        k = apply_rope(rms_norm(k, self.k_norm, cfg.eps), cos, sin)
+        if cache is not None:
+            if "k" in cache:
+                k = torch.cat([cache["k"], k], 2)
+                v = torch.cat([cache["v"], v], 2)
+            cache["k"], cache["v"] = k, v
+        rep = cfg.q_heads // cfg.kv_heads
+        kk = k.repeat_interleave(rep, 1).contiguous()
+        vv = v.repeat_interleave(rep, 1).contiguous()
+        causal = S > 1 and (cache is None or pos0 == 0)
+        if S == 1 or (cache is not None and pos0 > 0):
+            causal = False  # decode: the new token sees every cached key
+        o = attention(q.contiguous(), kk, vv, causal=causal)
+        return x + self.o_proj(o)
+
+    def moe(self, x, ep=None):
+        cfg = self.cfg
+        B, S, D = x.shape
+        h = rms_norm(x, self.ln2, cfg.eps).reshape(B * S, D)
+        logits = self.router(h).float()
+        probs = torch.softmax(logits, -1)
+        gates, idx = torch.topk(probs, cfg.top_k, dim=-1)
+        gates = (gates / gates.sum(-1, keepdim=True)).to(x.dtype)
+        self.last_router = (probs, idx)
+        if ep is not None:
+            out = ep.dispatch_combine(h, idx, gates, self.expert_ffn)
+        else:
+            out = grouped_expert_ffn(h, idx, gates, self.w_gate_up, self.w_down)
+        return x + out.view(B, S, D)
+
+    def expert_ffn(self, tokens: torch.Tensor, expert_ids: torch.Tensor) -> torch.Tensor:
+        """SwiGLU of locally-owned experts for tokens already grouped by expert."""
+        return _ffn_grouped(tokens, expert_ids, self.w_gate_up, self.w_down)
+
+    def forward(self, x, cos, sin, cache=None, pos0: int = 0, ep=None):
+        return self.moe(self.attn(x, cos, sin, cache, pos0), ep)
+
+
+def _ffn_grouped(tokens, expert_ids, w_gate_up, w_down):
+    out = torch.empty_like(tokens)
+    for e in torch.unique(expert_ids).tolist():
+        sel = (expert_ids == e).nonzero(as_tuple=True)[0]
+        t = tokens.index_select(0, sel)
+        gu = L.linear(t, w_gate_up[e].to(t.dtype))
+        g, u = gu.chunk(2, -1)
+        out.index_copy_(0, sel, L.linear(F.silu(g) * u, w_down[e].to(t.dtype)))
+    return out
+
+
+def grouped_expert_ffn(h, idx, gates, w_gate_up, w_down):
+    """Top-k routed SwiGLU experts: sort (token, slot) pairs by expert, run each expert once, combine."""
+    T, K = idx.shape
+    flat_e = idx.reshape(-1)
+    tok = torch.arange(T, device=h.device).repeat_interleave(K)
+    order = torch.argsort(flat_e, stable=True)
+    y = _ffn_grouped(h.index_select(0, tok[order]), flat_e[order], w_gate_up, w_down)
+    w = gates.reshape(-1)[order].unsqueeze(-1)
+    out = torch.zeros_like(h)
+    out.index_add_(0, tok[order], (y * w).to(h.dtype))
+    return out
+
+
+class _Encoder(nn.Module):
+    """Small pre-norm transformer encoder used for both the audio and the vision tower."""
+
+    def __init__(self, in_dim: int, dim: int, layers: int, out_dim: int, heads: int = 4):
+        super().__init__()
+        self.inp = Linear(in_dim, dim)
+        self.heads = heads
+        self.blocks = nn.ModuleList()
+        for _ in range(layers):
+            b = nn.Module()
+            b.ln1, b.ln2 = nn.Parameter(torch.ones(dim)), nn.Parameter(torch.ones(dim))
+            b.qkv, b.o = Linear(dim, 3 * dim), Linear(dim, dim)
+            b.fc1, b.fc2 = Linear(dim, 4 * dim), Linear(4 * dim, dim)
+            self.blocks.append(b)
+        self.proj = Linear(dim, out_dim)
+
+    def forward(self, x):
+        x = self.inp(x)
+        B, S, D = x.shape
+        H = self.heads
+        for b in self.blocks:
+            qkv = b.qkv(rms_norm(x, b.ln1, 1e-6)).view(B, S, 3, H, D // H).permute(2, 0, 3, 1, 4)
+            x = x + b.o(attention(qkv[0].contiguous(), qkv[1].contiguous(), qkv[2].contiguous()))
+            x = x + b.fc2(b.fc1(rms_norm(x, b.ln2, 1e-6), epilogue="gelu"))
+        return self.proj(x)
+
+
+class MoELLM(nn.Module):
+    def __init__(self, cfg: MoEConfig):
+        super().__init__()
+        self.cfg = cfg
+        self.embed = nn.Parameter(torch.randn(cfg.vocab, cfg.hidden) * 0.02)
+        self.layers = nn.ModuleList([MoEBlock(cfg) for _ in range(cfg.layers)])
+        self.norm = nn.Parameter(torch.ones(cfg.hidden))
+        self.lm_head = Linear(cfg.hidden, cfg.vocab, bias=False)
+        self.audio_tower = _Encoder(cfg.audio_mel, cfg.audio_dim, cfg.audio_layers, cfg.hidden)
+        self.visual = _Encoder(cfg.vision_patch_dim, cfg.vision_dim, cfg.vision_layers, cfg.hidden)
+        self.ep = None
+
+    def embed_tokens(self, ids, audio_feats=None, image_patches=None):
+        x = F.embedding(ids, self.embed)
+        for feats, tower, tok in ((audio_feats, self.audio_tower, self.cfg.audio_token),
+                                  (image_patches, self.visual, self.cfg.image_token)):
+            if feats is None:
+                continue
+            emb = tower(feats.to(x.dtype))  # [B, n, hidden]; each prompt holds n placeholder tokens
+            mask = ids == tok
+            mask = mask & (mask.cumsum(1) <= emb.shape[1])  # only the prompt's n placeholders
+            x = x.masked_scatter(mask.unsqueeze(-1), emb.reshape(-1, x.shape[-1]).to(x.dtype))
+        return x
+
+    def forward(self, ids, positions=None, caches=None, pos0: int = 0, audio_feats=None, image_patches=None,
+                return_hidden: bool = False):
+        cfg = self.cfg
+        B, S = ids.shape
+        x = self.embed_tokens(ids, audio_feats, image_patches) if pos0 == 0 else F.embedding(ids, self.embed)
+        pos = torch.arange(pos0, pos0 + S, device=ids.device)
+        cos, sin = rope_table(pos.cpu(), cfg.head_dim, cfg.rope_theta)
+        cos, sin = cos.to(ids.device), sin.to(ids.device)
+        for i, blk in enumerate(self.layers):
+            x = blk(x, cos, sin, None if caches is None else caches[i], pos0, self.ep)
+        h = rms_norm(x, self.norm, cfg.eps)
+        if return_hidden:
+            return h
+        return self.lm_head(h).float()
+
+
+def token_logprobs(logits: torch.Tensor, targets: torch.Tensor, temperature: float = 1.0) -> torch.Tensor:
+    """log p(target) per position: logits [B, S, V] (fp32), targets [B, S]."""
+    lp = torch.log_softmax(logits / temperature, -1)
+    return lp.gather(-1, targets.unsqueeze(-1)).squeeze(-1)

@@ -1,0 +1,107 @@
+"""Omni (Qwen3-Omni-thinker-shaped MoE) GRPO / GSPO trainer and offline DPO.
+
+Counterpart of ``main_omni`` / ``OmniPPOTrainerSync`` / ``OmniDirectPreferenceRayTrainer``
+(``verl_omni/trainer/main_omni.py:57-360``, ``verl_omni/trainer/omni/ray_omni_trainer.py:66-728``):
+one step = multimodal prompts (text ids + audio log-mel frames + image patches) -> ``n`` sampled
+responses per prompt -> rule reward (seeded hash of the response tokens) -> GRPO group advantage ->
+recomputed old log-probs -> token-level GRPO or sequence-level GSPO update.  Expert weights can be
+sharded over an EP group (all-to-all dispatch/combine).
+"""
+
+from __future__ import annotations
+
+import time
+from typing import Optional
+
+import numpy as np
+import torch
+
+from verl_omni_b200.models.moe_llm import MoEConfig, MoELLM, token_logprobs
+from verl_omni_b200.parallel import dist as D
+from verl_omni_b200.trainer.diffusion.diffusion_algos import group_normalize
+from verl_omni_b200.trainer.omni.omni_algos import get_omni_loss_fn, omni_dpo_loss, sequence_logps
+from verl_omni_b200.utils import metrics as M
+from verl_omni_b200.utils.dataproto import DataProto
+from verl_omni_b200.workers.config.diffusion import DiffusionActorConfig
+from verl_omni_b200.workers.engine.base import ShardedEngine
+from verl_omni_b200.workers.reward.reward_manager import hash_token_reward
+from verl_omni_b200.workers.rollout.llm_rollout import LLMRolloutEngine
+
+
+class OmniGRPOTrainer:
+    def __init__(self, cfg: MoEConfig, actor_cfg: DiffusionActorConfig, *, device, n: int = 8,
+                 prompt_text: int = 16, audio_tokens: int = 4, image_tokens: int = 4, response_len: int = 8,
+                 loss_mode: str = "grpo", ep_group=None, seed: int = 0):
+        torch.manual_seed(seed)
+        self.cfg, self.actor_cfg, self.device, self.n = cfg, actor_cfg, device, n
+        self.prompt_text, self.audio_tokens, self.image_tokens = prompt_text, audio_tokens, image_tokens
+        self.model = MoELLM(cfg).to(device)
+        if ep_group is not None and D.world_size(ep_group) > 1:
+            from verl_omni_b200.parallel.expert_parallel import ExpertParallel
+
+            self.model.ep = ExpertParallel(cfg.experts, ep_group)
+        self.engine = ShardedEngine(self.model, actor_cfg, device=device, total_steps=1000)
+        self.rollout = LLMRolloutEngine(self.model, max_new_tokens=response_len, device=device)
+        self.loss_fn = get_omni_loss_fn(loss_mode)
+        self.loss_mode = loss_mode
+        self.step_count = 0
+        self.rank = D.rank()
+
+    def make_prompts(self, num: int, seed: int) -> DataProto:
+        g = torch.Generator().manual_seed(seed)
+        cfg = self.cfg
+        text = torch.randint(0, cfg.vocab - 2, (num, self.prompt_text), generator=g)
+        ids = torch.cat([text, torch.full((num, self.audio_tokens), cfg.audio_token),
+                         torch.full((num, self.image_tokens), cfg.image_token)], 1)
+        return DataProto({"input_ids": ids,
+                          "audio_feats": torch.randn(num, self.audio_tokens, cfg.audio_mel, generator=g),
+                          "image_patches": torch.randn(num, self.image_tokens, cfg.vision_patch_dim, generator=g)},
+                         {"uid": np.array([f"{seed}-{i}" for i in range(num)], dtype=object)})
+
+    def _resp_logprobs(self, data: DataProto) -> torch.Tensor:
+        ids = data.batch["input_ids"].to(self.device)
+        P = data.batch["prompts"].shape[1]
+        logits = self.model(ids[:, :-1], audio_feats=data.batch["audio_feats"].to(self.device),
+                            image_patches=data.batch["image_patches"].to(self.device))
+        return token_logprobs(logits[:, P - 1:], ids[:, P:])
+
+    def step(self, num_prompts: int = 2) -> dict:
+        self.step_count += 1
+        t0 = time.perf_counter()
+        prompts = self.make_prompts(num_prompts, seed=1000 * self.step_count + self.rank).repeat(self.n)
+        out = self.rollout.generate(prompts, seed=self.step_count)
+        rewards = hash_token_reward(out, seed=7).to(self.device)
+        adv = group_normalize(rewards, out.non_tensor_batch["uid"], global_std=False)
+        mask = out.batch["response_mask"].to(self.device)
+        with torch.no_grad():
+            old = self._resp_logprobs(out)
+        self.engine.train_mode()
+        self.engine.zero_grad()
+        logp = self._resp_logprobs(out)
+        loss, m = self.loss_fn(logp, old, adv, mask)
+        loss.backward()
+        norm = self.engine.optimizer_step()
+        m.update({"actor/pg_loss": float(loss.detach()), "actor/grad_norm": float(norm.reshape(())),
+                  "critic/rewards/mean": float(rewards.mean()),
+                  "rollout_corr/logprob_abs_diff_mean": float(((old - out.batch["rollout_log_probs"].to(self.device))
+                                                               .abs() * mask).sum() / mask.sum())})
+        m.update(M.compute_throughput_metrics_diffusion(time.perf_counter() - t0, len(out) * D.world_size(),
+                                                         D.world_size()))
+        return m
+
+    def dpo_step(self, chosen: DataProto, rejected: DataProto, ref_model: MoELLM, beta: float = 0.1) -> dict:
+        """Offline omni DPO on (chosen, rejected) response pairs against a frozen reference."""
+        def seqlp(model, d):
+            ids = d.batch["input_ids"].to(self.device)
+            P = d.batch["prompts"].shape[1]
+            lg = model(ids[:, :-1], audio_feats=d.batch["audio_feats"].to(self.device),
+                       image_patches=d.batch["image_patches"].to(self.device))
+            return sequence_logps(token_logprobs(lg[:, P - 1:], ids[:, P:]), d.batch["response_mask"].to(self.device))
+
+        with torch.no_grad():
+            rc, rr = seqlp(ref_model, chosen), seqlp(ref_model, rejected)
+        self.engine.zero_grad()
+        loss, m = omni_dpo_loss(seqlp(self.model, chosen), seqlp(self.model, rejected), rc, rr, beta=beta)
+        loss.backward()
+        self.engine.optimizer_step()
+        return m

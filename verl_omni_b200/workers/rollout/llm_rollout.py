@@ -1,0 +1,73 @@
+"""Autoregressive rollout for the omni thinker (the vLLM-Omni AR mode of the reference,
+``verl_omni/workers/rollout/vllm_rollout/vllm_omni_async_server.py:537-579``).
+
+Batched prefill of the (multimodal) prompts, then token-by-token decode against per-layer KV caches;
+sampling with temperature / top-k / top-p from a seeded generator; returns the response ids, their
+log-probs under the sampling distribution (``rollout_log_probs``) and an EOS-aware response mask.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from verl_omni_b200.models.moe_llm import MoELLM
+from verl_omni_b200.utils.dataproto import DataProto
+
+
+def sample_next(logits: torch.Tensor, temperature: float, top_k: int, top_p: float, generator) -> torch.Tensor:
+    if temperature <= 0:
+        return logits.argmax(-1)
+    l = logits / temperature
+    if top_k and top_k > 0:
+        kth = torch.topk(l, min(top_k, l.shape[-1]), dim=-1).values[..., -1:]
+        l = l.masked_fill(l < kth, float("-inf"))
+    if top_p < 1.0:
+        sl, si = torch.sort(l, descending=True, dim=-1)
+        cp = torch.softmax(sl, -1).cumsum(-1)
+        drop = cp - torch.softmax(sl, -1) > top_p
+        sl = sl.masked_fill(drop, float("-inf"))
+        l = torch.full_like(l, float("-inf")).scatter(-1, si, sl)
+    probs = torch.softmax(l.float(), -1)
+    return torch.multinomial(probs.cpu(), 1, generator=generator).squeeze(-1).to(logits.device)
+
+
+class LLMRolloutEngine:
+    def __init__(self, module: MoELLM, *, max_new_tokens: int = 256, temperature: float = 1.0, top_k: int = 0,
+                 top_p: float = 1.0, eos_id: Optional[int] = None, device=None):
+        self.module = module
+        self.max_new_tokens = max_new_tokens
+        self.temperature, self.top_k, self.top_p = temperature, top_k, top_p
+        self.eos_id = eos_id
+        self.device = device
+
+    @torch.no_grad()
+    def generate(self, batch: DataProto, seed: int = 0) -> DataProto:
+        ids = batch.batch["input_ids"].to(self.device)
+        B, P = ids.shape
+        g = torch.Generator().manual_seed(int(seed))
+        caches = [dict() for _ in self.module.layers]
+        logits = self.module(ids, caches=caches, pos0=0, audio_feats=batch.batch.get("audio_feats"),
+                             image_patches=batch.batch.get("image_patches"))[:, -1]
+        out_ids, out_lp = [], []
+        done = torch.zeros(B, dtype=torch.bool, device=ids.device)
+        mask = []
+        for t in range(self.max_new_tokens):
+            lp_all = torch.log_softmax(logits.float() / max(self.temperature, 1e-6), -1)
+            nxt = sample_next(logits, self.temperature, self.top_k, self.top_p, g)
+            out_ids.append(nxt)
+            out_lp.append(lp_all.gather(-1, nxt[:, None]).squeeze(-1))
+            mask.append(~done)
+            if self.eos_id is not None:
+                done = done | (nxt == self.eos_id)
+            if t + 1 < self.max_new_tokens:
+                logits = self.module(nxt[:, None], caches=caches, pos0=P + t)[:, -1]
+        resp = torch.stack(out_ids, 1)
+        out = DataProto({"prompts": ids, "responses": resp, "rollout_log_probs": torch.stack(out_lp, 1),
+                         "response_mask": torch.stack(mask, 1).float(),
+                         "input_ids": torch.cat([ids, resp], 1)}, dict(batch.non_tensor_batch))
+        for k in ("audio_feats", "image_patches"):
+            if k in batch.batch:
+                out.batch[k] = batch.batch[k]
+        return out
