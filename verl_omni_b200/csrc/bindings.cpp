@@ -44,6 +44,19 @@ torch::Tensor gelu_tanh_bwd(torch::Tensor dy, torch::Tensor pre);
 int64_t gemm_error(bool reset);
 std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal, double scale);
 int64_t fmha_error(bool reset);
+std::vector<torch::Tensor> linear_bwd_prep(torch::Tensor dy, c10::optional<torch::Tensor> saved,
+                                           c10::optional<torch::Tensor> gate, int64_t S, int64_t mode,
+                                           c10::optional<torch::Tensor> db, bool db_accumulate);
+int64_t symm_malloc(int64_t nbytes);
+void symm_free(int64_t ptr);
+torch::Tensor ipc_get_handle(int64_t ptr);
+int64_t ipc_open(torch::Tensor handle);
+void ipc_close(int64_t ptr);
+torch::Tensor tensor_from_ptr(int64_t ptr, int64_t numel, int64_t dtype_code, int64_t device);
+torch::Tensor peer_grad_reduce(std::vector<int64_t> grad_ptrs, int64_t lo, int64_t n, double scale, torch::Tensor out);
+void peer_adamw_bcast(std::vector<int64_t> flat_ptrs, int64_t lo, int64_t n, torch::Tensor p, torch::Tensor grad,
+                      torch::Tensor m, torch::Tensor v, double lr, double b1, double b2, double eps, double wd,
+                      int64_t step, double max_norm, torch::Tensor sq_norm);
 std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
                                     torch::Tensor lse, torch::Tensor dO, bool causal, double scale);
 }  // namespace vo
@@ -69,4 +82,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fmha_fwd", &vo::fmha_fwd);
   m.def("fmha_error", &vo::fmha_error);
   m.def("fmha_bwd", &vo::fmha_bwd);
+  m.def("linear_bwd_prep", &vo::linear_bwd_prep);
+  m.def("symm_malloc", &vo::symm_malloc);
+  m.def("symm_free", &vo::symm_free);
+  m.def("ipc_get_handle", &vo::ipc_get_handle);
+  m.def("ipc_open", &vo::ipc_open);
+  m.def("ipc_close", &vo::ipc_close);
+  m.def("tensor_from_ptr", &vo::tensor_from_ptr);
+  m.def("peer_grad_reduce", &vo::peer_grad_reduce);
+  m.def("peer_adamw_bcast", &vo::peer_adamw_bcast);
 }

@@ -82,6 +82,8 @@ def bench_fmha(a) -> list[dict]:
         cases["bwd"] = (lambda: e.fmha_bwd(q, k, v, o, lse, do, False, scale), 2.5 * flops_f)
     if a.compare:
         cases["sdpa_fwd"] = (lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v), flops_f)
+    if a.only:
+        cases = {k: cases[k] for k in a.only.split(",")}
     out = []
     for name, (fn, fl) in cases.items():
         ms = timeit(fn, a.iters)

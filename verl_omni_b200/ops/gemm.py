@@ -25,7 +25,7 @@ _GELU_C = 0.7978845608028654  # sqrt(2/pi)
 
 
 def _use_native() -> bool:
-    return os.environ.get("VO_GEMM", "native") != "torch" and hasattr(ext(), "gemm")
+    return os.environ.get("VO_GEMM", "native") != "torch" and hasattr(ext(), "gemm_fwd")
 
 
 # epilogue codes shared with csrc/gemm_sm100.cu

@@ -19,6 +19,7 @@ import torch
 import torch.nn.functional as F
 
 from verl_omni_b200.ops import gemm as G
+from verl_omni_b200.ops._ext import ext
 
 
 def _accum(param: torch.Tensor, grad: torch.Tensor):
@@ -43,24 +44,53 @@ class _LinearFn(torch.autograd.Function):
     def backward(ctx, dy):
         x2, w, pre, gate = ctx.saved_tensors
         epilogue, S, xshape, has_b, b = ctx.meta
-        dy2 = dy.reshape(-1, w.shape[0]).contiguous()
+        N = w.shape[0]
+        dy2 = dy.reshape(-1, N)
+        if not dy2.is_contiguous():
+            dy2 = dy2.contiguous()
         d_gate = d_res = None
         if epilogue == "gate_res":
             d_res = dy  # residual passes through
-            # y_lin = pre (saved linear output); dgate[b, n] = sum_s dy * y_lin
-            B = dy2.shape[0] // S
-            d_gate = (dy2.float().view(B, S, -1) * pre.float().view(B, S, -1)).sum(1).to(gate.dtype)
-            dy2 = (dy2.view(B, S, -1) * gate.view(B, 1, -1)).reshape(dy2.shape).contiguous()
-        elif epilogue == "gelu":
-            dy2 = G.gelu_bwd(dy2, pre)
+        gb = None
+        if _fused_prep_ok(dy2, gate if epilogue == "gate_res" else None):
+            # one pass over dY: gelu'/gate scaling, gate grad and bias grad (into bias.main_grad)
+            mode = _MODE[epilogue]
+            mg = getattr(b, "main_grad", None) if has_b else None
+            db = None
+            if has_b:
+                db = mg if mg is not None else torch.empty(N, device=dy.device, dtype=torch.float32)
+            dy2, dg = ext().linear_bwd_prep(dy2, pre if mode else None, gate if mode == 2 else None, S, mode, db,
+                                            mg is not None)
+            if mode == 2:
+                d_gate = dg
+            if has_b and mg is None:
+                gb = db.to(b.dtype)
+        else:
+            if epilogue == "gate_res":
+                # y_lin = pre (saved linear output); dgate[b, n] = sum_s dy * y_lin
+                B = dy2.shape[0] // S
+                d_gate = (dy2.float().view(B, S, -1) * pre.float().view(B, S, -1)).sum(1).to(gate.dtype)
+                dy2 = (dy2.view(B, S, -1) * gate.view(B, 1, -1)).reshape(dy2.shape).contiguous()
+            elif epilogue == "gelu":
+                dy2 = G.gelu_bwd(dy2, pre)
+            if has_b:
+                gb = _accum(b, dy2.float().sum(0))
         dx = G.matmul_nn(dy2, w)  # [M, N] x [N, K] -> [M, K]
         dw = G.wgrad(dy2, x2, getattr(w, "main_grad", None))
         gw = None if dw is None else dw.to(w.dtype)
-        gb = None
-        if has_b:
-            db = dy2.float().sum(0)
-            gb = _accum(b, db)
         return dx.view(xshape), gw, gb, None, d_gate, d_res, None
+
+
+_MODE = {"none": 0, "gelu": 1, "gate_res": 2}
+
+
+def _fused_prep_ok(dy2: torch.Tensor, gate: Optional[torch.Tensor]) -> bool:
+    if dy2.dtype != torch.bfloat16 or dy2.shape[1] % 8 or dy2.data_ptr() % 16:
+        return False
+    if gate is not None and (gate.dtype != torch.bfloat16 or gate.dim() != 2 or gate.stride(1) != 1
+                             or gate.stride(0) % 8 or gate.data_ptr() % 16):
+        return False
+    return hasattr(ext(), "linear_bwd_prep")
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None, *, epilogue: str = "none",

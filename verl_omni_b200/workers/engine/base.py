@@ -47,7 +47,7 @@ class FlatParams:
     """Packs the trainable parameters of ``module`` into one flat buffer + fp32 grad buffer."""
 
     def __init__(self, module: nn.Module, dtype: torch.dtype, device: torch.device, world: int, rank: int,
-                 group=None):
+                 group=None, symmetric: bool = False):
         self.module = module
         self.group = group
         self.world, self.rank = world, rank
@@ -69,8 +69,17 @@ class FlatParams:
         self.shard_size = self.padded // world
         self.shard_lo = rank * self.shard_size
         self.device, self.dtype = device, dtype
-        self.flat = torch.zeros(self.padded, dtype=dtype, device=device)
-        self.main_grad = torch.zeros(self.padded, dtype=torch.float32, device=device)
+        self.symm_flat = self.symm_grad = None
+        if symmetric:
+            from verl_omni_b200.parallel.symm_mem import SymmetricBuffer
+
+            # peer-mapped buffers: the fused optimizer step reads peers' grads / writes peers' weights
+            self.symm_flat = SymmetricBuffer(self.padded, dtype, device, group)
+            self.symm_grad = SymmetricBuffer(self.padded, torch.float32, device, group)
+            self.flat, self.main_grad = self.symm_flat.tensor, self.symm_grad.tensor
+        else:
+            self.flat = torch.zeros(self.padded, dtype=dtype, device=device)
+            self.main_grad = torch.zeros(self.padded, dtype=torch.float32, device=device)
         master_full = torch.zeros(self.padded, dtype=torch.float32, device=device)
         for p, o, n in zip(self.params, self.offsets, self.numels):
             src = p.detach().reshape(-1).to(device=device, dtype=torch.float32)
@@ -171,10 +180,23 @@ class ShardedEngine:
             module.to(device=device, dtype=self.dtype)
             self.flat = None
         else:
-            self.flat = FlatParams(module, self.dtype, device, self.world, self.rank, group)
+            self.flat = FlatParams(module, self.dtype, device, self.world, self.rank, group,
+                                   symmetric=self._want_symmetric(actor_cfg, device, group))
         self.opt_step = 0
         self.sched = LRSchedule(actor_cfg.optim, total_steps) if trainable else None
         self.last_grad_norm = None
+
+    def _want_symmetric(self, actor_cfg, device, group) -> bool:
+        """``fsdp_config.fused_collectives``: "auto" (on for NCCL ranks of one node), "on", "off"."""
+        mode = str(getattr(actor_cfg.fsdp_config, "fused_collectives", "auto")).lower()
+        if mode in ("off", "false", "none") or device.type != "cuda" or self.world < 2:
+            return False
+        from verl_omni_b200.parallel import symm_mem
+
+        ok = symm_mem.available(group)
+        if mode in ("on", "true") and not ok:
+            raise RuntimeError("fused_collectives=on needs NCCL ranks on one node")
+        return ok
 
     # ------------------------------------------------------------------ modes
     def train_mode(self):
@@ -197,6 +219,20 @@ class ShardedEngine:
         """
         fp = self.flat
         oc = self.cfg.optim
+        if fp.symm_grad is not None:
+            from verl_omni_b200.parallel.symm_mem import fused_optimizer_step
+
+            self.opt_step += 1
+            norm = fused_optimizer_step(
+                fp.symm_flat, fp.symm_grad, fp.shard_lo, fp.shard_size, fp.master, fp.grad_shard, fp.exp_avg,
+                fp.exp_avg_sq, lr=self.sched.lr(), betas=(float(oc.betas[0]), float(oc.betas[1])),
+                eps=float(oc.eps), weight_decay=float(oc.weight_decay), step=self.opt_step,
+                max_norm=float(self.cfg.grad_clip if self.cfg.grad_clip is not None else oc.clip_grad),
+                group=self.group)
+            self.sched.step()
+            fp.zero_grad()
+            self.last_grad_norm = norm
+            return norm
         D.reduce_scatter_into(fp.grad_shard, fp.main_grad, self.group)
         if self.world > 1:
             fp.grad_shard.mul_(1.0 / self.world)
