@@ -32,15 +32,35 @@ def _ref(q, k, v, causal, scale):
     return o, lse
 
 
+@pytest.mark.parametrize("version", [1, 2])
 @pytest.mark.parametrize("B,H,Sq,Skv,D,causal", CASES)
-def test_fmha_fwd(E, B, H, Sq, Skv, D, causal):
+def test_fmha_fwd(E, B, H, Sq, Skv, D, causal, version):
     torch.manual_seed(0)
     q = torch.randn(B, H, Sq, D, device="cuda").bfloat16()
     k = torch.randn(B, H, Skv, D, device="cuda").bfloat16()
     v = torch.randn(B, H, Skv, D, device="cuda").bfloat16()
     scale = 1 / math.sqrt(D)
-    o, lse = E.fmha_fwd(q, k, v, causal, scale)
+    o, lse = E.fmha_fwd(q, k, v, causal, scale, version)
     ro, rlse = _ref(q, k, v, causal, scale)
+    torch.testing.assert_close(o.float(), ro.transpose(1, 2), rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(lse, rlse, rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("version", [1, 2])
+@pytest.mark.parametrize("D", [64, 128])
+def test_fmha_fwd_growing_max(E, D, version):
+    """Later key blocks carry far larger scores: exercises the running-max rescale of O."""
+    torch.manual_seed(3)
+    B, H, S = 1, 2, 700
+    q = torch.randn(B, H, S, D, device="cuda")
+    k = torch.randn(B, H, S, D, device="cuda")
+    k[:, :, 260:300] *= 6.0
+    k[:, :, 600:640] *= 12.0
+    q, k = q.bfloat16(), k.bfloat16()
+    v = torch.randn(B, H, S, D, device="cuda").bfloat16()
+    scale = 1 / math.sqrt(D)
+    o, lse = E.fmha_fwd(q, k, v, False, scale, version)
+    ro, rlse = _ref(q, k, v, False, scale)
     torch.testing.assert_close(o.float(), ro.transpose(1, 2), rtol=2e-2, atol=2e-2)
     torch.testing.assert_close(lse, rlse, rtol=1e-3, atol=1e-3)
 

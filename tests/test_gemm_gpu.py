@@ -5,7 +5,8 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-SHAPES = [(128, 256, 64), (333, 776, 200), (1000, 1536, 1536), (4096, 512, 4096)]
+SHAPES = [(128, 256, 64), (333, 776, 200), (1000, 1536, 1536), (4096, 512, 4096), (16, 1032, 1536),
+          (5328, 4608, 1536)]
 
 
 @pytest.fixture(scope="module")

@@ -11,7 +11,8 @@ int64_t launch_count() { return g_launches.load(); }
 std::vector<torch::Tensor> sde_step_fwd(torch::Tensor x, torch::Tensor v, torch::Tensor sigma, torch::Tensor sigma_prev,
                                         c10::optional<torch::Tensor> prev, c10::optional<torch::Tensor> noise,
                                         double sigma_max, double eta, int64_t type, int64_t seed, int64_t offset,
-                                        bool want_logp, bool norm);
+                                        bool want_logp, bool norm, c10::optional<torch::Tensor> row_seeds);
+torch::Tensor normal_fill(torch::Tensor row_seeds, int64_t n, int64_t offset);
 torch::Tensor sde_step_bwd(torch::Tensor x, torch::Tensor prev, torch::Tensor mean, torch::Tensor sigma,
                            torch::Tensor sigma_prev, torch::Tensor g_logp, torch::Tensor g_mean, double sigma_max,
                            double eta, int64_t type);
@@ -42,7 +43,8 @@ torch::Tensor gemm_dgrad(torch::Tensor dy, torch::Tensor w);
 void gemm_wgrad(torch::Tensor dy, torch::Tensor x, torch::Tensor out, bool accumulate);
 torch::Tensor gelu_tanh_bwd(torch::Tensor dy, torch::Tensor pre);
 int64_t gemm_error(bool reset);
-std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal, double scale);
+std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal, double scale,
+                                    int64_t version);
 int64_t fmha_error(bool reset);
 std::vector<torch::Tensor> linear_bwd_prep(torch::Tensor dy, c10::optional<torch::Tensor> saved,
                                            c10::optional<torch::Tensor> gate, int64_t S, int64_t mode,
@@ -64,7 +66,10 @@ std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Ten
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "verl_omni_b200 sm_100a kernels";
   m.def("launch_count", &vo::launch_count);
-  m.def("sde_step_fwd", &vo::sde_step_fwd);
+  m.def("sde_step_fwd", &vo::sde_step_fwd, py::arg("x"), py::arg("v"), py::arg("sigma"), py::arg("sigma_prev"),
+        py::arg("prev"), py::arg("noise"), py::arg("sigma_max"), py::arg("eta"), py::arg("type"), py::arg("seed"),
+        py::arg("offset"), py::arg("want_logp"), py::arg("norm"), py::arg("row_seeds") = py::none());
+  m.def("normal_fill", &vo::normal_fill);
   m.def("sde_step_bwd", &vo::sde_step_bwd);
   m.def("ppo_clip_fwd", &vo::ppo_clip_fwd);
   m.def("ppo_clip_bwd", &vo::ppo_clip_bwd);
@@ -79,7 +84,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_wgrad", &vo::gemm_wgrad);
   m.def("gelu_tanh_bwd", &vo::gelu_tanh_bwd);
   m.def("gemm_error", &vo::gemm_error);
-  m.def("fmha_fwd", &vo::fmha_fwd);
+  m.def("fmha_fwd", &vo::fmha_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("causal"), py::arg("scale"),
+        py::arg("version") = 2);
   m.def("fmha_error", &vo::fmha_error);
   m.def("fmha_bwd", &vo::fmha_bwd);
   m.def("linear_bwd_prep", &vo::linear_bwd_prep);

@@ -4,6 +4,9 @@
 extern "C" int vo_fmha_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int Sq,
                            int Skv, int D, float scale, int causal, cudaStream_t stream);
 extern "C" int vo_fmha_error(int reset);
+extern "C" int vo_fmha_fwd2(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int Sq,
+                            int Skv, int D, float scale, int causal, cudaStream_t stream);
+extern "C" int vo_fmha_fwd2_error(int reset);
 extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const void* o, const void* dO,
                            const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_acc, int B, int H,
                            int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream);
@@ -12,7 +15,10 @@ extern "C" int vo_fmha_bwd_error(int reset);
 namespace vo {
 
 // q [B, H, Sq, D], k/v [B, H, Skv, D] -> (o [B, Sq, H, D], lse [B, H, Sq] fp32)
-std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal, double scale) {
+// version 1: one query tile per CTA, P staged in shared memory; version 2: two query tiles per CTA,
+// P and O resident in tensor memory.
+std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal, double scale,
+                                    int64_t version) {
   VO_CHECK_INPUT(q);
   VO_CHECK_INPUT(k);
   VO_CHECK_INPUT(v);
@@ -22,14 +28,17 @@ std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Ten
   TORCH_CHECK(D == 64 || D == 128, "head_dim must be 64 or 128");
   auto o = torch::empty({B, Sq, H, D}, q.options());
   auto lse = torch::empty({B, H, Sq}, q.options().dtype(torch::kFloat32));
-  int rc = vo_fmha_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(), B, H, Sq, Skv,
-                       D, (float)scale, causal ? 1 : 0, stream());
+  auto fn = version == 2 ? vo_fmha_fwd2 : vo_fmha_fwd;
+  int rc = fn(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(), B, H, Sq, Skv, D,
+              (float)scale, causal ? 1 : 0, stream());
   TORCH_CHECK(rc == 0, "tcgen05 FMHA launch failed: code ", rc);
   count_launch();
   return {o, lse};
 }
 
-int64_t fmha_error(bool reset) { return vo_fmha_error(reset ? 1 : 0) | vo_fmha_bwd_error(reset ? 1 : 0); }
+int64_t fmha_error(bool reset) {
+  return vo_fmha_error(reset ? 1 : 0) | vo_fmha_fwd2_error(reset ? 1 : 0) | vo_fmha_bwd_error(reset ? 1 : 0);
+}
 
 // returns dq, dk, dv in the [B, H, S, D] layout of q, k, v
 std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,

@@ -1,0 +1,552 @@
+// Flash attention forward for sm_100a: two query tiles per CTA, P and O resident in tensor memory.
+//
+//   O = softmax(Q K^T * scale) V,  LSE = log(sum exp(Q K^T * scale))
+//   Q [BH, Sq, D], K/V [BH, Skv, D] (bf16, contiguous per head); O written token-major [B, Sq, H, D];
+//   D in {64, 128}; optional causal mask (query i sees keys <= i).
+//
+// One CTA = 256 query rows (two 128-row tiles t = 0, 1) of one head, 384 threads:
+//   warp 0        TMA producer: Q0, Q1 once; then K_0, and per key block j: K_{j+1}, V_j (rings);
+//   warp 1        TMEM allocator + single-thread MMA issuer;
+//   warps 4..7    softmax warpgroup of tile 0, one query row per thread;
+//   warps 8..11   softmax warpgroup of tile 1.
+// Tensor memory (512 columns): S_0 [0,128), S_1 [128,256), O_0 [256, 256+D), O_1 [256+D, 256+2D).
+// The softmax of tile t reads S_t, and writes the bf16 probabilities P_t back into the first 64
+// columns of S_t (tcgen05.st); the PV MMA then takes its A operand straight from tensor memory, so P
+// never touches shared memory.  O_t accumulates in tensor memory across key blocks.
+// MMA issue order per key block j:  PV_0(j), S_0(j+1), PV_1(j), S_1(j+1).  The tensor pipe executes
+// one thread's MMAs in order, so S_t(j+1) may overwrite P_t(j) right after PV_t(j) is issued, and the
+// commit that signals S_t(j) also proves PV_t(j-1) complete.  While softmax t works on S_t(j) the
+// tensor core runs the other tile's MMAs: the two warpgroups ping-pong against the tensor pipe.
+// Online softmax with a lazy rescale: the running max m only moves when a block's max exceeds it by
+// more than 2^8 (exp2 domain); only then is O_t read, scaled and written back in tensor memory.  P
+// values are bounded by 2^8, well inside bf16 / fp32 range, and l and O share the same reference m.
+// Every mbarrier wait is bounded; on timeout an error code is recorded and the CTA exits cleanly.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace vo_fmha2 {
+
+constexpr int BQ = 128, BKV = 128;
+constexpr int NUM_THREADS = 384;
+constexpr unsigned long long WAIT_BUDGET = 8ull * 1000 * 1000 * 1000;
+constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
+
+__device__ int g_error = 0;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t c) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(c));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t par) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(par)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t par, volatile int* abort_flag, int code) {
+  if (mbar_try_wait(b, par)) return true;
+  const unsigned long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait(b, par)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > WAIT_BUDGET) {
+      atomicCAS(&g_error, 0, code);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* m, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(m), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// D(tmem) (+)= A(smem) * B(smem)
+__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+// D(tmem) (+)= A(tmem) * B(smem)
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void commit(uint64_t* b) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(b))
+               : "memory");
+}
+// 32 lanes x 32 columns of 32-bit values; no wait (caller issues wait_ld)
+__device__ __forceinline__ void ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ uint64_t desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | (2ull << 61);
+}
+__host__ __device__ constexpr uint32_t idesc(int M, int N, int a_mn, int b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+// (a0, a1) * s + c on the paired fp32 pipe (one instruction for two lanes of work)
+__device__ __forceinline__ void ffma2(float a0, float a1, float s, float c, float& r0, float& r1) {
+  asm("{\n\t.reg .b64 x, y, z, r;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %4};\n\tmov.b64 z, {%5, %5};\n\t"
+      "fma.rn.f32x2 r, x, y, z;\n\tmov.b64 {%0, %1}, r;\n\t}"
+      : "=f"(r0), "=f"(r1)
+      : "f"(a0), "f"(a1), "f"(s), "f"(c));
+}
+__device__ __forceinline__ void fadd2(float& s0, float& s1, float a0, float a1) {
+  asm("{\n\t.reg .b64 x, y, r;\n\tmov.b64 x, {%0, %1};\n\tmov.b64 y, {%2, %3};\n\t"
+      "add.rn.f32x2 r, x, y;\n\tmov.b64 {%0, %1}, r;\n\t}"
+      : "+f"(s0), "+f"(s1)
+      : "f"(a0), "f"(a1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+struct Params {
+  int Sq, Skv, H, npairs;
+  float scale_log2;  // softmax scale * log2(e)
+  int causal;
+  __nv_bfloat16* o;  // [B, Sq, H, D]
+  float* lse;        // [B*H, Sq] natural log
+};
+
+template <int D>
+struct Cfg {
+  static constexpr int TILE = 128 * D * 2;  // one 128-row tile of Q/K/V (D/64 swizzled 16 KB chunks)
+  static constexpr int KST = D == 64 ? 3 : 2;
+  static constexpr int VST = 2;
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = 2 * TILE;
+  static constexpr int V_OFF = K_OFF + KST * TILE;
+  static constexpr int BAR_OFF = V_OFF + VST * TILE;
+  static constexpr int BYTES = BAR_OFF + 256;
+  static constexpr uint32_t S_COL0 = 0, O_COL0 = 256;
+};
+
+template <int D>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    fmha_fwd2_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+                     const __grid_constant__ CUtensorMap mv, Params p) {
+  using C = Cfg<D>;
+  extern __shared__ __align__(1024) uint8_t raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;              // [KST]
+  uint64_t* k_empty = k_full + C::KST;      // [KST]
+  uint64_t* v_full = k_empty + C::KST;      // [VST]
+  uint64_t* v_empty = v_full + C::VST;      // [VST]
+  uint64_t* s_full = v_empty + C::VST;      // [2] per tile
+  uint64_t* p_full = s_full + 2;            // [2]
+  uint64_t* o_final = p_full + 2;           // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // heavier (later) query pairs first under a causal mask
+  const int pr = p.npairs - 1 - (int)(blockIdx.x % p.npairs);
+  const int bh = blockIdx.x / p.npairs;
+  const int q0 = pr * 2 * BQ;
+  int kv_end = p.Skv;
+  if (p.causal) kv_end = min(p.Skv, q0 + 2 * BQ);
+  const int nkv = (kv_end + BKV - 1) / BKV;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < C::KST; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < C::VST; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&o_final[t], 1);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0 && nkv > 0) {
+      mbar_expect_tx(q_full, 2 * C::TILE);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_3d(sm + C::Q_OFF + t * C::TILE + c * 16384, &mq, q_full, c * 64, q0 + t * BQ, bh);
+      auto load_k = [&](int j) -> bool {
+        const int s = j % C::KST;
+        if (!mbar_wait(&k_empty[s], ((j / C::KST) & 1) ^ 1, abort_flag, 41)) return false;
+        mbar_expect_tx(&k_full[s], C::TILE);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_3d(sm + C::K_OFF + s * C::TILE + c * 16384, &mk, &k_full[s], c * 64, j * BKV, bh);
+        return true;
+      };
+      bool ok = load_k(0);
+      for (int j = 0; ok && j < nkv; ++j) {
+        if (j + 1 < nkv && !(ok = load_k(j + 1))) break;
+        const int s = j % C::VST;
+        if (!mbar_wait(&v_empty[s], ((j / C::VST) & 1) ^ 1, abort_flag, 42)) break;
+        mbar_expect_tx(&v_full[s], C::TILE);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_3d(sm + C::V_OFF + s * C::TILE + c * 16384, &mv, &v_full[s], c * 64, j * BKV, bh);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nkv > 0) {
+      const uint32_t id_s = idesc(128, 128, 0, 0);
+      const uint32_t id_o = idesc(128, D, 0, 1);
+      const uint32_t S_T[2] = {tmem + C::S_COL0, tmem + C::S_COL0 + 128};
+      const uint32_t O_T[2] = {tmem + C::O_COL0, tmem + C::O_COL0 + D};
+      auto issue_s = [&](int t, int j) {
+        const uint32_t qa = smem_u32(sm + C::Q_OFF + t * C::TILE);
+        const uint32_t ka = smem_u32(sm + C::K_OFF + (j % C::KST) * C::TILE);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          mma_ss(S_T[t], desc(qa + off, 16, 1024), desc(ka + off, 16, 1024), id_s, kk > 0);
+        }
+        commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t va = smem_u32(sm + C::V_OFF + (j % C::VST) * C::TILE);
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk)
+          mma_ts(O_T[t], S_T[t] + kk * 8, desc(va + kk * 2048, 16384, 1024), id_o, (j > 0 || kk > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag, 43) && mbar_wait(&k_full[0], 0, abort_flag, 44);
+      if (ok) {
+        fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        commit(&k_empty[0]);
+      }
+      for (int j = 0; ok && j < nkv; ++j) {
+        const bool more = j + 1 < nkv;
+        if (!mbar_wait(&v_full[j % C::VST], (j / C::VST) & 1, abort_flag, 45)) break;
+        if (!mbar_wait(&p_full[0], j & 1, abort_flag, 46)) break;
+        fence_after();
+        issue_pv(0, j);
+        if (more) {
+          if (!mbar_wait(&k_full[(j + 1) % C::KST], ((j + 1) / C::KST) & 1, abort_flag, 47)) break;
+          fence_after();
+          issue_s(0, j + 1);
+        } else {
+          commit(&o_final[0]);
+        }
+        if (!mbar_wait(&p_full[1], j & 1, abort_flag, 48)) break;
+        fence_after();
+        issue_pv(1, j);
+        commit(&v_empty[j % C::VST]);
+        if (more) {
+          issue_s(1, j + 1);
+          commit(&k_empty[(j + 1) % C::KST]);
+        } else {
+          commit(&o_final[1]);
+        }
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------------------------------------------------------- softmax warpgroups
+    const int t = (warp - 4) >> 2;
+    const int lane_base = 32 * (warp & 3);
+    const int row = lane_base + lane;
+    const int q = q0 + t * BQ + row;
+    const uint32_t lane_off = (uint32_t)lane_base << 16;
+    const uint32_t S_t = tmem + C::S_COL0 + t * 128 + lane_off;
+    const uint32_t O_t = tmem + C::O_COL0 + t * D + lane_off;
+    const float sl2 = p.scale_log2;
+    float m = -INFINITY, l = 0.f;
+    bool ok = nkv > 0;
+    for (int j = 0; ok && j < nkv; ++j) {
+      if (!mbar_wait(&s_full[t], j & 1, abort_flag, 49)) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      const int kv0 = j * BKV;
+      // keys [kv0, kv0 + lim) of this block are visible to this row
+      int lim = p.Skv - kv0;
+      if (p.causal) lim = min(lim, q - kv0 + 1);
+      lim = max(0, min(BKV, lim));
+      // pass 1: row max.  Chunks 2,3 first so chunks 0,1 stay in registers for pass 2.
+      uint32_t a[32], b[32];
+      float mx = -INFINITY;
+      ld32_nowait(S_t + 64, a);
+      ld32_nowait(S_t + 96, b);
+      wait_ld();
+      if (lim == BKV) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mx = max3(mx, __uint_as_float(a[i]), __uint_as_float(b[i]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (64 + i < lim) mx = fmaxf(mx, __uint_as_float(a[i]));
+          if (96 + i < lim) mx = fmaxf(mx, __uint_as_float(b[i]));
+        }
+      }
+      uint32_t c0[32], c1[32];
+      ld32_nowait(S_t + 0, c0);
+      ld32_nowait(S_t + 32, c1);
+      wait_ld();
+      if (lim == BKV) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mx = max3(mx, __uint_as_float(c0[i]), __uint_as_float(c1[i]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (i < lim) mx = fmaxf(mx, __uint_as_float(c0[i]));
+          if (32 + i < lim) mx = fmaxf(mx, __uint_as_float(c1[i]));
+        }
+      }
+      // lazy rescale: move m only when the block max exceeds it by more than the threshold
+      const float m_blk = mx * sl2;
+      float alpha = 1.f;
+      const bool move = m_blk > m + RESCALE_THRESHOLD || (m == -INFINITY && m_blk != -INFINITY);
+      if (move) {
+        alpha = (m == -INFINITY) ? 0.f : ex2(m - m_blk);
+        m = m_blk;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, move)) {
+        // O_t is quiescent: PV_t(j-1) completed before S_t(j) was signalled, PV_t(j) waits for us
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          ld32_nowait(O_t + c * 32, o);
+          wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          st32(O_t + c * 32, o);
+        }
+      }
+      const float mb = (m == -INFINITY) ? 0.f : m;
+      float rs = 0.f, rs0 = 0.f, rs1 = 0.f;
+      // pass 2: p = exp2(s*scale_log2 - m), packed bf16 pairs into columns [0, 64) of S_t
+      auto emit = [&](const uint32_t (&v)[32], int c) {
+        uint32_t w[16];
+        const float nmb = -mb;
+        if (lim == BKV) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float x0, x1;
+            ffma2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]), sl2, nmb, x0, x1);
+            const float e0 = ex2(x0), e1 = ex2(x1);
+            fadd2(rs0, rs1, e0, e1);
+            w[i] = pack_bf16(e0, e1);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int k = c * 32 + 2 * i;
+            const float e0 = k < lim ? ex2(fmaf(__uint_as_float(v[2 * i]), sl2, nmb)) : 0.f;
+            const float e1 = k + 1 < lim ? ex2(fmaf(__uint_as_float(v[2 * i + 1]), sl2, nmb)) : 0.f;
+            rs += e0 + e1;
+            w[i] = pack_bf16(e0, e1);
+          }
+        }
+        st16(S_t + c * 16, w);
+      };
+      ld32_nowait(S_t + 64, a);  // chunk 2 in flight while chunks 0, 1 are exponentiated
+      emit(c0, 0);
+      emit(c1, 1);
+      wait_ld();
+      ld32_nowait(S_t + 96, b);
+      emit(a, 2);
+      wait_ld();
+      emit(b, 3);
+      wait_st();
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+      l = l * alpha + (rs + (rs0 + rs1));
+    }
+    if (ok && mbar_wait(&o_final[t], 0, abort_flag, 50)) {
+      fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int bb = bh / p.H, h = bh % p.H;
+      const bool row_ok = q < p.Sq;
+      __nv_bfloat16* dst = p.o + (((int64_t)bb * p.Sq + q) * p.H + h) * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        ld32_nowait(O_t + c * 32, o);
+        wait_ld();
+        if (row_ok) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            uint4 pk;
+            pk.x = pack_bf16(__uint_as_float(o[g * 8 + 0]) * inv, __uint_as_float(o[g * 8 + 1]) * inv);
+            pk.y = pack_bf16(__uint_as_float(o[g * 8 + 2]) * inv, __uint_as_float(o[g * 8 + 3]) * inv);
+            pk.z = pack_bf16(__uint_as_float(o[g * 8 + 4]) * inv, __uint_as_float(o[g * 8 + 5]) * inv);
+            pk.w = pack_bf16(__uint_as_float(o[g * 8 + 6]) * inv, __uint_as_float(o[g * 8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + c * 32 + g * 8) = pk;
+          }
+        }
+      }
+      if (row_ok) p.lse[(int64_t)bh * p.Sq + q] = (m + __log2f(l)) * 0.69314718055994531f;
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+}
+
+typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                             const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                             CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeFn encode() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult qr;
+    void* ptr = nullptr;
+    cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &qr);
+    fn = reinterpret_cast<EncodeFn>(ptr);
+  }
+  return fn;
+}
+
+// 3D map over [BH, S, D] bf16 with box {64, 128, 1}, 128B swizzle.
+static int map3(CUtensorMap* m, const void* ptr, int BH, int S, int D) {
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)BH};
+  cuuint64_t str[2] = {(cuuint64_t)D * 2, (cuuint64_t)S * D * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return (int)encode()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, str, box, es,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+template <int D>
+static void launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const Params& p,
+                   unsigned grid, cudaStream_t stream) {
+  static bool set = false;
+  const int bytes = Cfg<D>::BYTES + 1024;
+  if (!set) {
+    cudaFuncSetAttribute(fmha_fwd2_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    set = true;
+  }
+  fmha_fwd2_kernel<D><<<grid, NUM_THREADS, bytes, stream>>>(mq, mk, mv, p);
+}
+
+}  // namespace vo_fmha2
+
+extern "C" int vo_fmha_fwd2(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int Sq,
+                            int Skv, int D, float scale, int causal, cudaStream_t stream) {
+  using namespace vo_fmha2;
+  if (D != 64 && D != 128) return -1;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15)
+    return -2;
+  CUtensorMap mq, mk, mv;
+  int r = map3(&mq, q, B * H, Sq, D);
+  if (!r) r = map3(&mk, k, B * H, Skv, D);
+  if (!r) r = map3(&mv, v, B * H, Skv, D);
+  if (r) return r;
+  Params p;
+  p.Sq = Sq;
+  p.Skv = Skv;
+  p.H = H;
+  p.npairs = (Sq + 2 * BQ - 1) / (2 * BQ);
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.causal = causal;
+  p.o = reinterpret_cast<__nv_bfloat16*>(o);
+  p.lse = lse;
+  const long long grid = (long long)p.npairs * B * H;
+  if (grid == 0) return 0;
+  if (D == 64)
+    launch<64>(mq, mk, mv, p, (unsigned)grid, stream);
+  else
+    launch<128>(mq, mk, mv, p, (unsigned)grid, stream);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int vo_fmha_fwd2_error(int reset) {
+  int e = 0;
+  cudaMemcpyFromSymbol(&e, vo_fmha2::g_error, sizeof(int));
+  if (reset) {
+    int z = 0;
+    cudaMemcpyToSymbol(vo_fmha2::g_error, &z, sizeof(int));
+  }
+  return e;
+}

@@ -22,6 +22,7 @@
 #include <stdint.h>
 #include <stdio.h>
 #include <stdlib.h>
+#include <string.h>
 
 namespace vo_gemm {
 
@@ -160,10 +161,6 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return 0.5f * x * (1.f + t);
 }
 
-__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
-}
 
 struct Shape {
   int M, N, K;
@@ -171,30 +168,130 @@ struct Shape {
   int a_mn, b_mn;
 };
 
-__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v, int ncols) {
-  if (ncols == 32) {
+
+// ------------------------------------------------------------------------------------ epilogue
+// Each epilogue warp owns 32 accumulator rows and drains them 32 columns at a time: tcgen05.ld ->
+// fused math in registers -> bf16 (or fp32) tile in a swizzled shared-memory staging buffer -> one
+// TMA bulk store (or, for F32_ACC, a TMA bulk reduce-add) per 32 x 32 tile.  Two staging buffers per
+// warp alternate so the next chunk is written while the previous store drains; bulk stores keep
+// the L1/TEX pipe free for the TMA operand loads of the main loop.
+constexpr int EPI_WARP_BYTES = 8192;              // 2 buffers x 4 KB per epilogue warp
+constexpr int EPI_SMEM_BYTES = 4 * EPI_WARP_BYTES;  // 32 KB
+constexpr int SMEM1_BYTES = STAGES * STAGE_BYTES + EPI_SMEM_BYTES + 1024 + 256;
+
+struct EpiMaps {
+  CUtensorMap out;   // bf16 [M, N], box {32, 32}, 64B swizzle
+  CUtensorMap out2;  // bf16 [M, N] (GELU pre-activation / GATE_RES linear output)
+  CUtensorMap acc;   // fp32 [M, N], box {32, 32}, 128B swizzle (F32_ACC)
+};
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map), "r"(src),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+               "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// row `lane` of a 32 x 32 bf16 tile (64 B rows, 64B TMA swizzle: 16-byte unit u lands at u ^ ((row >> 1) & 3))
+__device__ __forceinline__ void stage_bf16_row(uint8_t* buf, int lane, const float* v) {
+  uint8_t* rowp = buf + lane * 64;
 #pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-      uint4 pk;
-      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+  for (int u = 0; u < 4; ++u) {
+    uint4 pk;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) h[q] = __floats2bfloat162_rn(v[j + 2 * q], v[j + 2 * q + 1]);
-      *reinterpret_cast<uint4*>(dst + j) = pk;
+    for (int q = 0; q < 4; ++q) h[q] = __floats2bfloat162_rn(v[8 * u + 2 * q], v[8 * u + 2 * q + 1]);
+    *reinterpret_cast<uint4*>(rowp + 16 * (u ^ ((lane >> 1) & 3))) = pk;
+  }
+}
+// row `lane` of a 32 x 32 fp32 tile (128 B rows, 128B TMA swizzle: unit u lands at u ^ (row & 7))
+__device__ __forceinline__ void stage_f32_row(uint8_t* buf, int lane, const float* v) {
+  uint8_t* rowp = buf + lane * 128;
+#pragma unroll
+  for (int u = 0; u < 8; ++u)
+    *reinterpret_cast<float4*>(rowp + 16 * (u ^ (lane & 7))) = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2],
+                                                                           v[4 * u + 3]);
+}
+
+// Drains this warp's 32 rows x BN columns of one accumulator.  `tacc` = TMEM address of (row 0 of
+// this warp, column 0 of the accumulator); rows [row0, row0 + 32), columns [col_base, col_base + BN).
+template <typename ShapeT>
+__device__ __forceinline__ void epilogue_rows(uint32_t tacc, int row0, int col_base, const ShapeT& sh,
+                                              const EpiParams& ep, const EpiMaps& em, uint8_t* wbuf, int lane,
+                                              int& nchunk) {
+  const int row = row0 + lane;
+  const bool row_ok = row < sh.M;
+  for (int c = 0; c < BN / 32; ++c) {
+    uint32_t r[32];
+    tc_ld_32x32b_x32(tacc + c * 32, r);
+    const int col0 = col_base + c * 32;
+    if (col0 >= sh.N) continue;  // warp-uniform
+    const int ncols = min(32, sh.N - col0);
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    uint8_t* buf = wbuf + (nchunk & 1) * 4096;
+    ++nchunk;
+    if (lane == 0) bulk_wait_read1();  // the store issued from this buffer two chunks ago has read it
+    __syncwarp();
+    if (ep.epi == EPI_F32_ACC) {
+      stage_f32_row(buf, lane, v);
+    } else {
+      if (ep.bias) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += (j < ncols) ? __bfloat162float(ep.bias[col0 + j]) : 0.f;
+      }
+      if (ep.epi == EPI_GELU || ep.epi == EPI_GATE_RES) {
+        stage_bf16_row(buf + 2048, lane, v);
+        if (ep.epi == EPI_GELU) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(__bfloat162float(__float2bfloat16_rn(v[j])));
+        } else if (row_ok) {
+          const __nv_bfloat16* g = ep.gate + (int64_t)(row / ep.S) * ep.gate_ld + col0;
+          const __nv_bfloat16* rs = ep.res + (int64_t)row * ep.ldc + col0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (j < ncols) {
+              const float lin = __bfloat162float(__float2bfloat16_rn(v[j]));
+              v[j] = __bfloat162float(rs[j]) + __bfloat162float(g[j]) * lin;
+            }
+          }
+        }
+      }
+      stage_bf16_row(buf, lane, v);
     }
-  } else {
-    for (int j = 0; j < ncols; ++j) dst[j] = __float2bfloat16_rn(v[j]);
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      if (ep.epi == EPI_F32_ACC) {
+        tma_reduce_add_2d(&em.acc, smem_u32(buf), col0, row0);
+      } else {
+        tma_store_2d(&em.out, smem_u32(buf), col0, row0);
+        if (ep.epi == EPI_GELU || ep.epi == EPI_GATE_RES) tma_store_2d(&em.out2, smem_u32(buf + 2048), col0, row0);
+      }
+      bulk_commit();
+    }
   }
 }
 
 // ------------------------------------------------------------------------------------ kernel
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Shape sh,
-                EpiParams ep) {
+                EpiParams ep, const __grid_constant__ EpiMaps em) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_a = smem;
   uint8_t* stage_b = smem + STAGES * A_STAGE_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* epi_stage = smem + STAGES * STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + EPI_SMEM_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -315,7 +412,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..5)
     const int lane_base = 32 * (warp & 3);
-    int it = 0;
+    uint8_t* wbuf = epi_stage + (warp - 2) * EPI_WARP_BYTES;
+    int it = 0, nchunk = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
       const int tile = u / sh.splits;
       const int tm = tile / sh.tiles_n, tn = tile % sh.tiles_n;
@@ -323,55 +421,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, 4)) break;
       tc_fence_after();
-      const int row = tm * BM + lane_base + lane;
-      const bool row_ok = row < sh.M;
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tc_ld_32x32b_x32(tmem_base + ((uint32_t)lane_base << 16) + acc * BN + c * 32, r);
-        const int col0 = tn * BN + c * 32;
-        if (!row_ok || col0 >= sh.N) continue;
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        const int ncols = min(32, sh.N - col0);
-        if (ep.epi == EPI_F32_ACC) {
-          float* dst = ep.out_f32 + (int64_t)row * ep.ldc + col0;
-          if (ncols == 32) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) red_add_v4(dst + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
-          } else {
-            for (int j = 0; j < ncols; ++j) atomicAdd(dst + j, v[j]);
-          }
-          continue;
-        }
-        if (ep.bias) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] += (j < ncols) ? __bfloat162float(ep.bias[col0 + j]) : 0.f;
-        }
-        __nv_bfloat16* dst = ep.out + (int64_t)row * ep.ldc + col0;
-        if (ep.epi == EPI_GELU || ep.epi == EPI_GATE_RES) {
-          store_bf16x32(ep.out2 + (int64_t)row * ep.ldc + col0, v, ncols);
-          if (ep.epi == EPI_GELU) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(__bfloat162float(__float2bfloat16_rn(v[j])));
-          } else {
-            const __nv_bfloat16* g = ep.gate + (int64_t)(row / ep.S) * ep.gate_ld + col0;
-            const __nv_bfloat16* rs = ep.res + (int64_t)row * ep.ldc + col0;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (j < ncols) {
-                const float lin = __bfloat162float(__float2bfloat16_rn(v[j]));
-                v[j] = __bfloat162float(rs[j]) + __bfloat162float(g[j]) * lin;
-              }
-            }
-          }
-        }
-        store_bf16x32(dst, v, ncols);
-      }
+      epilogue_rows(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, tm * BM + lane_base, tn * BN, sh, ep, em,
+                    wbuf, lane, nchunk);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -392,7 +449,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // on CTA 0's "tmem empty" barrier.
 constexpr int STAGES2 = 6;
 constexpr int STAGE2_BYTES = 2 * BM * BK * 2;  // A 128x64 + B 128x64 per CTA = 32 KB
-constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 256;
+constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + EPI_SMEM_BYTES + 1024 + 256;
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -441,10 +498,11 @@ __host__ __device__ constexpr uint32_t make_idesc2(int a_mn, int b_mn) {
 
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm2sm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Shape sh,
-                   EpiParams ep) {
+                   EpiParams ep, const __grid_constant__ EpiMaps em) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES2 * STAGE2_BYTES);
+  uint8_t* epi_stage = smem + STAGES2 * STAGE2_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + EPI_SMEM_BYTES);
   uint64_t* empty = full + STAGES2;
   uint64_t* tfull = empty + STAGES2;
   uint64_t* tempty = tfull + 2;
@@ -562,62 +620,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else {
     const int lane_base = 32 * (warp & 3);
     const uint32_t tempty0[2] = {map_to_rank0(smem_u32(&tempty[0])), map_to_rank0(smem_u32(&tempty[1]))};
-    int it = 0;
+    uint8_t* wbuf = epi_stage + (warp - 2) * EPI_WARP_BYTES;
+    int it = 0, nchunk = 0;
     for (int u = pair; u < units; u += npairs, ++it) {
       const int tile = u / sh.splits;
       const int tm = tile / sh.tiles_n, tn = tile % sh.tiles_n;
       const int acc = it & 1;
       if (!mbar_wait(&tfull[acc], (it >> 1) & 1, abort_flag, 34)) break;
       tc_fence_after();
-      const int row = tm * 256 + (int)rank * 128 + lane_base + lane;
-      const bool row_ok = row < sh.M;
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tc_ld_32x32b_x32(tmem_base + ((uint32_t)lane_base << 16) + acc * BN + c * 32, r);
-        const int col0 = tn * BN + c * 32;
-        if (!row_ok || col0 >= sh.N) continue;
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        const int ncols = min(32, sh.N - col0);
-        if (ep.epi == EPI_F32_ACC) {
-          float* dst = ep.out_f32 + (int64_t)row * ep.ldc + col0;
-          if (ncols == 32) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) red_add_v4(dst + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
-          } else {
-            for (int j = 0; j < ncols; ++j) atomicAdd(dst + j, v[j]);
-          }
-          continue;
-        }
-        if (ep.bias) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] += (j < ncols) ? __bfloat162float(ep.bias[col0 + j]) : 0.f;
-        }
-        __nv_bfloat16* dst = ep.out + (int64_t)row * ep.ldc + col0;
-        if (ep.epi == EPI_GELU || ep.epi == EPI_GATE_RES) {
-          store_bf16x32(ep.out2 + (int64_t)row * ep.ldc + col0, v, ncols);
-          if (ep.epi == EPI_GELU) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(__bfloat162float(__float2bfloat16_rn(v[j])));
-          } else {
-            const __nv_bfloat16* g = ep.gate + (int64_t)(row / ep.S) * ep.gate_ld + col0;
-            const __nv_bfloat16* rs = ep.res + (int64_t)row * ep.ldc + col0;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (j < ncols) {
-                const float lin = __bfloat162float(__float2bfloat16_rn(v[j]));
-                v[j] = __bfloat162float(rs[j]) + __bfloat162float(g[j]) * lin;
-              }
-            }
-          }
-        }
-        store_bf16x32(dst, v, ncols);
-      }
+      epilogue_rows(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, tm * 256 + (int)rank * 128 + lane_base,
+                    tn * BN, sh, ep, em, wbuf, lane, nchunk);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty0[acc]);
     }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
   tc_fence_before();
   cluster_sync();
@@ -657,6 +675,20 @@ static int make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols,
   return r == CUDA_SUCCESS ? 0 : (int)r;
 }
 
+// 2D tensor map for an epilogue output: [rows, cols] with row stride `ld` elements, 32 x 32 box.
+static int make_out_map(CUtensorMap* m, const void* ptr, bool f32, int64_t rows, int64_t cols, int64_t ld) {
+  const int esz = f32 ? 4 : 2;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * esz)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode()(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                            const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : (int)r;
+}
+
 static int g_num_sms = 0;
 static int g_use_2sm = -1;
 
@@ -681,6 +713,23 @@ extern "C" int vo_gemm_launch(const void* A, const void* B, int M, int N, int K,
   const bool two_sm = g_use_2sm && M >= 256;
   CUtensorMap ma, mb;
   int r;
+  // epilogue outputs go out through TMA: 16-byte aligned bases and row strides
+  EpiMaps em;
+  memset(&em, 0, sizeof(em));
+  if (ep.epi == EPI_F32_ACC) {
+    if ((reinterpret_cast<uintptr_t>(ep.out_f32) & 15) || (ep.ldc * 4) % 16) return -4;
+    r = make_out_map(&em.acc, ep.out_f32, true, M, N, ep.ldc);
+    if (r) return r;
+  } else {
+    if ((reinterpret_cast<uintptr_t>(ep.out) & 15) || (ep.ldc * 2) % 16) return -4;
+    r = make_out_map(&em.out, ep.out, false, M, N, ep.ldc);
+    if (r) return r;
+    if (ep.epi == EPI_GELU || ep.epi == EPI_GATE_RES) {
+      if (reinterpret_cast<uintptr_t>(ep.out2) & 15) return -4;
+      r = make_out_map(&em.out2, ep.out2, false, M, N, ep.ldc);
+      if (r) return r;
+    }
+  }
   // 2-SM tiles load 128 rows of A and 128 columns of B per CTA
   if (a_mn)
     r = make_map(&ma, A, K, M, lda, 64, 64);
@@ -696,8 +745,7 @@ extern "C" int vo_gemm_launch(const void* A, const void* B, int M, int N, int K,
     int dev;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         STAGES * STAGE_BYTES + 1024 + 256);
+    cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM1_BYTES);
     cudaFuncSetAttribute(gemm2sm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
     cudaFuncSetAttribute(gemm2sm_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   }
@@ -729,11 +777,11 @@ extern "C" int vo_gemm_launch(const void* A, const void* B, int M, int N, int K,
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm2sm_kernel, ma, mb, sh, ep);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm2sm_kernel, ma, mb, sh, ep, em);
     return (int)e;
   }
   const int grid = units < g_num_sms ? units : g_num_sms;
-  gemm_kernel<<<grid, NUM_THREADS, STAGES * STAGE_BYTES + 1024 + 256, stream>>>(ma, mb, sh, ep);
+  gemm_kernel<<<grid, NUM_THREADS, SMEM1_BYTES, stream>>>(ma, mb, sh, ep, em);
   return (int)cudaGetLastError();
 }
 

@@ -220,67 +220,75 @@ __global__ void qk_rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ qkv, con
                                       const float* __restrict__ rope_cos, const float* __restrict__ rope_sin,
                                       __nv_bfloat16* __restrict__ dqkv, float* __restrict__ dw_partial, int64_t rows,
                                       int H, int S_seg, int S_total, int seg_off, int64_t row_stride, int3 part_off) {
+  // Thread (h, sub) owns 8 columns of head h for every row this block visits (rows strided by the
+  // grid), so the weight-gradient partial sums stay in registers; one shared-memory pass at the end
+  // folds the heads together.  blockDim.x = H * DH / 8 (rounded up to a warp multiple).
   constexpr int LPH = DH / 8;
-  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t head_task = gid / LPH;
-  const int sub = gid % LPH;
-  const bool active = head_task < rows * H;
-  const int64_t row = active ? head_task / H : 0;
-  const int h = active ? (int)(head_task % H) : 0;
-  const int64_t b = row / S_seg;
-  const int s = (int)(row % S_seg) + seg_off;
-  const int64_t in_off = (((int64_t)b * H + h) * S_total + s) * DH + sub * 8;
+  const int lanes = H * LPH;
+  const bool active = threadIdx.x < lanes;
+  const int h = active ? threadIdx.x / LPH : 0;
+  const int sub = threadIdx.x % LPH;
+  float wqv[8] = {0}, wkv[8] = {0};
+  if (wq && part_off.x >= 0) unpack8(*reinterpret_cast<const bf16x8*>(wq + sub * 8), wqv);
+  if (wk && part_off.y >= 0) unpack8(*reinterpret_cast<const bf16x8*>(wk + sub * 8), wkv);
   float dwacc[2][8] = {{0}};
+  // every thread runs the same trip count (the row loop is block-uniform) so the width-LPH shuffles
+  // below always see full warps; threads past H * LPH only skip their loads and stores
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const int64_t b = row / S_seg;
+    const int s = (int)(row % S_seg) + seg_off;
+    const int64_t in_off = (((int64_t)b * H + h) * S_total + s) * DH + sub * 8;
 #pragma unroll
-  for (int which = 0; which < 3; ++which) {
-    const int poff = which == 0 ? part_off.x : which == 1 ? part_off.y : part_off.z;
-    if (poff < 0) continue;
-    float g[8] = {0};
-    if (active) unpack8(*reinterpret_cast<const bf16x8*>((which == 0 ? dq : which == 1 ? dk : dv) + in_off), g);
-    float o[8];
-    if (which < 2) {
-      if (rope_cos) {  // transpose of the rotation
-        const float* cr = rope_cos + (int64_t)s * (DH / 2) + sub * 4;
-        const float* sr = rope_sin + (int64_t)s * (DH / 2) + sub * 4;
+    for (int which = 0; which < 3; ++which) {
+      const int poff = which == 0 ? part_off.x : which == 1 ? part_off.y : part_off.z;
+      if (poff < 0) continue;
+      float g[8] = {0};
+      if (active) unpack8(*reinterpret_cast<const bf16x8*>((which == 0 ? dq : which == 1 ? dk : dv) + in_off), g);
+      float o[8];
+      if (which < 2) {
+        if (rope_cos && active) {  // transpose of the rotation
+          const float* cr = rope_cos + (int64_t)s * (DH / 2) + sub * 4;
+          const float* sr = rope_sin + (int64_t)s * (DH / 2) + sub * 4;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float g0 = g[2 * j], g1 = g[2 * j + 1];
-          g[2 * j] = g0 * cr[j] + g1 * sr[j];
-          g[2 * j + 1] = -g0 * sr[j] + g1 * cr[j];
+          for (int j = 0; j < 4; ++j) {
+            const float g0 = g[2 * j], g1 = g[2 * j + 1];
+            g[2 * j] = g0 * cr[j] + g1 * sr[j];
+            g[2 * j + 1] = -g0 * sr[j] + g1 * cr[j];
+          }
         }
+        float x[8] = {0};
+        if (active) unpack8(*reinterpret_cast<const bf16x8*>(qkv + row * row_stride + poff + h * DH + sub * 8), x);
+        const float* w = which == 0 ? wqv : wkv;
+        const float rs = active ? (which == 0 ? rstd_q : rstd_k)[row * H + h] : 0.f;
+        float dot = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float xh = x[j] * rs;
+          dot += g[j] * w[j] * xh;
+          dwacc[which][j] += g[j] * xh;
+        }
+#pragma unroll
+        for (int off = LPH / 2; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off, LPH);
+        dot *= 1.f / DH;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = rs * (g[j] * w[j] - x[j] * rs * dot);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = g[j];
       }
-      float x[8] = {0}, w[8];
-      if (active) unpack8(*reinterpret_cast<const bf16x8*>(qkv + row * row_stride + poff + h * DH + sub * 8), x);
-      unpack8(*reinterpret_cast<const bf16x8*>((which == 0 ? wq : wk) + sub * 8), w);
-      const float rs = active ? (which == 0 ? rstd_q : rstd_k)[row * H + h] : 0.f;
-      float dot = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float xh = x[j] * rs;
-        dot += g[j] * w[j] * xh;
-        dwacc[which][j] += g[j] * xh;
-      }
-#pragma unroll
-      for (int off = LPH / 2; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
-      dot /= DH;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = rs * (g[j] * w[j] - x[j] * rs * dot);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = g[j];
+      if (active) *reinterpret_cast<bf16x8*>(dqkv + row * row_stride + poff + h * DH + sub * 8) = pack8(o);
     }
-    if (active) *reinterpret_cast<bf16x8*>(dqkv + row * row_stride + poff + h * DH + sub * 8) = pack8(o);
   }
-  // per-block partial of dw (q and k): reduce lanes with the same `sub` inside the block via smem
-  __shared__ float sm[2][DH];
-  for (int i = threadIdx.x; i < 2 * DH; i += blockDim.x) (&sm[0][0])[i] = 0.f;
+  // fold the heads: red[lane][16] -> dw_partial[block][which][DH]
+  extern __shared__ float red[];
+  for (int i = 0; i < 16; ++i) red[threadIdx.x * 16 + i] = active ? dwacc[i >> 3][i & 7] : 0.f;
   __syncthreads();
-#pragma unroll
-  for (int which = 0; which < 2; ++which)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) atomicAdd(&sm[which][sub * 8 + j], dwacc[which][j]);
-  __syncthreads();
-  for (int i = threadIdx.x; i < 2 * DH; i += blockDim.x) dw_partial[(int64_t)blockIdx.x * 2 * DH + i] = (&sm[0][0])[i];
+  for (int i = threadIdx.x; i < 2 * DH; i += blockDim.x) {
+    const int which = i / DH, col = i % DH, sb = col / 8, j = col % 8;
+    float s = 0.f;
+    for (int hh = 0; hh < H; ++hh) s += red[(hh * LPH + sb) * 16 + which * 8 + j];
+    dw_partial[(int64_t)blockIdx.x * 2 * DH + i] = s;
+  }
 }
 
 }  // namespace
@@ -419,27 +427,27 @@ std::vector<torch::Tensor> qk_rmsnorm_bwd(torch::Tensor qkv, torch::Tensor wq, t
   const int3 po = make_int3((int)part_off[0], (int)part_off[1], (int)part_off[2]);
   const int64_t rows = qkv.size(0);
   auto dqkv = torch::empty_like(qkv);
-  const int64_t threads = rows * H * (DH / 8);
-  const int nblk = (threads + 255) / 256;
+  const int lanes = H * (DH / 8);
+  TORCH_CHECK(lanes <= 1024, "too many heads for the q/k-norm backward");
+  const int threads = (lanes + 31) / 32 * 32;
+  const int nblk = (int)std::max<int64_t>(1, std::min<int64_t>(rows, 8LL * num_sms()));
+  const size_t smem = (size_t)threads * 16 * sizeof(float);
   auto part = torch::empty({nblk, 2, DH}, qkv.options().dtype(torch::kFloat32));
   const float* rc = (rope_cos.has_value() && rope_cos->defined()) ? rope_cos->data_ptr<float>() : nullptr;
   const float* rsn = (rope_sin.has_value() && rope_sin->defined()) ? rope_sin->data_ptr<float>() : nullptr;
   const int64_t rs_ = qkv.size(1);
+#define VO_QKBWD(DHV)                                                                                              \
+  qk_rmsnorm_bwd_kernel<DHV><<<nblk, threads, smem, stream()>>>(                                                   \
+      bptr(qkv), bptr(wq), bptr(wk), bptr(dq), bptr(dk), bptr(dv), rq.data_ptr<float>(), rk.data_ptr<float>(), rc, \
+      rsn, bptr(dqkv), part.data_ptr<float>(), rows, H, (int)S_seg, S_total, (int)seg_off, rs_, po)
   if (DH == 32)
-    qk_rmsnorm_bwd_kernel<32><<<nblk, 256, 0, stream()>>>(bptr(qkv), bptr(wq), bptr(wk), bptr(dq), bptr(dk), bptr(dv),
-                                                          rq.data_ptr<float>(), rk.data_ptr<float>(), rc, rsn,
-                                                          bptr(dqkv), part.data_ptr<float>(), rows, H, (int)S_seg,
-                                                          S_total, (int)seg_off, rs_, po);
+    VO_QKBWD(32);
   else if (DH == 64)
-    qk_rmsnorm_bwd_kernel<64><<<nblk, 256, 0, stream()>>>(bptr(qkv), bptr(wq), bptr(wk), bptr(dq), bptr(dk), bptr(dv),
-                                                          rq.data_ptr<float>(), rk.data_ptr<float>(), rc, rsn,
-                                                          bptr(dqkv), part.data_ptr<float>(), rows, H, (int)S_seg,
-                                                          S_total, (int)seg_off, rs_, po);
+    VO_QKBWD(64);
   else
-    qk_rmsnorm_bwd_kernel<128><<<nblk, 256, 0, stream()>>>(bptr(qkv), bptr(wq), bptr(wk), bptr(dq), bptr(dk),
-                                                           bptr(dv), rq.data_ptr<float>(), rk.data_ptr<float>(), rc,
-                                                           rsn, bptr(dqkv), part.data_ptr<float>(), rows, H,
-                                                           (int)S_seg, S_total, (int)seg_off, rs_, po); vo::count_launch();
+    VO_QKBWD(128);
+#undef VO_QKBWD
+  vo::count_launch();
   VO_CUDA_OK(cudaGetLastError());
   auto dw = part.sum(0);  // [2, DH]
   return {dqkv, dw[0], dw[1]};

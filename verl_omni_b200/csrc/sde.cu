@@ -88,14 +88,19 @@ __global__ void sde_fwd_kernel(const float* __restrict__ x, const float* __restr
                                const float* __restrict__ prev_in, const float* __restrict__ noise,
                                float* __restrict__ prev_out, float* __restrict__ mean_out,
                                float* __restrict__ partial, int64_t n, int64_t chunk, int nchunks,
-                               float sigma_max, float eta, int type, bool norm, uint64_t seed, uint32_t offset) {
+                               float sigma_max, float eta, int type, bool norm, uint64_t seed, uint32_t offset,
+                               const int64_t* __restrict__ row_seeds) {
   __shared__ float red[32];
   const int b = blockIdx.y;
   const RowCoef c = row_coef(sigma[b], sigma_prev[b], sigma_max, eta, type, norm);
   const int64_t base = (int64_t)b * n;
   const int64_t lo = (int64_t)blockIdx.x * chunk;
   const int64_t hi = min(lo + chunk, n);
-  const uint2 key = make_uint2((uint32_t)seed, (uint32_t)(seed >> 32));
+  // per-row seeds make a sample's noise independent of its position in the batch (request packing);
+  // otherwise one seed keys the whole call and the row index enters the Philox counter
+  const uint64_t s = row_seeds ? (uint64_t)row_seeds[b] : seed;
+  const uint2 key = make_uint2((uint32_t)s, (uint32_t)(s >> 32));
+  const uint32_t brow = row_seeds ? 0u : (uint32_t)b;
   float acc = 0.f;
   for (int64_t i = lo + 4 * (int64_t)threadIdx.x; i < hi; i += 4 * (int64_t)blockDim.x) {
     float xs[4], vs[4], ps[4], ms[4];
@@ -121,7 +126,7 @@ __global__ void sde_fwd_kernel(const float* __restrict__ x, const float* __restr
 #pragma unroll
       for (int j = 0; j < 4; ++j) ps[j] = (i + j < hi) ? ms[j] + c.scale * noise[base + i + j] : ms[j];
     } else {
-      uint4 r = philox(make_uint4((uint32_t)(i >> 2), (uint32_t)b, offset, 0u), key);
+      uint4 r = philox(make_uint4((uint32_t)(i >> 2), brow, offset, 0u), key);
       float2 z01 = box_muller(r.x, r.y), z23 = box_muller(r.z, r.w);
       ps[0] = ms[0] + c.scale * z01.x;
       ps[1] = ms[1] + c.scale * z01.y;
@@ -185,12 +190,47 @@ __global__ void sde_bwd_kernel(const float* __restrict__ prev, const float* __re
   }
 }
 
+// z[b, i] ~ N(0, 1) from the same Philox4x32-10 / Box-Muller stream the SDE step draws, keyed by
+// row_seeds[b] with counter (i / 4, 0, offset, 0): the initial latent noise of a rollout sample
+// depends only on its own seed.
+__global__ void normal_fill_kernel(float* __restrict__ out, const int64_t* __restrict__ row_seeds, int64_t n,
+                                   uint32_t offset) {
+  const int b = blockIdx.y;
+  const uint64_t s = (uint64_t)row_seeds[b];
+  const uint2 key = make_uint2((uint32_t)s, (uint32_t)(s >> 32));
+  float* o = out + (int64_t)b * n;
+  for (int64_t i = 4 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x); i < n; i += 4 * (int64_t)gridDim.x * blockDim.x) {
+    uint4 r = philox(make_uint4((uint32_t)(i >> 2), 0u, offset, 0u), key);
+    float2 z01 = box_muller(r.x, r.y), z23 = box_muller(r.z, r.w);
+    const float z[4] = {z01.x, z01.y, z23.x, z23.y};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (i + j < n) o[i + j] = z[j];
+  }
+}
+
 }  // namespace
+
+torch::Tensor normal_fill(torch::Tensor row_seeds, int64_t n, int64_t offset) {
+  VO_CHECK_INPUT(row_seeds);
+  TORCH_CHECK(row_seeds.scalar_type() == torch::kInt64, "row_seeds must be int64");
+  c10::cuda::CUDAGuard g(row_seeds.device());
+  const int64_t B = row_seeds.numel();
+  auto out = torch::empty({B, n}, row_seeds.options().dtype(torch::kFloat32));
+  if (B == 0 || n == 0) return out;
+  const int bx = (int)std::max<int64_t>(1, std::min<int64_t>((n / 4 + 255) / 256, 64));
+  normal_fill_kernel<<<dim3(bx, (unsigned)B), 256, 0, stream()>>>(out.data_ptr<float>(), row_seeds.data_ptr<int64_t>(),
+                                                                   n, (uint32_t)offset);
+  vo::count_launch();
+  VO_CUDA_OK(cudaGetLastError());
+  return out;
+}
 
 std::vector<torch::Tensor> sde_step_fwd(torch::Tensor x, torch::Tensor v, torch::Tensor sigma,
                                         torch::Tensor sigma_prev, c10::optional<torch::Tensor> prev,
                                         c10::optional<torch::Tensor> noise, double sigma_max, double eta, int64_t type,
-                                        int64_t seed, int64_t offset, bool want_logp, bool norm) {
+                                        int64_t seed, int64_t offset, bool want_logp, bool norm,
+                                        c10::optional<torch::Tensor> row_seeds) {
   VO_CHECK_INPUT(x);
   VO_CHECK_INPUT(v);
   TORCH_CHECK(x.scalar_type() == torch::kFloat32 && v.scalar_type() == torch::kFloat32, "fp32 inputs required");
@@ -222,12 +262,18 @@ std::vector<torch::Tensor> sde_step_fwd(torch::Tensor x, torch::Tensor v, torch:
   auto st = stream();
   const float* pp = has_prev ? prev->data_ptr<float>() : nullptr;
   const float* np_ = has_noise ? noise->data_ptr<float>() : nullptr;
+  const int64_t* rsp = nullptr;
+  if (row_seeds.has_value() && row_seeds->defined()) {
+    VO_CHECK_INPUT((*row_seeds));
+    TORCH_CHECK(row_seeds->scalar_type() == torch::kInt64 && row_seeds->numel() == B, "row_seeds must be int64 [B]");
+    rsp = row_seeds->data_ptr<int64_t>();
+  }
 #define VO_SDE_LAUNCH(HP, HN)                                                                               \
   sde_fwd_kernel<HP, HN><<<grid, 256, 0, st>>>(x.data_ptr<float>(), v.data_ptr<float>(),                   \
                                                sigma.data_ptr<float>(), sigma_prev.data_ptr<float>(), pp, np_, \
                                                prev_out.data_ptr<float>(), mean.data_ptr<float>(),          \
                                                partial.data_ptr<float>(), n, chunk, nchunks, (float)sigma_max, \
-                                               (float)eta, (int)type, norm, (uint64_t)seed, (uint32_t)offset)
+                                               (float)eta, (int)type, norm, (uint64_t)seed, (uint32_t)offset, rsp)
   if (has_prev)
     VO_SDE_LAUNCH(true, false);
   else if (has_noise)
@@ -311,15 +357,15 @@ extern "C" __attribute__((visibility("default"))) int vo_sde_step_fwd_noalloc(
   if (prev_in)
     vo::sde_fwd_kernel<true, false><<<grid, 256, 0, stream>>>(x, v, sigma, sigma_prev, prev_in, nullptr, prev_dst,
                                                              mean_out, partial, n, chunk, nchunks, sigma_max, eta,
-                                                             sde_type, norm != 0, seed, offset);
+                                                             sde_type, norm != 0, seed, offset, nullptr);
   else if (noise)
     vo::sde_fwd_kernel<false, true><<<grid, 256, 0, stream>>>(x, v, sigma, sigma_prev, nullptr, noise, prev_dst,
                                                              mean_out, partial, n, chunk, nchunks, sigma_max, eta,
-                                                             sde_type, norm != 0, seed, offset);
+                                                             sde_type, norm != 0, seed, offset, nullptr);
   else
     vo::sde_fwd_kernel<false, false><<<grid, 256, 0, stream>>>(x, v, sigma, sigma_prev, nullptr, nullptr, prev_dst,
                                                               mean_out, partial, n, chunk, nchunks, sigma_max, eta,
-                                                              sde_type, norm != 0, seed, offset);
+                                                              sde_type, norm != 0, seed, offset, nullptr);
   vo::sde_finalize_kernel<<<(B + 7) / 8, 256, 0, stream>>>(partial, sigma, sigma_prev, want_logp ? logp_out : nullptr,
                                                            std_out, B, nchunks, n, sigma_max, eta, sde_type,
                                                            norm != 0);

@@ -18,6 +18,10 @@ import torch.nn.functional as F
 from verl_omni_b200.ops._ext import ext
 
 
+# forward kernel generation: 2 = two query tiles per CTA with P/O in tensor memory, 1 = one tile per CTA
+_FWD_VERSION = int(os.environ.get("VO_FMHA_FWD", "1"))
+
+
 def _native() -> bool:
     return os.environ.get("VO_ATTN", "native") != "torch" and hasattr(ext(), "fmha_fwd")
 
@@ -25,7 +29,7 @@ def _native() -> bool:
 class _FMHA(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, causal, scale):
-        o, lse = ext().fmha_fwd(q, k, v, causal, scale)
+        o, lse = ext().fmha_fwd(q, k, v, causal, scale, _FWD_VERSION)
         ctx.save_for_backward(q, k, v, o, lse)
         ctx.meta = (causal, scale)
         return o

@@ -67,6 +67,40 @@ def bench_gemm(a) -> list[dict]:
     return out
 
 
+# (name, M, N, K) of the linear layers of one SD3.5-Medium-shaped joint block for a 16-sample
+# micro-batch (1024 image + 333 text tokens per sample), plus the 48-sample rollout batch
+SD35_SHAPES = [
+    ("img_qkv", 16 * 1024, 4608, 1536), ("img_out", 16 * 1024, 1536, 1536), ("img_ff1", 16 * 1024, 6144, 1536),
+    ("img_ff2", 16 * 1024, 1536, 6144), ("txt_qkv", 16 * 333, 4608, 1536), ("txt_out", 16 * 333, 1536, 1536),
+    ("txt_ff1", 16 * 333, 6144, 1536), ("txt_ff2", 16 * 333, 1536, 6144), ("mod", 16, 13824, 1536),
+    ("roll_ff1", 48 * 1024, 6144, 1536), ("roll_txt_qkv", 48 * 333, 4608, 1536),
+]
+
+
+def bench_gemm_sweep(a) -> list[dict]:
+    """Native tcgen05 GEMM vs cuBLAS on every linear-layer shape of the flagship workload."""
+    from verl_omni_b200.ops._ext import ext
+
+    e = ext()
+    out = []
+    for name, M, N, K in SD35_SHAPES:
+        x = torch.randn(M, K, device="cuda").bfloat16()
+        w = (torch.randn(N, K, device="cuda") / K ** 0.5).bfloat16()
+        dy = torch.randn(M, N, device="cuda").bfloat16()
+        gw = torch.zeros(N, K, device="cuda")
+        row = {"op": "gemm_sweep", "name": name, "M": M, "N": N, "K": K}
+        for kind, nat, ref in (
+                ("fwd", lambda: e.gemm_fwd(x, w, None, 0, None, None, 1), lambda: torch.matmul(x, w.t())),
+                ("dgrad", lambda: e.gemm_dgrad(dy, w), lambda: torch.matmul(dy, w)),
+                ("wgrad", lambda: e.gemm_wgrad(dy, x, gw, True), lambda: gw.add_(torch.matmul(dy.t(), x)))):
+            tn, tr = timeit(nat, a.iters), timeit(ref, a.iters)
+            row[kind] = {"native_ms": round(tn, 4), "cublas_ms": round(tr, 4),
+                         "native_tflops": round(2.0 * M * N * K / tn / 1e9, 1)}
+        out.append(row)
+        del x, w, dy, gw
+    return out
+
+
 def bench_fmha(a) -> list[dict]:
     from verl_omni_b200.ops._ext import ext
 
@@ -74,10 +108,11 @@ def bench_fmha(a) -> list[dict]:
     B, H, S, D = a.B, a.H, a.S, a.D
     q, k, v = (torch.randn(B, H, S, D, device="cuda").bfloat16() for _ in range(3))
     scale = 1 / math.sqrt(D)
-    o, lse = e.fmha_fwd(q, k, v, False, scale)
+    o, lse = e.fmha_fwd(q, k, v, False, scale, 1)
     do = torch.randn_like(o)
     flops_f = 4.0 * B * H * S * S * D
-    cases = {"fwd": (lambda: e.fmha_fwd(q, k, v, False, scale), flops_f)}
+    cases = {"fwd": (lambda: e.fmha_fwd(q, k, v, False, scale, 1), flops_f),
+             "fwd2": (lambda: e.fmha_fwd(q, k, v, False, scale, 2), flops_f)}
     if hasattr(e, "fmha_bwd"):
         cases["bwd"] = (lambda: e.fmha_bwd(q, k, v, o, lse, do, False, scale), 2.5 * flops_f)
     if a.compare:
@@ -117,7 +152,7 @@ def bench_adaln(a) -> list[dict]:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "fmha", "sde", "adaln"])
+    ap.add_argument("op", choices=["gemm", "gemm_sweep", "fmha", "sde", "adaln"])
     ap.add_argument("--M", type=int, default=21712)
     ap.add_argument("--N", type=int, default=6144)
     ap.add_argument("--K", type=int, default=1536)
@@ -130,7 +165,7 @@ def main() -> None:
     ap.add_argument("--compare", action="store_true")
     a = ap.parse_args()
     pk = _peaks()
-    rows = {"gemm": bench_gemm, "fmha": bench_fmha, "sde": bench_sde, "adaln": bench_adaln}[a.op](a)
+    rows = {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "fmha": bench_fmha, "sde": bench_sde, "adaln": bench_adaln}[a.op](a)
     for r in rows:
         if "tflops" in r:
             r[f"frac_of_{pk['src']}_gemm_peak"] = round(r["tflops"] / pk["tflops"], 3)

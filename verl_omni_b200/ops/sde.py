@@ -43,14 +43,26 @@ def philox4x32(counter: list[torch.Tensor], key: tuple[int, int], rounds: int = 
     return [c0, c1, c2, c3]
 
 
-def philox_normal(seed: int, rows: int, n: int, offset: int = 0) -> torch.Tensor:
-    """[rows, n] standard normals, bit-for-bit the stream the CUDA kernel draws (up to libm ulps)."""
+def philox_normal(seed: int, rows: int, n: int, offset: int = 0,
+                  row_seeds: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """[rows, n] standard normals, bit-for-bit the stream the CUDA kernels draw (up to libm ulps).
+
+    Without ``row_seeds`` one key (``seed``) serves the call and the row index enters the counter;
+    with ``row_seeds`` (int64 [rows]) row ``b`` is keyed by its own seed and its counter omits the row,
+    so a sample's noise does not depend on where it sits in a batch.
+    """
     n4 = (n + 3) // 4
     i4 = torch.arange(n4, dtype=torch.int64).unsqueeze(0).expand(rows, n4)
-    b = torch.arange(rows, dtype=torch.int64).unsqueeze(1).expand(rows, n4)
     off = torch.full_like(i4, offset & _MASK)
     zero = torch.zeros_like(i4)
-    x0, x1, x2, x3 = philox4x32([i4, b, off, zero], (seed & _MASK, (seed >> 32) & _MASK))
+    if row_seeds is None:
+        b = torch.arange(rows, dtype=torch.int64).unsqueeze(1).expand(rows, n4)
+        key = (seed & _MASK, (seed >> 32) & _MASK)
+    else:
+        rs = row_seeds.detach().cpu().to(torch.int64).reshape(rows, 1)
+        b = zero
+        key = ((rs & _MASK).expand(rows, n4), ((rs >> 32) & _MASK).expand(rows, n4))
+    x0, x1, x2, x3 = philox4x32([i4, b, off, zero], key)
     inv = 2.0 ** -32
 
     def bm(a, c):
@@ -64,6 +76,16 @@ def philox_normal(seed: int, rows: int, n: int, offset: int = 0) -> torch.Tensor
     z2, z3 = bm(x2, x3)
     out = torch.stack([z0, z1, z2, z3], dim=-1).reshape(rows, n4 * 4)
     return out[:, :n].contiguous()
+
+
+def normal_rows(row_seeds: torch.Tensor, shape: tuple, offset: int, device) -> torch.Tensor:
+    """[B, *shape] standard normals, row b keyed by ``row_seeds[b]`` (same stream on CPU and GPU)."""
+    B, n = int(row_seeds.numel()), int(math.prod(shape))
+    if torch.device(device).type == "cuda":
+        z = ext().normal_fill(row_seeds.to(device=device, dtype=torch.int64).contiguous(), n, int(offset))
+    else:
+        z = philox_normal(0, B, n, offset, row_seeds=row_seeds)
+    return z.reshape((B,) + tuple(shape))
 
 
 def _bcast(v: torch.Tensor, ref: torch.Tensor) -> torch.Tensor:
@@ -113,39 +135,43 @@ def sde_step(sample: torch.Tensor, model_output: torch.Tensor, sigma: torch.Tens
              sigma_max: float, noise_level: float, sde_type: str = "sde", prev_sample: Optional[torch.Tensor] = None,
              noise: Optional[torch.Tensor] = None, generator: Optional[torch.Generator] = None,
              seed: Optional[int] = None, noise_offset: int = 0, return_logprobs: bool = True,
-             include_logprob_normalizer: bool = True):
+             include_logprob_normalizer: bool = True, row_seeds: Optional[torch.Tensor] = None):
     """Returns ``(prev_sample, log_prob[B] or None, prev_sample_mean, std_dev_t[B])``.
+
+    In-kernel noise is keyed by ``seed`` (whole call) or by ``row_seeds`` (int64 [B], one per sample).
 
     Differentiable w.r.t. ``model_output`` (the training path backpropagates the log-prob and
     the mean through it); ``sample``/``prev_sample`` are trajectory data and get no gradient.
     """
     b = sample.shape[0]
-    need_noise = prev_sample is None and noise is None and seed is None
+    need_noise = prev_sample is None and noise is None and seed is None and row_seeds is None
     if need_noise:
         noise = torch.randn(sample.shape, generator=generator, device=sample.device, dtype=torch.float32)
     if not sample.is_cuda:
         if prev_sample is None and noise is None:
-            noise = philox_normal(seed, b, sample[0].numel(), noise_offset).reshape(sample.shape)
+            noise = philox_normal(int(seed or 0), b, sample[0].numel(), noise_offset,
+                                  row_seeds=row_seeds).reshape(sample.shape)
         return sde_step_reference(sample, model_output, sigma, sigma_prev, sigma_max=sigma_max,
                                   noise_level=noise_level, sde_type=sde_type, prev_sample=prev_sample, noise=noise,
                                   return_logprobs=return_logprobs,
                                   include_logprob_normalizer=include_logprob_normalizer)
+    rs = row_seeds.to(device=sample.device, dtype=torch.int64).contiguous() if row_seeds is not None else None
     return _SDEStepFn.apply(sample, model_output, sigma, sigma_prev, prev_sample, noise, float(sigma_max),
                             float(noise_level), SDE_TYPES[sde_type], int(seed or 0), int(noise_offset),
-                            bool(return_logprobs), bool(include_logprob_normalizer))
+                            bool(return_logprobs), bool(include_logprob_normalizer), rs)
 
 
 class _SDEStepFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, sample, model_output, sigma, sigma_prev, prev_sample, noise, sigma_max, noise_level, sde_type,
-                seed, noise_offset, return_logprobs, include_norm):
+                seed, noise_offset, return_logprobs, include_norm, row_seeds):
         s = sample.contiguous()
         m = model_output.contiguous()
         prev, logp, mean, std = ext().sde_step_fwd(
             s, m, sigma.contiguous().float(), sigma_prev.contiguous().float(),
             prev_sample.contiguous() if prev_sample is not None else None,
             noise.contiguous() if noise is not None else None,
-            sigma_max, noise_level, sde_type, seed, noise_offset, return_logprobs, include_norm)
+            sigma_max, noise_level, sde_type, seed, noise_offset, return_logprobs, include_norm, row_seeds)
         ctx.save_for_backward(s, prev, mean, sigma, sigma_prev)
         ctx.cfg = (sigma_max, noise_level, sde_type, include_norm)
         return prev, (logp if return_logprobs else None), mean, std
@@ -160,4 +186,4 @@ class _SDEStepFn(torch.autograd.Function):
             g_mean = torch.zeros_like(s)
         grad_mo = ext().sde_step_bwd(s, prev, mean, sigma.float(), sigma_prev.float(), g_logp.float().contiguous(),
                                      g_mean.float().contiguous(), sigma_max, noise_level, sde_type)
-        return (None, grad_mo, None, None, None, None, None, None, None, None, None, None, None)
+        return (None, grad_mo, None, None, None, None, None, None, None, None, None, None, None, None)

@@ -129,12 +129,14 @@ class FlowMatchSDEDiscreteScheduler:
                              sde_type: str = "sde", return_logprobs: bool = True, return_sqrt_dt: bool = False,
                              include_logprob_normalizer: bool = True, generator: Optional[torch.Generator] = None,
                              seed: Optional[int] = None, noise: Optional[torch.Tensor] = None,
+                             row_seeds: Optional[torch.Tensor] = None,
                              noise_offset: int = 0) -> SchedulerStepOutput:
         """One reverse step.  ``step_index`` (int or per-sample tensor) or ``timestep`` selects sigma.
 
         ``noise`` supplies the Gaussian draw explicitly; otherwise the CUDA kernel draws it from a
         counter-based Philox stream keyed by ``seed`` (one stream per sample row, offset by
-        ``noise_offset``) and the CPU path uses ``generator``.
+        ``noise_offset``) or, with ``row_seeds``, by each sample's own seed; the CPU path draws the
+        same stream when a seed is given and uses ``generator`` otherwise.
         """
         if sde_type not in ("sde", "cps", "dance_sde"):
             raise ValueError(sde_type)
@@ -162,7 +164,7 @@ class FlowMatchSDEDiscreteScheduler:
         sigma_max = float(self.sigmas[1])
         res = sde_ops.sde_step(sample, model_output, sigma.float(), sigma_prev.float(), sigma_max=sigma_max,
                                noise_level=float(noise_level), sde_type=sde_type, prev_sample=prev_sample,
-                               noise=noise, generator=generator, seed=seed, noise_offset=noise_offset,
+                               noise=noise, generator=generator, seed=seed, noise_offset=noise_offset, row_seeds=row_seeds,
                                return_logprobs=return_logprobs,
                                include_logprob_normalizer=include_logprob_normalizer)
         prev, logp, mean, std = res

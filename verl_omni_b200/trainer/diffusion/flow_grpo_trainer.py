@@ -113,6 +113,18 @@ class PolicyGradientTrainer:
         self.reward_fn = VisualRewardManager(scorer, name="score")
         self.rollout = DiTRolloutEngine(module, self.adapter, self.rollout_cfg, self.model_cfg, device=self.device,
                                         latent_shape=self.spec.latent_shape, decoder=decoder)
+        # optional agent-loop path: per-sample coroutines over a request-packing rollout server
+        agent_cfg = config.actor_rollout_ref.rollout.get("agent", {}) or {}
+        self.agent_manager = None
+        if bool(agent_cfg.get("enable", False)):
+            from verl_omni_b200.workers.agent_loop import DiffusionAgentLoopManager
+            from verl_omni_b200.workers.rollout.server import DiffusionRolloutServer
+
+            self.rollout_server = DiffusionRolloutServer(self.rollout)
+            self.agent_manager = DiffusionAgentLoopManager(
+                self.rollout_server, config.actor_rollout_ref.rollout, self.reward_fn,
+                cond_keys=tuple(self.adapter.cond_keys()), num_workers=int(agent_cfg.get("num_workers", 8)),
+                default_agent_loop=str(agent_cfg.get("default_agent_loop", "diffusion_single_turn_agent")))
         # ---------------------------------------------------------------- data
         n_prompts = int(config.data.get("synthetic", {}).get("num_prompts", 1024))
         self.dataset = SyntheticPromptDataset(n_prompts, seed=int(config.data.get("seed", 0) or 0),
@@ -163,6 +175,14 @@ class PolicyGradientTrainer:
         gen = cond.repeat(self.n, interleave=True)
         base_seed = int(self.rollout_cfg.seed if self.rollout_cfg.seed is not None else 12345)
         seed = (base_seed + step - 1) * 9973 + self.rank * 7 + (zlib.crc32(pre.encode()) & 0xFFFF) * 131
+        if self.agent_manager is not None and rollout is self.rollout:
+            # per-row seeds from the step seed and each row's global index (prompt id x n + sample)
+            gen.meta_info.update({"global_steps": step, "rollout_seed": seed})
+            gen.non_tensor_batch["_rollout_seed_global_idx"] = np.array(
+                [int(i) * self.n + j for i in ids for j in range(self.n)], dtype=np.int64)
+            out = self.agent_manager.generate_sequences(gen)
+            scores = out.batch.pop("rm_scores")[:, 0]
+            return out, scores.to(self.device), {"reward/score_mean": float(scores.mean())}
         out = rollout.generate(gen, seed=seed, global_step=step)
         out.non_tensor_batch.update({k: v[: len(out)] for k, v in gen.non_tensor_batch.items()})
         scores, rmetrics = self.reward_fn(out)

@@ -36,6 +36,7 @@ from verl_omni_b200.parallel import dist as D
 from verl_omni_b200.ops._ext import ext
 
 _ALIGN = 128
+_PARAM_ALIGN = 16  # elements
 
 
 def _dtype(name: str) -> torch.dtype:
@@ -62,7 +63,9 @@ class FlatParams:
         off = 0
         for n in self.numels:
             self.offsets.append(off)
-            off += n
+            # every parameter (and its main_grad slice) starts on a 64-byte boundary: TMA epilogues
+            # and vector reductions address them directly
+            off += (n + _PARAM_ALIGN - 1) // _PARAM_ALIGN * _PARAM_ALIGN
         self.numel = off
         unit = world * _ALIGN
         self.padded = max(unit, (off + unit - 1) // unit * unit)

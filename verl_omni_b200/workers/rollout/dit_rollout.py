@@ -25,8 +25,13 @@ from typing import Callable, Optional
 import numpy as np
 import torch
 
+from verl_omni_b200.ops.sde import normal_rows
 from verl_omni_b200.pipelines.model_base import DiffusionModelBase
 from verl_omni_b200.utils.dataproto import DataProto
+
+
+# Philox counter offset of the initial latent noise (SDE step t uses offset t)
+_INIT_NOISE_OFFSET = 0x7FFFFFFF
 
 
 def select_sde_window(algo_cfg, T: int, global_step: int, seed: int = 0) -> tuple[int, int]:
@@ -104,16 +109,26 @@ class DiTRolloutEngine:
     # ------------------------------------------------------------------ generate
     @torch.no_grad()
     def generate(self, batch: DataProto, *, seed: int = 0, global_step: int = 0, record_logprobs: bool = True,
-                 decode: bool = True) -> DataProto:
-        """``batch`` holds the conditioning tensors (adapter ``cond_keys``, optional ``negative_*``)."""
+                 decode: bool = True, row_seeds: Optional[torch.Tensor] = None,
+                 window: Optional[tuple[int, int]] = None, noise_level: Optional[float] = None,
+                 sde_type: Optional[str] = None, guidance_scale: Optional[float] = None) -> DataProto:
+        """``batch`` holds the conditioning tensors (adapter ``cond_keys``, optional ``negative_*``).
+
+        ``row_seeds`` (int64 [B]) keys each sample's initial noise and SDE noise by its own seed, so
+        a sample's trajectory does not depend on how requests were packed into device batches.
+        ``window`` / ``noise_level`` / ``sde_type`` / ``guidance_scale`` override the configured
+        values for this call (validation sampling, request-level parameters).
+        """
         if self.sleeping:
             self.wake_up()
         self._abort.clear()
         cfg, algo = self.cfg, self.cfg.algo
         T = cfg.pipeline.num_inference_steps
-        w0, W = select_sde_window(algo, T, global_step, seed)
+        w0, W = window if window is not None else select_sde_window(algo, T, global_step, seed)
         B = len(batch)
-        guidance = cfg.pipeline.guidance_scale
+        guidance = cfg.pipeline.guidance_scale if guidance_scale is None else guidance_scale
+        nl = algo.noise_level if noise_level is None else float(noise_level)
+        st = algo.sde_type if sde_type is None else sde_type
         cfg_mult = 2 if (guidance is not None and guidance > 1.0) else 1
         mbs = max(1, min(B, cfg.max_num_seqs // cfg_mult))
         sched = self.scheduler
@@ -123,7 +138,8 @@ class DiTRolloutEngine:
             if self._abort.is_set():
                 break
             mb = batch.select_idxs(slice(s, min(B, s + mbs)))
-            chunks.append(self._run_chunk(mb, T, w0, W, seed * 1_000_003 + s, guidance, record_logprobs))
+            rs = row_seeds[s:min(B, s + mbs)] if row_seeds is not None else None
+            chunks.append(self._run_chunk(mb, T, w0, W, seed * 1_000_003 + s, guidance, record_logprobs, rs, nl, st))
         done = sum(len(c) for c in chunks)
         out = DataProto.concat(chunks) if chunks else DataProto()
         if done < B:  # aborted: synthesize aborted outputs for the unfinished requests
@@ -141,15 +157,19 @@ class DiTRolloutEngine:
         imgs = [self.decoder(latents[i:i + chunk]) for i in range(0, latents.shape[0], chunk)]
         return torch.cat(imgs, 0)
 
-    def _run_chunk(self, mb: DataProto, T: int, w0: int, W: int, seed: int, guidance, record: bool) -> DataProto:
-        algo = self.cfg.algo
+    def _run_chunk(self, mb: DataProto, T: int, w0: int, W: int, seed: int, guidance, record: bool,
+                   row_seeds: Optional[torch.Tensor], noise_level: float, sde_type: str) -> DataProto:
         keys = self.adapter.cond_keys()
         cond = {k: mb.batch[k].to(self.device) for k in keys}
         neg = None
         if guidance is not None and guidance > 1.0 and ("negative_" + keys[0]) in mb.batch:
             neg = {k: mb.batch["negative_" + k].to(self.device) for k in keys}
         b = len(mb)
-        x = self._initial_noise(b, seed)
+        if row_seeds is not None:
+            row_seeds = row_seeds.to(device=self.device, dtype=torch.int64)
+            x = normal_rows(row_seeds, self.latent_shape, _INIT_NOISE_OFFSET, self.device)
+        else:
+            x = self._initial_noise(b, seed)
         sched = self.scheduler
         traj = [x] if w0 == 0 else []
         logps, steps = [], []
@@ -157,10 +177,11 @@ class DiTRolloutEngine:
             tt = sched.timesteps[t].expand(b).to(self.device)
             v = self.adapter.predict(self.module, x, tt, cond, neg, guidance)
             in_window = w0 <= t < w0 + W
-            nl = algo.noise_level if in_window else 0.0
+            nl = noise_level if in_window else 0.0
             out = sched.sample_previous_step(x.float(), v.float(), step_index=t, noise_level=nl,
-                                             sde_type=algo.sde_type if in_window else "sde",
-                                             seed=seed, noise_offset=t, return_logprobs=in_window and record)
+                                             sde_type=sde_type if in_window else "sde",
+                                             seed=seed, noise_offset=t, return_logprobs=in_window and record,
+                                             row_seeds=row_seeds)
             if not in_window:
                 x = out.prev_sample_mean
             else:
