@@ -185,3 +185,16 @@ def test_rollout_correction_modes():
     assert torch.equal(b2.batch["old_log_probs"], roll)
     mm = compute_rollout_corr_metrics_from_logprobs(old, roll, timesteps=torch.arange(3).expand(6, 3))
     assert "rollout_corr/logprob_abs_diff/ts_0" in mm
+
+
+def test_true_cfg_renorm_matches_per_token_norm_form():
+    """Channel-axis renorm on [B, C, H, W] equals the reference's last-axis form on packed [B, L, C]."""
+    from verl_omni_b200.ops.cfg import cfg_combine
+
+    torch.manual_seed(0)
+    pos, neg = torch.randn(2, 8, 4, 5), torch.randn(2, 8, 4, 5)
+    out = cfg_combine(pos, neg, 3.0, renorm=True)
+    p, n = pos.flatten(2).transpose(1, 2), neg.flatten(2).transpose(1, 2)  # [B, L, C]
+    comb = n + 3.0 * (p - n)
+    ref = comb * (torch.norm(p, dim=-1, keepdim=True) / torch.norm(comb, dim=-1, keepdim=True))
+    torch.testing.assert_close(out.flatten(2).transpose(1, 2), ref)

@@ -82,8 +82,9 @@ def test_attention_op_autograd():
         torch.testing.assert_close(a.grad.float(), b.grad, rtol=5e-2, atol=5e-2)
 
 
+@pytest.mark.parametrize("version", [1, 2])
 @pytest.mark.parametrize("B,H,Sq,Skv,D,causal", CASES)
-def test_fmha_bwd(E, B, H, Sq, Skv, D, causal):
+def test_fmha_bwd(E, B, H, Sq, Skv, D, causal, version):
     torch.manual_seed(2)
     q = torch.randn(B, H, Sq, D, device="cuda").bfloat16()
     k = torch.randn(B, H, Skv, D, device="cuda").bfloat16()
@@ -91,7 +92,7 @@ def test_fmha_bwd(E, B, H, Sq, Skv, D, causal):
     scale = 1 / math.sqrt(D)
     o, lse = E.fmha_fwd(q, k, v, causal, scale)
     do = torch.randn(B, Sq, H, D, device="cuda").bfloat16()
-    dq, dk, dv = E.fmha_bwd(q, k, v, o, lse, do, causal, scale)
+    dq, dk, dv = E.fmha_bwd(q, k, v, o, lse, do, causal, scale, version)
     qr, kr, vr = (t.detach().float().requires_grad_(True) for t in (q, k, v))
     ro, _ = _ref(qr, kr, vr, causal, scale)
     ro.backward(do.float().transpose(1, 2))

@@ -206,3 +206,40 @@ def test_trainer_step_gpu_sd35_tiny():
     for m in (m1, m2):
         assert math.isfinite(m["actor/grad_norm"]) and math.isfinite(m["actor/pg_loss"])
     assert abs(m1["actor/ppo_kl"]) < 1e-4
+
+
+def test_row_seeded_noise_matches_cpu_stream():
+    """Per-row Philox keys: GPU initial noise and SDE noise equal the CPU oracle and ignore row order."""
+    from verl_omni_b200.ops.sde import normal_rows, philox_normal, sde_step, sde_step_reference
+
+    seeds = torch.tensor([5, -7, 123456789012345, 5], dtype=torch.int64)
+    z_gpu = normal_rows(seeds, (4, 8, 8), 0x7FFFFFFF, "cuda").cpu()
+    z_cpu = normal_rows(seeds, (4, 8, 8), 0x7FFFFFFF, "cpu")
+    torch.testing.assert_close(z_gpu, z_cpu, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(z_gpu[0], z_gpu[3])  # same seed, same noise
+    B = 4
+    x = torch.randn(B, 4, 8, 8, device="cuda")
+    v = torch.randn_like(x)
+    sig = torch.full((B,), 0.6, device="cuda")
+    sigp = torch.full((B,), 0.5, device="cuda")
+    prev, lp, mean, std = sde_step(x, v, sig, sigp, sigma_max=0.95, noise_level=0.7, seed=0, noise_offset=3,
+                                   row_seeds=seeds)
+    z = philox_normal(0, B, 4 * 8 * 8, 3, row_seeds=seeds).reshape(x.shape).cuda()
+    ref_prev, _, _, _ = sde_step_reference(x, v, sig, sigp, sigma_max=0.95, noise_level=0.7, sde_type="sde", noise=z)
+    torch.testing.assert_close(prev, ref_prev, rtol=1e-4, atol=1e-4)
+    perm = torch.tensor([2, 0, 3, 1])
+    prev_p, _, _, _ = sde_step(x[perm], v[perm], sig, sigp, sigma_max=0.95, noise_level=0.7, seed=0, noise_offset=3,
+                               row_seeds=seeds[perm])
+    torch.testing.assert_close(prev_p, prev[perm])
+
+
+@pytest.mark.parametrize("renorm", [False, True])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_cfg_combine_matches_reference(renorm, dtype):
+    from verl_omni_b200.ops.cfg import cfg_combine, cfg_combine_reference
+
+    pos = torch.randn(3, 16, 12, 10, device="cuda").to(dtype)
+    neg = torch.randn_like(pos)
+    with torch.no_grad():
+        out = cfg_combine(pos, neg, 4.5, renorm)
+    torch.testing.assert_close(out, cfg_combine_reference(pos, neg, 4.5, renorm), rtol=1e-5, atol=1e-5)

@@ -49,6 +49,7 @@ int64_t fmha_error(bool reset);
 std::vector<torch::Tensor> linear_bwd_prep(torch::Tensor dy, c10::optional<torch::Tensor> saved,
                                            c10::optional<torch::Tensor> gate, int64_t S, int64_t mode,
                                            c10::optional<torch::Tensor> db, bool db_accumulate);
+torch::Tensor cfg_combine(torch::Tensor pos, torch::Tensor neg, double g, bool renorm);
 int64_t symm_malloc(int64_t nbytes);
 void symm_free(int64_t ptr);
 torch::Tensor ipc_get_handle(int64_t ptr);
@@ -60,7 +61,7 @@ void peer_adamw_bcast(std::vector<int64_t> flat_ptrs, int64_t lo, int64_t n, tor
                       torch::Tensor m, torch::Tensor v, double lr, double b1, double b2, double eps, double wd,
                       int64_t step, double max_norm, torch::Tensor sq_norm);
 std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
-                                    torch::Tensor lse, torch::Tensor dO, bool causal, double scale);
+                                    torch::Tensor lse, torch::Tensor dO, bool causal, double scale, int64_t version);
 }  // namespace vo
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -87,8 +88,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fmha_fwd", &vo::fmha_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("causal"), py::arg("scale"),
         py::arg("version") = 2);
   m.def("fmha_error", &vo::fmha_error);
-  m.def("fmha_bwd", &vo::fmha_bwd);
+  m.def("fmha_bwd", &vo::fmha_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
+        py::arg("dO"), py::arg("causal"), py::arg("scale"), py::arg("version") = 1);
   m.def("linear_bwd_prep", &vo::linear_bwd_prep);
+  m.def("cfg_combine", &vo::cfg_combine);
   m.def("symm_malloc", &vo::symm_malloc);
   m.def("symm_free", &vo::symm_free);
   m.def("ipc_get_handle", &vo::ipc_get_handle);

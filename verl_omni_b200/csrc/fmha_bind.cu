@@ -9,7 +9,7 @@ extern "C" int vo_fmha_fwd2(const void* q, const void* k, const void* v, void* o
 extern "C" int vo_fmha_fwd2_error(int reset);
 extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const void* o, const void* dO,
                            const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_acc, int B, int H,
-                           int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream);
+                           int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream, int version);
 extern "C" int vo_fmha_bwd_error(int reset);
 
 namespace vo {
@@ -41,8 +41,10 @@ int64_t fmha_error(bool reset) {
 }
 
 // returns dq, dk, dv in the [B, H, S, D] layout of q, k, v
+// version 1: one key tile per CTA, serial per query tile; version 2: pipelined (P^T / dS^T in
+// tensor memory, concurrent dQ drain, next S^T overlapped for head_dim 64)
 std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
-                                    torch::Tensor lse, torch::Tensor dO, bool causal, double scale) {
+                                    torch::Tensor lse, torch::Tensor dO, bool causal, double scale, int64_t version) {
   VO_CHECK_INPUT(q);
   VO_CHECK_INPUT(k);
   VO_CHECK_INPUT(v);
@@ -60,7 +62,7 @@ std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Ten
   auto dq_acc = torch::zeros({B, H, Sq, D}, fo);
   int rc = vo_fmha_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dO.data_ptr(), lse.data_ptr<float>(),
                        dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), delta.data_ptr<float>(), dq_acc.data_ptr<float>(),
-                       B, H, Sq, Skv, D, (float)scale, causal ? 1 : 0, stream());
+                       B, H, Sq, Skv, D, (float)scale, causal ? 1 : 0, stream(), (int)version);
   TORCH_CHECK(rc == 0, "tcgen05 FMHA backward launch failed: code ", rc);
   count_launch(3);
   return {dq, dk, dv};

@@ -392,6 +392,345 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ------------------------------------------------------------------------------------ version 2
+// Same math, pipelined.  384 threads:
+//   warp 0       TMA: K, V once; Q_i and dO_i per query tile (2-stage ring);
+//   warp 1       MMA issuer;
+//   warps 4..7   gradient warpgroup (one key row per thread): P^T = exp2(S^T*scale_log2 - lse) and
+//                dS^T = P^T * (dP^T - Delta) computed chunk by chunk; P^T and dS^T go back into
+//                tensor memory in place (bf16 pairs over the first 64 columns of their fp32 tiles)
+//                where the dV / dK MMAs read them as A operands, and dS^T also into swizzled SMEM
+//                for the dQ MMA (A = dS, MN-major);
+//   warps 8..11  dQ drain: dQ_i tile (one query row per thread) from tensor memory into the fp32
+//                dQ accumulator with vector reductions, concurrently with the next tile's math.
+// Tensor memory (512 columns): S^T buffers (two for head_dim 64, one for 128), dP^T, dV, dK; dQ_i
+// is written into the S^T buffer of tile i after the dV MMA has consumed P^T_i (the tensor pipe
+// executes one thread's MMAs in order).  For head_dim 64 the next tile's S^T MMA runs while the
+// gradient warpgroup works on the current tile.
+namespace v2 {
+__device__ __forceinline__ void ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int D>
+struct Lay2 {
+  static constexpr int ST = 2;  // Q / dO stages
+  static constexpr int TILE = 128 * D * 2;
+  static constexpr int K_OFF = 0;
+  static constexpr int V_OFF = TILE;
+  static constexpr int Q_OFF = 2 * TILE;
+  static constexpr int DO_OFF = Q_OFF + ST * TILE;
+  static constexpr int DS_OFF = DO_OFF + ST * TILE;  // dS^T [128 keys x 128 queries] bf16, 2 x 16 KB
+  static constexpr int LSE_OFF = DS_OFF + 32768;     // [2 warpgroups][2 parities][64] float2 (lse*log2e, delta)
+  static constexpr int BAR_OFF = LSE_OFF + 2048;
+  static constexpr int BYTES = BAR_OFF + 256;
+  // tensor memory: S^T [0,128), dP^T [128,256), dV, dK, then (head_dim 64) two dQ buffers
+  static constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 256 + D;
+  static constexpr bool DQ_OWN = D == 64;  // head_dim 128: dQ reuses the S^T columns after the dV MMA
+  __device__ static constexpr uint32_t dq_col(int i) { return DQ_OWN ? 384u + (uint32_t)(i & 1) * 64u : C_S; }
+  // warpgroup w writes its 64 query columns as 32 packed columns at [64 w, 64 w + 32) of S^T / dP^T
+  __device__ static constexpr uint32_t packed_col(int kk) { return kk < 4 ? kk * 8 : 64 + (kk - 4) * 8; }
+};
+
+template <int D>
+__global__ void __launch_bounds__(512, 1)
+    fmha_bwd2_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+                     const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo, Params p) {
+  using L = Lay2<D>;
+  constexpr int ST = L::ST;
+  extern __shared__ __align__(1024) uint8_t raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR_OFF);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qdo_full = bars + 1;   // [2]
+  uint64_t* qdo_empty = bars + 3;  // [2]
+  uint64_t* sp_full = bars + 5;
+  uint64_t* ds_full = bars + 6;
+  uint64_t* dq_full = bars + 7;
+  uint64_t* dq_free = bars + 8;  // [2]: one per dQ buffer (a single barrier could run two phases ahead)
+  uint64_t* kv_done = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x % p.nkv_tiles;
+  const int bh = blockIdx.x / p.nkv_tiles;
+  const int b = bh / p.H, h = bh % p.H;
+  const int kv0 = kt * 128;
+  const int i0 = p.causal ? kv0 / 128 : 0;
+  const int nq = (p.Sq + 127) / 128;
+  const int ntile = nq - i0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qdo_full[i], 1);
+      mbar_init(&qdo_empty[i], 1);
+    }
+    mbar_init(sp_full, 1);
+    mbar_init(ds_full, 8);
+    mbar_init(dq_full, 1);
+    mbar_init(&dq_free[0], 4);
+    mbar_init(&dq_free[1], 4);
+    mbar_init(kv_done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0 && ntile > 0) {
+      mbar_expect_tx(kv_full, 2 * L::TILE);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        tma3(sm + L::K_OFF + c * 16384, &mk, kv_full, c * 64, kv0, bh);
+        tma3(sm + L::V_OFF + c * 16384, &mv, kv_full, c * 64, kv0, bh);
+      }
+      for (int it = 0; it < ntile; ++it) {
+        const int i = i0 + it, st = it % ST;
+        if (!mbar_wait(&qdo_empty[st], ((it / ST) & 1) ^ 1, abort_flag, 61)) break;
+        mbar_expect_tx(&qdo_full[st], 2 * L::TILE);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          tma3(sm + L::Q_OFF + st * L::TILE + c * 16384, &mq, &qdo_full[st], c * 64, i * 128, bh);
+          tma4(sm + L::DO_OFF + st * L::TILE + c * 16384, &mdo, &qdo_full[st], c * 64, h, i * 128, b);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && ntile > 0) {
+      const uint32_t id_kk = idesc(128, 128, 0, 0);  // S^T = K Q^T, dP^T = V dO^T
+      const uint32_t id_kn = idesc(128, D, 0, 1);    // dV = P^T dO, dK = dS^T Q (A from tensor memory)
+      const uint32_t id_nn = idesc(128, D, 1, 1);    // dQ = dS K (A = dS^T in SMEM read MN-major)
+      const uint32_t ka = smem_u32(sm + L::K_OFF), va = smem_u32(sm + L::V_OFF);
+      const uint32_t da = smem_u32(sm + L::DS_OFF);
+      auto issue_sdp = [&](int it) {  // S^T_it and dP^T_it
+        const uint32_t qa = smem_u32(sm + L::Q_OFF + (it % ST) * L::TILE);
+        const uint32_t oa = smem_u32(sm + L::DO_OFF + (it % ST) * L::TILE);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          mma(tmem + L::C_S, desc(ka + off, 16, 1024), desc(qa + off, 16, 1024), id_kk, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          mma(tmem + L::C_DP, desc(va + off, 16, 1024), desc(oa + off, 16, 1024), id_kk, kk > 0);
+        }
+        commit(sp_full);
+      };
+      bool ok = mbar_wait(kv_full, 0, abort_flag, 62) && mbar_wait(&qdo_full[0], 0, abort_flag, 63);
+      if (ok) {
+        fence_after();
+        issue_sdp(0);
+      }
+      for (int it = 0; ok && it < ntile; ++it) {
+        const int st = it % ST;
+        if (!mbar_wait(ds_full, it & 1, abort_flag, 66)) break;
+        fence_after();
+        const uint32_t qa = smem_u32(sm + L::Q_OFF + st * L::TILE);
+        const uint32_t oa = smem_u32(sm + L::DO_OFF + st * L::TILE);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // dV += P^T dO over 128 queries (8 packed columns per K=16 step)
+          mma_ts(tmem + L::C_DV, tmem + L::C_S + L::packed_col(kk), desc(oa + kk * 2048, 16384, 1024), id_kn,
+                 (it > 0 || kk > 0));
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // dK += dS^T Q
+          mma_ts(tmem + L::C_DK, tmem + L::C_DP + L::packed_col(kk), desc(qa + kk * 2048, 16384, 1024), id_kn,
+                 (it > 0 || kk > 0));
+        // buffer it%2 was last used by tile it-2: wait for its drain (phase (it-2)/2 of that buffer's barrier)
+        if (L::DQ_OWN && it >= 2 && !mbar_wait(&dq_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, 64)) break;
+        fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // dQ_it = dS K over 128 keys
+          mma(tmem + L::dq_col(it), desc(da + kk * 2048, 16384, 1024), desc(ka + kk * 2048, 16384, 1024), id_nn,
+              kk > 0);
+        commit(dq_full);
+        commit(&qdo_empty[st]);
+        if (it + 1 < ntile) {
+          if (!mbar_wait(&qdo_full[(it + 1) % ST], ((it + 1) / ST) & 1, abort_flag, 67)) break;
+          if (!L::DQ_OWN && !mbar_wait(&dq_free[0], it & 1, abort_flag, 68)) break;  // dQ_it drained from S^T
+          fence_after();
+          issue_sdp(it + 1);
+        } else {
+          commit(kv_done);
+        }
+      }
+    }
+  } else if (warp >= 4 && warp < 12) {
+    // ---------------------------------------------------------------- gradient warpgroups
+    // warpgroup g (0, 1) owns query columns [64 g, 64 g + 64) of every tile, one key row per thread
+    const int g = (warp - 4) >> 2;
+    const int tid = threadIdx.x - 128 - 128 * g;  // 0..127 within the warpgroup
+    const int lane_base = 32 * (warp & 3);
+    const int r = lane_base + lane;
+    const int kv = kv0 + r;
+    const uint32_t lane_off = (uint32_t)lane_base << 16;
+    uint8_t* ds = sm + L::DS_OFF;
+    float2* ld_base = reinterpret_cast<float2*>(sm + L::LSE_OFF) + g * 128;  // [2 parities][64]
+    // lse / delta of one query column per thread (threads 0..63: lse, 64..127: delta), one tile ahead
+    auto fetch = [&](int it) -> float {
+      const int q = (i0 + it) * 128 + 64 * g + (tid & 63);
+      if (it >= ntile || q >= p.Sq) return tid < 64 ? INFINITY : 0.f;
+      return tid < 64 ? p.lse[(int64_t)bh * p.Sq + q] * 1.4426950408889634f : p.delta[(int64_t)bh * p.Sq + q];
+    };
+    float pre = fetch(0);
+    bool ok = ntile > 0;
+    for (int it = 0; ok && it < ntile; ++it) {
+      float2* lds = ld_base + (it & 1) * 64;
+      if (tid < 64)
+        lds[tid].x = pre;
+      else
+        lds[tid - 64].y = pre;
+      named_bar(1 + g, 128);  // this tile's lse/delta visible (the other parity buffer is still being read)
+      pre = fetch(it + 1);    // next tile's values load under this tile's math
+      const int q0 = (i0 + it) * 128 + 64 * g;
+      if (!mbar_wait(sp_full, it & 1, abort_flag, 69)) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      // visible query columns of this key row within the warpgroup's 64: [qlo, qhi)
+      int qhi = kv < p.Skv ? min(64, p.Sq - q0) : 0;
+      int qlo = p.causal ? max(0, kv - q0) : 0;
+      qhi = max(qhi, 0);
+      if (qlo > qhi) qlo = qhi;
+      const uint32_t S_t = tmem + L::C_S + lane_off + 64 * g;
+      const uint32_t DP_t = tmem + L::C_DP + lane_off + 64 * g;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t sa[32], pa[32];
+        ld32_nowait(S_t + c * 32, sa);
+        ld32_nowait(DP_t + c * 32, pa);
+        wait_ld();
+        uint32_t wp[16], wd[16];
+        float dsv[32];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          const int qc = c * 32 + j;
+          const float4 l2 = *reinterpret_cast<const float4*>(&lds[qc]);  // (lse0, delta0, lse1, delta1)
+          float e0 = ex2(fmaf(__uint_as_float(sa[j]), p.scale_log2, -l2.x));
+          float e1 = ex2(fmaf(__uint_as_float(sa[j + 1]), p.scale_log2, -l2.z));
+          if (qc < qlo || qc >= qhi) e0 = 0.f;
+          if (qc + 1 < qlo || qc + 1 >= qhi) e1 = 0.f;
+          const float d0 = e0 * (__uint_as_float(pa[j]) - l2.y);
+          const float d1 = e1 * (__uint_as_float(pa[j + 1]) - l2.w);
+          wp[j >> 1] = pack_bf16(e0, e1);
+          wd[j >> 1] = pack_bf16(d0, d1);
+          dsv[j] = d0;
+          dsv[j + 1] = d1;
+        }
+        st16(S_t + c * 16, wp);
+        st16(DP_t + c * 16, wd);
+        store_row_chunk(ds, r, 2 * g + c, dsv);
+      }
+      wait_st();
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ds_full);
+    }
+    if (g == 0 && ok && ntile > 0 && mbar_wait(kv_done, 0, abort_flag, 71)) {
+      fence_after();
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float vv[32], kk[32];
+        ld32(tmem + L::C_DV + lane_off + c * 32, vv);
+        ld32(tmem + L::C_DK + lane_off + c * 32, kk);
+        if (kv < p.Skv) {
+          __nv_bfloat16* dvp = p.dv + ((int64_t)bh * p.Skv + kv) * D + c * 32;
+          __nv_bfloat16* dkp = p.dk + ((int64_t)bh * p.Skv + kv) * D + c * 32;
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            uint4 a, bq;
+            a.x = pack_bf16(vv[j], vv[j + 1]);
+            a.y = pack_bf16(vv[j + 2], vv[j + 3]);
+            a.z = pack_bf16(vv[j + 4], vv[j + 5]);
+            a.w = pack_bf16(vv[j + 6], vv[j + 7]);
+            bq.x = pack_bf16(kk[j] * p.scale, kk[j + 1] * p.scale);
+            bq.y = pack_bf16(kk[j + 2] * p.scale, kk[j + 3] * p.scale);
+            bq.z = pack_bf16(kk[j + 4] * p.scale, kk[j + 5] * p.scale);
+            bq.w = pack_bf16(kk[j + 6] * p.scale, kk[j + 7] * p.scale);
+            *reinterpret_cast<uint4*>(dvp + j) = a;
+            *reinterpret_cast<uint4*>(dkp + j) = bq;
+          }
+        }
+      }
+    } else if (g == 0 && ok && ntile == 0 && kv < p.Skv) {  // causal key tile past every query
+      for (int j = 0; j < D; ++j) {
+        p.dv[((int64_t)bh * p.Skv + kv) * D + j] = __float2bfloat16_rn(0.f);
+        p.dk[((int64_t)bh * p.Skv + kv) * D + j] = __float2bfloat16_rn(0.f);
+      }
+    }
+  } else if (warp >= 12) {
+    // ---------------------------------------------------------------- dQ drain
+    const int lane_base = 32 * (warp & 3);
+    const int r = lane_base + lane;
+    const uint32_t lane_off = (uint32_t)lane_base << 16;
+    for (int it = 0; it < ntile; ++it) {
+      if (!mbar_wait(dq_full, it & 1, abort_flag, 72)) break;
+      fence_after();
+      const int q = (i0 + it) * 128 + r;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float v[32];
+        ld32(tmem + L::dq_col(it) + lane_off + c * 32, v);
+        if (q < p.Sq) {
+          float* dst = p.dq_acc + ((int64_t)bh * p.Sq + q) * D + c * 32;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) red_add_v4(dst + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&dq_free[L::DQ_OWN ? (it & 1) : 0]);
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+  }
+}
+}  // namespace v2
+
 // Delta[bh, q] = sum_d dO[b, q, h, d] * O[b, q, h, d]
 template <int D>
 __global__ void delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dO,
@@ -482,13 +821,26 @@ static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMa
   return (int)cudaGetLastError();
 }
 
+template <int D>
+static int launch2(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
+                   Params p, int grid, cudaStream_t st) {
+  using L = v2::Lay2<D>;
+  static bool set = false;
+  if (!set) {
+    cudaFuncSetAttribute(v2::fmha_bwd2_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES + 1024);
+    set = true;
+  }
+  v2::fmha_bwd2_kernel<D><<<grid, 512, L::BYTES + 1024, st>>>(mq, mk, mv, mdo, p);
+  return (int)cudaGetLastError();
+}
+
 }  // namespace vo_fbwd
 
 // q [B,H,Sq,D], k/v [B,H,Skv,D], o/do [B,Sq,H,D], lse [B,H,Sq]; outputs dq [B,H,Sq,D], dk/dv [B,H,Skv,D].
 // Scratch: delta [B*H*Sq] fp32 and dq_acc [B*H*Sq*D] fp32 (dq_acc must be zero on entry).
 extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const void* o, const void* dO,
                            const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_acc, int B, int H,
-                           int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream) {
+                           int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream, int version) {
   using namespace vo_fbwd;
   if (D != 64 && D != 128) return -1;
   const int64_t rows = (int64_t)B * Sq * H;
@@ -519,7 +871,10 @@ extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const vo
   p.dk = (__nv_bfloat16*)dk;
   p.dv = (__nv_bfloat16*)dv;
   const int grid = p.nkv_tiles * B * H;
-  r = D == 64 ? launch<64>(mq, mk, mv, mdo, p, grid, stream) : launch<128>(mq, mk, mv, mdo, p, grid, stream);
+  if (version == 2)
+    r = D == 64 ? launch2<64>(mq, mk, mv, mdo, p, grid, stream) : launch2<128>(mq, mk, mv, mdo, p, grid, stream);
+  else
+    r = D == 64 ? launch<64>(mq, mk, mv, mdo, p, grid, stream) : launch<128>(mq, mk, mv, mdo, p, grid, stream);
   if (r) return r;
   const int64_t n4 = (int64_t)B * H * Sq * D / 4;
   dq_finalize_kernel<<<(unsigned)((n4 + 255) / 256 < 4096 ? (n4 + 255) / 256 : 4096), 256, 0, stream>>>(

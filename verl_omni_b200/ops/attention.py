@@ -20,6 +20,8 @@ from verl_omni_b200.ops._ext import ext
 
 # forward kernel generation: 2 = two query tiles per CTA with P/O in tensor memory, 1 = one tile per CTA
 _FWD_VERSION = int(os.environ.get("VO_FMHA_FWD", "1"))
+# backward kernel generation: 2 = pipelined (P^T/dS^T in tensor memory, concurrent dQ drain), 1 = serial
+_BWD_VERSION = int(os.environ.get("VO_FMHA_BWD", "1"))
 
 
 def _native() -> bool:
@@ -40,7 +42,8 @@ class _FMHA(torch.autograd.Function):
         causal, scale = ctx.meta
         if os.environ.get("VO_ATTN_BWD", "native") != "torch" and hasattr(ext(), "fmha_bwd"):
             B, S, H, D = o.shape
-            dq, dk, dv = ext().fmha_bwd(q, k, v, o, lse, do.contiguous().view(B, S, H, D), causal, scale)
+            dq, dk, dv = ext().fmha_bwd(q, k, v, o, lse, do.contiguous().view(B, S, H, D), causal, scale,
+                                        _BWD_VERSION)
             return dq, dk, dv, None, None
         # backward kernel not built: recompute through SDPA autograd
         B, S, H, D = o.shape

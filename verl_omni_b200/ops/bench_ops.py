@@ -114,7 +114,8 @@ def bench_fmha(a) -> list[dict]:
     cases = {"fwd": (lambda: e.fmha_fwd(q, k, v, False, scale, 1), flops_f),
              "fwd2": (lambda: e.fmha_fwd(q, k, v, False, scale, 2), flops_f)}
     if hasattr(e, "fmha_bwd"):
-        cases["bwd"] = (lambda: e.fmha_bwd(q, k, v, o, lse, do, False, scale), 2.5 * flops_f)
+        cases["bwd"] = (lambda: e.fmha_bwd(q, k, v, o, lse, do, False, scale, 1), 2.5 * flops_f)
+        cases["bwd2"] = (lambda: e.fmha_bwd(q, k, v, o, lse, do, False, scale, 2), 2.5 * flops_f)
     if a.compare:
         cases["sdpa_fwd"] = (lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v), flops_f)
     if a.only:

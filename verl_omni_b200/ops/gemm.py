@@ -24,10 +24,15 @@ from verl_omni_b200.ops._ext import ext
 _GELU_C = 0.7978845608028654  # sqrt(2/pi)
 
 
-def _use_native(*dims: int) -> bool:
+# Below this many output rows a 128/256-row tensor-core tile is mostly padding (e.g. the AdaLN
+# modulation linear over one embedding per sample): such skinny GEMMs go to cuBLAS.
+_MIN_ROWS = 128
+
+
+def _use_native(*dims: int, rows: int = _MIN_ROWS) -> bool:
     """The tcgen05 GEMM needs 16-byte rows (every dim a multiple of 8 bf16); odd-width heads such as a
-    scalar reward head (N = 1) go to cuBLAS."""
-    if any(d % 8 for d in dims):
+    scalar reward head (N = 1) go to cuBLAS, as do GEMMs with fewer than ``_MIN_ROWS`` output rows."""
+    if any(d % 8 for d in dims) or rows < _MIN_ROWS:
         return False
     return os.environ.get("VO_GEMM", "native") != "torch" and hasattr(ext(), "gemm_fwd")
 
@@ -39,7 +44,7 @@ EPI_NONE, EPI_BIAS, EPI_GELU, EPI_GATE_RES = 0, 1, 2, 3
 def linear_fwd(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor], *, epilogue: str = "none",
                gate: Optional[torch.Tensor] = None, res: Optional[torch.Tensor] = None, S: int = 1):
     """Returns ``(out, saved)``: ``saved`` is the pre-activation (gelu) or the linear output (gate_res)."""
-    if _use_native(x.shape[1], w.shape[0]):
+    if _use_native(x.shape[1], w.shape[0], rows=x.shape[0]):
         e = ext()
         if epilogue == "gelu":
             out, pre = e.gemm_fwd(x, w, b, EPI_GELU, None, None, S)
@@ -61,14 +66,14 @@ def linear_fwd(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor], *, e
 
 def matmul_nn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     """``a[M,N] @ b[N,K]`` (b row-major: the MN-major B operand)."""
-    if _use_native(a.shape[1], b.shape[1]):
+    if _use_native(a.shape[1], b.shape[1], rows=a.shape[0]):
         return ext().gemm_dgrad(a, b)
     return a @ b
 
 
 def wgrad(dy: torch.Tensor, x: torch.Tensor, main_grad: Optional[torch.Tensor]):
     """``dy[M,N]^T @ x[M,K]``; accumulated (fp32) into ``main_grad`` when given (returns None)."""
-    if _use_native(dy.shape[1], x.shape[1]):
+    if _use_native(dy.shape[1], x.shape[1], rows=min(dy.shape[0], dy.shape[1])):
         if main_grad is not None:
             ext().gemm_wgrad(dy, x, main_grad, True)
             return None

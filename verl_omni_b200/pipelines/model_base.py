@@ -67,6 +67,9 @@ class DiffusionModelBase:
     def forward(cls, module, latents: torch.Tensor, timesteps: torch.Tensor, cond: dict) -> torch.Tensor:
         raise NotImplementedError
 
+    # Qwen-Image-style "true CFG": rescale the guided prediction to the conditional one's norm
+    true_cfg_renorm = False
+
     @classmethod
     def predict(cls, module, latents, timesteps, cond: dict, neg_cond: Optional[dict] = None,
                 guidance_scale: Optional[float] = None) -> torch.Tensor:
@@ -75,7 +78,9 @@ class DiffusionModelBase:
             both = {k: torch.cat([cond[k], neg_cond[k]], 0) for k in cond}
             out = cls.forward(module, torch.cat([latents, latents], 0), torch.cat([timesteps, timesteps], 0), both)
             pos, neg = out.chunk(2, 0)
-            return neg + guidance_scale * (pos - neg)
+            from verl_omni_b200.ops.cfg import cfg_combine
+
+            return cfg_combine(pos, neg, guidance_scale, renorm=cls.true_cfg_renorm)
         return cls.forward(module, latents, timesteps, cond)
 
     @classmethod
