@@ -32,7 +32,7 @@ def _ref(q, k, v, causal, scale):
     return o, lse
 
 
-@pytest.mark.parametrize("version", [1, 2])
+@pytest.mark.parametrize("version", [1, 2, 3])
 @pytest.mark.parametrize("B,H,Sq,Skv,D,causal", CASES)
 def test_fmha_fwd(E, B, H, Sq, Skv, D, causal, version):
     torch.manual_seed(0)
@@ -46,7 +46,7 @@ def test_fmha_fwd(E, B, H, Sq, Skv, D, causal, version):
     torch.testing.assert_close(lse, rlse, rtol=1e-3, atol=1e-3)
 
 
-@pytest.mark.parametrize("version", [1, 2])
+@pytest.mark.parametrize("version", [1, 2, 3])
 @pytest.mark.parametrize("D", [64, 128])
 def test_fmha_fwd_growing_max(E, D, version):
     """Later key blocks carry far larger scores: exercises the running-max rescale of O."""

@@ -7,6 +7,8 @@ extern "C" int vo_fmha_error(int reset);
 extern "C" int vo_fmha_fwd2(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int Sq,
                             int Skv, int D, float scale, int causal, cudaStream_t stream);
 extern "C" int vo_fmha_fwd2_error(int reset);
+extern "C" int vo_fmha_fwd3(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int Sq,
+                            int Skv, int D, float scale, int causal, cudaStream_t stream);
 extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const void* o, const void* dO,
                            const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_acc, int B, int H,
                            int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream, int version);
@@ -16,7 +18,7 @@ namespace vo {
 
 // q [B, H, Sq, D], k/v [B, H, Skv, D] -> (o [B, Sq, H, D], lse [B, H, Sq] fp32)
 // version 1: one query tile per CTA, P staged in shared memory; version 2: two query tiles per CTA,
-// P and O resident in tensor memory.
+// P and O resident in tensor memory; version 3: as 2 with two softmax warpgroups per query tile.
 std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal, double scale,
                                     int64_t version) {
   VO_CHECK_INPUT(q);
@@ -28,7 +30,7 @@ std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Ten
   TORCH_CHECK(D == 64 || D == 128, "head_dim must be 64 or 128");
   auto o = torch::empty({B, Sq, H, D}, q.options());
   auto lse = torch::empty({B, H, Sq}, q.options().dtype(torch::kFloat32));
-  auto fn = version == 2 ? vo_fmha_fwd2 : vo_fmha_fwd;
+  auto fn = version == 3 ? vo_fmha_fwd3 : version == 2 ? vo_fmha_fwd2 : vo_fmha_fwd;
   int rc = fn(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(), B, H, Sq, Skv, D,
               (float)scale, causal ? 1 : 0, stream());
   TORCH_CHECK(rc == 0, "tcgen05 FMHA launch failed: code ", rc);

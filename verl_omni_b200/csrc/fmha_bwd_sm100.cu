@@ -148,6 +148,7 @@ struct Lay {
   static constexpr int DEL_OFF = LSE_OFF + 512;   // 128 floats
   static constexpr int BAR_OFF = DEL_OFF + 512;
   static constexpr int BYTES = BAR_OFF + 256;
+  static_assert(BYTES + 1024 <= 232448, "shared memory above the 227 KB per-block limit");
 };
 
 // write 32 bf16 values (one 32-column chunk of a 128-col row) into a 128B-swizzled [128 x 128] tile
@@ -449,9 +450,14 @@ struct Lay2 {
   static constexpr int Q_OFF = 2 * TILE;
   static constexpr int DO_OFF = Q_OFF + ST * TILE;
   static constexpr int DS_OFF = DO_OFF + ST * TILE;  // dS^T [128 keys x 128 queries] bf16, 2 x 16 KB
-  static constexpr int LSE_OFF = DS_OFF + 32768;     // [2 warpgroups][2 parities][64] float2 (lse*log2e, delta)
-  static constexpr int BAR_OFF = LSE_OFF + 2048;
-  static constexpr int BYTES = BAR_OFF + 256;
+  // head_dim 64: the dQ drain stages 32 x 32 fp32 tiles for TMA bulk reduce-adds (2 x 4 KB per drain
+  // warp); head_dim 128 has no room left and reduces with vector atomics
+  static constexpr bool TMA_DQ = D == 64;
+  static constexpr int DQST_OFF = DS_OFF + 32768;
+  static constexpr int LSE_OFF = DQST_OFF + (TMA_DQ ? 32768 : 0);  // [2 warpgroups][64] float2 (lse*log2e, delta)
+  static constexpr int BAR_OFF = LSE_OFF + 1024;
+  static constexpr int BYTES = BAR_OFF + 256;  // head_dim 128: 224.25 KB, inside the 227 KB opt-in limit
+  static_assert(BYTES + 1024 <= 232448, "shared memory above the 227 KB per-block limit");
   // tensor memory: S^T [0,128), dP^T [128,256), dV, dK, then (head_dim 64) two dQ buffers
   static constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 256 + D;
   static constexpr bool DQ_OWN = D == 64;  // head_dim 128: dQ reuses the S^T columns after the dV MMA
@@ -463,7 +469,8 @@ struct Lay2 {
 template <int D>
 __global__ void __launch_bounds__(512, 1)
     fmha_bwd2_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
-                     const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo, Params p) {
+                     const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
+                     const __grid_constant__ CUtensorMap mdq, Params p) {
   using L = Lay2<D>;
   constexpr int ST = L::ST;
   extern __shared__ __align__(1024) uint8_t raw[];
@@ -602,7 +609,7 @@ __global__ void __launch_bounds__(512, 1)
     const int kv = kv0 + r;
     const uint32_t lane_off = (uint32_t)lane_base << 16;
     uint8_t* ds = sm + L::DS_OFF;
-    float2* ld_base = reinterpret_cast<float2*>(sm + L::LSE_OFF) + g * 128;  // [2 parities][64]
+    float2* lds = reinterpret_cast<float2*>(sm + L::LSE_OFF) + g * 64;
     // lse / delta of one query column per thread (threads 0..63: lse, 64..127: delta), one tile ahead
     auto fetch = [&](int it) -> float {
       const int q = (i0 + it) * 128 + 64 * g + (tid & 63);
@@ -612,12 +619,12 @@ __global__ void __launch_bounds__(512, 1)
     float pre = fetch(0);
     bool ok = ntile > 0;
     for (int it = 0; ok && it < ntile; ++it) {
-      float2* lds = ld_base + (it & 1) * 64;
+      named_bar(1 + g, 128);  // previous tile's readers of lds are done
       if (tid < 64)
         lds[tid].x = pre;
       else
         lds[tid - 64].y = pre;
-      named_bar(1 + g, 128);  // this tile's lse/delta visible (the other parity buffer is still being read)
+      named_bar(1 + g, 128);  // this tile's values visible
       pre = fetch(it + 1);    // next tile's values load under this tile's math
       const int q0 = (i0 + it) * 128 + 64 * g;
       if (!mbar_wait(sp_full, it & 1, abort_flag, 69)) {
@@ -702,6 +709,8 @@ __global__ void __launch_bounds__(512, 1)
     const int lane_base = 32 * (warp & 3);
     const int r = lane_base + lane;
     const uint32_t lane_off = (uint32_t)lane_base << 16;
+    uint8_t* stage = sm + L::DQST_OFF + (warp - 12) * 8192;
+    int nchunk = 0;
     for (int it = 0; it < ntile; ++it) {
       if (!mbar_wait(dq_full, it & 1, abort_flag, 72)) break;
       fence_after();
@@ -710,7 +719,28 @@ __global__ void __launch_bounds__(512, 1)
       for (int c = 0; c < D / 32; ++c) {
         float v[32];
         ld32(tmem + L::dq_col(it) + lane_off + c * 32, v);
-        if (q < p.Sq) {
+        if constexpr (L::TMA_DQ) {
+          // 32 rows x 32 columns of this warp -> swizzled staging -> one bulk reduce-add into dQ_acc
+          uint8_t* buf = stage + (nchunk & 1) * 4096;
+          ++nchunk;
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          __syncwarp();
+          uint8_t* rowp = buf + lane * 128;
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<float4*>(rowp + 16 * (u ^ (lane & 7))) =
+                make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            asm volatile(
+                "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                    &mdq),
+                "r"(smem_u32(buf)), "r"(c * 32), "r"((i0 + it) * 128 + lane_base), "r"(bh)
+                : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+        } else if (q < p.Sq) {
           float* dst = p.dq_acc + ((int64_t)bh * p.Sq + q) * D + c * 32;
 #pragma unroll
           for (int j = 0; j < 32; j += 4) red_add_v4(dst + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
@@ -720,6 +750,8 @@ __global__ void __launch_bounds__(512, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&dq_free[L::DQ_OWN ? (it & 1) : 0]);
     }
+    if (L::TMA_DQ && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
   }
   fence_before();
   __syncthreads();
@@ -798,6 +830,16 @@ static int map3(CUtensorMap* m, const void* ptr, int BH, int S, int D) {
                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
+// fp32 [BH, S, D] with box {32, 32, 1}, 128B swizzle (dQ accumulator, bulk reduce-add target)
+static int map3_f32(CUtensorMap* m, const void* ptr, int BH, int S, int D) {
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)BH};
+  cuuint64_t str[2] = {(cuuint64_t)D * 4, (cuuint64_t)S * D * 4};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return (int)encode()(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(ptr), dims, str, box, es,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
 // token-major [B, S, H, D] viewed as 4D {D, H, S, B}; box {64, 1, 128, 1}
 static int map4_tok(CUtensorMap* m, const void* ptr, int B, int S, int H, int D) {
   cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
@@ -814,7 +856,9 @@ static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMa
                   Params p, int grid, cudaStream_t st) {
   static bool set = false;
   if (!set) {
-    cudaFuncSetAttribute(fmha_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay<D>::BYTES + 1024);
+    const cudaError_t e =
+        cudaFuncSetAttribute(fmha_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay<D>::BYTES + 1024);
+    if (e != cudaSuccess) return (int)e;
     set = true;
   }
   fmha_bwd_kernel<D><<<grid, NUM_THREADS, Lay<D>::BYTES + 1024, st>>>(mq, mk, mv, mdo, p);
@@ -823,14 +867,16 @@ static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMa
 
 template <int D>
 static int launch2(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
-                   Params p, int grid, cudaStream_t st) {
+                   const CUtensorMap& mdq, Params p, int grid, cudaStream_t st) {
   using L = v2::Lay2<D>;
   static bool set = false;
   if (!set) {
-    cudaFuncSetAttribute(v2::fmha_bwd2_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES + 1024);
+    const cudaError_t e =
+        cudaFuncSetAttribute(v2::fmha_bwd2_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES + 1024);
+    if (e != cudaSuccess) return (int)e;
     set = true;
   }
-  v2::fmha_bwd2_kernel<D><<<grid, 512, L::BYTES + 1024, st>>>(mq, mk, mv, mdo, p);
+  v2::fmha_bwd2_kernel<D><<<grid, 512, L::BYTES + 1024, st>>>(mq, mk, mv, mdo, mdq, p);
   return (int)cudaGetLastError();
 }
 
@@ -871,10 +917,15 @@ extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const vo
   p.dk = (__nv_bfloat16*)dk;
   p.dv = (__nv_bfloat16*)dv;
   const int grid = p.nkv_tiles * B * H;
-  if (version == 2)
-    r = D == 64 ? launch2<64>(mq, mk, mv, mdo, p, grid, stream) : launch2<128>(mq, mk, mv, mdo, p, grid, stream);
-  else
+  if (version == 2) {
+    CUtensorMap mdq;
+    if ((r = map3_f32(&mdq, dq_acc, B * H, Sq, D))) return r;
+    r = D == 64 ? launch2<64>(mq, mk, mv, mdo, mdq, p, grid, stream)
+                : launch2<128>(mq, mk, mv, mdo, mdq, p, grid, stream);
+  }
+  else {
     r = D == 64 ? launch<64>(mq, mk, mv, mdo, p, grid, stream) : launch<128>(mq, mk, mv, mdo, p, grid, stream);
+  }
   if (r) return r;
   const int64_t n4 = (int64_t)B * H * Sq * D / 4;
   dq_finalize_kernel<<<(unsigned)((n4 + 255) / 256 < 4096 ? (n4 + 255) / 256 : 4096), 256, 0, stream>>>(

@@ -182,12 +182,167 @@ struct Cfg {
   static constexpr int K_OFF = 2 * TILE;
   static constexpr int V_OFF = K_OFF + KST * TILE;
   static constexpr int BAR_OFF = V_OFF + VST * TILE;
-  static constexpr int BYTES = BAR_OFF + 256;
+  static constexpr int BYTES = BAR_OFF + 256 + 4096 + 1024;
+  static_assert(BYTES + 1024 <= 232448, "shared memory above the 227 KB per-block limit");
   static constexpr uint32_t S_COL0 = 0, O_COL0 = 256;
 };
 
+__device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n)); }
+
+// Softmax of one key half of one query tile (SPLIT == 2).  Warps 2..17 form groups g = 0..3 of four
+// consecutive warps (covering the four 32-lane quarters of tensor memory); tile t = g / 2, key half
+// h = g % 2.  Per key block: row max over the 64 own columns, exchange with the partner half through
+// shared memory (double-buffered by block parity, one 256-thread named barrier), the shared lazy
+// rescale of the own half of O_t, P for the own keys packed into the first 32 own columns.
 template <int D>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__device__ __forceinline__ void softmax_split2(const Params& p, uint32_t tmem, int warp, int lane, int q0, int bh,
+                                               int nkv, uint64_t* s_full, uint64_t* p_full, uint64_t* o_final,
+                                               volatile int* abort_flag, float* xmax, float* xsum) {
+  using C = Cfg<D>;
+  const int g = (warp - 2) >> 2;
+  const int t = g >> 1, hf = g & 1;
+  const int quarter = warp & 3;
+  const int row = 32 * quarter + lane;
+  const int q = q0 + t * BQ + row;
+  const uint32_t lane_off = (uint32_t)(32 * quarter) << 16;
+  const uint32_t S_t = tmem + C::S_COL0 + t * 128 + lane_off + 64 * hf;
+  const uint32_t O_t = tmem + C::O_COL0 + t * D + lane_off + hf * (D / 2);
+  const int bar_id = 1 + t;
+  float* mx_mine = xmax + (t * 2 + hf) * 256;
+  const float* mx_other = xmax + (t * 2 + (hf ^ 1)) * 256;
+  const float sl2 = p.scale_log2;
+  float m = -INFINITY, l = 0.f;
+  bool ok = nkv > 0;
+  for (int j = 0; ok && j < nkv; ++j) {
+    if (!mbar_wait(&s_full[t], j & 1, abort_flag, 49)) {
+      ok = false;
+      break;
+    }
+    fence_after();
+    const int kv0 = j * BKV + 64 * hf;
+    int lim = p.Skv - kv0;
+    if (p.causal) lim = min(lim, q - kv0 + 1);
+    lim = max(0, min(64, lim));
+    float mx = -INFINITY;
+    {  // pass 1 (values are read again in pass 2: keeps the register budget of 576 threads)
+    uint32_t a[32], b[32];
+    ld32_nowait(S_t, a);
+    ld32_nowait(S_t + 32, b);
+    wait_ld();
+    if (lim == 64) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) mx = max3(mx, __uint_as_float(a[i]), __uint_as_float(b[i]));
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (i < lim) mx = fmaxf(mx, __uint_as_float(a[i]));
+        if (32 + i < lim) mx = fmaxf(mx, __uint_as_float(b[i]));
+      }
+    }
+    }
+    const int par = (j & 1) * 128;
+    mx_mine[par + row] = mx;
+    named_bar(bar_id, 256);
+    mx = fmaxf(mx, mx_other[par + row]);
+    const float m_blk = mx * sl2;
+    float alpha = 1.f;
+    const bool move = m_blk > m + RESCALE_THRESHOLD || (m == -INFINITY && m_blk != -INFINITY);
+    if (move) {
+      alpha = (m == -INFINITY) ? 0.f : ex2(m - m_blk);
+      m = m_blk;
+    }
+    if (j > 0 && __any_sync(0xffffffffu, move)) {
+      // both halves take the same decision; each rescales its own half of O_t (quiescent, see above)
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        uint32_t o[32];
+        ld32_nowait(O_t + c * 32, o);
+        wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+        st32(O_t + c * 32, o);
+      }
+    }
+    const float nmb = (m == -INFINITY) ? 0.f : -m;
+    float rs = 0.f, rs0 = 0.f, rs1 = 0.f;
+    auto emit = [&](const uint32_t (&v)[32], int c) {
+      uint32_t w[16];
+      if (lim == 64) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float x0, x1;
+          ffma2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]), sl2, nmb, x0, x1);
+          const float e0 = ex2(x0), e1 = ex2(x1);
+          fadd2(rs0, rs1, e0, e1);
+          w[i] = pack_bf16(e0, e1);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int k = c * 32 + 2 * i;
+          const float e0 = k < lim ? ex2(fmaf(__uint_as_float(v[2 * i]), sl2, nmb)) : 0.f;
+          const float e1 = k + 1 < lim ? ex2(fmaf(__uint_as_float(v[2 * i + 1]), sl2, nmb)) : 0.f;
+          rs += e0 + e1;
+          w[i] = pack_bf16(e0, e1);
+        }
+      }
+      st16(S_t + c * 16, w);
+    };
+    {
+      uint32_t v[32];
+      ld32_nowait(S_t, v);
+      wait_ld();
+      emit(v, 0);
+      ld32_nowait(S_t + 32, v);  // columns 32..63 are not touched by the chunk-0 stores (columns 0..15)
+      wait_ld();
+      emit(v, 1);
+    }
+    wait_st();
+    fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&p_full[t]);
+    l = l * alpha + (rs + (rs0 + rs1));
+  }
+  if (ok && mbar_wait(&o_final[t], 0, abort_flag, 50)) {
+    fence_after();
+    xsum[(t * 2 + hf) * 128 + row] = l;
+    named_bar(bar_id, 256);
+    const float lt = l + xsum[(t * 2 + (hf ^ 1)) * 128 + row];
+    const float inv = lt > 0.f ? 1.f / lt : 0.f;
+    const int bb = bh / p.H, h = bh % p.H;
+    const bool row_ok = q < p.Sq;
+    __nv_bfloat16* dst = p.o + (((int64_t)bb * p.Sq + q) * p.H + h) * D + hf * (D / 2);
+#pragma unroll
+    for (int c = 0; c < D / 64; ++c) {
+      uint32_t o[32];
+      ld32_nowait(O_t + c * 32, o);
+      wait_ld();
+      if (row_ok) {
+#pragma unroll
+        for (int gg = 0; gg < 4; ++gg) {
+          uint4 pk;
+          pk.x = pack_bf16(__uint_as_float(o[gg * 8 + 0]) * inv, __uint_as_float(o[gg * 8 + 1]) * inv);
+          pk.y = pack_bf16(__uint_as_float(o[gg * 8 + 2]) * inv, __uint_as_float(o[gg * 8 + 3]) * inv);
+          pk.z = pack_bf16(__uint_as_float(o[gg * 8 + 4]) * inv, __uint_as_float(o[gg * 8 + 5]) * inv);
+          pk.w = pack_bf16(__uint_as_float(o[gg * 8 + 6]) * inv, __uint_as_float(o[gg * 8 + 7]) * inv);
+          *reinterpret_cast<uint4*>(dst + c * 32 + gg * 8) = pk;
+        }
+      }
+    }
+    if (row_ok && hf == 0) p.lse[(int64_t)bh * p.Sq + q] = (m + __log2f(lt)) * 0.69314718055994531f;
+  }
+}
+
+// SPLIT = softmax warpgroups per query tile.  SPLIT == 2 (576 threads): warpgroup (t, h) owns key
+// columns [64 h, 64 h + 64) of S_t; the two halves exchange row maxima and row sums through shared
+// memory (one named barrier per key block), write P for their keys into their own 64-column half
+// (packed into its first 32 columns) and rescale / store their half of O_t.  Twice the softmax
+// warps per SMSP hide the tensor-memory and MUFU latencies that bound SPLIT == 1.
+template <int SPLIT>
+__host__ __device__ constexpr int fwd_threads() { return SPLIT == 2 ? 576 : NUM_THREADS; }
+
+template <int D, int SPLIT>
+__global__ void __launch_bounds__(fwd_threads<SPLIT>(), 1)
     fmha_fwd2_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                      const __grid_constant__ CUtensorMap mv, Params p) {
   using C = Cfg<D>;
@@ -204,6 +359,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* o_final = p_full + 2;           // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // SPLIT == 2 exchange buffers: [tile][half][parity][128 rows] maxima, [tile][half][128] row sums
+  float* xmax = reinterpret_cast<float*>(sm + C::BAR_OFF + 256);
+  float* xsum = xmax + 2 * 2 * 2 * 128;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // heavier (later) query pairs first under a causal mask
@@ -226,7 +384,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 4);
+      mbar_init(&p_full[t], 4 * SPLIT);
       mbar_init(&o_final[t], 1);
     }
     *abort_flag = 0;
@@ -290,7 +448,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t va = smem_u32(sm + C::V_OFF + (j % C::VST) * C::TILE);
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk)
-          mma_ts(O_T[t], S_T[t] + kk * 8, desc(va + kk * 2048, 16384, 1024), id_o, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(O_T[t], S_T[t] + (SPLIT == 2 && kk >= 4 ? 64 + (kk - 4) * 8 : kk * 8),
+                 desc(va + kk * 2048, 16384, 1024), id_o, (j > 0 || kk > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(q_full, 0, abort_flag, 43) && mbar_wait(&k_full[0], 0, abort_flag, 44);
       if (ok) {
@@ -324,7 +483,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
-  } else if (warp >= 4) {
+  } else if (SPLIT == 2 && warp >= 2) {
+    softmax_split2<D>(p, tmem, warp, lane, q0, bh, nkv, s_full, p_full, o_final, abort_flag, xmax, xsum);
+  } else if (SPLIT == 1 && warp >= 4) {
     // ---------------------------------------------------------------- softmax warpgroups
     const int t = (warp - 4) >> 2;
     const int lane_base = 32 * (warp & 3);
@@ -498,23 +659,23 @@ static int map3(CUtensorMap* m, const void* ptr, int BH, int S, int D) {
                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
-template <int D>
-static void launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const Params& p,
-                   unsigned grid, cudaStream_t stream) {
+template <int D, int SPLIT>
+static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const Params& p,
+                  unsigned grid, cudaStream_t stream) {
   static bool set = false;
   const int bytes = Cfg<D>::BYTES + 1024;
   if (!set) {
-    cudaFuncSetAttribute(fmha_fwd2_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    const cudaError_t e =
+        cudaFuncSetAttribute(fmha_fwd2_kernel<D, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return (int)e;
     set = true;
   }
-  fmha_fwd2_kernel<D><<<grid, NUM_THREADS, bytes, stream>>>(mq, mk, mv, p);
+  fmha_fwd2_kernel<D, SPLIT><<<grid, fwd_threads<SPLIT>(), bytes, stream>>>(mq, mk, mv, p);
+  return (int)cudaGetLastError();
 }
 
-}  // namespace vo_fmha2
-
-extern "C" int vo_fmha_fwd2(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int Sq,
-                            int Skv, int D, float scale, int causal, cudaStream_t stream) {
-  using namespace vo_fmha2;
+static int fwd2_impl(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int Sq, int Skv,
+                     int D, float scale, int causal, cudaStream_t stream, int split) {
   if (D != 64 && D != 128) return -1;
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15)
     return -2;
@@ -535,10 +696,23 @@ extern "C" int vo_fmha_fwd2(const void* q, const void* k, const void* v, void* o
   const long long grid = (long long)p.npairs * B * H;
   if (grid == 0) return 0;
   if (D == 64)
-    launch<64>(mq, mk, mv, p, (unsigned)grid, stream);
-  else
-    launch<128>(mq, mk, mv, p, (unsigned)grid, stream);
-  return (int)cudaGetLastError();
+    return split == 2 ? launch<64, 2>(mq, mk, mv, p, (unsigned)grid, stream)
+                      : launch<64, 1>(mq, mk, mv, p, (unsigned)grid, stream);
+  return split == 2 ? launch<128, 2>(mq, mk, mv, p, (unsigned)grid, stream)
+                    : launch<128, 1>(mq, mk, mv, p, (unsigned)grid, stream);
+}
+
+}  // namespace vo_fmha2
+
+extern "C" int vo_fmha_fwd2(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int Sq,
+                            int Skv, int D, float scale, int causal, cudaStream_t stream) {
+  return vo_fmha2::fwd2_impl(q, k, v, o, lse, B, H, Sq, Skv, D, scale, causal, stream, 1);
+}
+
+// two softmax warpgroups per query tile (576 threads)
+extern "C" int vo_fmha_fwd3(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int Sq,
+                            int Skv, int D, float scale, int causal, cudaStream_t stream) {
+  return vo_fmha2::fwd2_impl(q, k, v, o, lse, B, H, Sq, Skv, D, scale, causal, stream, 2);
 }
 
 extern "C" int vo_fmha_fwd2_error(int reset) {

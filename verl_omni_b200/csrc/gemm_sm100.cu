@@ -178,6 +178,7 @@ struct Shape {
 constexpr int EPI_WARP_BYTES = 8192;              // 2 buffers x 4 KB per epilogue warp
 constexpr int EPI_SMEM_BYTES = 4 * EPI_WARP_BYTES;  // 32 KB
 constexpr int SMEM1_BYTES = STAGES * STAGE_BYTES + EPI_SMEM_BYTES + 1024 + 256;
+static_assert(SMEM1_BYTES <= 232448, "shared memory above the 227 KB per-block limit");
 
 struct EpiMaps {
   CUtensorMap out;   // bf16 [M, N], box {32, 32}, 64B swizzle
@@ -450,6 +451,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 constexpr int STAGES2 = 6;
 constexpr int STAGE2_BYTES = 2 * BM * BK * 2;  // A 128x64 + B 128x64 per CTA = 32 KB
 constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + EPI_SMEM_BYTES + 1024 + 256;
+static_assert(SMEM2_BYTES <= 232448, "shared memory above the 227 KB per-block limit");
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;

@@ -112,7 +112,8 @@ def bench_fmha(a) -> list[dict]:
     do = torch.randn_like(o)
     flops_f = 4.0 * B * H * S * S * D
     cases = {"fwd": (lambda: e.fmha_fwd(q, k, v, False, scale, 1), flops_f),
-             "fwd2": (lambda: e.fmha_fwd(q, k, v, False, scale, 2), flops_f)}
+             "fwd2": (lambda: e.fmha_fwd(q, k, v, False, scale, 2), flops_f),
+             "fwd3": (lambda: e.fmha_fwd(q, k, v, False, scale, 3), flops_f)}
     if hasattr(e, "fmha_bwd"):
         cases["bwd"] = (lambda: e.fmha_bwd(q, k, v, o, lse, do, False, scale, 1), 2.5 * flops_f)
         cases["bwd2"] = (lambda: e.fmha_bwd(q, k, v, o, lse, do, False, scale, 2), 2.5 * flops_f)
