@@ -99,3 +99,27 @@ def test_fmha_bwd(E, B, H, Sq, Skv, D, causal, version):
     for a, b in ((dq, qr.grad), (dk, kr.grad), (dv, vr.grad)):
         rel = float((a.float() - b).norm() / (b.norm() + 1e-6))
         assert rel < 2e-2, rel
+
+
+@pytest.mark.parametrize("fwd,bwd", [(2, 1), (3, 2)])
+@pytest.mark.parametrize("D", [64, 128])
+def test_attention_split_matches_joint(E, fwd, bwd, D, monkeypatch):
+    """Split outputs (image rows / text rows in separate tensors) equal slices of the joint output,
+    forward and backward, on the kernel versions the split path uses."""
+    import verl_omni_b200.ops.attention as A
+
+    monkeypatch.setattr(A, "_FWD_VERSION", fwd)
+    monkeypatch.setattr(A, "_BWD_VERSION", bwd)
+    torch.manual_seed(5)
+    B, H, Si, St = 2, 3, 256, 77
+    q, k, v = (torch.randn(B, H, Si + St, D, device="cuda").bfloat16().requires_grad_(True) for _ in range(3))
+    oa, ob = A.attention_split(q, k, v, Si)
+    ga, gb = torch.randn_like(oa), torch.randn_like(ob)
+    torch.autograd.backward([oa, ob], [ga, gb])
+    qr, kr, vr = (t.detach().clone().requires_grad_(True) for t in (q, k, v))
+    o = A.attention(qr, kr, vr)
+    torch.testing.assert_close(oa, o[:, :Si])
+    torch.testing.assert_close(ob, o[:, Si:])
+    o.backward(torch.cat([ga, gb], 1))
+    for a, b in ((q, qr), (k, kr), (v, vr)):
+        torch.testing.assert_close(a.grad.float(), b.grad.float(), rtol=1e-2, atol=1e-2)

@@ -44,7 +44,7 @@ void gemm_wgrad(torch::Tensor dy, torch::Tensor x, torch::Tensor out, bool accum
 torch::Tensor gelu_tanh_bwd(torch::Tensor dy, torch::Tensor pre);
 int64_t gemm_error(bool reset);
 std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal, double scale,
-                                    int64_t version);
+                                    int64_t version, int64_t split);
 int64_t fmha_error(bool reset);
 std::vector<torch::Tensor> linear_bwd_prep(torch::Tensor dy, c10::optional<torch::Tensor> saved,
                                            c10::optional<torch::Tensor> gate, int64_t S, int64_t mode,
@@ -61,7 +61,8 @@ void peer_adamw_bcast(std::vector<int64_t> flat_ptrs, int64_t lo, int64_t n, tor
                       torch::Tensor m, torch::Tensor v, double lr, double b1, double b2, double eps, double wd,
                       int64_t step, double max_norm, torch::Tensor sq_norm);
 std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
-                                    torch::Tensor lse, torch::Tensor dO, bool causal, double scale, int64_t version);
+                                    torch::Tensor lse, torch::Tensor dO, bool causal, double scale, int64_t version,
+                                    c10::optional<torch::Tensor> o2, c10::optional<torch::Tensor> dO2, int64_t split);
 }  // namespace vo
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -86,10 +87,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gelu_tanh_bwd", &vo::gelu_tanh_bwd);
   m.def("gemm_error", &vo::gemm_error);
   m.def("fmha_fwd", &vo::fmha_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("causal"), py::arg("scale"),
-        py::arg("version") = 2);
+        py::arg("version") = 2, py::arg("split") = 0);
   m.def("fmha_error", &vo::fmha_error);
   m.def("fmha_bwd", &vo::fmha_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
-        py::arg("dO"), py::arg("causal"), py::arg("scale"), py::arg("version") = 1);
+        py::arg("dO"), py::arg("causal"), py::arg("scale"), py::arg("version") = 1, py::arg("o2") = py::none(),
+        py::arg("dO2") = py::none(), py::arg("split") = 0);
   m.def("linear_bwd_prep", &vo::linear_bwd_prep);
   m.def("cfg_combine", &vo::cfg_combine);
   m.def("symm_malloc", &vo::symm_malloc);

@@ -1,26 +1,30 @@
-// Torch-facing wrapper of the tcgen05 flash-attention forward.
+// Torch-facing wrappers of the tcgen05 flash-attention forward and backward kernels.
 #include "common.cuh"
 
 extern "C" int vo_fmha_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int Sq,
                            int Skv, int D, float scale, int causal, cudaStream_t stream);
 extern "C" int vo_fmha_error(int reset);
-extern "C" int vo_fmha_fwd2(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int Sq,
-                            int Skv, int D, float scale, int causal, cudaStream_t stream);
+extern "C" int vo_fmha_fwd2(const void* q, const void* k, const void* v, void* o, void* o2, int out_split, float* lse,
+                            int B, int H, int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream);
 extern "C" int vo_fmha_fwd2_error(int reset);
-extern "C" int vo_fmha_fwd3(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int Sq,
-                            int Skv, int D, float scale, int causal, cudaStream_t stream);
+extern "C" int vo_fmha_fwd3(const void* q, const void* k, const void* v, void* o, void* o2, int out_split, float* lse,
+                            int B, int H, int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream);
 extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const void* o, const void* dO,
-                           const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_acc, int B, int H,
-                           int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream, int version);
+                           const void* o2, const void* dO2, int split, const float* lse, void* dq, void* dk, void* dv,
+                           float* delta, float* dq_acc, int B, int H, int Sq, int Skv, int D, float scale, int causal,
+                           cudaStream_t stream, int version);
 extern "C" int vo_fmha_bwd_error(int reset);
 
 namespace vo {
 
-// q [B, H, Sq, D], k/v [B, H, Skv, D] -> (o [B, Sq, H, D], lse [B, H, Sq] fp32)
+// q [B, H, Sq, D], k/v [B, H, Skv, D] -> (o [B, Sq, H, D], lse [B, H, Sq] fp32[, o2])
 // version 1: one query tile per CTA, P staged in shared memory; version 2: two query tiles per CTA,
 // P and O resident in tensor memory; version 3: as 2 with two softmax warpgroups per query tile.
+// split > 0 (versions 2 / 3): query rows [0, split) go to o [B, split, H, D] and rows [split, Sq) to a
+// second tensor o2 [B, Sq - split, H, D] (the image / text halves of a joint attention, each feeding
+// its own output projection without a copy).
 std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal, double scale,
-                                    int64_t version) {
+                                    int64_t version, int64_t split) {
   VO_CHECK_INPUT(q);
   VO_CHECK_INPUT(k);
   VO_CHECK_INPUT(v);
@@ -28,13 +32,23 @@ std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Ten
   c10::cuda::CUDAGuard g(q.device());
   const int B = q.size(0), H = q.size(1), Sq = q.size(2), D = q.size(3), Skv = k.size(2);
   TORCH_CHECK(D == 64 || D == 128, "head_dim must be 64 or 128");
-  auto o = torch::empty({B, Sq, H, D}, q.options());
+  TORCH_CHECK(split >= 0 && split < Sq, "bad output split");
+  TORCH_CHECK(split == 0 || version >= 2, "split outputs need forward version 2 or 3");
+  auto o = torch::empty({B, split > 0 ? split : Sq, H, D}, q.options());
+  torch::Tensor o2 = split > 0 ? torch::empty({B, Sq - split, H, D}, q.options()) : torch::Tensor();
   auto lse = torch::empty({B, H, Sq}, q.options().dtype(torch::kFloat32));
-  auto fn = version == 3 ? vo_fmha_fwd3 : version == 2 ? vo_fmha_fwd2 : vo_fmha_fwd;
-  int rc = fn(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(), B, H, Sq, Skv, D,
-              (float)scale, causal ? 1 : 0, stream());
+  int rc;
+  if (version >= 2) {
+    auto fn = version == 3 ? vo_fmha_fwd3 : vo_fmha_fwd2;
+    rc = fn(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), split > 0 ? o2.data_ptr() : nullptr, (int)split,
+            lse.data_ptr<float>(), B, H, Sq, Skv, D, (float)scale, causal ? 1 : 0, stream());
+  } else {
+    rc = vo_fmha_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(), B, H, Sq, Skv, D,
+                     (float)scale, causal ? 1 : 0, stream());
+  }
   TORCH_CHECK(rc == 0, "tcgen05 FMHA launch failed: code ", rc);
   count_launch();
+  if (split > 0) return {o, lse, o2};
   return {o, lse};
 }
 
@@ -44,9 +58,11 @@ int64_t fmha_error(bool reset) {
 
 // returns dq, dk, dv in the [B, H, S, D] layout of q, k, v
 // version 1: one key tile per CTA, serial per query tile; version 2: pipelined (P^T / dS^T in
-// tensor memory, concurrent dQ drain, next S^T overlapped for head_dim 64)
+// tensor memory, two gradient warpgroups, concurrent dQ drain).  split > 0: O and dO are given as
+// two halves (o, dO: rows [0, split); o2, dO2: rows [split, Sq)); split must be a multiple of 128.
 std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
-                                    torch::Tensor lse, torch::Tensor dO, bool causal, double scale, int64_t version) {
+                                    torch::Tensor lse, torch::Tensor dO, bool causal, double scale, int64_t version,
+                                    c10::optional<torch::Tensor> o2, c10::optional<torch::Tensor> dO2, int64_t split) {
   VO_CHECK_INPUT(q);
   VO_CHECK_INPUT(k);
   VO_CHECK_INPUT(v);
@@ -56,15 +72,26 @@ std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Ten
   c10::cuda::CUDAGuard g(q.device());
   const int B = q.size(0), H = q.size(1), Sq = q.size(2), D = q.size(3), Skv = k.size(2);
   TORCH_CHECK(D == 64 || D == 128, "head_dim must be 64 or 128");
+  const void* po2 = nullptr;
+  const void* pdo2 = nullptr;
+  if (split > 0) {
+    TORCH_CHECK(split % 128 == 0 && split < Sq, "split must be a multiple of 128 below Sq");
+    TORCH_CHECK(o2.has_value() && dO2.has_value(), "split needs o2 and dO2");
+    VO_CHECK_INPUT((*o2));
+    VO_CHECK_INPUT((*dO2));
+    po2 = o2->data_ptr();
+    pdo2 = dO2->data_ptr();
+  }
   auto dq = torch::empty_like(q);
   auto dk = torch::empty_like(k);
   auto dv = torch::empty_like(v);
   auto fo = q.options().dtype(torch::kFloat32);
   auto delta = torch::empty({B, H, Sq}, fo);
   auto dq_acc = torch::zeros({B, H, Sq, D}, fo);
-  int rc = vo_fmha_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dO.data_ptr(), lse.data_ptr<float>(),
-                       dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), delta.data_ptr<float>(), dq_acc.data_ptr<float>(),
-                       B, H, Sq, Skv, D, (float)scale, causal ? 1 : 0, stream(), (int)version);
+  int rc = vo_fmha_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dO.data_ptr(), po2, pdo2, (int)split,
+                       lse.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), delta.data_ptr<float>(),
+                       dq_acc.data_ptr<float>(), B, H, Sq, Skv, D, (float)scale, causal ? 1 : 0, stream(),
+                       (int)version);
   TORCH_CHECK(rc == 0, "tcgen05 FMHA backward launch failed: code ", rc);
   count_launch(3);
   return {dq, dk, dv};

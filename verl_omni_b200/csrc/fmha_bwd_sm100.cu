@@ -132,6 +132,7 @@ struct Params {
   float* dq_acc;       // [BH, Sq, D] fp32 (pre-zeroed)
   __nv_bfloat16* dk;   // [BH, Skv, D]
   __nv_bfloat16* dv;   // [BH, Skv, D]
+  int split;           // > 0: dO rows q >= split come from the second dO tensor map (split % 128 == 0)
 };
 
 template <int D>
@@ -171,7 +172,8 @@ __device__ __forceinline__ void store_row_chunk(uint8_t* tile, int row, int c, c
 template <int D>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     fmha_bwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
-                    const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo, Params p) {
+                    const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
+                    const __grid_constant__ CUtensorMap mdo2, Params p) {
   using L = Lay<D>;
   constexpr int ST = L::STAGES;
   extern __shared__ __align__(1024) uint8_t raw[];
@@ -235,7 +237,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
           tma3(sm + L::Q_OFF + st * L::TILE + c * 16384, &mq, &qdo_full[st], c * 64, i * 128, bh);
-          tma4(sm + L::DO_OFF + st * L::TILE + c * 16384, &mdo, &qdo_full[st], c * 64, h, i * 128, b);
+          if (p.split > 0 && i * 128 >= p.split)
+            tma4(sm + L::DO_OFF + st * L::TILE + c * 16384, &mdo2, &qdo_full[st], c * 64, h, i * 128 - p.split, b);
+          else
+            tma4(sm + L::DO_OFF + st * L::TILE + c * 16384, &mdo, &qdo_full[st], c * 64, h, i * 128, b);
         }
       }
     }
@@ -440,6 +445,21 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
 }
+// (a0, a1) * s + (c0, c1) on the paired fp32 pipe
+__device__ __forceinline__ void ffma2p(float a0, float a1, float s, float c0, float c1, float& r0, float& r1) {
+  asm("{\n\t.reg .b64 x, y, z, r;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %4};\n\tmov.b64 z, {%5, %6};\n\t"
+      "fma.rn.f32x2 r, x, y, z;\n\tmov.b64 {%0, %1}, r;\n\t}"
+      : "=f"(r0), "=f"(r1)
+      : "f"(a0), "f"(a1), "f"(s), "f"(c0), "f"(c1));
+}
+// (e0, e1) * ((p0, p1) - (d0, d1)) on the paired fp32 pipe
+__device__ __forceinline__ void sub_mul2(float p0, float p1, float d0, float d1, float e0, float e1, float& r0,
+                                         float& r1) {
+  asm("{\n\t.reg .b64 x, y, e, t;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\tmov.b64 e, {%6, %7};\n\t"
+      "sub.rn.f32x2 t, x, y;\n\tmul.rn.f32x2 t, t, e;\n\tmov.b64 {%0, %1}, t;\n\t}"
+      : "=f"(r0), "=f"(r1)
+      : "f"(p0), "f"(p1), "f"(d0), "f"(d1), "f"(e0), "f"(e1));
+}
 
 template <int D>
 struct Lay2 {
@@ -454,7 +474,7 @@ struct Lay2 {
   // warp); head_dim 128 has no room left and reduces with vector atomics
   static constexpr bool TMA_DQ = D == 64;
   static constexpr int DQST_OFF = DS_OFF + 32768;
-  static constexpr int LSE_OFF = DQST_OFF + (TMA_DQ ? 32768 : 0);  // [2 warpgroups][64] float2 (lse*log2e, delta)
+  static constexpr int LSE_OFF = DQST_OFF + (TMA_DQ ? 32768 : 0);  // [2 warpgroups][32 pairs] float4
   static constexpr int BAR_OFF = LSE_OFF + 1024;
   static constexpr int BYTES = BAR_OFF + 256;  // head_dim 128: 224.25 KB, inside the 227 KB opt-in limit
   static_assert(BYTES + 1024 <= 232448, "shared memory above the 227 KB per-block limit");
@@ -470,7 +490,7 @@ template <int D>
 __global__ void __launch_bounds__(512, 1)
     fmha_bwd2_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                      const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
-                     const __grid_constant__ CUtensorMap mdq, Params p) {
+                     const __grid_constant__ CUtensorMap mdo2, const __grid_constant__ CUtensorMap mdq, Params p) {
   using L = Lay2<D>;
   constexpr int ST = L::ST;
   extern __shared__ __align__(1024) uint8_t raw[];
@@ -535,7 +555,10 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
           tma3(sm + L::Q_OFF + st * L::TILE + c * 16384, &mq, &qdo_full[st], c * 64, i * 128, bh);
-          tma4(sm + L::DO_OFF + st * L::TILE + c * 16384, &mdo, &qdo_full[st], c * 64, h, i * 128, b);
+          if (p.split > 0 && i * 128 >= p.split)
+            tma4(sm + L::DO_OFF + st * L::TILE + c * 16384, &mdo2, &qdo_full[st], c * 64, h, i * 128 - p.split, b);
+          else
+            tma4(sm + L::DO_OFF + st * L::TILE + c * 16384, &mdo, &qdo_full[st], c * 64, h, i * 128, b);
         }
       }
     }
@@ -609,21 +632,22 @@ __global__ void __launch_bounds__(512, 1)
     const int kv = kv0 + r;
     const uint32_t lane_off = (uint32_t)lane_base << 16;
     uint8_t* ds = sm + L::DS_OFF;
-    float2* lds = reinterpret_cast<float2*>(sm + L::LSE_OFF) + g * 64;
-    // lse / delta of one query column per thread (threads 0..63: lse, 64..127: delta), one tile ahead
+    // per column pair (2i, 2i+1): {-lse_2i*log2e, -lse_2i+1*log2e, delta_2i, delta_2i+1}
+    float* lsm = reinterpret_cast<float*>(sm + L::LSE_OFF) + g * 128;
+    // one query column per thread (threads 0..63: -lse*log2e, 64..127: delta), fetched one tile ahead
+    const int col = tid & 63;
+    const int slot = (col >> 1) * 4 + (col & 1) + (tid < 64 ? 0 : 2);
     auto fetch = [&](int it) -> float {
-      const int q = (i0 + it) * 128 + 64 * g + (tid & 63);
-      if (it >= ntile || q >= p.Sq) return tid < 64 ? INFINITY : 0.f;
-      return tid < 64 ? p.lse[(int64_t)bh * p.Sq + q] * 1.4426950408889634f : p.delta[(int64_t)bh * p.Sq + q];
+      const int q = (i0 + it) * 128 + 64 * g + col;
+      if (it >= ntile || q >= p.Sq) return tid < 64 ? -INFINITY : 0.f;
+      return tid < 64 ? -p.lse[(int64_t)bh * p.Sq + q] * 1.4426950408889634f : p.delta[(int64_t)bh * p.Sq + q];
     };
     float pre = fetch(0);
+    const float sl2 = p.scale_log2;
     bool ok = ntile > 0;
     for (int it = 0; ok && it < ntile; ++it) {
-      named_bar(1 + g, 128);  // previous tile's readers of lds are done
-      if (tid < 64)
-        lds[tid].x = pre;
-      else
-        lds[tid - 64].y = pre;
+      named_bar(1 + g, 128);  // previous tile's readers of lsm are done
+      lsm[slot] = pre;
       named_bar(1 + g, 128);  // this tile's values visible
       pre = fetch(it + 1);    // next tile's values load under this tile's math
       const int q0 = (i0 + it) * 128 + 64 * g;
@@ -637,6 +661,7 @@ __global__ void __launch_bounds__(512, 1)
       int qlo = p.causal ? max(0, kv - q0) : 0;
       qhi = max(qhi, 0);
       if (qlo > qhi) qlo = qhi;
+      const bool full = qlo == 0 && qhi == 64;
       const uint32_t S_t = tmem + L::C_S + lane_off + 64 * g;
       const uint32_t DP_t = tmem + L::C_DP + lane_off + 64 * g;
 #pragma unroll 1
@@ -646,25 +671,32 @@ __global__ void __launch_bounds__(512, 1)
         ld32_nowait(DP_t + c * 32, pa);
         wait_ld();
         uint32_t wp[16], wd[16];
-        float dsv[32];
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
           const int qc = c * 32 + j;
-          const float4 l2 = *reinterpret_cast<const float4*>(&lds[qc]);  // (lse0, delta0, lse1, delta1)
-          float e0 = ex2(fmaf(__uint_as_float(sa[j]), p.scale_log2, -l2.x));
-          float e1 = ex2(fmaf(__uint_as_float(sa[j + 1]), p.scale_log2, -l2.z));
-          if (qc < qlo || qc >= qhi) e0 = 0.f;
-          if (qc + 1 < qlo || qc + 1 >= qhi) e1 = 0.f;
-          const float d0 = e0 * (__uint_as_float(pa[j]) - l2.y);
-          const float d1 = e1 * (__uint_as_float(pa[j + 1]) - l2.w);
+          const float4 l4 = *reinterpret_cast<const float4*>(lsm + (qc >> 1) * 4);  // broadcast
+          float x0, x1;
+          ffma2p(__uint_as_float(sa[j]), __uint_as_float(sa[j + 1]), sl2, l4.x, l4.y, x0, x1);
+          float e0 = ex2(x0), e1 = ex2(x1);
+          if (!full) {
+            if (qc < qlo || qc >= qhi) e0 = 0.f;
+            if (qc + 1 < qlo || qc + 1 >= qhi) e1 = 0.f;
+          }
+          float d0, d1;
+          sub_mul2(__uint_as_float(pa[j]), __uint_as_float(pa[j + 1]), l4.z, l4.w, e0, e1, d0, d1);
           wp[j >> 1] = pack_bf16(e0, e1);
           wd[j >> 1] = pack_bf16(d0, d1);
-          dsv[j] = d0;
-          dsv[j + 1] = d1;
         }
         st16(S_t + c * 16, wp);
         st16(DP_t + c * 16, wd);
-        store_row_chunk(ds, r, 2 * g + c, dsv);
+        // dS^T row r, query columns 64 g + 32 c .. +31 -> 128B-swizzled tile for the dQ MMA
+        const int chunk = g;  // 64-column chunk of the 128-query tile
+#pragma unroll
+        for (int u4 = 0; u4 < 4; ++u4) {
+          const int unit = c * 4 + u4;  // 16-byte unit (8 queries) within the 128-byte row
+          *reinterpret_cast<uint4*>(ds + chunk * 16384 + r * 128 + ((unit ^ (r & 7)) << 4)) =
+              make_uint4(wd[4 * u4], wd[4 * u4 + 1], wd[4 * u4 + 2], wd[4 * u4 + 3]);
+        }
       }
       wait_st();
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -766,16 +798,30 @@ __global__ void __launch_bounds__(512, 1)
 // Delta[bh, q] = sum_d dO[b, q, h, d] * O[b, q, h, d]
 template <int D>
 __global__ void delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dO,
+                             const __nv_bfloat16* __restrict__ o2, const __nv_bfloat16* __restrict__ dO2, int split,
                              float* __restrict__ delta, int B, int Sq, int H) {
   constexpr int LPR = D / 8;  // lanes per row
   const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t row = gid / LPR;  // row over (b, q, h) token-major
   const int sub = gid % LPR;
   const int64_t rows = (int64_t)B * Sq * H;
+  const int h = (int)(row % H);
+  const int64_t bq = row / H;
+  const int q = (int)(bq % Sq);
+  const int b = (int)(bq / Sq);
   float s = 0.f;
   if (row < rows) {
-    const uint4 a = *reinterpret_cast<const uint4*>(o + row * D + sub * 8);
-    const uint4 g = *reinterpret_cast<const uint4*>(dO + row * D + sub * 8);
+    int64_t off;
+    const __nv_bfloat16 *po = o, *pg = dO;
+    if (split > 0 && q >= split) {
+      off = (((int64_t)b * (Sq - split) + (q - split)) * H + h) * D;
+      po = o2;
+      pg = dO2;
+    } else {
+      off = (((int64_t)b * (split > 0 ? split : Sq) + q) * H + h) * D;
+    }
+    const uint4 a = *reinterpret_cast<const uint4*>(po + off + sub * 8);
+    const uint4 g = *reinterpret_cast<const uint4*>(pg + off + sub * 8);
     const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&a);
     const __nv_bfloat162* hg = reinterpret_cast<const __nv_bfloat162*>(&g);
 #pragma unroll
@@ -786,13 +832,7 @@ __global__ void delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfl
   }
 #pragma unroll
   for (int off = LPR / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  if (row < rows && sub == 0) {
-    const int h = row % H;
-    const int64_t bq = row / H;
-    const int q = bq % Sq;
-    const int b = bq / Sq;
-    delta[((int64_t)b * H + h) * Sq + q] = s;
-  }
+  if (row < rows && sub == 0) delta[((int64_t)b * H + h) * Sq + q] = s;
 }
 
 __global__ void dq_finalize_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq, int64_t n4,
@@ -853,7 +893,7 @@ static int map4_tok(CUtensorMap* m, const void* ptr, int B, int S, int H, int D)
 
 template <int D>
 static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
-                  Params p, int grid, cudaStream_t st) {
+                  const CUtensorMap& mdo2, Params p, int grid, cudaStream_t st) {
   static bool set = false;
   if (!set) {
     const cudaError_t e =
@@ -861,13 +901,13 @@ static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMa
     if (e != cudaSuccess) return (int)e;
     set = true;
   }
-  fmha_bwd_kernel<D><<<grid, NUM_THREADS, Lay<D>::BYTES + 1024, st>>>(mq, mk, mv, mdo, p);
+  fmha_bwd_kernel<D><<<grid, NUM_THREADS, Lay<D>::BYTES + 1024, st>>>(mq, mk, mv, mdo, mdo2, p);
   return (int)cudaGetLastError();
 }
 
 template <int D>
 static int launch2(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
-                   const CUtensorMap& mdq, Params p, int grid, cudaStream_t st) {
+                   const CUtensorMap& mdo2, const CUtensorMap& mdq, Params p, int grid, cudaStream_t st) {
   using L = v2::Lay2<D>;
   static bool set = false;
   if (!set) {
@@ -876,7 +916,7 @@ static int launch2(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
     if (e != cudaSuccess) return (int)e;
     set = true;
   }
-  v2::fmha_bwd2_kernel<D><<<grid, 512, L::BYTES + 1024, st>>>(mq, mk, mv, mdo, mdq, p);
+  v2::fmha_bwd2_kernel<D><<<grid, 512, L::BYTES + 1024, st>>>(mq, mk, mv, mdo, mdo2, mdq, p);
   return (int)cudaGetLastError();
 }
 
@@ -884,24 +924,32 @@ static int launch2(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
 
 // q [B,H,Sq,D], k/v [B,H,Skv,D], o/do [B,Sq,H,D], lse [B,H,Sq]; outputs dq [B,H,Sq,D], dk/dv [B,H,Skv,D].
 // Scratch: delta [B*H*Sq] fp32 and dq_acc [B*H*Sq*D] fp32 (dq_acc must be zero on entry).
+// o2 / dO2 / split: rows q >= split of O and dO live in separate [B, Sq - split, H, D] tensors
+// (split % 128 == 0); split = 0: single O / dO.
 extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const void* o, const void* dO,
-                           const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_acc, int B, int H,
-                           int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream, int version) {
+                           const void* o2, const void* dO2, int split, const float* lse, void* dq, void* dk, void* dv,
+                           float* delta, float* dq_acc, int B, int H, int Sq, int Skv, int D, float scale, int causal,
+                           cudaStream_t stream, int version) {
   using namespace vo_fbwd;
   if (D != 64 && D != 128) return -1;
   const int64_t rows = (int64_t)B * Sq * H;
   const int64_t threads = rows * (D / 8);
   if (D == 64)
     delta_kernel<64><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
-        (const __nv_bfloat16*)o, (const __nv_bfloat16*)dO, delta, B, Sq, H);
+        (const __nv_bfloat16*)o, (const __nv_bfloat16*)dO, (const __nv_bfloat16*)o2, (const __nv_bfloat16*)dO2, split,
+        delta, B, Sq, H);
   else
     delta_kernel<128><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
-        (const __nv_bfloat16*)o, (const __nv_bfloat16*)dO, delta, B, Sq, H);
+        (const __nv_bfloat16*)o, (const __nv_bfloat16*)dO, (const __nv_bfloat16*)o2, (const __nv_bfloat16*)dO2, split,
+        delta, B, Sq, H);
   CUtensorMap mq, mk, mv, mdo;
   int r = map3(&mq, q, B * H, Sq, D);
   if (!r) r = map3(&mk, k, B * H, Skv, D);
   if (!r) r = map3(&mv, v, B * H, Skv, D);
-  if (!r) r = map4_tok(&mdo, dO, B, Sq, H, D);
+  if (split < 0 || split >= Sq || split % 128 || (split > 0 && (!o2 || !dO2))) return -3;
+  CUtensorMap mdo2;
+  if (!r) r = map4_tok(&mdo, dO, B, split > 0 ? split : Sq, H, D);
+  if (!r) r = split > 0 ? map4_tok(&mdo2, dO2, B, Sq - split, H, D) : map4_tok(&mdo2, dO, B, Sq, H, D);
   if (r) return r;
   Params p;
   p.Sq = Sq;
@@ -916,15 +964,17 @@ extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const vo
   p.dq_acc = dq_acc;
   p.dk = (__nv_bfloat16*)dk;
   p.dv = (__nv_bfloat16*)dv;
+  p.split = split;
   const int grid = p.nkv_tiles * B * H;
   if (version == 2) {
     CUtensorMap mdq;
     if ((r = map3_f32(&mdq, dq_acc, B * H, Sq, D))) return r;
-    r = D == 64 ? launch2<64>(mq, mk, mv, mdo, mdq, p, grid, stream)
-                : launch2<128>(mq, mk, mv, mdo, mdq, p, grid, stream);
+    r = D == 64 ? launch2<64>(mq, mk, mv, mdo, mdo2, mdq, p, grid, stream)
+                : launch2<128>(mq, mk, mv, mdo, mdo2, mdq, p, grid, stream);
   }
   else {
-    r = D == 64 ? launch<64>(mq, mk, mv, mdo, p, grid, stream) : launch<128>(mq, mk, mv, mdo, p, grid, stream);
+    r = D == 64 ? launch<64>(mq, mk, mv, mdo, mdo2, p, grid, stream)
+                : launch<128>(mq, mk, mv, mdo, mdo2, p, grid, stream);
   }
   if (r) return r;
   const int64_t n4 = (int64_t)B * H * Sq * D / 4;

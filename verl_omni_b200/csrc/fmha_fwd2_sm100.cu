@@ -169,9 +169,18 @@ struct Params {
   int Sq, Skv, H, npairs;
   float scale_log2;  // softmax scale * log2(e)
   int causal;
-  __nv_bfloat16* o;  // [B, Sq, H, D]
-  float* lse;        // [B*H, Sq] natural log
+  __nv_bfloat16* o;   // [B, Sq, H, D], or [B, split, H, D] when split > 0
+  __nv_bfloat16* o2;  // [B, Sq - split, H, D] (split > 0): rows q >= split
+  int split;
+  float* lse;         // [B*H, Sq] natural log
 };
+
+// token-major output row of query q (head h, batch b): one buffer, or split at `split` into two
+__device__ __forceinline__ __nv_bfloat16* out_row(const Params& p, int b, int q, int h, int D) {
+  if (p.split > 0 && q >= p.split) return p.o2 + (((int64_t)b * (p.Sq - p.split) + (q - p.split)) * p.H + h) * D;
+  const int rows = p.split > 0 ? p.split : p.Sq;
+  return p.o + (((int64_t)b * rows + q) * p.H + h) * D;
+}
 
 template <int D>
 struct Cfg {
@@ -311,7 +320,7 @@ __device__ __forceinline__ void softmax_split2(const Params& p, uint32_t tmem, i
     const float inv = lt > 0.f ? 1.f / lt : 0.f;
     const int bb = bh / p.H, h = bh % p.H;
     const bool row_ok = q < p.Sq;
-    __nv_bfloat16* dst = p.o + (((int64_t)bb * p.Sq + q) * p.H + h) * D + hf * (D / 2);
+    __nv_bfloat16* dst = out_row(p, bb, q, h, D) + hf * (D / 2);
 #pragma unroll
     for (int c = 0; c < D / 64; ++c) {
       uint32_t o[32];
@@ -604,7 +613,7 @@ __global__ void __launch_bounds__(fwd_threads<SPLIT>(), 1)
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const int bb = bh / p.H, h = bh % p.H;
       const bool row_ok = q < p.Sq;
-      __nv_bfloat16* dst = p.o + (((int64_t)bb * p.Sq + q) * p.H + h) * D;
+      __nv_bfloat16* dst = out_row(p, bb, q, h, D);
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
@@ -674,8 +683,8 @@ static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMa
   return (int)cudaGetLastError();
 }
 
-static int fwd2_impl(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int Sq, int Skv,
-                     int D, float scale, int causal, cudaStream_t stream, int split) {
+static int fwd2_impl(const void* q, const void* k, const void* v, void* o, void* o2, int out_split, float* lse, int B,
+                     int H, int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream, int split) {
   if (D != 64 && D != 128) return -1;
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15)
     return -2;
@@ -692,6 +701,9 @@ static int fwd2_impl(const void* q, const void* k, const void* v, void* o, float
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal;
   p.o = reinterpret_cast<__nv_bfloat16*>(o);
+  p.o2 = reinterpret_cast<__nv_bfloat16*>(o2);
+  p.split = out_split;
+  if (out_split < 0 || out_split >= Sq || (out_split > 0 && !o2)) return -3;
   p.lse = lse;
   const long long grid = (long long)p.npairs * B * H;
   if (grid == 0) return 0;
@@ -704,15 +716,16 @@ static int fwd2_impl(const void* q, const void* k, const void* v, void* o, float
 
 }  // namespace vo_fmha2
 
-extern "C" int vo_fmha_fwd2(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int Sq,
-                            int Skv, int D, float scale, int causal, cudaStream_t stream) {
-  return vo_fmha2::fwd2_impl(q, k, v, o, lse, B, H, Sq, Skv, D, scale, causal, stream, 1);
+// o2 / out_split: rows q >= out_split go to o2 ([B, Sq - out_split, H, D]); out_split = 0: one output
+extern "C" int vo_fmha_fwd2(const void* q, const void* k, const void* v, void* o, void* o2, int out_split, float* lse,
+                            int B, int H, int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream) {
+  return vo_fmha2::fwd2_impl(q, k, v, o, o2, out_split, lse, B, H, Sq, Skv, D, scale, causal, stream, 1);
 }
 
 // two softmax warpgroups per query tile (576 threads)
-extern "C" int vo_fmha_fwd3(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int Sq,
-                            int Skv, int D, float scale, int causal, cudaStream_t stream) {
-  return vo_fmha2::fwd2_impl(q, k, v, o, lse, B, H, Sq, Skv, D, scale, causal, stream, 2);
+extern "C" int vo_fmha_fwd3(const void* q, const void* k, const void* v, void* o, void* o2, int out_split, float* lse,
+                            int B, int H, int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream) {
+  return vo_fmha2::fwd2_impl(q, k, v, o, o2, out_split, lse, B, H, Sq, Skv, D, scale, causal, stream, 2);
 }
 
 extern "C" int vo_fmha_fwd2_error(int reset) {

@@ -81,24 +81,42 @@ __global__ void __launch_bounds__(kThreads) bwd_prep_kernel(const __nv_bfloat16*
   }
 }
 
-// db[n] (+)= sum over all chunks; dgate[b, n] = sum over sample b's chunks (bf16 out)
-__global__ void bwd_prep_reduce_kernel(const float* __restrict__ part_db, const float* __restrict__ part_dg, int N,
-                                       int B, int cps, float* __restrict__ db, int db_accumulate,
-                                       __nv_bfloat16* __restrict__ dgate) {
-  const int n = blockIdx.x * blockDim.x + threadIdx.x;
-  if (n >= N) return;
+// db[n] (+)= sum over all chunks; dgate[b, n] = sum over sample b's chunks (bf16 out).
+// Block = 32 columns x 8 chunk lanes: lane rl sums chunks rl, rl + 8, ... of each sample, then the
+// eight partial sums are added in a fixed order through shared memory (deterministic).
+constexpr int kRedCols = 32, kRedLanes = 8;
+__global__ void __launch_bounds__(kRedCols* kRedLanes)
+    bwd_prep_reduce_kernel(const float* __restrict__ part_db, const float* __restrict__ part_dg, int N, int B,
+                           int cps, float* __restrict__ db, int db_accumulate, __nv_bfloat16* __restrict__ dgate) {
+  __shared__ float red[2][kRedLanes][kRedCols];
+  const int cx = threadIdx.x % kRedCols, rl = threadIdx.x / kRedCols;
+  const int n = blockIdx.x * kRedCols + cx;
   float tot = 0.f;
   for (int b = 0; b < B; ++b) {
     float s = 0.f, sg = 0.f;
-    for (int j = 0; j < cps; ++j) {
-      const int64_t p = (int64_t)(b * cps + j) * N + n;
-      if (part_db) s += part_db[p];
-      if (part_dg) sg += part_dg[p];
+    if (n < N) {
+      for (int j = rl; j < cps; j += kRedLanes) {
+        const int64_t p = (int64_t)(b * cps + j) * N + n;
+        if (part_db) s += part_db[p];
+        if (part_dg) sg += part_dg[p];
+      }
     }
-    tot += s;
-    if (dgate) dgate[(int64_t)b * N + n] = __float2bfloat16_rn(sg);
+    red[0][rl][cx] = s;
+    red[1][rl][cx] = sg;
+    __syncthreads();
+    if (rl == 0 && n < N) {
+      float a = 0.f, c = 0.f;
+#pragma unroll
+      for (int i = 0; i < kRedLanes; ++i) {
+        a += red[0][i][cx];
+        c += red[1][i][cx];
+      }
+      tot += a;
+      if (dgate) dgate[(int64_t)b * N + n] = __float2bfloat16_rn(c);
+    }
+    __syncthreads();
   }
-  if (db) db[n] = db_accumulate ? db[n] + tot : tot;
+  if (rl == 0 && n < N && db) db[n] = db_accumulate ? db[n] + tot : tot;
 }
 
 template <int MODE, bool DB>
@@ -174,7 +192,7 @@ std::vector<torch::Tensor> linear_bwd_prep(torch::Tensor dy, c10::optional<torch
   else launch_prep<2, false>(grid, cbf(dy), sp, gp, gate_ld, o, a, g, iN, iS, cps);
   count_launch();
   if (want_db || mode == 2) {
-    bwd_prep_reduce_kernel<<<(unsigned)((N + 127) / 128), 128, 0, stream()>>>(
+    bwd_prep_reduce_kernel<<<(unsigned)((N + kRedCols - 1) / kRedCols), kRedCols * kRedLanes, 0, stream()>>>(
         a, g, iN, (int)Bs, cps, want_db ? db->data_ptr<float>() : nullptr, db_accumulate ? 1 : 0,
         mode == 2 ? reinterpret_cast<__nv_bfloat16*>(dgate.data_ptr<at::BFloat16>()) : nullptr);
     count_launch();

@@ -17,7 +17,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from verl_omni_b200.models.layers import Linear, RMSWeight, TimestepMLP, patchify, rope_nd, timestep_embedding, unpatchify
-from verl_omni_b200.ops.attention import attention
+from verl_omni_b200.ops.attention import attention, attention_split
 from verl_omni_b200.ops.norm import adaln_layernorm, qk_norm_split_into
 
 
@@ -74,10 +74,10 @@ class DoubleBlock(nn.Module):
                                      self.img_norm_q.weight, self.img_norm_k.weight, Si, 0, rope=rope, eps=self.eps)
         q, k, v = qk_norm_split_into(q, k, v, self.txt_qkv(ht).reshape(B * St, 3 * D), self.txt_norm_q.weight,
                                      self.txt_norm_k.weight, St, Si, rope=rope, eps=self.eps)
-        o = attention(q, k, v)
+        o_img, o_txt = attention_split(q, k, v, Si)
         vi, vt = mi.view(B, 6, D), mt.view(B, 6, D)
-        x = self.img_out(o[:, :Si].contiguous(), epilogue="gate_res", gate=vi[:, 2], res=x, S=Si)
-        c = self.txt_out(o[:, Si:].contiguous(), epilogue="gate_res", gate=vt[:, 2], res=c, S=St)
+        x = self.img_out(o_img, epilogue="gate_res", gate=vi[:, 2], res=x, S=Si)
+        c = self.txt_out(o_txt, epilogue="gate_res", gate=vt[:, 2], res=c, S=St)
         x = self.img_mlp_2(self.img_mlp_1(adaln_layernorm(x, mi, 3, 4, 6, self.eps), epilogue="gelu"),
                            epilogue="gate_res", gate=vi[:, 5], res=x, S=Si)
         c = self.txt_mlp_2(self.txt_mlp_1(adaln_layernorm(c, mt, 3, 4, 6, self.eps), epilogue="gelu"),

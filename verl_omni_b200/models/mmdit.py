@@ -24,7 +24,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from verl_omni_b200.models.layers import Linear, RMSWeight, TimestepMLP, patchify, sincos_2d, timestep_embedding, unpatchify
-from verl_omni_b200.ops.attention import attention
+from verl_omni_b200.ops.attention import attention, attention_split
 from verl_omni_b200.ops.norm import adaln_layernorm, qk_norm_split_into
 
 
@@ -104,8 +104,7 @@ class JointBlock(nn.Module):
         q, k, v = qk_norm_split_into(q, k, v, qkv, self.norm_q.weight, self.norm_k.weight, Si, 0, eps=self.eps)
         q, k, v = qk_norm_split_into(q, k, v, qkvc, self.norm_added_q.weight, self.norm_added_k.weight, St, Si,
                                      eps=self.eps)
-        o = attention(q, k, v)  # [B, S, D]
-        o_img = o[:, :Si].contiguous()
+        o_img, o_txt = attention_split(q, k, v, Si)  # [B, Si, D], [B, St, D]
         gate_msa = mod.view(B, self.n_mod, D)[:, 2]
         x_new = self.to_out(o_img, epilogue="gate_res", gate=gate_msa, res=x, S=Si)
         if self.dual:
@@ -124,7 +123,6 @@ class JointBlock(nn.Module):
         x = self.ff_2(u, epilogue="gate_res", gate=mod.view(B, self.n_mod, D)[:, 5], res=x, S=Si)
         if self.cpo:
             return x, None
-        o_txt = o[:, Si:].contiguous()
         mc = modc.view(B, self.n_mod_c, D)
         c = self.to_add_out(o_txt, epilogue="gate_res", gate=mc[:, 2], res=c, S=St)
         hcm = adaln_layernorm(c, modc, 3, 4, self.n_mod_c, self.eps)

@@ -54,6 +54,45 @@ class _FMHA(torch.autograd.Function):
         return dq, dk, dv, None, None
 
 
+class _FMHASplit(torch.autograd.Function):
+    """Joint attention whose query rows [0, split) and [split, S) land in two separate outputs."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, causal, scale, split):
+        o_a, lse, o_b = ext().fmha_fwd(q, k, v, causal, scale, _FWD_VERSION, split)
+        ctx.save_for_backward(q, k, v, o_a, o_b, lse)
+        ctx.meta = (causal, scale, split)
+        B, _, H, D = o_a.shape
+        return o_a.view(B, split, H * D), o_b.view(B, -1, H * D)
+
+    @staticmethod
+    def backward(ctx, do_a, do_b):
+        q, k, v, o_a, o_b, lse = ctx.saved_tensors
+        causal, scale, split = ctx.meta
+        do_a = torch.zeros_like(o_a) if do_a is None else do_a.contiguous().view_as(o_a)
+        do_b = torch.zeros_like(o_b) if do_b is None else do_b.contiguous().view_as(o_b)
+        dq, dk, dv = ext().fmha_bwd(q, k, v, o_a, lse, do_a, causal, scale, _BWD_VERSION, o2=o_b, dO2=do_b,
+                                    split=split)
+        return dq, dk, dv, None, None, None
+
+
+def attention_split(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, split: int, causal: bool = False,
+                    scale: Optional[float] = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Joint attention returning ``(o[:, :split], o[:, split:])`` as two ``[B, *, H*Dh]`` tensors.
+
+    The tcgen05 forward writes each query row straight into its half (the image / text streams of an
+    MMDiT block feed separate output projections), so no slice copies are made; the backward reads
+    the two output gradients in place.  Needs ``split`` a multiple of 128 on the native path.
+    """
+    B, H, S, Dh = q.shape
+    scale = scale if scale is not None else 1.0 / math.sqrt(Dh)
+    if (q.is_cuda and _native() and Dh in (64, 128) and q.dtype == torch.bfloat16 and _FWD_VERSION >= 2
+            and 0 < split < S and split % 128 == 0):
+        return _FMHASplit.apply(q, k, v, causal, scale, int(split))
+    o = attention(q, k, v, causal, scale)
+    return o[:, :split].contiguous(), o[:, split:].contiguous()
+
+
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
               scale: Optional[float] = None) -> torch.Tensor:
     """softmax(q k^T * scale) v over [B, H, S, Dh]; returns [B, S, H*Dh]."""

@@ -59,30 +59,43 @@ class SymmetricBuffer:
         self.numel, self.dtype, self.device, self.group = int(numel), dtype, device, group
         self.world, self.rank = D.world_size(group), D.rank(group)
         nbytes = self.numel * torch.empty((), dtype=dtype).element_size()
+        self.ptr, handle, err = None, None, None
+        self.peer_ptrs = []
+        self._closed = True
         with torch.cuda.device(device):
-            self.ptr = _ext().symm_malloc(nbytes)
-            handle = _ext().ipc_get_handle(self.ptr)
-            handles = D.all_gather_object(bytes(handle.numpy().tobytes()), group)
-            self.peer_ptrs = []
+            try:  # local steps first: a failure here must not leave peers waiting in the exchange
+                self.ptr = _ext().symm_malloc(nbytes)
+                handle = bytes(_ext().ipc_get_handle(self.ptr).numpy().tobytes())
+            except Exception as e:  # noqa: BLE001 - re-raised after the collective
+                err = e
+            handles = D.all_gather_object(handle, group)
+            if err is not None or any(h is None for h in handles):
+                if self.ptr is not None:
+                    _ext().symm_free(self.ptr)
+                raise err or RuntimeError("a peer could not export its symmetric buffer")
+            self._closed = False
             for r, h in enumerate(handles):
                 if r == self.rank:
                     self.peer_ptrs.append(self.ptr)
                 else:
                     self.peer_ptrs.append(_ext().ipc_open(torch.frombuffer(bytearray(h), dtype=torch.uint8)))
         self.tensor = _ext().tensor_from_ptr(self.ptr, self.numel, _DTYPE_CODE[dtype], device.index or 0)
-        self._closed = False
 
-    def close(self) -> None:
-        """Unmap peers and free the local allocation (collective: every rank calls it)."""
+    def close(self, collective: bool = True) -> None:
+        """Unmap peers and free the local allocation.  ``collective``: every rank calls it, and barriers
+        keep a peer's memory mapped until no rank can still touch it; ``False`` only before any kernel
+        has used the buffer (set-up failure paths)."""
         if self._closed:
             return
         self._closed = True
         torch.cuda.synchronize(self.device)
-        D.barrier(self.group)
+        if collective:
+            D.barrier(self.group)
         for r, p in enumerate(self.peer_ptrs):
             if r != self.rank:
                 _ext().ipc_close(p)
-        D.barrier(self.group)
+        if collective:
+            D.barrier(self.group)
         _ext().symm_free(self.ptr)
 
 

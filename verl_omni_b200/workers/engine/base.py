@@ -74,11 +74,8 @@ class FlatParams:
         self.device, self.dtype = device, dtype
         self.symm_flat = self.symm_grad = None
         if symmetric:
-            from verl_omni_b200.parallel.symm_mem import SymmetricBuffer
-
-            # peer-mapped buffers: the fused optimizer step reads peers' grads / writes peers' weights
-            self.symm_flat = SymmetricBuffer(self.padded, dtype, device, group)
-            self.symm_grad = SymmetricBuffer(self.padded, torch.float32, device, group)
+            self._try_symmetric(dtype, device, group)
+        if self.symm_flat is not None:
             self.flat, self.main_grad = self.symm_flat.tensor, self.symm_grad.tensor
         else:
             self.flat = torch.zeros(self.padded, dtype=dtype, device=device)
@@ -105,6 +102,30 @@ class FlatParams:
             for k, b in list(m._buffers.items()):
                 if b is not None:
                     m._buffers[k] = b.to(device=device)
+
+    def _try_symmetric(self, dtype, device, group) -> None:
+        """Peer-mapped flat buffers (the fused optimizer step reads peers' grads and writes peers'
+        weights).  Every rank must succeed: the outcome is agreed collectively and, if any rank could not
+        map its peers, all ranks fall back to ordinary buffers and NCCL collectives."""
+        from verl_omni_b200.parallel.symm_mem import SymmetricBuffer
+
+        bufs, err = [], None
+        try:
+            bufs.append(SymmetricBuffer(self.padded, dtype, device, group))
+            bufs.append(SymmetricBuffer(self.padded, torch.float32, device, group))
+        except Exception as e:  # noqa: BLE001 - agreed on below, reported by rank
+            err = e
+        ok = torch.tensor([0 if err is not None else 1], dtype=torch.int32, device=device)
+        D.all_reduce(ok, op=torch.distributed.ReduceOp.MIN, group=group)
+        if int(ok.item()) == 1:
+            self.symm_flat, self.symm_grad = bufs
+            return
+        for b in bufs:
+            b.close(collective=False)
+        if err is not None:
+            import warnings
+
+            warnings.warn(f"symmetric memory unavailable, using NCCL collectives: {err}")
 
     @staticmethod
     def _accumulate(p: torch.Tensor) -> None:
