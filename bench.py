@@ -161,11 +161,17 @@ def main() -> None:
     if args.profile_step:
         from torch.profiler import ProfilerActivity, profile
 
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA], record_shapes=True) as prof:
             trainer.step()
             torch.cuda.synchronize()
         if info.rank == 0:
             print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=40, max_name_column_width=70))
+            # torch-level ops (copies, elementwise) by input shape: where the non-kernel device time goes
+            ka = [e for e in prof.key_averages(group_by_input_shape=True) if e.key.startswith("aten::")]
+            ka.sort(key=lambda e: -e.device_time_total)
+            print("aten ops by input shape (device time, calls):")
+            for e in ka[:25]:
+                print(f"  {e.device_time_total / 1e3:10.1f} ms  {e.count:7d}  {e.key:28s} {str(e.input_shapes)[:110]}")
         D.destroy()
         return
     # ----------------------------------------------------------- device-timed region

@@ -56,3 +56,31 @@ def test_tiny_flowgrpo_gloo_world2(tmp_path):
     assert os.path.exists(tmp_path / "global_step_2" / "actor" / "model_world_size_2_rank_1.pt")
     assert os.path.exists(tmp_path / "global_step_2" / "actor" / "fsdp_config.json")
     assert (tmp_path / "latest_checkpointed_iteration.txt").read_text() == "2"
+
+
+def _hsdp(rank, world, outdir):
+    from verl_omni_b200.parallel import dist as D
+    from verl_omni_b200.trainer.diffusion.flow_grpo_trainer import PolicyGradientTrainer
+    from verl_omni_b200.utils.config import load_config
+
+    cfg = load_config("diffusion_trainer", OVR + [f"trainer.default_local_dir={outdir}", "trainer.total_training_steps=1",
+                                                  "trainer.save_freq=1", "trainer.resume_mode=disable",
+                                                  "actor_rollout_ref.actor.fsdp_config.fsdp_size=2"])
+    t = PolicyGradientTrainer(cfg)
+    eng = t.actor.engine
+    assert eng.world == 2 and eng.n_replicas == 2
+    t.fit()
+    # every rank (both shard groups, both replicas) ends with identical full weights
+    ws = D.all_gather_object(eng.flat.flat.clone())
+    for w in ws[1:]:
+        assert torch.equal(ws[0], w)
+
+
+def test_hsdp_world4_fsdp2(tmp_path):
+    """HSDP (2 shard groups x 2 replicas) on 4 gloo ranks: replicas stay identical, checkpoint written once."""
+    run_ranks(_hsdp, world=4, args=(str(tmp_path),))
+    step_dir = [d for d in os.listdir(tmp_path) if d.startswith("global_step")]
+    assert step_dir
+    actor = os.path.join(tmp_path, step_dir[0], "actor")
+    files = sorted(os.listdir(actor))
+    assert "model_world_size_2_rank_0.pt" in files and "model_world_size_2_rank_1.pt" in files

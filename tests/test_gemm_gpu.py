@@ -94,3 +94,35 @@ def test_linear_layer_autograd_native_vs_torch():
     assert _rel(y, yr) < 2e-2
     assert _rel(x.grad, xr.grad) < 3e-2
     assert w.grad is None and _rel(w.main_grad, wr.grad) < 3e-2
+
+
+@pytest.mark.parametrize("epilogue", ["none", "gelu", "gate_res"])
+def test_fused_lora_linear_matches_unfused(E, epilogue):
+    """Low-rank term folded into the base GEMM (extension operands): forward and adapter/input grads."""
+    from verl_omni_b200.ops.linear import lora_linear
+
+    torch.manual_seed(7)
+    Bs, S, K, N, r, s = 2, 160, 256, 384, 16, 2.0
+    x = torch.randn(Bs, S, K, device="cuda").bfloat16().requires_grad_(True)
+    w = (torch.randn(N, K, device="cuda") / K ** 0.5).bfloat16()
+    b = torch.randn(N, device="cuda").bfloat16()
+    A = (torch.randn(r, K, device="cuda") / K ** 0.5).bfloat16().requires_grad_(True)
+    B = (torch.randn(N, r, device="cuda") * 0.1).bfloat16().requires_grad_(True)
+    gate = torch.randn(Bs, N, device="cuda").bfloat16()
+    res = torch.randn(Bs, S, N, device="cuda").bfloat16()
+    kw = dict(gate=gate, res=res, S=S) if epilogue == "gate_res" else {}
+    y = lora_linear(x, w, b, A, B, s, epilogue=epilogue, **kw)
+    g = torch.randn_like(y)
+    y.backward(g)
+    xr, Ar, Br = (t.detach().float().requires_grad_(True) for t in (x, A, B))
+    lin = xr @ w.float().t() + b.float() + s * (xr @ Ar.t()) @ Br.t()
+    if epilogue == "gelu":
+        yr = torch.nn.functional.gelu(lin, approximate="tanh")
+    elif epilogue == "gate_res":
+        yr = res.float() + lin * gate.float()[:, None]
+    else:
+        yr = lin
+    yr.backward(g.float())
+    assert _rel(y, yr) < 2e-2
+    for a, ref in ((x, xr), (A, Ar), (B, Br)):
+        assert _rel(a.grad, ref.grad) < 3e-2, (a.shape, _rel(a.grad, ref.grad))

@@ -71,3 +71,49 @@ def test_cli_entrypoints(capsys):
     assert "torch" in diagnose.collect()
     print_cfg.main(["actor_rollout_ref.rollout.n=5"])
     assert "n: 5" in capsys.readouterr().out
+
+
+def test_non_diffusers_model_base_roundtrip(tmp_path):
+    from dataclasses import dataclass
+
+    import torch.nn as nn
+
+    from verl_omni_b200.pipelines.non_diffusers_model_base import NonDiffusersModelBase
+
+    @dataclass
+    class Cfg:
+        dim: int = 8
+        layers: int = 2
+
+    class Block(nn.Module):
+        def __init__(self, d):
+            super().__init__()
+            self.lin = nn.Linear(d, d)
+
+        def forward(self, x):
+            return torch.relu(self.lin(x))
+
+    class Toy(NonDiffusersModelBase):
+        config_class = Cfg
+        _no_split_modules = ("Block",)
+        supports_gradient_checkpointing = True
+
+        def __init__(self, config):
+            super().__init__(config)
+            self.blocks = nn.ModuleList([Block(config.dim) for _ in range(config.layers)])
+
+        def forward(self, x):
+            for b in self.blocks:
+                x = self.maybe_checkpoint(b, x)
+            return x
+
+    torch.manual_seed(0)
+    m = Toy(Cfg())
+    m.save_pretrained(str(tmp_path))
+    m2 = Toy.from_pretrained(str(tmp_path))
+    x = torch.randn(3, 8, requires_grad=True)
+    torch.testing.assert_close(m(x), m2(x))
+    assert len(m.no_split_module_instances()) == 2
+    m2.enable_gradient_checkpointing()
+    m2(x).sum().backward()
+    assert x.grad is not None

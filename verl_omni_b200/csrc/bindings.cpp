@@ -38,8 +38,10 @@ void adamw_flat(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor
                 double lr, double b1, double b2, double eps, double wd, int64_t step, double max_norm,
                 c10::optional<torch::Tensor> sq_norm_t, double grad_scale);
 std::vector<torch::Tensor> gemm_fwd(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> b, int64_t epi,
-                                    c10::optional<torch::Tensor> gate, c10::optional<torch::Tensor> res, int64_t S);
-torch::Tensor gemm_dgrad(torch::Tensor dy, torch::Tensor w);
+                                    c10::optional<torch::Tensor> gate, c10::optional<torch::Tensor> res, int64_t S,
+                                    c10::optional<torch::Tensor> ext_a, c10::optional<torch::Tensor> ext_b);
+torch::Tensor gemm_dgrad(torch::Tensor dy, torch::Tensor w, c10::optional<torch::Tensor> ext_a,
+                         c10::optional<torch::Tensor> ext_b);
 void gemm_wgrad(torch::Tensor dy, torch::Tensor x, torch::Tensor out, bool accumulate);
 torch::Tensor gelu_tanh_bwd(torch::Tensor dy, torch::Tensor pre);
 int64_t gemm_error(bool reset);
@@ -81,8 +83,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_rmsnorm_bwd", &vo::qk_rmsnorm_bwd);
   m.def("sq_norm", &vo::sq_norm);
   m.def("adamw_flat", &vo::adamw_flat);
-  m.def("gemm_fwd", &vo::gemm_fwd);
-  m.def("gemm_dgrad", &vo::gemm_dgrad);
+  m.def("gemm_fwd", &vo::gemm_fwd, py::arg("x"), py::arg("w"), py::arg("b"), py::arg("epi"), py::arg("gate"),
+        py::arg("res"), py::arg("S"), py::arg("ext_a") = py::none(), py::arg("ext_b") = py::none());
+  m.def("gemm_dgrad", &vo::gemm_dgrad, py::arg("dy"), py::arg("w"), py::arg("ext_a") = py::none(),
+        py::arg("ext_b") = py::none());
   m.def("gemm_wgrad", &vo::gemm_wgrad);
   m.def("gelu_tanh_bwd", &vo::gelu_tanh_bwd);
   m.def("gemm_error", &vo::gemm_error);

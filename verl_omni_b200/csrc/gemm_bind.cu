@@ -20,6 +20,9 @@ struct EpiParams {
 extern "C" int vo_gemm_launch(const void* A, const void* B, int M, int N, int K, int64_t lda, int64_t ldb, int a_mn,
                               int b_mn, int splits, vo_gemm::EpiParams ep, cudaStream_t stream);
 extern "C" int vo_gemm_error(int reset);
+extern "C" int vo_gemm_launch_ext(const void* A, const void* B, const void* A2, const void* B2, int M, int N, int K,
+                                  int K2, int64_t lda, int64_t ldb, int64_t lda2, int64_t ldb2, int a_mn, int b_mn,
+                                  int splits, vo_gemm::EpiParams ep, cudaStream_t stream);
 
 namespace vo {
 namespace {
@@ -52,8 +55,11 @@ __global__ void gelu_tanh_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const
 
 // y = x W^T (+ b) with epilogue; returns (out, saved) where saved is the GELU pre-activation or
 // the GATE_RES linear output (undefined tensor otherwise).
+// ext_a / ext_b (optional): extra reduction operands, out = x W^T + ext_a ext_b^T (+ epilogue) -- the
+// fused low-rank path: ext_a = x A_lora^T [M, r], ext_b = scale * B_lora [N, r].
 std::vector<torch::Tensor> gemm_fwd(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> b, int64_t epi,
-                                    c10::optional<torch::Tensor> gate, c10::optional<torch::Tensor> res, int64_t S) {
+                                    c10::optional<torch::Tensor> gate, c10::optional<torch::Tensor> res, int64_t S,
+                                    c10::optional<torch::Tensor> ext_a, c10::optional<torch::Tensor> ext_b) {
   VO_CHECK_INPUT(x);
   VO_CHECK_INPUT(w);
   TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && w.scalar_type() == torch::kBFloat16, "bf16 GEMM operands");
@@ -82,13 +88,28 @@ std::vector<torch::Tensor> gemm_fwd(torch::Tensor x, torch::Tensor w, c10::optio
     TORCH_CHECK(res->is_contiguous() && res->numel() == M * N, "res must be contiguous [M, N]");
     ep.res = bf(*res);
   }
-  check_rc(vo_gemm_launch(x.data_ptr(), w.data_ptr(), (int)M, (int)N, (int)K, K, K, 0, 0, 1, ep, stream()), "fwd");
+  const void *a2 = nullptr, *b2 = nullptr;
+  int64_t K2 = 0;
+  if (ext_a.has_value() && ext_a->defined()) {
+    TORCH_CHECK(ext_b.has_value() && ext_b->defined(), "ext_a needs ext_b");
+    VO_CHECK_INPUT((*ext_a));
+    VO_CHECK_INPUT((*ext_b));
+    K2 = ext_a->size(1);
+    TORCH_CHECK(ext_a->size(0) == M && ext_b->size(0) == N && ext_b->size(1) == K2 && K2 % 8 == 0,
+                "extension operands must be [M, r] and [N, r] with r % 8 == 0");
+    a2 = ext_a->data_ptr();
+    b2 = ext_b->data_ptr();
+  }
+  check_rc(vo_gemm_launch_ext(x.data_ptr(), w.data_ptr(), a2, b2, (int)M, (int)N, (int)K, (int)K2, K, K, K2, K2, 0, 0,
+                              1, ep, stream()),
+           "fwd");
   count_launch();
   return {out, saved};
 }
 
-// dX[M, K] = dY[M, N] W[N, K]   (B operand MN-major)
-torch::Tensor gemm_dgrad(torch::Tensor dy, torch::Tensor w) {
+// dX[M, K] = dY[M, N] W[N, K] (+ ext_a[M, r] ext_b[r, K])   (B operands MN-major)
+torch::Tensor gemm_dgrad(torch::Tensor dy, torch::Tensor w, c10::optional<torch::Tensor> ext_a,
+                         c10::optional<torch::Tensor> ext_b) {
   VO_CHECK_INPUT(dy);
   VO_CHECK_INPUT(w);
   c10::cuda::CUDAGuard g(dy.device());
@@ -100,7 +121,21 @@ torch::Tensor gemm_dgrad(torch::Tensor dy, torch::Tensor w) {
   ep.out = bf(dx);
   ep.ldc = (int)K;
   // GEMM: C[M, K] = sum_n dY(m, n) * W(n, k): GEMM-N = K, GEMM-K = N, B(col=k, red=n) = W[n, k] -> MN-major
-  check_rc(vo_gemm_launch(dy.data_ptr(), w.data_ptr(), (int)M, (int)K, (int)N, N, K, 0, 1, 1, ep, stream()), "dgrad");
+  const void *a2 = nullptr, *b2 = nullptr;
+  int64_t R = 0;
+  if (ext_a.has_value() && ext_a->defined()) {
+    TORCH_CHECK(ext_b.has_value() && ext_b->defined(), "ext_a needs ext_b");
+    VO_CHECK_INPUT((*ext_a));
+    VO_CHECK_INPUT((*ext_b));
+    R = ext_a->size(1);
+    TORCH_CHECK(ext_a->size(0) == M && ext_b->size(0) == R && ext_b->size(1) == K && R % 8 == 0,
+                "extension operands must be [M, r] and [r, K] with r % 8 == 0");
+    a2 = ext_a->data_ptr();
+    b2 = ext_b->data_ptr();
+  }
+  check_rc(vo_gemm_launch_ext(dy.data_ptr(), w.data_ptr(), a2, b2, (int)M, (int)K, (int)N, (int)R, N, K, R, K, 0, 1, 1,
+                              ep, stream()),
+           "dgrad");
   count_launch();
   return dx;
 }

@@ -166,6 +166,13 @@ struct Shape {
   int M, N, K;
   int tiles_m, tiles_n, splits, k_blocks_per_split, total_k_blocks;
   int a_mn, b_mn;
+  int kb_main;  // k-blocks [0, kb_main) come from (A, B), the rest from the extension operands (A2, B2)
+};
+
+// Extension operands concatenated along the reduction: C = A B^T + A2 B2^T in one accumulation
+// (the low-rank LoRA path: A2 = x A_lora^T, B2 = scale * B_lora), same majorness as A / B.
+struct ExtMaps {
+  CUtensorMap a2, b2;
 };
 
 
@@ -286,7 +293,7 @@ __device__ __forceinline__ void epilogue_rows(uint32_t tacc, int row0, int col_b
 // ------------------------------------------------------------------------------------ kernel
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Shape sh,
-                EpiParams ep, const __grid_constant__ EpiMaps em) {
+                EpiParams ep, const __grid_constant__ EpiMaps em, const __grid_constant__ ExtMaps xm) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_a = smem;
@@ -348,18 +355,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           mbar_expect_tx(&full[stage], STAGE_BYTES);
           uint8_t* sa = stage_a + stage * A_STAGE_BYTES;
           uint8_t* sb = stage_b + stage * B_STAGE_BYTES;
-          const int k0 = kb * BK;
+          const bool ext = kb >= sh.kb_main;
+          const CUtensorMap* ma = ext ? &xm.a2 : &map_a;
+          const CUtensorMap* mb = ext ? &xm.b2 : &map_b;
+          const int k0 = (ext ? kb - sh.kb_main : kb) * BK;
           if (sh.a_mn) {  // [K, M] row-major: two 64x64 boxes (M chunks)
-            tma_load_2d(sa, &map_a, &full[stage], tm * BM, k0);
-            tma_load_2d(sa + 8192, &map_a, &full[stage], tm * BM + 64, k0);
+            tma_load_2d(sa, ma, &full[stage], tm * BM, k0);
+            tma_load_2d(sa + 8192, ma, &full[stage], tm * BM + 64, k0);
           } else {
-            tma_load_2d(sa, &map_a, &full[stage], k0, tm * BM);
+            tma_load_2d(sa, ma, &full[stage], k0, tm * BM);
           }
           if (sh.b_mn) {  // [K, N] row-major: four 64x64 boxes (N chunks)
 #pragma unroll
-            for (int c = 0; c < 4; ++c) tma_load_2d(sb + c * 8192, &map_b, &full[stage], tn * BN + 64 * c, k0);
+            for (int c = 0; c < 4; ++c) tma_load_2d(sb + c * 8192, mb, &full[stage], tn * BN + 64 * c, k0);
           } else {
-            tma_load_2d(sb, &map_b, &full[stage], k0, tn * BN);
+            tma_load_2d(sb, mb, &full[stage], k0, tn * BN);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -500,7 +510,7 @@ __host__ __device__ constexpr uint32_t make_idesc2(int a_mn, int b_mn) {
 
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm2sm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Shape sh,
-                   EpiParams ep, const __grid_constant__ EpiMaps em) {
+                   EpiParams ep, const __grid_constant__ EpiMaps em, const __grid_constant__ ExtMaps xm) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* epi_stage = smem + STAGES2 * STAGE2_BYTES;
@@ -560,18 +570,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (rank == 0) mbar_expect_tx(&full[stage], 2 * STAGE2_BYTES);
           uint8_t* sa = smem + stage * STAGE2_BYTES;
           uint8_t* sb = sa + BM * BK * 2;
-          const int k0 = kb * BK;
+          const bool ext = kb >= sh.kb_main;
+          const CUtensorMap* ma = ext ? &xm.a2 : &map_a;
+          const CUtensorMap* mb = ext ? &xm.b2 : &map_b;
+          const int k0 = (ext ? kb - sh.kb_main : kb) * BK;
           if (sh.a_mn) {
-            tma_load_2d_pair(sa, &map_a, bar0, m0, k0);
-            tma_load_2d_pair(sa + 8192, &map_a, bar0, m0 + 64, k0);
+            tma_load_2d_pair(sa, ma, bar0, m0, k0);
+            tma_load_2d_pair(sa + 8192, ma, bar0, m0 + 64, k0);
           } else {
-            tma_load_2d_pair(sa, &map_a, bar0, k0, m0);
+            tma_load_2d_pair(sa, ma, bar0, k0, m0);
           }
           if (sh.b_mn) {
-            tma_load_2d_pair(sb, &map_b, bar0, n0, k0);
-            tma_load_2d_pair(sb + 8192, &map_b, bar0, n0 + 64, k0);
+            tma_load_2d_pair(sb, mb, bar0, n0, k0);
+            tma_load_2d_pair(sb + 8192, mb, bar0, n0 + 64, k0);
           } else {
-            tma_load_2d_pair(sb, &map_b, bar0, k0, n0);
+            tma_load_2d_pair(sb, mb, bar0, k0, n0);
           }
           if (++stage == STAGES2) {
             stage = 0;
@@ -701,10 +714,13 @@ static int g_use_2sm = -1;
 //   b_mn == 0: B is row-major [N, K] (ldb >= K);  b_mn == 1: B is row-major [K, N] (ldb >= N)
 // splits > 1 is only valid with EPI_F32_ACC (partial sums are reduced in global memory).
 // Returns 0 on success, otherwise a CUDA / driver error code.
-extern "C" int vo_gemm_launch(const void* A, const void* B, int M, int N, int K, int64_t lda, int64_t ldb, int a_mn,
-                              int b_mn, int splits, vo_gemm::EpiParams ep, cudaStream_t stream) {
+// General form: C = A B^T (+ A2 B2^T when A2 != null, K2 extra reduction columns, same majorness).
+extern "C" int vo_gemm_launch_ext(const void* A, const void* B, const void* A2, const void* B2, int M, int N, int K,
+                                  int K2, int64_t lda, int64_t ldb, int64_t lda2, int64_t ldb2, int a_mn, int b_mn,
+                                  int splits, vo_gemm::EpiParams ep, cudaStream_t stream) {
   using namespace vo_gemm;
   if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const bool has_ext = A2 != nullptr && B2 != nullptr && K2 > 0;
   if ((lda * 2) % 16 || (ldb * 2) % 16) return -1;  // TMA strides must be 16-byte multiples
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) return -2;
   if (splits > 1 && ep.epi != EPI_F32_ACC) return -3;
@@ -743,6 +759,16 @@ extern "C" int vo_gemm_launch(const void* A, const void* B, int M, int N, int K,
   else
     r = make_map(&mb, B, N, K, ldb, 64, two_sm ? 128 : BN);
   if (r) return r;
+  ExtMaps xm;
+  memset(&xm, 0, sizeof(xm));
+  if (has_ext) {
+    if ((lda2 * 2) % 16 || (ldb2 * 2) % 16 || ((reinterpret_cast<uintptr_t>(A2) | reinterpret_cast<uintptr_t>(B2)) & 15))
+      return -5;
+    r = a_mn ? make_map(&xm.a2, A2, K2, M, lda2, 64, 64) : make_map(&xm.a2, A2, M, K2, lda2, 64, BM);
+    if (r) return r;
+    r = b_mn ? make_map(&xm.b2, B2, K2, N, ldb2, 64, 64) : make_map(&xm.b2, B2, N, K2, ldb2, 64, two_sm ? 128 : BN);
+    if (r) return r;
+  }
   if (!g_num_sms) {
     int dev;
     cudaGetDevice(&dev);
@@ -757,7 +783,8 @@ extern "C" int vo_gemm_launch(const void* A, const void* B, int M, int N, int K,
   sh.K = K;
   sh.tiles_m = two_sm ? (M + 255) / 256 : (M + BM - 1) / BM;
   sh.tiles_n = (N + BN - 1) / BN;
-  sh.total_k_blocks = (K + BK - 1) / BK;
+  sh.kb_main = (K + BK - 1) / BK;
+  sh.total_k_blocks = sh.kb_main + (has_ext ? (K2 + BK - 1) / BK : 0);
   splits = splits < 1 ? 1 : splits;
   if (splits > sh.total_k_blocks) splits = sh.total_k_blocks;
   sh.k_blocks_per_split = (sh.total_k_blocks + splits - 1) / splits;
@@ -779,12 +806,17 @@ extern "C" int vo_gemm_launch(const void* A, const void* B, int M, int N, int K,
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm2sm_kernel, ma, mb, sh, ep, em);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm2sm_kernel, ma, mb, sh, ep, em, xm);
     return (int)e;
   }
   const int grid = units < g_num_sms ? units : g_num_sms;
-  gemm_kernel<<<grid, NUM_THREADS, SMEM1_BYTES, stream>>>(ma, mb, sh, ep, em);
+  gemm_kernel<<<grid, NUM_THREADS, SMEM1_BYTES, stream>>>(ma, mb, sh, ep, em, xm);
   return (int)cudaGetLastError();
+}
+
+extern "C" int vo_gemm_launch(const void* A, const void* B, int M, int N, int K, int64_t lda, int64_t ldb, int a_mn,
+                              int b_mn, int splits, vo_gemm::EpiParams ep, cudaStream_t stream) {
+  return vo_gemm_launch_ext(A, B, nullptr, nullptr, M, N, K, 0, lda, ldb, 0, 0, a_mn, b_mn, splits, ep, stream);
 }
 
 extern "C" int vo_gemm_error(int reset) {

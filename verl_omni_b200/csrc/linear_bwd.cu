@@ -19,9 +19,12 @@ namespace {
 constexpr int kRows = 64;     // rows per chunk
 constexpr int kThreads = 64;  // 64 threads x 8 columns = 512 columns per block
 
+// d/dx of 0.5 x (1 + tanh(k0 (x + k1 x^3))); tanh via the hardware approximation, as in the
+// forward GEMM epilogue that produced the activation
 __device__ __forceinline__ float gelu_tanh_grad(float x) {
   const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-  const float t = tanhf(k0 * (x + k1 * x * x * x));
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(k0 * (x + k1 * x * x * x)));
   return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * k0 * (1.f + 3.f * k1 * x * x);
 }
 

@@ -22,6 +22,65 @@ struct ModPtr {
   int64_t stride;
 };
 
+// Register-resident variant: one warp per row, the row's D = 256 * NV bf16 values stay in registers
+// (NV 16-byte vectors per lane), so x is read from memory once; mean and variance are two passes
+// over registers.
+template <int NV>
+__global__ void __launch_bounds__(256) adaln_ln_fwd_reg_kernel(const __nv_bfloat16* __restrict__ x,
+                                                               __nv_bfloat16* __restrict__ y,
+                                                               float* __restrict__ mean_out,
+                                                               float* __restrict__ rstd_out, ModPtr mod,
+                                                               const __nv_bfloat16* __restrict__ aff_w,
+                                                               const __nv_bfloat16* __restrict__ aff_b, int64_t rows,
+                                                               int S, float eps) {
+  constexpr int D = NV * 256;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const bf16x8* xr = reinterpret_cast<const bf16x8*>(x + row * D);
+  float f[NV][8];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) unpack8(xr[v * 32 + lane], f[v]);
+  float s = 0.f;
+#pragma unroll
+  for (int v = 0; v < NV; ++v)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += f[v][j];
+  const float mu = warp_sum(s) * (1.f / D);
+  float ss = 0.f;
+#pragma unroll
+  for (int v = 0; v < NV; ++v)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float d = f[v][j] - mu;
+      ss += d * d;
+    }
+  const float rstd = rsqrtf(warp_sum(ss) * (1.f / D) + eps);
+  if (lane == 0) {
+    mean_out[row] = mu;
+    rstd_out[row] = rstd;
+  }
+  const int64_t b = row / S;
+  bf16x8* yr = reinterpret_cast<bf16x8*>(y + row * D);
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int i = v * 32 + lane;
+    float a[8], c[8], o[8];
+    if (aff_w) {
+      unpack8(reinterpret_cast<const bf16x8*>(aff_w)[i], a);
+      unpack8(reinterpret_cast<const bf16x8*>(aff_b)[i], c);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = (f[v][j] - mu) * rstd * a[j] + c[j];
+    } else {
+      unpack8(reinterpret_cast<const bf16x8*>(mod.scale + b * mod.stride)[i], a);
+      unpack8(reinterpret_cast<const bf16x8*>(mod.shift + b * mod.stride)[i], c);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = (f[v][j] - mu) * rstd * (1.f + a[j]) + c[j];
+    }
+    yr[i] = pack8(o);
+  }
+}
+
 __global__ void adaln_ln_fwd_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y,
                                     float* __restrict__ mean_out, float* __restrict__ rstd_out, ModPtr mod,
                                     const __nv_bfloat16* __restrict__ aff_w, const __nv_bfloat16* __restrict__ aff_b,
@@ -325,10 +384,30 @@ std::vector<torch::Tensor> adaln_ln_fwd(torch::Tensor x, c10::optional<torch::Te
     ab = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr<at::BFloat16>());
   }
   const int wpb = 8;
-  adaln_ln_fwd_kernel<<<(rows + wpb - 1) / wpb, wpb * 32, 0, stream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr<at::BFloat16>()),
-      reinterpret_cast<__nv_bfloat16*>(y.data_ptr<at::BFloat16>()), mean.data_ptr<float>(), rstd.data_ptr<float>(), m,
-      aw, ab, rows, D, (int)S, (float)eps); vo::count_launch();
+  const unsigned grid = (unsigned)((rows + wpb - 1) / wpb);
+  const auto* xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr<at::BFloat16>());
+  auto* yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr<at::BFloat16>());
+  switch (D) {  // register-resident rows for the hidden sizes of the model zoo (1536 / 3072 / 2048)
+    case 1536:
+      adaln_ln_fwd_reg_kernel<6><<<grid, wpb * 32, 0, stream()>>>(xp, yp, mean.data_ptr<float>(),
+                                                                   rstd.data_ptr<float>(), m, aw, ab, rows, (int)S,
+                                                                   (float)eps);
+      break;
+    case 2048:
+      adaln_ln_fwd_reg_kernel<8><<<grid, wpb * 32, 0, stream()>>>(xp, yp, mean.data_ptr<float>(),
+                                                                   rstd.data_ptr<float>(), m, aw, ab, rows, (int)S,
+                                                                   (float)eps);
+      break;
+    case 3072:
+      adaln_ln_fwd_reg_kernel<12><<<grid, wpb * 32, 0, stream()>>>(xp, yp, mean.data_ptr<float>(),
+                                                                    rstd.data_ptr<float>(), m, aw, ab, rows, (int)S,
+                                                                    (float)eps);
+      break;
+    default:
+      adaln_ln_fwd_kernel<<<grid, wpb * 32, 0, stream()>>>(xp, yp, mean.data_ptr<float>(), rstd.data_ptr<float>(), m,
+                                                           aw, ab, rows, D, (int)S, (float)eps);
+  }
+  vo::count_launch();
   VO_CUDA_OK(cudaGetLastError());
   return {y, mean, rstd};
 }

@@ -74,6 +74,10 @@ class LoRALinear(nn.Module):
         if self.active is None:
             return self.base(x, epilogue=epilogue, gate=gate, res=res, S=S)
         A, B = self.lora_A[self.active], self.lora_B[self.active]
+        if L.lora_linear_native_ok(x, self.base.weight, A) and B.dtype == x.dtype:
+            # low-rank term reduced inside the base GEMM, epilogue fused (ops/linear.py)
+            return L.lora_linear(x, self.base.weight, self.base.bias, A, B, self.scaling, epilogue=epilogue,
+                                 gate=gate, res=res, S=S)
         delta = L.linear(L.linear(x, A.to(x.dtype)), B.to(x.dtype)) * self.scaling
         if epilogue == "none":
             return self.base(x) + delta

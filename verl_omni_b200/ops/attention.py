@@ -18,10 +18,11 @@ import torch.nn.functional as F
 from verl_omni_b200.ops._ext import ext
 
 
-# forward kernel generation: 2 = two query tiles per CTA with P/O in tensor memory, 1 = one tile per CTA
-_FWD_VERSION = int(os.environ.get("VO_FMHA_FWD", "1"))
+# forward kernel generation: 3 = two query tiles per CTA, P/O in tensor memory, two softmax warpgroups per
+# tile (default); 2 = one softmax warpgroup per tile; 1 = one query tile per CTA
+_FWD_VERSION = int(os.environ.get("VO_FMHA_FWD", "3"))
 # backward kernel generation: 2 = pipelined (P^T/dS^T in tensor memory, concurrent dQ drain), 1 = serial
-_BWD_VERSION = int(os.environ.get("VO_FMHA_BWD", "1"))
+_BWD_VERSION = int(os.environ.get("VO_FMHA_BWD", "2"))
 
 
 def _native() -> bool:

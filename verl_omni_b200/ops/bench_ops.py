@@ -101,6 +101,64 @@ def bench_gemm_sweep(a) -> list[dict]:
     return out
 
 
+def bench_optstep(a) -> list[dict]:
+    """Sharded optimizer step over ``--numel`` parameters on every rank (run under torchrun):
+    NCCL reduce-scatter + AdamW + all-gather vs the fused peer-memory kernels.  Device time of the
+    slowest rank; roofline = bytes that must cross NVLink per GPU / measured peer bandwidth."""
+    import torch.distributed as dist
+
+    from verl_omni_b200.ops._ext import ext
+    from verl_omni_b200.parallel import dist as D
+    from verl_omni_b200.parallel.symm_mem import SymmetricBuffer, fused_optimizer_step
+
+    info = D.init_distributed(device="cuda", timeout_s=300)
+    W, dev = D.world_size(), info.device
+    P = (a.numel + 128 * W - 1) // (128 * W) * 128 * W
+    n, lo = P // W, (P // W) * D.rank()
+    flat = SymmetricBuffer(P, torch.bfloat16, dev)
+    grad = SymmetricBuffer(P, torch.float32, dev)
+    grad.tensor.normal_()
+    master = torch.randn(n, device=dev)
+    m, v, gs = torch.zeros_like(master), torch.zeros_like(master), torch.empty_like(master)
+    kw = dict(lr=1e-5, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, max_norm=1.0)
+
+    def nccl_step(step):
+        dist.reduce_scatter_tensor(gs, grad.tensor)
+        gs.mul_(1.0 / W)
+        sq = ext().sq_norm(gs)
+        dist.all_reduce(sq)
+        ext().adamw_flat(master, gs, m, v, flat.tensor[lo:lo + n], kw["lr"], 0.9, 0.999, 1e-8, 0.0, step, 1.0, sq, 1.0)
+        dist.all_gather_into_tensor(flat.tensor, flat.tensor[lo:lo + n].clone())
+
+    def fused_step(step):
+        fused_optimizer_step(flat, grad, lo, n, master, gs, m, v, step=step, **kw)
+
+    out = []
+    for name, fn in (("nccl", nccl_step), ("fused_peer", fused_step)):
+        for s in range(3):
+            fn(s + 1)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for s in range(a.iters):
+            fn(s + 4)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([e0.elapsed_time(e1) / a.iters], device=dev, dtype=torch.float64)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        # per GPU over NVLink: fp32 grads of the other shards in, bf16 of own shard to W-1 peers out
+        link_bytes = (W - 1) * n * 4 + (W - 1) * n * 2
+        out.append({"op": f"optstep_{name}", "world": W, "params": P, "ms": round(float(ms), 3),
+                    "link_gbs": round(link_bytes / float(ms) / 1e6, 1),
+                    "frac_of_770gbs_link": round(link_bytes / float(ms) / 1e6 / 770.0, 3)})
+    flat.close()
+    grad.close()
+    if D.rank() != 0:
+        return []
+    return out
+
+
 def bench_fmha(a) -> list[dict]:
     from verl_omni_b200.ops._ext import ext
 
@@ -154,7 +212,8 @@ def bench_adaln(a) -> list[dict]:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "gemm_sweep", "fmha", "sde", "adaln"])
+    ap.add_argument("op", choices=["gemm", "gemm_sweep", "fmha", "sde", "adaln", "optstep"])
+    ap.add_argument("--numel", type=int, default=2_240_000_000)
     ap.add_argument("--M", type=int, default=21712)
     ap.add_argument("--N", type=int, default=6144)
     ap.add_argument("--K", type=int, default=1536)
@@ -167,7 +226,7 @@ def main() -> None:
     ap.add_argument("--compare", action="store_true")
     a = ap.parse_args()
     pk = _peaks()
-    rows = {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "fmha": bench_fmha, "sde": bench_sde, "adaln": bench_adaln}[a.op](a)
+    rows = {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "fmha": bench_fmha, "optstep": bench_optstep, "sde": bench_sde, "adaln": bench_adaln}[a.op](a)
     for r in rows:
         if "tflops" in r:
             r[f"frac_of_{pk['src']}_gemm_peak"] = round(r["tflops"] / pk["tflops"], 3)

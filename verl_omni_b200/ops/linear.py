@@ -105,3 +105,78 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None, *
             return res + (y.view(B, -1, y.shape[-1]) * gate[:, None]).view_as(res)
         return y
     return _LinearFn.apply(x, w, b, epilogue, gate, res, S)
+
+
+class _LoRALinearFn(torch.autograd.Function):
+    """``y = epilogue(x W^T + b + s * (x A^T) B^T)`` with the low-rank term folded into the main GEMM.
+
+    Forward: ``u = x A^T`` (skinny GEMM), then one tcgen05 GEMM reducing over ``[x | u]`` against
+    ``[W | s B]`` with the fused epilogue.  Backward (W and b frozen): ``v = dY (s B)``, one dgrad GEMM
+    over ``[dY | v]`` against ``[W ; A]`` gives dX, and the two adapter gradients are skinny weight
+    GEMMs ``dB = dY^T (s u)``, ``dA = v^T x`` accumulated into the adapters' fp32 ``main_grad``.
+    """
+
+    @staticmethod
+    def forward(ctx, x, w, b, A, B, scaling, epilogue, gate, res, S):
+        e = ext()
+        x2 = x.reshape(-1, x.shape[-1])
+        u = e.gemm_fwd(x2, A, None, EPI_CODES["none"], None, None, 1)[0]  # [M, r]
+        sB = (B.float() * scaling).to(x.dtype).contiguous()
+        res2 = res.reshape(-1, w.shape[0]) if res is not None else None
+        out, saved = e.gemm_fwd(x2, w, b, _epi_code(epilogue, b), gate, res2, S, ext_a=u, ext_b=sB)
+        empty = torch.empty(0, device=x.device)
+        ctx.save_for_backward(x2, w, A, B, u, sB, saved if saved is not None and saved.numel() else empty,
+                              gate if gate is not None else empty)
+        ctx.meta = (epilogue, S, x.shape, float(scaling))
+        return out.view(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w, A, B, u, sB, pre, gate = ctx.saved_tensors
+        epilogue, S, xshape, scaling = ctx.meta
+        e = ext()
+        N = w.shape[0]
+        dy2 = dy.reshape(-1, N).contiguous()
+        d_gate = d_res = None
+        if epilogue == "gate_res":
+            d_res = dy
+        mode = _MODE[epilogue]
+        if mode:
+            dy2, dg = e.linear_bwd_prep(dy2, pre, gate if mode == 2 else None, S, mode, None, False)
+            if mode == 2:
+                d_gate = dg
+        v = e.gemm_dgrad(dy2, sB)  # [M, r] = dY (s B)
+        dx = e.gemm_dgrad(dy2, w, ext_a=v, ext_b=A)
+        gA = gB = None
+        su = (u.float() * scaling).to(u.dtype)
+        for p, lhs, rhs in ((B, dy2, su), (A, v, x2)):
+            mg = getattr(p, "main_grad", None)
+            if mg is not None:
+                G.wgrad(lhs, rhs, mg)
+            else:
+                g = G.wgrad(lhs, rhs, None).to(p.dtype)
+                if p is A:
+                    gA = g
+                else:
+                    gB = g
+        return dx.view(xshape), None, None, gA, gB, None, None, d_gate, d_res, None
+
+
+EPI_CODES = {"none": 0, "bias": 1, "gelu": 2, "gate_res": 3}
+
+
+def _epi_code(epilogue: str, b) -> int:
+    if epilogue == "none":
+        return EPI_CODES["bias"] if b is not None else EPI_CODES["none"]
+    return EPI_CODES[epilogue]
+
+
+def lora_linear_native_ok(x: torch.Tensor, w: torch.Tensor, A: torch.Tensor) -> bool:
+    rows = x.numel() // x.shape[-1]
+    return (x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and A.dtype == torch.bfloat16
+            and G._use_native(x.shape[-1], w.shape[0], A.shape[0], rows=rows) and hasattr(ext(), "gemm_fwd"))
+
+
+def lora_linear(x, w, b, A, B, scaling: float, *, epilogue: str = "none", gate=None, res=None, S: int = 1):
+    """Fused LoRA linear on the tcgen05 GEMM (bf16, CUDA); see :class:`_LoRALinearFn`."""
+    return _LoRALinearFn.apply(x, w, b, A, B, float(scaling), epilogue, gate, res, S)

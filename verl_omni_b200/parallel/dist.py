@@ -76,6 +76,24 @@ def rank(group=None) -> int:
     return dist.get_rank(group) if dist.is_initialized() else 0
 
 
+_HSDP_CACHE: dict = {}
+
+
+def make_hsdp_groups(fsdp_size: int):
+    """(shard_group, replica_group) of this rank: shards are ``fsdp_size`` consecutive ranks, replicas
+    the ranks with the same position in their shard group.  Every rank creates every group (the
+    collective contract of ``new_group``); results are cached per size."""
+    if fsdp_size in _HSDP_CACHE:
+        return _HSDP_CACHE[fsdp_size]
+    ws, r = world_size(), rank()
+    if ws % fsdp_size:
+        raise ValueError(f"world size {ws} not divisible by fsdp_size {fsdp_size}")
+    shard = [dist.new_group(list(range(i, i + fsdp_size))) for i in range(0, ws, fsdp_size)]
+    rep = [dist.new_group(list(range(j, ws, fsdp_size))) for j in range(fsdp_size)]
+    _HSDP_CACHE[fsdp_size] = (shard[r // fsdp_size], rep[r % fsdp_size])
+    return _HSDP_CACHE[fsdp_size]
+
+
 def barrier(group=None) -> None:
     if dist.is_initialized():
         if dist.get_backend(group) == "nccl":

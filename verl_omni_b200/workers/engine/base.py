@@ -192,8 +192,15 @@ class ShardedEngine:
                  trainable: bool = True):
         self.cfg = actor_cfg
         self.group = group
-        self.world = D.world_size(group)
-        self.rank = D.rank(group)
+        self.replica_group = None
+        self.n_replicas = 1
+        fs = int(getattr(actor_cfg.fsdp_config, "fsdp_size", -1) or -1)
+        if group is None and 0 < fs < D.world_size() and trainable:
+            # HSDP: shard within groups of fsdp_size consecutive ranks (one node), replicate across them
+            self.group, self.replica_group = D.make_hsdp_groups(fs)
+            self.n_replicas = D.world_size() // fs
+        self.world = D.world_size(self.group)
+        self.rank = D.rank(self.group)
         self.device = device
         self.dtype = _dtype(actor_cfg.fsdp_config.dtype) if device.type == "cuda" else torch.float32
         self.module = module
@@ -204,8 +211,9 @@ class ShardedEngine:
             module.to(device=device, dtype=self.dtype)
             self.flat = None
         else:
-            self.flat = FlatParams(module, self.dtype, device, self.world, self.rank, group,
-                                   symmetric=self._want_symmetric(actor_cfg, device, group))
+            self.flat = FlatParams(module, self.dtype, device, self.world, self.rank, self.group,
+                                   symmetric=self.replica_group is None and self._want_symmetric(actor_cfg, device,
+                                                                                                 self.group))
         self.opt_step = 0
         self.sched = LRSchedule(actor_cfg.optim, total_steps) if trainable else None
         self.last_grad_norm = None
@@ -258,8 +266,10 @@ class ShardedEngine:
             self.last_grad_norm = norm
             return norm
         D.reduce_scatter_into(fp.grad_shard, fp.main_grad, self.group)
-        if self.world > 1:
-            fp.grad_shard.mul_(1.0 / self.world)
+        if self.replica_group is not None:  # HSDP: average the shard over the replicas
+            D.all_reduce(fp.grad_shard, group=self.replica_group)
+        if self.world * self.n_replicas > 1:
+            fp.grad_shard.mul_(1.0 / (self.world * self.n_replicas))
         self.opt_step += 1
         lr = self.sched.lr()
         b1, b2 = float(oc.betas[0]), float(oc.betas[1])
@@ -310,6 +320,8 @@ class ShardedEngine:
         os.makedirs(local_path, exist_ok=True)
         W, r = self.world, self.rank
         fp = self.flat
+        # HSDP: every replica holds the same shards; replica 0 writes them
+        writer = self.replica_group is None or D.rank() // self.world == 0
         if "model" in save_contents:
             full = fp.full_master()
             shards = {}
@@ -317,28 +329,30 @@ class ShardedEngine:
                 rows = view.shape[0] if view.ndim else 1
                 per = (rows + W - 1) // W
                 shards[n] = view[r * per:(r + 1) * per].detach().cpu().clone() if view.ndim else view.detach().cpu()
-            torch.save({"params": shards, "placements": {"type": "Shard", "dim": 0}, "world_size": W},
-                       os.path.join(local_path, f"model_world_size_{W}_rank_{r}.pt"))
-            if hf_export and r == 0:
+            if writer:
+                torch.save({"params": shards, "placements": {"type": "Shard", "dim": 0}, "world_size": W},
+                           os.path.join(local_path, f"model_world_size_{W}_rank_{r}.pt"))
+            if hf_export and r == 0 and writer:
                 from safetensors.torch import save_file
 
                 os.makedirs(os.path.join(local_path, "huggingface"), exist_ok=True)
                 save_file({n: v.to(torch.bfloat16).contiguous().cpu() for n, v in fp.param_views(full)},
                           os.path.join(local_path, "huggingface", "diffusion_pytorch_model.safetensors"))
             del full
-        if "optimizer" in save_contents:
+        if "optimizer" in save_contents and writer:
             torch.save({"exp_avg": fp.exp_avg.cpu(), "exp_avg_sq": fp.exp_avg_sq.cpu(), "step": self.opt_step,
                         "padded": fp.padded, "world_size": W},
                        os.path.join(local_path, f"optim_world_size_{W}_rank_{r}.pt"))
-        if "extra" in save_contents:
+        if "extra" in save_contents and writer:
             torch.save({"lr_scheduler": self.sched.state_dict(), "global_step": global_step,
                         "rng": torch.get_rng_state(),
                         "cuda_rng": torch.cuda.get_rng_state() if torch.cuda.is_available() else None},
                        os.path.join(local_path, f"extra_state_world_size_{W}_rank_{r}.pt"))
-        if r == 0:
+        if r == 0 and writer:
             with open(os.path.join(local_path, "fsdp_config.json"), "w") as f:
-                json.dump({"FSDP_version": 2, "world_size": W, "layout": "flat-shard-adamw"}, f)
-        D.barrier(self.group)
+                json.dump({"FSDP_version": 2, "world_size": W, "layout": "flat-shard-adamw",
+                           "replicas": self.n_replicas}, f)
+        D.barrier()
 
     def load_checkpoint(self, local_path: str, load_contents=("model", "optimizer", "extra")) -> dict:
         with open(os.path.join(local_path, "fsdp_config.json")) as f:
