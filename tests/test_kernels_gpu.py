@@ -243,3 +243,21 @@ def test_cfg_combine_matches_reference(renorm, dtype):
     with torch.no_grad():
         out = cfg_combine(pos, neg, 4.5, renorm)
     torch.testing.assert_close(out, cfg_combine_reference(pos, neg, 4.5, renorm), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("silu", [False, True])
+@pytest.mark.parametrize("C,H", [(128, 64), (512, 16), (256, 33)])
+def test_group_norm_nhwc_matches_reference(C, H, silu):
+    from verl_omni_b200.ops.norm import group_norm_act
+
+    torch.manual_seed(0)
+    x = (torch.randn(3, C, H, H + 5, device="cuda") * 2 + 0.5).bfloat16().contiguous(memory_format=torch.channels_last)
+    w = (1 + 0.1 * torch.randn(C, device="cuda")).bfloat16()
+    b = (0.1 * torch.randn(C, device="cuda")).bfloat16()
+    with torch.no_grad():
+        y = group_norm_act(x, w, b, 32, 1e-6, silu)
+    ref = torch.nn.functional.group_norm(x.float(), 32, w.float(), b.float(), 1e-6)
+    if silu:
+        ref = torch.nn.functional.silu(ref)
+    assert y.is_contiguous(memory_format=torch.channels_last)
+    torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2)

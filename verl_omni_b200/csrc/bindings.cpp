@@ -52,6 +52,9 @@ std::vector<torch::Tensor> linear_bwd_prep(torch::Tensor dy, c10::optional<torch
                                            c10::optional<torch::Tensor> gate, int64_t S, int64_t mode,
                                            c10::optional<torch::Tensor> db, bool db_accumulate);
 torch::Tensor cfg_combine(torch::Tensor pos, torch::Tensor neg, double g, bool renorm);
+void peer_push(int64_t src_ptr, torch::Tensor plan, std::vector<int64_t> dst_ptrs);
+torch::Tensor group_norm_nhwc(torch::Tensor x, torch::Tensor gamma, torch::Tensor beta, int64_t groups, double eps,
+                              bool silu);
 int64_t symm_malloc(int64_t nbytes);
 void symm_free(int64_t ptr);
 torch::Tensor ipc_get_handle(int64_t ptr);
@@ -98,6 +101,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("dO2") = py::none(), py::arg("split") = 0);
   m.def("linear_bwd_prep", &vo::linear_bwd_prep);
   m.def("cfg_combine", &vo::cfg_combine);
+  m.def("peer_push", &vo::peer_push);
+  m.def("group_norm_nhwc", &vo::group_norm_nhwc);
   m.def("symm_malloc", &vo::symm_malloc);
   m.def("symm_free", &vo::symm_free);
   m.def("ipc_get_handle", &vo::ipc_get_handle);

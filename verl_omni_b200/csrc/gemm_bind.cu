@@ -82,9 +82,10 @@ std::vector<torch::Tensor> gemm_fwd(torch::Tensor x, torch::Tensor w, c10::optio
   torch::Tensor gate_c;
   if (epi == 3) {
     TORCH_CHECK(gate.has_value() && res.has_value(), "GATE_RES needs gate and res");
-    gate_c = gate->contiguous();
+    // a strided per-sample row view (an AdaLN chunk of the modulation output) is read in place
+    gate_c = (gate->dim() == 2 && gate->stride(1) == 1) ? *gate : gate->contiguous();
     ep.gate = bf(gate_c);
-    ep.gate_ld = gate_c.size(-1);
+    ep.gate_ld = gate_c.stride(0);
     TORCH_CHECK(res->is_contiguous() && res->numel() == M * N, "res must be contiguous [M, N]");
     ep.res = bf(*res);
   }

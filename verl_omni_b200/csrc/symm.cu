@@ -94,6 +94,30 @@ __global__ void sum_partials(const float* __restrict__ p, int n, float* __restri
   if (threadIdx.x == 0) out[0] = s;
 }
 
+// One kernel for every copy of a weight-sync plan: chunk c moves bytes [src_off, src_off + nbytes) of the
+// local source buffer to dst_off of destination slot dst (a peer's mapped buffer).  16-byte vector
+// stores over NVLink; each block walks the chunks with a grid-stride loop over 16-byte units.
+struct PushChunk {
+  int64_t src_off, dst_off, nbytes;
+  int32_t dst, pad;
+};
+__global__ void peer_push_kernel(const uint8_t* __restrict__ src, const PushChunk* __restrict__ chunks, int nchunks,
+                                 PeerPtrs dst) {
+  for (int c = 0; c < nchunks; ++c) {
+    const PushChunk ch = chunks[c];
+    const uint4* s = reinterpret_cast<const uint4*>(src + ch.src_off);
+    uint4* d = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(dst.flat16[ch.dst]) + ch.dst_off);
+    const int64_t n16 = ch.nbytes >> 4;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x)
+      d[i] = s[i];
+    // tail (< 16 bytes)
+    if (blockIdx.x == 0 && threadIdx.x < (ch.nbytes & 15)) {
+      const int64_t o = (n16 << 4) + threadIdx.x;
+      reinterpret_cast<uint8_t*>(dst.flat16[ch.dst])[ch.dst_off + o] = src[ch.src_off + o];
+    }
+  }
+}
+
 PeerPtrs make_ptrs(const std::vector<int64_t>& grads, const std::vector<int64_t>& flats) {
   TORCH_CHECK(grads.size() <= (size_t)kMaxPeers && flats.size() == grads.size(), "bad peer pointer lists");
   PeerPtrs pp{};
@@ -174,6 +198,33 @@ void peer_adamw_bcast(std::vector<int64_t> flat_ptrs, int64_t lo, int64_t n, tor
                                                m.data_ptr<float>(), v.data_ptr<float>(), (float)lr, (float)b1,
                                                (float)b2, (float)eps, (float)wd, (float)bc1, (float)std::sqrt(bc2),
                                                (float)max_norm, sq_norm.data_ptr<float>());
+  count_launch();
+  VO_CUDA_OK(cudaGetLastError());
+}
+
+// Trainer -> rollout weight resharding: executes a copy plan (int64 [n, 5] rows: src_off, dst_off,
+// nbytes, dst_slot, 0) from the local buffer at src_ptr into the mapped destination buffers.
+void peer_push(int64_t src_ptr, torch::Tensor plan, std::vector<int64_t> dst_ptrs) {
+  TORCH_CHECK(plan.dim() == 2 && plan.size(1) == 5 && plan.scalar_type() == torch::kInt64, "plan must be int64 [n, 5]");
+  TORCH_CHECK(!dst_ptrs.empty() && dst_ptrs.size() <= (size_t)kMaxPeers, "1..16 destinations");
+  auto pc = plan.contiguous().cpu();
+  const int64_t* rows = pc.data_ptr<int64_t>();
+  const int n = (int)pc.size(0);
+  std::vector<PushChunk> chunks(n);
+  for (int i = 0; i < n; ++i) {
+    chunks[i] = PushChunk{rows[5 * i], rows[5 * i + 1], rows[5 * i + 2], (int32_t)rows[5 * i + 3], 0};
+    TORCH_CHECK(chunks[i].dst >= 0 && chunks[i].dst < (int)dst_ptrs.size(), "bad destination slot");
+    TORCH_CHECK(((chunks[i].src_off | chunks[i].dst_off) & 15) == 0, "chunk offsets must be 16-byte aligned");
+  }
+  if (n == 0) return;
+  PeerPtrs pp{};
+  for (size_t r = 0; r < dst_ptrs.size(); ++r) pp.flat16[r] = reinterpret_cast<__nv_bfloat16*>(dst_ptrs[r]);
+  auto dev_chunks = torch::empty({(int64_t)(n * sizeof(PushChunk))}, torch::dtype(torch::kUInt8).device(torch::kCUDA));
+  VO_CUDA_OK(cudaMemcpyAsync(dev_chunks.data_ptr(), chunks.data(), n * sizeof(PushChunk), cudaMemcpyHostToDevice,
+                             stream()));
+  peer_push_kernel<<<2 * num_sms(), 512, 0, stream()>>>(reinterpret_cast<const uint8_t*>(src_ptr),
+                                                        reinterpret_cast<const PushChunk*>(dev_chunks.data_ptr()), n,
+                                                        pp);
   count_launch();
   VO_CUDA_OK(cudaGetLastError());
 }

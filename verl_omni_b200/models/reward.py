@@ -77,6 +77,13 @@ class ViTScorer(nn.Module):
         return self.head(x).squeeze(-1).float()
 
 
+def _gn(norm: nn.GroupNorm, x: torch.Tensor, silu: bool = False) -> torch.Tensor:
+    """GroupNorm (+SiLU) on the NHWC kernel for channels-last bf16 activations."""
+    from verl_omni_b200.ops.norm import group_norm_act
+
+    return group_norm_act(x, norm.weight, norm.bias, norm.num_groups, norm.eps, silu)
+
+
 class _ResBlock(nn.Module):
     def __init__(self, cin: int, cout: int):
         super().__init__()
@@ -87,8 +94,8 @@ class _ResBlock(nn.Module):
         self.skip = nn.Conv2d(cin, cout, 1) if cin != cout else None
 
     def forward(self, x):
-        h = self.c1(F.silu(self.n1(x)))
-        h = self.c2(F.silu(self.n2(h)))
+        h = self.c1(_gn(self.n1, x, silu=True))
+        h = self.c2(_gn(self.n2, h, silu=True))
         return h + (self.skip(x) if self.skip is not None else x)
 
 
@@ -101,7 +108,7 @@ class _MidAttn(nn.Module):
 
     def forward(self, x):
         B, C, H, W = x.shape
-        h = self.norm(x).flatten(2).transpose(1, 2)
+        h = _gn(self.norm, x).flatten(2).transpose(1, 2)
         q, k, v = self.qkv(h).chunk(3, dim=-1)
         o = attention(q[:, None].contiguous(), k[:, None].contiguous(), v[:, None].contiguous())
         return x + self.out(o).transpose(1, 2).reshape(B, C, H, W)
@@ -142,7 +149,7 @@ class VAEDecoder(nn.Module):
                 x = r(x)
             if st.up is not None:
                 x = st.up(F.interpolate(x, scale_factor=2.0, mode="nearest"))
-        x = self.conv_out(F.silu(self.norm_out(x)))
+        x = self.conv_out(_gn(self.norm_out, x, silu=True))
         return x.clamp(-1, 1)
 
     def decode_video(self, latents: torch.Tensor) -> torch.Tensor:

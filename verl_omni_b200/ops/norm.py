@@ -149,3 +149,15 @@ def qk_norm_split_into(q_buf, k_buf, v_buf, x2d, wq, wk, S_seg: int, seg_off: in
         return tuple(res)
     rc, rs = (rope if rope is not None else (None, None))
     return _QKSplit.apply(q_buf, k_buf, v_buf, x2d.contiguous(), wq, wk, S_seg, seg_off, tuple(parts), rc, rs, eps)
+
+
+# ----------------------------------------------------------------------------- GroupNorm (+SiLU)
+def group_norm_act(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, groups: int, eps: float = 1e-6,
+                   silu: bool = False) -> torch.Tensor:
+    """GroupNorm with an optional fused SiLU.  bf16 channels-last CUDA tensors without autograd use the
+    NHWC kernel (``csrc/groupnorm.cu``); everything else the eager op."""
+    if (x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 4 and not torch.is_grad_enabled()
+            and x.is_contiguous(memory_format=torch.channels_last) and x.shape[1] % 8 == 0):
+        return ext().group_norm_nhwc(x, weight.to(x.dtype), bias.to(x.dtype), groups, eps, silu)
+    y = F.group_norm(x, groups, weight, bias, eps)
+    return F.silu(y) if silu else y
