@@ -203,11 +203,15 @@ __device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.syn
 // h = g % 2.  Per key block: row max over the 64 own columns, exchange with the partner half through
 // shared memory (double-buffered by block parity, one 256-thread named barrier), the shared lazy
 // rescale of the own half of O_t, P for the own keys packed into the first 32 own columns.
-template <int D>
+// INDEP (head_dim 64): the two key halves keep separate running maxima, row sums and O accumulators
+// (O_{t,h} = 64 columns each, 4 x 64 + 2 x 128 = 512 tensor-memory columns), so no exchange is needed
+// per key block; the halves are combined once in the epilogue.
+template <int D, bool INDEP>
 __device__ __forceinline__ void softmax_split2(const Params& p, uint32_t tmem, int warp, int lane, int q0, int bh,
                                                int nkv, uint64_t* s_full, uint64_t* p_full, uint64_t* o_final,
                                                volatile int* abort_flag, float* xmax, float* xsum) {
   using C = Cfg<D>;
+  static_assert(!INDEP || D == 64, "independent halves need 4 O tiles of 64 columns");
   const int g = (warp - 2) >> 2;
   const int t = g >> 1, hf = g & 1;
   const int quarter = warp & 3;
@@ -215,7 +219,9 @@ __device__ __forceinline__ void softmax_split2(const Params& p, uint32_t tmem, i
   const int q = q0 + t * BQ + row;
   const uint32_t lane_off = (uint32_t)(32 * quarter) << 16;
   const uint32_t S_t = tmem + C::S_COL0 + t * 128 + lane_off + 64 * hf;
-  const uint32_t O_t = tmem + C::O_COL0 + t * D + lane_off + hf * (D / 2);
+  // shared O_t: this half rescales / stores columns [hf D/2, (hf+1) D/2); INDEP: own O_{t,h}, all columns
+  const uint32_t O_t = INDEP ? tmem + C::O_COL0 + t * 128 + hf * 64 + lane_off
+                             : tmem + C::O_COL0 + t * D + lane_off + hf * (D / 2);
   const int bar_id = 1 + t;
   float* mx_mine = xmax + (t * 2 + hf) * 256;
   const float* mx_other = xmax + (t * 2 + (hf ^ 1)) * 256;
@@ -249,10 +255,12 @@ __device__ __forceinline__ void softmax_split2(const Params& p, uint32_t tmem, i
       }
     }
     }
-    const int par = (j & 1) * 128;
-    mx_mine[par + row] = mx;
-    named_bar(bar_id, 256);
-    mx = fmaxf(mx, mx_other[par + row]);
+    if (!INDEP) {
+      const int par = (j & 1) * 128;
+      mx_mine[par + row] = mx;
+      named_bar(bar_id, 256);
+      mx = fmaxf(mx, mx_other[par + row]);
+    }
     const float m_blk = mx * sl2;
     float alpha = 1.f;
     const bool move = m_blk > m + RESCALE_THRESHOLD || (m == -INFINITY && m_blk != -INFINITY);
@@ -261,9 +269,10 @@ __device__ __forceinline__ void softmax_split2(const Params& p, uint32_t tmem, i
       m = m_blk;
     }
     if (j > 0 && __any_sync(0xffffffffu, move)) {
-      // both halves take the same decision; each rescales its own half of O_t (quiescent, see above)
+      // shared O: both halves take the same decision and each rescales its half of O_t; INDEP: this
+      // half's own O_{t,h} (all 64 columns).  O is quiescent here (see the MMA ordering above).
 #pragma unroll
-      for (int c = 0; c < D / 64; ++c) {
+      for (int c = 0; c < (INDEP ? 2 : D / 64); ++c) {
         uint32_t o[32];
         ld32_nowait(O_t + c * 32, o);
         wait_ld();
@@ -315,17 +324,41 @@ __device__ __forceinline__ void softmax_split2(const Params& p, uint32_t tmem, i
   if (ok && mbar_wait(&o_final[t], 0, abort_flag, 50)) {
     fence_after();
     xsum[(t * 2 + hf) * 128 + row] = l;
+    if (INDEP) mx_mine[row] = m;
     named_bar(bar_id, 256);
-    const float lt = l + xsum[(t * 2 + (hf ^ 1)) * 128 + row];
+    const float l_o = xsum[(t * 2 + (hf ^ 1)) * 128 + row];
+    float c_mine = 1.f, c_other = 1.f, lt, m_out = m;
+    if (INDEP) {  // combine the halves against the larger reference max
+      const float m_o = mx_other[row];
+      m_out = fmaxf(m, m_o);
+      c_mine = (m == -INFINITY) ? 0.f : ex2(m - m_out);
+      c_other = (m_o == -INFINITY) ? 0.f : ex2(m_o - m_out);
+      lt = l * c_mine + l_o * c_other;
+    } else {
+      lt = l + l_o;
+    }
     const float inv = lt > 0.f ? 1.f / lt : 0.f;
     const int bb = bh / p.H, h = bh % p.H;
     const bool row_ok = q < p.Sq;
     __nv_bfloat16* dst = out_row(p, bb, q, h, D) + hf * (D / 2);
+    // INDEP: both O_{t,0} and O_{t,1} are read for this half's output columns [hf D/2, +D/2)
+    const uint32_t Oa = INDEP ? tmem + C::O_COL0 + t * 128 + hf * (D / 2) + lane_off : O_t;
+    const uint32_t Ob = INDEP ? tmem + C::O_COL0 + t * 128 + 64 + hf * (D / 2) + lane_off : O_t;
+    const float ca = INDEP ? (hf == 0 ? c_mine : c_other) : 1.f;  // O_{t,0} belongs to half 0
+    const float cb = INDEP ? (hf == 0 ? c_other : c_mine) : 0.f;
 #pragma unroll
     for (int c = 0; c < D / 64; ++c) {
       uint32_t o[32];
-      ld32_nowait(O_t + c * 32, o);
+      ld32_nowait(Oa + c * 32, o);
       wait_ld();
+      if (INDEP) {
+        uint32_t o2[32];
+        ld32_nowait(Ob + c * 32, o2);
+        wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          o[i] = __float_as_uint(__uint_as_float(o[i]) * ca + __uint_as_float(o2[i]) * cb);
+      }
       if (row_ok) {
 #pragma unroll
         for (int gg = 0; gg < 4; ++gg) {
@@ -338,7 +371,7 @@ __device__ __forceinline__ void softmax_split2(const Params& p, uint32_t tmem, i
         }
       }
     }
-    if (row_ok && hf == 0) p.lse[(int64_t)bh * p.Sq + q] = (m + __log2f(lt)) * 0.69314718055994531f;
+    if (row_ok && hf == 0) p.lse[(int64_t)bh * p.Sq + q] = (m_out + __log2f(lt)) * 0.69314718055994531f;
   }
 }
 
@@ -347,8 +380,9 @@ __device__ __forceinline__ void softmax_split2(const Params& p, uint32_t tmem, i
 // memory (one named barrier per key block), write P for their keys into their own 64-column half
 // (packed into its first 32 columns) and rescale / store their half of O_t.  Twice the softmax
 // warps per SMSP hide the tensor-memory and MUFU latencies that bound SPLIT == 1.
+// SPLIT == 3: as 2 with independent key halves (head_dim 64 only), see softmax_split2.
 template <int SPLIT>
-__host__ __device__ constexpr int fwd_threads() { return SPLIT == 2 ? 576 : NUM_THREADS; }
+__host__ __device__ constexpr int fwd_threads() { return SPLIT >= 2 ? 576 : NUM_THREADS; }
 
 template <int D, int SPLIT>
 __global__ void __launch_bounds__(fwd_threads<SPLIT>(), 1)
@@ -393,7 +427,7 @@ __global__ void __launch_bounds__(fwd_threads<SPLIT>(), 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 4 * SPLIT);
+      mbar_init(&p_full[t], SPLIT >= 2 ? 8 : 4);
       mbar_init(&o_final[t], 1);
     }
     *abort_flag = 0;
@@ -455,10 +489,19 @@ __global__ void __launch_bounds__(fwd_threads<SPLIT>(), 1)
       };
       auto issue_pv = [&](int t, int j) {
         const uint32_t va = smem_u32(sm + C::V_OFF + (j % C::VST) * C::TILE);
+        if (SPLIT == 3) {  // keys [64 h, 64 h + 64) into O_{t,h}
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk)
-          mma_ts(O_T[t], S_T[t] + (SPLIT == 2 && kk >= 4 ? 64 + (kk - 4) * 8 : kk * 8),
-                 desc(va + kk * 2048, 16384, 1024), id_o, (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BKV / 16; ++kk) {
+            const int hh = kk >> 2;
+            mma_ts(tmem + C::O_COL0 + t * 128 + hh * 64, S_T[t] + hh * 64 + (kk & 3) * 8,
+                   desc(va + kk * 2048, 16384, 1024), id_o, (j > 0 || (kk & 3) > 0) ? 1u : 0u);
+          }
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk)
+            mma_ts(O_T[t], S_T[t] + (SPLIT == 2 && kk >= 4 ? 64 + (kk - 4) * 8 : kk * 8),
+                   desc(va + kk * 2048, 16384, 1024), id_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
       };
       bool ok = mbar_wait(q_full, 0, abort_flag, 43) && mbar_wait(&k_full[0], 0, abort_flag, 44);
       if (ok) {
@@ -492,8 +535,8 @@ __global__ void __launch_bounds__(fwd_threads<SPLIT>(), 1)
         }
       }
     }
-  } else if (SPLIT == 2 && warp >= 2) {
-    softmax_split2<D>(p, tmem, warp, lane, q0, bh, nkv, s_full, p_full, o_final, abort_flag, xmax, xsum);
+  } else if (SPLIT >= 2 && warp >= 2) {
+    softmax_split2<D, SPLIT == 3>(p, tmem, warp, lane, q0, bh, nkv, s_full, p_full, o_final, abort_flag, xmax, xsum);
   } else if (SPLIT == 1 && warp >= 4) {
     // ---------------------------------------------------------------- softmax warpgroups
     const int t = (warp - 4) >> 2;
@@ -708,8 +751,9 @@ static int fwd2_impl(const void* q, const void* k, const void* v, void* o, void*
   const long long grid = (long long)p.npairs * B * H;
   if (grid == 0) return 0;
   if (D == 64)
-    return split == 2 ? launch<64, 2>(mq, mk, mv, p, (unsigned)grid, stream)
-                      : launch<64, 1>(mq, mk, mv, p, (unsigned)grid, stream);
+    return split == 3 ? launch<64, 3>(mq, mk, mv, p, (unsigned)grid, stream)
+           : split == 2 ? launch<64, 2>(mq, mk, mv, p, (unsigned)grid, stream)
+                        : launch<64, 1>(mq, mk, mv, p, (unsigned)grid, stream);
   return split == 2 ? launch<128, 2>(mq, mk, mv, p, (unsigned)grid, stream)
                     : launch<128, 1>(mq, mk, mv, p, (unsigned)grid, stream);
 }
@@ -722,10 +766,10 @@ extern "C" int vo_fmha_fwd2(const void* q, const void* k, const void* v, void* o
   return vo_fmha2::fwd2_impl(q, k, v, o, o2, out_split, lse, B, H, Sq, Skv, D, scale, causal, stream, 1);
 }
 
-// two softmax warpgroups per query tile (576 threads)
+// two softmax warpgroups per query tile (576 threads); head_dim 64: independent key halves
 extern "C" int vo_fmha_fwd3(const void* q, const void* k, const void* v, void* o, void* o2, int out_split, float* lse,
                             int B, int H, int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream) {
-  return vo_fmha2::fwd2_impl(q, k, v, o, o2, out_split, lse, B, H, Sq, Skv, D, scale, causal, stream, 2);
+  return vo_fmha2::fwd2_impl(q, k, v, o, o2, out_split, lse, B, H, Sq, Skv, D, scale, causal, stream, D == 64 ? 3 : 2);
 }
 
 extern "C" int vo_fmha_fwd2_error(int reset) {
