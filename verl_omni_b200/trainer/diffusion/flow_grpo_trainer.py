@@ -232,6 +232,7 @@ class PolicyGradientTrainer:
 
     # ------------------------------------------------------------------ one step
     def step(self, global_ids: Optional[list[int]] = None) -> dict:
+        self._check_ranks_alive()
         self.global_step += 1
         timer = M.PhaseTimer(self.device)
         t_start = time.perf_counter()
@@ -245,14 +246,42 @@ class PolicyGradientTrainer:
         with timer("update_weights"):
             self.rollout.update_weights(self.actor.engine.get_per_tensor_param())
         save_freq = int(self.config.trainer.save_freq)
-        if save_freq > 0 and self.global_step % save_freq == 0:
-            with timer("save_checkpoint"):
-                self.save_checkpoint()
+        if save_freq > 0:
+            esi = self._esi_close_to_expiration()
+            if esi or self.global_step >= self.total_steps or self.global_step % save_freq == 0:
+                if esi and self.rank == 0:
+                    print("Force saving checkpoint: ESI instance expiration approaching.")
+                with timer("save_checkpoint"):
+                    self.save_checkpoint()
         step_time = time.perf_counter() - t_start
+        self.max_steps_duration = max(getattr(self, "max_steps_duration", 0.0), step_time)
         metrics.update(rmetrics)
         metrics.update(M.compute_timing_metrics_diffusion(timer.timing, len(out)))
         metrics.update(M.compute_throughput_metrics_diffusion(step_time, len(out) * self.world, self.world))
         return metrics
+
+    def _esi_close_to_expiration(self) -> bool:
+        """Capacity-block expiration rule, agreed by every rank (one flag all-reduce, MAX)."""
+        from verl_omni_b200.utils.failure import should_save_ckpt_esi
+
+        flag = should_save_ckpt_esi(getattr(self, "max_steps_duration", 0.0),
+                                    float(self.config.trainer.get("esi_redundant_time", 0) or 0))
+        if self.world > 1:
+            flag = D.all_reduce_max(1.0 if flag else 0.0, device=self.device) > 0
+        return flag
+
+    def _check_ranks_alive(self) -> None:
+        """Host-side liveness check between steps (``trainer.heartbeat_timeout_s`` > 0 turns it on)."""
+        timeout = float(self.config.trainer.get("heartbeat_timeout_s", 0) or 0)
+        if timeout <= 0 or self.world <= 1:
+            return
+        if getattr(self, "_heartbeat", None) is None:
+            from verl_omni_b200.utils.failure import HeartbeatMonitor
+
+            port = int(os.environ.get("VERL_OMNI_HEARTBEAT_PORT", int(os.environ.get("MASTER_PORT", 29500)) + 17))
+            self._heartbeat = HeartbeatMonitor(self.rank, self.world, os.environ.get("MASTER_ADDR", "127.0.0.1"),
+                                               port, interval_s=min(1.0, timeout / 4), timeout_s=timeout)
+        self._heartbeat.check()
 
     def fit(self, steps: Optional[int] = None, log_fn=None) -> list[dict]:
         steps = steps or self.total_steps

@@ -15,6 +15,7 @@ from __future__ import annotations
 
 import asyncio
 import concurrent.futures
+import os
 from typing import Optional
 
 from verl_omni_b200.pipelines.request_batch import (DiffusionRequest, RolloutOutput, collate_requests, pack_key,
@@ -32,6 +33,8 @@ class DiffusionRolloutServer:
         self._task: Optional[asyncio.Task] = None
         self._pool = concurrent.futures.ThreadPoolExecutor(max_workers=1, thread_name_prefix="dit-rollout")
         self.num_engine_calls = 0
+        self._inflight: Optional[asyncio.Future] = None
+        self._pending: list = []  # taken off the queue, not yet in an engine call
 
     # ------------------------------------------------------------------ lifecycle
     def _ensure_started(self) -> None:
@@ -52,6 +55,42 @@ class DiffusionRolloutServer:
     def abort(self) -> None:
         """Stops the running engine call; its unfinished rows come back marked aborted."""
         self.engine.abort()
+
+    async def abort_all_requests(self, drain_timeout_s: Optional[float] = None) -> int:
+        """Drain, then hard abort (``vllm_omni_async_server.py:790-912`` of the reference).
+
+        Requests still queued are answered at once with a synthesized aborted output; the engine call in
+        flight gets ``drain_timeout_s`` (default ``VERL_OMNI_ABORT_DRAIN_TIMEOUT_S`` or 120 s) to finish,
+        after which the engine is told to abort and returns its unfinished rows marked aborted.  Returns
+        the number of queued requests answered without running, so callers never wait forever."""
+        if drain_timeout_s is None:
+            drain_timeout_s = float(os.environ.get("VERL_OMNI_ABORT_DRAIN_TIMEOUT_S", "120"))
+        waiting = list(self._pending)
+        if self._queue is not None:
+            while True:
+                try:
+                    waiting.append(self._queue.get_nowait())
+                except asyncio.QueueEmpty:
+                    break
+        n = 0
+        for req, fut in waiting:
+            if not fut.done():
+                fut.set_result(RolloutOutput({}, {"aborted": True, "request_id": req.request_id,
+                                                  "finish_reason": "abort"}))
+                n += 1
+        inflight = self._inflight
+        if inflight is not None and not inflight.done():
+            try:
+                await asyncio.wait_for(asyncio.shield(inflight), drain_timeout_s)
+            except asyncio.TimeoutError:
+                self.engine.abort()
+                try:
+                    await inflight
+                except Exception:  # noqa: BLE001 - the aborted call's error already reached its requests
+                    pass
+            except Exception:  # noqa: BLE001
+                pass
+        return n
 
     async def wake_up(self) -> None:
         self.engine.wake_up()
@@ -89,11 +128,17 @@ class DiffusionRolloutServer:
             groups: dict[tuple, list] = {}
             for req, fut in items:
                 groups.setdefault(pack_key(req, self._window(req)), []).append((req, fut))
+            self._pending = list(items)
             for group in groups.values():
                 for s in range(0, len(group), self.max_num_seqs):
-                    chunk = group[s:s + self.max_num_seqs]
+                    chunk = [(r, f) for r, f in group[s:s + self.max_num_seqs] if not f.done()]
+                    running = {id(f) for _, f in chunk}
+                    self._pending = [it for it in self._pending if id(it[1]) not in running and not it[1].done()]
+                    if not chunk:
+                        continue
                     try:
-                        outs = await loop.run_in_executor(self._pool, self._run, [r for r, _ in chunk])
+                        self._inflight = loop.run_in_executor(self._pool, self._run, [r for r, _ in chunk])
+                        outs = await self._inflight
                     except Exception as e:  # noqa: BLE001 - surface the failure to every waiting request
                         for _, fut in chunk:
                             if not fut.done():
