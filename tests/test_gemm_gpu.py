@@ -126,3 +126,85 @@ def test_fused_lora_linear_matches_unfused(E, epilogue):
     assert _rel(y, yr) < 2e-2
     for a, ref in ((x, xr), (A, Ar), (B, Br)):
         assert _rel(a.grad, ref.grad) < 3e-2, (a.shape, _rel(a.grad, ref.grad))
+
+
+PAIRS = [((16384, 1536, 1536), (5328, 1536, 1536)), ((1024, 4608, 1536), (333, 4608, 1536)),
+         ((5328, 6144, 1536), (200, 6144, 1536)), ((640, 1536, 6144), (2048, 1536, 6144))]
+
+
+@pytest.mark.parametrize("p0,p1", PAIRS)
+@pytest.mark.parametrize("epi", [1, 2, 3])
+def test_gemm_fwd_pair_matches_single(E, p0, p1, epi):
+    """A grouped launch computes every tile exactly as the single launch of the same shape."""
+    torch.manual_seed(5)
+    args = []
+    for (M, N, K) in (p0, p1):
+        S = M // 2 if M % 2 == 0 else M
+        x = torch.randn(M, K, device="cuda").bfloat16()
+        w = (torch.randn(N, K, device="cuda") / K ** 0.5).bfloat16()
+        b = torch.randn(N, device="cuda").bfloat16()
+        gate = torch.randn(M // S, N, device="cuda").bfloat16() if epi == 3 else None
+        res = torch.randn(M, N, device="cuda").bfloat16() if epi == 3 else None
+        args.append((x, w, b, gate, res, S))
+    outs = E.gemm_fwd_pair(*args[0], *args[1], epi)
+    for i, (x, w, b, gate, res, S) in enumerate(args):
+        two_sm_same = min(p0[0], p1[0]) >= 256 or x.shape[0] < 256
+        o, s = E.gemm_fwd(x, w, b, epi, gate, res, S)
+        if two_sm_same:  # same kernel variant as the single launch: bitwise identical
+            assert torch.equal(outs[2 * i], o)
+        lin = x.float() @ w.float().t() + b.float()
+        if epi == 1:
+            ref = lin
+        elif epi == 2:
+            ref = torch.nn.functional.gelu(lin, approximate="tanh")
+        else:
+            B = x.shape[0] // S
+            ref = res.float() + (lin.view(B, S, -1) * gate.float()[:, None]).view_as(lin)
+        assert _rel(outs[2 * i], ref) < 2e-2
+        if epi in (2, 3):
+            assert _rel(outs[2 * i + 1], lin) < 1e-2
+
+
+@pytest.mark.parametrize("p0,p1", PAIRS)
+def test_gemm_dgrad_wgrad_pair(E, p0, p1):
+    torch.manual_seed(6)
+    dys, ws, xs, gws = [], [], [], []
+    for (M, N, K) in (p0, p1):
+        dys.append(torch.randn(M, N, device="cuda").bfloat16())
+        ws.append((torch.randn(N, K, device="cuda") / N ** 0.5).bfloat16())
+        xs.append(torch.randn(M, K, device="cuda").bfloat16())
+        gws.append(torch.randn(N, K, device="cuda"))
+    dx0, dx1 = E.gemm_dgrad_pair(dys[0], ws[0], dys[1], ws[1])
+    for dx, dy, w in ((dx0, dys[0], ws[0]), (dx1, dys[1], ws[1])):
+        assert _rel(dx, dy.float() @ w.float()) < 1e-2
+    init = [g.clone() for g in gws]
+    E.gemm_wgrad_pair(dys[0], xs[0], gws[0], dys[1], xs[1], gws[1], True)
+    for g, g0, dy, x in zip(gws, init, dys, xs):
+        assert _rel(g, g0 + dy.float().t() @ x.float()) < 1e-3
+
+
+def test_linear_pair_autograd_matches_two_linears(E):
+    from verl_omni_b200.ops.linear import linear, linear_pair
+
+    torch.manual_seed(7)
+    B, Si, St, D = 4, 256, 77 + 3, 512
+    mk = lambda *s: torch.randn(*s, device="cuda").bfloat16()
+    for epi in ("none", "gelu", "gate_res"):
+        x0, x1 = mk(B, Si, D).requires_grad_(), mk(B, St, D).requires_grad_()
+        w0, w1 = (mk(2 * D, D) * 0.05).requires_grad_(), (mk(2 * D, D) * 0.05).requires_grad_()
+        b0, b1 = mk(2 * D).requires_grad_(), mk(2 * D).requires_grad_()
+        g0 = mk(B, 2 * D).requires_grad_() if epi == "gate_res" else None
+        g1 = mk(B, 2 * D).requires_grad_() if epi == "gate_res" else None
+        r0 = mk(B, Si, 2 * D).requires_grad_() if epi == "gate_res" else None
+        r1 = mk(B, St, 2 * D).requires_grad_() if epi == "gate_res" else None
+        leaves = [t for t in (x0, x1, w0, w1, b0, b1, g0, g1, r0, r1) if t is not None]
+        y0, y1 = linear_pair(x0, w0, b0, x1, w1, b1, epilogue=epi, gate0=g0, res0=r0, S0=Si, gate1=g1, res1=r1,
+                             S1=St)
+        gy0, gy1 = mk(*y0.shape), mk(*y1.shape)
+        gp = torch.autograd.grad((y0 * gy0).sum() + (y1 * gy1).sum(), leaves)
+        z0 = linear(x0, w0, b0, epilogue=epi, gate=g0, res=r0, S=Si)
+        z1 = linear(x1, w1, b1, epilogue=epi, gate=g1, res=r1, S=St)
+        gs = torch.autograd.grad((z0 * gy0).sum() + (z1 * gy1).sum(), leaves)
+        assert torch.equal(y0, z0) and torch.equal(y1, z1)
+        for a, b in zip(gp, gs):
+            assert _rel(a, b) < 1e-2, epi

@@ -261,3 +261,27 @@ def test_group_norm_nhwc_matches_reference(C, H, silu):
         ref = torch.nn.functional.silu(ref)
     assert y.is_contiguous(memory_format=torch.channels_last)
     torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2)
+
+
+def test_qwen_image_gpu_matches_cpu():
+    """Qwen-Image-shaped blocks at sizes that take the native paths (grouped image/text GEMMs, split joint
+    attention with 256 image rows, head_dim 128) against the fp32 CPU model; then a masked prompt."""
+    from verl_omni_b200.models.qwen_image import QwenImageConfig, QwenImageDiT
+
+    torch.manual_seed(0)
+    cfg = QwenImageConfig(in_channels=4, hidden=256, heads=2, depth=2, joint_attention_dim=64)
+    m = QwenImageDiT(cfg)
+    x = torch.randn(2, 4, 32, 32)
+    t = torch.tensor([900.0, 300.0])
+    c = torch.randn(2, 128, 64)
+    ref = m(x, t, c)
+    mask = torch.ones(2, 128)
+    mask[1, 100:] = 0
+    ref_m = m(x, t, c, mask)
+    mg = m.cuda().bfloat16()
+    out = mg(x.cuda(), t.cuda(), c.cuda())
+    torch.testing.assert_close(out.cpu(), ref, rtol=5e-2, atol=5e-2)
+    out_m = mg(x.cuda(), t.cuda(), c.cuda(), mask.cuda())
+    torch.testing.assert_close(out_m.cpu(), ref_m, rtol=5e-2, atol=5e-2)
+    out_m.square().mean().backward()
+    assert all(torch.isfinite(p.grad).all() for p in mg.parameters() if p.grad is not None)

@@ -1,0 +1,76 @@
+"""Qwen-Image-shaped MMDiT (and the Edit variant) on CPU: shapes, masking, adapter registry, rope layout."""
+
+import torch
+
+from verl_omni_b200.models.qwen_image import QwenImageConfig, QwenImageDiT
+from verl_omni_b200.pipelines.model_base import DiffusionModelBase
+
+
+def _inputs(B=2, St=12, C=4, H=8, W=8):
+    g = torch.Generator().manual_seed(0)
+    lat = torch.randn(B, C, H, W, generator=g)
+    emb = torch.randn(B, St, 48, generator=g)
+    t = torch.tensor([900.0, 300.0])[:B]
+    return lat, t, emb
+
+
+def test_forward_shapes_and_backward():
+    torch.manual_seed(0)
+    m = QwenImageDiT(QwenImageConfig.tiny())
+    lat, t, emb = _inputs()
+    out = m(lat, t, emb)
+    assert out.shape == lat.shape and torch.isfinite(out).all()
+    out.square().mean().backward()
+    assert m.transformer_blocks[0].img_qkv.weight.grad is not None
+    assert m.txt_norm_weight.grad is not None
+
+
+def test_padded_prompt_tokens_do_not_change_the_output():
+    """Masked (right-padded) prompt positions are excluded from attention: changing their embeddings
+    leaves the prediction unchanged, changing a valid position does not."""
+    torch.manual_seed(0)
+    m = QwenImageDiT(QwenImageConfig.tiny()).eval()
+    lat, t, emb = _inputs()
+    mask = torch.ones(2, 12)
+    mask[0, 7:] = 0
+    mask[1, 10:] = 0
+    with torch.no_grad():
+        a = m(lat, t, emb, mask)
+        emb2 = emb.clone()
+        emb2[0, 9] += 5.0
+        emb2[1, 11] -= 3.0
+        b = m(lat, t, emb2, mask)
+        emb3 = emb.clone()
+        emb3[0, 2] += 5.0
+        c = m(lat, t, emb3, mask)
+    torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-5)
+    assert (a - c).abs().max() > 1e-4
+
+
+def test_edit_variant_appends_reference_tokens():
+    torch.manual_seed(0)
+    m = QwenImageDiT(QwenImageConfig.tiny()).eval()
+    lat, t, emb = _inputs()
+    ref = torch.randn_like(lat)
+    with torch.no_grad():
+        a = m(lat, t, emb, image_latents=ref)
+        b = m(lat, t, emb, image_latents=ref + 1.0)
+    assert a.shape == lat.shape
+    assert (a - b).abs().max() > 1e-4  # the reference image conditions the prediction
+    c, s = m._rope(4, 4, 1, 12, "cpu")
+    assert c.shape[0] == 2 * 16 + 12  # generated tokens, reference tokens, text
+
+
+def test_adapters_registered():
+    a = DiffusionModelBase.get("QwenImage", "flow_grpo")
+    assert a.true_cfg_renorm and a.scheduler_kind == "qwen_image"
+    assert DiffusionModelBase.get("QwenImage", "dpo") is a
+    e = DiffusionModelBase.get("QwenImageEdit", "flow_grpo")
+    assert "image_latents" in e.cond_keys()
+    m = QwenImageDiT(QwenImageConfig.tiny()).eval()
+    lat, t, emb = _inputs()
+    cond = {"prompt_embeds": emb, "prompt_embeds_mask": torch.ones(2, 12)}
+    with torch.no_grad():
+        v = a.predict(m, lat, t, cond, {"prompt_embeds": torch.zeros_like(emb),
+                                        "prompt_embeds_mask": torch.ones(2, 12)}, 4.0)
+    assert v.shape == lat.shape

@@ -43,6 +43,14 @@ std::vector<torch::Tensor> gemm_fwd(torch::Tensor x, torch::Tensor w, c10::optio
 torch::Tensor gemm_dgrad(torch::Tensor dy, torch::Tensor w, c10::optional<torch::Tensor> ext_a,
                          c10::optional<torch::Tensor> ext_b);
 void gemm_wgrad(torch::Tensor dy, torch::Tensor x, torch::Tensor out, bool accumulate);
+std::vector<torch::Tensor> gemm_fwd_pair(torch::Tensor x0, torch::Tensor w0, c10::optional<torch::Tensor> b0,
+                                         c10::optional<torch::Tensor> gate0, c10::optional<torch::Tensor> res0,
+                                         int64_t S0, torch::Tensor x1, torch::Tensor w1,
+                                         c10::optional<torch::Tensor> b1, c10::optional<torch::Tensor> gate1,
+                                         c10::optional<torch::Tensor> res1, int64_t S1, int64_t epi);
+std::vector<torch::Tensor> gemm_dgrad_pair(torch::Tensor dy0, torch::Tensor w0, torch::Tensor dy1, torch::Tensor w1);
+void gemm_wgrad_pair(torch::Tensor dy0, torch::Tensor x0, torch::Tensor out0, torch::Tensor dy1, torch::Tensor x1,
+                     torch::Tensor out1, bool accumulate);
 torch::Tensor gelu_tanh_bwd(torch::Tensor dy, torch::Tensor pre);
 int64_t gemm_error(bool reset);
 std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal, double scale,
@@ -91,6 +99,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_dgrad", &vo::gemm_dgrad, py::arg("dy"), py::arg("w"), py::arg("ext_a") = py::none(),
         py::arg("ext_b") = py::none());
   m.def("gemm_wgrad", &vo::gemm_wgrad);
+  m.def("gemm_fwd_pair", &vo::gemm_fwd_pair, "two linear forwards in one persistent GEMM launch");
+  m.def("gemm_dgrad_pair", &vo::gemm_dgrad_pair);
+  m.def("gemm_wgrad_pair", &vo::gemm_wgrad_pair);
   m.def("gelu_tanh_bwd", &vo::gelu_tanh_bwd);
   m.def("gemm_error", &vo::gemm_error);
   m.def("fmha_fwd", &vo::fmha_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("causal"), py::arg("scale"),

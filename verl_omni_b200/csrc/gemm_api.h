@@ -1,0 +1,48 @@
+// C interface of the tcgen05 GEMM (gemm_sm100.cu), shared by its torch bindings and other kernels' hosts.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace vo_gemm {
+
+enum Epi : int { EPI_NONE = 0, EPI_BIAS = 1, EPI_GELU = 2, EPI_GATE_RES = 3, EPI_F32_ACC = 4 };
+
+struct EpiParams {
+  int epi;
+  __nv_bfloat16* out;          // [M, N] bf16 (primary output)
+  __nv_bfloat16* out2;         // GELU: pre-activation; GATE_RES: linear output (saved for backward)
+  float* out_f32;              // F32_ACC: [M, N] fp32, accumulated
+  const __nv_bfloat16* bias;   // [N] or null
+  const __nv_bfloat16* gate;   // [M/S, gate_ld] (GATE_RES)
+  const __nv_bfloat16* res;    // [M, N] (GATE_RES)
+  int64_t gate_ld;
+  int S;  // rows per sample (GATE_RES)
+  int ldc;
+};
+
+// One GEMM of a grouped launch: C = A B^T (+ A2 B2^T), operand conventions as vo_gemm_launch_ext.
+struct GemmDesc {
+  const void* A;
+  const void* B;
+  const void* A2;
+  const void* B2;
+  int M, N, K, K2;
+  int64_t lda, ldb, lda2, ldb2;
+  int a_mn, b_mn, splits;
+  EpiParams ep;
+};
+
+constexpr int kMaxGroup = 2;
+
+}  // namespace vo_gemm
+
+extern "C" int vo_gemm_launch(const void* A, const void* B, int M, int N, int K, int64_t lda, int64_t ldb, int a_mn,
+                              int b_mn, int splits, vo_gemm::EpiParams ep, cudaStream_t stream);
+extern "C" int vo_gemm_launch_ext(const void* A, const void* B, const void* A2, const void* B2, int M, int N, int K,
+                                  int K2, int64_t lda, int64_t ldb, int64_t lda2, int64_t ldb2, int a_mn, int b_mn,
+                                  int splits, vo_gemm::EpiParams ep, cudaStream_t stream);
+// Up to kMaxGroup independent GEMMs in one persistent launch: their output tiles form one work list,
+// so a small GEMM fills the last partial wave of a large one instead of running its own tail.
+extern "C" int vo_gemm_launch_group(const vo_gemm::GemmDesc* d, int n, cudaStream_t stream);
+extern "C" int vo_gemm_error(int reset);

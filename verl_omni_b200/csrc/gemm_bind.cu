@@ -2,27 +2,7 @@
 // GELU(tanh) backward used with the fused GELU epilogue.
 #include "common.cuh"
 
-namespace vo_gemm {
-struct EpiParams {
-  int epi;
-  __nv_bfloat16* out;
-  __nv_bfloat16* out2;
-  float* out_f32;
-  const __nv_bfloat16* bias;
-  const __nv_bfloat16* gate;
-  const __nv_bfloat16* res;
-  int64_t gate_ld;
-  int S;
-  int ldc;
-};
-}  // namespace vo_gemm
-
-extern "C" int vo_gemm_launch(const void* A, const void* B, int M, int N, int K, int64_t lda, int64_t ldb, int a_mn,
-                              int b_mn, int splits, vo_gemm::EpiParams ep, cudaStream_t stream);
-extern "C" int vo_gemm_error(int reset);
-extern "C" int vo_gemm_launch_ext(const void* A, const void* B, const void* A2, const void* B2, int M, int N, int K,
-                                  int K2, int64_t lda, int64_t ldb, int64_t lda2, int64_t ldb2, int a_mn, int b_mn,
-                                  int splits, vo_gemm::EpiParams ep, cudaStream_t stream);
+#include "gemm_api.h"
 
 namespace vo {
 namespace {
@@ -57,35 +37,39 @@ __global__ void gelu_tanh_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const
 // the GATE_RES linear output (undefined tensor otherwise).
 // ext_a / ext_b (optional): extra reduction operands, out = x W^T + ext_a ext_b^T (+ epilogue) -- the
 // fused low-rank path: ext_a = x A_lora^T [M, r], ext_b = scale * B_lora [N, r].
-std::vector<torch::Tensor> gemm_fwd(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> b, int64_t epi,
-                                    c10::optional<torch::Tensor> gate, c10::optional<torch::Tensor> res, int64_t S,
-                                    c10::optional<torch::Tensor> ext_a, c10::optional<torch::Tensor> ext_b) {
+struct FwdArgs {
+  vo_gemm::GemmDesc d;
+  torch::Tensor out, saved, gate_c;
+};
+
+FwdArgs prep_fwd(const torch::Tensor& x, const torch::Tensor& w, const c10::optional<torch::Tensor>& b, int64_t epi,
+                 const c10::optional<torch::Tensor>& gate, const c10::optional<torch::Tensor>& res, int64_t S,
+                 const c10::optional<torch::Tensor>& ext_a, const c10::optional<torch::Tensor>& ext_b) {
   VO_CHECK_INPUT(x);
   VO_CHECK_INPUT(w);
   TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && w.scalar_type() == torch::kBFloat16, "bf16 GEMM operands");
-  c10::cuda::CUDAGuard g(x.device());
   const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
   TORCH_CHECK(w.size(1) == K, "shape mismatch");
   TORCH_CHECK(N % 8 == 0 && K % 8 == 0, "GEMM dims must be multiples of 8 (16-byte rows)");
-  auto out = torch::empty({M, N}, x.options());
-  torch::Tensor saved;
-  vo_gemm::EpiParams ep{};
+  FwdArgs a;
+  a.out = torch::empty({M, N}, x.options());
+  vo_gemm::EpiParams& ep = a.d.ep;
+  ep = vo_gemm::EpiParams{};
   ep.epi = (int)epi;
-  ep.out = bf(out);
+  ep.out = bf(a.out);
   ep.ldc = (int)N;
   ep.S = (int)S;
   if (b.has_value() && b->defined()) ep.bias = bf(*b);
   if (epi == 2 || epi == 3) {
-    saved = torch::empty({M, N}, x.options());
-    ep.out2 = bf(saved);
+    a.saved = torch::empty({M, N}, x.options());
+    ep.out2 = bf(a.saved);
   }
-  torch::Tensor gate_c;
   if (epi == 3) {
     TORCH_CHECK(gate.has_value() && res.has_value(), "GATE_RES needs gate and res");
     // a strided per-sample row view (an AdaLN chunk of the modulation output) is read in place
-    gate_c = (gate->dim() == 2 && gate->stride(1) == 1) ? *gate : gate->contiguous();
-    ep.gate = bf(gate_c);
-    ep.gate_ld = gate_c.stride(0);
+    a.gate_c = (gate->dim() == 2 && gate->stride(1) == 1) ? *gate : gate->contiguous();
+    ep.gate = bf(a.gate_c);
+    ep.gate_ld = a.gate_c.stride(0);
     TORCH_CHECK(res->is_contiguous() && res->numel() == M * N, "res must be contiguous [M, N]");
     ep.res = bf(*res);
   }
@@ -101,28 +85,64 @@ std::vector<torch::Tensor> gemm_fwd(torch::Tensor x, torch::Tensor w, c10::optio
     a2 = ext_a->data_ptr();
     b2 = ext_b->data_ptr();
   }
-  check_rc(vo_gemm_launch_ext(x.data_ptr(), w.data_ptr(), a2, b2, (int)M, (int)N, (int)K, (int)K2, K, K, K2, K2, 0, 0,
-                              1, ep, stream()),
-           "fwd");
+  a.d.A = x.data_ptr();
+  a.d.B = w.data_ptr();
+  a.d.A2 = a2;
+  a.d.B2 = b2;
+  a.d.M = (int)M;
+  a.d.N = (int)N;
+  a.d.K = (int)K;
+  a.d.K2 = (int)K2;
+  a.d.lda = K;
+  a.d.ldb = K;
+  a.d.lda2 = K2;
+  a.d.ldb2 = K2;
+  a.d.a_mn = 0;
+  a.d.b_mn = 0;
+  a.d.splits = 1;
+  return a;
+}
+
+std::vector<torch::Tensor> gemm_fwd(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> b, int64_t epi,
+                                    c10::optional<torch::Tensor> gate, c10::optional<torch::Tensor> res, int64_t S,
+                                    c10::optional<torch::Tensor> ext_a, c10::optional<torch::Tensor> ext_b) {
+  c10::cuda::CUDAGuard g(x.device());
+  FwdArgs a = prep_fwd(x, w, b, epi, gate, res, S, ext_a, ext_b);
+  check_rc(vo_gemm_launch_group(&a.d, 1, stream()), "fwd");
   count_launch();
-  return {out, saved};
+  return {a.out, a.saved};
+}
+
+// Two independent linear forwards (the image and text streams of a joint block) in one persistent
+// launch; same epilogue kind for both.  Returns (out0, saved0, out1, saved1).
+std::vector<torch::Tensor> gemm_fwd_pair(torch::Tensor x0, torch::Tensor w0, c10::optional<torch::Tensor> b0,
+                                         c10::optional<torch::Tensor> gate0, c10::optional<torch::Tensor> res0,
+                                         int64_t S0, torch::Tensor x1, torch::Tensor w1,
+                                         c10::optional<torch::Tensor> b1, c10::optional<torch::Tensor> gate1,
+                                         c10::optional<torch::Tensor> res1, int64_t S1, int64_t epi) {
+  c10::cuda::CUDAGuard g(x0.device());
+  const c10::optional<torch::Tensor> none;
+  FwdArgs a0 = prep_fwd(x0, w0, b0, epi, gate0, res0, S0, none, none);
+  FwdArgs a1 = prep_fwd(x1, w1, b1, epi, gate1, res1, S1, none, none);
+  vo_gemm::GemmDesc d[2] = {a0.d, a1.d};
+  check_rc(vo_gemm_launch_group(d, 2, stream()), "fwd pair");
+  count_launch();
+  return {a0.out, a0.saved, a1.out, a1.saved};
 }
 
 // dX[M, K] = dY[M, N] W[N, K] (+ ext_a[M, r] ext_b[r, K])   (B operands MN-major)
-torch::Tensor gemm_dgrad(torch::Tensor dy, torch::Tensor w, c10::optional<torch::Tensor> ext_a,
-                         c10::optional<torch::Tensor> ext_b) {
+vo_gemm::GemmDesc prep_dgrad(const torch::Tensor& dy, const torch::Tensor& w, const torch::Tensor& dx,
+                             const c10::optional<torch::Tensor>& ext_a, const c10::optional<torch::Tensor>& ext_b) {
   VO_CHECK_INPUT(dy);
   VO_CHECK_INPUT(w);
-  c10::cuda::CUDAGuard g(dy.device());
   const int64_t M = dy.size(0), N = dy.size(1), K = w.size(1);
+  TORCH_CHECK(w.size(0) == N, "shape mismatch");
   TORCH_CHECK(N % 8 == 0 && K % 8 == 0, "GEMM dims must be multiples of 8 (16-byte rows)");
-  auto dx = torch::empty({M, K}, dy.options());
-  vo_gemm::EpiParams ep{};
-  ep.epi = 0;
-  ep.out = bf(dx);
-  ep.ldc = (int)K;
+  vo_gemm::GemmDesc d{};
+  d.ep.epi = 0;
+  d.ep.out = bf(dx);
+  d.ep.ldc = (int)K;
   // GEMM: C[M, K] = sum_n dY(m, n) * W(n, k): GEMM-N = K, GEMM-K = N, B(col=k, red=n) = W[n, k] -> MN-major
-  const void *a2 = nullptr, *b2 = nullptr;
   int64_t R = 0;
   if (ext_a.has_value() && ext_a->defined()) {
     TORCH_CHECK(ext_b.has_value() && ext_b->defined(), "ext_a needs ext_b");
@@ -131,37 +151,95 @@ torch::Tensor gemm_dgrad(torch::Tensor dy, torch::Tensor w, c10::optional<torch:
     R = ext_a->size(1);
     TORCH_CHECK(ext_a->size(0) == M && ext_b->size(0) == R && ext_b->size(1) == K && R % 8 == 0,
                 "extension operands must be [M, r] and [r, K] with r % 8 == 0");
-    a2 = ext_a->data_ptr();
-    b2 = ext_b->data_ptr();
+    d.A2 = ext_a->data_ptr();
+    d.B2 = ext_b->data_ptr();
   }
-  check_rc(vo_gemm_launch_ext(dy.data_ptr(), w.data_ptr(), a2, b2, (int)M, (int)K, (int)N, (int)R, N, K, R, K, 0, 1, 1,
-                              ep, stream()),
-           "dgrad");
+  d.A = dy.data_ptr();
+  d.B = w.data_ptr();
+  d.M = (int)M;
+  d.N = (int)K;
+  d.K = (int)N;
+  d.K2 = (int)R;
+  d.lda = N;
+  d.ldb = K;
+  d.lda2 = R;
+  d.ldb2 = K;
+  d.a_mn = 0;
+  d.b_mn = 1;
+  d.splits = 1;
+  return d;
+}
+
+torch::Tensor gemm_dgrad(torch::Tensor dy, torch::Tensor w, c10::optional<torch::Tensor> ext_a,
+                         c10::optional<torch::Tensor> ext_b) {
+  c10::cuda::CUDAGuard g(dy.device());
+  auto dx = torch::empty({dy.size(0), w.size(1)}, dy.options());
+  vo_gemm::GemmDesc d = prep_dgrad(dy, w, dx, ext_a, ext_b);
+  check_rc(vo_gemm_launch_group(&d, 1, stream()), "dgrad");
   count_launch();
   return dx;
 }
 
+std::vector<torch::Tensor> gemm_dgrad_pair(torch::Tensor dy0, torch::Tensor w0, torch::Tensor dy1, torch::Tensor w1) {
+  c10::cuda::CUDAGuard g(dy0.device());
+  const c10::optional<torch::Tensor> none;
+  auto dx0 = torch::empty({dy0.size(0), w0.size(1)}, dy0.options());
+  auto dx1 = torch::empty({dy1.size(0), w1.size(1)}, dy1.options());
+  vo_gemm::GemmDesc d[2] = {prep_dgrad(dy0, w0, dx0, none, none), prep_dgrad(dy1, w1, dx1, none, none)};
+  check_rc(vo_gemm_launch_group(d, 2, stream()), "dgrad pair");
+  count_launch();
+  return {dx0, dx1};
+}
+
 // out[N, K] (+)= dY[M, N]^T X[M, K]   (both operands MN-major), fp32 output, split-K over M
-void gemm_wgrad(torch::Tensor dy, torch::Tensor x, torch::Tensor out, bool accumulate) {
+// `tiles_total`: output tiles of every problem in the launch (sizes the split so the launch fills the GPU).
+vo_gemm::GemmDesc prep_wgrad(const torch::Tensor& dy, const torch::Tensor& x, torch::Tensor& out, bool accumulate,
+                             int tiles_total) {
   VO_CHECK_INPUT(dy);
   VO_CHECK_INPUT(x);
   VO_CHECK_INPUT(out);
   TORCH_CHECK(out.scalar_type() == torch::kFloat32, "wgrad output must be fp32");
-  c10::cuda::CUDAGuard g(dy.device());
   const int64_t M = dy.size(0), N = dy.size(1), K = x.size(1);
+  TORCH_CHECK(x.size(0) == M, "shape mismatch");
   TORCH_CHECK(out.numel() == N * K, "wgrad output shape");
   TORCH_CHECK(N % 8 == 0 && K % 8 == 0, "GEMM dims must be multiples of 8 (16-byte rows)");
   if (!accumulate) out.zero_();
-  vo_gemm::EpiParams ep{};
-  ep.epi = 4;
-  ep.out_f32 = out.data_ptr<float>();
-  ep.ldc = (int)K;
-  const int tiles = (int)(((N + 127) / 128) * ((K + 255) / 256));
+  vo_gemm::GemmDesc d{};
+  d.ep.epi = 4;
+  d.ep.out_f32 = out.data_ptr<float>();
+  d.ep.ldc = (int)K;
   const int kblocks = (int)((M + 63) / 64);
-  int splits = std::max(1, std::min((2 * num_sms() + tiles - 1) / tiles, kblocks / 4));
+  d.splits = std::max(1, std::min((2 * num_sms() + tiles_total - 1) / tiles_total, kblocks / 4));
   // GEMM-M = N (rows of dW), GEMM-N = K, GEMM-K = M tokens; A(m=n, k=t) = dY[t, n] (MN-major), B = X[t, k] (MN-major)
-  check_rc(vo_gemm_launch(dy.data_ptr(), x.data_ptr(), (int)N, (int)K, (int)M, N, K, 1, 1, splits, ep, stream()),
-           "wgrad");
+  d.A = dy.data_ptr();
+  d.B = x.data_ptr();
+  d.M = (int)N;
+  d.N = (int)K;
+  d.K = (int)M;
+  d.lda = N;
+  d.ldb = K;
+  d.a_mn = 1;
+  d.b_mn = 1;
+  return d;
+}
+
+inline int wgrad_tiles(const torch::Tensor& dy, const torch::Tensor& x) {
+  return (int)(((dy.size(1) + 127) / 128) * ((x.size(1) + 255) / 256));
+}
+
+void gemm_wgrad(torch::Tensor dy, torch::Tensor x, torch::Tensor out, bool accumulate) {
+  c10::cuda::CUDAGuard g(dy.device());
+  vo_gemm::GemmDesc d = prep_wgrad(dy, x, out, accumulate, wgrad_tiles(dy, x));
+  check_rc(vo_gemm_launch_group(&d, 1, stream()), "wgrad");
+  count_launch();
+}
+
+void gemm_wgrad_pair(torch::Tensor dy0, torch::Tensor x0, torch::Tensor out0, torch::Tensor dy1, torch::Tensor x1,
+                     torch::Tensor out1, bool accumulate) {
+  c10::cuda::CUDAGuard g(dy0.device());
+  const int tiles = wgrad_tiles(dy0, x0) + wgrad_tiles(dy1, x1);
+  vo_gemm::GemmDesc d[2] = {prep_wgrad(dy0, x0, out0, accumulate, tiles), prep_wgrad(dy1, x1, out1, accumulate, tiles)};
+  check_rc(vo_gemm_launch_group(d, 2, stream()), "wgrad pair");
   count_launch();
 }
 

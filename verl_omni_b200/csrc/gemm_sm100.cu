@@ -24,6 +24,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include "gemm_api.h"
+
 namespace vo_gemm {
 
 constexpr int BM = 128;
@@ -36,21 +38,6 @@ constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int NUM_THREADS = 192;
 constexpr int TMEM_COLS = 512;
 constexpr unsigned long long WAIT_BUDGET = 8ull * 1000 * 1000 * 1000;  // ~4 s of SM clock
-
-enum Epi : int { EPI_NONE = 0, EPI_BIAS = 1, EPI_GELU = 2, EPI_GATE_RES = 3, EPI_F32_ACC = 4 };
-
-struct EpiParams {
-  int epi;
-  __nv_bfloat16* out;          // [M, N] bf16 (primary output)
-  __nv_bfloat16* out2;         // GELU: pre-activation; GATE_RES: linear output (saved for backward)
-  float* out_f32;              // F32_ACC: [M, N] fp32, accumulated
-  const __nv_bfloat16* bias;   // [N] or null
-  const __nv_bfloat16* gate;   // [M/S, gate_ld] (GATE_RES)
-  const __nv_bfloat16* res;    // [M, N] (GATE_RES)
-  int64_t gate_ld;
-  int S;  // rows per sample (GATE_RES)
-  int ldc;
-};
 
 __device__ int g_error = 0;
 
@@ -193,6 +180,30 @@ struct EpiMaps {
   CUtensorMap acc;   // fp32 [M, N], box {32, 32}, 128B swizzle (F32_ACC)
 };
 
+// One GEMM of a launch.  A launch runs kMaxGroup problems at most; their work units are numbered
+// consecutively (problem 0 first) and every role maps a unit to its problem with unit_of().
+struct Prob {
+  CUtensorMap a, b;
+  EpiMaps em;
+  ExtMaps xm;
+  Shape sh;
+  EpiParams ep;
+  int unit_begin;
+};
+struct Launch {
+  Prob p[kMaxGroup];
+  int nprob;
+  int units;
+};
+
+// Problem that owns work unit `u`; `local` = the unit's index inside that problem.  The launch lives
+// in kernel-parameter space (__grid_constant__), so the reference is read in place, not copied.
+__device__ __forceinline__ const Prob& unit_of(const Launch& L, int u, int& local) {
+  const int p = (L.nprob > 1 && u >= L.p[1].unit_begin) ? 1 : 0;
+  local = u - L.p[p].unit_begin;
+  return L.p[p];
+}
+
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map), "r"(src),
                "r"(c0), "r"(c1)
@@ -292,8 +303,7 @@ __device__ __forceinline__ void epilogue_rows(uint32_t tacc, int row0, int col_b
 
 // ------------------------------------------------------------------------------------ kernel
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Shape sh,
-                EpiParams ep, const __grid_constant__ EpiMaps em, const __grid_constant__ ExtMaps xm) {
+    gemm_kernel(const __grid_constant__ Launch L) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_a = smem;
@@ -320,8 +330,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(&map_a) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(&map_b) : "memory");
+    for (int q = 0; q < L.nprob; ++q) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&L.p[q].a) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&L.p[q].b) : "memory");
+    }
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_base_slot)),
@@ -333,7 +345,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
 
-  const int units = sh.tiles_m * sh.tiles_n * sh.splits;
+  const int units = L.units;
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -342,8 +354,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const int split = u % sh.splits;
-        const int tile = u / sh.splits;
+        int lu;
+        const Prob& P = unit_of(L, u, lu);
+        const Shape sh = P.sh;  // registers: the loops below re-read it per k-block
+        const int split = lu % sh.splits;
+        const int tile = lu / sh.splits;
         const int tm = tile / sh.tiles_n, tn = tile % sh.tiles_n;
         const int kb0 = split * sh.k_blocks_per_split;
         const int kb1 = min(sh.total_k_blocks, kb0 + sh.k_blocks_per_split);
@@ -356,8 +371,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint8_t* sa = stage_a + stage * A_STAGE_BYTES;
           uint8_t* sb = stage_b + stage * B_STAGE_BYTES;
           const bool ext = kb >= sh.kb_main;
-          const CUtensorMap* ma = ext ? &xm.a2 : &map_a;
-          const CUtensorMap* mb = ext ? &xm.b2 : &map_b;
+          const CUtensorMap* ma = ext ? &P.xm.a2 : &P.a;
+          const CUtensorMap* mb = ext ? &P.xm.b2 : &P.b;
           const int k0 = (ext ? kb - sh.kb_main : kb) * BK;
           if (sh.a_mn) {  // [K, M] row-major: two 64x64 boxes (M chunks)
             tma_load_2d(sa, ma, &full[stage], tm * BM, k0);
@@ -381,15 +396,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = make_idesc(sh.a_mn, sh.b_mn);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++it) {
-        const int split = u % sh.splits;
+        int lu;
+        const Prob& P = unit_of(L, u, lu);
+        const Shape sh = P.sh;  // registers: the loops below re-read it per k-block
+        const int split = lu % sh.splits;
         const int kb0 = split * sh.k_blocks_per_split;
         const int kb1 = min(sh.total_k_blocks, kb0 + sh.k_blocks_per_split);
+        const uint32_t idesc = make_idesc(sh.a_mn, sh.b_mn);
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, 2)) break;
@@ -426,13 +444,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint8_t* wbuf = epi_stage + (warp - 2) * EPI_WARP_BYTES;
     int it = 0, nchunk = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
-      const int tile = u / sh.splits;
+      int lu;
+      const Prob& P = unit_of(L, u, lu);
+      const Shape sh = P.sh;  // registers: the loops below re-read it per k-block
+      const int tile = lu / sh.splits;
       const int tm = tile / sh.tiles_n, tn = tile % sh.tiles_n;
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, 4)) break;
       tc_fence_after();
-      epilogue_rows(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, tm * BM + lane_base, tn * BN, sh, ep, em,
+      const EpiParams ep = P.ep;
+      epilogue_rows(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, tm * BM + lane_base, tn * BN, sh, ep, P.em,
                     wbuf, lane, nchunk);
       tc_fence_before();
       __syncwarp();
@@ -509,8 +531,7 @@ __host__ __device__ constexpr uint32_t make_idesc2(int a_mn, int b_mn) {
 }
 
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    gemm2sm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Shape sh,
-                   EpiParams ep, const __grid_constant__ EpiMaps em, const __grid_constant__ ExtMaps xm) {
+    gemm2sm_kernel(const __grid_constant__ Launch L) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* epi_stage = smem + STAGES2 * STAGE2_BYTES;
@@ -535,8 +556,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(&map_a) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(&map_b) : "memory");
+    for (int q = 0; q < L.nprob; ++q) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&L.p[q].a) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&L.p[q].b) : "memory");
+    }
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_base_slot)),
@@ -547,7 +570,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
-  const int units = sh.tiles_m * sh.tiles_n * sh.splits;  // tiles_m counts 256-row tiles here
+  const int units = L.units;  // tiles_m counts 256-row tiles in the 2-SM kernel
 
   if (warp == 0) {
     if (lane == 0) {
@@ -555,8 +578,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int u = pair; u < units && ok; u += npairs) {
-        const int split = u % sh.splits;
-        const int tile = u / sh.splits;
+        int lu;
+        const Prob& P = unit_of(L, u, lu);
+        const Shape sh = P.sh;  // registers: the loops below re-read it per k-block
+        const int split = lu % sh.splits;
+        const int tile = lu / sh.splits;
         const int tm = tile / sh.tiles_n, tn = tile % sh.tiles_n;
         const int kb0 = split * sh.k_blocks_per_split;
         const int kb1 = min(sh.total_k_blocks, kb0 + sh.k_blocks_per_split);
@@ -571,8 +597,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint8_t* sa = smem + stage * STAGE2_BYTES;
           uint8_t* sb = sa + BM * BK * 2;
           const bool ext = kb >= sh.kb_main;
-          const CUtensorMap* ma = ext ? &xm.a2 : &map_a;
-          const CUtensorMap* mb = ext ? &xm.b2 : &map_b;
+          const CUtensorMap* ma = ext ? &P.xm.a2 : &P.a;
+          const CUtensorMap* mb = ext ? &P.xm.b2 : &P.b;
           const int k0 = (ext ? kb - sh.kb_main : kb) * BK;
           if (sh.a_mn) {
             tma_load_2d_pair(sa, ma, bar0, m0, k0);
@@ -595,15 +621,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
-      const uint32_t idesc = make_idesc2(sh.a_mn, sh.b_mn);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
       for (int u = pair; u < units && ok; u += npairs, ++it) {
-        const int split = u % sh.splits;
+        int lu;
+        const Prob& P = unit_of(L, u, lu);
+        const Shape sh = P.sh;  // registers: the loops below re-read it per k-block
+        const int split = lu % sh.splits;
         const int kb0 = split * sh.k_blocks_per_split;
         const int kb1 = min(sh.total_k_blocks, kb0 + sh.k_blocks_per_split);
+        const uint32_t idesc = make_idesc2(sh.a_mn, sh.b_mn);
         const int acc = it & 1;
         if (!mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1, abort_flag, 32)) break;
         tc_fence_after();
@@ -638,13 +667,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint8_t* wbuf = epi_stage + (warp - 2) * EPI_WARP_BYTES;
     int it = 0, nchunk = 0;
     for (int u = pair; u < units; u += npairs, ++it) {
-      const int tile = u / sh.splits;
+      int lu;
+      const Prob& P = unit_of(L, u, lu);
+      const Shape sh = P.sh;  // registers: the loops below re-read it per k-block
+      const int tile = lu / sh.splits;
       const int tm = tile / sh.tiles_n, tn = tile % sh.tiles_n;
       const int acc = it & 1;
       if (!mbar_wait(&tfull[acc], (it >> 1) & 1, abort_flag, 34)) break;
       tc_fence_after();
+      const EpiParams ep = P.ep;
       epilogue_rows(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, tm * 256 + (int)rank * 128 + lane_base,
-                    tn * BN, sh, ep, em, wbuf, lane, nchunk);
+                    tn * BN, sh, ep, P.em, wbuf, lane, nchunk);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty0[acc]);
@@ -707,91 +740,107 @@ static int make_out_map(CUtensorMap* m, const void* ptr, bool f32, int64_t rows,
 static int g_num_sms = 0;
 static int g_use_2sm = -1;
 
+// Fills one problem of a launch (tensor maps, tile shape, epilogue); 0 or an error code.
+static int build_prob(const GemmDesc& d, bool two_sm, Prob* P) {
+  memset(P, 0, sizeof(Prob));
+  const bool has_ext = d.A2 != nullptr && d.B2 != nullptr && d.K2 > 0;
+  const EpiParams& ep = d.ep;
+  if ((d.lda * 2) % 16 || (d.ldb * 2) % 16) return -1;  // TMA strides must be 16-byte multiples
+  if ((reinterpret_cast<uintptr_t>(d.A) | reinterpret_cast<uintptr_t>(d.B)) & 15) return -2;
+  if (d.splits > 1 && ep.epi != EPI_F32_ACC) return -3;
+  int r;
+  // epilogue outputs go out through TMA: 16-byte aligned bases and row strides
+  if (ep.epi == EPI_F32_ACC) {
+    if ((reinterpret_cast<uintptr_t>(ep.out_f32) & 15) || (ep.ldc * 4) % 16) return -4;
+    if ((r = make_out_map(&P->em.acc, ep.out_f32, true, d.M, d.N, ep.ldc))) return r;
+  } else {
+    if ((reinterpret_cast<uintptr_t>(ep.out) & 15) || (ep.ldc * 2) % 16) return -4;
+    if ((r = make_out_map(&P->em.out, ep.out, false, d.M, d.N, ep.ldc))) return r;
+    if (ep.epi == EPI_GELU || ep.epi == EPI_GATE_RES) {
+      if (reinterpret_cast<uintptr_t>(ep.out2) & 15) return -4;
+      if ((r = make_out_map(&P->em.out2, ep.out2, false, d.M, d.N, ep.ldc))) return r;
+    }
+  }
+  // 2-SM tiles load 128 rows of A and 128 columns of B per CTA
+  r = d.a_mn ? make_map(&P->a, d.A, d.K, d.M, d.lda, 64, 64) : make_map(&P->a, d.A, d.M, d.K, d.lda, 64, BM);
+  if (r) return r;
+  r = d.b_mn ? make_map(&P->b, d.B, d.K, d.N, d.ldb, 64, 64)
+             : make_map(&P->b, d.B, d.N, d.K, d.ldb, 64, two_sm ? 128 : BN);
+  if (r) return r;
+  if (has_ext) {
+    if ((d.lda2 * 2) % 16 || (d.ldb2 * 2) % 16 ||
+        ((reinterpret_cast<uintptr_t>(d.A2) | reinterpret_cast<uintptr_t>(d.B2)) & 15))
+      return -5;
+    r = d.a_mn ? make_map(&P->xm.a2, d.A2, d.K2, d.M, d.lda2, 64, 64)
+               : make_map(&P->xm.a2, d.A2, d.M, d.K2, d.lda2, 64, BM);
+    if (r) return r;
+    r = d.b_mn ? make_map(&P->xm.b2, d.B2, d.K2, d.N, d.ldb2, 64, 64)
+               : make_map(&P->xm.b2, d.B2, d.N, d.K2, d.ldb2, 64, two_sm ? 128 : BN);
+    if (r) return r;
+  }
+  Shape& sh = P->sh;
+  sh.M = d.M;
+  sh.N = d.N;
+  sh.K = d.K;
+  sh.tiles_m = two_sm ? (d.M + 255) / 256 : (d.M + BM - 1) / BM;
+  sh.tiles_n = (d.N + BN - 1) / BN;
+  sh.kb_main = (d.K + BK - 1) / BK;
+  sh.total_k_blocks = sh.kb_main + (has_ext ? (d.K2 + BK - 1) / BK : 0);
+  int splits = d.splits < 1 ? 1 : d.splits;
+  if (splits > sh.total_k_blocks) splits = sh.total_k_blocks;
+  sh.k_blocks_per_split = (sh.total_k_blocks + splits - 1) / splits;
+  sh.splits = (sh.total_k_blocks + sh.k_blocks_per_split - 1) / sh.k_blocks_per_split;
+  sh.a_mn = d.a_mn;
+  sh.b_mn = d.b_mn;
+  P->ep = ep;
+  return 0;
+}
+
 }  // namespace vo_gemm
 
-// C-style launcher (no torch dependency).  Operand conventions:
+// C-style launchers (no torch dependency).  Operand conventions:
 //   a_mn == 0: A is row-major [M, K] (lda >= K);  a_mn == 1: A is row-major [K, M] (lda >= M)
 //   b_mn == 0: B is row-major [N, K] (ldb >= K);  b_mn == 1: B is row-major [K, N] (ldb >= N)
 // splits > 1 is only valid with EPI_F32_ACC (partial sums are reduced in global memory).
 // Returns 0 on success, otherwise a CUDA / driver error code.
 // General form: C = A B^T (+ A2 B2^T when A2 != null, K2 extra reduction columns, same majorness).
-extern "C" int vo_gemm_launch_ext(const void* A, const void* B, const void* A2, const void* B2, int M, int N, int K,
-                                  int K2, int64_t lda, int64_t ldb, int64_t lda2, int64_t ldb2, int a_mn, int b_mn,
-                                  int splits, vo_gemm::EpiParams ep, cudaStream_t stream) {
+extern "C" int vo_gemm_launch_group(const vo_gemm::GemmDesc* d, int n, cudaStream_t stream) {
   using namespace vo_gemm;
-  if (M <= 0 || N <= 0 || K <= 0) return 0;
-  const bool has_ext = A2 != nullptr && B2 != nullptr && K2 > 0;
-  if ((lda * 2) % 16 || (ldb * 2) % 16) return -1;  // TMA strides must be 16-byte multiples
-  if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) return -2;
-  if (splits > 1 && ep.epi != EPI_F32_ACC) return -3;
+  if (n < 1 || n > kMaxGroup) return -6;
   if (g_use_2sm < 0) {
     const char* e = getenv("VO_GEMM_2SM");
     g_use_2sm = (e && e[0] == '0') ? 0 : 1;
-  }
-  const bool two_sm = g_use_2sm && M >= 256;
-  CUtensorMap ma, mb;
-  int r;
-  // epilogue outputs go out through TMA: 16-byte aligned bases and row strides
-  EpiMaps em;
-  memset(&em, 0, sizeof(em));
-  if (ep.epi == EPI_F32_ACC) {
-    if ((reinterpret_cast<uintptr_t>(ep.out_f32) & 15) || (ep.ldc * 4) % 16) return -4;
-    r = make_out_map(&em.acc, ep.out_f32, true, M, N, ep.ldc);
-    if (r) return r;
-  } else {
-    if ((reinterpret_cast<uintptr_t>(ep.out) & 15) || (ep.ldc * 2) % 16) return -4;
-    r = make_out_map(&em.out, ep.out, false, M, N, ep.ldc);
-    if (r) return r;
-    if (ep.epi == EPI_GELU || ep.epi == EPI_GATE_RES) {
-      if (reinterpret_cast<uintptr_t>(ep.out2) & 15) return -4;
-      r = make_out_map(&em.out2, ep.out2, false, M, N, ep.ldc);
-      if (r) return r;
-    }
-  }
-  // 2-SM tiles load 128 rows of A and 128 columns of B per CTA
-  if (a_mn)
-    r = make_map(&ma, A, K, M, lda, 64, 64);
-  else
-    r = make_map(&ma, A, M, K, lda, 64, BM);
-  if (r) return r;
-  if (b_mn)
-    r = make_map(&mb, B, K, N, ldb, 64, 64);
-  else
-    r = make_map(&mb, B, N, K, ldb, 64, two_sm ? 128 : BN);
-  if (r) return r;
-  ExtMaps xm;
-  memset(&xm, 0, sizeof(xm));
-  if (has_ext) {
-    if ((lda2 * 2) % 16 || (ldb2 * 2) % 16 || ((reinterpret_cast<uintptr_t>(A2) | reinterpret_cast<uintptr_t>(B2)) & 15))
-      return -5;
-    r = a_mn ? make_map(&xm.a2, A2, K2, M, lda2, 64, 64) : make_map(&xm.a2, A2, M, K2, lda2, 64, BM);
-    if (r) return r;
-    r = b_mn ? make_map(&xm.b2, B2, K2, N, ldb2, 64, 64) : make_map(&xm.b2, B2, N, K2, ldb2, 64, two_sm ? 128 : BN);
-    if (r) return r;
   }
   if (!g_num_sms) {
     int dev;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM1_BYTES);
-    cudaFuncSetAttribute(gemm2sm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
-    cudaFuncSetAttribute(gemm2sm_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    cudaError_t e1 = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM1_BYTES);
+    cudaError_t e2 = cudaFuncSetAttribute(gemm2sm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
+    cudaError_t e3 = cudaFuncSetAttribute(gemm2sm_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess) {
+      g_num_sms = 0;
+      return (int)(e1 != cudaSuccess ? e1 : e2 != cudaSuccess ? e2 : e3);
+    }
   }
-  Shape sh;
-  sh.M = M;
-  sh.N = N;
-  sh.K = K;
-  sh.tiles_m = two_sm ? (M + 255) / 256 : (M + BM - 1) / BM;
-  sh.tiles_n = (N + BN - 1) / BN;
-  sh.kb_main = (K + BK - 1) / BK;
-  sh.total_k_blocks = sh.kb_main + (has_ext ? (K2 + BK - 1) / BK : 0);
-  splits = splits < 1 ? 1 : splits;
-  if (splits > sh.total_k_blocks) splits = sh.total_k_blocks;
-  sh.k_blocks_per_split = (sh.total_k_blocks + splits - 1) / splits;
-  sh.splits = (sh.total_k_blocks + sh.k_blocks_per_split - 1) / sh.k_blocks_per_split;
-  sh.a_mn = a_mn;
-  sh.b_mn = b_mn;
-  const int units = sh.tiles_m * sh.tiles_n * sh.splits;
+  // all problems of a launch share the kernel: the 2-SM form only when every one has >= 256 rows
+  bool two_sm = g_use_2sm != 0;
+  for (int i = 0; i < n; ++i)
+    if (d[i].M > 0 && d[i].N > 0 && d[i].K > 0 && d[i].M < 256) two_sm = false;
+  Launch L;
+  memset(&L, 0, sizeof(L));
+  int units = 0;
+  for (int i = 0; i < n; ++i) {
+    if (d[i].M <= 0 || d[i].N <= 0 || d[i].K <= 0) continue;
+    Prob* P = &L.p[L.nprob];
+    const int r = build_prob(d[i], two_sm, P);
+    if (r) return r;
+    P->unit_begin = units;
+    units += P->sh.tiles_m * P->sh.tiles_n * P->sh.splits;
+    ++L.nprob;
+  }
+  if (L.nprob == 0) return 0;
+  L.units = units;
   if (two_sm) {
     const int pairs = units < g_num_sms / 2 ? units : g_num_sms / 2;
     cudaLaunchConfig_t cfg = {};
@@ -806,12 +855,18 @@ extern "C" int vo_gemm_launch_ext(const void* A, const void* B, const void* A2, 
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm2sm_kernel, ma, mb, sh, ep, em, xm);
-    return (int)e;
+    return (int)cudaLaunchKernelEx(&cfg, gemm2sm_kernel, L);
   }
   const int grid = units < g_num_sms ? units : g_num_sms;
-  gemm_kernel<<<grid, NUM_THREADS, SMEM1_BYTES, stream>>>(ma, mb, sh, ep, em, xm);
+  gemm_kernel<<<grid, NUM_THREADS, SMEM1_BYTES, stream>>>(L);
   return (int)cudaGetLastError();
+}
+
+extern "C" int vo_gemm_launch_ext(const void* A, const void* B, const void* A2, const void* B2, int M, int N, int K,
+                                  int K2, int64_t lda, int64_t ldb, int64_t lda2, int64_t ldb2, int a_mn, int b_mn,
+                                  int splits, vo_gemm::EpiParams ep, cudaStream_t stream) {
+  vo_gemm::GemmDesc d{A, B, A2, B2, M, N, K, K2, lda, ldb, lda2, ldb2, a_mn, b_mn, splits, ep};
+  return vo_gemm_launch_group(&d, 1, stream);
 }
 
 extern "C" int vo_gemm_launch(const void* A, const void* B, int M, int N, int K, int64_t lda, int64_t ldb, int a_mn,

@@ -16,7 +16,8 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from verl_omni_b200.models.layers import Linear, RMSWeight, TimestepMLP, patchify, rope_nd, timestep_embedding, unpatchify
+from verl_omni_b200.models.layers import (Linear, RMSWeight, TimestepMLP, linear_pair, patchify, rope_nd,
+                                         timestep_embedding, unpatchify)
 from verl_omni_b200.ops.attention import attention, attention_split
 from verl_omni_b200.ops.norm import adaln_layernorm, qk_norm_split_into
 
@@ -61,7 +62,7 @@ class DoubleBlock(nn.Module):
             setattr(self, f"{s}_mlp_1", Linear(D, hid))
             setattr(self, f"{s}_mlp_2", Linear(hid, D))
 
-    def forward(self, x, c, temb_act, rope):
+    def forward(self, x, c, temb_act, rope, kv_len=None):
         B, Si, D = x.shape
         St = c.shape[1]
         H, dh = self.H, self.dh
@@ -70,18 +71,17 @@ class DoubleBlock(nn.Module):
         ht = adaln_layernorm(c, mt, 0, 1, 6, self.eps)
         S = Si + St
         mk = lambda: torch.empty(B, H, S, dh, device=x.device, dtype=x.dtype)  # noqa: E731
-        q, k, v = qk_norm_split_into(mk(), mk(), mk(), self.img_qkv(hi).reshape(B * Si, 3 * D),
-                                     self.img_norm_q.weight, self.img_norm_k.weight, Si, 0, rope=rope, eps=self.eps)
-        q, k, v = qk_norm_split_into(q, k, v, self.txt_qkv(ht).reshape(B * St, 3 * D), self.txt_norm_q.weight,
+        qkv_i, qkv_t = linear_pair(self.img_qkv, hi, self.txt_qkv, ht)
+        q, k, v = qk_norm_split_into(mk(), mk(), mk(), qkv_i.reshape(B * Si, 3 * D), self.img_norm_q.weight,
+                                     self.img_norm_k.weight, Si, 0, rope=rope, eps=self.eps)
+        q, k, v = qk_norm_split_into(q, k, v, qkv_t.reshape(B * St, 3 * D), self.txt_norm_q.weight,
                                      self.txt_norm_k.weight, St, Si, rope=rope, eps=self.eps)
-        o_img, o_txt = attention_split(q, k, v, Si)
+        o_img, o_txt = attention_split(q, k, v, Si, kv_len=kv_len)
         vi, vt = mi.view(B, 6, D), mt.view(B, 6, D)
-        x = self.img_out(o_img, epilogue="gate_res", gate=vi[:, 2], res=x, S=Si)
-        c = self.txt_out(o_txt, epilogue="gate_res", gate=vt[:, 2], res=c, S=St)
-        x = self.img_mlp_2(self.img_mlp_1(adaln_layernorm(x, mi, 3, 4, 6, self.eps), epilogue="gelu"),
-                           epilogue="gate_res", gate=vi[:, 5], res=x, S=Si)
-        c = self.txt_mlp_2(self.txt_mlp_1(adaln_layernorm(c, mt, 3, 4, 6, self.eps), epilogue="gelu"),
-                           epilogue="gate_res", gate=vt[:, 5], res=c, S=St)
+        x, c = linear_pair(self.img_out, o_img, self.txt_out, o_txt, "gate_res", vi[:, 2], x, Si, vt[:, 2], c, St)
+        ui, ut = linear_pair(self.img_mlp_1, adaln_layernorm(x, mi, 3, 4, 6, self.eps), self.txt_mlp_1,
+                             adaln_layernorm(c, mt, 3, 4, 6, self.eps), "gelu")
+        x, c = linear_pair(self.img_mlp_2, ui, self.txt_mlp_2, ut, "gate_res", vi[:, 5], x, Si, vt[:, 5], c, St)
         return x, c
 
 

@@ -32,6 +32,16 @@ class Linear(nn.Module):
         return L.linear(x, self.weight, self.bias, epilogue=epilogue, gate=gate, res=res, S=S)
 
 
+def linear_pair(m0: nn.Module, x0, m1: nn.Module, x1, epilogue: str = "none", gate0=None, res0=None, S0: int = 1,
+                gate1=None, res1=None, S1: int = 1):
+    """``(m0(x0, ...), m1(x1, ...))``; two plain :class:`Linear` modules share one grouped GEMM launch per
+    pass (forward, dgrad, wgrad), adapters and other module types run one after the other."""
+    if type(m0) is Linear and type(m1) is Linear:
+        return L.linear_pair(x0, m0.weight, m0.bias, x1, m1.weight, m1.bias, epilogue=epilogue, gate0=gate0,
+                             res0=res0, S0=S0, gate1=gate1, res1=res1, S1=S1)
+    return m0(x0, epilogue, gate0, res0, S0), m1(x1, epilogue, gate1, res1, S1)
+
+
 class RMSWeight(nn.Module):
     """Learned per-channel scale of an RMSNorm (the normalisation itself is fused elsewhere)."""
 

@@ -23,7 +23,8 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from verl_omni_b200.models.layers import Linear, RMSWeight, TimestepMLP, patchify, sincos_2d, timestep_embedding, unpatchify
+from verl_omni_b200.models.layers import (Linear, RMSWeight, TimestepMLP, linear_pair, patchify, sincos_2d,
+                                         timestep_embedding, unpatchify)
 from verl_omni_b200.ops.attention import attention, attention_split
 from verl_omni_b200.ops.norm import adaln_layernorm, qk_norm_split_into
 
@@ -94,8 +95,8 @@ class JointBlock(nn.Module):
         #              6 shift_msa2, 7 scale_msa2, 8 gate_msa2
         h = adaln_layernorm(x, mod, 0, 1, self.n_mod, self.eps)
         hc = adaln_layernorm(c, modc, 0, 1, self.n_mod_c, self.eps)
-        qkv = self.to_qkv(h).reshape(B * Si, 3 * D)
-        qkvc = self.add_qkv(hc).reshape(B * St, 3 * D)
+        qkv, qkvc = linear_pair(self.to_qkv, h, self.add_qkv, hc)
+        qkv, qkvc = qkv.reshape(B * Si, 3 * D), qkvc.reshape(B * St, 3 * D)
         S = Si + St
         dev, dt = x.device, x.dtype
         q = torch.empty(B, H, S, dh, device=dev, dtype=dt)
@@ -106,7 +107,12 @@ class JointBlock(nn.Module):
                                      eps=self.eps)
         o_img, o_txt = attention_split(q, k, v, Si)  # [B, Si, D], [B, St, D]
         gate_msa = mod.view(B, self.n_mod, D)[:, 2]
-        x_new = self.to_out(o_img, epilogue="gate_res", gate=gate_msa, res=x, S=Si)
+        mc = modc.view(B, self.n_mod_c, D)
+        if self.cpo:
+            x_new = self.to_out(o_img, epilogue="gate_res", gate=gate_msa, res=x, S=Si)
+        else:
+            x_new, c = linear_pair(self.to_out, o_img, self.to_add_out, o_txt, "gate_res", gate_msa, x, Si,
+                                   mc[:, 2], c, St)
         if self.dual:
             h2 = adaln_layernorm(x, mod, 6, 7, self.n_mod, self.eps)
             qkv2 = self.attn2_qkv(h2).reshape(B * Si, 3 * D)
@@ -119,15 +125,13 @@ class JointBlock(nn.Module):
             x_new = self.attn2_out(o2, epilogue="gate_res", gate=mod.view(B, self.n_mod, D)[:, 8], res=x_new, S=Si)
         x = x_new
         hm = adaln_layernorm(x, mod, 3, 4, self.n_mod, self.eps)
-        u = self.ff_1(hm, epilogue="gelu")
-        x = self.ff_2(u, epilogue="gate_res", gate=mod.view(B, self.n_mod, D)[:, 5], res=x, S=Si)
+        gate_mlp = mod.view(B, self.n_mod, D)[:, 5]
         if self.cpo:
-            return x, None
-        mc = modc.view(B, self.n_mod_c, D)
-        c = self.to_add_out(o_txt, epilogue="gate_res", gate=mc[:, 2], res=c, S=St)
+            u = self.ff_1(hm, epilogue="gelu")
+            return self.ff_2(u, epilogue="gate_res", gate=gate_mlp, res=x, S=Si), None
         hcm = adaln_layernorm(c, modc, 3, 4, self.n_mod_c, self.eps)
-        uc = self.ff_context_1(hcm, epilogue="gelu")
-        c = self.ff_context_2(uc, epilogue="gate_res", gate=mc[:, 5], res=c, S=St)
+        u, uc = linear_pair(self.ff_1, hm, self.ff_context_1, hcm, "gelu")
+        x, c = linear_pair(self.ff_2, u, self.ff_context_2, uc, "gate_res", gate_mlp, x, Si, mc[:, 5], c, St)
         return x, c
 
 

@@ -26,6 +26,12 @@ class ArchSpec:
     notes: str = ""
 
 
+def _qwen_build(tiny: bool):
+    from verl_omni_b200.models.qwen_image import QwenImageConfig, QwenImageDiT
+
+    return QwenImageDiT(QwenImageConfig.tiny() if tiny else QwenImageConfig.qwen_image())
+
+
 def _flux_build():
     from verl_omni_b200.models.flux import FluxConfig, FluxDiT
 
@@ -51,6 +57,21 @@ ARCHS: dict[str, ArchSpec] = {
         "flux_tiny", "FluxDiT", lambda: __import__("verl_omni_b200.models.flux", fromlist=["x"]).FluxDiT(
             __import__("verl_omni_b200.models.flux", fromlist=["x"]).FluxConfig.tiny()), (4, 8, 8),
         {"prompt_embeds": (12, 48), "pooled_prompt_embeds": (32,)}, reward="mlp", image_size=64),
+    "qwen_image": ArchSpec(
+        "qwen_image", "QwenImage", lambda: _qwen_build(False), (16, 128, 128),
+        {"prompt_embeds": (512, 3584), "prompt_embeds_mask": (512,)}, reward="vit", image_size=1024,
+        notes="60 joint blocks, hidden 3072, 24 heads x 128, 2x2-packed 16-ch latents, Qwen2.5-VL 3584-d text"),
+    "qwen_image_tiny": ArchSpec(
+        "qwen_image_tiny", "QwenImage", lambda: _qwen_build(True), (4, 8, 8),
+        {"prompt_embeds": (12, 48), "prompt_embeds_mask": (12,)}, reward="mlp", image_size=64),
+    "qwen_image_edit": ArchSpec(
+        "qwen_image_edit", "QwenImageEdit", lambda: _qwen_build(False), (16, 128, 128),
+        {"prompt_embeds": (512, 3584), "prompt_embeds_mask": (512,), "image_latents": (16, 128, 128)},
+        reward="vit", image_size=1024, notes="Qwen-Image-Edit: reference-image latents appended to the image tokens"),
+    "qwen_image_edit_tiny": ArchSpec(
+        "qwen_image_edit_tiny", "QwenImageEdit", lambda: _qwen_build(True), (4, 8, 8),
+        {"prompt_embeds": (12, 48), "prompt_embeds_mask": (12,), "image_latents": (4, 8, 8)}, reward="mlp",
+        image_size=64),
     "wan_tiny": ArchSpec(
         "wan_tiny", "WanDiT", lambda: DiT(DiTConfig(in_channels=4, out_channels=4, hidden=128, heads=2, depth=2,
                                                     ffn=256, text_dim=48)), (4, 3, 8, 8),

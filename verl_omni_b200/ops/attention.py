@@ -78,7 +78,8 @@ class _FMHASplit(torch.autograd.Function):
 
 
 def attention_split(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, split: int, causal: bool = False,
-                    scale: Optional[float] = None) -> tuple[torch.Tensor, torch.Tensor]:
+                    scale: Optional[float] = None, kv_len: Optional[torch.Tensor] = None
+                    ) -> tuple[torch.Tensor, torch.Tensor]:
     """Joint attention returning ``(o[:, :split], o[:, split:])`` as two ``[B, *, H*Dh]`` tensors.
 
     The tcgen05 forward writes each query row straight into its half (the image / text streams of an
@@ -87,18 +88,25 @@ def attention_split(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, split: in
     """
     B, H, S, Dh = q.shape
     scale = scale if scale is not None else 1.0 / math.sqrt(Dh)
-    if (q.is_cuda and _native() and Dh in (64, 128) and q.dtype == torch.bfloat16 and _FWD_VERSION >= 2
-            and 0 < split < S and split % 128 == 0):
+    if (kv_len is None and q.is_cuda and _native() and Dh in (64, 128) and q.dtype == torch.bfloat16
+            and _FWD_VERSION >= 2 and 0 < split < S and split % 128 == 0):
         return _FMHASplit.apply(q, k, v, causal, scale, int(split))
-    o = attention(q, k, v, causal, scale)
+    o = attention(q, k, v, causal, scale, kv_len=kv_len)
     return o[:, :split].contiguous(), o[:, split:].contiguous()
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
-              scale: Optional[float] = None) -> torch.Tensor:
-    """softmax(q k^T * scale) v over [B, H, S, Dh]; returns [B, S, H*Dh]."""
+              scale: Optional[float] = None, kv_len: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """softmax(q k^T * scale) v over [B, H, S, Dh]; returns [B, S, H*Dh].
+
+    ``kv_len`` [B] (optional): keys at positions >= kv_len[b] are masked (padded prompt tokens at the tail
+    of a joint sequence); that case runs on SDPA with a boolean key mask."""
     B, H, S, Dh = q.shape
     scale = scale if scale is not None else 1.0 / math.sqrt(Dh)
+    if kv_len is not None:
+        keep = torch.arange(k.shape[2], device=q.device)[None, :] < kv_len.to(q.device)[:, None]
+        o = F.scaled_dot_product_attention(q, k, v, attn_mask=keep[:, None, None, :], is_causal=False, scale=scale)
+        return o.transpose(1, 2).reshape(B, S, H * Dh)
     # the tcgen05 kernels cover head_dim 64 / 128 (every DiT, ViT and LLM head here); other widths
     # (the VAE's single 512-wide mid-block head, miniature test models) use SDPA
     if q.is_cuda and _native() and Dh in (64, 128) and q.dtype == torch.bfloat16:

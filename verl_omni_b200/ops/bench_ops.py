@@ -101,6 +101,38 @@ def bench_gemm_sweep(a) -> list[dict]:
     return out
 
 
+# image / text stream pairs of the joint blocks (16 samples x 1024 image + 333 text tokens)
+SD35_PAIRS = [("qkv", 4608, 1536), ("out", 1536, 1536), ("ff1", 6144, 1536), ("ff2", 1536, 6144)]
+
+
+def bench_gemm_pair(a) -> list[dict]:
+    """Image + text linears as one grouped launch vs two launches (forward / dgrad / wgrad)."""
+    from verl_omni_b200.ops._ext import ext
+
+    e = ext()
+    Mi, Mt = 16 * 1024, 16 * 333
+    out = []
+    for name, N, K in SD35_PAIRS:
+        xs = [torch.randn(M, K, device="cuda").bfloat16() for M in (Mi, Mt)]
+        ws = [(torch.randn(N, K, device="cuda") / K ** 0.5).bfloat16() for _ in range(2)]
+        dys = [torch.randn(M, N, device="cuda").bfloat16() for M in (Mi, Mt)]
+        gws = [torch.zeros(N, K, device="cuda") for _ in range(2)]
+        flops = 2.0 * (Mi + Mt) * N * K
+        row = {"op": "gemm_pair", "name": name, "M": [Mi, Mt], "N": N, "K": K}
+        for kind, pair, two in (
+                ("fwd", lambda: e.gemm_fwd_pair(xs[0], ws[0], None, None, None, 1, xs[1], ws[1], None, None, None, 1, 0),
+                 lambda: (e.gemm_fwd(xs[0], ws[0], None, 0, None, None, 1), e.gemm_fwd(xs[1], ws[1], None, 0, None, None, 1))),
+                ("dgrad", lambda: e.gemm_dgrad_pair(dys[0], ws[0], dys[1], ws[1]),
+                 lambda: (e.gemm_dgrad(dys[0], ws[0]), e.gemm_dgrad(dys[1], ws[1]))),
+                ("wgrad", lambda: e.gemm_wgrad_pair(dys[0], xs[0], gws[0], dys[1], xs[1], gws[1], True),
+                 lambda: (e.gemm_wgrad(dys[0], xs[0], gws[0], True), e.gemm_wgrad(dys[1], xs[1], gws[1], True)))):
+            tp, tt = timeit(pair, a.iters), timeit(two, a.iters)
+            row[kind] = {"pair_ms": round(tp, 4), "two_launch_ms": round(tt, 4), "pair_tflops": round(flops / tp / 1e9, 1),
+                         "speedup": round(tt / tp, 3)}
+        out.append(row)
+    return out
+
+
 def bench_optstep(a) -> list[dict]:
     """Sharded optimizer step over ``--numel`` parameters on every rank (run under torchrun):
     NCCL reduce-scatter + AdamW + all-gather vs the fused peer-memory kernels.  Device time of the
@@ -212,7 +244,7 @@ def bench_adaln(a) -> list[dict]:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "gemm_sweep", "fmha", "sde", "adaln", "optstep"])
+    ap.add_argument("op", choices=["gemm", "gemm_sweep", "gemm_pair", "fmha", "sde", "adaln", "optstep"])
     ap.add_argument("--numel", type=int, default=2_240_000_000)
     ap.add_argument("--M", type=int, default=21712)
     ap.add_argument("--N", type=int, default=6144)
@@ -226,7 +258,7 @@ def main() -> None:
     ap.add_argument("--compare", action="store_true")
     a = ap.parse_args()
     pk = _peaks()
-    rows = {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "fmha": bench_fmha, "optstep": bench_optstep, "sde": bench_sde, "adaln": bench_adaln}[a.op](a)
+    rows = {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "gemm_pair": bench_gemm_pair, "fmha": bench_fmha, "optstep": bench_optstep, "sde": bench_sde, "adaln": bench_adaln}[a.op](a)
     for r in rows:
         if "tflops" in r:
             r[f"frac_of_{pk['src']}_gemm_peak"] = round(r["tflops"] / pk["tflops"], 3)

@@ -146,3 +146,36 @@ class FluxFlowGRPO(DiffusionModelBase):
     @classmethod
     def forward(cls, module, latents, timesteps, cond):
         return module(latents, timesteps, cond["prompt_embeds"], cond["pooled_prompt_embeds"])
+
+
+@DiffusionModelBase.register("QwenImage", ("flow_grpo", "mix_grpo", "diffusion_nft", "dpo"))
+class QwenImageFlowGRPO(DiffusionModelBase):
+    """Qwen-Image (``verl_omni/pipelines/qwen_image_flow_grpo/diffusers_training_adapter.py:66``): dynamic
+    shift from the image sequence length, true CFG with the guided prediction rescaled to the conditional
+    one's norm (``qwen_image_flow_grpo/common.py:32-40``), right-padded prompts with a mask."""
+
+    scheduler_kind = "qwen_image"
+    true_cfg_renorm = True
+
+    @classmethod
+    def cond_keys(cls):
+        return ("prompt_embeds", "prompt_embeds_mask")
+
+    @classmethod
+    def forward(cls, module, latents, timesteps, cond):
+        return module(latents, timesteps, cond["prompt_embeds"], cond.get("prompt_embeds_mask"))
+
+
+@DiffusionModelBase.register("QwenImageEdit", ("flow_grpo",))
+class QwenImageEditFlowGRPO(QwenImageFlowGRPO):
+    """Qwen-Image-Edit image-to-image (``verl_omni/pipelines/qwen_image_edit_flow_grpo/diffusers_training_adapter.py:31``):
+    the reference image's latents ride along as conditioning and are appended to the image tokens."""
+
+    @classmethod
+    def cond_keys(cls):
+        return ("prompt_embeds", "prompt_embeds_mask", "image_latents")
+
+    @classmethod
+    def forward(cls, module, latents, timesteps, cond):
+        return module(latents, timesteps, cond["prompt_embeds"], cond.get("prompt_embeds_mask"),
+                      image_latents=cond["image_latents"])

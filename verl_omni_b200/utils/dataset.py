@@ -43,6 +43,12 @@ class SyntheticPromptDataset:
             rows = [torch.randint(0, self.vocab, (self.token_len,), generator=self._gen(i)) for i in ids]
             tensors["input_ids"] = torch.stack(rows)
         for k, shape in self.cond_shapes.items():
+            if k.endswith("_mask"):
+                # right-padded prompt: a per-prompt valid length in [L/2, L]
+                L = shape[0]
+                lens = [int(torch.randint(L // 2, L + 1, (1,), generator=self._gen(i * 31 + 7)).item()) for i in ids]
+                tensors[k] = (torch.arange(L)[None, :] < torch.tensor(lens)[:, None]).to(self.embed_dtype)
+                continue
             rows = [torch.randn(shape, generator=self._gen(i * 31 + zlib.crc32(k.encode()) % 17)) for i in ids]
             tensors[k] = torch.stack(rows).to(self.embed_dtype)
         return DataProto(tensors, {"prompt_id": np.array(ids, dtype=object),
