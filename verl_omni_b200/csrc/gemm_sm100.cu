@@ -198,7 +198,14 @@ struct Launch {
 
 // Problem that owns work unit `u`; `local` = the unit's index inside that problem.  The launch lives
 // in kernel-parameter space (__grid_constant__), so the reference is read in place, not copied.
+// Single-problem launches (GROUPED = false) index the problem at a compile-time offset, so its fields
+// are plain kernel-parameter loads.
+template <bool GROUPED>
 __device__ __forceinline__ const Prob& unit_of(const Launch& L, int u, int& local) {
+  if (!GROUPED) {
+    local = u;
+    return L.p[0];
+  }
   const int p = (L.nprob > 1 && u >= L.p[1].unit_begin) ? 1 : 0;
   local = u - L.p[p].unit_begin;
   return L.p[p];
@@ -302,6 +309,7 @@ __device__ __forceinline__ void epilogue_rows(uint32_t tacc, int row0, int col_b
 }
 
 // ------------------------------------------------------------------------------------ kernel
+template <bool GROUPED>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ Launch L) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -355,7 +363,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
         int lu;
-        const Prob& P = unit_of(L, u, lu);
+        const Prob& P = unit_of<GROUPED>(L, u, lu);
         const Shape sh = P.sh;  // registers: the loops below re-read it per k-block
         const int split = lu % sh.splits;
         const int tile = lu / sh.splits;
@@ -402,7 +410,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++it) {
         int lu;
-        const Prob& P = unit_of(L, u, lu);
+        const Prob& P = unit_of<GROUPED>(L, u, lu);
         const Shape sh = P.sh;  // registers: the loops below re-read it per k-block
         const int split = lu % sh.splits;
         const int kb0 = split * sh.k_blocks_per_split;
@@ -445,7 +453,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int it = 0, nchunk = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
       int lu;
-      const Prob& P = unit_of(L, u, lu);
+      const Prob& P = unit_of<GROUPED>(L, u, lu);
       const Shape sh = P.sh;  // registers: the loops below re-read it per k-block
       const int tile = lu / sh.splits;
       const int tm = tile / sh.tiles_n, tn = tile % sh.tiles_n;
@@ -530,6 +538,7 @@ __host__ __device__ constexpr uint32_t make_idesc2(int a_mn, int b_mn) {
          ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 }
 
+template <bool GROUPED>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm2sm_kernel(const __grid_constant__ Launch L) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -579,7 +588,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       for (int u = pair; u < units && ok; u += npairs) {
         int lu;
-        const Prob& P = unit_of(L, u, lu);
+        const Prob& P = unit_of<GROUPED>(L, u, lu);
         const Shape sh = P.sh;  // registers: the loops below re-read it per k-block
         const int split = lu % sh.splits;
         const int tile = lu / sh.splits;
@@ -627,7 +636,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       for (int u = pair; u < units && ok; u += npairs, ++it) {
         int lu;
-        const Prob& P = unit_of(L, u, lu);
+        const Prob& P = unit_of<GROUPED>(L, u, lu);
         const Shape sh = P.sh;  // registers: the loops below re-read it per k-block
         const int split = lu % sh.splits;
         const int kb0 = split * sh.k_blocks_per_split;
@@ -668,7 +677,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int it = 0, nchunk = 0;
     for (int u = pair; u < units; u += npairs, ++it) {
       int lu;
-      const Prob& P = unit_of(L, u, lu);
+      const Prob& P = unit_of<GROUPED>(L, u, lu);
       const Shape sh = P.sh;  // registers: the loops below re-read it per k-block
       const int tile = lu / sh.splits;
       const int tm = tile / sh.tiles_n, tn = tile % sh.tiles_n;
@@ -815,13 +824,18 @@ extern "C" int vo_gemm_launch_group(const vo_gemm::GemmDesc* d, int n, cudaStrea
     int dev;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaError_t e1 = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM1_BYTES);
-    cudaError_t e2 = cudaFuncSetAttribute(gemm2sm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
-    cudaError_t e3 = cudaFuncSetAttribute(gemm2sm_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess) {
-      g_num_sms = 0;
-      return (int)(e1 != cudaSuccess ? e1 : e2 != cudaSuccess ? e2 : e3);
-    }
+    cudaError_t es[6] = {
+        cudaFuncSetAttribute(gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM1_BYTES),
+        cudaFuncSetAttribute(gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM1_BYTES),
+        cudaFuncSetAttribute(gemm2sm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES),
+        cudaFuncSetAttribute(gemm2sm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES),
+        cudaFuncSetAttribute(gemm2sm_kernel<false>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+        cudaFuncSetAttribute(gemm2sm_kernel<true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1)};
+    for (cudaError_t e : es)
+      if (e != cudaSuccess) {
+        g_num_sms = 0;
+        return (int)e;
+      }
   }
   // all problems of a launch share the kernel: the 2-SM form only when every one has >= 256 rows
   bool two_sm = g_use_2sm != 0;
@@ -855,10 +869,14 @@ extern "C" int vo_gemm_launch_group(const vo_gemm::GemmDesc* d, int n, cudaStrea
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return (int)cudaLaunchKernelEx(&cfg, gemm2sm_kernel, L);
+    return (int)(L.nprob > 1 ? cudaLaunchKernelEx(&cfg, gemm2sm_kernel<true>, L)
+                             : cudaLaunchKernelEx(&cfg, gemm2sm_kernel<false>, L));
   }
   const int grid = units < g_num_sms ? units : g_num_sms;
-  gemm_kernel<<<grid, NUM_THREADS, SMEM1_BYTES, stream>>>(L);
+  if (L.nprob > 1)
+    gemm_kernel<true><<<grid, NUM_THREADS, SMEM1_BYTES, stream>>>(L);
+  else
+    gemm_kernel<false><<<grid, NUM_THREADS, SMEM1_BYTES, stream>>>(L);
   return (int)cudaGetLastError();
 }
 

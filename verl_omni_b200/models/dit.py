@@ -21,6 +21,7 @@ import torch.nn.functional as F
 from verl_omni_b200.models.layers import (Linear, RMSWeight, TimestepMLP, patchify, patchify_3d, rope_nd,
                                           timestep_embedding, unpatchify, unpatchify_3d)
 from verl_omni_b200.ops.attention import attention
+from verl_omni_b200.parallel.ulysses import gather_sequence, local_rows, shard_sequence, ulysses_attention
 from verl_omni_b200.ops.norm import adaln_layernorm, layer_norm, qk_norm_split_into
 
 
@@ -68,7 +69,7 @@ class DiTBlock(nn.Module):
         self.ffn_1, self.ffn_2 = Linear(D, cfg.ffn), Linear(cfg.ffn, D)
         self.eps = cfg.eps
 
-    def forward(self, x, ctx, temb_proj, rope=None):
+    def forward(self, x, ctx, temb_proj, rope=None, sp_group=None):
         B, S, D = x.shape
         St = ctx.shape[1]
         H, dh = self.H, self.dh
@@ -78,7 +79,7 @@ class DiTBlock(nn.Module):
         mk = lambda n: torch.empty(B, H, n, dh, device=x.device, dtype=x.dtype)  # noqa: E731
         q, k, v = qk_norm_split_into(mk(S), mk(S), mk(S), qkv, self.norm_q.weight, self.norm_k.weight, S, 0,
                                      rope=rope, eps=self.eps)
-        o = attention(q, k, v)
+        o = ulysses_attention(q, k, v, sp_group)  # local queries; keys over the whole sequence
         x = self.o(o, epilogue="gate_res", gate=mod.view(B, 6, D)[:, 2], res=x, S=S)
         # cross attention (no gate)
         hn = F.layer_norm(x, (D,), self.norm3_w.to(x.dtype), self.norm3_b.to(x.dtype), self.eps)
@@ -146,14 +147,22 @@ class DiT(nn.Module):
         temb_proj = self.time_projection(temb_act)
         ctx = self.text_embedding_2(F.gelu(self.text_embedding_1(context.to(dt)), approximate="tanh"))
         rope = self._rope(*grid, x.device) if cfg.rope else None
+        sp = getattr(self, "sp_group", None)
+        if sp is not None:  # Ulysses: 1/sp of the video tokens per rank; the text context stays whole
+            S = x.shape[1]
+            x = shard_sequence(x, sp)
+            if rope is not None:
+                rope = (local_rows(rope[0], [S], sp), local_rows(rope[1], [S], sp))
         for blk in self.blocks:
             if self.gradient_checkpointing and torch.is_grad_enabled():
-                x = torch.utils.checkpoint.checkpoint(blk, x, ctx, temb_proj, rope, use_reentrant=False)
+                x = torch.utils.checkpoint.checkpoint(blk, x, ctx, temb_proj, rope, sp, use_reentrant=False)
             else:
-                x = blk(x, ctx, temb_proj, rope)
+                x = blk(x, ctx, temb_proj, rope, sp)
         mod = self.head_mod(temb_act)
         x = adaln_layernorm(x, mod, 0, 1, 2, cfg.eps)
         out = self.head(x)
+        if sp is not None:
+            out = gather_sequence(out, sp)
         if video:
             return unpatchify_3d(out, pt, ph, pw, cfg.out_channels, Fr, Hh, Ww).float()
         return unpatchify(out, ph, cfg.out_channels, Hh, Ww).float()

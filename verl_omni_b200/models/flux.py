@@ -18,7 +18,8 @@ import torch.nn.functional as F
 
 from verl_omni_b200.models.layers import (Linear, RMSWeight, TimestepMLP, linear_pair, patchify, rope_nd,
                                          timestep_embedding, unpatchify)
-from verl_omni_b200.ops.attention import attention, attention_split
+from verl_omni_b200.ops.attention import attention, attention_split  # noqa: F401
+from verl_omni_b200.parallel.ulysses import gather_sequence, joint_attention, local_rows, shard_sequence, ulysses_attention
 from verl_omni_b200.ops.norm import adaln_layernorm, qk_norm_split_into
 
 
@@ -62,7 +63,7 @@ class DoubleBlock(nn.Module):
             setattr(self, f"{s}_mlp_1", Linear(D, hid))
             setattr(self, f"{s}_mlp_2", Linear(hid, D))
 
-    def forward(self, x, c, temb_act, rope, kv_len=None):
+    def forward(self, x, c, temb_act, rope, kv_len=None, sp_group=None, key_mask=None):
         B, Si, D = x.shape
         St = c.shape[1]
         H, dh = self.H, self.dh
@@ -76,7 +77,7 @@ class DoubleBlock(nn.Module):
                                      self.img_norm_k.weight, Si, 0, rope=rope, eps=self.eps)
         q, k, v = qk_norm_split_into(q, k, v, qkv_t.reshape(B * St, 3 * D), self.txt_norm_q.weight,
                                      self.txt_norm_k.weight, St, Si, rope=rope, eps=self.eps)
-        o_img, o_txt = attention_split(q, k, v, Si, kv_len=kv_len)
+        o_img, o_txt = joint_attention(q, k, v, Si, sp_group=sp_group, kv_len=kv_len, key_mask=key_mask)
         vi, vt = mi.view(B, 6, D), mt.view(B, 6, D)
         x, c = linear_pair(self.img_out, o_img, self.txt_out, o_txt, "gate_res", vi[:, 2], x, Si, vt[:, 2], c, St)
         ui, ut = linear_pair(self.img_mlp_1, adaln_layernorm(x, mi, 3, 4, 6, self.eps), self.txt_mlp_1,
@@ -97,14 +98,14 @@ class SingleBlock(nn.Module):
         self.norm_q, self.norm_k = RMSWeight(self.dh), RMSWeight(self.dh)
         self.proj_out = Linear(D + hid, D)
 
-    def forward(self, x, temb_act, rope):
+    def forward(self, x, temb_act, rope, sp_group=None):
         B, S, D = x.shape
         m = self.mod(temb_act)
         h = adaln_layernorm(x, m, 0, 1, 3, self.eps)
         mk = lambda: torch.empty(B, self.H, S, self.dh, device=x.device, dtype=x.dtype)  # noqa: E731
         q, k, v = qk_norm_split_into(mk(), mk(), mk(), self.qkv(h).reshape(B * S, 3 * D), self.norm_q.weight,
                                      self.norm_k.weight, S, 0, rope=rope, eps=self.eps)
-        o = attention(q, k, v)
+        o = ulysses_attention(q, k, v, sp_group)
         a = self.mlp_in(h, epilogue="gelu")
         return self.proj_out(torch.cat([o, a], -1), epilogue="gate_res", gate=m.view(B, 3, D)[:, 2], res=x, S=S)
 
@@ -155,11 +156,19 @@ class FluxDiT(nn.Module):
         c = self.context_embedder(encoder_hidden_states.to(dt))
         Si, St = x.shape[1], c.shape[1]
         rope = self._rope(Hh // p, Ww // p, St, x.device)
+        sp = getattr(self, "sp_group", None)
+        if sp is not None:  # Ulysses: this rank keeps 1/sp of the image tokens and of the text tokens
+            x, c = shard_sequence(x, sp), shard_sequence(c, sp)
+            rope = (local_rows(rope[0], [Si, St], sp), local_rows(rope[1], [Si, St], sp))
+        Sl = x.shape[1]
         for blk in self.transformer_blocks:
-            x, c = blk(x, c, ta, rope)
+            x, c = blk(x, c, ta, rope, sp_group=sp)
         xs = torch.cat([x, c], 1)
         for blk in self.single_transformer_blocks:
-            xs = blk(xs, ta, rope)
-        x = xs[:, :Si].contiguous()
+            xs = blk(xs, ta, rope, sp_group=sp)
+        x = xs[:, :Sl].contiguous()
         x = adaln_layernorm(x, self.norm_out_linear(ta), 1, 0, 2, cfg.eps)
-        return unpatchify(self.proj_out(x), p, cfg.in_channels, Hh, Ww).float()
+        y = self.proj_out(x)
+        if sp is not None:
+            y = gather_sequence(y, sp)
+        return unpatchify(y, p, cfg.in_channels, Hh, Ww).float()

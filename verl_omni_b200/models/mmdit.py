@@ -25,8 +25,9 @@ import torch.nn.functional as F
 
 from verl_omni_b200.models.layers import (Linear, RMSWeight, TimestepMLP, linear_pair, patchify, sincos_2d,
                                          timestep_embedding, unpatchify)
-from verl_omni_b200.ops.attention import attention, attention_split
 from verl_omni_b200.ops.norm import adaln_layernorm, qk_norm_split_into
+from verl_omni_b200.parallel.ulysses import (gather_key_mask, gather_sequence, joint_attention, pad_to_multiple,
+                                             shard_sequence, sp_info, ulysses_attention)
 
 
 @dataclass
@@ -85,7 +86,7 @@ class JointBlock(nn.Module):
             self.norm2_q, self.norm2_k = RMSWeight(self.dh), RMSWeight(self.dh)
         self.eps = cfg.eps
 
-    def forward(self, x: torch.Tensor, c: torch.Tensor, temb_act: torch.Tensor):
+    def forward(self, x: torch.Tensor, c: torch.Tensor, temb_act: torch.Tensor, sp_group=None, key_mask=None):
         B, Si, D = x.shape
         St = c.shape[1]
         H, dh = self.H, self.dh
@@ -105,7 +106,7 @@ class JointBlock(nn.Module):
         q, k, v = qk_norm_split_into(q, k, v, qkv, self.norm_q.weight, self.norm_k.weight, Si, 0, eps=self.eps)
         q, k, v = qk_norm_split_into(q, k, v, qkvc, self.norm_added_q.weight, self.norm_added_k.weight, St, Si,
                                      eps=self.eps)
-        o_img, o_txt = attention_split(q, k, v, Si)  # [B, Si, D], [B, St, D]
+        o_img, o_txt = joint_attention(q, k, v, Si, sp_group=sp_group, key_mask=key_mask)  # [B, Si, D], [B, St, D]
         gate_msa = mod.view(B, self.n_mod, D)[:, 2]
         mc = modc.view(B, self.n_mod_c, D)
         if self.cpo:
@@ -121,7 +122,7 @@ class JointBlock(nn.Module):
             v2 = torch.empty_like(q2)
             q2, k2, v2 = qk_norm_split_into(q2, k2, v2, qkv2, self.norm2_q.weight, self.norm2_k.weight, Si, 0,
                                             eps=self.eps)
-            o2 = attention(q2, k2, v2)
+            o2 = ulysses_attention(q2, k2, v2, sp_group)
             x_new = self.attn2_out(o2, epilogue="gate_res", gate=mod.view(B, self.n_mod, D)[:, 8], res=x_new, S=Si)
         x = x_new
         hm = adaln_layernorm(x, mod, 3, 4, self.n_mod, self.eps)
@@ -176,12 +177,26 @@ class MMDiT(nn.Module):
         temb = self.time_embed(timestep_embedding(timestep, 256).to(dt)) + self.text_embed(pooled_projections.to(dt))
         temb_act = F.silu(temb)
         c = self.context_embedder(encoder_hidden_states.to(dt))
+        sp = getattr(self, "sp_group", None)
+        key_mask = None
+        if sp is not None:
+            # Ulysses: 1/sp of the image tokens and of the (zero-padded, masked) text tokens per rank
+            St = c.shape[1]
+            r, W = sp_info(sp)
+            c = pad_to_multiple(c, W, 1)
+            x, c = shard_sequence(x, sp), shard_sequence(c, sp)
+            if c.shape[1] * W != St:
+                txt_ok = (torch.arange(c.shape[1], device=c.device) + r * c.shape[1]) < St
+                local = torch.cat([torch.ones(x.shape[1], dtype=torch.bool, device=x.device), txt_ok])
+                key_mask = gather_key_mask(local[None].expand(B, -1), sp)
         for blk in self.transformer_blocks:
             if self.gradient_checkpointing and torch.is_grad_enabled():
-                x, c = torch.utils.checkpoint.checkpoint(blk, x, c, temb_act, use_reentrant=False)
+                x, c = torch.utils.checkpoint.checkpoint(blk, x, c, temb_act, sp, key_mask, use_reentrant=False)
             else:
-                x, c = blk(x, c, temb_act)
+                x, c = blk(x, c, temb_act, sp, key_mask)
         mod = self.norm_out_linear(temb_act)
         h = adaln_layernorm(x, mod, 1, 0, 2, cfg.eps)
         out = self.proj_out(h)
+        if sp is not None:
+            out = gather_sequence(out, sp)
         return unpatchify(out, p, cfg.out_channels, Hh, Ww).float()

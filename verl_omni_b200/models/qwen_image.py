@@ -29,6 +29,7 @@ import torch.nn.functional as F
 from verl_omni_b200.models.flux import DoubleBlock, FluxConfig
 from verl_omni_b200.models.layers import Linear, TimestepMLP, patchify, rope_nd, timestep_embedding, unpatchify
 from verl_omni_b200.ops.norm import adaln_layernorm
+from verl_omni_b200.parallel.ulysses import gather_key_mask, gather_sequence, local_rows, shard_sequence
 
 
 @dataclass
@@ -115,13 +116,26 @@ class QwenImageDiT(nn.Module):
         e = prompt_embeds.float()
         e = e * torch.rsqrt(e.pow(2).mean(-1, keepdim=True) + cfg.eps) * self.txt_norm_weight.float()
         c = self.txt_in(e.to(dt))
-        kv_len = None
-        if prompt_mask is not None and not bool(prompt_mask.all()):
+        Si, St = x.shape[1], c.shape[1]
+        masked = prompt_mask is not None and not bool(prompt_mask.all())
+        rope = self._rope(Hh // p, Ww // p, n_ref, St, x.device)
+        sp = getattr(self, "sp_group", None)
+        kv_len = key_mask = None
+        if sp is not None:  # Ulysses: this rank keeps 1/sp of the image tokens and of the text tokens
+            x, c = shard_sequence(x, sp), shard_sequence(c, sp)
+            rope = (local_rows(rope[0], [Si, St], sp), local_rows(rope[1], [Si, St], sp))
+            if masked:  # valid keys in the gathered order [img_0 txt_0 img_1 txt_1 ...]
+                local = torch.cat([torch.ones(B, x.shape[1], dtype=torch.bool, device=x.device),
+                                   shard_sequence(prompt_mask.to(x.device).bool(), sp)], 1)
+                key_mask = gather_key_mask(local, sp)
+        elif masked:
             # right-padded prompts: keys past image tokens + valid text tokens are masked in every block
-            kv_len = (x.shape[1] + prompt_mask.to(torch.int64).sum(1)).to(torch.int32)
-        rope = self._rope(Hh // p, Ww // p, n_ref, c.shape[1], x.device)
+            kv_len = (Si + prompt_mask.to(torch.int64).sum(1)).to(torch.int32)
         for blk in self.transformer_blocks:
-            x, c = blk(x, c, ta, rope, kv_len)
-        x = x[:, :Sg].contiguous() if n_ref else x
+            x, c = blk(x, c, ta, rope, kv_len, sp_group=sp, key_mask=key_mask)
         x = adaln_layernorm(x, self.norm_out_linear(ta), 1, 0, 2, cfg.eps)
-        return unpatchify(self.proj_out(x), p, cfg.in_channels, Hh, Ww).float()
+        y = self.proj_out(x)
+        if sp is not None:
+            y = gather_sequence(y, sp)
+        y = y[:, :Sg].contiguous() if n_ref else y
+        return unpatchify(y, p, cfg.in_channels, Hh, Ww).float()

@@ -96,15 +96,18 @@ def attention_split(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, split: in
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
-              scale: Optional[float] = None, kv_len: Optional[torch.Tensor] = None) -> torch.Tensor:
+              scale: Optional[float] = None, kv_len: Optional[torch.Tensor] = None,
+              key_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
     """softmax(q k^T * scale) v over [B, H, S, Dh]; returns [B, S, H*Dh].
 
     ``kv_len`` [B] (optional): keys at positions >= kv_len[b] are masked (padded prompt tokens at the tail
-    of a joint sequence); that case runs on SDPA with a boolean key mask."""
+    of a joint sequence); ``key_mask`` [B, Skv] bool (optional): keys where it is False are masked (the
+    same padding after a sequence-parallel gather interleaved it).  Masked cases run on SDPA."""
     B, H, S, Dh = q.shape
     scale = scale if scale is not None else 1.0 / math.sqrt(Dh)
-    if kv_len is not None:
-        keep = torch.arange(k.shape[2], device=q.device)[None, :] < kv_len.to(q.device)[:, None]
+    if kv_len is not None or key_mask is not None:
+        keep = key_mask.to(q.device, torch.bool) if key_mask is not None else (
+            torch.arange(k.shape[2], device=q.device)[None, :] < kv_len.to(q.device)[:, None])
         o = F.scaled_dot_product_attention(q, k, v, attn_mask=keep[:, None, None, :], is_causal=False, scale=scale)
         return o.transpose(1, 2).reshape(B, S, H * Dh)
     # the tcgen05 kernels cover head_dim 64 / 128 (every DiT, ViT and LLM head here); other widths

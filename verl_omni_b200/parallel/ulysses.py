@@ -90,15 +90,55 @@ def head_to_seq(o: torch.Tensor, group, head_dim: int) -> torch.Tensor:
 
 
 def ulysses_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, group, causal: bool = False,
-                      scale: Optional[float] = None) -> torch.Tensor:
-    """q/k/v [B, H, S/sp, D] (local tokens, all heads) -> token-major output [B, S/sp, H*D]."""
+                      scale: Optional[float] = None, key_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """q/k/v [B, H, S/sp, D] (local tokens, all heads) -> token-major output [B, S/sp, H*D].
+
+    ``key_mask`` [B, S] (optional) marks valid keys in the gathered order (rank-major concatenation of the
+    local sequences, see :func:`gather_key_mask`)."""
     from verl_omni_b200.ops.attention import attention
 
-    if D.world_size(group) == 1:
-        return attention(q, k, v, causal=causal, scale=scale)
+    if group is None or D.world_size(group) == 1:
+        return attention(q, k, v, causal=causal, scale=scale, key_mask=key_mask)
     Dh = q.shape[-1]
-    o = attention(seq_to_head(q, group), seq_to_head(k, group), seq_to_head(v, group), causal=causal, scale=scale)
+    o = attention(seq_to_head(q, group), seq_to_head(k, group), seq_to_head(v, group), causal=causal, scale=scale,
+                  key_mask=key_mask)
     return head_to_seq(o, group, Dh)
+
+
+def joint_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, split: int, *, sp_group=None,
+                    kv_len: Optional[torch.Tensor] = None, key_mask: Optional[torch.Tensor] = None):
+    """Joint image+text attention of a double-stream block: returns the image rows ``[:split]`` and text rows
+    ``[split:]`` of the (local) sequence.  Without sequence parallelism this is the split-output FMHA; with
+    it, q/k/v hold this rank's image and text tokens and the exchange runs around a full-sequence attention
+    (the gathered sequence is ordered [img_0 txt_0 img_1 txt_1 ...], which full attention does not see)."""
+    from verl_omni_b200.ops.attention import attention_split
+
+    if sp_group is None or D.world_size(sp_group) == 1:
+        if key_mask is not None:
+            from verl_omni_b200.ops.attention import attention
+
+            o = attention(q, k, v, key_mask=key_mask)
+            return o[:, :split].contiguous(), o[:, split:].contiguous()
+        return attention_split(q, k, v, split, kv_len=kv_len)
+    o = ulysses_attention(q, k, v, sp_group, key_mask=key_mask)
+    return o[:, :split].contiguous(), o[:, split:].contiguous()
+
+
+def gather_key_mask(local_valid: torch.Tensor, group) -> torch.Tensor:
+    """[B, S_local] bool validity of this rank's keys -> [B, S] in the gathered (rank-major) order."""
+    if group is None or D.world_size(group) == 1:
+        return local_valid
+    lv = local_valid.to(torch.uint8).contiguous()
+    parts = [torch.empty_like(lv) for _ in range(D.world_size(group))]
+    dist.all_gather(parts, lv, group=group)
+    return torch.cat(parts, 1).bool()
+
+
+def sp_info(group) -> tuple[int, int]:
+    """(rank, world) inside the sequence-parallel group (0, 1 without one)."""
+    if group is None:
+        return 0, 1
+    return D.rank(group), D.world_size(group)
 
 
 class _GatherSeq(torch.autograd.Function):
@@ -158,3 +198,19 @@ def make_sp_groups(sp: int):
     sp_groups = [dist.new_group(list(range(i, i + sp))) for i in range(0, ws, sp)]
     dp_groups = [dist.new_group(list(range(j, ws, sp))) for j in range(sp)]
     return sp_groups[r // sp], dp_groups[r % sp]
+
+
+def local_rows(table: torch.Tensor, segments: list[int], group) -> torch.Tensor:
+    """Rows of a per-position table (RoPE cos/sin) for this rank's slice of every segment: the table is laid
+    out segment after segment (e.g. image tokens then text tokens); each segment is split into ``world``
+    equal chunks and the local sequence is the concatenation of this rank's chunk of each segment."""
+    r, W = sp_info(group)
+    if W == 1:
+        return table
+    out, off = [], 0
+    for n in segments:
+        if n % W:
+            raise ValueError(f"segment length {n} is not divisible by the Ulysses degree {W}; pad first")
+        out.append(table[off + r * (n // W): off + (r + 1) * (n // W)])
+        off += n
+    return torch.cat(out, 0).contiguous()

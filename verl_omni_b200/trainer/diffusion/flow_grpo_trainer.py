@@ -59,10 +59,21 @@ class PolicyGradientTrainer:
         self.spec: ArchSpec = get_arch(arch or self.model_cfg.architecture or "tiny_dit")
         self.adapter = DiffusionModelBase.get(self.spec.adapter, self.model_cfg.algorithm)
         self.n = self.rollout_cfg.n
+        # Ulysses sequence parallelism: groups of `sp` consecutive ranks share their samples (each rank
+        # runs 1/sp of every sequence); data parallelism runs over the dp = world / sp groups
+        self.sp = int(getattr(self.actor_cfg.fsdp_config, "ulysses_sequence_parallel_size", 1) or 1)
+        if self.world % self.sp:
+            raise ValueError(f"world size {self.world} not divisible by ulysses_sequence_parallel_size={self.sp}")
+        self.dp, self.dp_rank = self.world // self.sp, self.rank // self.sp
+        self.sp_group = None
+        if self.sp > 1:
+            from verl_omni_b200.parallel.ulysses import make_sp_groups
+
+            self.sp_group, self.dp_group = make_sp_groups(self.sp)
         gbs = int(config.data.train_batch_size)
-        if gbs % self.world:
-            raise ValueError(f"data.train_batch_size={gbs} must be divisible by the world size {self.world}")
-        self.prompts_per_rank = gbs // self.world
+        if gbs % self.dp:
+            raise ValueError(f"data.train_batch_size={gbs} must be divisible by the data-parallel size {self.dp}")
+        self.prompts_per_rank = gbs // self.dp
         self.global_step = 0
         self.total_steps = int(config.trainer.total_training_steps or 1)
         seed = int(self.actor_cfg.fsdp_config.seed)
@@ -82,6 +93,10 @@ class PolicyGradientTrainer:
                         init=self.model_cfg.lora_init_weights)
         # with LoRA the reference policy is the base model (adapters disabled): no second copy
         ref_module = copy.deepcopy(module) if (self.actor_cfg.use_kl_loss and not self.lora) else None
+        if self.sp_group is not None:
+            module.sp_group = self.sp_group
+            if ref_module is not None:
+                ref_module.sp_group = self.sp_group
         T = self.rollout_cfg.pipeline.num_inference_steps
         seq = int(np.prod(self.spec.latent_shape[-2:])) // 4
         self.scheduler = self.adapter.build_scheduler(T, image_seq_len=seq, device=self.device)
@@ -117,6 +132,9 @@ class PolicyGradientTrainer:
         agent_cfg = config.actor_rollout_ref.rollout.get("agent", {}) or {}
         self.agent_manager = None
         if bool(agent_cfg.get("enable", False)):
+            if self.sp > 1:
+                raise NotImplementedError("agent-loop rollout with Ulysses sequence parallelism: every rank of a "
+                                          "sequence-parallel group must run the same engine batches")
             from verl_omni_b200.workers.agent_loop import DiffusionAgentLoopManager
             from verl_omni_b200.workers.rollout.server import DiffusionRolloutServer
 
@@ -148,19 +166,20 @@ class PolicyGradientTrainer:
 
     def local_prompt_ids(self, global_ids: list[int]) -> list[int]:
         p = self.prompts_per_rank
-        return global_ids[self.rank * p:(self.rank + 1) * p]
+        return global_ids[self.dp_rank * p:(self.dp_rank + 1) * p]
 
     def compute_advantage(self, scores: torch.Tensor, uid: np.ndarray, T: int) -> torch.Tensor:
-        """Group-normalised advantage; global std needs every rank's scores (one small all-gather)."""
-        all_scores = D.all_gather_object(scores.detach().float().cpu())
-        all_uid = D.all_gather_object(list(uid))
+        """Group-normalised advantage; global std needs every rank's scores (one small all-gather).  Ranks
+        of one sequence-parallel group hold the same samples: one copy per data-parallel rank is kept."""
+        all_scores = D.all_gather_object(scores.detach().float().cpu())[::self.sp]
+        all_uid = D.all_gather_object(list(uid))[::self.sp]
         g_scores = torch.cat(all_scores)
         g_uid = np.concatenate([np.asarray(u, dtype=object) for u in all_uid])
         est = algos.get_diffusion_adv_estimator_fn(self.algo_cfg.adv_estimator)
         adv, _ = est(g_scores[:, None].expand(-1, T), g_uid, norm_adv_by_std_in_grpo=self.algo_cfg.norm_adv_by_std_in_grpo,
                      global_std=self.algo_cfg.global_std)
         B = scores.shape[0]
-        return adv[self.rank * B:(self.rank + 1) * B]
+        return adv[self.dp_rank * B:(self.dp_rank + 1) * B]
 
     # ------------------------------------------------------------------ one step
     def generate(self, ids: list[int], *, rollout=None, seed_step: Optional[int] = None,
@@ -174,7 +193,7 @@ class PolicyGradientTrainer:
         cond.non_tensor_batch["uid"] = np.array([f"{pre}-{i}" for i in ids], dtype=object)
         gen = cond.repeat(self.n, interleave=True)
         base_seed = int(self.rollout_cfg.seed if self.rollout_cfg.seed is not None else 12345)
-        seed = (base_seed + step - 1) * 9973 + self.rank * 7 + (zlib.crc32(pre.encode()) & 0xFFFF) * 131
+        seed = (base_seed + step - 1) * 9973 + self.dp_rank * 7 + (zlib.crc32(pre.encode()) & 0xFFFF) * 131
         if self.agent_manager is not None and rollout is self.rollout:
             # per-row seeds from the step seed and each row's global index (prompt id x n + sample)
             gen.meta_info.update({"global_steps": step, "rollout_seed": seed})
@@ -221,7 +240,7 @@ class PolicyGradientTrainer:
         train_metrics = {}
         with timer("update_actor"):
             for _ in range(self.actor_cfg.ppo_epochs):
-                mini = max(1, int(self.actor_cfg.ppo_mini_batch_size) * self.n // self.world)
+                mini = max(1, int(self.actor_cfg.ppo_mini_batch_size) * self.n // self.dp)
                 for s in range(0, len(out), mini):
                     train_metrics = self.actor.train_batch(out.select_idxs(slice(s, min(len(out), s + mini))),
                                                            self.loss_fn)
@@ -257,7 +276,7 @@ class PolicyGradientTrainer:
         self.max_steps_duration = max(getattr(self, "max_steps_duration", 0.0), step_time)
         metrics.update(rmetrics)
         metrics.update(M.compute_timing_metrics_diffusion(timer.timing, len(out)))
-        metrics.update(M.compute_throughput_metrics_diffusion(step_time, len(out) * self.world, self.world))
+        metrics.update(M.compute_throughput_metrics_diffusion(step_time, len(out) * self.dp, self.world))
         return metrics
 
     def _esi_close_to_expiration(self) -> bool:

@@ -69,6 +69,9 @@ class PPODiffusionEngine:
         self.cfg = actor_cfg
         self.model_cfg = model_cfg
         self.device = device
+        # sequence-parallel ranks each back-propagate their own tokens' share: the loss is scaled by sp so the
+        # world-averaged gradient equals the data-parallel average
+        self.sp = int(getattr(actor_cfg.fsdp_config, "ulysses_sequence_parallel_size", 1) or 1)
 
     # ------------------------------------------------------------------ helpers
     def _micro_batches(self, data: DataProto, mbs: Optional[int]) -> list[DataProto]:
@@ -128,7 +131,7 @@ class PPODiffusionEngine:
                 out = self._step_out(mb, t)
                 d = {"old_log_probs": mb.batch["old_log_probs"][:, t].to(self.device),
                      "advantages": mb.batch["advantages"][:, t].to(self.device),
-                     "gradient_accumulation_steps": gas, "sp_size": 1}
+                     "gradient_accumulation_steps": gas, "sp_size": self.sp}
                 for k in ("ref_prev_sample_mean", "old_prev_sample_mean", "teacher_prev_sample_mean",
                           "rollout_is_weights"):
                     if k in mb.batch:
