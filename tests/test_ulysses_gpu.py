@@ -8,35 +8,93 @@ from tests._dist_util import run_ranks
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 
 
+def _grads(m, x, t, c, gy):
+    out = m(x, t, c)
+    (out.float() * gy).sum().backward()
+    g = {n: p.grad.float().clone() for n, p in m.named_parameters() if p.grad is not None}
+    m.zero_grad(set_to_none=True)
+    return out.float().detach(), g
+
+
 def _run(rank, world):
+    import copy
+
     import torch.distributed as dist
 
     from verl_omni_b200.models.qwen_image import QwenImageConfig, QwenImageDiT
 
     torch.manual_seed(0)
     cfg = QwenImageConfig(in_channels=4, hidden=256, heads=4, depth=2, joint_attention_dim=64)
-    m = QwenImageDiT(cfg).cuda().bfloat16()
+    m32 = QwenImageDiT(cfg).cuda()
+    m = copy.deepcopy(m32).bfloat16()
     g = torch.Generator().manual_seed(1)
     x = torch.randn(2, 4, 32, 32, generator=g).cuda()
     t = torch.tensor([900.0, 300.0]).cuda()
     c = torch.randn(2, 256, 64, generator=g).cuda()
     gy = torch.randn(x.shape, generator=torch.Generator().manual_seed(2)).cuda()
-    ref = m(x, t, c)
-    (ref * gy).sum().backward()
-    ref_g = {n: p.grad.float().clone() for n, p in m.named_parameters() if p.grad is not None}
-    m.zero_grad(set_to_none=True)
+    ref32, g32 = _grads(m32, x, t, c, gy)  # fp32 oracle (cuBLAS / SDPA)
+    ref16, g16 = _grads(m, x, t, c, gy)    # bf16 native kernels, one rank
     m.sp_group = dist.group.WORLD
-    out = m(x, t, c)
-    torch.testing.assert_close(out, ref.detach(), rtol=3e-2, atol=3e-2)
-    (out * gy).sum().backward()
-    for n, p in m.named_parameters():
-        if p.grad is None:
-            continue
-        gs = p.grad.float().clone()
+    out, gsp = _grads(m, x, t, c, gy)      # bf16 native kernels, SP=2
+    torch.testing.assert_close(out, ref16, rtol=3e-2, atol=3e-2)
+    rel = lambda a, b: float((a - b).norm() / (b.norm() + 1e-6))  # noqa: E731
+    for n, gs in gsp.items():
         dist.all_reduce(gs)
-        err = float((gs - ref_g[n]).norm() / (ref_g[n].norm() + 1e-6))
-        assert err < 5e-2, (n, err)
+        e16, esp = rel(g16[n], g32[n]), rel(gs, g32[n])
+        # the SP gradient is as close to the fp32 oracle as the one-rank bf16 gradient is
+        assert esp <= max(5e-2, 1.5 * e16 + 2e-2), (n, esp, e16)
 
 
 def test_qwen_image_ulysses_sp2_nccl():
     run_ranks(_run, 2, device="cuda")
+
+
+def _fused(rank, world):
+    import os
+
+    import torch.distributed as dist
+
+    from verl_omni_b200.models.dit import DiT, DiTConfig
+    from verl_omni_b200.models.mmdit import MMDiT, MMDiTConfig
+    from verl_omni_b200.models.qwen_image import QwenImageConfig, QwenImageDiT
+    from verl_omni_b200.parallel import ulysses_fused as UF
+
+    g = torch.Generator().manual_seed(1)
+    cases = [
+        ("qwen", QwenImageDiT(QwenImageConfig(in_channels=4, hidden=256, heads=4, depth=2, joint_attention_dim=64)),
+         (torch.randn(2, 4, 32, 32, generator=g), torch.tensor([900.0, 300.0]), torch.randn(2, 256, 64, generator=g))),
+        ("mmdit", MMDiT(MMDiTConfig(in_channels=4, out_channels=4, hidden=256, heads=4, depth=2, joint_attention_dim=64,
+                                    pooled_projection_dim=32, dual_attention_layers=1, sample_size=32,
+                                    pos_embed_max_size=32)),
+         (torch.randn(2, 4, 32, 32, generator=g), torch.tensor([900.0, 300.0]), torch.randn(2, 256, 64, generator=g),
+          torch.randn(2, 32, generator=g))),
+        ("wan", DiT(DiTConfig(in_channels=4, out_channels=4, hidden=256, heads=2, depth=2, ffn=512, text_dim=64)),
+         (torch.randn(2, 4, 4, 16, 16, generator=g), torch.tensor([900.0, 300.0]), torch.randn(2, 64, 64, generator=g))),
+    ]
+    for name, m, inputs in cases:
+        torch.manual_seed(0)
+        m = m.cuda().bfloat16().eval()
+        inputs = [t.cuda() for t in inputs]
+        with torch.no_grad():
+            ref = m(*inputs)
+            m.sp_group = dist.group.WORLD
+            os.environ["VO_ULYSSES_FUSED"] = "0"
+            nccl = m(*inputs)
+            os.environ["VO_ULYSSES_FUSED"] = "1"
+            assert UF.enabled(m.sp_group, torch.empty(1, device="cuda", dtype=torch.bfloat16),
+                              4 if name != "wan" else 2, 256)
+            fused = m(*inputs)
+            fused2 = m(*inputs)  # buffers reused across calls
+        torch.testing.assert_close(nccl, ref, rtol=3e-2, atol=3e-2, msg=lambda s: f"{name} nccl: {s}")
+        torch.testing.assert_close(fused, nccl, rtol=2e-2, atol=2e-2, msg=lambda s: f"{name} fused: {s}")
+        assert torch.equal(fused, fused2), name
+        del m.sp_group
+    from verl_omni_b200.ops._ext import ext
+
+    assert ext().gemm_error(True) == 0 and ext().fmha_error(True) == 0
+    UF.release_all()
+
+
+def test_ulysses_fused_exchange_matches_nccl_sp2():
+    """QKV-GEMM scatter + attention peer output (both exchanges inside kernels) == NCCL all-to-all path."""
+    run_ranks(_fused, 2, device="cuda")

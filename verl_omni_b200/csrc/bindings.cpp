@@ -48,6 +48,10 @@ std::vector<torch::Tensor> gemm_fwd_pair(torch::Tensor x0, torch::Tensor w0, c10
                                          int64_t S0, torch::Tensor x1, torch::Tensor w1,
                                          c10::optional<torch::Tensor> b1, c10::optional<torch::Tensor> gate1,
                                          c10::optional<torch::Tensor> res1, int64_t S1, int64_t epi);
+void gemm_scatter(torch::Tensor x0, torch::Tensor w0, c10::optional<torch::Tensor> b0, int64_t seg_rows0,
+                  int64_t dst_seq0, int64_t row_off0, c10::optional<torch::Tensor> x1, c10::optional<torch::Tensor> w1,
+                  c10::optional<torch::Tensor> b1, int64_t seg_rows1, int64_t dst_seq1, int64_t row_off1,
+                  std::vector<int64_t> peers, int64_t part_cols, int64_t dst_cols, int64_t dst_ld, int64_t dst_rows);
 std::vector<torch::Tensor> gemm_dgrad_pair(torch::Tensor dy0, torch::Tensor w0, torch::Tensor dy1, torch::Tensor w1);
 void gemm_wgrad_pair(torch::Tensor dy0, torch::Tensor x0, torch::Tensor out0, torch::Tensor dy1, torch::Tensor x1,
                      torch::Tensor out1, bool accumulate);
@@ -56,6 +60,8 @@ int64_t gemm_error(bool reset);
 std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal, double scale,
                                     int64_t version, int64_t split);
 int64_t fmha_error(bool reset);
+void fmha_fwd_peer(torch::Tensor q, torch::Tensor k, torch::Tensor v, std::vector<int64_t> peer_o,
+                   std::vector<int64_t> peer_o2, int64_t sl, int64_t si, int64_t htot, int64_t h0, double scale);
 std::vector<torch::Tensor> linear_bwd_prep(torch::Tensor dy, c10::optional<torch::Tensor> saved,
                                            c10::optional<torch::Tensor> gate, int64_t S, int64_t mode,
                                            c10::optional<torch::Tensor> db, bool db_accumulate);
@@ -101,12 +107,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_wgrad", &vo::gemm_wgrad);
   m.def("gemm_fwd_pair", &vo::gemm_fwd_pair, "two linear forwards in one persistent GEMM launch");
   m.def("gemm_dgrad_pair", &vo::gemm_dgrad_pair);
+  m.def("gemm_scatter", &vo::gemm_scatter, "QKV projection with the Ulysses head scatter in the epilogue");
   m.def("gemm_wgrad_pair", &vo::gemm_wgrad_pair);
   m.def("gelu_tanh_bwd", &vo::gelu_tanh_bwd);
   m.def("gemm_error", &vo::gemm_error);
   m.def("fmha_fwd", &vo::fmha_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("causal"), py::arg("scale"),
         py::arg("version") = 2, py::arg("split") = 0);
   m.def("fmha_error", &vo::fmha_error);
+  m.def("fmha_fwd_peer", &vo::fmha_fwd_peer, "Ulysses attention writing each output row to its owner rank");
   m.def("fmha_bwd", &vo::fmha_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
         py::arg("dO"), py::arg("causal"), py::arg("scale"), py::arg("version") = 1, py::arg("o2") = py::none(),
         py::arg("dO2") = py::none(), py::arg("split") = 0);

@@ -9,6 +9,9 @@ extern "C" int vo_fmha_fwd2(const void* q, const void* k, const void* v, void* o
 extern "C" int vo_fmha_fwd2_error(int reset);
 extern "C" int vo_fmha_fwd3(const void* q, const void* k, const void* v, void* o, void* o2, int out_split, float* lse,
                             int B, int H, int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream);
+extern "C" int vo_fmha_fwd_peer(const void* q, const void* k, const void* v, void* const* peer_o,
+                                void* const* peer_o2, int nranks, int sl, int si, int htot, int h0, float* lse, int B,
+                                int H, int Sq, int Skv, int D, float scale, cudaStream_t stream);
 extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const void* o, const void* dO,
                            const void* o2, const void* dO2, int split, const float* lse, void* dq, void* dk, void* dv,
                            float* delta, float* dq_acc, int B, int H, int Sq, int Skv, int D, float scale, int causal,
@@ -50,6 +53,33 @@ std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Ten
   count_launch();
   if (split > 0) return {o, lse, o2};
   return {o, lse};
+}
+
+// Ulysses attention with the output exchange fused into the epilogue (inference): q/k/v [B, H, Sq, D] hold
+// this rank's H heads of the sequence gathered from the group (sl rows per rank: si image rows, then text);
+// each output row is stored into the owning rank's buffer: peer_o[r] [B, si, htot, D] (image rows) or
+// peer_o2[r] [B, sl - si, htot, D] (text rows), this rank's heads at head offset h0.
+void fmha_fwd_peer(torch::Tensor q, torch::Tensor k, torch::Tensor v, std::vector<int64_t> peer_o,
+                   std::vector<int64_t> peer_o2, int64_t sl, int64_t si, int64_t htot, int64_t h0, double scale) {
+  VO_CHECK_INPUT(q);
+  VO_CHECK_INPUT(k);
+  VO_CHECK_INPUT(v);
+  TORCH_CHECK(q.scalar_type() == torch::kBFloat16, "bf16 attention inputs");
+  c10::cuda::CUDAGuard g(q.device());
+  const int B = q.size(0), H = q.size(1), Sq = q.size(2), D = q.size(3), Skv = k.size(2);
+  TORCH_CHECK(D == 64 || D == 128, "head_dim must be 64 or 128");
+  const int n = (int)peer_o.size();
+  TORCH_CHECK(n >= 1 && n <= 8 && (peer_o2.empty() || (int)peer_o2.size() == n), "1..8 peer buffers");
+  std::vector<void*> po(n), po2(n, nullptr);
+  for (int i = 0; i < n; ++i) {
+    po[i] = reinterpret_cast<void*>(peer_o[i]);
+    if (!peer_o2.empty()) po2[i] = reinterpret_cast<void*>(peer_o2[i]);
+  }
+  auto lse = torch::empty({B, H, Sq}, q.options().dtype(torch::kFloat32));
+  const int rc = vo_fmha_fwd_peer(q.data_ptr(), k.data_ptr(), v.data_ptr(), po.data(), po2.data(), n, (int)sl, (int)si,
+                                  (int)htot, (int)h0, lse.data_ptr<float>(), B, H, Sq, Skv, D, (float)scale, stream());
+  TORCH_CHECK(rc == 0, "tcgen05 FMHA (peer output) launch failed: code ", rc);
+  count_launch();
 }
 
 int64_t fmha_error(bool reset) {

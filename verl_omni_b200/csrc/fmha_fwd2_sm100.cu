@@ -25,6 +25,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
 
 namespace vo_fmha2 {
 
@@ -173,10 +174,25 @@ struct Params {
   __nv_bfloat16* o2;  // [B, Sq - split, H, D] (split > 0): rows q >= split
   int split;
   float* lse;         // [B*H, Sq] natural log
+  // Ulysses output exchange (peer_sl > 0): the query rows are a sequence gathered from the ranks of a
+  // sequence-parallel group (peer_sl rows per rank, image rows first); row q belongs to rank q / peer_sl
+  // and is stored straight into that rank's buffers over NVLink -- image rows into peer_o[r], text rows
+  // into peer_o2[r], both [B, rows, peer_htot, D] with this rank's heads at head offset peer_h0.
+  __nv_bfloat16* peer_o[8];
+  __nv_bfloat16* peer_o2[8];
+  int peer_sl, peer_si, peer_htot, peer_h0;
 };
 
 // token-major output row of query q (head h, batch b): one buffer, or split at `split` into two
 __device__ __forceinline__ __nv_bfloat16* out_row(const Params& p, int b, int q, int h, int D) {
+  if (p.peer_sl > 0) {
+    const int r = q / p.peer_sl, t = q - r * p.peer_sl;
+    const bool img = t < p.peer_si;
+    __nv_bfloat16* base = img ? p.peer_o[r] : p.peer_o2[r];
+    const int rows = img ? p.peer_si : p.peer_sl - p.peer_si;
+    const int row = img ? t : t - p.peer_si;
+    return base + (((int64_t)b * rows + row) * p.peer_htot + p.peer_h0 + h) * D;
+  }
   if (p.split > 0 && q >= p.split) return p.o2 + (((int64_t)b * (p.Sq - p.split) + (q - p.split)) * p.H + h) * D;
   const int rows = p.split > 0 ? p.split : p.Sq;
   return p.o + (((int64_t)b * rows + q) * p.H + h) * D;
@@ -387,7 +403,7 @@ __host__ __device__ constexpr int fwd_threads() { return SPLIT >= 2 ? 576 : NUM_
 template <int D, int SPLIT>
 __global__ void __launch_bounds__(fwd_threads<SPLIT>(), 1)
     fmha_fwd2_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
-                     const __grid_constant__ CUtensorMap mv, Params p) {
+                     const __grid_constant__ CUtensorMap mv, const __grid_constant__ Params p) {
   using C = Cfg<D>;
   extern __shared__ __align__(1024) uint8_t raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
@@ -726,8 +742,15 @@ static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMa
   return (int)cudaGetLastError();
 }
 
+struct PeerOut {
+  void* const* o;   // per rank: image-row output [B, si, htot, D]
+  void* const* o2;  // per rank: text-row output [B, sl - si, htot, D] (null entries when sl == si)
+  int nranks, sl, si, htot, h0;
+};
+
 static int fwd2_impl(const void* q, const void* k, const void* v, void* o, void* o2, int out_split, float* lse, int B,
-                     int H, int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream, int split) {
+                     int H, int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream, int split,
+                     const PeerOut* peer = nullptr) {
   if (D != 64 && D != 128) return -1;
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15)
     return -2;
@@ -737,6 +760,21 @@ static int fwd2_impl(const void* q, const void* k, const void* v, void* o, void*
   if (!r) r = map3(&mv, v, B * H, Skv, D);
   if (r) return r;
   Params p;
+  memset(&p, 0, sizeof(p));
+  if (peer) {
+    if (peer->nranks < 1 || peer->nranks > 8 || peer->sl * peer->nranks != Sq || peer->si < 1 || peer->si > peer->sl ||
+        peer->h0 + H > peer->htot)
+      return -4;
+    for (int r = 0; r < peer->nranks; ++r) {
+      p.peer_o[r] = reinterpret_cast<__nv_bfloat16*>(peer->o[r]);
+      p.peer_o2[r] = peer->sl > peer->si ? reinterpret_cast<__nv_bfloat16*>(peer->o2[r]) : nullptr;
+      if (!p.peer_o[r] || (peer->sl > peer->si && !p.peer_o2[r])) return -4;
+    }
+    p.peer_sl = peer->sl;
+    p.peer_si = peer->si;
+    p.peer_htot = peer->htot;
+    p.peer_h0 = peer->h0;
+  }
   p.Sq = Sq;
   p.Skv = Skv;
   p.H = H;
@@ -770,6 +808,17 @@ extern "C" int vo_fmha_fwd2(const void* q, const void* k, const void* v, void* o
 extern "C" int vo_fmha_fwd3(const void* q, const void* k, const void* v, void* o, void* o2, int out_split, float* lse,
                             int B, int H, int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream) {
   return vo_fmha2::fwd2_impl(q, k, v, o, o2, out_split, lse, B, H, Sq, Skv, D, scale, causal, stream, D == 64 ? 3 : 2);
+}
+
+// Ulysses attention with the output exchange fused into the epilogue: q/k/v hold this rank's heads of the
+// gathered sequence; every output row is written into the owning rank's image / text buffer (peer
+// pointers of a sequence-parallel group, this rank's heads at head offset h0 of htot).
+extern "C" int vo_fmha_fwd_peer(const void* q, const void* k, const void* v, void* const* peer_o,
+                                void* const* peer_o2, int nranks, int sl, int si, int htot, int h0, float* lse, int B,
+                                int H, int Sq, int Skv, int D, float scale, cudaStream_t stream) {
+  vo_fmha2::PeerOut po{peer_o, peer_o2, nranks, sl, si, htot, h0};
+  return vo_fmha2::fwd2_impl(q, k, v, nullptr, nullptr, 0, lse, B, H, Sq, Skv, D, scale, 0, stream, D == 64 ? 3 : 2,
+                             &po);
 }
 
 extern "C" int vo_fmha_fwd2_error(int reset) {

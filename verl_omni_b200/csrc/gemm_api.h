@@ -6,7 +6,18 @@
 
 namespace vo_gemm {
 
-enum Epi : int { EPI_NONE = 0, EPI_BIAS = 1, EPI_GELU = 2, EPI_GATE_RES = 3, EPI_F32_ACC = 4 };
+enum Epi : int { EPI_NONE = 0, EPI_BIAS = 1, EPI_GELU = 2, EPI_GATE_RES = 3, EPI_F32_ACC = 4, EPI_SCATTER = 5 };
+
+constexpr int kMaxPeers = 8;
+
+// EPI_SCATTER (Ulysses head scatter): the bf16 (+bias) output is stored straight into peer buffers.
+// Output column c of part q = c / part_cols goes to destination d = (c % part_cols) / dst_cols, column
+// q * dst_cols + c % dst_cols; output row m (sample m / seg_rows, token m % seg_rows) goes to row
+// (m / seg_rows) * dst_seq + row_off + m % seg_rows of a destination with row stride dst_ld elements.
+struct ScatterParams {
+  __nv_bfloat16* peers[kMaxPeers];
+  int part_cols, dst_cols, seg_rows, dst_seq, row_off, dst_ld;
+};
 
 struct EpiParams {
   int epi;
@@ -19,6 +30,7 @@ struct EpiParams {
   int64_t gate_ld;
   int S;  // rows per sample (GATE_RES)
   int ldc;
+  ScatterParams sc;  // EPI_SCATTER
 };
 
 // One GEMM of a grouped launch: C = A B^T (+ A2 B2^T), operand conventions as vo_gemm_launch_ext.

@@ -44,7 +44,8 @@ struct FwdArgs {
 
 FwdArgs prep_fwd(const torch::Tensor& x, const torch::Tensor& w, const c10::optional<torch::Tensor>& b, int64_t epi,
                  const c10::optional<torch::Tensor>& gate, const c10::optional<torch::Tensor>& res, int64_t S,
-                 const c10::optional<torch::Tensor>& ext_a, const c10::optional<torch::Tensor>& ext_b) {
+                 const c10::optional<torch::Tensor>& ext_a, const c10::optional<torch::Tensor>& ext_b,
+                 bool alloc_out = true) {
   VO_CHECK_INPUT(x);
   VO_CHECK_INPUT(w);
   TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && w.scalar_type() == torch::kBFloat16, "bf16 GEMM operands");
@@ -52,11 +53,11 @@ FwdArgs prep_fwd(const torch::Tensor& x, const torch::Tensor& w, const c10::opti
   TORCH_CHECK(w.size(1) == K, "shape mismatch");
   TORCH_CHECK(N % 8 == 0 && K % 8 == 0, "GEMM dims must be multiples of 8 (16-byte rows)");
   FwdArgs a;
-  a.out = torch::empty({M, N}, x.options());
+  if (alloc_out) a.out = torch::empty({M, N}, x.options());
   vo_gemm::EpiParams& ep = a.d.ep;
   ep = vo_gemm::EpiParams{};
   ep.epi = (int)epi;
-  ep.out = bf(a.out);
+  ep.out = alloc_out ? bf(a.out) : nullptr;
   ep.ldc = (int)N;
   ep.S = (int)S;
   if (b.has_value() && b->defined()) ep.bias = bf(*b);
@@ -128,6 +129,45 @@ std::vector<torch::Tensor> gemm_fwd_pair(torch::Tensor x0, torch::Tensor w0, c10
   check_rc(vo_gemm_launch_group(d, 2, stream()), "fwd pair");
   count_launch();
   return {a0.out, a0.saved, a1.out, a1.saved};
+}
+
+// Ulysses QKV projection with the head scatter fused into the epilogue: y = x W^T (+ b) for one or two
+// token segments (image rows x0, text rows x1 of this rank), each output row and 32-column chunk stored
+// straight into the buffer of the rank that owns its heads (`peers`: data pointers of the group's
+// destination buffers, dst_rows rows of dst_ld elements).  Row t of sample b of segment i lands at
+// destination row b * dst_seq_i + row_off_i + t.
+void gemm_scatter(torch::Tensor x0, torch::Tensor w0, c10::optional<torch::Tensor> b0, int64_t seg_rows0,
+                  int64_t dst_seq0, int64_t row_off0, c10::optional<torch::Tensor> x1, c10::optional<torch::Tensor> w1,
+                  c10::optional<torch::Tensor> b1, int64_t seg_rows1, int64_t dst_seq1, int64_t row_off1,
+                  std::vector<int64_t> peers, int64_t part_cols, int64_t dst_cols, int64_t dst_ld, int64_t dst_rows) {
+  c10::cuda::CUDAGuard g(x0.device());
+  TORCH_CHECK(!peers.empty() && (int64_t)peers.size() <= vo_gemm::kMaxPeers, "1..8 destination buffers");
+  TORCH_CHECK(part_cols == dst_cols * (int64_t)peers.size(), "part_cols must be dst_cols x number of peers");
+  const c10::optional<torch::Tensor> none;
+  vo_gemm::GemmDesc d[2];
+  int n = 0;
+  auto add = [&](const torch::Tensor& x, const torch::Tensor& w, const c10::optional<torch::Tensor>& b,
+                 int64_t seg_rows, int64_t dst_seq, int64_t row_off) {
+    TORCH_CHECK(seg_rows > 0 && x.size(0) % seg_rows == 0, "rows must be whole samples of seg_rows tokens");
+    const int64_t nb = x.size(0) / seg_rows;
+    TORCH_CHECK(row_off >= 0 && seg_rows <= dst_seq && (nb - 1) * dst_seq + row_off + seg_rows <= dst_rows,
+                "scatter rows fall outside the destination buffers");
+    FwdArgs a = prep_fwd(x, w, b, 1, none, none, 1, none, none, false);
+    a.d.ep.epi = vo_gemm::EPI_SCATTER;
+    vo_gemm::ScatterParams& sc = a.d.ep.sc;
+    for (size_t i = 0; i < peers.size(); ++i) sc.peers[i] = reinterpret_cast<__nv_bfloat16*>(peers[i]);
+    sc.part_cols = (int)part_cols;
+    sc.dst_cols = (int)dst_cols;
+    sc.seg_rows = (int)seg_rows;
+    sc.dst_seq = (int)dst_seq;
+    sc.row_off = (int)row_off;
+    sc.dst_ld = (int)dst_ld;
+    d[n++] = a.d;
+  };
+  add(x0, w0, b0, seg_rows0, dst_seq0, row_off0);
+  if (x1.has_value() && x1->defined()) add(*x1, *w1, b1, seg_rows1, dst_seq1, row_off1);
+  check_rc(vo_gemm_launch_group(d, n, stream()), "scatter");
+  count_launch();
 }
 
 // dX[M, K] = dY[M, N] W[N, K] (+ ext_a[M, r] ext_b[r, K])   (B operands MN-major)

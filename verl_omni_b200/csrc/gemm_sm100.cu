@@ -181,7 +181,7 @@ struct EpiMaps {
 };
 
 // One GEMM of a launch.  A launch runs kMaxGroup problems at most; their work units are numbered
-// consecutively (problem 0 first) and every role maps a unit to its problem with unit_of().
+// consecutively (problem 0 first) and every role maps a unit to its problem with prob_of().
 struct Prob {
   CUtensorMap a, b;
   EpiMaps em;
@@ -198,18 +198,22 @@ struct Launch {
 
 // Problem that owns work unit `u`; `local` = the unit's index inside that problem.  The launch lives
 // in kernel-parameter space (__grid_constant__), so the reference is read in place, not copied.
-// Single-problem launches (GROUPED = false) index the problem at a compile-time offset, so its fields
-// are plain kernel-parameter loads.
+// Problem index of work unit `u` (0 or 1) and the unit's index inside that problem.  Single-problem
+// launches (GROUPED = false) fold to problem 0; grouped launches hold exactly two problems.  Fields are then
+// read with PROB(field), a select between two compile-time parameter offsets, never a dynamic index into
+// parameter space.
 template <bool GROUPED>
-__device__ __forceinline__ const Prob& unit_of(const Launch& L, int u, int& local) {
+__device__ __forceinline__ int prob_of(const Launch& L, int u, int& local) {
   if (!GROUPED) {
     local = u;
-    return L.p[0];
+    return 0;
   }
-  const int p = (L.nprob > 1 && u >= L.p[1].unit_begin) ? 1 : 0;
-  local = u - L.p[p].unit_begin;
-  return L.p[p];
+  const int b1 = L.p[1].unit_begin;
+  local = u >= b1 ? u - b1 : u;
+  return u >= b1 ? 1 : 0;
 }
+#define PROB(field) (p ? L.p[1].field : L.p[0].field)
+#define PROB_ADDR(field) (p ? &L.p[1].field : &L.p[0].field)
 
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map), "r"(src),
@@ -249,6 +253,46 @@ __device__ __forceinline__ void stage_f32_row(uint8_t* buf, int lane, const floa
 
 // Drains this warp's 32 rows x BN columns of one accumulator.  `tacc` = TMEM address of (row 0 of
 // this warp, column 0 of the accumulator); rows [row0, row0 + 32), columns [col_base, col_base + BN).
+// EPI_SCATTER: each lane stores its row's 32 columns (64 B) into the destination rank's buffer with plain
+// 16-byte stores (peer memory over NVLink); `peers` points at the launch's parameter-space pointer table.
+template <typename ShapeT>
+__device__ __forceinline__ void epilogue_scatter(uint32_t tacc, int row0, int col_base, const ShapeT& sh,
+                                                 const EpiParams& ep, __nv_bfloat16* const* peers, int lane) {
+  const int row = row0 + lane;
+  const bool row_ok = row < sh.M;
+  const ScatterParams& sc = ep.sc;
+  int64_t drow = 0;
+  if (row_ok) {
+    const int b = row / sc.seg_rows;
+    drow = (int64_t)b * sc.dst_seq + sc.row_off + (row - b * sc.seg_rows);
+  }
+  for (int c = 0; c < BN / 32; ++c) {
+    uint32_t r[32];
+    tc_ld_32x32b_x32(tacc + c * 32, r);
+    const int col0 = col_base + c * 32;
+    if (col0 >= sh.N || !row_ok) continue;  // col0 warp-uniform; a 32-column chunk never crosses a destination
+    const int part = col0 / sc.part_cols, within = col0 - part * sc.part_cols;
+    const int d = within / sc.dst_cols;
+    const int dcol = part * sc.dst_cols + (within - d * sc.dst_cols);
+    __nv_bfloat16* dst = peers[d] + drow * sc.dst_ld + dcol;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      uint4 pk;
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float a = __uint_as_float(r[8 * u + 2 * q]), b2 = __uint_as_float(r[8 * u + 2 * q + 1]);
+        if (ep.bias) {
+          a += __bfloat162float(ep.bias[col0 + 8 * u + 2 * q]);
+          b2 += __bfloat162float(ep.bias[col0 + 8 * u + 2 * q + 1]);
+        }
+        h[q] = __floats2bfloat162_rn(a, b2);
+      }
+      *reinterpret_cast<uint4*>(dst + 8 * u) = pk;
+    }
+  }
+}
+
 template <typename ShapeT>
 __device__ __forceinline__ void epilogue_rows(uint32_t tacc, int row0, int col_base, const ShapeT& sh,
                                               const EpiParams& ep, const EpiMaps& em, uint8_t* wbuf, int lane,
@@ -363,8 +407,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
         int lu;
-        const Prob& P = unit_of<GROUPED>(L, u, lu);
-        const Shape sh = P.sh;  // registers: the loops below re-read it per k-block
+        const int p = prob_of<GROUPED>(L, u, lu);
+        const Shape sh = PROB(sh);
         const int split = lu % sh.splits;
         const int tile = lu / sh.splits;
         const int tm = tile / sh.tiles_n, tn = tile % sh.tiles_n;
@@ -379,8 +423,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint8_t* sa = stage_a + stage * A_STAGE_BYTES;
           uint8_t* sb = stage_b + stage * B_STAGE_BYTES;
           const bool ext = kb >= sh.kb_main;
-          const CUtensorMap* ma = ext ? &P.xm.a2 : &P.a;
-          const CUtensorMap* mb = ext ? &P.xm.b2 : &P.b;
+          const CUtensorMap* ma = ext ? PROB_ADDR(xm.a2) : PROB_ADDR(a);
+          const CUtensorMap* mb = ext ? PROB_ADDR(xm.b2) : PROB_ADDR(b);
           const int k0 = (ext ? kb - sh.kb_main : kb) * BK;
           if (sh.a_mn) {  // [K, M] row-major: two 64x64 boxes (M chunks)
             tma_load_2d(sa, ma, &full[stage], tm * BM, k0);
@@ -410,8 +454,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++it) {
         int lu;
-        const Prob& P = unit_of<GROUPED>(L, u, lu);
-        const Shape sh = P.sh;  // registers: the loops below re-read it per k-block
+        const int p = prob_of<GROUPED>(L, u, lu);
+        const Shape sh = PROB(sh);
         const int split = lu % sh.splits;
         const int kb0 = split * sh.k_blocks_per_split;
         const int kb1 = min(sh.total_k_blocks, kb0 + sh.k_blocks_per_split);
@@ -453,17 +497,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int it = 0, nchunk = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
       int lu;
-      const Prob& P = unit_of<GROUPED>(L, u, lu);
-      const Shape sh = P.sh;  // registers: the loops below re-read it per k-block
+      const int p = prob_of<GROUPED>(L, u, lu);
+      const Shape sh = PROB(sh);
       const int tile = lu / sh.splits;
       const int tm = tile / sh.tiles_n, tn = tile % sh.tiles_n;
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, 4)) break;
       tc_fence_after();
-      const EpiParams ep = P.ep;
-      epilogue_rows(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, tm * BM + lane_base, tn * BN, sh, ep, P.em,
-                    wbuf, lane, nchunk);
+      const EpiParams ep = PROB(ep);
+      if (ep.epi == EPI_SCATTER)
+        epilogue_scatter(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, tm * BM + lane_base, tn * BN, sh, ep,
+                         PROB(ep.sc.peers), lane);
+      else
+        epilogue_rows(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, tm * BM + lane_base, tn * BN, sh, ep,
+                      *PROB_ADDR(em), wbuf, lane, nchunk);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -588,8 +636,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       for (int u = pair; u < units && ok; u += npairs) {
         int lu;
-        const Prob& P = unit_of<GROUPED>(L, u, lu);
-        const Shape sh = P.sh;  // registers: the loops below re-read it per k-block
+        const int p = prob_of<GROUPED>(L, u, lu);
+        const Shape sh = PROB(sh);
         const int split = lu % sh.splits;
         const int tile = lu / sh.splits;
         const int tm = tile / sh.tiles_n, tn = tile % sh.tiles_n;
@@ -606,8 +654,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint8_t* sa = smem + stage * STAGE2_BYTES;
           uint8_t* sb = sa + BM * BK * 2;
           const bool ext = kb >= sh.kb_main;
-          const CUtensorMap* ma = ext ? &P.xm.a2 : &P.a;
-          const CUtensorMap* mb = ext ? &P.xm.b2 : &P.b;
+          const CUtensorMap* ma = ext ? PROB_ADDR(xm.a2) : PROB_ADDR(a);
+          const CUtensorMap* mb = ext ? PROB_ADDR(xm.b2) : PROB_ADDR(b);
           const int k0 = (ext ? kb - sh.kb_main : kb) * BK;
           if (sh.a_mn) {
             tma_load_2d_pair(sa, ma, bar0, m0, k0);
@@ -636,8 +684,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       for (int u = pair; u < units && ok; u += npairs, ++it) {
         int lu;
-        const Prob& P = unit_of<GROUPED>(L, u, lu);
-        const Shape sh = P.sh;  // registers: the loops below re-read it per k-block
+        const int p = prob_of<GROUPED>(L, u, lu);
+        const Shape sh = PROB(sh);
         const int split = lu % sh.splits;
         const int kb0 = split * sh.k_blocks_per_split;
         const int kb1 = min(sh.total_k_blocks, kb0 + sh.k_blocks_per_split);
@@ -677,16 +725,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int it = 0, nchunk = 0;
     for (int u = pair; u < units; u += npairs, ++it) {
       int lu;
-      const Prob& P = unit_of<GROUPED>(L, u, lu);
-      const Shape sh = P.sh;  // registers: the loops below re-read it per k-block
+      const int p = prob_of<GROUPED>(L, u, lu);
+      const Shape sh = PROB(sh);
       const int tile = lu / sh.splits;
       const int tm = tile / sh.tiles_n, tn = tile % sh.tiles_n;
       const int acc = it & 1;
       if (!mbar_wait(&tfull[acc], (it >> 1) & 1, abort_flag, 34)) break;
       tc_fence_after();
-      const EpiParams ep = P.ep;
-      epilogue_rows(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, tm * 256 + (int)rank * 128 + lane_base,
-                    tn * BN, sh, ep, P.em, wbuf, lane, nchunk);
+      const EpiParams ep = PROB(ep);
+      if (ep.epi == EPI_SCATTER)
+        epilogue_scatter(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, tm * 256 + (int)rank * 128 + lane_base,
+                         tn * BN, sh, ep, PROB(ep.sc.peers), lane);
+      else
+        epilogue_rows(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, tm * 256 + (int)rank * 128 + lane_base,
+                      tn * BN, sh, ep, *PROB_ADDR(em), wbuf, lane, nchunk);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty0[acc]);
@@ -759,7 +811,15 @@ static int build_prob(const GemmDesc& d, bool two_sm, Prob* P) {
   if (d.splits > 1 && ep.epi != EPI_F32_ACC) return -3;
   int r;
   // epilogue outputs go out through TMA: 16-byte aligned bases and row strides
-  if (ep.epi == EPI_F32_ACC) {
+  if (ep.epi == EPI_SCATTER) {
+    const ScatterParams& sc = ep.sc;
+    if (sc.part_cols <= 0 || sc.dst_cols <= 0 || sc.part_cols % 32 || sc.dst_cols % 32 || sc.part_cols % sc.dst_cols ||
+        d.N % sc.part_cols || sc.seg_rows <= 0 || (sc.dst_ld * 2) % 16 || sc.part_cols / sc.dst_cols > kMaxPeers ||
+        sc.dst_ld < (d.N / sc.part_cols) * sc.dst_cols || sc.row_off < 0 || sc.seg_rows > sc.dst_seq)
+      return -7;
+    for (int i = 0; i < sc.part_cols / sc.dst_cols; ++i)
+      if (!sc.peers[i] || (reinterpret_cast<uintptr_t>(sc.peers[i]) & 15)) return -7;
+  } else if (ep.epi == EPI_F32_ACC) {
     if ((reinterpret_cast<uintptr_t>(ep.out_f32) & 15) || (ep.ldc * 4) % 16) return -4;
     if ((r = make_out_map(&P->em.acc, ep.out_f32, true, d.M, d.N, ep.ldc))) return r;
   } else {

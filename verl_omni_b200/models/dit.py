@@ -21,6 +21,7 @@ import torch.nn.functional as F
 from verl_omni_b200.models.layers import (Linear, RMSWeight, TimestepMLP, patchify, patchify_3d, rope_nd,
                                           timestep_embedding, unpatchify, unpatchify_3d)
 from verl_omni_b200.ops.attention import attention
+from verl_omni_b200.parallel import ulysses_fused as UF
 from verl_omni_b200.parallel.ulysses import gather_sequence, local_rows, shard_sequence, ulysses_attention
 from verl_omni_b200.ops.norm import adaln_layernorm, layer_norm, qk_norm_split_into
 
@@ -69,17 +70,22 @@ class DiTBlock(nn.Module):
         self.ffn_1, self.ffn_2 = Linear(D, cfg.ffn), Linear(cfg.ffn, D)
         self.eps = cfg.eps
 
-    def forward(self, x, ctx, temb_proj, rope=None, sp_group=None):
+    def forward(self, x, ctx, temb_proj, rope=None, sp_group=None, rope_full=None):
         B, S, D = x.shape
         St = ctx.shape[1]
         H, dh = self.H, self.dh
         mod = temb_proj + self.modulation.to(temb_proj.dtype)[None]
         h = adaln_layernorm(x, mod, 0, 1, 6, self.eps)
-        qkv = self.qkv(h).reshape(B * S, 3 * D)
         mk = lambda n: torch.empty(B, H, n, dh, device=x.device, dtype=x.dtype)  # noqa: E731
-        q, k, v = qk_norm_split_into(mk(S), mk(S), mk(S), qkv, self.norm_q.weight, self.norm_k.weight, S, 0,
-                                     rope=rope, eps=self.eps)
-        o = ulysses_attention(q, k, v, sp_group)  # local queries; keys over the whole sequence
+        if type(self.qkv) is Linear and UF.enabled(sp_group, x, H, D):
+            # sequence-parallel inference: both exchanges inside the QKV GEMM and attention kernels
+            o, _ = UF.joint_attention_fused(h, None, self.qkv, None, (self.norm_q.weight, self.norm_k.weight), None,
+                                            H, sp_group, rope=rope_full, eps=self.eps)
+        else:
+            qkv = self.qkv(h).reshape(B * S, 3 * D)
+            q, k, v = qk_norm_split_into(mk(S), mk(S), mk(S), qkv, self.norm_q.weight, self.norm_k.weight, S, 0,
+                                         rope=rope, eps=self.eps)
+            o = ulysses_attention(q, k, v, sp_group)  # local queries; keys over the whole sequence
         x = self.o(o, epilogue="gate_res", gate=mod.view(B, 6, D)[:, 2], res=x, S=S)
         # cross attention (no gate)
         hn = F.layer_norm(x, (D,), self.norm3_w.to(x.dtype), self.norm3_b.to(x.dtype), self.eps)
@@ -148,6 +154,7 @@ class DiT(nn.Module):
         ctx = self.text_embedding_2(F.gelu(self.text_embedding_1(context.to(dt)), approximate="tanh"))
         rope = self._rope(*grid, x.device) if cfg.rope else None
         sp = getattr(self, "sp_group", None)
+        rope_full = rope
         if sp is not None:  # Ulysses: 1/sp of the video tokens per rank; the text context stays whole
             S = x.shape[1]
             x = shard_sequence(x, sp)
@@ -155,9 +162,9 @@ class DiT(nn.Module):
                 rope = (local_rows(rope[0], [S], sp), local_rows(rope[1], [S], sp))
         for blk in self.blocks:
             if self.gradient_checkpointing and torch.is_grad_enabled():
-                x = torch.utils.checkpoint.checkpoint(blk, x, ctx, temb_proj, rope, sp, use_reentrant=False)
+                x = torch.utils.checkpoint.checkpoint(blk, x, ctx, temb_proj, rope, sp, rope_full, use_reentrant=False)
             else:
-                x = blk(x, ctx, temb_proj, rope, sp)
+                x = blk(x, ctx, temb_proj, rope, sp, rope_full)
         mod = self.head_mod(temb_act)
         x = adaln_layernorm(x, mod, 0, 1, 2, cfg.eps)
         out = self.head(x)

@@ -19,6 +19,7 @@ import torch.nn.functional as F
 from verl_omni_b200.models.layers import (Linear, RMSWeight, TimestepMLP, linear_pair, patchify, rope_nd,
                                          timestep_embedding, unpatchify)
 from verl_omni_b200.ops.attention import attention, attention_split  # noqa: F401
+from verl_omni_b200.parallel import ulysses_fused as UF
 from verl_omni_b200.parallel.ulysses import gather_sequence, joint_attention, local_rows, shard_sequence, ulysses_attention
 from verl_omni_b200.ops.norm import adaln_layernorm, qk_norm_split_into
 
@@ -63,7 +64,7 @@ class DoubleBlock(nn.Module):
             setattr(self, f"{s}_mlp_1", Linear(D, hid))
             setattr(self, f"{s}_mlp_2", Linear(hid, D))
 
-    def forward(self, x, c, temb_act, rope, kv_len=None, sp_group=None, key_mask=None):
+    def forward(self, x, c, temb_act, rope, kv_len=None, sp_group=None, key_mask=None, rope_full=None):
         B, Si, D = x.shape
         St = c.shape[1]
         H, dh = self.H, self.dh
@@ -71,13 +72,21 @@ class DoubleBlock(nn.Module):
         hi = adaln_layernorm(x, mi, 0, 1, 6, self.eps)
         ht = adaln_layernorm(c, mt, 0, 1, 6, self.eps)
         S = Si + St
-        mk = lambda: torch.empty(B, H, S, dh, device=x.device, dtype=x.dtype)  # noqa: E731
-        qkv_i, qkv_t = linear_pair(self.img_qkv, hi, self.txt_qkv, ht)
-        q, k, v = qk_norm_split_into(mk(), mk(), mk(), qkv_i.reshape(B * Si, 3 * D), self.img_norm_q.weight,
-                                     self.img_norm_k.weight, Si, 0, rope=rope, eps=self.eps)
-        q, k, v = qk_norm_split_into(q, k, v, qkv_t.reshape(B * St, 3 * D), self.txt_norm_q.weight,
-                                     self.txt_norm_k.weight, St, Si, rope=rope, eps=self.eps)
-        o_img, o_txt = joint_attention(q, k, v, Si, sp_group=sp_group, kv_len=kv_len, key_mask=key_mask)
+        if (key_mask is None and kv_len is None and type(self.img_qkv) is Linear and type(self.txt_qkv) is Linear
+                and UF.enabled(sp_group, x, H, D)):
+            # sequence-parallel inference: both exchanges inside the QKV GEMM and attention kernels
+            o_img, o_txt = UF.joint_attention_fused(hi, ht, self.img_qkv, self.txt_qkv,
+                                                    (self.img_norm_q.weight, self.img_norm_k.weight),
+                                                    (self.txt_norm_q.weight, self.txt_norm_k.weight), H, sp_group,
+                                                    rope=rope_full, eps=self.eps)
+        else:
+            mk = lambda: torch.empty(B, H, S, dh, device=x.device, dtype=x.dtype)  # noqa: E731
+            qkv_i, qkv_t = linear_pair(self.img_qkv, hi, self.txt_qkv, ht)
+            q, k, v = qk_norm_split_into(mk(), mk(), mk(), qkv_i.reshape(B * Si, 3 * D), self.img_norm_q.weight,
+                                         self.img_norm_k.weight, Si, 0, rope=rope, eps=self.eps)
+            q, k, v = qk_norm_split_into(q, k, v, qkv_t.reshape(B * St, 3 * D), self.txt_norm_q.weight,
+                                         self.txt_norm_k.weight, St, Si, rope=rope, eps=self.eps)
+            o_img, o_txt = joint_attention(q, k, v, Si, sp_group=sp_group, kv_len=kv_len, key_mask=key_mask)
         vi, vt = mi.view(B, 6, D), mt.view(B, 6, D)
         x, c = linear_pair(self.img_out, o_img, self.txt_out, o_txt, "gate_res", vi[:, 2], x, Si, vt[:, 2], c, St)
         ui, ut = linear_pair(self.img_mlp_1, adaln_layernorm(x, mi, 3, 4, 6, self.eps), self.txt_mlp_1,
@@ -157,12 +166,13 @@ class FluxDiT(nn.Module):
         Si, St = x.shape[1], c.shape[1]
         rope = self._rope(Hh // p, Ww // p, St, x.device)
         sp = getattr(self, "sp_group", None)
+        rope_full = rope
         if sp is not None:  # Ulysses: this rank keeps 1/sp of the image tokens and of the text tokens
             x, c = shard_sequence(x, sp), shard_sequence(c, sp)
             rope = (local_rows(rope[0], [Si, St], sp), local_rows(rope[1], [Si, St], sp))
         Sl = x.shape[1]
         for blk in self.transformer_blocks:
-            x, c = blk(x, c, ta, rope, sp_group=sp)
+            x, c = blk(x, c, ta, rope, sp_group=sp, rope_full=rope_full)
         xs = torch.cat([x, c], 1)
         for blk in self.single_transformer_blocks:
             xs = blk(xs, ta, rope, sp_group=sp)

@@ -26,6 +26,7 @@ import torch.nn.functional as F
 from verl_omni_b200.models.layers import (Linear, RMSWeight, TimestepMLP, linear_pair, patchify, sincos_2d,
                                          timestep_embedding, unpatchify)
 from verl_omni_b200.ops.norm import adaln_layernorm, qk_norm_split_into
+from verl_omni_b200.parallel import ulysses_fused as UF
 from verl_omni_b200.parallel.ulysses import (gather_key_mask, gather_sequence, joint_attention, pad_to_multiple,
                                              shard_sequence, sp_info, ulysses_attention)
 
@@ -96,17 +97,25 @@ class JointBlock(nn.Module):
         #              6 shift_msa2, 7 scale_msa2, 8 gate_msa2
         h = adaln_layernorm(x, mod, 0, 1, self.n_mod, self.eps)
         hc = adaln_layernorm(c, modc, 0, 1, self.n_mod_c, self.eps)
-        qkv, qkvc = linear_pair(self.to_qkv, h, self.add_qkv, hc)
-        qkv, qkvc = qkv.reshape(B * Si, 3 * D), qkvc.reshape(B * St, 3 * D)
         S = Si + St
         dev, dt = x.device, x.dtype
-        q = torch.empty(B, H, S, dh, device=dev, dtype=dt)
-        k = torch.empty(B, H, S, dh, device=dev, dtype=dt)
-        v = torch.empty(B, H, S, dh, device=dev, dtype=dt)
-        q, k, v = qk_norm_split_into(q, k, v, qkv, self.norm_q.weight, self.norm_k.weight, Si, 0, eps=self.eps)
-        q, k, v = qk_norm_split_into(q, k, v, qkvc, self.norm_added_q.weight, self.norm_added_k.weight, St, Si,
-                                     eps=self.eps)
-        o_img, o_txt = joint_attention(q, k, v, Si, sp_group=sp_group, key_mask=key_mask)  # [B, Si, D], [B, St, D]
+        if (key_mask is None and type(self.to_qkv) is Linear and type(self.add_qkv) is Linear
+                and UF.enabled(sp_group, x, H, D)):
+            # sequence-parallel inference: both exchanges inside the QKV GEMM and attention kernels
+            o_img, o_txt = UF.joint_attention_fused(h, hc, self.to_qkv, self.add_qkv,
+                                                    (self.norm_q.weight, self.norm_k.weight),
+                                                    (self.norm_added_q.weight, self.norm_added_k.weight), H,
+                                                    sp_group, eps=self.eps)
+        else:
+            qkv, qkvc = linear_pair(self.to_qkv, h, self.add_qkv, hc)
+            qkv, qkvc = qkv.reshape(B * Si, 3 * D), qkvc.reshape(B * St, 3 * D)
+            q = torch.empty(B, H, S, dh, device=dev, dtype=dt)
+            k = torch.empty(B, H, S, dh, device=dev, dtype=dt)
+            v = torch.empty(B, H, S, dh, device=dev, dtype=dt)
+            q, k, v = qk_norm_split_into(q, k, v, qkv, self.norm_q.weight, self.norm_k.weight, Si, 0, eps=self.eps)
+            q, k, v = qk_norm_split_into(q, k, v, qkvc, self.norm_added_q.weight, self.norm_added_k.weight, St, Si,
+                                         eps=self.eps)
+            o_img, o_txt = joint_attention(q, k, v, Si, sp_group=sp_group, key_mask=key_mask)  # [B, Si|St, D]
         gate_msa = mod.view(B, self.n_mod, D)[:, 2]
         mc = modc.view(B, self.n_mod_c, D)
         if self.cpo:
@@ -116,13 +125,18 @@ class JointBlock(nn.Module):
                                    mc[:, 2], c, St)
         if self.dual:
             h2 = adaln_layernorm(x, mod, 6, 7, self.n_mod, self.eps)
-            qkv2 = self.attn2_qkv(h2).reshape(B * Si, 3 * D)
-            q2 = torch.empty(B, H, Si, dh, device=dev, dtype=dt)
-            k2 = torch.empty_like(q2)
-            v2 = torch.empty_like(q2)
-            q2, k2, v2 = qk_norm_split_into(q2, k2, v2, qkv2, self.norm2_q.weight, self.norm2_k.weight, Si, 0,
-                                            eps=self.eps)
-            o2 = ulysses_attention(q2, k2, v2, sp_group)
+            if type(self.attn2_qkv) is Linear and UF.enabled(sp_group, x, H, D):
+                o2, _ = UF.joint_attention_fused(h2, None, self.attn2_qkv, None,
+                                                 (self.norm2_q.weight, self.norm2_k.weight), None, H, sp_group,
+                                                 eps=self.eps)
+            else:
+                qkv2 = self.attn2_qkv(h2).reshape(B * Si, 3 * D)
+                q2 = torch.empty(B, H, Si, dh, device=dev, dtype=dt)
+                k2 = torch.empty_like(q2)
+                v2 = torch.empty_like(q2)
+                q2, k2, v2 = qk_norm_split_into(q2, k2, v2, qkv2, self.norm2_q.weight, self.norm2_k.weight, Si, 0,
+                                                eps=self.eps)
+                o2 = ulysses_attention(q2, k2, v2, sp_group)
             x_new = self.attn2_out(o2, epilogue="gate_res", gate=mod.view(B, self.n_mod, D)[:, 8], res=x_new, S=Si)
         x = x_new
         hm = adaln_layernorm(x, mod, 3, 4, self.n_mod, self.eps)

@@ -118,7 +118,7 @@ class QwenImageDiT(nn.Module):
         c = self.txt_in(e.to(dt))
         Si, St = x.shape[1], c.shape[1]
         masked = prompt_mask is not None and not bool(prompt_mask.all())
-        rope = self._rope(Hh // p, Ww // p, n_ref, St, x.device)
+        rope = rope_full = self._rope(Hh // p, Ww // p, n_ref, St, x.device)
         sp = getattr(self, "sp_group", None)
         kv_len = key_mask = None
         if sp is not None:  # Ulysses: this rank keeps 1/sp of the image tokens and of the text tokens
@@ -132,7 +132,7 @@ class QwenImageDiT(nn.Module):
             # right-padded prompts: keys past image tokens + valid text tokens are masked in every block
             kv_len = (Si + prompt_mask.to(torch.int64).sum(1)).to(torch.int32)
         for blk in self.transformer_blocks:
-            x, c = blk(x, c, ta, rope, kv_len, sp_group=sp, key_mask=key_mask)
+            x, c = blk(x, c, ta, rope, kv_len, sp_group=sp, key_mask=key_mask, rope_full=rope_full)
         x = adaln_layernorm(x, self.norm_out_linear(ta), 1, 0, 2, cfg.eps)
         y = self.proj_out(x)
         if sp is not None:

@@ -133,6 +133,70 @@ def bench_gemm_pair(a) -> list[dict]:
     return out
 
 
+def bench_ulysses(a) -> list[dict]:
+    """One joint-attention layer under Ulysses SP (run under torchrun, one rank per GPU): NCCL all-to-all
+    path vs the fused path (QKV GEMM epilogue scatter + attention peer output).  FLUX-shaped by default:
+    ``--B 1 --S 4096`` image tokens + 512 text tokens, hidden 3072, 24 heads.  Device time of the slowest
+    rank; roofline = max(FLOPs / measured GEMM peak, bytes that cross NVLink per GPU / 770 GB/s)."""
+    import os
+
+    import torch.distributed as dist
+
+    from verl_omni_b200.models.layers import Linear
+    from verl_omni_b200.ops.norm import qk_norm_split_into
+    from verl_omni_b200.parallel import dist as D
+    from verl_omni_b200.parallel import ulysses_fused as UF
+    from verl_omni_b200.parallel.ulysses import joint_attention
+
+    info = D.init_distributed(device="cuda", timeout_s=300)
+    W, dev, grp = D.world_size(), info.device, dist.group.WORLD
+    B, Si, St, Dm, H = a.B, a.S, 512, 3072, 24
+    dh, si, st = Dm // H, Si // W, St // W
+    torch.manual_seed(0)
+    qi, qt = Linear(Dm, 3 * Dm).to(dev, torch.bfloat16), Linear(Dm, 3 * Dm).to(dev, torch.bfloat16)
+    wn = [torch.ones(dh, device=dev, dtype=torch.bfloat16) for _ in range(4)]
+    hi = torch.randn(B, si, Dm, device=dev, dtype=torch.bfloat16)
+    ht = torch.randn(B, st, Dm, device=dev, dtype=torch.bfloat16)
+
+    def nccl():
+        a0, a1 = qi(hi).reshape(B * si, 3 * Dm), qt(ht).reshape(B * st, 3 * Dm)
+        mk = lambda: torch.empty(B, H, si + st, dh, device=dev, dtype=torch.bfloat16)  # noqa: E731
+        q, k, v = qk_norm_split_into(mk(), mk(), mk(), a0, wn[0], wn[1], si, 0)
+        q, k, v = qk_norm_split_into(q, k, v, a1, wn[2], wn[3], st, si)
+        return joint_attention(q, k, v, si, sp_group=grp)
+
+    def fused():
+        return UF.joint_attention_fused(hi, ht, qi, qt, (wn[0], wn[1]), (wn[2], wn[3]), H, grp)
+
+    rows = []
+    with torch.no_grad():
+        for name, fn in (("nccl_all_to_all", nccl), ("fused_peer", fused)):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(a.iters):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = torch.tensor([e0.elapsed_time(e1) / a.iters], device=dev)
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+            S = Si + St
+            flops = 2.0 * B * (si + st) * Dm * 3 * Dm + 4.0 * B * (H // W) * S * S * dh
+            xbytes = 2.0 * B * (si + st) * (3 * Dm + Dm) * (W - 1) / W
+            t_roof = max(flops / 1.59e15, xbytes / 770e9) * 1e3
+            rows.append({"op": f"ulysses_{name}", "world": W, "B": B, "S_img": Si, "S_txt": St, "hidden": Dm,
+                         "ms": round(float(ms), 4), "tflops": round(flops / float(ms) / 1e9, 1),
+                         "nvlink_gb": round(xbytes / 1e9, 3), "roofline_ms": round(t_roof, 4),
+                         "frac_of_roofline": round(t_roof / float(ms), 3)})
+    UF.release_all()
+    if D.rank() != 0:
+        return []
+    return rows
+
+
 def bench_optstep(a) -> list[dict]:
     """Sharded optimizer step over ``--numel`` parameters on every rank (run under torchrun):
     NCCL reduce-scatter + AdamW + all-gather vs the fused peer-memory kernels.  Device time of the
@@ -244,7 +308,7 @@ def bench_adaln(a) -> list[dict]:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "gemm_sweep", "gemm_pair", "fmha", "sde", "adaln", "optstep"])
+    ap.add_argument("op", choices=["gemm", "gemm_sweep", "gemm_pair", "ulysses", "fmha", "sde", "adaln", "optstep"])
     ap.add_argument("--numel", type=int, default=2_240_000_000)
     ap.add_argument("--M", type=int, default=21712)
     ap.add_argument("--N", type=int, default=6144)
@@ -258,7 +322,7 @@ def main() -> None:
     ap.add_argument("--compare", action="store_true")
     a = ap.parse_args()
     pk = _peaks()
-    rows = {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "gemm_pair": bench_gemm_pair, "fmha": bench_fmha, "optstep": bench_optstep, "sde": bench_sde, "adaln": bench_adaln}[a.op](a)
+    rows = {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "gemm_pair": bench_gemm_pair, "ulysses": bench_ulysses, "fmha": bench_fmha, "optstep": bench_optstep, "sde": bench_sde, "adaln": bench_adaln}[a.op](a)
     for r in rows:
         if "tflops" in r:
             r[f"frac_of_{pk['src']}_gemm_peak"] = round(r["tflops"] / pk["tflops"], 3)
