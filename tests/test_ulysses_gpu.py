@@ -25,14 +25,16 @@ def _run(rank, world):
 
     torch.manual_seed(0)
     cfg = QwenImageConfig(in_channels=4, hidden=256, heads=4, depth=2, joint_attention_dim=64)
-    m32 = QwenImageDiT(cfg).cuda()
-    m = copy.deepcopy(m32).bfloat16()
+    m32 = QwenImageDiT(cfg)
+    m = copy.deepcopy(m32).cuda().bfloat16()
     g = torch.Generator().manual_seed(1)
-    x = torch.randn(2, 4, 32, 32, generator=g).cuda()
-    t = torch.tensor([900.0, 300.0]).cuda()
-    c = torch.randn(2, 256, 64, generator=g).cuda()
-    gy = torch.randn(x.shape, generator=torch.Generator().manual_seed(2)).cuda()
-    ref32, g32 = _grads(m32, x, t, c, gy)  # fp32 oracle (cuBLAS / SDPA)
+    x = torch.randn(2, 4, 32, 32, generator=g)
+    t = torch.tensor([900.0, 300.0])
+    c = torch.randn(2, 256, 64, generator=g)
+    gy = torch.randn(x.shape, generator=torch.Generator().manual_seed(2))
+    ref32, g32 = _grads(m32, x, t, c, gy)  # fp32 oracle on the CPU
+    g32 = {n: v.cuda() for n, v in g32.items()}
+    x, t, c, gy = x.cuda(), t.cuda(), c.cuda(), gy.cuda()
     ref16, g16 = _grads(m, x, t, c, gy)    # bf16 native kernels, one rank
     m.sp_group = dist.group.WORLD
     out, gsp = _grads(m, x, t, c, gy)      # bf16 native kernels, SP=2

@@ -52,6 +52,9 @@ void gemm_scatter(torch::Tensor x0, torch::Tensor w0, c10::optional<torch::Tenso
                   int64_t dst_seq0, int64_t row_off0, c10::optional<torch::Tensor> x1, c10::optional<torch::Tensor> w1,
                   c10::optional<torch::Tensor> b1, int64_t seg_rows1, int64_t dst_seq1, int64_t row_off1,
                   std::vector<int64_t> peers, int64_t part_cols, int64_t dst_cols, int64_t dst_ld, int64_t dst_rows);
+torch::Tensor moe_gemm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor tile_expert);
+torch::Tensor moe_gemm_dgrad(torch::Tensor dy, torch::Tensor w, torch::Tensor tile_expert);
+void moe_gemm_wgrad(torch::Tensor dy, torch::Tensor x, torch::Tensor seg, torch::Tensor out, bool accumulate);
 std::vector<torch::Tensor> gemm_dgrad_pair(torch::Tensor dy0, torch::Tensor w0, torch::Tensor dy1, torch::Tensor w1);
 void gemm_wgrad_pair(torch::Tensor dy0, torch::Tensor x0, torch::Tensor out0, torch::Tensor dy1, torch::Tensor x1,
                      torch::Tensor out1, bool accumulate);
@@ -107,6 +110,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_wgrad", &vo::gemm_wgrad);
   m.def("gemm_fwd_pair", &vo::gemm_fwd_pair, "two linear forwards in one persistent GEMM launch");
   m.def("gemm_dgrad_pair", &vo::gemm_dgrad_pair);
+  m.def("moe_gemm_fwd", &vo::moe_gemm_fwd, "expert-grouped GEMM over expert-sorted, 128-padded rows");
+  m.def("moe_gemm_dgrad", &vo::moe_gemm_dgrad);
+  m.def("moe_gemm_wgrad", &vo::moe_gemm_wgrad);
   m.def("gemm_scatter", &vo::gemm_scatter, "QKV projection with the Ulysses head scatter in the epilogue");
   m.def("gemm_wgrad_pair", &vo::gemm_wgrad_pair);
   m.def("gelu_tanh_bwd", &vo::gelu_tanh_bwd);

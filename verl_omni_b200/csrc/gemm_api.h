@@ -43,6 +43,12 @@ struct GemmDesc {
   int64_t lda, ldb, lda2, ldb2;
   int a_mn, b_mn, splits;
   EpiParams ep;
+  // Expert-grouped GEMM (mixture of experts; see Shape in gemm_sm100.cu): grp_mode 1 = forward / dgrad over
+  // expert-sorted rows padded to 128 per expert, grp_tab[m-tile] = expert (-1 unused); B holds n_groups
+  // stacked expert matrices.  grp_mode 2 = weight gradient: M = grp_rows per expert, output [n_groups *
+  // grp_rows, N], reduction over rows [grp_tab[e], grp_tab[e+1]) of A and B.
+  const int* grp_tab;
+  int grp_mode, n_groups, grp_rows;
 };
 
 constexpr int kMaxGroup = 2;

@@ -283,6 +283,107 @@ void gemm_wgrad_pair(torch::Tensor dy0, torch::Tensor x0, torch::Tensor out0, to
   count_launch();
 }
 
+// ---------------------------------------------------------------- mixture-of-experts grouped GEMMs
+// Rows are (token, expert) pairs sorted by expert, each expert's segment padded with zero rows to a
+// multiple of 128 (so every 128-row tile belongs to one expert); `tile_expert[t]` = expert of tile t, -1
+// for unused tiles.  Weights are stacked [E, N, K] (one tensor map over E*N rows).
+
+// y[Mp, N] = x[Mp, K] W_e^T for the expert e of each row tile
+torch::Tensor moe_gemm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor tile_expert) {
+  VO_CHECK_INPUT(x);
+  VO_CHECK_INPUT(w);
+  VO_CHECK_INPUT(tile_expert);
+  TORCH_CHECK(w.dim() == 3 && x.size(1) == w.size(2) && tile_expert.scalar_type() == torch::kInt32, "moe shapes");
+  const int64_t Mp = x.size(0), K = x.size(1), E = w.size(0), N = w.size(1);
+  TORCH_CHECK(Mp % 128 == 0 && tile_expert.numel() == Mp / 128 && N % 8 == 0 && K % 8 == 0, "moe tiling");
+  c10::cuda::CUDAGuard g(x.device());
+  auto y = torch::empty({Mp, N}, x.options());
+  vo_gemm::GemmDesc d{};
+  d.A = x.data_ptr();
+  d.B = w.data_ptr();
+  d.M = (int)Mp;
+  d.N = (int)N;
+  d.K = (int)K;
+  d.lda = K;
+  d.ldb = K;
+  d.splits = 1;
+  d.ep.epi = vo_gemm::EPI_NONE;
+  d.ep.out = bf(y);
+  d.ep.ldc = (int)N;
+  d.grp_mode = 1;
+  d.grp_tab = tile_expert.data_ptr<int>();
+  d.n_groups = (int)E;
+  check_rc(vo_gemm_launch_group(&d, 1, stream()), "moe fwd");
+  count_launch();
+  return y;
+}
+
+// dx[Mp, K] = dy[Mp, N] W_e
+torch::Tensor moe_gemm_dgrad(torch::Tensor dy, torch::Tensor w, torch::Tensor tile_expert) {
+  VO_CHECK_INPUT(dy);
+  VO_CHECK_INPUT(w);
+  VO_CHECK_INPUT(tile_expert);
+  const int64_t Mp = dy.size(0), N = dy.size(1), E = w.size(0), K = w.size(2);
+  TORCH_CHECK(w.dim() == 3 && w.size(1) == N && Mp % 128 == 0 && tile_expert.numel() == Mp / 128 &&
+                  tile_expert.scalar_type() == torch::kInt32,
+              "moe shapes");
+  c10::cuda::CUDAGuard g(dy.device());
+  auto dx = torch::empty({Mp, K}, dy.options());
+  vo_gemm::GemmDesc d{};
+  d.A = dy.data_ptr();
+  d.B = w.data_ptr();
+  d.M = (int)Mp;
+  d.N = (int)K;
+  d.K = (int)N;
+  d.lda = N;
+  d.ldb = K;
+  d.b_mn = 1;
+  d.splits = 1;
+  d.ep.epi = vo_gemm::EPI_NONE;
+  d.ep.out = bf(dx);
+  d.ep.ldc = (int)K;
+  d.grp_mode = 1;
+  d.grp_tab = tile_expert.data_ptr<int>();
+  d.n_groups = (int)E;
+  check_rc(vo_gemm_launch_group(&d, 1, stream()), "moe dgrad");
+  count_launch();
+  return dx;
+}
+
+// out[E, N, K] (+)= dy_e^T x_e over each expert's rows [seg[e], seg[e+1]) (fp32)
+void moe_gemm_wgrad(torch::Tensor dy, torch::Tensor x, torch::Tensor seg, torch::Tensor out, bool accumulate) {
+  VO_CHECK_INPUT(dy);
+  VO_CHECK_INPUT(x);
+  VO_CHECK_INPUT(seg);
+  VO_CHECK_INPUT(out);
+  const int64_t Mp = dy.size(0), N = dy.size(1), K = x.size(1), E = out.size(0);
+  TORCH_CHECK(out.dim() == 3 && out.size(1) == N && out.size(2) == K && out.scalar_type() == torch::kFloat32 &&
+                  x.size(0) == Mp && seg.numel() == E + 1 && seg.scalar_type() == torch::kInt32 && N % 128 == 0,
+              "moe wgrad shapes");
+  c10::cuda::CUDAGuard g(dy.device());
+  if (!accumulate) out.zero_();
+  vo_gemm::GemmDesc d{};
+  d.A = dy.data_ptr();
+  d.B = x.data_ptr();
+  d.M = (int)(E * N);
+  d.N = (int)K;
+  d.K = (int)Mp;
+  d.lda = N;
+  d.ldb = K;
+  d.a_mn = 1;
+  d.b_mn = 1;
+  d.splits = 1;
+  d.ep.epi = vo_gemm::EPI_F32_ACC;
+  d.ep.out_f32 = out.data_ptr<float>();
+  d.ep.ldc = (int)K;
+  d.grp_mode = 2;
+  d.grp_tab = seg.data_ptr<int>();
+  d.n_groups = (int)E;
+  d.grp_rows = (int)N;
+  check_rc(vo_gemm_launch_group(&d, 1, stream()), "moe wgrad");
+  count_launch();
+}
+
 torch::Tensor gelu_tanh_bwd(torch::Tensor dy, torch::Tensor pre) {
   VO_CHECK_INPUT(dy);
   VO_CHECK_INPUT(pre);

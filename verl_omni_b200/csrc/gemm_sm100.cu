@@ -154,7 +154,49 @@ struct Shape {
   int tiles_m, tiles_n, splits, k_blocks_per_split, total_k_blocks;
   int a_mn, b_mn;
   int kb_main;  // k-blocks [0, kb_main) come from (A, B), the rest from the extension operands (A2, B2)
+  // Expert-grouped GEMMs (mixture-of-experts, 1-SM kernel only), tables in device memory:
+  //   grp_mode 1 (forward / dgrad over expert-sorted rows padded to 128 per expert): grp_tab[m-tile] =
+  //     expert of that 128-row tile (-1: unused tile, skipped); B rows are offset by expert * grp_stride;
+  //   grp_mode 2 (weight gradient): units are (expert, output tile); the reduction runs over the expert's
+  //     rows [grp_tab[e], grp_tab[e+1]) (multiples of 128) and output rows are offset by e * grp_stride.
+  const int* grp_tab;
+  int grp_mode, grp_stride, n_groups;
 };
+
+struct UnitInfo {
+  int tm, tn, kb0, kb1, b_off, row_off;
+  bool skip;
+};
+
+// Tile, k-block range and group offsets of one work unit (every role derives the same values).
+__device__ __forceinline__ UnitInfo unit_info(const Shape& sh, int lu) {
+  UnitInfo x;
+  const int split = lu % sh.splits;
+  int tile = lu / sh.splits;
+  x.b_off = 0;
+  x.row_off = 0;
+  x.skip = false;
+  if (sh.grp_mode == 2) {
+    const int per = sh.tiles_m * sh.tiles_n;
+    const int g = tile / per;
+    tile -= g * per;
+    x.kb0 = __ldg(sh.grp_tab + g) / BK;
+    x.kb1 = __ldg(sh.grp_tab + g + 1) / BK;
+    x.skip = x.kb1 <= x.kb0;
+    x.row_off = g * sh.grp_stride;
+  } else {
+    x.kb0 = split * sh.k_blocks_per_split;
+    x.kb1 = min(sh.total_k_blocks, x.kb0 + sh.k_blocks_per_split);
+  }
+  x.tm = tile / sh.tiles_n;
+  x.tn = tile % sh.tiles_n;
+  if (sh.grp_mode == 1) {
+    const int g = __ldg(sh.grp_tab + x.tm);
+    x.skip = g < 0;
+    x.b_off = g * sh.grp_stride;
+  }
+  return x;
+}
 
 // Extension operands concatenated along the reduction: C = A B^T + A2 B2^T in one accumulation
 // (the low-rank LoRA path: A2 = x A_lora^T, B2 = scale * B_lora), same majorness as A / B.
@@ -409,12 +451,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int lu;
         const int p = prob_of<GROUPED>(L, u, lu);
         const Shape sh = PROB(sh);
-        const int split = lu % sh.splits;
-        const int tile = lu / sh.splits;
-        const int tm = tile / sh.tiles_n, tn = tile % sh.tiles_n;
-        const int kb0 = split * sh.k_blocks_per_split;
-        const int kb1 = min(sh.total_k_blocks, kb0 + sh.k_blocks_per_split);
-        for (int kb = kb0; kb < kb1; ++kb) {
+        const UnitInfo ui = unit_info(sh, lu);
+        if (ui.skip) continue;
+        const int tm = ui.tm, tn = ui.tn;
+        for (int kb = ui.kb0; kb < ui.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, 1)) {
             ok = false;
             break;
@@ -434,9 +474,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           if (sh.b_mn) {  // [K, N] row-major: four 64x64 boxes (N chunks)
 #pragma unroll
-            for (int c = 0; c < 4; ++c) tma_load_2d(sb + c * 8192, mb, &full[stage], tn * BN + 64 * c, k0);
+            for (int c = 0; c < 4; ++c)
+              tma_load_2d(sb + c * 8192, mb, &full[stage], tn * BN + 64 * c, ui.b_off + k0);
           } else {
-            tma_load_2d(sb, mb, &full[stage], k0, tn * BN);
+            tma_load_2d(sb, mb, &full[stage], k0, ui.b_off + tn * BN);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -452,13 +493,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++it) {
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
         int lu;
         const int p = prob_of<GROUPED>(L, u, lu);
         const Shape sh = PROB(sh);
-        const int split = lu % sh.splits;
-        const int kb0 = split * sh.k_blocks_per_split;
-        const int kb1 = min(sh.total_k_blocks, kb0 + sh.k_blocks_per_split);
+        const UnitInfo ui = unit_info(sh, lu);
+        if (ui.skip) continue;
+        const int kb0 = ui.kb0, kb1 = ui.kb1;
         const uint32_t idesc = make_idesc(sh.a_mn, sh.b_mn);
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
@@ -488,6 +529,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         if (!ok) break;
         tc_commit(&tfull[acc]);
+        ++it;
       }
     }
   } else {
@@ -495,12 +537,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int lane_base = 32 * (warp & 3);
     uint8_t* wbuf = epi_stage + (warp - 2) * EPI_WARP_BYTES;
     int it = 0, nchunk = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
       int lu;
       const int p = prob_of<GROUPED>(L, u, lu);
       const Shape sh = PROB(sh);
-      const int tile = lu / sh.splits;
-      const int tm = tile / sh.tiles_n, tn = tile % sh.tiles_n;
+      const UnitInfo ui = unit_info(sh, lu);
+      if (ui.skip) continue;
+      const int tm = ui.tm, tn = ui.tn;
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, 4)) break;
@@ -510,11 +553,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         epilogue_scatter(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, tm * BM + lane_base, tn * BN, sh, ep,
                          PROB(ep.sc.peers), lane);
       else
-        epilogue_rows(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, tm * BM + lane_base, tn * BN, sh, ep,
-                      *PROB_ADDR(em), wbuf, lane, nchunk);
+        epilogue_rows(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, ui.row_off + tm * BM + lane_base, tn * BN,
+                      sh, ep, *PROB_ADDR(em), wbuf, lane, nchunk);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
+      ++it;
     }
     if (lane == 0) bulk_wait_all();
     __syncwarp();
@@ -830,11 +874,21 @@ static int build_prob(const GemmDesc& d, bool two_sm, Prob* P) {
       if ((r = make_out_map(&P->em.out2, ep.out2, false, d.M, d.N, ep.ldc))) return r;
     }
   }
+  if (d.grp_mode) {
+    if (two_sm || !d.grp_tab || d.n_groups < 1 || has_ext || d.splits > 1 || ep.epi == EPI_SCATTER) return -8;
+    if (d.grp_mode == 2 && (d.grp_rows <= 0 || d.grp_rows % BM || ep.epi != EPI_F32_ACC || !d.a_mn || !d.b_mn))
+      return -8;
+    if (d.grp_mode == 1 && d.M % BM) return -8;
+  }
+  // grouped forward / dgrad: B stacks n_groups expert matrices along its rows
+  const int64_t bscale = d.grp_mode == 1 ? d.n_groups : 1;
   // 2-SM tiles load 128 rows of A and 128 columns of B per CTA
-  r = d.a_mn ? make_map(&P->a, d.A, d.K, d.M, d.lda, 64, 64) : make_map(&P->a, d.A, d.M, d.K, d.lda, 64, BM);
+  // (grouped weight gradient: A's columns are one expert's output rows; the output stacks n_groups of them)
+  r = d.a_mn ? make_map(&P->a, d.A, d.K, d.grp_mode == 2 ? d.grp_rows : d.M, d.lda, 64, 64)
+             : make_map(&P->a, d.A, d.M, d.K, d.lda, 64, BM);
   if (r) return r;
-  r = d.b_mn ? make_map(&P->b, d.B, d.K, d.N, d.ldb, 64, 64)
-             : make_map(&P->b, d.B, d.N, d.K, d.ldb, 64, two_sm ? 128 : BN);
+  r = d.b_mn ? make_map(&P->b, d.B, d.K * bscale, d.N, d.ldb, 64, 64)
+             : make_map(&P->b, d.B, d.N * bscale, d.K, d.ldb, 64, two_sm ? 128 : BN);
   if (r) return r;
   if (has_ext) {
     if ((d.lda2 * 2) % 16 || (d.ldb2 * 2) % 16 ||
@@ -861,6 +915,18 @@ static int build_prob(const GemmDesc& d, bool two_sm, Prob* P) {
   sh.splits = (sh.total_k_blocks + sh.k_blocks_per_split - 1) / sh.k_blocks_per_split;
   sh.a_mn = d.a_mn;
   sh.b_mn = d.b_mn;
+  sh.grp_tab = d.grp_tab;
+  sh.grp_mode = d.grp_mode;
+  sh.n_groups = d.n_groups;
+  sh.grp_stride = 0;
+  if (d.grp_mode == 1) {
+    sh.grp_stride = d.b_mn ? d.K : d.N;  // rows of one expert's B matrix
+  } else if (d.grp_mode == 2) {
+    sh.grp_stride = d.grp_rows;
+    sh.tiles_m = d.grp_rows / BM;  // per expert; units = n_groups x tiles_m x tiles_n
+    sh.splits = 1;
+    sh.k_blocks_per_split = sh.total_k_blocks;
+  }
   P->ep = ep;
   return 0;
 }
@@ -897,10 +963,16 @@ extern "C" int vo_gemm_launch_group(const vo_gemm::GemmDesc* d, int n, cudaStrea
         return (int)e;
       }
   }
-  // all problems of a launch share the kernel: the 2-SM form only when every one has >= 256 rows
+  // all problems of a launch share the kernel: the 2-SM form only when every one has >= 256 rows (expert-
+  // grouped GEMMs run 128-row tiles on the 1-SM kernel)
   bool two_sm = g_use_2sm != 0;
-  for (int i = 0; i < n; ++i)
+  for (int i = 0; i < n; ++i) {
     if (d[i].M > 0 && d[i].N > 0 && d[i].K > 0 && d[i].M < 256) two_sm = false;
+    if (d[i].grp_mode) {
+      two_sm = false;
+      if (n > 1) return -8;
+    }
+  }
   Launch L;
   memset(&L, 0, sizeof(L));
   int units = 0;
@@ -910,7 +982,7 @@ extern "C" int vo_gemm_launch_group(const vo_gemm::GemmDesc* d, int n, cudaStrea
     const int r = build_prob(d[i], two_sm, P);
     if (r) return r;
     P->unit_begin = units;
-    units += P->sh.tiles_m * P->sh.tiles_n * P->sh.splits;
+    units += P->sh.tiles_m * P->sh.tiles_n * P->sh.splits * (P->sh.grp_mode == 2 ? P->sh.n_groups : 1);
     ++L.nprob;
   }
   if (L.nprob == 0) return 0;

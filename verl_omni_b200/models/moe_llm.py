@@ -139,6 +139,11 @@ class MoEBlock(nn.Module):
 
 
 def _ffn_grouped(tokens, expert_ids, w_gate_up, w_down):
+    from verl_omni_b200.ops import moe as MO
+
+    if MO.native_ok(tokens, w_gate_up, w_down):  # one grouped GEMM launch per projection, no host syncs
+        ones = torch.ones(tokens.shape[0], 1, device=tokens.device, dtype=tokens.dtype)
+        return MO.moe_ffn(tokens, expert_ids.reshape(-1, 1), ones, w_gate_up, w_down)
     out = torch.empty_like(tokens)
     for e in torch.unique(expert_ids).tolist():
         sel = (expert_ids == e).nonzero(as_tuple=True)[0]
@@ -151,6 +156,10 @@ def _ffn_grouped(tokens, expert_ids, w_gate_up, w_down):
 
 def grouped_expert_ffn(h, idx, gates, w_gate_up, w_down):
     """Top-k routed SwiGLU experts: sort (token, slot) pairs by expert, run each expert once, combine."""
+    from verl_omni_b200.ops import moe as MO
+
+    if MO.native_ok(h, w_gate_up, w_down):
+        return MO.moe_ffn(h, idx, gates, w_gate_up, w_down)
     T, K = idx.shape
     flat_e = idx.reshape(-1)
     tok = torch.arange(T, device=h.device).repeat_interleave(K)

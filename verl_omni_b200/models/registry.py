@@ -24,12 +24,19 @@ class ArchSpec:
     reward: str = "vit"
     image_size: int = 512
     notes: str = ""
+    sched_seq_len: Optional[int] = None  # token count that sets the dynamic shift (default: latent H x W / 4)
 
 
 def _qwen_build(tiny: bool):
     from verl_omni_b200.models.qwen_image import QwenImageConfig, QwenImageDiT
 
     return QwenImageDiT(QwenImageConfig.tiny() if tiny else QwenImageConfig.qwen_image())
+
+
+def _ltx2_build(tiny: bool):
+    from verl_omni_b200.models.ltx2 import LTX2AVDiT, LTX2Config
+
+    return LTX2AVDiT(LTX2Config.tiny() if tiny else LTX2Config.ltx2())
 
 
 def _flux_build():
@@ -72,6 +79,15 @@ ARCHS: dict[str, ArchSpec] = {
         "qwen_image_edit_tiny", "QwenImageEdit", lambda: _qwen_build(True), (4, 8, 8),
         {"prompt_embeds": (12, 48), "prompt_embeds_mask": (12,), "image_latents": (4, 8, 8)}, reward="mlp",
         image_size=64),
+    "ltx2": ArchSpec(
+        "ltx2", "LTX2", lambda: _ltx2_build(False), (16 * 16 * 24 + 126, 128),
+        {"prompt_embeds": (256, 3840), "audio_prompt_embeds": (256, 3840)}, reward="mlp", image_size=512,
+        sched_seq_len=16 * 16 * 24,
+        notes="joint audio-video: 48 layers, video 4096 / 32 heads, audio 2048 / 32 heads, 6144 video + 126 audio "
+              "tokens of 128 channels (121 frames at 512 x 768)"),
+    "ltx2_tiny": ArchSpec(
+        "ltx2_tiny", "LTX2", lambda: _ltx2_build(True), (2 * 4 * 4 + 16, 16),
+        {"prompt_embeds": (12, 48), "audio_prompt_embeds": (12, 48)}, reward="mlp", image_size=64, sched_seq_len=32),
     "wan_tiny": ArchSpec(
         "wan_tiny", "WanDiT", lambda: DiT(DiTConfig(in_channels=4, out_channels=4, hidden=128, heads=2, depth=2,
                                                     ffn=256, text_dim=48)), (4, 3, 8, 8),

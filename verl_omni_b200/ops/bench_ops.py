@@ -306,9 +306,53 @@ def bench_adaln(a) -> list[dict]:
     return [{"op": "adaln_ln_fwd", "B": B, "S": S, "D": D, "ms": round(ms, 4), "gbs": round(nbytes / ms / 1e6, 1)}]
 
 
+def bench_moe(a) -> list[dict]:
+    """Qwen3-Omni-30B-A3B-shaped MoE layer (128 experts, top-8, hidden 2048, expert FFN 768) on ``--B`` x
+    ``--S`` tokens: the expert-grouped GEMMs (one launch per projection) vs a per-expert cuBLAS loop."""
+    from verl_omni_b200.ops._ext import ext
+    from verl_omni_b200.ops.moe import plan_dispatch
+
+    E, K, D, Fh = 128, 8, 2048, 768
+    T = a.B * a.S
+    torch.manual_seed(0)
+    idx = torch.topk(torch.randn(T, E, device="cuda"), K, dim=-1).indices
+    plan = plan_dispatch(idx, E)
+    x = torch.randn(plan.rows, D, device="cuda").bfloat16()
+    w = (torch.randn(E, 2 * Fh, D, device="cuda") / D ** 0.5).bfloat16()
+    e = ext()
+    ms = timeit(lambda: e.moe_gemm_fwd(x, w, plan.tile_expert), a.iters)
+    flops = 2.0 * T * K * 2 * Fh * D
+    seg = plan.seg.tolist()
+
+    def loop():
+        for i in range(E):
+            if seg[i + 1] > seg[i]:
+                torch.matmul(x[seg[i]:seg[i + 1]], w[i].t())
+
+    ms_loop = timeit(loop, a.iters)
+    return [{"op": "moe_grouped_gemm_fwd", "tokens": T, "experts": E, "top_k": K, "N": 2 * Fh, "K": D,
+             "padded_rows": int(seg[-1]), "ms": round(ms, 4), "tflops": round(flops / ms / 1e9, 1),
+             "cublas_per_expert_loop_ms": round(ms_loop, 4)}]
+
+
+def bench_groupnorm(a) -> list[dict]:
+    """VAE-decoder GroupNorm(32)+SiLU on channels-last [8, 128, 512, 512] bf16 (one read + one write pass
+    after the statistics pass)."""
+    from verl_omni_b200.ops.norm import group_norm_act
+
+    x = torch.randn(8, 128, 512, 512, device="cuda").bfloat16().to(memory_format=torch.channels_last)
+    w = torch.ones(128, device="cuda").bfloat16()
+    b = torch.zeros(128, device="cuda").bfloat16()
+    with torch.no_grad():
+        ms = timeit(lambda: group_norm_act(x, w, b, 32, 1e-6, True), a.iters)
+    nbytes = 3 * 2 * x.numel()  # stats read, apply read + write
+    return [{"op": "group_norm_silu_nhwc", "shape": list(x.shape), "ms": round(ms, 4),
+             "gbs": round(nbytes / ms / 1e6, 1)}]
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "gemm_sweep", "gemm_pair", "ulysses", "fmha", "sde", "adaln", "optstep"])
+    ap.add_argument("op", choices=["gemm", "gemm_sweep", "gemm_pair", "ulysses", "fmha", "sde", "adaln", "optstep", "moe", "groupnorm"])
     ap.add_argument("--numel", type=int, default=2_240_000_000)
     ap.add_argument("--M", type=int, default=21712)
     ap.add_argument("--N", type=int, default=6144)
@@ -322,7 +366,7 @@ def main() -> None:
     ap.add_argument("--compare", action="store_true")
     a = ap.parse_args()
     pk = _peaks()
-    rows = {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "gemm_pair": bench_gemm_pair, "ulysses": bench_ulysses, "fmha": bench_fmha, "optstep": bench_optstep, "sde": bench_sde, "adaln": bench_adaln}[a.op](a)
+    rows = {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "gemm_pair": bench_gemm_pair, "ulysses": bench_ulysses, "fmha": bench_fmha, "optstep": bench_optstep, "sde": bench_sde, "adaln": bench_adaln, "moe": bench_moe, "groupnorm": bench_groupnorm}[a.op](a)
     for r in rows:
         if "tflops" in r:
             r[f"frac_of_{pk['src']}_gemm_peak"] = round(r["tflops"] / pk["tflops"], 3)

@@ -44,7 +44,7 @@ EPI_NONE, EPI_BIAS, EPI_GELU, EPI_GATE_RES = 0, 1, 2, 3
 def linear_fwd(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor], *, epilogue: str = "none",
                gate: Optional[torch.Tensor] = None, res: Optional[torch.Tensor] = None, S: int = 1):
     """Returns ``(out, saved)``: ``saved`` is the pre-activation (gelu) or the linear output (gate_res)."""
-    if _use_native(x.shape[1], w.shape[0], rows=x.shape[0]):
+    if x.dtype == w.dtype == torch.bfloat16 and _use_native(x.shape[1], w.shape[0], rows=x.shape[0]):
         e = ext()
         if epilogue == "gelu":
             out, pre = e.gemm_fwd(x, w, b, EPI_GELU, None, None, S)
@@ -66,14 +66,15 @@ def linear_fwd(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor], *, e
 
 def matmul_nn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     """``a[M,N] @ b[N,K]`` (b row-major: the MN-major B operand)."""
-    if _use_native(a.shape[1], b.shape[1], rows=a.shape[0]):
+    if a.dtype == b.dtype == torch.bfloat16 and _use_native(a.shape[1], b.shape[1], rows=a.shape[0]):
         return ext().gemm_dgrad(a, b)
     return a @ b
 
 
 def wgrad(dy: torch.Tensor, x: torch.Tensor, main_grad: Optional[torch.Tensor]):
     """``dy[M,N]^T @ x[M,K]``; accumulated (fp32) into ``main_grad`` when given (returns None)."""
-    if _use_native(dy.shape[1], x.shape[1], rows=min(dy.shape[0], dy.shape[1])):
+    if dy.dtype == x.dtype == torch.bfloat16 and _use_native(dy.shape[1], x.shape[1],
+                                                             rows=min(dy.shape[0], dy.shape[1])):
         if main_grad is not None:
             ext().gemm_wgrad(dy, x, main_grad, True)
             return None

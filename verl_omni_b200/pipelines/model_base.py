@@ -179,3 +179,22 @@ class QwenImageEditFlowGRPO(QwenImageFlowGRPO):
     def forward(cls, module, latents, timesteps, cond):
         return module(latents, timesteps, cond["prompt_embeds"], cond.get("prompt_embeds_mask"),
                       image_latents=cond["image_latents"])
+
+
+@DiffusionModelBase.register("LTX2", ("flow_grpo",))
+class LTX2FlowGRPO(DiffusionModelBase):
+    """LTX-2 joint audio-video (``verl_omni/pipelines/ltx2_flow_grpo/diffusers_training_adapter.py:33``): one
+    packed latent sequence (video tokens, then audio tokens), separate video / audio prompt embeddings, the SDE
+    step and log-probability over the concatenation.  The reference's clean-sample-space guidance
+    (``ltx2_flow_grpo/common.py:69-80``) equals velocity-space CFG for a shared sample and sigma, so the
+    common combine is used."""
+
+    scheduler_kind = "ltx2"
+
+    @classmethod
+    def cond_keys(cls):
+        return ("prompt_embeds", "audio_prompt_embeds")
+
+    @classmethod
+    def forward(cls, module, latents, timesteps, cond):
+        return module(latents, timesteps, cond["prompt_embeds"], cond["audio_prompt_embeds"])

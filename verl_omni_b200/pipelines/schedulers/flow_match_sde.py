@@ -175,13 +175,16 @@ class FlowMatchSDEDiscreteScheduler:
 
 def build_scheduler(kind: str = "sd3", num_inference_steps: int = 10, image_seq_len: Optional[int] = None,
                     device=None) -> FlowMatchSDEDiscreteScheduler:
-    """Scheduler presets of the model families (SD3: shift 3; FLUX/Qwen-Image: dynamic; Wan: shift 5)."""
+    """Scheduler presets of the model families (SD3: shift 3; FLUX/Qwen-Image/LTX-2: dynamic; Wan: shift 5)."""
     if kind in ("sd3", "mmdit", "tiny"):
         sch = FlowMatchSDEDiscreteScheduler(shift=3.0)
     elif kind in ("flux", "qwen_image"):
         sch = FlowMatchSDEDiscreteScheduler(shift=1.0, use_dynamic_shifting=True, max_shift=1.15)
     elif kind == "wan":
         sch = FlowMatchSDEDiscreteScheduler(shift=5.0)
+    elif kind == "ltx2":  # dynamic shift over the video token count (base 1024 -> 0.95, 4096 -> 2.05)
+        sch = FlowMatchSDEDiscreteScheduler(shift=1.0, use_dynamic_shifting=True, base_image_seq_len=1024,
+                                            max_image_seq_len=4096, base_shift=0.95, max_shift=2.05)
     else:
         raise ValueError(kind)
     sch.set_timesteps(num_inference_steps, device=device, image_seq_len=image_seq_len)

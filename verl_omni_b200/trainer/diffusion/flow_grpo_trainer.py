@@ -98,7 +98,7 @@ class PolicyGradientTrainer:
             if ref_module is not None:
                 ref_module.sp_group = self.sp_group
         T = self.rollout_cfg.pipeline.num_inference_steps
-        seq = int(np.prod(self.spec.latent_shape[-2:])) // 4
+        seq = self.spec.sched_seq_len or int(np.prod(self.spec.latent_shape[-2:])) // 4
         self.scheduler = self.adapter.build_scheduler(T, image_seq_len=seq, device=self.device)
         self.actor = PPODiffusionEngine(module, self.adapter, self.scheduler, self.actor_cfg, self.model_cfg,
                                         device=self.device, total_steps=self.total_steps)
@@ -127,7 +127,8 @@ class PolicyGradientTrainer:
             scorer = ModelScorer(ViTScorer(image_size=self.spec.image_size).to(self.device, dt), "images", self.device)
         self.reward_fn = VisualRewardManager(scorer, name="score")
         self.rollout = DiTRolloutEngine(module, self.adapter, self.rollout_cfg, self.model_cfg, device=self.device,
-                                        latent_shape=self.spec.latent_shape, decoder=decoder)
+                                        latent_shape=self.spec.latent_shape, decoder=decoder,
+                                        sched_seq_len=self.spec.sched_seq_len)
         # optional agent-loop path: per-sample coroutines over a request-packing rollout server
         agent_cfg = config.actor_rollout_ref.rollout.get("agent", {}) or {}
         self.agent_manager = None

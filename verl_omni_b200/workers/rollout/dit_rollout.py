@@ -64,7 +64,7 @@ class RolloutRequest:
 
 class DiTRolloutEngine:
     def __init__(self, module, adapter: type[DiffusionModelBase], rollout_cfg, model_cfg, *, device,
-                 latent_shape: tuple, decoder: Optional[Callable] = None):
+                 latent_shape: tuple, decoder: Optional[Callable] = None, sched_seq_len: Optional[int] = None):
         self.module = module
         self.adapter = adapter
         self.cfg = rollout_cfg
@@ -73,7 +73,7 @@ class DiTRolloutEngine:
         self.latent_shape = tuple(latent_shape)
         self.decoder = decoder
         T = rollout_cfg.pipeline.num_inference_steps
-        seq = int(np.prod(self.latent_shape[-2:])) // 4
+        seq = sched_seq_len or int(np.prod(self.latent_shape[-2:])) // 4
         self.scheduler = adapter.build_scheduler(T, image_seq_len=seq, device=device)
         self._abort = threading.Event()
         self.sleeping = False
