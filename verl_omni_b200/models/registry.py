@@ -39,6 +39,12 @@ def _ltx2_build(tiny: bool):
     return LTX2AVDiT(LTX2Config.tiny() if tiny else LTX2Config.ltx2())
 
 
+def _bagel_build(tiny: bool):
+    from verl_omni_b200.models.bagel import BagelConfig, BagelMoT
+
+    return BagelMoT(BagelConfig.tiny() if tiny else BagelConfig.bagel_7b_mot())
+
+
 def _flux_build():
     from verl_omni_b200.models.flux import FluxConfig, FluxDiT
 
@@ -88,6 +94,14 @@ ARCHS: dict[str, ArchSpec] = {
     "ltx2_tiny": ArchSpec(
         "ltx2_tiny", "LTX2", lambda: _ltx2_build(True), (2 * 4 * 4 + 16, 16),
         {"prompt_embeds": (12, 48), "audio_prompt_embeds": (12, 48)}, reward="mlp", image_size=64, sched_seq_len=32),
+    "bagel_7b_mot": ArchSpec(
+        "bagel_7b_mot", "Bagel", lambda: _bagel_build(False), (16, 64, 64), {"prompt_ids": (64,)}, vocab=152064,
+        reward="vit", image_size=512,
+        notes="Mixture-of-Transformers: Qwen2.5-7B-shaped layers with understanding / generation weight sets, "
+              "1024 latent tokens (16-ch VAE latents, 2x2 packed) after a 64-token prompt"),
+    "bagel_tiny": ArchSpec(
+        "bagel_tiny", "Bagel", lambda: _bagel_build(True), (4, 8, 8), {"prompt_ids": (12,)}, vocab=512, reward="mlp",
+        image_size=64),
     "wan_tiny": ArchSpec(
         "wan_tiny", "WanDiT", lambda: DiT(DiTConfig(in_channels=4, out_channels=4, hidden=128, heads=2, depth=2,
                                                     ffn=256, text_dim=48)), (4, 3, 8, 8),

@@ -198,3 +198,55 @@ class LTX2FlowGRPO(DiffusionModelBase):
     @classmethod
     def forward(cls, module, latents, timesteps, cond):
         return module(latents, timesteps, cond["prompt_embeds"], cond["audio_prompt_embeds"])
+
+
+def bagel_combine_cfg(v: torch.Tensor, v_text: torch.Tensor, v_img: Optional[torch.Tensor], text_scale: float,
+                      img_scale: float, renorm_type: str = "global", renorm_min: float = 0.0) -> torch.Tensor:
+    """BAGEL's 3-branch guidance (``verl_omni/pipelines/bagel_flow_grpo/diffusers_training_adapter.py:216-270``):
+    text guidance, then optional image guidance, then a norm rescale clamped to [renorm_min, 1] -- per sample
+    over all positions ("global"), per token over channels ("channel"), or on the text-guided prediction only
+    ("text_channel")."""
+    if renorm_type == "text_channel":
+        vt = v_text + text_scale * (v - v_text)
+        scale = (v.norm(dim=1, keepdim=True) / (vt.norm(dim=1, keepdim=True) + 1e-8)).clamp(min=renorm_min, max=1.0)
+        vt = vt * scale
+        return v_img + img_scale * (vt - v_img) if (img_scale > 1.0 and v_img is not None) else vt
+    vt = v_text + text_scale * (v - v_text)
+    out = v_img + img_scale * (vt - v_img) if (img_scale > 1.0 and v_img is not None) else vt
+    if renorm_type == "global":
+        dims = tuple(range(1, v.ndim))
+        n, n_ = torch.linalg.vector_norm(v, dim=dims, keepdim=True), torch.linalg.vector_norm(out, dim=dims, keepdim=True)
+    elif renorm_type == "channel":
+        n, n_ = v.norm(dim=1, keepdim=True), out.norm(dim=1, keepdim=True)
+    else:
+        raise NotImplementedError(f"cfg_renorm_type={renorm_type!r}")
+    return out * (n / (n_ + 1e-8)).clamp(min=renorm_min, max=1.0)
+
+
+@DiffusionModelBase.register("Bagel", ("flow_grpo",))
+class BagelFlowGRPO(DiffusionModelBase):
+    """BAGEL-7B-MoT text-to-image (``verl_omni/pipelines/bagel_flow_grpo/diffusers_training_adapter.py:44``):
+    prompt token ids embedded by the model itself; guidance combines the conditional and text-unconditional
+    branches with BAGEL's global renorm (the image-unconditional branch only matters for editing)."""
+
+    scheduler_kind = "sd3"
+    cfg_renorm_type = "global"
+    cfg_renorm_min = 0.0
+
+    @classmethod
+    def cond_keys(cls):
+        return ("prompt_ids",)
+
+    @classmethod
+    def forward(cls, module, latents, timesteps, cond):
+        return module(latents, timesteps, cond["prompt_ids"])
+
+    @classmethod
+    def predict(cls, module, latents, timesteps, cond: dict, neg_cond: Optional[dict] = None,
+                guidance_scale: Optional[float] = None) -> torch.Tensor:
+        if guidance_scale is not None and guidance_scale > 1.0 and neg_cond is not None:
+            both = {k: torch.cat([cond[k], neg_cond[k]], 0) for k in cond}
+            out = cls.forward(module, torch.cat([latents, latents], 0), torch.cat([timesteps, timesteps], 0), both)
+            v, v_text = out.chunk(2, 0)
+            return bagel_combine_cfg(v, v_text, None, guidance_scale, 1.0, cls.cfg_renorm_type, cls.cfg_renorm_min)
+        return cls.forward(module, latents, timesteps, cond)

@@ -162,7 +162,8 @@ class PolicyGradientTrainer:
         if self.text_encoder is not None:
             t["prompt_embeds"] = self.text_encoder(batch.batch["input_ids"].to(self.device, non_blocking=True))
         for k in self.spec.cond_shapes:
-            t[k] = batch.batch[k].to(self.device, non_blocking=True).to(dt)
+            v = batch.batch[k].to(self.device, non_blocking=True)
+            t[k] = v.to(dt) if v.is_floating_point() else v
         return DataProto(t, dict(batch.non_tensor_batch))
 
     def local_prompt_ids(self, global_ids: list[int]) -> list[int]:

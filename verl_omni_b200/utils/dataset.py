@@ -43,6 +43,10 @@ class SyntheticPromptDataset:
             rows = [torch.randint(0, self.vocab, (self.token_len,), generator=self._gen(i)) for i in ids]
             tensors["input_ids"] = torch.stack(rows)
         for k, shape in self.cond_shapes.items():
+            if k.endswith("_ids"):  # token ids of a model that embeds its own prompt
+                rows = [torch.randint(0, self.vocab, shape, generator=self._gen(i * 31 + 3)) for i in ids]
+                tensors[k] = torch.stack(rows)
+                continue
             if k.endswith("_mask"):
                 # right-padded prompt: a per-prompt valid length in [L/2, L]
                 L = shape[0]
