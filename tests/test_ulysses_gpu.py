@@ -24,7 +24,8 @@ def _run(rank, world):
     from verl_omni_b200.models.qwen_image import QwenImageConfig, QwenImageDiT
 
     torch.manual_seed(0)
-    cfg = QwenImageConfig(in_channels=4, hidden=256, heads=4, depth=2, joint_attention_dim=64)
+    cfg = QwenImageConfig(in_channels=4, hidden=256, heads=4, depth=2, joint_attention_dim=64,
+                                          axes_dim=(8, 28, 28))
     m32 = QwenImageDiT(cfg)
     m = copy.deepcopy(m32).cuda().bfloat16()
     g = torch.Generator().manual_seed(1)
@@ -63,7 +64,8 @@ def _fused(rank, world):
 
     g = torch.Generator().manual_seed(1)
     cases = [
-        ("qwen", QwenImageDiT(QwenImageConfig(in_channels=4, hidden=256, heads=4, depth=2, joint_attention_dim=64)),
+        ("qwen", QwenImageDiT(QwenImageConfig(in_channels=4, hidden=256, heads=4, depth=2, joint_attention_dim=64,
+                                          axes_dim=(8, 28, 28))),
          (torch.randn(2, 4, 32, 32, generator=g), torch.tensor([900.0, 300.0]), torch.randn(2, 256, 64, generator=g))),
         ("mmdit", MMDiT(MMDiTConfig(in_channels=4, out_channels=4, hidden=256, heads=4, depth=2, joint_attention_dim=64,
                                     pooled_projection_dim=32, dual_attention_layers=1, sample_size=32,

@@ -35,20 +35,20 @@ struct EpiParams {
 
 // One GEMM of a grouped launch: C = A B^T (+ A2 B2^T), operand conventions as vo_gemm_launch_ext.
 struct GemmDesc {
-  const void* A;
-  const void* B;
-  const void* A2;
-  const void* B2;
-  int M, N, K, K2;
-  int64_t lda, ldb, lda2, ldb2;
-  int a_mn, b_mn, splits;
-  EpiParams ep;
+  const void* A = nullptr;
+  const void* B = nullptr;
+  const void* A2 = nullptr;
+  const void* B2 = nullptr;
+  int M = 0, N = 0, K = 0, K2 = 0;
+  int64_t lda = 0, ldb = 0, lda2 = 0, ldb2 = 0;
+  int a_mn = 0, b_mn = 0, splits = 1;
+  EpiParams ep{};
   // Expert-grouped GEMM (mixture of experts; see Shape in gemm_sm100.cu): grp_mode 1 = forward / dgrad over
   // expert-sorted rows padded to 128 per expert, grp_tab[m-tile] = expert (-1 unused); B holds n_groups
   // stacked expert matrices.  grp_mode 2 = weight gradient: M = grp_rows per expert, output [n_groups *
   // grp_rows, N], reduction over rows [grp_tab[e], grp_tab[e+1]) of A and B.
-  const int* grp_tab;
-  int grp_mode, n_groups, grp_rows;
+  const int* grp_tab = nullptr;
+  int grp_mode = 0, n_groups = 0, grp_rows = 0;
 };
 
 constexpr int kMaxGroup = 2;

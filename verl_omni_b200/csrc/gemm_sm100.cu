@@ -874,6 +874,7 @@ static int build_prob(const GemmDesc& d, bool two_sm, Prob* P) {
       if ((r = make_out_map(&P->em.out2, ep.out2, false, d.M, d.N, ep.ldc))) return r;
     }
   }
+  if (d.grp_mode < 0 || d.grp_mode > 2) return -8;
   if (d.grp_mode) {
     if (two_sm || !d.grp_tab || d.n_groups < 1 || has_ext || d.splits > 1 || ep.epi == EPI_SCATTER) return -8;
     if (d.grp_mode == 2 && (d.grp_rows <= 0 || d.grp_rows % BM || ep.epi != EPI_F32_ACC || !d.a_mn || !d.b_mn))

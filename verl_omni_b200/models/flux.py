@@ -128,6 +128,8 @@ class FluxDiT(nn.Module):
         super().__init__()
         self.cfg = cfg
         D, p = cfg.hidden, cfg.patch_size
+        if sum(cfg.axes_dim) != D // cfg.heads:
+            raise ValueError(f"RoPE axes {cfg.axes_dim} must cover the head dim {D // cfg.heads}")
         self.x_embedder = Linear(cfg.in_channels * p * p, D)
         self.time_embed = TimestepMLP(256, D)
         self.guidance_embed = TimestepMLP(256, D) if cfg.guidance_embeds else None

@@ -69,6 +69,8 @@ class QwenImageDiT(nn.Module):
         super().__init__()
         self.cfg = cfg
         D, p = cfg.hidden, cfg.patch_size
+        if sum(cfg.axes_dim) != D // cfg.heads:
+            raise ValueError(f"RoPE axes {cfg.axes_dim} must cover the head dim {D // cfg.heads}")
         self.img_in = Linear(cfg.in_channels * p * p, D)
         self.txt_norm_weight = nn.Parameter(torch.ones(cfg.joint_attention_dim))
         self.txt_in = Linear(cfg.joint_attention_dim, D)
