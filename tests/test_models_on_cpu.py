@@ -7,7 +7,7 @@ from verl_omni_b200.models.registry import ARCHS, get_arch
 
 
 @pytest.mark.parametrize("name", ["tiny_dit", "sd35_tiny", "flux_tiny", "wan_tiny", "qwen_image_tiny",
-                                  "qwen_image_edit_tiny", "ltx2_tiny", "bagel_tiny"])
+                                  "qwen_image_edit_tiny", "ltx2_tiny", "bagel_tiny", "minimax_h3_tiny"])
 def test_tiny_forward_backward(name):
     from verl_omni_b200.pipelines.model_base import DiffusionModelBase
 
@@ -41,7 +41,8 @@ def test_tiny_forward_backward(name):
 
 @pytest.mark.parametrize("name,lo,hi", [("sd35_medium", 2.0e9, 2.6e9), ("flux1_dev", 11.0e9, 12.6e9),
                                         ("wan21_14b", 13.0e9, 15.5e9), ("qwen_image", 19.0e9, 21.5e9),
-                                        ("ltx2", 17.0e9, 21.0e9), ("bagel_7b_mot", 13.0e9, 16.5e9)])
+                                        ("ltx2", 17.0e9, 21.0e9), ("bagel_7b_mot", 13.0e9, 16.5e9),
+                                        ("minimax_h3", 5.0e9, 7.0e9)])
 def test_full_size_param_counts(name, lo, hi):
     with torch.device("meta"):
         m = get_arch(name).build()

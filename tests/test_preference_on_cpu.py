@@ -45,3 +45,19 @@ def test_dpo_online_and_offline():
     ds = OfflineDPODataset(t, num_pairs=8)
     m2 = t.step(offline_batch=ds.get_batch([0, 1]))
     assert math.isfinite(m2["actor/dpo_loss"])
+
+
+def test_diffusion_nft_minimax_h3_tiny():
+    """DiffusionNFT (the reference's objective for MiniMax-H3) on the packed audio-video model."""
+    extra = ["actor_rollout_ref.model.algorithm=diffusion_nft", "algorithm.old_policy_decay_schedule=linear_to_0_5",
+             "algorithm.timestep_fraction=0.67"]
+    base = [b for b in BASE if not b.startswith("actor_rollout_ref.model.architecture")]
+    from verl_omni_b200.parallel import dist as D
+    from verl_omni_b200.trainer.diffusion.preference_trainer import DirectPreferenceTrainer
+    from verl_omni_b200.utils.config import load_config
+
+    D.init_distributed(device="cpu")
+    t = DirectPreferenceTrainer(load_config("diffusion_trainer", base + extra + [
+        "actor_rollout_ref.model.architecture=minimax_h3_tiny"]))
+    m = t.step()
+    assert math.isfinite(m["actor/policy_loss"]) and math.isfinite(m["actor/grad_norm"])

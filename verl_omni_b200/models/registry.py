@@ -45,6 +45,12 @@ def _bagel_build(tiny: bool):
     return BagelMoT(BagelConfig.tiny() if tiny else BagelConfig.bagel_7b_mot())
 
 
+def _h3_build(tiny: bool):
+    from verl_omni_b200.models.minimax_h3 import H3Config, MiniMaxH3DiT
+
+    return MiniMaxH3DiT(H3Config.tiny() if tiny else H3Config.h3())
+
+
 def _flux_build():
     from verl_omni_b200.models.flux import FluxConfig, FluxDiT
 
@@ -102,6 +108,14 @@ ARCHS: dict[str, ArchSpec] = {
     "bagel_tiny": ArchSpec(
         "bagel_tiny", "Bagel", lambda: _bagel_build(True), (4, 8, 8), {"prompt_ids": (12,)}, vocab=512, reward="mlp",
         image_size=64),
+    "minimax_h3": ArchSpec(
+        "minimax_h3", "MiniMaxH3", lambda: _h3_build(False), (32, (8 * 30 * 52 * 96 + 256 * 32) // 32),
+        {"prompt_embeds": (256, 4096)}, reward="mlp", image_size=480, sched_seq_len=8 * 30 * 52,
+        notes="single-stream text/audio/video DiT: 40 layers, hidden 3072, 24 heads; 12480 video rows of 96 + "
+              "256 audio rows of 32 packed into one flat latent (stored as [32, n/32])"),
+    "minimax_h3_tiny": ArchSpec(
+        "minimax_h3_tiny", "MiniMaxH3", lambda: _h3_build(True), (32, (32 * 96 + 8 * 32) // 32),
+        {"prompt_embeds": (12, 48)}, reward="mlp", image_size=64, sched_seq_len=32),
     "wan_tiny": ArchSpec(
         "wan_tiny", "WanDiT", lambda: DiT(DiTConfig(in_channels=4, out_channels=4, hidden=128, heads=2, depth=2,
                                                     ffn=256, text_dim=48)), (4, 3, 8, 8),

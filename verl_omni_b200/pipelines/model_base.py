@@ -250,3 +250,20 @@ class BagelFlowGRPO(DiffusionModelBase):
             v, v_text = out.chunk(2, 0)
             return bagel_combine_cfg(v, v_text, None, guidance_scale, 1.0, cls.cfg_renorm_type, cls.cfg_renorm_min)
         return cls.forward(module, latents, timesteps, cond)
+
+
+@DiffusionModelBase.register("MiniMaxH3", ("diffusion_nft", "flow_grpo"))
+class MiniMaxH3Adapter(DiffusionModelBase):
+    """MiniMax-H3 audio-video (``verl_omni/pipelines/minimax_h3_diffusion_nft/diffusers_training_adapter.py:38``):
+    packed flat video / audio rows, text prompt embeddings; DiffusionNFT is its objective in the reference
+    (the reverse-SDE path is available here as well since the model returns flow-matching velocities)."""
+
+    scheduler_kind = "flux"
+
+    @classmethod
+    def cond_keys(cls):
+        return ("prompt_embeds",)
+
+    @classmethod
+    def forward(cls, module, latents, timesteps, cond):
+        return module(latents, timesteps, cond["prompt_embeds"])
