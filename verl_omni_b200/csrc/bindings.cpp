@@ -53,6 +53,11 @@ void gemm_scatter(torch::Tensor x0, torch::Tensor w0, c10::optional<torch::Tenso
                   c10::optional<torch::Tensor> b1, int64_t seg_rows1, int64_t dst_seq1, int64_t row_off1,
                   std::vector<int64_t> peers, int64_t part_cols, int64_t dst_cols, int64_t dst_ld, int64_t dst_rows);
 torch::Tensor moe_gemm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor tile_expert);
+void gemm_tp(c10::optional<torch::Tensor> a, c10::optional<torch::Tensor> b, int64_t M, int64_t N, int64_t K,
+             int64_t lda, int64_t ldb, int64_t a_mn, int64_t b_mn, c10::optional<torch::Tensor> out,
+             c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> bias, int64_t gather,
+             std::vector<int64_t> gather_ptrs, int64_t gather_rows, std::vector<int64_t> red_ptrs,
+             int64_t red_rows);
 torch::Tensor moe_gemm_dgrad(torch::Tensor dy, torch::Tensor w, torch::Tensor tile_expert);
 void moe_gemm_wgrad(torch::Tensor dy, torch::Tensor x, torch::Tensor seg, torch::Tensor out, bool accumulate);
 std::vector<torch::Tensor> gemm_dgrad_pair(torch::Tensor dy0, torch::Tensor w0, torch::Tensor dy1, torch::Tensor w1);
@@ -110,6 +115,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_wgrad", &vo::gemm_wgrad);
   m.def("gemm_fwd_pair", &vo::gemm_fwd_pair, "two linear forwards in one persistent GEMM launch");
   m.def("gemm_dgrad_pair", &vo::gemm_dgrad_pair);
+  m.def("gemm_tp", &vo::gemm_tp, "GEMM with a tensor-parallel operand gather and / or peer reduce-scatter");
   m.def("moe_gemm_fwd", &vo::moe_gemm_fwd, "expert-grouped GEMM over expert-sorted, 128-padded rows");
   m.def("moe_gemm_dgrad", &vo::moe_gemm_dgrad);
   m.def("moe_gemm_wgrad", &vo::moe_gemm_wgrad);

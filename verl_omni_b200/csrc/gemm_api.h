@@ -6,7 +6,15 @@
 
 namespace vo_gemm {
 
-enum Epi : int { EPI_NONE = 0, EPI_BIAS = 1, EPI_GELU = 2, EPI_GATE_RES = 3, EPI_F32_ACC = 4, EPI_SCATTER = 5 };
+enum Epi : int {
+  EPI_NONE = 0,
+  EPI_BIAS = 1,
+  EPI_GELU = 2,
+  EPI_GATE_RES = 3,
+  EPI_F32_ACC = 4,
+  EPI_SCATTER = 5,
+  EPI_PEER_RED = 6  // fp32 tile added into the owning rank's buffer (tensor-parallel reduce-scatter)
+};
 
 constexpr int kMaxPeers = 8;
 
@@ -31,6 +39,10 @@ struct EpiParams {
   int S;  // rows per sample (GATE_RES)
   int ldc;
   ScatterParams sc;  // EPI_SCATTER
+  // EPI_PEER_RED: output row m is owned by rank m / red_rows and added (fp32, system-scope vector atomics
+  // over NVLink) at row m % red_rows of red_peers[owner] ([red_rows, ldc] fp32 each).
+  float* red_peers[kMaxPeers];
+  int red_rows;
 };
 
 // One GEMM of a grouped launch: C = A B^T (+ A2 B2^T), operand conventions as vo_gemm_launch_ext.
@@ -49,6 +61,11 @@ struct GemmDesc {
   // grp_rows, N], reduction over rows [grp_tab[e], grp_tab[e+1]) of A and B.
   const int* grp_tab = nullptr;
   int grp_mode = 0, n_groups = 0, grp_rows = 0;
+  // Operand gathered from the ranks of a tensor-parallel group (plain TMA loads of peer memory): gather 1 =
+  // A rows (K-major A), 2 = A along the reduction (MN-major A), 3 = B along the reduction (MN-major B);
+  // block r of gather_rows rows (of the gathered dimension) is read from gather_ptrs[r].
+  const void* gather_ptrs[kMaxPeers] = {};
+  int gather = 0, gather_rows = 0, gather_n = 0;
 };
 
 constexpr int kMaxGroup = 2;

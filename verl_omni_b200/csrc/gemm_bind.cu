@@ -283,6 +283,62 @@ void gemm_wgrad_pair(torch::Tensor dy0, torch::Tensor x0, torch::Tensor out0, to
   count_launch();
 }
 
+// ---------------------------------------------------------------- tensor-parallel GEMMs over peer memory
+// C[M, N] = A B^T with the operand conventions of vo_gemm_launch_ext (a_mn / b_mn), where one operand may
+// be gathered from the ranks of a tensor-parallel group (gather 1: rows of a K-major A; 2: reduction rows
+// of an MN-major A; 3: reduction rows of an MN-major B -- gather_rows rows per rank, read with plain TMA
+// loads from the peers' buffers) and the output may be added into the owning ranks' fp32 buffers
+// (red_ptrs, red_rows output rows per rank) instead of stored locally.
+// out: bf16 [M, N] (ignored with red_ptrs); out_f32: fp32 [M, N] accumulated (weight gradients).
+void gemm_tp(c10::optional<torch::Tensor> a, c10::optional<torch::Tensor> b, int64_t M, int64_t N, int64_t K,
+             int64_t lda, int64_t ldb, int64_t a_mn, int64_t b_mn, c10::optional<torch::Tensor> out,
+             c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> bias, int64_t gather,
+             std::vector<int64_t> gather_ptrs, int64_t gather_rows, std::vector<int64_t> red_ptrs,
+             int64_t red_rows) {
+  const torch::Tensor& dev_t = a.has_value() && a->defined() ? *a : *b;
+  c10::cuda::CUDAGuard g(dev_t.device());
+  vo_gemm::GemmDesc d{};
+  d.A = a.has_value() && a->defined() ? a->data_ptr() : nullptr;
+  d.B = b.has_value() && b->defined() ? b->data_ptr() : nullptr;
+  d.M = (int)M;
+  d.N = (int)N;
+  d.K = (int)K;
+  d.lda = lda;
+  d.ldb = ldb;
+  d.a_mn = (int)a_mn;
+  d.b_mn = (int)b_mn;
+  d.splits = 1;
+  TORCH_CHECK(gather_ptrs.size() <= (size_t)vo_gemm::kMaxPeers && red_ptrs.size() <= (size_t)vo_gemm::kMaxPeers,
+              "at most 8 ranks");
+  d.gather = (int)gather;
+  d.gather_rows = (int)gather_rows;
+  d.gather_n = (int)gather_ptrs.size();
+  for (size_t i = 0; i < gather_ptrs.size(); ++i) d.gather_ptrs[i] = reinterpret_cast<const void*>(gather_ptrs[i]);
+  TORCH_CHECK((gather == 0) == gather_ptrs.empty(), "gather mode needs peer pointers");
+  TORCH_CHECK(gather == 1 || gather == 2 || d.A, "A operand missing");
+  TORCH_CHECK(gather == 3 || d.B, "B operand missing");
+  if (!red_ptrs.empty()) {
+    d.ep.epi = vo_gemm::EPI_PEER_RED;
+    d.ep.red_rows = (int)red_rows;
+    d.ep.ldc = (int)N;
+    for (size_t i = 0; i < red_ptrs.size(); ++i) d.ep.red_peers[i] = reinterpret_cast<float*>(red_ptrs[i]);
+    TORCH_CHECK((int64_t)red_ptrs.size() * red_rows >= M, "owners must cover every output row");
+  } else if (out_f32.has_value() && out_f32->defined()) {
+    TORCH_CHECK(out_f32->scalar_type() == torch::kFloat32 && out_f32->numel() == M * N, "fp32 [M, N] output");
+    d.ep.epi = vo_gemm::EPI_F32_ACC;
+    d.ep.out_f32 = out_f32->data_ptr<float>();
+    d.ep.ldc = (int)N;
+  } else {
+    TORCH_CHECK(out.has_value() && out->defined() && out->numel() == M * N, "bf16 [M, N] output");
+    d.ep.epi = bias.has_value() && bias->defined() ? vo_gemm::EPI_BIAS : vo_gemm::EPI_NONE;
+    d.ep.out = bf(*out);
+    d.ep.ldc = (int)N;
+    if (bias.has_value() && bias->defined()) d.ep.bias = bf(*bias);
+  }
+  check_rc(vo_gemm_launch_group(&d, 1, stream()), "tp");
+  count_launch();
+}
+
 // ---------------------------------------------------------------- mixture-of-experts grouped GEMMs
 // Rows are (token, expert) pairs sorted by expert, each expert's segment padded with zero rows to a
 // multiple of 128 (so every 128-row tile belongs to one expert); `tile_expert[t]` = expert of tile t, -1

@@ -161,12 +161,21 @@ struct Shape {
   //     rows [grp_tab[e], grp_tab[e+1]) (multiples of 128) and output rows are offset by e * grp_stride.
   const int* grp_tab;
   int grp_mode, grp_stride, n_groups;
+  int gather, gather_rows;  // operand gathered from tensor-parallel peers (GemmDesc::gather)
 };
 
 struct UnitInfo {
   int tm, tn, kb0, kb1, b_off, row_off;
   bool skip;
 };
+
+// Tensor-parallel gather: picks the peer's tensor map for the operand block that holds coordinate `x` of the
+// gathered dimension and rebases `x` into that peer's buffer.
+__device__ __forceinline__ const CUtensorMap* gather_map(const CUtensorMap* maps, int rows, int& x) {
+  const int r = x / rows;
+  x -= r * rows;
+  return maps + r;
+}
 
 // Tile, k-block range and group offsets of one work unit (every role derives the same values).
 __device__ __forceinline__ UnitInfo unit_info(const Shape& sh, int lu) {
@@ -224,10 +233,15 @@ struct EpiMaps {
 
 // One GEMM of a launch.  A launch runs kMaxGroup problems at most; their work units are numbered
 // consecutively (problem 0 first) and every role maps a unit to its problem with prob_of().
+struct GatherMaps {
+  CUtensorMap m[kMaxPeers];
+};
+
 struct Prob {
   CUtensorMap a, b;
   EpiMaps em;
   ExtMaps xm;
+  GatherMaps gm;
   Shape sh;
   EpiParams ep;
   int unit_begin;
@@ -332,6 +346,28 @@ __device__ __forceinline__ void epilogue_scatter(uint32_t tacc, int row0, int co
       }
       *reinterpret_cast<uint4*>(dst + 8 * u) = pk;
     }
+  }
+}
+
+// EPI_PEER_RED: each lane adds its row's 32 fp32 values into the owning rank's buffer (system-scope vector
+// atomics over NVLink); `peers` points at the launch's parameter-space pointer table.
+template <typename ShapeT>
+__device__ __forceinline__ void epilogue_red(uint32_t tacc, int row0, int col_base, const ShapeT& sh,
+                                             const EpiParams& ep, float* const* peers, int lane) {
+  const int row = row0 + lane;
+  const bool row_ok = row < sh.M;
+  const int owner = row_ok ? row / ep.red_rows : 0;
+  float* base = row_ok ? peers[owner] + (int64_t)(row - owner * ep.red_rows) * ep.ldc : nullptr;
+  for (int c = 0; c < BN / 32; ++c) {
+    uint32_t r[32];
+    tc_ld_32x32b_x32(tacc + c * 32, r);
+    const int col0 = col_base + c * 32;
+    if (col0 >= sh.N || !row_ok) continue;  // N is a multiple of 32 (checked on the host)
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      atomicAdd_system(reinterpret_cast<float4*>(base + col0 + 4 * j),
+                       make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
   }
 }
 
@@ -466,18 +502,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const CUtensorMap* ma = ext ? PROB_ADDR(xm.a2) : PROB_ADDR(a);
           const CUtensorMap* mb = ext ? PROB_ADDR(xm.b2) : PROB_ADDR(b);
           const int k0 = (ext ? kb - sh.kb_main : kb) * BK;
+          int am = tm * BM, ak = k0, bk = k0;
+          if (sh.gather == 1) ma = gather_map(PROB(gm.m), sh.gather_rows, am);
+          else if (sh.gather == 2) ma = gather_map(PROB(gm.m), sh.gather_rows, ak);
+          else if (sh.gather == 3) mb = gather_map(PROB(gm.m), sh.gather_rows, bk);
           if (sh.a_mn) {  // [K, M] row-major: two 64x64 boxes (M chunks)
-            tma_load_2d(sa, ma, &full[stage], tm * BM, k0);
-            tma_load_2d(sa + 8192, ma, &full[stage], tm * BM + 64, k0);
+            tma_load_2d(sa, ma, &full[stage], am, ak);
+            tma_load_2d(sa + 8192, ma, &full[stage], am + 64, ak);
           } else {
-            tma_load_2d(sa, ma, &full[stage], k0, tm * BM);
+            tma_load_2d(sa, ma, &full[stage], ak, am);
           }
           if (sh.b_mn) {  // [K, N] row-major: four 64x64 boxes (N chunks)
 #pragma unroll
             for (int c = 0; c < 4; ++c)
-              tma_load_2d(sb + c * 8192, mb, &full[stage], tn * BN + 64 * c, ui.b_off + k0);
+              tma_load_2d(sb + c * 8192, mb, &full[stage], tn * BN + 64 * c, ui.b_off + bk);
           } else {
-            tma_load_2d(sb, mb, &full[stage], k0, ui.b_off + tn * BN);
+            tma_load_2d(sb, mb, &full[stage], bk, ui.b_off + tn * BN);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -552,6 +592,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (ep.epi == EPI_SCATTER)
         epilogue_scatter(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, tm * BM + lane_base, tn * BN, sh, ep,
                          PROB(ep.sc.peers), lane);
+      else if (ep.epi == EPI_PEER_RED)
+        epilogue_red(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, tm * BM + lane_base, tn * BN, sh, ep,
+                     PROB(ep.red_peers), lane);
       else
         epilogue_rows(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, ui.row_off + tm * BM + lane_base, tn * BN,
                       sh, ep, *PROB_ADDR(em), wbuf, lane, nchunk);
@@ -701,17 +744,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const CUtensorMap* ma = ext ? PROB_ADDR(xm.a2) : PROB_ADDR(a);
           const CUtensorMap* mb = ext ? PROB_ADDR(xm.b2) : PROB_ADDR(b);
           const int k0 = (ext ? kb - sh.kb_main : kb) * BK;
+          int am = m0, ak = k0, bk = k0;
+          if (sh.gather == 1) ma = gather_map(PROB(gm.m), sh.gather_rows, am);
+          else if (sh.gather == 2) ma = gather_map(PROB(gm.m), sh.gather_rows, ak);
+          else if (sh.gather == 3) mb = gather_map(PROB(gm.m), sh.gather_rows, bk);
           if (sh.a_mn) {
-            tma_load_2d_pair(sa, ma, bar0, m0, k0);
-            tma_load_2d_pair(sa + 8192, ma, bar0, m0 + 64, k0);
+            tma_load_2d_pair(sa, ma, bar0, am, ak);
+            tma_load_2d_pair(sa + 8192, ma, bar0, am + 64, ak);
           } else {
-            tma_load_2d_pair(sa, ma, bar0, k0, m0);
+            tma_load_2d_pair(sa, ma, bar0, ak, am);
           }
           if (sh.b_mn) {
-            tma_load_2d_pair(sb, mb, bar0, n0, k0);
-            tma_load_2d_pair(sb + 8192, mb, bar0, n0 + 64, k0);
+            tma_load_2d_pair(sb, mb, bar0, n0, bk);
+            tma_load_2d_pair(sb + 8192, mb, bar0, n0 + 64, bk);
           } else {
-            tma_load_2d_pair(sb, mb, bar0, k0, n0);
+            tma_load_2d_pair(sb, mb, bar0, bk, n0);
           }
           if (++stage == STAGES2) {
             stage = 0;
@@ -780,6 +827,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (ep.epi == EPI_SCATTER)
         epilogue_scatter(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, tm * 256 + (int)rank * 128 + lane_base,
                          tn * BN, sh, ep, PROB(ep.sc.peers), lane);
+      else if (ep.epi == EPI_PEER_RED)
+        epilogue_red(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, tm * 256 + (int)rank * 128 + lane_base,
+                     tn * BN, sh, ep, PROB(ep.red_peers), lane);
       else
         epilogue_rows(tmem_base + ((uint32_t)lane_base << 16) + acc * BN, tm * 256 + (int)rank * 128 + lane_base,
                       tn * BN, sh, ep, *PROB_ADDR(em), wbuf, lane, nchunk);
@@ -852,10 +902,29 @@ static int build_prob(const GemmDesc& d, bool two_sm, Prob* P) {
   const EpiParams& ep = d.ep;
   if ((d.lda * 2) % 16 || (d.ldb * 2) % 16) return -1;  // TMA strides must be 16-byte multiples
   if ((reinterpret_cast<uintptr_t>(d.A) | reinterpret_cast<uintptr_t>(d.B)) & 15) return -2;
+  const bool a_gathered = d.gather == 1 || d.gather == 2, b_gathered = d.gather == 3;
+  if (d.gather < 0 || d.gather > 3) return -9;
+  if (d.gather) {
+    // whole tiles per peer block: 128 rows of A (gather 1) or 64-row k-blocks (gather 2 / 3)
+    const int unit = d.gather == 1 ? BM : BK;
+    const int total = d.gather == 1 ? d.M : d.K;
+    if (d.gather_n < 1 || d.gather_n > kMaxPeers || d.gather_rows <= 0 || d.gather_rows % unit ||
+        d.gather_rows * d.gather_n != total || d.A2 || d.grp_mode || (d.gather == 1 && d.a_mn) ||
+        (d.gather == 2 && !d.a_mn) || (d.gather == 3 && !d.b_mn))
+      return -9;
+    for (int i = 0; i < d.gather_n; ++i)
+      if (!d.gather_ptrs[i] || (reinterpret_cast<uintptr_t>(d.gather_ptrs[i]) & 15)) return -9;
+  }
   if (d.splits > 1 && ep.epi != EPI_F32_ACC) return -3;
   int r;
   // epilogue outputs go out through TMA: 16-byte aligned bases and row strides
-  if (ep.epi == EPI_SCATTER) {
+  if (ep.epi == EPI_PEER_RED) {
+    if (ep.red_rows <= 0 || d.N % 32 || (ep.ldc * 4) % 16 || ep.ldc < d.N) return -10;
+    const int owners = (d.M + ep.red_rows - 1) / ep.red_rows;
+    if (owners > kMaxPeers) return -10;
+    for (int i = 0; i < owners; ++i)
+      if (!ep.red_peers[i] || (reinterpret_cast<uintptr_t>(ep.red_peers[i]) & 15)) return -10;
+  } else if (ep.epi == EPI_SCATTER) {
     const ScatterParams& sc = ep.sc;
     if (sc.part_cols <= 0 || sc.dst_cols <= 0 || sc.part_cols % 32 || sc.dst_cols % 32 || sc.part_cols % sc.dst_cols ||
         d.N % sc.part_cols || sc.seg_rows <= 0 || (sc.dst_ld * 2) % 16 || sc.part_cols / sc.dst_cols > kMaxPeers ||
@@ -885,12 +954,23 @@ static int build_prob(const GemmDesc& d, bool two_sm, Prob* P) {
   const int64_t bscale = d.grp_mode == 1 ? d.n_groups : 1;
   // 2-SM tiles load 128 rows of A and 128 columns of B per CTA
   // (grouped weight gradient: A's columns are one expert's output rows; the output stacks n_groups of them)
-  r = d.a_mn ? make_map(&P->a, d.A, d.K, d.grp_mode == 2 ? d.grp_rows : d.M, d.lda, 64, 64)
-             : make_map(&P->a, d.A, d.M, d.K, d.lda, 64, BM);
-  if (r) return r;
-  r = d.b_mn ? make_map(&P->b, d.B, d.K * bscale, d.N, d.ldb, 64, 64)
-             : make_map(&P->b, d.B, d.N * bscale, d.K, d.ldb, 64, two_sm ? 128 : BN);
-  if (r) return r;
+  if (!a_gathered) {
+    r = d.a_mn ? make_map(&P->a, d.A, d.K, d.grp_mode == 2 ? d.grp_rows : d.M, d.lda, 64, 64)
+               : make_map(&P->a, d.A, d.M, d.K, d.lda, 64, BM);
+    if (r) return r;
+  }
+  if (!b_gathered) {
+    r = d.b_mn ? make_map(&P->b, d.B, d.K * bscale, d.N, d.ldb, 64, 64)
+               : make_map(&P->b, d.B, d.N * bscale, d.K, d.ldb, 64, two_sm ? 128 : BN);
+    if (r) return r;
+  }
+  for (int i = 0; i < d.gather_n && d.gather; ++i) {
+    // each peer holds gather_rows rows of the gathered dimension, same row stride as the local operand
+    if (d.gather == 1) r = make_map(&P->gm.m[i], d.gather_ptrs[i], d.gather_rows, d.K, d.lda, 64, BM);
+    else if (d.gather == 2) r = make_map(&P->gm.m[i], d.gather_ptrs[i], d.gather_rows, d.M, d.lda, 64, 64);
+    else r = make_map(&P->gm.m[i], d.gather_ptrs[i], d.gather_rows, d.N, d.ldb, 64, 64);
+    if (r) return r;
+  }
   if (has_ext) {
     if ((d.lda2 * 2) % 16 || (d.ldb2 * 2) % 16 ||
         ((reinterpret_cast<uintptr_t>(d.A2) | reinterpret_cast<uintptr_t>(d.B2)) & 15))
@@ -916,6 +996,8 @@ static int build_prob(const GemmDesc& d, bool two_sm, Prob* P) {
   sh.splits = (sh.total_k_blocks + sh.k_blocks_per_split - 1) / sh.k_blocks_per_split;
   sh.a_mn = d.a_mn;
   sh.b_mn = d.b_mn;
+  sh.gather = d.gather;
+  sh.gather_rows = d.gather_rows;
   sh.grp_tab = d.grp_tab;
   sh.grp_mode = d.grp_mode;
   sh.n_groups = d.n_groups;

@@ -1,0 +1,249 @@
+"""Megatron-style tensor parallelism with sequence parallelism, collectives fused into the GEMMs.
+
+Layout (Megatron TP + SP, the reference's ``strategy: megatron`` engine for the Qwen3-Omni thinker,
+``trainer/config/_generated_omni_megatron_trainer.yaml:34-67``): between layers every rank holds ``S / tp``
+tokens of the sequence; a column-parallel linear needs the whole sequence (all-gather, then GEMM with this
+rank's output columns) and a row-parallel linear produces partial sums of the whole sequence that are
+reduce-scattered back to the token owners.
+
+Fused path (CUDA, NCCL group on one node, symmetric memory):
+
+* all-gather -> GEMM: each rank publishes its token shard in a symmetric buffer; the GEMM's TMA producer
+  reads every 128-row A tile straight from the owning peer's buffer (``GemmDesc::gather`` 1).  The weight
+  gradient of the same layer re-reads the gathered activations along the reduction (``gather`` 3);
+* GEMM -> reduce-scatter: the epilogue adds each output row into the owner's fp32 buffer with system-scope
+  vector atomics over NVLink (``EPI_PEER_RED``); the owner converts its rows to bf16 after a one-element
+  all-reduce orders the ranks.  The dgrad of a column-parallel layer uses the same epilogue, and the
+  dgrad / wgrad of a row-parallel layer gather the output gradient (``gather`` 1 / 2).
+
+Reference path (CPU / gloo, or when the fused path does not apply): all-gather and reduce-scatter as
+collectives around plain GEMMs -- numerically the oracle of the fused path.
+
+Symmetric buffers come in pairs used alternately: a rank rewrites a buffer only after an all-reduce that
+every peer reaches once it has finished reading that buffer's previous contents.
+"""
+
+from __future__ import annotations
+
+import os
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from verl_omni_b200.parallel import dist as D
+
+
+def _ext():
+    from verl_omni_b200.ops._ext import ext
+
+    return ext()
+
+
+# ---------------------------------------------------------------- reference collectives
+def all_gather_seq(x: torch.Tensor, group) -> torch.Tensor:
+    """[S_l, C] shards -> [S, C] (rank-major)."""
+    W = D.world_size(group)
+    if W == 1:
+        return x
+    parts = [torch.empty_like(x) for _ in range(W)]
+    dist.all_gather(parts, x.contiguous(), group=group)
+    return torch.cat(parts, 0)
+
+
+def reduce_scatter_seq(y: torch.Tensor, group) -> torch.Tensor:
+    """[S, C] partial sums -> this rank's [S / W, C] rows of the sum."""
+    W = D.world_size(group)
+    if W == 1:
+        return y
+    t = y.float().contiguous()
+    dist.all_reduce(t, group=group)  # gloo has no reduce-scatter; the reference path sums everywhere
+    r = D.rank(group)
+    n = y.shape[0] // W
+    return t[r * n:(r + 1) * n].to(y.dtype)
+
+
+# ---------------------------------------------------------------- fused workspace
+class _Pair:
+    """Two symmetric buffers of one size, handed out alternately."""
+
+    def __init__(self, numel: int, dtype, device, group):
+        from verl_omni_b200.parallel.symm_mem import SymmetricBuffer
+
+        self.bufs = [SymmetricBuffer(numel, dtype, device, group) for _ in range(2)]
+        for b in self.bufs:  # reduce targets start from zero (cudaMalloc does not clear)
+            b.tensor.zero_()
+        torch.cuda.synchronize(device)
+        D.barrier(group)
+        self.i = 0
+
+    def next(self):
+        b = self.bufs[self.i]
+        self.i ^= 1
+        return b
+
+
+class TPContext:
+    """Tensor-parallel group + the symmetric buffers of its fused collectives."""
+
+    def __init__(self, group):
+        self.group = group
+        self.world, self.rank = D.world_size(group), D.rank(group)
+        self._pairs: dict = {}
+        self._fused: Optional[bool] = None
+
+    def fused(self, t: torch.Tensor) -> bool:
+        if os.environ.get("VO_TP_FUSED", "1") == "0" or self.world < 2 or self.world > 8:
+            return False
+        if not (t.is_cuda and t.dtype == torch.bfloat16):
+            return False
+        if self._fused is None:
+            from verl_omni_b200.parallel.symm_mem import available
+
+            self._fused = available(self.group) and hasattr(_ext(), "gemm_tp")
+        return self._fused
+
+    def buf(self, key: str, numel: int, dtype, device):
+        k = (key, numel, dtype, str(device))
+        if k not in self._pairs:
+            self._pairs[k] = _Pair(numel, dtype, device, self.group)
+        return self._pairs[k].next()
+
+    def barrier(self, device) -> None:
+        from verl_omni_b200.parallel.symm_mem import stream_barrier
+
+        stream_barrier(self.group, device)
+
+    def publish(self, key: str, x: torch.Tensor):
+        """Copies this rank's shard into a symmetric buffer and orders the ranks: peers may read it."""
+        b = self.buf(key, x.numel(), x.dtype, x.device)
+        b.tensor.view_as(x).copy_(x)
+        self.barrier(x.device)
+        return b
+
+    def release(self) -> None:
+        for p in self._pairs.values():
+            for b in p.bufs:
+                b.close()
+        self._pairs.clear()
+
+
+def _fused_ok(ctx: TPContext, x: torch.Tensor, *dims: int) -> bool:
+    return ctx.fused(x) and all(d % 128 == 0 for d in dims)
+
+
+def _gemm_ag(ctx: TPContext, xb, S_l: int, K: int, w: torch.Tensor, bias) -> torch.Tensor:
+    """y[S, N] = gather(x)[S, K] W^T with the A tiles read from the peers' published shards."""
+    S, N = S_l * ctx.world, w.shape[0]
+    y = torch.empty(S, N, device=w.device, dtype=w.dtype)
+    _ext().gemm_tp(None, w, S, N, K, K, K, 0, 0, y, None, bias, 1, xb.peer_ptrs, S_l, [], 0)
+    return y
+
+
+def _reduce_to_owner(ctx: TPContext, key: str, S: int, N: int, launch) -> torch.Tensor:
+    """Runs ``launch(red_ptrs, rows)`` (a GEMM whose epilogue adds into the owners' fp32 buffers), orders
+    the ranks, returns this rank's rows in bf16 and clears its buffer for the next use."""
+    S_l = S // ctx.world
+    acc = ctx.buf(key, S_l * N, torch.float32, torch.device("cuda", torch.cuda.current_device()))
+    launch(acc.peer_ptrs, S_l)
+    ctx.barrier(acc.tensor.device)
+    t = acc.tensor.view(S_l, N)
+    out = t.to(torch.bfloat16)
+    t.zero_()
+    return out
+
+
+# ---------------------------------------------------------------- autograd functions
+class _ColumnParallel(torch.autograd.Function):
+    """x shard [S_l, K] -> y [S, N_l] = all_gather(x) W_l^T (+ b_l)."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, tp: TPContext):
+        ctx.tp = tp
+        S_l, K = x.shape
+        if _fused_ok(tp, x, S_l, K, w.shape[0]):
+            xb = tp.publish("col_x", x)
+            y = _gemm_ag(tp, xb, S_l, K, w, b)
+            ctx.fused = True
+        else:
+            y = torch.nn.functional.linear(all_gather_seq(x, tp.group), w, b)
+            ctx.fused = False
+        ctx.save_for_backward(x, w)
+        ctx.has_b = b is not None
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        tp = ctx.tp
+        dy = dy.contiguous()
+        S, N_l = dy.shape
+        S_l, K = x.shape
+        gb = dy.float().sum(0).to(w.dtype) if ctx.has_b else None
+        if ctx.fused:
+            # dX: partial over this rank's output columns, reduce-scattered by the dgrad epilogue
+            dx = _reduce_to_owner(tp, "col_dx", S, K, lambda red, rows: _ext().gemm_tp(
+                dy, w, S, K, N_l, N_l, K, 0, 1, None, None, None, 0, [], 0, red, rows))
+            # dW = dY^T gather(x): the reduction over tokens reads every peer's x shard again
+            xb = tp.publish("col_x", x)
+            gw = torch.zeros(N_l, K, device=w.device, dtype=torch.float32)
+            _ext().gemm_tp(dy, None, N_l, K, S, N_l, K, 1, 1, None, gw, None, 3, xb.peer_ptrs, S_l, [], 0)
+            return dx, gw.to(w.dtype), gb, None
+        xg = all_gather_seq(x, tp.group)
+        dx = reduce_scatter_seq(dy @ w, tp.group)
+        return dx, (dy.t().float() @ xg.float()).to(w.dtype), gb, None
+
+
+class _RowParallel(torch.autograd.Function):
+    """x [S, K_l] -> y shard [S_l, N] = reduce_scatter(x W_l^T) (+ b)."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, tp: TPContext):
+        ctx.tp = tp
+        S, K_l = x.shape
+        N = w.shape[0]
+        if _fused_ok(tp, x, S // max(tp.world, 1), K_l, N) and S % tp.world == 0:
+            y = _reduce_to_owner(tp, "row_y", S, N, lambda red, rows: _ext().gemm_tp(
+                x, w, S, N, K_l, K_l, K_l, 0, 0, None, None, None, 0, [], 0, red, rows))
+            ctx.fused = True
+        else:
+            y = reduce_scatter_seq(torch.nn.functional.linear(x, w), tp.group)
+            ctx.fused = False
+        if b is not None:
+            y = y + b
+        ctx.save_for_backward(x, w)
+        ctx.has_b = b is not None
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        tp = ctx.tp
+        dy = dy.contiguous()
+        S_l, N = dy.shape
+        S, K_l = x.shape
+        gb = dy.float().sum(0) if ctx.has_b else None
+        if gb is not None:  # every rank's bias gradient covers only its tokens: sum them
+            dist.all_reduce(gb, group=tp.group)
+            gb = gb.to(w.dtype)
+        if ctx.fused:
+            yb = tp.publish("row_dy", dy)
+            dx = torch.empty(S, K_l, device=x.device, dtype=x.dtype)
+            # dX = gather(dY) W_l: A tiles from the peers' dY shards
+            _ext().gemm_tp(None, w, S, K_l, N, N, K_l, 0, 1, dx, None, None, 1, yb.peer_ptrs, S_l, [], 0)
+            # dW = gather(dY)^T x: the reduction over tokens reads the peers' dY shards
+            gw = torch.zeros(N, K_l, device=w.device, dtype=torch.float32)
+            _ext().gemm_tp(None, x, N, K_l, S, N, K_l, 1, 1, None, gw, None, 2, yb.peer_ptrs, S_l, [], 0)
+            return dx, gw.to(w.dtype), gb, None
+        dyg = all_gather_seq(dy, tp.group)
+        return (dyg @ w).to(x.dtype), (dyg.t().float() @ x.float()).to(w.dtype), gb, None
+
+
+def column_parallel_linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor], tp: TPContext):
+    """Sequence-sharded x [S_l, K] -> full-sequence output columns of this rank [S, N_l]."""
+    return _ColumnParallel.apply(x, w, b, tp)
+
+
+def row_parallel_linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor], tp: TPContext):
+    """Full-sequence input columns of this rank [S, K_l] -> sequence-sharded output [S_l, N]."""
+    return _RowParallel.apply(x, w, b, tp)
