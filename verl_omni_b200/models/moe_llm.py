@@ -91,6 +91,36 @@ class MoEBlock(nn.Module):
         self.w_gate_up = nn.Parameter(torch.randn(E, 2 * F_, D) * 0.02)  # [E, 2F, D]
         self.w_down = nn.Parameter(torch.randn(E, D, F_) * 0.02)  # [E, D, F]
 
+    def attn_tp(self, x, cos, sin, tp):
+        """Tensor + sequence parallel attention: ``x`` [B, S_l, D] holds this rank's tokens (rank r: positions
+        [r S_l, (r+1) S_l)); q/k/v of this rank's heads come from one all-gather->GEMM over the whole
+        sequence, the output projection's partial sums are reduce-scattered back to the token owners
+        (``parallel/tensor_parallel.py``).  ``cos`` / ``sin`` cover the full sequence."""
+        from verl_omni_b200.parallel.tensor_parallel import column_parallel_linear, row_parallel_linear
+
+        cfg = self.cfg
+        B, Sl, D = x.shape
+        W, r = tp.world, tp.rank
+        hd, Hq, Hk = cfg.head_dim, cfg.q_heads // W, cfg.kv_heads // W
+        S = Sl * W
+        h = rms_norm(x, self.ln1, cfg.eps).reshape(B * Sl, D)
+        kvw = self.kv_proj.weight.view(2, cfg.kv_heads * hd, D)
+        w = torch.cat([self.q_proj.weight[r * Hq * hd:(r + 1) * Hq * hd],
+                       kvw[0, r * Hk * hd:(r + 1) * Hk * hd], kvw[1, r * Hk * hd:(r + 1) * Hk * hd]], 0)
+        y = column_parallel_linear(h, w, None, tp)  # [W*B*Sl, (Hq + 2Hk) hd], rank-major rows
+        y = y.view(W, B, Sl, -1).permute(1, 0, 2, 3).reshape(B, S, -1)
+        q = y[..., :Hq * hd].view(B, S, Hq, hd)
+        k = y[..., Hq * hd:(Hq + Hk) * hd].view(B, S, Hk, hd)
+        v = y[..., (Hq + Hk) * hd:].view(B, S, Hk, hd).transpose(1, 2)
+        q = apply_rope(rms_norm(q.transpose(1, 2), self.q_norm, cfg.eps), cos, sin)
+        k = apply_rope(rms_norm(k.transpose(1, 2), self.k_norm, cfg.eps), cos, sin)
+        rep = Hq // Hk
+        o = attention(q.contiguous(), k.repeat_interleave(rep, 1).contiguous(),
+                      v.repeat_interleave(rep, 1).contiguous(), causal=True)  # [B, S, Hq hd]
+        o = o.view(B, W, Sl, -1).permute(1, 0, 2, 3).reshape(W * B * Sl, -1)
+        wo = self.o_proj.weight[:, r * Hq * hd:(r + 1) * Hq * hd]
+        return x + row_parallel_linear(o, wo, None, tp).view(B, Sl, D)
+
     def attn(self, x, cos, sin, cache: Optional[dict], pos0: int):
         cfg = self.cfg
         B, S, D = x.shape
@@ -134,7 +164,9 @@ class MoEBlock(nn.Module):
         """SwiGLU of locally-owned experts for tokens already grouped by expert."""
         return _ffn_grouped(tokens, expert_ids, self.w_gate_up, self.w_down)
 
-    def forward(self, x, cos, sin, cache=None, pos0: int = 0, ep=None):
+    def forward(self, x, cos, sin, cache=None, pos0: int = 0, ep=None, tp=None):
+        if tp is not None:
+            return self.moe(self.attn_tp(x, cos, sin, tp), ep)
         return self.moe(self.attn(x, cos, sin, cache, pos0), ep)
 
 
@@ -209,6 +241,7 @@ class MoELLM(nn.Module):
         self.audio_tower = _Encoder(cfg.audio_mel, cfg.audio_dim, cfg.audio_layers, cfg.hidden)
         self.visual = _Encoder(cfg.vision_patch_dim, cfg.vision_dim, cfg.vision_layers, cfg.hidden)
         self.ep = None
+        self.tp = None  # TPContext: tensor + sequence parallel training forwards (no KV cache)
 
     def embed_tokens(self, ids, audio_feats=None, image_patches=None):
         x = F.embedding(ids, self.embed)
@@ -230,6 +263,26 @@ class MoELLM(nn.Module):
         pos = torch.arange(pos0, pos0 + S, device=ids.device)
         cos, sin = rope_table(pos.cpu(), cfg.head_dim, cfg.rope_theta)
         cos, sin = cos.to(ids.device), sin.to(ids.device)
+        tp = self.tp if (self.tp is not None and caches is None and pos0 == 0 and self.tp.world > 1) else None
+        if tp is not None:
+            from verl_omni_b200.parallel.ulysses import gather_sequence
+
+            W = tp.world
+            pad = (-S) % W  # causal: zero tokens appended at the end change no earlier position
+            if pad:
+                x = torch.cat([x, x.new_zeros(B, pad, x.shape[-1])], 1)
+                pos = torch.arange(S + pad, device=ids.device)
+                cos, sin = rope_table(pos.cpu(), cfg.head_dim, cfg.rope_theta)
+                cos, sin = cos.to(ids.device), sin.to(ids.device)
+            Sl = x.shape[1] // W
+            x = x[:, tp.rank * Sl:(tp.rank + 1) * Sl]
+            for blk in self.layers:
+                x = blk(x, cos, sin, None, 0, self.ep, tp)
+            h = rms_norm(x, self.norm, cfg.eps)
+            if return_hidden:
+                return gather_sequence(h, tp.group)[:, :S]
+            # the vocabulary projection stays partitioned by tokens; the logits are gathered
+            return gather_sequence(self.lm_head(h).float(), tp.group)[:, :S]
         for i, blk in enumerate(self.layers):
             x = blk(x, cos, sin, None if caches is None else caches[i], pos0, self.ep)
         h = rms_norm(x, self.norm, cfg.eps)

@@ -197,6 +197,56 @@ def bench_ulysses(a) -> list[dict]:
     return rows
 
 
+def bench_tp(a) -> list[dict]:
+    """Tensor + sequence parallel attention projections of the Qwen3-Omni-30B-A3B thinker shape (hidden 2048,
+    32 x 128 query heads) over ``--S`` tokens (run under torchrun): column-parallel q projection (all-gather
+    -> GEMM) and row-parallel output projection (GEMM -> reduce-scatter), forward; NCCL collectives around
+    tcgen05 GEMMs vs the fused kernels.  Roofline = max(FLOPs / measured GEMM peak, NVLink bytes / 770 GB/s)."""
+    import os
+
+    import torch.distributed as dist
+
+    from verl_omni_b200.parallel import dist as D
+    from verl_omni_b200.parallel.tensor_parallel import TPContext, column_parallel_linear, row_parallel_linear
+
+    D.init_distributed(device="cuda", timeout_s=300)
+    W, dev = D.world_size(), torch.device("cuda", torch.cuda.current_device())
+    S, Dm, Q = a.S, 2048, 4096
+    torch.manual_seed(0)
+    x = torch.randn(S // W, Dm, device=dev, dtype=torch.bfloat16)
+    wq = (torch.randn(Q // W, Dm, device=dev) * 0.02).bfloat16()
+    wo = (torch.randn(Dm, Q // W, device=dev) * 0.02).bfloat16()
+    tp = TPContext(dist.group.WORLD)
+    rows = []
+    with torch.no_grad():
+        for name, fused in (("nccl", "0"), ("fused_peer", "1")):
+            os.environ["VO_TP_FUSED"] = fused
+
+            def step():
+                return row_parallel_linear(column_parallel_linear(x, wq, None, tp), wo, None, tp)
+
+            for _ in range(3):
+                step()
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(a.iters):
+                step()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = torch.tensor([e0.elapsed_time(e1) / a.iters], device=dev)
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+            flops = 2.0 * 2 * S * Dm * (Q // W)
+            xbytes = (W - 1) / W * S * Dm * (2 + 4)  # gathered bf16 activations in, fp32 partial sums out
+            t_roof = max(flops / 1.59e15, xbytes / 770e9) * 1e3
+            rows.append({"op": f"tp_attn_proj_{name}", "world": W, "tokens": S, "hidden": Dm, "ms": round(float(ms), 4),
+                         "tflops": round(flops / float(ms) / 1e9, 1), "roofline_ms": round(t_roof, 4),
+                         "frac_of_roofline": round(t_roof / float(ms), 3)})
+    tp.release()
+    return rows if D.rank() == 0 else []
+
+
 def bench_optstep(a) -> list[dict]:
     """Sharded optimizer step over ``--numel`` parameters on every rank (run under torchrun):
     NCCL reduce-scatter + AdamW + all-gather vs the fused peer-memory kernels.  Device time of the
@@ -352,7 +402,7 @@ def bench_groupnorm(a) -> list[dict]:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "gemm_sweep", "gemm_pair", "ulysses", "fmha", "sde", "adaln", "optstep", "moe", "groupnorm"])
+    ap.add_argument("op", choices=["gemm", "gemm_sweep", "gemm_pair", "ulysses", "tp", "fmha", "sde", "adaln", "optstep", "moe", "groupnorm"])
     ap.add_argument("--numel", type=int, default=2_240_000_000)
     ap.add_argument("--M", type=int, default=21712)
     ap.add_argument("--N", type=int, default=6144)
@@ -366,7 +416,7 @@ def main() -> None:
     ap.add_argument("--compare", action="store_true")
     a = ap.parse_args()
     pk = _peaks()
-    rows = {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "gemm_pair": bench_gemm_pair, "ulysses": bench_ulysses, "fmha": bench_fmha, "optstep": bench_optstep, "sde": bench_sde, "adaln": bench_adaln, "moe": bench_moe, "groupnorm": bench_groupnorm}[a.op](a)
+    rows = {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "gemm_pair": bench_gemm_pair, "ulysses": bench_ulysses, "tp": bench_tp, "fmha": bench_fmha, "optstep": bench_optstep, "sde": bench_sde, "adaln": bench_adaln, "moe": bench_moe, "groupnorm": bench_groupnorm}[a.op](a)
     for r in rows:
         if "tflops" in r:
             r[f"frac_of_{pk['src']}_gemm_peak"] = round(r["tflops"] / pk["tflops"], 3)

@@ -31,7 +31,7 @@ from verl_omni_b200.workers.rollout.llm_rollout import LLMRolloutEngine
 class OmniGRPOTrainer:
     def __init__(self, cfg: MoEConfig, actor_cfg: DiffusionActorConfig, *, device, n: int = 8,
                  prompt_text: int = 16, audio_tokens: int = 4, image_tokens: int = 4, response_len: int = 8,
-                 loss_mode: str = "grpo", ep_group=None, seed: int = 0):
+                 loss_mode: str = "grpo", ep_group=None, tp_group=None, seed: int = 0):
         torch.manual_seed(seed)
         self.cfg, self.actor_cfg, self.device, self.n = cfg, actor_cfg, device, n
         self.prompt_text, self.audio_tokens, self.image_tokens = prompt_text, audio_tokens, image_tokens
@@ -40,12 +40,21 @@ class OmniGRPOTrainer:
             from verl_omni_b200.parallel.expert_parallel import ExpertParallel
 
             self.model.ep = ExpertParallel(cfg.experts, ep_group)
+        # tensor + sequence parallelism (Megatron layout): ranks of a TP group share their samples and split each
+        # sequence and the attention heads; weights stay replicated, so every rank's gradient is its share and
+        # the loss is scaled by tp for the world-averaged gradient (groups of consecutive ranks)
+        self.tp_size = D.world_size(tp_group) if tp_group is not None else 1
+        if self.tp_size > 1:
+            from verl_omni_b200.parallel.tensor_parallel import TPContext
+
+            self.model.tp = TPContext(tp_group)
         self.engine = ShardedEngine(self.model, actor_cfg, device=device, total_steps=1000)
         self.rollout = LLMRolloutEngine(self.model, max_new_tokens=response_len, device=device)
         self.loss_fn = get_omni_loss_fn(loss_mode)
         self.loss_mode = loss_mode
         self.step_count = 0
         self.rank = D.rank()
+        self.dp_rank, self.dp = self.rank // self.tp_size, D.world_size() // self.tp_size
 
     def make_prompts(self, num: int, seed: int) -> DataProto:
         g = torch.Generator().manual_seed(seed)
@@ -68,7 +77,7 @@ class OmniGRPOTrainer:
     def step(self, num_prompts: int = 2) -> dict:
         self.step_count += 1
         t0 = time.perf_counter()
-        prompts = self.make_prompts(num_prompts, seed=1000 * self.step_count + self.rank).repeat(self.n)
+        prompts = self.make_prompts(num_prompts, seed=1000 * self.step_count + self.dp_rank).repeat(self.n)
         out = self.rollout.generate(prompts, seed=self.step_count)
         rewards = hash_token_reward(out, seed=7).to(self.device)
         adv = group_normalize(rewards, out.non_tensor_batch["uid"], global_std=False)
@@ -79,13 +88,13 @@ class OmniGRPOTrainer:
         self.engine.zero_grad()
         logp = self._resp_logprobs(out)
         loss, m = self.loss_fn(logp, old, adv, mask)
-        loss.backward()
+        (loss * self.tp_size).backward()
         norm = self.engine.optimizer_step()
         m.update({"actor/pg_loss": float(loss.detach()), "actor/grad_norm": float(norm.reshape(())),
                   "critic/rewards/mean": float(rewards.mean()),
                   "rollout_corr/logprob_abs_diff_mean": float(((old - out.batch["rollout_log_probs"].to(self.device))
                                                                .abs() * mask).sum() / mask.sum())})
-        m.update(M.compute_throughput_metrics_diffusion(time.perf_counter() - t0, len(out) * D.world_size(),
+        m.update(M.compute_throughput_metrics_diffusion(time.perf_counter() - t0, len(out) * self.dp,
                                                          D.world_size()))
         return m
 
