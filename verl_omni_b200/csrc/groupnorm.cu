@@ -70,32 +70,50 @@ __global__ void gn_finalize_kernel(const float* __restrict__ part, int nchunks, 
   }
 }
 
+// grid (position chunks, sample): each thread owns one 8-channel vector column (fixed per thread, so the
+// per-channel scale / shift are computed once) and walks positions with a stride; no integer division in
+// the loop.
 template <bool SILU>
 __global__ void __launch_bounds__(kThreads) gn_apply_kernel(const __nv_bfloat16* __restrict__ x,
                                                             const __nv_bfloat16* __restrict__ gamma,
                                                             const __nv_bfloat16* __restrict__ beta,
                                                             const float* __restrict__ mean,
                                                             const float* __restrict__ rstd,
-                                                            __nv_bfloat16* __restrict__ y, int64_t NP, int64_t P, int C,
-                                                            int G) {
+                                                            __nv_bfloat16* __restrict__ y, int64_t P, int C, int G,
+                                                            int64_t pos_per_chunk) {
+  const int n = blockIdx.y;
   const int vpr = C / 8;
   const int cpg = C / G;
-  const int64_t nvec = NP * vpr;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += (int64_t)gridDim.x * blockDim.x) {
-    const int vc = (int)(i % vpr);
-    const int n = (int)(i / vpr / P);
-    float f[8], w[8], b[8], o[8];
-    unpack8(reinterpret_cast<const bf16x8*>(x)[i], f);
+  const int pstep = blockDim.x / vpr;
+  if (threadIdx.x >= pstep * vpr) return;
+  const int vc = threadIdx.x % vpr;
+  float sc[8], sh[8];
+  {
+    float w[8], b[8];
     unpack8(reinterpret_cast<const bf16x8*>(gamma)[vc], w);
     unpack8(reinterpret_cast<const bf16x8*>(beta)[vc], b);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int g = (vc * 8 + j) / cpg;
-      float v = (f[j] - mean[n * G + g]) * rstd[n * G + g] * w[j] + b[j];
+      const float r = rstd[n * G + g];
+      sc[j] = r * w[j];
+      sh[j] = b[j] - mean[n * G + g] * sc[j];
+    }
+  }
+  const int64_t p0 = (int64_t)blockIdx.x * pos_per_chunk;
+  const int64_t p1 = min(P, p0 + pos_per_chunk);
+  const bf16x8* xin = reinterpret_cast<const bf16x8*>(x + (int64_t)n * P * C) + vc;
+  bf16x8* yout = reinterpret_cast<bf16x8*>(y + (int64_t)n * P * C) + vc;
+  for (int64_t p = p0 + threadIdx.x / vpr; p < p1; p += pstep) {
+    float f[8], o[8];
+    unpack8(xin[p * vpr], f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float v = fmaf(f[j], sc[j], sh[j]);
       if (SILU) v = v / (1.f + __expf(-v));
       o[j] = v;
     }
-    reinterpret_cast<bf16x8*>(y)[i] = pack8(o);
+    yout[p * vpr] = pack8(o);
   }
 }
 
@@ -127,17 +145,19 @@ torch::Tensor group_norm_nhwc(torch::Tensor x, torch::Tensor gamma, torch::Tenso
       xp, P, (int)C, G, per, part.data_ptr<float>());
   gn_finalize_kernel<<<(unsigned)N, 64, 0, stream()>>>(part.data_ptr<float>(), nchunks, G, (double)P * (C / G),
                                                        (float)eps, mean.data_ptr<float>(), rstd.data_ptr<float>());
-  const int64_t nvec = N * P * C / 8;
-  const unsigned grid = (unsigned)std::min<int64_t>((nvec + kThreads - 1) / kThreads, 16LL * num_sms());
+  // ~8 blocks per SM over the batch for the apply pass
+  const int64_t want2 = std::max<int64_t>(1, 8LL * num_sms() / N);
+  const int64_t per2 = std::max<int64_t>(32, (P + want2 - 1) / want2);
+  const unsigned nch2 = (unsigned)((P + per2 - 1) / per2);
   auto* gp = reinterpret_cast<const __nv_bfloat16*>(g.data_ptr<at::BFloat16>());
   auto* bp = reinterpret_cast<const __nv_bfloat16*>(b.data_ptr<at::BFloat16>());
   auto* yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr<at::BFloat16>());
   if (silu)
-    gn_apply_kernel<true><<<grid, kThreads, 0, stream()>>>(xp, gp, bp, mean.data_ptr<float>(), rstd.data_ptr<float>(),
-                                                           yp, N * P, P, (int)C, G);
+    gn_apply_kernel<true><<<dim3(nch2, (unsigned)N), kThreads, 0, stream()>>>(
+        xp, gp, bp, mean.data_ptr<float>(), rstd.data_ptr<float>(), yp, P, (int)C, G, per2);
   else
-    gn_apply_kernel<false><<<grid, kThreads, 0, stream()>>>(xp, gp, bp, mean.data_ptr<float>(),
-                                                            rstd.data_ptr<float>(), yp, N * P, P, (int)C, G);
+    gn_apply_kernel<false><<<dim3(nch2, (unsigned)N), kThreads, 0, stream()>>>(
+        xp, gp, bp, mean.data_ptr<float>(), rstd.data_ptr<float>(), yp, P, (int)C, G, per2);
   count_launch(3);
   VO_CUDA_OK(cudaGetLastError());
   return y;
