@@ -1,0 +1,41 @@
+"""Grouped-query decode attention over a preallocated KV cache, and the device sampler, against fp32
+references."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("hd,rep,Hk", [(128, 8, 4), (128, 1, 8), (64, 4, 2), (64, 2, 4)])
+@pytest.mark.parametrize("splits", [1, 3])
+def test_decode_attention_matches_reference(hd, rep, Hk, splits):
+    from verl_omni_b200.ops.decode import decode_attention, decode_attention_reference
+
+    torch.manual_seed(0)
+    B, Lmax = 3, 700
+    q = torch.randn(B, Hk * rep, hd, device="cuda").bfloat16()
+    kc = torch.randn(B, Hk, Lmax, hd, device="cuda").bfloat16()
+    vc = torch.randn(B, Hk, Lmax, hd, device="cuda").bfloat16()
+    lens = torch.tensor([1, 333, 700], dtype=torch.int32, device="cuda")
+    out = decode_attention(q, kc, vc, lens, splits=splits)
+    ref = decode_attention_reference(q, kc, vc, lens, hd ** -0.5)
+    torch.testing.assert_close(out.float(), ref.float(), rtol=2e-2, atol=2e-2)
+
+
+def test_device_sampler_distribution_and_logprobs():
+    from verl_omni_b200.ops.decode import sample_tokens
+
+    torch.manual_seed(0)
+    logits = torch.randn(4, 50, device="cuda") * 2
+    g = torch.Generator(device="cuda").manual_seed(1)
+    counts = torch.zeros(4, 50, device="cuda")
+    for _ in range(4000):
+        ids, lp = sample_tokens(logits, 1.0, 0, 1.0, g)
+        counts[torch.arange(4), ids] += 1
+    freq = counts / 4000
+    torch.testing.assert_close(freq, torch.softmax(logits, -1), rtol=0, atol=0.03)
+    torch.testing.assert_close(lp, torch.log_softmax(logits, -1).gather(-1, ids[:, None]).squeeze(-1))
+    ids, _ = sample_tokens(logits, 1.0, 5, 1.0, g)  # top-k keeps the 5 largest
+    top5 = torch.topk(logits, 5, -1).indices
+    assert bool((top5 == ids[:, None]).any(-1).all())

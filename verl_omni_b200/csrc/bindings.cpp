@@ -68,6 +68,8 @@ int64_t gemm_error(bool reset);
 std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal, double scale,
                                     int64_t version, int64_t split);
 int64_t fmha_error(bool reset);
+torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor lens,
+                               double scale, int64_t splits);
 void fmha_fwd_peer(torch::Tensor q, torch::Tensor k, torch::Tensor v, std::vector<int64_t> peer_o,
                    std::vector<int64_t> peer_o2, int64_t sl, int64_t si, int64_t htot, int64_t h0, double scale);
 std::vector<torch::Tensor> linear_bwd_prep(torch::Tensor dy, c10::optional<torch::Tensor> saved,
@@ -126,6 +128,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fmha_fwd", &vo::fmha_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("causal"), py::arg("scale"),
         py::arg("version") = 2, py::arg("split") = 0);
   m.def("fmha_error", &vo::fmha_error);
+  m.def("decode_attention", &vo::decode_attention, "grouped-query decode attention over a KV cache");
   m.def("fmha_fwd_peer", &vo::fmha_fwd_peer, "Ulysses attention writing each output row to its owner rank");
   m.def("fmha_bwd", &vo::fmha_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
         py::arg("dO"), py::arg("causal"), py::arg("scale"), py::arg("version") = 1, py::arg("o2") = py::none(),

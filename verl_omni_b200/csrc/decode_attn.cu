@@ -1,0 +1,229 @@
+// Grouped-query decode attention over a preallocated KV cache (one new query token per sequence).
+//
+// Decode is bound by reading the cache, so each CTA owns one (sequence, KV head) pair and a slice of the
+// keys, and serves every query head of that group from one read of each K / V tile:
+//   * K and V tiles of 64 keys are staged in shared memory with 16-byte loads (rows padded by 16 bytes so
+//     the per-key row reads of the score phase do not collide in banks);
+//   * scores: the REP x 64 scores of a tile are spread over the 128 threads (consecutive threads take
+//     consecutive keys of one query head; REP <= 8 heads per group);
+//   * online softmax per head over the CTA's keys; P V with each thread owning one head-dim column for
+//     all heads of the group;
+//   * key ranges split over `splits` CTAs (flash-decoding) write (max, sum, O) partials that a second
+//     kernel merges; with one split the first kernel writes the output directly.
+// Lengths differ per sequence (`lens[b]` valid cache rows).
+#include "common.cuh"
+
+namespace vo {
+namespace {
+
+constexpr int kTile = 64;
+constexpr int kDecThreads = 128;
+
+template <int HD, int REP>
+__global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
+    const __nv_bfloat16* __restrict__ q,      // [B, Hk * REP, HD]
+    const __nv_bfloat16* __restrict__ kc,     // [B, Hk, Lmax, HD]
+    const __nv_bfloat16* __restrict__ vc,     // [B, Hk, Lmax, HD]
+    const int* __restrict__ lens, int Hk, int Lmax, float scale_log2, int splits,
+    __nv_bfloat16* __restrict__ out,          // [B, Hk * REP, HD] (splits == 1)
+    float* __restrict__ part_o,               // [B, Hk, splits, REP, HD]
+    float* __restrict__ part_ml) {            // [B, Hk, splits, REP, 2]
+  constexpr int ROW = HD + 8;  // padded smem row (bf16 elements)
+  __shared__ __align__(16) __nv_bfloat16 ks[kTile * ROW];
+  __shared__ __align__(16) __nv_bfloat16 vs[kTile * HD];
+  __shared__ float qs[REP * HD];
+  __shared__ float ps[REP * kTile];
+  __shared__ float mrow[REP], lrow[REP], alpha_s[REP];
+
+  const int bk = blockIdx.x, split = blockIdx.y;
+  const int b = bk / Hk, kh = bk % Hk;
+  const int L = lens[b];
+  const int per = (L + splits - 1) / splits;
+  const int s0 = split * per, s1 = min(L, s0 + per);
+  const int tid = threadIdx.x;
+  const __nv_bfloat16* qb = q + ((int64_t)b * Hk * REP + (int64_t)kh * REP) * HD;
+  for (int i = tid; i < REP * HD; i += kDecThreads) qs[i] = bf2f(qb[i]) * scale_log2;
+  if (tid < REP) {
+    mrow[tid] = -INFINITY;
+    lrow[tid] = 0.f;
+  }
+  // this thread's output columns: d = tid % HD for heads h = tid / HD + k (HD / kDecThreads ...)
+  constexpr int OUT_PER = (REP * HD + kDecThreads - 1) / kDecThreads;  // outputs owned per thread
+  float acc[OUT_PER];
+#pragma unroll
+  for (int i = 0; i < OUT_PER; ++i) acc[i] = 0.f;
+  const int64_t kvbase = ((int64_t)b * Hk + kh) * Lmax * HD;
+  __syncthreads();
+
+  for (int t0 = s0; t0 < s1; t0 += kTile) {
+    const int nk = min(kTile, s1 - t0);
+    // stage K (padded rows) and V
+    for (int i = tid; i < kTile * (HD / 8); i += kDecThreads) {
+      const int r = i / (HD / 8), c = i % (HD / 8);
+      bf16x8 kv = {}, vv = {};
+      if (r < nk) {
+        kv = reinterpret_cast<const bf16x8*>(kc + kvbase + (int64_t)(t0 + r) * HD)[c];
+        vv = reinterpret_cast<const bf16x8*>(vc + kvbase + (int64_t)(t0 + r) * HD)[c];
+      }
+      *reinterpret_cast<bf16x8*>(ks + r * ROW + c * 8) = kv;
+      *reinterpret_cast<bf16x8*>(vs + r * HD + c * 8) = vv;
+    }
+    __syncthreads();
+    // scores (log2 domain)
+    for (int i = tid; i < REP * kTile; i += kDecThreads) {
+      const int h = i / kTile, k = i % kTile;
+      float s = -INFINITY;
+      if (k < nk) {
+        s = 0.f;
+        const float* qh = qs + h * HD;
+#pragma unroll 4
+        for (int c = 0; c < HD / 8; ++c) {
+          float f[8];
+          unpack8(*reinterpret_cast<const bf16x8*>(ks + k * ROW + c * 8), f);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) s = fmaf(qh[c * 8 + j], f[j], s);
+        }
+      }
+      ps[i] = s;
+    }
+    __syncthreads();
+    // per-head running max / sum (one warp per head, heads strided over the 4 warps)
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int h = warp; h < REP; h += kDecThreads / 32) {
+      const float a = ps[h * kTile + lane], c2 = ps[h * kTile + 32 + lane];
+      const float mx = warp_max(fmaxf(a, c2));
+      const float m_old = mrow[h];
+      const float m_new = fmaxf(m_old, mx);
+      const float e0 = (a == -INFINITY) ? 0.f : exp2f(a - m_new);
+      const float e1 = (c2 == -INFINITY) ? 0.f : exp2f(c2 - m_new);
+      ps[h * kTile + lane] = e0;
+      ps[h * kTile + 32 + lane] = e1;
+      const float sum = warp_sum(e0 + e1);
+      if (lane == 0) {
+        const float al = (m_old == -INFINITY) ? 0.f : exp2f(m_old - m_new);
+        alpha_s[h] = al;
+        lrow[h] = lrow[h] * al + sum;
+        mrow[h] = m_new;
+      }
+    }
+    __syncthreads();
+    // O = O * alpha + P V
+#pragma unroll
+    for (int i = 0; i < OUT_PER; ++i) {
+      const int o = tid + i * kDecThreads;
+      if (o >= REP * HD) break;
+      const int h = o / HD, d = o % HD;
+      float a = acc[i] * alpha_s[h];
+      const float* ph = ps + h * kTile;
+      for (int k = 0; k < nk; ++k) a = fmaf(ph[k], bf2f(vs[k * HD + d]), a);
+      acc[i] = a;
+    }
+    __syncthreads();
+  }
+  if (splits == 1) {
+#pragma unroll
+    for (int i = 0; i < OUT_PER; ++i) {
+      const int o = tid + i * kDecThreads;
+      if (o >= REP * HD) break;
+      const int h = o / HD, d = o % HD;
+      const float l = lrow[h];
+      out[((int64_t)b * Hk * REP + (int64_t)kh * REP + h) * HD + d] = f2bf(l > 0.f ? acc[i] / l : 0.f);
+    }
+    return;
+  }
+  const int64_t pbase = (((int64_t)b * Hk + kh) * splits + split) * REP;
+#pragma unroll
+  for (int i = 0; i < OUT_PER; ++i) {
+    const int o = tid + i * kDecThreads;
+    if (o < REP * HD) part_o[pbase * HD + o] = acc[i];
+  }
+  if (tid < REP) {
+    part_ml[(pbase + tid) * 2] = mrow[tid];
+    part_ml[(pbase + tid) * 2 + 1] = lrow[tid];
+  }
+}
+
+// merges the split partials: one thread per (sequence, head, dim)
+template <int HD, int REP>
+__global__ void decode_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int Hk,
+                                      int splits, int64_t total, __nv_bfloat16* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int d = (int)(i % HD);
+    const int64_t bhq = i / HD;  // (b, kh, h)
+    const int h = (int)(bhq % REP);
+    const int64_t bk = bhq / REP;
+    float m = -INFINITY;
+    for (int s = 0; s < splits; ++s) m = fmaxf(m, part_ml[((bk * splits + s) * REP + h) * 2]);
+    float l = 0.f, o = 0.f;
+    if (m != -INFINITY) {
+      for (int s = 0; s < splits; ++s) {
+        const int64_t pi = (bk * splits + s) * REP + h;
+        const float ms = part_ml[pi * 2];
+        if (ms == -INFINITY) continue;
+        const float w = exp2f(ms - m);
+        l += part_ml[pi * 2 + 1] * w;
+        o += part_o[pi * HD + d] * w;
+      }
+    }
+    out[bhq * HD + d] = f2bf(l > 0.f ? o / l : 0.f);
+  }
+}
+
+template <int HD, int REP>
+void launch_decode(const torch::Tensor& q, const torch::Tensor& kc, const torch::Tensor& vc, const torch::Tensor& lens,
+                   float scale_log2, int splits, torch::Tensor& out) {
+  const int B = (int)kc.size(0), Hk = (int)kc.size(1), Lmax = (int)kc.size(2);
+  auto fo = q.options().dtype(torch::kFloat32);
+  torch::Tensor po, pml;
+  if (splits > 1) {
+    po = torch::empty({B, Hk, splits, REP, HD}, fo);
+    pml = torch::empty({B, Hk, splits, REP, 2}, fo);
+  }
+  auto bfp = [](const torch::Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr<at::BFloat16>()); };
+  decode_attn_kernel<HD, REP><<<dim3(B * Hk, splits), kDecThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      bfp(q), bfp(kc), bfp(vc), lens.data_ptr<int>(), Hk, Lmax, scale_log2, splits,
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()), splits > 1 ? po.data_ptr<float>() : nullptr,
+      splits > 1 ? pml.data_ptr<float>() : nullptr);
+  count_launch();
+  if (splits > 1) {
+    const int64_t total = (int64_t)B * Hk * REP * HD;
+    const int grid = (int)std::min<int64_t>((total + 255) / 256, 4096);
+    decode_combine_kernel<HD, REP><<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        po.data_ptr<float>(), pml.data_ptr<float>(), Hk, splits, total,
+        reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()));
+    count_launch();
+  }
+  VO_CUDA_OK(cudaGetLastError());
+}
+
+}  // namespace
+
+// q [B, Hq, HD] bf16; k_cache / v_cache [B, Hk, Lmax, HD] bf16; lens [B] int32 (valid rows, >= 1).
+// Returns o [B, Hq, HD].  Hq = Hk x rep with rep in {1, 2, 4, 8}; HD in {64, 128}.
+torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor lens,
+                               double scale, int64_t splits) {
+  VO_CHECK_INPUT(q);
+  VO_CHECK_INPUT(k_cache);
+  VO_CHECK_INPUT(v_cache);
+  VO_CHECK_INPUT(lens);
+  TORCH_CHECK(q.scalar_type() == torch::kBFloat16 && k_cache.scalar_type() == torch::kBFloat16 &&
+                  lens.scalar_type() == torch::kInt32,
+              "bf16 q / cache, int32 lengths");
+  const int64_t B = q.size(0), Hq = q.size(1), HD = q.size(2), Hk = k_cache.size(1);
+  TORCH_CHECK(k_cache.size(0) == B && k_cache.size(3) == HD && v_cache.sizes() == k_cache.sizes() && Hq % Hk == 0 &&
+                  lens.numel() == B,
+              "decode attention shapes");
+  c10::cuda::CUDAGuard g(q.device());
+  auto out = torch::empty_like(q);
+  const int rep = (int)(Hq / Hk);
+  const float sl2 = (float)scale * 1.4426950408889634f;
+  const int sp = (int)std::max<int64_t>(1, splits);
+#define VO_DEC(HDV, REPV) \
+  if (HD == HDV && rep == REPV) return launch_decode<HDV, REPV>(q, k_cache, v_cache, lens, sl2, sp, out), out;
+  VO_DEC(128, 8) VO_DEC(128, 4) VO_DEC(128, 2) VO_DEC(128, 1) VO_DEC(64, 8) VO_DEC(64, 4) VO_DEC(64, 2) VO_DEC(64, 1)
+#undef VO_DEC
+  TORCH_CHECK(false, "decode attention: head_dim 64 / 128 and 1, 2, 4 or 8 query heads per KV head");
+  return out;
+}
+
+}  // namespace vo

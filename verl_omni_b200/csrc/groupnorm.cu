@@ -110,7 +110,7 @@ __global__ void __launch_bounds__(kThreads) gn_apply_kernel(const __nv_bfloat16*
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       float v = fmaf(f[j], sc[j], sh[j]);
-      if (SILU) v = v / (1.f + __expf(-v));
+      if (SILU) v = __fdividef(v, 1.f + __expf(-v));
       o[j] = v;
     }
     yout[p * vpr] = pack8(o);

@@ -26,6 +26,7 @@ import torch.nn.functional as F
 from verl_omni_b200.models.layers import Linear, rope_table
 from verl_omni_b200.ops.attention import attention
 from verl_omni_b200.ops import linear as L
+from verl_omni_b200.ops.decode import KVCache, decode_attention
 
 
 @dataclass
@@ -131,7 +132,16 @@ class MoEBlock(nn.Module):
         k, v = kv[:, :, 0].transpose(1, 2), kv[:, :, 1].transpose(1, 2)
         q = apply_rope(rms_norm(q, self.q_norm, cfg.eps), cos, sin)
         k = apply_rope(rms_norm(k, self.k_norm, cfg.eps), cos, sin)
-        if cache is not None:
+        if isinstance(cache, KVCache):
+            # preallocated cache: in-place append; one-token steps use the grouped-query decode kernel
+            first = cache.len == 0
+            cache.append(k, v)
+            if S == 1 and not first:
+                o = decode_attention(q[:, :, 0], cache.k, cache.v, cache.lens())  # [B, Hq, hd]
+                return x + self.o_proj(o.reshape(B, 1, cfg.q_heads * hd))
+            if not first:
+                k, v = cache.k[:, :, :cache.len], cache.v[:, :, :cache.len]
+        elif cache is not None:
             if "k" in cache:
                 k = torch.cat([cache["k"], k], 2)
                 v = torch.cat([cache["v"], v], 2)

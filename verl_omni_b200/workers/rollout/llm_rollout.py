@@ -1,9 +1,10 @@
 """Autoregressive rollout for the omni thinker (the vLLM-Omni AR mode of the reference,
 ``verl_omni/workers/rollout/vllm_rollout/vllm_omni_async_server.py:537-579``).
 
-Batched prefill of the (multimodal) prompts, then token-by-token decode against per-layer KV caches;
-sampling with temperature / top-k / top-p from a seeded generator; returns the response ids, their
-log-probs under the sampling distribution (``rollout_log_probs``) and an EOS-aware response mask.
+Batched prefill of the (multimodal) prompts, then token-by-token decode against preallocated per-layer KV
+caches (grouped-query decode kernel); sampling with temperature / top-k / top-p on the device from a
+seeded generator; returns the response ids, their log-probs under the sampling distribution
+(``rollout_log_probs``) and an EOS-aware response mask.
 """
 
 from __future__ import annotations
@@ -13,6 +14,7 @@ from typing import Optional
 import torch
 
 from verl_omni_b200.models.moe_llm import MoELLM
+from verl_omni_b200.ops.decode import KVCache, sample_tokens
 from verl_omni_b200.utils.dataproto import DataProto
 
 
@@ -46,18 +48,22 @@ class LLMRolloutEngine:
     def generate(self, batch: DataProto, seed: int = 0) -> DataProto:
         ids = batch.batch["input_ids"].to(self.device)
         B, P = ids.shape
-        g = torch.Generator().manual_seed(int(seed))
-        caches = [dict() for _ in self.module.layers]
+        dev = ids.device
+        g = torch.Generator(device=dev).manual_seed(int(seed))  # sampling stays on the device
+        cfg = self.module.cfg
+        caches = [KVCache(B, cfg.kv_heads, P + self.max_new_tokens, cfg.head_dim, dev, self.module.embed.dtype)
+                  for _ in self.module.layers]
         logits = self.module(ids, caches=caches, pos0=0, audio_feats=batch.batch.get("audio_feats"),
                              image_patches=batch.batch.get("image_patches"))[:, -1]
         out_ids, out_lp = [], []
         done = torch.zeros(B, dtype=torch.bool, device=ids.device)
         mask = []
         for t in range(self.max_new_tokens):
-            lp_all = torch.log_softmax(logits.float() / max(self.temperature, 1e-6), -1)
-            nxt = sample_next(logits, self.temperature, self.top_k, self.top_p, g)
+            nxt, lp = sample_tokens(logits, self.temperature, self.top_k, self.top_p, g)
+            if self.temperature <= 0:
+                lp = torch.log_softmax(logits.float(), -1).gather(-1, nxt[:, None]).squeeze(-1)
             out_ids.append(nxt)
-            out_lp.append(lp_all.gather(-1, nxt[:, None]).squeeze(-1))
+            out_lp.append(lp)
             mask.append(~done)
             if self.eos_id is not None:
                 done = done | (nxt == self.eos_id)
