@@ -4,6 +4,7 @@ import os
 import time
 
 import pytest
+import torch
 import torch.multiprocessing as mp
 
 from tests._dist_util import free_port
@@ -129,3 +130,48 @@ def test_rollout_server_drain_then_abort():
     assert n == 2 and dt < 10
     assert all(o.aborted for o in outs)
     assert sorted(o.metadata["request_id"] for o in outs) == ["r0", "r1", "r2"]
+
+
+def _retention(rank, world, outdir):
+    from tests.test_e2e_tiny_on_cpu import OVR
+    from verl_omni_b200.trainer.diffusion.flow_grpo_trainer import PolicyGradientTrainer
+    from verl_omni_b200.utils.config import load_config
+
+    cfg = load_config("diffusion_trainer", OVR + [f"trainer.default_local_dir={outdir}", "trainer.total_training_steps=3",
+                                                  "trainer.save_freq=1", "trainer.resume_mode=disable",
+                                                  "trainer.max_actor_ckpt_to_keep=2",
+                                                  "global_profiler.tool=torch", "global_profiler.steps=[2]",
+                                                  f"global_profiler.save_path={outdir}/prof"])
+    PolicyGradientTrainer(cfg).fit()
+
+
+def test_checkpoint_retention_and_step_profiler(tmp_path):
+    from tests._dist_util import run_ranks
+
+    run_ranks(_retention, 1, (str(tmp_path),))
+    kept = sorted(d for d in os.listdir(tmp_path) if d.startswith("global_step_"))
+    assert kept == ["global_step_2", "global_step_3"]
+    assert (tmp_path / "prof" / "trace_step2_rank0.json").exists()
+
+
+def _det(rank, world, outdir, tag):
+    from tests.test_e2e_tiny_on_cpu import OVR
+    from verl_omni_b200.trainer.diffusion.flow_grpo_trainer import PolicyGradientTrainer
+    from verl_omni_b200.utils.config import load_config
+
+    cfg = load_config("diffusion_trainer", OVR + ["trainer.total_training_steps=2", "trainer.resume_mode=disable"])
+    t = PolicyGradientTrainer(cfg)
+    t.fit()
+    if rank == 0:
+        torch.save(t.actor.engine.flat.flat.clone(), f"{outdir}/{tag}.pt")
+
+
+def test_two_identical_runs_are_bitwise_equal(tmp_path):
+    """Deterministic mode: the same seeds and config give bit-identical weights (two gloo world-2 runs)."""
+    import torch
+
+    from tests._dist_util import run_ranks
+
+    run_ranks(_det, 2, (str(tmp_path), "a"))
+    run_ranks(_det, 2, (str(tmp_path), "b"))
+    assert torch.equal(torch.load(tmp_path / "a.pt"), torch.load(tmp_path / "b.pt"))

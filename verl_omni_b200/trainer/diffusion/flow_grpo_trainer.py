@@ -255,6 +255,17 @@ class PolicyGradientTrainer:
     def step(self, global_ids: Optional[list[int]] = None) -> dict:
         self._check_ranks_alive()
         self.global_step += 1
+        if getattr(self, "_profiler", None) is None:
+            from verl_omni_b200.utils.profiler import StepProfiler
+
+            self._profiler = StepProfiler(self.config.get("global_profiler"), self.rank)
+        self._profiler.start(self.global_step)
+        try:
+            return self._step_body(global_ids)
+        finally:
+            self._profiler.stop(self.global_step)
+
+    def _step_body(self, global_ids: Optional[list[int]] = None) -> dict:
         timer = M.PhaseTimer(self.device)
         t_start = time.perf_counter()
         if self.device.type == "cuda":
@@ -327,8 +338,21 @@ class PolicyGradientTrainer:
                        os.path.join(root, "data.pt"))
             with open(os.path.join(self.ckpt_dir, "latest_checkpointed_iteration.txt"), "w") as f:
                 f.write(str(self.global_step))
+            self._prune_checkpoints()
         D.barrier()
         return root
+
+    def _prune_checkpoints(self) -> None:
+        """``trainer.max_actor_ckpt_to_keep``: keep the newest K ``global_step_*`` directories."""
+        keep = self.config.trainer.get("max_actor_ckpt_to_keep")
+        if not keep or int(keep) <= 0:
+            return
+        import shutil
+
+        steps = sorted(int(d.split("_")[-1]) for d in os.listdir(self.ckpt_dir)
+                       if d.startswith("global_step_") and d.split("_")[-1].isdigit())
+        for st in steps[:-int(keep)]:
+            shutil.rmtree(os.path.join(self.ckpt_dir, f"global_step_{st}"), ignore_errors=True)
 
     def maybe_resume(self) -> bool:
         mode = self.config.trainer.resume_mode

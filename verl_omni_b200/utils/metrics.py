@@ -56,14 +56,17 @@ class PhaseTimer:
 
     @contextmanager
     def __call__(self, name: str):
-        if self.device is not None and self.device.type == "cuda":
+        cuda = self.device is not None and self.device.type == "cuda"
+        if cuda:
             torch.cuda.synchronize(self.device)
+            torch.cuda.nvtx.range_push(name)  # phase ranges for nsys / ncu range filters
         t0 = time.perf_counter()
         try:
             yield
         finally:
-            if self.device is not None and self.device.type == "cuda":
+            if cuda:
                 torch.cuda.synchronize(self.device)
+                torch.cuda.nvtx.range_pop()
             self.timing[name] = self.timing.get(name, 0.0) + time.perf_counter() - t0
 
 
