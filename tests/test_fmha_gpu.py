@@ -123,3 +123,23 @@ def test_attention_split_matches_joint(E, fwd, bwd, D, monkeypatch):
     o.backward(torch.cat([ga, gb], 1))
     for a, b in ((q, qr), (k, kr), (v, vr)):
         torch.testing.assert_close(a.grad.float(), b.grad.float(), rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_split_attention_with_key_counts_matches_masked_sdpa(D):
+    """Right-padded prompts: the tcgen05 forward with per-sequence key counts equals masked SDPA."""
+    from verl_omni_b200.ops.attention import attention_split
+
+    torch.manual_seed(0)
+    B, H, Si, St = 3, 4, 256, 200
+    S = Si + St
+    q, k, v = (torch.randn(B, H, S, D, device="cuda").bfloat16() for _ in range(3))
+    kv_len = torch.tensor([S, Si + 57, Si + 1], dtype=torch.int32, device="cuda")
+    with torch.no_grad():
+        oi, ot = attention_split(q, k, v, Si, kv_len=kv_len)
+        keep = torch.arange(S, device="cuda")[None, :] < kv_len[:, None].long()
+        ref = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float(),
+                                                               attn_mask=keep[:, None, None, :])
+        ref = ref.transpose(1, 2).reshape(B, S, H * D)
+    torch.testing.assert_close(oi.float(), ref[:, :Si], rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(ot.float(), ref[:, Si:], rtol=2e-2, atol=2e-2)

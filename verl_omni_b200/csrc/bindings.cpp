@@ -66,7 +66,7 @@ void gemm_wgrad_pair(torch::Tensor dy0, torch::Tensor x0, torch::Tensor out0, to
 torch::Tensor gelu_tanh_bwd(torch::Tensor dy, torch::Tensor pre);
 int64_t gemm_error(bool reset);
 std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal, double scale,
-                                    int64_t version, int64_t split);
+                                    int64_t version, int64_t split, c10::optional<torch::Tensor> kv_len);
 int64_t fmha_error(bool reset);
 torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor lens,
                                double scale, int64_t splits);
@@ -126,7 +126,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gelu_tanh_bwd", &vo::gelu_tanh_bwd);
   m.def("gemm_error", &vo::gemm_error);
   m.def("fmha_fwd", &vo::fmha_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("causal"), py::arg("scale"),
-        py::arg("version") = 2, py::arg("split") = 0);
+        py::arg("version") = 2, py::arg("split") = 0, py::arg("kv_len") = py::none());
   m.def("fmha_error", &vo::fmha_error);
   m.def("decode_attention", &vo::decode_attention, "grouped-query decode attention over a KV cache");
   m.def("fmha_fwd_peer", &vo::fmha_fwd_peer, "Ulysses attention writing each output row to its owner rank");

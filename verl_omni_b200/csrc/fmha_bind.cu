@@ -9,6 +9,9 @@ extern "C" int vo_fmha_fwd2(const void* q, const void* k, const void* v, void* o
 extern "C" int vo_fmha_fwd2_error(int reset);
 extern "C" int vo_fmha_fwd3(const void* q, const void* k, const void* v, void* o, void* o2, int out_split, float* lse,
                             int B, int H, int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream);
+extern "C" int vo_fmha_fwd3_kvlen(const void* q, const void* k, const void* v, void* o, void* o2, int out_split,
+                                  float* lse, const int* kv_len, int B, int H, int Sq, int Skv, int D, float scale,
+                                  cudaStream_t stream);
 extern "C" int vo_fmha_fwd_peer(const void* q, const void* k, const void* v, void* const* peer_o,
                                 void* const* peer_o2, int nranks, int sl, int si, int htot, int h0, float* lse, int B,
                                 int H, int Sq, int Skv, int D, float scale, cudaStream_t stream);
@@ -27,7 +30,7 @@ namespace vo {
 // second tensor o2 [B, Sq - split, H, D] (the image / text halves of a joint attention, each feeding
 // its own output projection without a copy).
 std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal, double scale,
-                                    int64_t version, int64_t split) {
+                                    int64_t version, int64_t split, c10::optional<torch::Tensor> kv_len) {
   VO_CHECK_INPUT(q);
   VO_CHECK_INPUT(k);
   VO_CHECK_INPUT(v);
@@ -41,7 +44,14 @@ std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Ten
   torch::Tensor o2 = split > 0 ? torch::empty({B, Sq - split, H, D}, q.options()) : torch::Tensor();
   auto lse = torch::empty({B, H, Sq}, q.options().dtype(torch::kFloat32));
   int rc;
-  if (version >= 2) {
+  if (kv_len.has_value() && kv_len->defined()) {
+    // per-sequence key counts (right-padded keys masked); non-causal, forward v3
+    VO_CHECK_INPUT((*kv_len));
+    TORCH_CHECK(kv_len->scalar_type() == torch::kInt32 && kv_len->numel() == B && !causal, "int32 [B] key counts");
+    rc = vo_fmha_fwd3_kvlen(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), split > 0 ? o2.data_ptr() : nullptr,
+                            (int)split, lse.data_ptr<float>(), kv_len->data_ptr<int>(), B, H, Sq, Skv, D, (float)scale,
+                            stream());
+  } else if (version >= 2) {
     auto fn = version == 3 ? vo_fmha_fwd3 : vo_fmha_fwd2;
     rc = fn(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), split > 0 ? o2.data_ptr() : nullptr, (int)split,
             lse.data_ptr<float>(), B, H, Sq, Skv, D, (float)scale, causal ? 1 : 0, stream());

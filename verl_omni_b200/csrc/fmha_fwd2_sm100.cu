@@ -181,7 +181,13 @@ struct Params {
   __nv_bfloat16* peer_o[8];
   __nv_bfloat16* peer_o2[8];
   int peer_sl, peer_si, peer_htot, peer_h0;
+  // optional per-sequence key count [B] (right-padded keys past it are masked: padded prompts)
+  const int* kv_len;
 };
+
+__device__ __forceinline__ int kv_limit(const Params& p, int bh) {
+  return p.kv_len ? min(p.Skv, max(0, __ldg(p.kv_len + bh / p.H))) : p.Skv;
+}
 
 // token-major output row of query q (head h, batch b): one buffer, or split at `split` into two
 __device__ __forceinline__ __nv_bfloat16* out_row(const Params& p, int b, int q, int h, int D) {
@@ -251,7 +257,7 @@ __device__ __forceinline__ void softmax_split2(const Params& p, uint32_t tmem, i
     }
     fence_after();
     const int kv0 = j * BKV + 64 * hf;
-    int lim = p.Skv - kv0;
+    int lim = kv_limit(p, bh) - kv0;
     if (p.causal) lim = min(lim, q - kv0 + 1);
     lim = max(0, min(64, lim));
     float mx = -INFINITY;
@@ -427,8 +433,8 @@ __global__ void __launch_bounds__(fwd_threads<SPLIT>(), 1)
   const int pr = p.npairs - 1 - (int)(blockIdx.x % p.npairs);
   const int bh = blockIdx.x / p.npairs;
   const int q0 = pr * 2 * BQ;
-  int kv_end = p.Skv;
-  if (p.causal) kv_end = min(p.Skv, q0 + 2 * BQ);
+  int kv_end = kv_limit(p, bh);
+  if (p.causal) kv_end = min(kv_end, q0 + 2 * BQ);
   const int nkv = (kv_end + BKV - 1) / BKV;
 
   if (threadIdx.x == 0) {
@@ -573,7 +579,7 @@ __global__ void __launch_bounds__(fwd_threads<SPLIT>(), 1)
       fence_after();
       const int kv0 = j * BKV;
       // keys [kv0, kv0 + lim) of this block are visible to this row
-      int lim = p.Skv - kv0;
+      int lim = kv_limit(p, bh) - kv0;
       if (p.causal) lim = min(lim, q - kv0 + 1);
       lim = max(0, min(BKV, lim));
       // pass 1: row max.  Chunks 2,3 first so chunks 0,1 stay in registers for pass 2.
@@ -750,7 +756,7 @@ struct PeerOut {
 
 static int fwd2_impl(const void* q, const void* k, const void* v, void* o, void* o2, int out_split, float* lse, int B,
                      int H, int Sq, int Skv, int D, float scale, int causal, cudaStream_t stream, int split,
-                     const PeerOut* peer = nullptr) {
+                     const PeerOut* peer = nullptr, const int* kv_len = nullptr) {
   if (D != 64 && D != 128) return -1;
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15)
     return -2;
@@ -775,6 +781,7 @@ static int fwd2_impl(const void* q, const void* k, const void* v, void* o, void*
     p.peer_htot = peer->htot;
     p.peer_h0 = peer->h0;
   }
+  p.kv_len = kv_len;
   p.Sq = Sq;
   p.Skv = Skv;
   p.H = H;
@@ -819,6 +826,14 @@ extern "C" int vo_fmha_fwd_peer(const void* q, const void* k, const void* v, voi
   vo_fmha2::PeerOut po{peer_o, peer_o2, nranks, sl, si, htot, h0};
   return vo_fmha2::fwd2_impl(q, k, v, nullptr, nullptr, 0, lse, B, H, Sq, Skv, D, scale, 0, stream, D == 64 ? 3 : 2,
                              &po);
+}
+
+// forward v3 with a per-sequence key count (int32 [B], device memory)
+extern "C" int vo_fmha_fwd3_kvlen(const void* q, const void* k, const void* v, void* o, void* o2, int out_split,
+                                  float* lse, const int* kv_len, int B, int H, int Sq, int Skv, int D, float scale,
+                                  cudaStream_t stream) {
+  return vo_fmha2::fwd2_impl(q, k, v, o, o2, out_split, lse, B, H, Sq, Skv, D, scale, 0, stream, D == 64 ? 3 : 2,
+                             nullptr, kv_len);
 }
 
 extern "C" int vo_fmha_fwd2_error(int reset) {

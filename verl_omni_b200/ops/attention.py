@@ -91,6 +91,11 @@ def attention_split(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, split: in
     if (kv_len is None and q.is_cuda and _native() and Dh in (64, 128) and q.dtype == torch.bfloat16
             and _FWD_VERSION >= 2 and 0 < split < S and split % 128 == 0):
         return _FMHASplit.apply(q, k, v, causal, scale, int(split))
+    if (kv_len is not None and not torch.is_grad_enabled() and not causal and q.is_cuda and _native()
+            and Dh in (64, 128) and q.dtype == torch.bfloat16 and 0 < split < S and split % 128 == 0):
+        # gradient-free forwards (rollout, log-prob recompute) of right-padded prompts: native key counts
+        out = ext().fmha_fwd(q, k, v, False, scale, 3, int(split), kv_len=kv_len.to(torch.int32).contiguous())
+        return out[0].view(B, split, H * Dh), out[2].view(B, S - split, H * Dh)
     o = attention(q, k, v, causal, scale, kv_len=kv_len)
     return o[:, :split].contiguous(), o[:, split:].contiguous()
 
