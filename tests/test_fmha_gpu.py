@@ -143,3 +143,27 @@ def test_split_attention_with_key_counts_matches_masked_sdpa(D):
         ref = ref.transpose(1, 2).reshape(B, S, H * D)
     torch.testing.assert_close(oi.float(), ref[:, :Si], rtol=2e-2, atol=2e-2)
     torch.testing.assert_close(ot.float(), ref[:, Si:], rtol=2e-2, atol=2e-2)
+
+
+def test_split_attention_with_key_counts_backward():
+    """Gradients of the key-count path equal masked SDPA's; padded keys get zero dK / dV."""
+    from verl_omni_b200.ops.attention import attention_split
+
+    torch.manual_seed(1)
+    B, H, Si, St, D = 2, 4, 256, 130, 64
+    S = Si + St
+    base = [torch.randn(B, H, S, D, device="cuda").bfloat16() for _ in range(3)]
+    kv_len = torch.tensor([S, Si + 40], dtype=torch.int32, device="cuda")
+    g_i, g_t = torch.randn(B, Si, H * D, device="cuda"), torch.randn(B, St, H * D, device="cuda")
+    q, k, v = (t.clone().requires_grad_() for t in base)
+    oi, ot = attention_split(q, k, v, Si, kv_len=kv_len)
+    ((oi.float() * g_i).sum() + (ot.float() * g_t).sum()).backward()
+    qr, kr, vr = (t.float().clone().requires_grad_() for t in base)
+    keep = torch.arange(S, device="cuda")[None, :] < kv_len[:, None].long()
+    ref = torch.nn.functional.scaled_dot_product_attention(qr, kr, vr, attn_mask=keep[:, None, None, :])
+    ref = ref.transpose(1, 2).reshape(B, S, H * D)
+    ((ref[:, :Si] * g_i).sum() + (ref[:, Si:] * g_t).sum()).backward()
+    rel = lambda a, b: float((a.float() - b).norm() / (b.norm() + 1e-6))  # noqa: E731
+    for a, b in ((q.grad, qr.grad), (k.grad, kr.grad), (v.grad, vr.grad)):
+        assert rel(a, b) < 3e-2
+    assert float(k.grad[1, :, Si + 40:].abs().max()) == 0.0 and float(v.grad[1, :, Si + 40:].abs().max()) == 0.0

@@ -91,7 +91,8 @@ void peer_adamw_bcast(std::vector<int64_t> flat_ptrs, int64_t lo, int64_t n, tor
                       int64_t step, double max_norm, torch::Tensor sq_norm);
 std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
                                     torch::Tensor lse, torch::Tensor dO, bool causal, double scale, int64_t version,
-                                    c10::optional<torch::Tensor> o2, c10::optional<torch::Tensor> dO2, int64_t split);
+                                    c10::optional<torch::Tensor> o2, c10::optional<torch::Tensor> dO2, int64_t split,
+                                    c10::optional<torch::Tensor> kv_len);
 }  // namespace vo
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -132,7 +133,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fmha_fwd_peer", &vo::fmha_fwd_peer, "Ulysses attention writing each output row to its owner rank");
   m.def("fmha_bwd", &vo::fmha_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
         py::arg("dO"), py::arg("causal"), py::arg("scale"), py::arg("version") = 1, py::arg("o2") = py::none(),
-        py::arg("dO2") = py::none(), py::arg("split") = 0);
+        py::arg("dO2") = py::none(), py::arg("split") = 0, py::arg("kv_len") = py::none());
   m.def("linear_bwd_prep", &vo::linear_bwd_prep);
   m.def("cfg_combine", &vo::cfg_combine);
   m.def("peer_push", &vo::peer_push);

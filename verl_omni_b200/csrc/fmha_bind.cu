@@ -18,7 +18,7 @@ extern "C" int vo_fmha_fwd_peer(const void* q, const void* k, const void* v, voi
 extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const void* o, const void* dO,
                            const void* o2, const void* dO2, int split, const float* lse, void* dq, void* dk, void* dv,
                            float* delta, float* dq_acc, int B, int H, int Sq, int Skv, int D, float scale, int causal,
-                           cudaStream_t stream, int version);
+                           cudaStream_t stream, int version, const int* kv_len);
 extern "C" int vo_fmha_bwd_error(int reset);
 
 namespace vo {
@@ -102,7 +102,8 @@ int64_t fmha_error(bool reset) {
 // two halves (o, dO: rows [0, split); o2, dO2: rows [split, Sq)); split must be a multiple of 128.
 std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
                                     torch::Tensor lse, torch::Tensor dO, bool causal, double scale, int64_t version,
-                                    c10::optional<torch::Tensor> o2, c10::optional<torch::Tensor> dO2, int64_t split) {
+                                    c10::optional<torch::Tensor> o2, c10::optional<torch::Tensor> dO2, int64_t split,
+                                    c10::optional<torch::Tensor> kv_len) {
   VO_CHECK_INPUT(q);
   VO_CHECK_INPUT(k);
   VO_CHECK_INPUT(v);
@@ -122,6 +123,12 @@ std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Ten
     po2 = o2->data_ptr();
     pdo2 = dO2->data_ptr();
   }
+  const int* kvp = nullptr;
+  if (kv_len.has_value() && kv_len->defined()) {
+    VO_CHECK_INPUT((*kv_len));
+    TORCH_CHECK(kv_len->scalar_type() == torch::kInt32 && kv_len->numel() == B && !causal, "int32 [B] key counts");
+    kvp = kv_len->data_ptr<int>();
+  }
   auto dq = torch::empty_like(q);
   auto dk = torch::empty_like(k);
   auto dv = torch::empty_like(v);
@@ -131,7 +138,7 @@ std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Ten
   int rc = vo_fmha_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dO.data_ptr(), po2, pdo2, (int)split,
                        lse.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), delta.data_ptr<float>(),
                        dq_acc.data_ptr<float>(), B, H, Sq, Skv, D, (float)scale, causal ? 1 : 0, stream(),
-                       (int)version);
+                       (int)version, kvp);
   TORCH_CHECK(rc == 0, "tcgen05 FMHA backward launch failed: code ", rc);
   count_launch(3);
   return {dq, dk, dv};

@@ -126,6 +126,7 @@ __device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.syn
 
 struct Params {
   int Sq, Skv, H, nkv_tiles, causal;
+  const int* kv_len;  // optional per-sequence key count [B]: keys at or past it get no attention
   float scale, scale_log2;
   const float* lse;    // [BH, Sq]
   const float* delta;  // [BH, Sq]
@@ -323,7 +324,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int j = 0; j < 32; ++j) {
           const int qc = c * 32 + j;
           const int q = q0 + qc;
-          const bool valid = kv < p.Skv && (!p.causal || kv <= q);
+          const bool valid = kv < (p.kv_len ? min(p.Skv, __ldg(p.kv_len + bh / p.H)) : p.Skv) &&
+                             (!p.causal || kv <= q);
           const float pv = valid ? ex2(s[j] * p.scale_log2 - lse_s[qc]) : 0.f;
           s[j] = pv;
           dp[j] = pv * (dp[j] - del_s[qc]);
@@ -657,7 +659,7 @@ __global__ void __launch_bounds__(512, 1)
       }
       fence_after();
       // visible query columns of this key row within the warpgroup's 64: [qlo, qhi)
-      int qhi = kv < p.Skv ? min(64, p.Sq - q0) : 0;
+      int qhi = kv < (p.kv_len ? min(p.Skv, __ldg(p.kv_len + bh / p.H)) : p.Skv) ? min(64, p.Sq - q0) : 0;
       int qlo = p.causal ? max(0, kv - q0) : 0;
       qhi = max(qhi, 0);
       if (qlo > qhi) qlo = qhi;
@@ -929,7 +931,7 @@ static int launch2(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
 extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const void* o, const void* dO,
                            const void* o2, const void* dO2, int split, const float* lse, void* dq, void* dk, void* dv,
                            float* delta, float* dq_acc, int B, int H, int Sq, int Skv, int D, float scale, int causal,
-                           cudaStream_t stream, int version) {
+                           cudaStream_t stream, int version, const int* kv_len) {
   using namespace vo_fbwd;
   if (D != 64 && D != 128) return -1;
   const int64_t rows = (int64_t)B * Sq * H;
@@ -952,6 +954,7 @@ extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const vo
   if (!r) r = split > 0 ? map4_tok(&mdo2, dO2, B, Sq - split, H, D) : map4_tok(&mdo2, dO, B, Sq, H, D);
   if (r) return r;
   Params p;
+  p.kv_len = kv_len;
   p.Sq = Sq;
   p.Skv = Skv;
   p.H = H;

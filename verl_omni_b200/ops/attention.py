@@ -59,9 +59,13 @@ class _FMHASplit(torch.autograd.Function):
     """Joint attention whose query rows [0, split) and [split, S) land in two separate outputs."""
 
     @staticmethod
-    def forward(ctx, q, k, v, causal, scale, split):
-        o_a, lse, o_b = ext().fmha_fwd(q, k, v, causal, scale, _FWD_VERSION, split)
+    def forward(ctx, q, k, v, causal, scale, split, kv_len=None):
+        if kv_len is not None:  # right-padded keys: per-sequence key counts (forward v3)
+            o_a, lse, o_b = ext().fmha_fwd(q, k, v, causal, scale, 3, split, kv_len=kv_len)
+        else:
+            o_a, lse, o_b = ext().fmha_fwd(q, k, v, causal, scale, _FWD_VERSION, split)
         ctx.save_for_backward(q, k, v, o_a, o_b, lse)
+        ctx.kv_len = kv_len
         ctx.meta = (causal, scale, split)
         B, _, H, D = o_a.shape
         return o_a.view(B, split, H * D), o_b.view(B, -1, H * D)
@@ -73,8 +77,8 @@ class _FMHASplit(torch.autograd.Function):
         do_a = torch.zeros_like(o_a) if do_a is None else do_a.contiguous().view_as(o_a)
         do_b = torch.zeros_like(o_b) if do_b is None else do_b.contiguous().view_as(o_b)
         dq, dk, dv = ext().fmha_bwd(q, k, v, o_a, lse, do_a, causal, scale, _BWD_VERSION, o2=o_b, dO2=do_b,
-                                    split=split)
-        return dq, dk, dv, None, None, None
+                                    split=split, kv_len=ctx.kv_len)
+        return dq, dk, dv, None, None, None, None
 
 
 def attention_split(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, split: int, causal: bool = False,
@@ -91,11 +95,10 @@ def attention_split(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, split: in
     if (kv_len is None and q.is_cuda and _native() and Dh in (64, 128) and q.dtype == torch.bfloat16
             and _FWD_VERSION >= 2 and 0 < split < S and split % 128 == 0):
         return _FMHASplit.apply(q, k, v, causal, scale, int(split))
-    if (kv_len is not None and not torch.is_grad_enabled() and not causal and q.is_cuda and _native()
-            and Dh in (64, 128) and q.dtype == torch.bfloat16 and 0 < split < S and split % 128 == 0):
-        # gradient-free forwards (rollout, log-prob recompute) of right-padded prompts: native key counts
-        out = ext().fmha_fwd(q, k, v, False, scale, 3, int(split), kv_len=kv_len.to(torch.int32).contiguous())
-        return out[0].view(B, split, H * Dh), out[2].view(B, S - split, H * Dh)
+    if (kv_len is not None and not causal and q.is_cuda and _native() and Dh in (64, 128)
+            and q.dtype == torch.bfloat16 and _FWD_VERSION >= 2 and 0 < split < S and split % 128 == 0):
+        # right-padded prompts: native forward / backward with per-sequence key counts
+        return _FMHASplit.apply(q, k, v, False, scale, int(split), kv_len.to(torch.int32).contiguous())
     o = attention(q, k, v, causal, scale, kv_len=kv_len)
     return o[:, :split].contiguous(), o[:, split:].contiguous()
 
