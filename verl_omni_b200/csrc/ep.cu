@@ -1,0 +1,65 @@
+// Expert-parallel token exchange over peer memory: row copies into other GPUs' buffers.
+//
+// The dispatch of a mixture-of-experts layer sends every routed (token, slot) row to the rank that owns its
+// expert, straight into that rank's expert-sorted, 128-row-padded input buffer (the layout of the
+// expert-grouped GEMM); the combine sends every expert output row back to the slot of the rank that routed
+// it.  Both are this one kernel: row i of `src` (row src_idx[i]) is stored at row dst_row[i] of the buffer
+// of rank dst_rank[i] (a peer pointer of a symmetric allocation), one warp per row, 16-byte vectors over
+// NVLink.  The grouped GEMMs run between the exchanges on each owner's own memory.
+#include "common.cuh"
+
+namespace vo {
+namespace {
+
+constexpr int kMaxRanks = 8;
+
+struct PeerTable {
+  __nv_bfloat16* ptr[kMaxRanks];
+};
+
+__global__ void peer_row_copy_kernel(const __nv_bfloat16* __restrict__ src, const int64_t* __restrict__ src_idx,
+                                     const int* __restrict__ dst_rank, const int64_t* __restrict__ dst_row,
+                                     PeerTable peers, int64_t n, int vecs) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t i = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < n; i += warps) {
+    const bf16x8* s = reinterpret_cast<const bf16x8*>(src) + src_idx[i] * vecs;
+    bf16x8* d = reinterpret_cast<bf16x8*>(peers.ptr[dst_rank[i]]) + dst_row[i] * vecs;
+    for (int v = lane; v < vecs; v += 32) d[v] = s[v];
+  }
+}
+
+}  // namespace
+
+// src [N, D] bf16; src_idx int64 [n]; dst_rank int32 [n] (< number of peers); dst_row int64 [n];
+// peers: data pointers of each rank's [rows, D] bf16 buffer (this rank's own included).
+void peer_row_copy(torch::Tensor src, torch::Tensor src_idx, torch::Tensor dst_rank, torch::Tensor dst_row,
+                   std::vector<int64_t> peers) {
+  VO_CHECK_INPUT(src);
+  VO_CHECK_INPUT(src_idx);
+  VO_CHECK_INPUT(dst_rank);
+  VO_CHECK_INPUT(dst_row);
+  TORCH_CHECK(src.scalar_type() == torch::kBFloat16 && src.dim() == 2 && src.size(1) % 8 == 0, "bf16 [N, D % 8] rows");
+  TORCH_CHECK(src_idx.scalar_type() == torch::kInt64 && dst_row.scalar_type() == torch::kInt64 &&
+                  dst_rank.scalar_type() == torch::kInt32 && src_idx.numel() == dst_row.numel() &&
+                  dst_rank.numel() == dst_row.numel(),
+              "row maps: int64 source rows, int32 ranks, int64 destination rows of one length");
+  TORCH_CHECK(!peers.empty() && peers.size() <= (size_t)kMaxRanks, "1..8 destination buffers");
+  const int64_t n = src_idx.numel();
+  if (n == 0) return;
+  c10::cuda::CUDAGuard g(src.device());
+  PeerTable t{};
+  for (size_t i = 0; i < peers.size(); ++i) {
+    TORCH_CHECK(peers[i] % 16 == 0, "destination buffers must be 16-byte aligned");
+    t.ptr[i] = reinterpret_cast<__nv_bfloat16*>(peers[i]);
+  }
+  const int vecs = (int)(src.size(1) / 8);
+  const int grid = (int)std::min<int64_t>((n + 7) / 8, 8LL * num_sms());
+  peer_row_copy_kernel<<<grid, 256, 0, stream()>>>(reinterpret_cast<const __nv_bfloat16*>(src.data_ptr<at::BFloat16>()),
+                                                  src_idx.data_ptr<int64_t>(), dst_rank.data_ptr<int>(),
+                                                  dst_row.data_ptr<int64_t>(), t, n, vecs);
+  count_launch();
+  VO_CUDA_OK(cudaGetLastError());
+}
+
+}  // namespace vo
