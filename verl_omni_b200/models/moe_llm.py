@@ -164,7 +164,9 @@ class MoEBlock(nn.Module):
         gates, idx = torch.topk(probs, cfg.top_k, dim=-1)
         gates = (gates / gates.sum(-1, keepdim=True)).to(x.dtype)
         self.last_router = (probs, idx)
-        if ep is not None:
+        if ep is not None and hasattr(ep, "fused_ok") and ep.fused_ok(h, self.w_gate_up, self.w_down):
+            out = ep.dispatch_combine_fused(h, idx, gates, self.w_gate_up, self.w_down)  # peer-memory exchange
+        elif ep is not None:
             out = ep.dispatch_combine(h, idx, gates, self.expert_ffn)
         else:
             out = grouped_expert_ffn(h, idx, gates, self.w_gate_up, self.w_down)

@@ -37,9 +37,10 @@ class OmniGRPOTrainer:
         self.prompt_text, self.audio_tokens, self.image_tokens = prompt_text, audio_tokens, image_tokens
         self.model = MoELLM(cfg).to(device)
         if ep_group is not None and D.world_size(ep_group) > 1:
-            from verl_omni_b200.parallel.expert_parallel import ExpertParallel
+            from verl_omni_b200.parallel.expert_parallel import FusedExpertParallel
 
-            self.model.ep = ExpertParallel(cfg.experts, ep_group)
+            # peer-memory dispatch / combine where it applies (CUDA, one node), NCCL all-to-all otherwise
+            self.model.ep = FusedExpertParallel(cfg.experts, ep_group)
         # tensor + sequence parallelism (Megatron layout): ranks of a TP group share their samples and split each
         # sequence and the attention heads; weights stay replicated, so every rank's gradient is its share and
         # the loss is scaled by tp for the world-averaged gradient (groups of consecutive ranks)
