@@ -43,6 +43,9 @@ def _run(rank, world):
     rel = lambda a, b: float((a - b).norm() / (b.norm() + 1e-6))  # noqa: E731
     for n, gs in gsp.items():
         dist.all_reduce(gs)
+        if n not in g32:  # discarded last-block text outputs: the grouped GEMM reports zero gradients
+            assert float(gs.abs().max()) == 0.0, n
+            continue
         e16, esp = rel(g16[n], g32[n]), rel(gs, g32[n])
         # the SP gradient is as close to the fp32 oracle as the one-rank bf16 gradient is
         assert esp <= max(5e-2, 1.5 * e16 + 2e-2), (n, esp, e16)
