@@ -65,6 +65,7 @@ def _fused(rank, world):
     from verl_omni_b200.models.qwen_image import QwenImageConfig, QwenImageDiT
     from verl_omni_b200.parallel import ulysses_fused as UF
 
+    torch.manual_seed(0)  # every rank builds the same weights
     g = torch.Generator().manual_seed(1)
     cases = [
         ("qwen", QwenImageDiT(QwenImageConfig(in_channels=4, hidden=256, heads=4, depth=2, joint_attention_dim=64,
@@ -79,7 +80,6 @@ def _fused(rank, world):
          (torch.randn(2, 4, 4, 16, 16, generator=g), torch.tensor([900.0, 300.0]), torch.randn(2, 64, 64, generator=g))),
     ]
     for name, m, inputs in cases:
-        torch.manual_seed(0)
         m = m.cuda().bfloat16().eval()
         inputs = [t.cuda() for t in inputs]
         with torch.no_grad():

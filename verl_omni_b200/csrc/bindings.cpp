@@ -57,7 +57,7 @@ void gemm_tp(c10::optional<torch::Tensor> a, c10::optional<torch::Tensor> b, int
              int64_t lda, int64_t ldb, int64_t a_mn, int64_t b_mn, c10::optional<torch::Tensor> out,
              c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> bias, int64_t gather,
              std::vector<int64_t> gather_ptrs, int64_t gather_rows, std::vector<int64_t> red_ptrs,
-             int64_t red_rows);
+             int64_t red_rows, int64_t red_slot);
 torch::Tensor moe_gemm_dgrad(torch::Tensor dy, torch::Tensor w, torch::Tensor tile_expert);
 void moe_gemm_wgrad(torch::Tensor dy, torch::Tensor x, torch::Tensor seg, torch::Tensor out, bool accumulate);
 std::vector<torch::Tensor> gemm_dgrad_pair(torch::Tensor dy0, torch::Tensor w0, torch::Tensor dy1, torch::Tensor w1);
@@ -68,6 +68,7 @@ int64_t gemm_error(bool reset);
 std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal, double scale,
                                     int64_t version, int64_t split, c10::optional<torch::Tensor> kv_len);
 int64_t fmha_error(bool reset);
+torch::Tensor slot_sum(torch::Tensor slots, int64_t W, c10::optional<torch::Tensor> bias);
 void peer_row_copy(torch::Tensor src, torch::Tensor src_idx, torch::Tensor dst_rank, torch::Tensor dst_row,
                    std::vector<int64_t> peers);
 torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor lens,
@@ -120,7 +121,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_wgrad", &vo::gemm_wgrad);
   m.def("gemm_fwd_pair", &vo::gemm_fwd_pair, "two linear forwards in one persistent GEMM launch");
   m.def("gemm_dgrad_pair", &vo::gemm_dgrad_pair);
-  m.def("gemm_tp", &vo::gemm_tp, "GEMM with a tensor-parallel operand gather and / or peer reduce-scatter");
+  m.def("gemm_tp", &vo::gemm_tp, "GEMM with a tensor-parallel operand gather and / or peer reduce-scatter",
+        py::arg("a"), py::arg("b"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("lda"), py::arg("ldb"),
+        py::arg("a_mn"), py::arg("b_mn"), py::arg("out"), py::arg("out_f32"), py::arg("bias"), py::arg("gather"),
+        py::arg("gather_ptrs"), py::arg("gather_rows"), py::arg("red_ptrs"), py::arg("red_rows"),
+        py::arg("red_slot") = -1);
   m.def("moe_gemm_fwd", &vo::moe_gemm_fwd, "expert-grouped GEMM over expert-sorted, 128-padded rows");
   m.def("moe_gemm_dgrad", &vo::moe_gemm_dgrad);
   m.def("moe_gemm_wgrad", &vo::moe_gemm_wgrad);
@@ -131,6 +136,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fmha_fwd", &vo::fmha_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("causal"), py::arg("scale"),
         py::arg("version") = 2, py::arg("split") = 0, py::arg("kv_len") = py::none());
   m.def("fmha_error", &vo::fmha_error);
+  m.def("slot_sum", &vo::slot_sum, "sum of W bf16 partial-sum slots (+ bias), fp32 accumulation",
+        py::arg("slots"), py::arg("W"), py::arg("bias") = py::none());
   m.def("peer_row_copy", &vo::peer_row_copy, "row copies into peer GPUs' buffers (expert-parallel exchange)");
   m.def("decode_attention", &vo::decode_attention, "grouped-query decode attention over a KV cache");
   m.def("fmha_fwd_peer", &vo::fmha_fwd_peer, "Ulysses attention writing each output row to its owner rank");

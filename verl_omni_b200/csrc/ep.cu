@@ -29,7 +29,55 @@ __global__ void peer_row_copy_kernel(const __nv_bfloat16* __restrict__ src, cons
   }
 }
 
+// out[r, :] = sum over s < W of slots[s * R + r, :] (+ bias), fp32 accumulation, 8 columns per thread.
+__global__ void slot_sum_kernel(const bf16x8* __restrict__ slots, const bf16x8* __restrict__ bias,
+                                bf16x8* __restrict__ out, int64_t R, int vecs, int W) {
+  const int64_t n = R * vecs;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float acc[8], f[8];
+    if (bias) {
+      unpack8(bias[i % vecs], acc);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    }
+    for (int s = 0; s < W; ++s) {
+      unpack8(slots[(int64_t)s * n + i], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += f[j];
+    }
+    out[i] = pack8(acc);
+  }
+}
+
 }  // namespace
+
+// slots: bf16 [W * R, N] (W partial-sum slots of R rows, this rank's own buffer) -> [R, N] bf16 sum (+ bias).
+torch::Tensor slot_sum(torch::Tensor slots, int64_t W, c10::optional<torch::Tensor> bias) {
+  VO_CHECK_INPUT(slots);
+  TORCH_CHECK(slots.scalar_type() == torch::kBFloat16 && slots.dim() == 2 && slots.size(1) % 8 == 0 && W >= 1 &&
+                  slots.size(0) % W == 0,
+              "bf16 [W * R, N % 8] slots");
+  const int64_t R = slots.size(0) / W, N = slots.size(1);
+  const __nv_bfloat16* bp = nullptr;
+  if (bias.has_value() && bias->defined()) {
+    VO_CHECK_INPUT(*bias);
+    TORCH_CHECK(bias->scalar_type() == torch::kBFloat16 && bias->numel() == N, "bf16 [N] bias");
+    bp = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr<at::BFloat16>());
+  }
+  auto out = torch::empty({R, N}, slots.options());
+  if (R == 0) return out;
+  c10::cuda::CUDAGuard g(slots.device());
+  const int vecs = (int)(N / 8);
+  const int64_t n = R * vecs;
+  const int grid = (int)std::min<int64_t>((n + 255) / 256, 8LL * num_sms());
+  slot_sum_kernel<<<grid, 256, 0, stream()>>>(reinterpret_cast<const bf16x8*>(slots.data_ptr<at::BFloat16>()),
+                                              reinterpret_cast<const bf16x8*>(bp),
+                                              reinterpret_cast<bf16x8*>(out.data_ptr<at::BFloat16>()), R, vecs, (int)W);
+  count_launch();
+  VO_CUDA_OK(cudaGetLastError());
+  return out;
+}
 
 // src [N, D] bf16; src_idx int64 [n]; dst_rank int32 [n] (< number of peers); dst_row int64 [n];
 // peers: data pointers of each rank's [rows, D] bf16 buffer (this rank's own included).

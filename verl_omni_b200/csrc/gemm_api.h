@@ -39,10 +39,14 @@ struct EpiParams {
   int S;  // rows per sample (GATE_RES)
   int ldc;
   ScatterParams sc;  // EPI_SCATTER
-  // EPI_PEER_RED: output row m is owned by rank m / red_rows and added (fp32, system-scope vector atomics
-  // over NVLink) at row m % red_rows of red_peers[owner] ([red_rows, ldc] fp32 each).
+  // EPI_PEER_RED: output row m is owned by rank m / red_rows.  red_store 0: the row is added (fp32,
+  // system-scope vector atomics over NVLink) at row m % red_rows of red_peers[owner] ([red_rows, ldc] fp32
+  // each).  red_store 1: the row is stored in bf16 at row red_slot_off + m % red_rows of red_peers[owner]
+  // (bf16 buffers holding one [red_rows, ldc] slot per source rank; the owner sums the slots afterwards).
   float* red_peers[kMaxPeers];
   int red_rows;
+  int red_store;
+  int red_slot_off;
 };
 
 // One GEMM of a grouped launch: C = A B^T (+ A2 B2^T), operand conventions as vo_gemm_launch_ext.

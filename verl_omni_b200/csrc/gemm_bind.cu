@@ -288,13 +288,14 @@ void gemm_wgrad_pair(torch::Tensor dy0, torch::Tensor x0, torch::Tensor out0, to
 // be gathered from the ranks of a tensor-parallel group (gather 1: rows of a K-major A; 2: reduction rows
 // of an MN-major A; 3: reduction rows of an MN-major B -- gather_rows rows per rank, read with plain TMA
 // loads from the peers' buffers) and the output may be added into the owning ranks' fp32 buffers
-// (red_ptrs, red_rows output rows per rank) instead of stored locally.
+// (red_ptrs, red_rows output rows per rank) instead of stored locally; with red_slot >= 0 the rows are
+// stored in bf16 at slot red_slot ([red_rows, N] each) of the owners' buffers, for the owner to sum.
 // out: bf16 [M, N] (ignored with red_ptrs); out_f32: fp32 [M, N] accumulated (weight gradients).
 void gemm_tp(c10::optional<torch::Tensor> a, c10::optional<torch::Tensor> b, int64_t M, int64_t N, int64_t K,
              int64_t lda, int64_t ldb, int64_t a_mn, int64_t b_mn, c10::optional<torch::Tensor> out,
              c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> bias, int64_t gather,
              std::vector<int64_t> gather_ptrs, int64_t gather_rows, std::vector<int64_t> red_ptrs,
-             int64_t red_rows) {
+             int64_t red_rows, int64_t red_slot) {
   const torch::Tensor& dev_t = a.has_value() && a->defined() ? *a : *b;
   c10::cuda::CUDAGuard g(dev_t.device());
   vo_gemm::GemmDesc d{};
@@ -320,6 +321,8 @@ void gemm_tp(c10::optional<torch::Tensor> a, c10::optional<torch::Tensor> b, int
   if (!red_ptrs.empty()) {
     d.ep.epi = vo_gemm::EPI_PEER_RED;
     d.ep.red_rows = (int)red_rows;
+    d.ep.red_store = red_slot >= 0;  // bf16 slot stores (slot red_slot) instead of fp32 atomics
+    d.ep.red_slot_off = red_slot >= 0 ? (int)(red_slot * red_rows) : 0;
     d.ep.ldc = (int)N;
     for (size_t i = 0; i < red_ptrs.size(); ++i) d.ep.red_peers[i] = reinterpret_cast<float*>(red_ptrs[i]);
     TORCH_CHECK((int64_t)red_ptrs.size() * red_rows >= M, "owners must cover every output row");

@@ -357,6 +357,28 @@ __device__ __forceinline__ void epilogue_red(uint32_t tacc, int row0, int col_ba
   const int row = row0 + lane;
   const bool row_ok = row < sh.M;
   const int owner = row_ok ? row / ep.red_rows : 0;
+  if (ep.red_store) {  // bf16 partial rows into this rank's slot of the owner's buffer: plain 16-byte stores
+    __nv_bfloat16* dst =
+        row_ok ? reinterpret_cast<__nv_bfloat16*>(peers[owner]) +
+                     (int64_t)(ep.red_slot_off + row - owner * ep.red_rows) * ep.ldc
+               : nullptr;
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tc_ld_32x32b_x32(tacc + c * 32, r);
+      const int col0 = col_base + c * 32;
+      if (col0 >= sh.N || !row_ok) continue;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        uint4 pk;
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          h[q] = __floats2bfloat162_rn(__uint_as_float(r[8 * u + 2 * q]), __uint_as_float(r[8 * u + 2 * q + 1]));
+        *reinterpret_cast<uint4*>(dst + col0 + 8 * u) = pk;
+      }
+    }
+    return;
+  }
   float* base = row_ok ? peers[owner] + (int64_t)(row - owner * ep.red_rows) * ep.ldc : nullptr;
   for (int c = 0; c < BN / 32; ++c) {
     uint32_t r[32];
@@ -919,7 +941,9 @@ static int build_prob(const GemmDesc& d, bool two_sm, Prob* P) {
   int r;
   // epilogue outputs go out through TMA: 16-byte aligned bases and row strides
   if (ep.epi == EPI_PEER_RED) {
-    if (ep.red_rows <= 0 || d.N % 32 || (ep.ldc * 4) % 16 || ep.ldc < d.N) return -10;
+    if (ep.red_rows <= 0 || d.N % 32 || (ep.ldc * (ep.red_store ? 2 : 4)) % 16 || ep.ldc < d.N ||
+        ep.red_slot_off < 0)
+      return -10;
     const int owners = (d.M + ep.red_rows - 1) / ep.red_rows;
     if (owners > kMaxPeers) return -10;
     for (int i = 0; i < owners; ++i)

@@ -11,10 +11,11 @@ Fused path (CUDA, NCCL group on one node, symmetric memory):
 * all-gather -> GEMM: each rank publishes its token shard in a symmetric buffer; the GEMM's TMA producer
   reads every 128-row A tile straight from the owning peer's buffer (``GemmDesc::gather`` 1).  The weight
   gradient of the same layer re-reads the gathered activations along the reduction (``gather`` 3);
-* GEMM -> reduce-scatter: the epilogue adds each output row into the owner's fp32 buffer with system-scope
-  vector atomics over NVLink (``EPI_PEER_RED``); the owner converts its rows to bf16 after a one-element
-  all-reduce orders the ranks.  The dgrad of a column-parallel layer uses the same epilogue, and the
-  dgrad / wgrad of a row-parallel layer gather the output gradient (``gather`` 1 / 2).
+* GEMM -> reduce-scatter: the epilogue stores each output row, in bf16 with plain 16-byte stores over
+  NVLink, into this rank's slot of the owner's buffer (``EPI_PEER_RED`` slot mode); after a one-element
+  all-reduce orders the ranks the owner sums its slots (``slot_sum``, bias fused).  The dgrad of a
+  column-parallel layer uses the same epilogue, and the dgrad / wgrad of a row-parallel layer gather the
+  output gradient (``gather`` 1 / 2).
 
 Reference path (CPU / gloo, or when the fused path does not apply): all-gather and reduce-scatter as
 collectives around plain GEMMs -- numerically the oracle of the fused path.
@@ -71,7 +72,7 @@ class _Pair:
         from verl_omni_b200.parallel.symm_mem import SymmetricBuffer
 
         self.bufs = [SymmetricBuffer(numel, dtype, device, group) for _ in range(2)]
-        for b in self.bufs:  # reduce targets start from zero (cudaMalloc does not clear)
+        for b in self.bufs:  # defined contents before first use (cudaMalloc does not clear)
             b.tensor.zero_()
         torch.cuda.synchronize(device)
         D.barrier(group)
@@ -140,17 +141,17 @@ def _gemm_ag(ctx: TPContext, xb, S_l: int, K: int, w: torch.Tensor, bias) -> tor
     return y
 
 
-def _reduce_to_owner(ctx: TPContext, key: str, S: int, N: int, launch) -> torch.Tensor:
-    """Runs ``launch(red_ptrs, rows)`` (a GEMM whose epilogue adds into the owners' fp32 buffers), orders
-    the ranks, returns this rank's rows in bf16 and clears its buffer for the next use."""
+def _reduce_to_owner(ctx: TPContext, key: str, S: int, N: int, launch, bias=None) -> torch.Tensor:
+    """Runs ``launch(red_ptrs, rows, slot)`` (a GEMM whose epilogue stores every output row, in bf16, into
+    this rank's slot of the owning rank's buffer ``[world, S / world, N]``), orders the ranks and returns
+    the sum of this rank's slots (+ ``bias``).  Every slot is rewritten in full by each use, so the buffers
+    need no clearing; the partial sums are rounded to bf16 before the fp32 sum, as a bf16 reduce-scatter
+    rounds them."""
     S_l = S // ctx.world
-    acc = ctx.buf(key, S_l * N, torch.float32, torch.device("cuda", torch.cuda.current_device()))
-    launch(acc.peer_ptrs, S_l)
-    ctx.barrier(acc.tensor.device)
-    t = acc.tensor.view(S_l, N)
-    out = t.to(torch.bfloat16)
-    t.zero_()
-    return out
+    slots = ctx.buf(key, ctx.world * S_l * N, torch.bfloat16, torch.device("cuda", torch.cuda.current_device()))
+    launch(slots.peer_ptrs, S_l, ctx.rank)
+    ctx.barrier(slots.tensor.device)
+    return _ext().slot_sum(slots.tensor.view(ctx.world * S_l, N), ctx.world, bias)
 
 
 # ---------------------------------------------------------------- autograd functions
@@ -182,8 +183,8 @@ class _ColumnParallel(torch.autograd.Function):
         gb = dy.float().sum(0).to(w.dtype) if ctx.has_b else None
         if ctx.fused:
             # dX: partial over this rank's output columns, reduce-scattered by the dgrad epilogue
-            dx = _reduce_to_owner(tp, "col_dx", S, K, lambda red, rows: _ext().gemm_tp(
-                dy, w, S, K, N_l, N_l, K, 0, 1, None, None, None, 0, [], 0, red, rows))
+            dx = _reduce_to_owner(tp, "col_dx", S, K, lambda red, rows, slot: _ext().gemm_tp(
+                dy, w, S, K, N_l, N_l, K, 0, 1, None, None, None, 0, [], 0, red, rows, slot))
             # dW = dY^T gather(x): the reduction over tokens reads every peer's x shard again
             xb = tp.publish("col_x", x)
             gw = torch.zeros(N_l, K, device=w.device, dtype=torch.float32)
@@ -203,14 +204,14 @@ class _RowParallel(torch.autograd.Function):
         S, K_l = x.shape
         N = w.shape[0]
         if _fused_ok(tp, x, S // max(tp.world, 1), K_l, N) and S % tp.world == 0:
-            y = _reduce_to_owner(tp, "row_y", S, N, lambda red, rows: _ext().gemm_tp(
-                x, w, S, N, K_l, K_l, K_l, 0, 0, None, None, None, 0, [], 0, red, rows))
+            y = _reduce_to_owner(tp, "row_y", S, N, lambda red, rows, slot: _ext().gemm_tp(
+                x, w, S, N, K_l, K_l, K_l, 0, 0, None, None, None, 0, [], 0, red, rows, slot), bias=b)
             ctx.fused = True
         else:
             y = reduce_scatter_seq(torch.nn.functional.linear(x, w), tp.group)
+            if b is not None:
+                y = y + b
             ctx.fused = False
-        if b is not None:
-            y = y + b
         ctx.save_for_backward(x, w)
         ctx.has_b = b is not None
         return y
