@@ -285,3 +285,22 @@ def test_qwen_image_gpu_matches_cpu():
     torch.testing.assert_close(out_m.cpu(), ref_m, rtol=5e-2, atol=5e-2)
     out_m.square().mean().backward()
     assert all(torch.isfinite(p.grad).all() for p in mg.parameters() if p.grad is not None)
+
+
+def test_wan_dit_gpu_matches_cpu():
+    """Wan-style DiT (self attention, then cross attention whose q-only and k/v-only projections go through
+    the q/k-norm split with absent destinations) in bf16 on the native kernels against the fp32 CPU model,
+    then a backward pass."""
+    from verl_omni_b200.models.dit import DiT, DiTConfig
+
+    torch.manual_seed(0)
+    m = DiT(DiTConfig(in_channels=4, out_channels=4, hidden=256, heads=2, depth=2, ffn=512, text_dim=64))
+    x = torch.randn(2, 4, 4, 16, 16)
+    t = torch.tensor([900.0, 300.0])
+    c = torch.randn(2, 64, 64)
+    ref = m(x, t, c)
+    mg = m.cuda().bfloat16()
+    out = mg(x.cuda(), t.cuda(), c.cuda())
+    torch.testing.assert_close(out.float().cpu(), ref, rtol=5e-2, atol=5e-2)
+    out.float().square().mean().backward()
+    assert all(torch.isfinite(p.grad).all() for p in mg.parameters() if p.grad is not None)

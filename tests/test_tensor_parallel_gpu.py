@@ -1,5 +1,6 @@
-"""Tensor + sequence parallel linears on 2 B200s: the fused path (all-gather inside the GEMM's TMA
-producer, reduce-scatter inside its epilogue) equals the NCCL collective path."""
+"""Tensor + sequence parallel linears on 2 B200s: both fused paths (all-gather by copy-engine pulls
+overlapped with the GEMMs, or inside the GEMM's TMA producer; reduce-scatter inside the GEMM epilogue)
+equal the NCCL collective path."""
 
 import pytest
 import torch
@@ -27,7 +28,7 @@ def _run(rank, world):
     gy = torch.randn(S, Dm, generator=g).cuda()
     tp = TPContext(dist.group.WORLD)
     res = {}
-    for fused in ("0", "1"):
+    for fused in ("0", "1", "kernel"):
         os.environ["VO_TP_FUSED"] = fused
         xs = x[rank * sl:(rank + 1) * sl].clone().requires_grad_()
         w1s = w1[rank * hl:(rank + 1) * hl].clone().requires_grad_()
@@ -39,8 +40,9 @@ def _run(rank, world):
         (y.float() * gy[rank * sl:(rank + 1) * sl]).sum().backward()
         res[fused] = [t.float().clone() for t in (y, xs.grad, w1s.grad, b1s.grad, w2s.grad)]
     rel = lambda a, b: float((a - b).norm() / (b.norm() + 1e-6))  # noqa: E731
-    for name, a, b in zip(("y", "dx", "dw1", "db1", "dw2"), res["1"], res["0"]):
-        assert rel(a, b) < 2e-2, (name, rel(a, b))
+    for mode in ("1", "kernel"):
+        for name, a, b in zip(("y", "dx", "dw1", "db1", "dw2"), res[mode], res["0"]):
+            assert rel(a, b) < 2e-2, (mode, name, rel(a, b))
     from verl_omni_b200.ops._ext import ext
 
     assert ext().gemm_error(True) == 0

@@ -25,12 +25,14 @@ std::vector<torch::Tensor> adaln_ln_fwd(torch::Tensor x, c10::optional<torch::Te
                                         c10::optional<torch::Tensor> bias, int64_t S, double eps);
 std::vector<torch::Tensor> adaln_ln_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor mean, torch::Tensor rstd,
                                         torch::Tensor mod, int64_t shift_off, int64_t scale_off, int64_t S);
-std::vector<torch::Tensor> qk_rmsnorm_fwd(torch::Tensor qkv, torch::Tensor wq, torch::Tensor wk, torch::Tensor q,
-                                          torch::Tensor k, torch::Tensor v, int64_t S_seg, int64_t seg_off,
+std::vector<torch::Tensor> qk_rmsnorm_fwd(torch::Tensor qkv, torch::Tensor wq, torch::Tensor wk,
+                                          c10::optional<torch::Tensor> q_, c10::optional<torch::Tensor> k_,
+                                          c10::optional<torch::Tensor> v_, int64_t S_seg, int64_t seg_off,
                                           c10::optional<torch::Tensor> rope_cos, c10::optional<torch::Tensor> rope_sin,
                                           double eps, std::vector<int64_t> part_off);
-std::vector<torch::Tensor> qk_rmsnorm_bwd(torch::Tensor qkv, torch::Tensor wq, torch::Tensor wk, torch::Tensor dq,
-                                          torch::Tensor dk, torch::Tensor dv, torch::Tensor rq, torch::Tensor rk,
+std::vector<torch::Tensor> qk_rmsnorm_bwd(torch::Tensor qkv, torch::Tensor wq, torch::Tensor wk,
+                                          c10::optional<torch::Tensor> dq_, c10::optional<torch::Tensor> dk_,
+                                          c10::optional<torch::Tensor> dv_, torch::Tensor rq, torch::Tensor rk,
                                           int64_t S_seg, int64_t seg_off, c10::optional<torch::Tensor> rope_cos,
                                           c10::optional<torch::Tensor> rope_sin, std::vector<int64_t> part_off);
 torch::Tensor sq_norm(torch::Tensor g);
@@ -68,6 +70,7 @@ int64_t gemm_error(bool reset);
 std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal, double scale,
                                     int64_t version, int64_t split, c10::optional<torch::Tensor> kv_len);
 int64_t fmha_error(bool reset);
+void peer_copy(torch::Tensor dst, int64_t src_ptr, int64_t nbytes);
 torch::Tensor slot_sum(torch::Tensor slots, int64_t W, c10::optional<torch::Tensor> bias);
 void peer_row_copy(torch::Tensor src, torch::Tensor src_idx, torch::Tensor dst_rank, torch::Tensor dst_row,
                    std::vector<int64_t> peers);
@@ -136,6 +139,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fmha_fwd", &vo::fmha_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("causal"), py::arg("scale"),
         py::arg("version") = 2, py::arg("split") = 0, py::arg("kv_len") = py::none());
   m.def("fmha_error", &vo::fmha_error);
+  m.def("peer_copy", &vo::peer_copy, "copy-engine read of a peer buffer into a local tensor");
   m.def("slot_sum", &vo::slot_sum, "sum of W bf16 partial-sum slots (+ bias), fp32 accumulation",
         py::arg("slots"), py::arg("W"), py::arg("bias") = py::none());
   m.def("peer_row_copy", &vo::peer_row_copy, "row copies into peer GPUs' buffers (expert-parallel exchange)");

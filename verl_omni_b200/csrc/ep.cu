@@ -79,6 +79,17 @@ torch::Tensor slot_sum(torch::Tensor slots, int64_t W, c10::optional<torch::Tens
   return out;
 }
 
+// dst (contiguous, this GPU) <- nbytes read from src_ptr (a peer's symmetric buffer) by the copy engine on
+// the current stream: a remote operand crosses NVLink once before local GEMMs re-read it.
+void peer_copy(torch::Tensor dst, int64_t src_ptr, int64_t nbytes) {
+  VO_CHECK_INPUT(dst);
+  TORCH_CHECK(nbytes >= 0 && nbytes <= (int64_t)(dst.numel() * dst.element_size()), "copy larger than dst");
+  if (nbytes == 0) return;
+  c10::cuda::CUDAGuard g(dst.device());
+  VO_CUDA_OK(cudaMemcpyAsync(dst.data_ptr(), reinterpret_cast<const void*>(src_ptr), (size_t)nbytes,
+                             cudaMemcpyDeviceToDevice, stream()));
+}
+
 // src [N, D] bf16; src_idx int64 [n]; dst_rank int32 [n] (< number of peers); dst_row int64 [n];
 // peers: data pointers of each rank's [rows, D] bf16 buffer (this rank's own included).
 void peer_row_copy(torch::Tensor src, torch::Tensor src_idx, torch::Tensor dst_rank, torch::Tensor dst_row,

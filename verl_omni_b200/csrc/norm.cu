@@ -462,12 +462,16 @@ static __nv_bfloat16* bptr(const torch::Tensor& t) {
 }
 
 // Parts: q at column part_off[0], k at part_off[1], v at part_off[2] of each qkv row (-1 = absent).
-std::vector<torch::Tensor> qk_rmsnorm_fwd(torch::Tensor qkv, torch::Tensor wq, torch::Tensor wk, torch::Tensor q,
-                                          torch::Tensor k, torch::Tensor v, int64_t S_seg, int64_t seg_off,
+std::vector<torch::Tensor> qk_rmsnorm_fwd(torch::Tensor qkv, torch::Tensor wq, torch::Tensor wk,
+                                          c10::optional<torch::Tensor> q_, c10::optional<torch::Tensor> k_,
+                                          c10::optional<torch::Tensor> v_, int64_t S_seg, int64_t seg_off,
                                           c10::optional<torch::Tensor> rope_cos, c10::optional<torch::Tensor> rope_sin,
                                           double eps, std::vector<int64_t> part_off) {
   VO_CHECK_INPUT(qkv);
   c10::cuda::CUDAGuard g(qkv.device());
+  // absent destinations (a q-only or k/v-only projection) are undefined tensors: the kernel skips them
+  const torch::Tensor q = q_.value_or(torch::Tensor()), k = k_.value_or(torch::Tensor()),
+                      v = v_.value_or(torch::Tensor());
   auto ref = first_defined({q, k, v});
   const int H = ref.size(1), S_total = ref.size(2), DH = ref.size(3);
   const int3 po = make_int3((int)part_off[0], (int)part_off[1], (int)part_off[2]);
@@ -496,11 +500,14 @@ std::vector<torch::Tensor> qk_rmsnorm_fwd(torch::Tensor qkv, torch::Tensor wq, t
 }
 
 // returns dqkv [rows, 3D] (bf16), dwq [Dh] fp32, dwk [Dh] fp32
-std::vector<torch::Tensor> qk_rmsnorm_bwd(torch::Tensor qkv, torch::Tensor wq, torch::Tensor wk, torch::Tensor dq,
-                                          torch::Tensor dk, torch::Tensor dv, torch::Tensor rq, torch::Tensor rk,
+std::vector<torch::Tensor> qk_rmsnorm_bwd(torch::Tensor qkv, torch::Tensor wq, torch::Tensor wk,
+                                          c10::optional<torch::Tensor> dq_, c10::optional<torch::Tensor> dk_,
+                                          c10::optional<torch::Tensor> dv_, torch::Tensor rq, torch::Tensor rk,
                                           int64_t S_seg, int64_t seg_off, c10::optional<torch::Tensor> rope_cos,
                                           c10::optional<torch::Tensor> rope_sin, std::vector<int64_t> part_off) {
   c10::cuda::CUDAGuard g(qkv.device());
+  const torch::Tensor dq = dq_.value_or(torch::Tensor()), dk = dk_.value_or(torch::Tensor()),
+                      dv = dv_.value_or(torch::Tensor());
   auto ref = first_defined({dq, dk, dv});
   const int H = ref.size(1), S_total = ref.size(2), DH = ref.size(3);
   const int3 po = make_int3((int)part_off[0], (int)part_off[1], (int)part_off[2]);

@@ -219,7 +219,7 @@ def bench_tp(a) -> list[dict]:
     tp = TPContext(dist.group.WORLD)
     rows = []
     with torch.no_grad():
-        for name, fused in (("nccl", "0"), ("fused_peer", "1")):
+        for name, fused in (("nccl", "0"), ("fused_peer_tma_gather", "kernel"), ("fused_peer", "1")):
             os.environ["VO_TP_FUSED"] = fused
 
             def step():
@@ -238,7 +238,7 @@ def bench_tp(a) -> list[dict]:
             ms = torch.tensor([e0.elapsed_time(e1) / a.iters], device=dev)
             dist.all_reduce(ms, op=dist.ReduceOp.MAX)
             flops = 2.0 * 2 * S * Dm * (Q // W)
-            xbytes = (W - 1) / W * S * Dm * (2 + 4)  # gathered bf16 activations in, fp32 partial sums out
+            xbytes = (W - 1) / W * S * Dm * (2 + 2)  # gathered bf16 activations in, bf16 partial sums out
             t_roof = max(flops / 1.59e15, xbytes / 770e9) * 1e3
             rows.append({"op": f"tp_attn_proj_{name}", "world": W, "tokens": S, "hidden": Dm, "ms": round(float(ms), 4),
                          "tflops": round(flops / float(ms) / 1e9, 1), "roofline_ms": round(t_roof, 4),

@@ -6,16 +6,20 @@ tokens of the sequence; a column-parallel linear needs the whole sequence (all-g
 rank's output columns) and a row-parallel linear produces partial sums of the whole sequence that are
 reduce-scattered back to the token owners.
 
-Fused path (CUDA, NCCL group on one node, symmetric memory):
+Fused path (CUDA, NCCL group on one node, symmetric memory; ``VO_TP_FUSED``, default ``1``):
 
-* all-gather -> GEMM: each rank publishes its token shard in a symmetric buffer; the GEMM's TMA producer
-  reads every 128-row A tile straight from the owning peer's buffer (``GemmDesc::gather`` 1).  The weight
-  gradient of the same layer re-reads the gathered activations along the reduction (``gather`` 3);
+* all-gather -> GEMM: each rank publishes its token shard in a symmetric buffer.  The GEMM on the rank's
+  own rows starts at once while the copy engine pulls the peers' shards over NVLink on a side stream, one
+  event per peer, so each shard crosses NVLink once and its GEMM starts as soon as it has landed (the
+  pull of the next shard overlaps the GEMM on the previous one).  ``VO_TP_FUSED=kernel`` instead lets the
+  GEMM's TMA producer read every A tile straight from the owning peer (``GemmDesc::gather`` 1; the weight
+  gradients ``gather`` 2 / 3): no staging copy, but every output column tile re-reads its A tiles across
+  NVLink, which costs more than the copy at the layer sizes measured;
 * GEMM -> reduce-scatter: the epilogue stores each output row, in bf16 with plain 16-byte stores over
   NVLink, into this rank's slot of the owner's buffer (``EPI_PEER_RED`` slot mode); after a one-element
   all-reduce orders the ranks the owner sums its slots (``slot_sum``, bias fused).  The dgrad of a
-  column-parallel layer uses the same epilogue, and the dgrad / wgrad of a row-parallel layer gather the
-  output gradient (``gather`` 1 / 2).
+  column-parallel layer uses the same epilogue; the dgrad / wgrad of a row-parallel layer consume the
+  gathered output gradient chunk by chunk like the forward of a column-parallel layer.
 
 Reference path (CPU / gloo, or when the fused path does not apply): all-gather and reduce-scatter as
 collectives around plain GEMMs -- numerically the oracle of the fused path.
@@ -92,6 +96,7 @@ class TPContext:
         self.world, self.rank = D.world_size(group), D.rank(group)
         self._pairs: dict = {}
         self._fused: Optional[bool] = None
+        self._side: Optional[torch.cuda.Stream] = None
 
     def fused(self, t: torch.Tensor) -> bool:
         if os.environ.get("VO_TP_FUSED", "1") == "0" or self.world < 2 or self.world > 8:
@@ -109,6 +114,15 @@ class TPContext:
         if k not in self._pairs:
             self._pairs[k] = _Pair(numel, dtype, device, self.group)
         return self._pairs[k].next()
+
+    @staticmethod
+    def in_kernel_gather() -> bool:
+        return os.environ.get("VO_TP_FUSED", "1") == "kernel"
+
+    def side_stream(self, device) -> torch.cuda.Stream:
+        if self._side is None:
+            self._side = torch.cuda.Stream(device)
+        return self._side
 
     def barrier(self, device) -> None:
         from verl_omni_b200.parallel.symm_mem import stream_barrier
@@ -131,6 +145,31 @@ class TPContext:
 
 def _fused_ok(ctx: TPContext, x: torch.Tensor, *dims: int) -> bool:
     return ctx.fused(x) and all(d % 128 == 0 for d in dims)
+
+
+def _gathered_chunks(tp: TPContext, key: str, x: torch.Tensor, consume) -> None:
+    """All-gather overlapped with its consumer: publishes ``x`` [S_l, C], then calls ``consume(p, chunk)``
+    for every rank p, own shard first, then each peer's shard once the copy engine has pulled it into this
+    GPU's memory (side stream, one event per peer)."""
+    xb = tp.publish(key, x)
+    W, r = tp.world, tp.rank
+    main = torch.cuda.current_stream(x.device)
+    side = tp.side_stream(x.device)
+    side.wait_stream(main)  # after the barrier: every peer's shard is published
+    peers = [(r + j) % W for j in range(1, W)]
+    staged = torch.empty((W - 1,) + tuple(x.shape), device=x.device, dtype=x.dtype)
+    nbytes = x.numel() * x.element_size()
+    events = []
+    with torch.cuda.stream(side):
+        for j, p in enumerate(peers):
+            _ext().peer_copy(staged[j], xb.peer_ptrs[p], nbytes)
+            ev = torch.cuda.Event()
+            ev.record(side)
+            events.append(ev)
+    consume(r, x)
+    for j, p in enumerate(peers):
+        main.wait_event(events[j])
+        consume(p, staged[j])
 
 
 def _gemm_ag(ctx: TPContext, xb, S_l: int, K: int, w: torch.Tensor, bias) -> torch.Tensor:
@@ -163,8 +202,13 @@ class _ColumnParallel(torch.autograd.Function):
         ctx.tp = tp
         S_l, K = x.shape
         if _fused_ok(tp, x, S_l, K, w.shape[0]):
-            xb = tp.publish("col_x", x)
-            y = _gemm_ag(tp, xb, S_l, K, w, b)
+            N_l = w.shape[0]
+            if tp.in_kernel_gather():
+                y = _gemm_ag(tp, tp.publish("col_x", x), S_l, K, w, b)
+            else:
+                y = torch.empty(S_l * tp.world, N_l, device=x.device, dtype=x.dtype)
+                _gathered_chunks(tp, "col_x", x.contiguous(), lambda p, xc: _ext().gemm_tp(
+                    xc, w, S_l, N_l, K, K, K, 0, 0, y[p * S_l:(p + 1) * S_l], None, b, 0, [], 0, [], 0))
             ctx.fused = True
         else:
             y = torch.nn.functional.linear(all_gather_seq(x, tp.group), w, b)
@@ -186,9 +230,13 @@ class _ColumnParallel(torch.autograd.Function):
             dx = _reduce_to_owner(tp, "col_dx", S, K, lambda red, rows, slot: _ext().gemm_tp(
                 dy, w, S, K, N_l, N_l, K, 0, 1, None, None, None, 0, [], 0, red, rows, slot))
             # dW = dY^T gather(x): the reduction over tokens reads every peer's x shard again
-            xb = tp.publish("col_x", x)
             gw = torch.zeros(N_l, K, device=w.device, dtype=torch.float32)
-            _ext().gemm_tp(dy, None, N_l, K, S, N_l, K, 1, 1, None, gw, None, 3, xb.peer_ptrs, S_l, [], 0)
+            if tp.in_kernel_gather():
+                xb = tp.publish("col_x", x)
+                _ext().gemm_tp(dy, None, N_l, K, S, N_l, K, 1, 1, None, gw, None, 3, xb.peer_ptrs, S_l, [], 0)
+            else:
+                _gathered_chunks(tp, "col_x", x.contiguous(), lambda p, xc: _ext().gemm_tp(
+                    dy[p * S_l:(p + 1) * S_l], xc, N_l, K, S_l, N_l, K, 1, 1, None, gw, None, 0, [], 0, [], 0))
             return dx, gw.to(w.dtype), gb, None
         xg = all_gather_seq(x, tp.group)
         dx = reduce_scatter_seq(dy @ w, tp.group)
@@ -228,13 +276,23 @@ class _RowParallel(torch.autograd.Function):
             dist.all_reduce(gb, group=tp.group)
             gb = gb.to(w.dtype)
         if ctx.fused:
-            yb = tp.publish("row_dy", dy)
+            x = x.contiguous()
             dx = torch.empty(S, K_l, device=x.device, dtype=x.dtype)
-            # dX = gather(dY) W_l: A tiles from the peers' dY shards
-            _ext().gemm_tp(None, w, S, K_l, N, N, K_l, 0, 1, dx, None, None, 1, yb.peer_ptrs, S_l, [], 0)
-            # dW = gather(dY)^T x: the reduction over tokens reads the peers' dY shards
             gw = torch.zeros(N, K_l, device=w.device, dtype=torch.float32)
-            _ext().gemm_tp(None, x, N, K_l, S, N, K_l, 1, 1, None, gw, None, 2, yb.peer_ptrs, S_l, [], 0)
+            if tp.in_kernel_gather():
+                yb = tp.publish("row_dy", dy)
+                # dX = gather(dY) W_l: A tiles from the peers' dY shards
+                _ext().gemm_tp(None, w, S, K_l, N, N, K_l, 0, 1, dx, None, None, 1, yb.peer_ptrs, S_l, [], 0)
+                # dW = gather(dY)^T x: the reduction over tokens reads the peers' dY shards
+                _ext().gemm_tp(None, x, N, K_l, S, N, K_l, 1, 1, None, gw, None, 2, yb.peer_ptrs, S_l, [], 0)
+            else:
+                def consume(p, dyc):  # rows of rank p: dX rows = dY_p W_l, dW += dY_p^T x_p
+                    _ext().gemm_tp(dyc, w, S_l, K_l, N, N, K_l, 0, 1, dx[p * S_l:(p + 1) * S_l], None, None, 0,
+                                   [], 0, [], 0)
+                    _ext().gemm_tp(dyc, x[p * S_l:(p + 1) * S_l], N, K_l, S_l, N, K_l, 1, 1, None, gw, None, 0,
+                                   [], 0, [], 0)
+
+                _gathered_chunks(tp, "row_dy", dy, consume)
             return dx, gw.to(w.dtype), gb, None
         dyg = all_gather_seq(dy, tp.group)
         return (dyg @ w).to(x.dtype), (dyg.t().float() @ x.float()).to(w.dtype), gb, None
