@@ -23,6 +23,25 @@ def test_decode_attention_matches_reference(hd, rep, Hk, splits):
     torch.testing.assert_close(out.float(), ref.float(), rtol=2e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("hd,rep,Hk", [(128, 4, 2), (64, 8, 1)])
+@pytest.mark.parametrize("splits", [1, 4])
+def test_paged_decode_attention_matches_contiguous(hd, rep, Hk, splits):
+    """Block-table reads from a shuffled block pool equal the contiguous-cache oracle."""
+    from verl_omni_b200.ops.decode import decode_attention, decode_attention_reference, gather_paged
+
+    torch.manual_seed(0)
+    B, bs, nb = 3, 16, 120
+    lens = torch.tensor([5, 300, 640], dtype=torch.int32, device="cuda")
+    width = (int(lens.max()) + bs - 1) // bs
+    table = torch.randperm(nb)[:B * width].view(B, width).to(torch.int32).cuda()
+    kp = torch.randn(nb, Hk, bs, hd, device="cuda").bfloat16()
+    vp = torch.randn(nb, Hk, bs, hd, device="cuda").bfloat16()
+    q = torch.randn(B, Hk * rep, hd, device="cuda").bfloat16()
+    out = decode_attention(q, kp, vp, lens, splits=splits, block_table=table)
+    ref = decode_attention_reference(q, gather_paged(kp, table, lens), gather_paged(vp, table, lens), lens, hd ** -0.5)
+    torch.testing.assert_close(out.float(), ref.float(), rtol=2e-2, atol=2e-2)
+
+
 def test_device_sampler_distribution_and_logprobs():
     from verl_omni_b200.ops.decode import sample_tokens
 

@@ -25,6 +25,37 @@ def test_decode_matches_full_forward():
     torch.testing.assert_close(c[:, 0], full[:, 6], rtol=1e-4, atol=1e-4)
 
 
+def test_paged_cache_decode_matches_full_forward():
+    from verl_omni_b200.ops.decode import PagedKVCache
+
+    torch.manual_seed(0)
+    m = MoELLM(MoEConfig.tiny())
+    cfg = m.cfg
+    ids = torch.randint(0, 500, (2, 7))
+    full = m(ids)
+    caches = []
+    for _ in m.layers:
+        pool = PagedKVCache(8, cfg.kv_heads, 2, cfg.head_dim, "cpu", torch.float32)
+        caches.append(pool.view([pool.add_sequence(), pool.add_sequence()]))
+    a = m(ids[:, :5], caches=caches, pos0=0)
+    b = m(ids[:, 5:6], caches=caches, pos0=5)
+    c = m(ids[:, 6:7], caches=caches, pos0=6)
+    torch.testing.assert_close(a, full[:, :5], rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(b[:, 0], full[:, 5], rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(c[:, 0], full[:, 6], rtol=1e-4, atol=1e-4)
+
+
+def test_rollout_paged_cache_same_tokens():
+    from verl_omni_b200.trainer.omni.omni_trainer import OmniGRPOTrainer
+
+    t = OmniGRPOTrainer(MoEConfig.tiny(), DiffusionActorConfig(), device=torch.device("cpu"), n=1)
+    p = t.make_prompts(2, seed=3)
+    a = t.rollout.generate(p, seed=1)
+    t.rollout.kv_block_size = 4
+    b = t.rollout.generate(p, seed=1)
+    assert torch.equal(a.batch["responses"], b.batch["responses"])
+
+
 def test_grouped_experts_match_dense_loop():
     torch.manual_seed(1)
     E, D, F = 4, 8, 6

@@ -75,7 +75,7 @@ torch::Tensor slot_sum(torch::Tensor slots, int64_t W, c10::optional<torch::Tens
 void peer_row_copy(torch::Tensor src, torch::Tensor src_idx, torch::Tensor dst_rank, torch::Tensor dst_row,
                    std::vector<int64_t> peers);
 torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor lens,
-                               double scale, int64_t splits);
+                               double scale, int64_t splits, c10::optional<torch::Tensor> block_table);
 void fmha_fwd_peer(torch::Tensor q, torch::Tensor k, torch::Tensor v, std::vector<int64_t> peer_o,
                    std::vector<int64_t> peer_o2, int64_t sl, int64_t si, int64_t htot, int64_t h0, double scale);
 std::vector<torch::Tensor> linear_bwd_prep(torch::Tensor dy, c10::optional<torch::Tensor> saved,
@@ -143,7 +143,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("slot_sum", &vo::slot_sum, "sum of W bf16 partial-sum slots (+ bias), fp32 accumulation",
         py::arg("slots"), py::arg("W"), py::arg("bias") = py::none());
   m.def("peer_row_copy", &vo::peer_row_copy, "row copies into peer GPUs' buffers (expert-parallel exchange)");
-  m.def("decode_attention", &vo::decode_attention, "grouped-query decode attention over a KV cache");
+  m.def("decode_attention", &vo::decode_attention,
+        "grouped-query decode attention over a contiguous or paged (block table) KV cache", py::arg("q"),
+        py::arg("k_cache"), py::arg("v_cache"), py::arg("lens"), py::arg("scale"), py::arg("splits"),
+        py::arg("block_table") = py::none());
   m.def("fmha_fwd_peer", &vo::fmha_fwd_peer, "Ulysses attention writing each output row to its owner rank");
   m.def("fmha_bwd", &vo::fmha_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
         py::arg("dO"), py::arg("causal"), py::arg("scale"), py::arg("version") = 1, py::arg("o2") = py::none(),

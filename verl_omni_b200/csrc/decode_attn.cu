@@ -11,6 +11,10 @@
 //   * key ranges split over `splits` CTAs (flash-decoding) write (max, sum, O) partials that a second
 //     kernel merges; with one split the first kernel writes the output directly.
 // Lengths differ per sequence (`lens[b]` valid cache rows).
+//
+// Paged mode (vLLM-style block tables): the cache is a pool of fixed-size blocks [blocks, Hk, block, HD] and
+// row t of sequence b lives in block table[b][t / block] at offset t % block; the staging loads resolve
+// every row through the table, the rest of the kernel is unchanged.
 #include "common.cuh"
 
 namespace vo {
@@ -19,12 +23,18 @@ namespace {
 constexpr int kTile = 64;
 constexpr int kDecThreads = 128;
 
+struct PageTable {
+  const int* table;  // [B, stride] block ids, null: contiguous [B, Hk, Lmax, HD] cache
+  int stride;
+  int block;  // rows per block
+};
+
 template <int HD, int REP>
 __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
     const __nv_bfloat16* __restrict__ q,      // [B, Hk * REP, HD]
     const __nv_bfloat16* __restrict__ kc,     // [B, Hk, Lmax, HD]
     const __nv_bfloat16* __restrict__ vc,     // [B, Hk, Lmax, HD]
-    const int* __restrict__ lens, int Hk, int Lmax, float scale_log2, int splits,
+    const int* __restrict__ lens, int Hk, int Lmax, float scale_log2, int splits, PageTable pt,
     __nv_bfloat16* __restrict__ out,          // [B, Hk * REP, HD] (splits == 1)
     float* __restrict__ part_o,               // [B, Hk, splits, REP, HD]
     float* __restrict__ part_ml) {            // [B, Hk, splits, REP, 2]
@@ -62,8 +72,14 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
       const int r = i / (HD / 8), c = i % (HD / 8);
       bf16x8 kv = {}, vv = {};
       if (r < nk) {
-        kv = reinterpret_cast<const bf16x8*>(kc + kvbase + (int64_t)(t0 + r) * HD)[c];
-        vv = reinterpret_cast<const bf16x8*>(vc + kvbase + (int64_t)(t0 + r) * HD)[c];
+        const int t = t0 + r;
+        int64_t off = kvbase + (int64_t)t * HD;
+        if (pt.table) {
+          const int blk = __ldg(pt.table + (int64_t)b * pt.stride + t / pt.block);
+          off = (((int64_t)blk * Hk + kh) * pt.block + t % pt.block) * HD;
+        }
+        kv = reinterpret_cast<const bf16x8*>(kc + off)[c];
+        vv = reinterpret_cast<const bf16x8*>(vc + off)[c];
       }
       *reinterpret_cast<bf16x8*>(ks + r * ROW + c * 8) = kv;
       *reinterpret_cast<bf16x8*>(vs + r * HD + c * 8) = vv;
@@ -171,8 +187,8 @@ __global__ void decode_combine_kernel(const float* __restrict__ part_o, const fl
 
 template <int HD, int REP>
 void launch_decode(const torch::Tensor& q, const torch::Tensor& kc, const torch::Tensor& vc, const torch::Tensor& lens,
-                   float scale_log2, int splits, torch::Tensor& out) {
-  const int B = (int)kc.size(0), Hk = (int)kc.size(1), Lmax = (int)kc.size(2);
+                   float scale_log2, int splits, PageTable pt, torch::Tensor& out) {
+  const int B = (int)q.size(0), Hk = (int)kc.size(1), Lmax = (int)kc.size(2);
   auto fo = q.options().dtype(torch::kFloat32);
   torch::Tensor po, pml;
   if (splits > 1) {
@@ -181,7 +197,7 @@ void launch_decode(const torch::Tensor& q, const torch::Tensor& kc, const torch:
   }
   auto bfp = [](const torch::Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr<at::BFloat16>()); };
   decode_attn_kernel<HD, REP><<<dim3(B * Hk, splits), kDecThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      bfp(q), bfp(kc), bfp(vc), lens.data_ptr<int>(), Hk, Lmax, scale_log2, splits,
+      bfp(q), bfp(kc), bfp(vc), lens.data_ptr<int>(), Hk, Lmax, scale_log2, splits, pt,
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()), splits > 1 ? po.data_ptr<float>() : nullptr,
       splits > 1 ? pml.data_ptr<float>() : nullptr);
   count_launch();
@@ -198,10 +214,11 @@ void launch_decode(const torch::Tensor& q, const torch::Tensor& kc, const torch:
 
 }  // namespace
 
-// q [B, Hq, HD] bf16; k_cache / v_cache [B, Hk, Lmax, HD] bf16; lens [B] int32 (valid rows, >= 1).
-// Returns o [B, Hq, HD].  Hq = Hk x rep with rep in {1, 2, 4, 8}; HD in {64, 128}.
+// q [B, Hq, HD] bf16; k_cache / v_cache [B, Hk, Lmax, HD] bf16 -- or, with block_table [B, max_blocks]
+// int32, block pools [blocks, Hk, block, HD]; lens [B] int32 (valid rows, >= 1; with a table at most
+// max_blocks x block).  Returns o [B, Hq, HD].  Hq = Hk x rep with rep in {1, 2, 4, 8}; HD in {64, 128}.
 torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor lens,
-                               double scale, int64_t splits) {
+                               double scale, int64_t splits, c10::optional<torch::Tensor> block_table) {
   VO_CHECK_INPUT(q);
   VO_CHECK_INPUT(k_cache);
   VO_CHECK_INPUT(v_cache);
@@ -210,8 +227,19 @@ torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Te
                   lens.scalar_type() == torch::kInt32,
               "bf16 q / cache, int32 lengths");
   const int64_t B = q.size(0), Hq = q.size(1), HD = q.size(2), Hk = k_cache.size(1);
-  TORCH_CHECK(k_cache.size(0) == B && k_cache.size(3) == HD && v_cache.sizes() == k_cache.sizes() && Hq % Hk == 0 &&
-                  lens.numel() == B,
+  PageTable pt{nullptr, 0, 0};
+  if (block_table.has_value() && block_table->defined()) {
+    VO_CHECK_INPUT(*block_table);
+    TORCH_CHECK(block_table->scalar_type() == torch::kInt32 && block_table->dim() == 2 && block_table->size(0) == B,
+                "int32 [B, max_blocks] block table");
+    pt.table = block_table->data_ptr<int>();
+    pt.stride = (int)block_table->size(1);
+    pt.block = (int)k_cache.size(2);
+    TORCH_CHECK(pt.block > 0, "empty blocks");
+  } else {
+    TORCH_CHECK(k_cache.size(0) == B, "one cache row per sequence");
+  }
+  TORCH_CHECK(k_cache.size(3) == HD && v_cache.sizes() == k_cache.sizes() && Hq % Hk == 0 && lens.numel() == B,
               "decode attention shapes");
   c10::cuda::CUDAGuard g(q.device());
   auto out = torch::empty_like(q);
@@ -219,7 +247,7 @@ torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Te
   const float sl2 = (float)scale * 1.4426950408889634f;
   const int sp = (int)std::max<int64_t>(1, splits);
 #define VO_DEC(HDV, REPV) \
-  if (HD == HDV && rep == REPV) return launch_decode<HDV, REPV>(q, k_cache, v_cache, lens, sl2, sp, out), out;
+  if (HD == HDV && rep == REPV) return launch_decode<HDV, REPV>(q, k_cache, v_cache, lens, sl2, sp, pt, out), out;
   VO_DEC(128, 8) VO_DEC(128, 4) VO_DEC(128, 2) VO_DEC(128, 1) VO_DEC(64, 8) VO_DEC(64, 4) VO_DEC(64, 2) VO_DEC(64, 1)
 #undef VO_DEC
   TORCH_CHECK(false, "decode attention: head_dim 64 / 128 and 1, 2, 4 or 8 query heads per KV head");

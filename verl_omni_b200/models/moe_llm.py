@@ -26,7 +26,7 @@ import torch.nn.functional as F
 from verl_omni_b200.models.layers import Linear, rope_table
 from verl_omni_b200.ops.attention import attention
 from verl_omni_b200.ops import linear as L
-from verl_omni_b200.ops.decode import KVCache, decode_attention
+from verl_omni_b200.ops.decode import KVCache, PagedView, decode_attention
 
 
 @dataclass
@@ -141,6 +141,15 @@ class MoEBlock(nn.Module):
                 return x + self.o_proj(o.reshape(B, 1, cfg.q_heads * hd))
             if not first:
                 k, v = cache.k[:, :, :cache.len], cache.v[:, :, :cache.len]
+        elif isinstance(cache, PagedView):
+            # paged cache (block pool + block table): same steps through the block-table decode kernel
+            first = cache.len == 0
+            cache.append(k, v)
+            if S == 1 and not first:
+                o = cache.decode(q[:, :, 0])
+                return x + self.o_proj(o.reshape(B, 1, cfg.q_heads * hd))
+            if not first:
+                k, v = cache.contiguous()
         elif cache is not None:
             if "k" in cache:
                 k = torch.cat([cache["k"], k], 2)

@@ -14,7 +14,7 @@ from typing import Optional
 import torch
 
 from verl_omni_b200.models.moe_llm import MoELLM
-from verl_omni_b200.ops.decode import KVCache, sample_tokens
+from verl_omni_b200.ops.decode import KVCache, PagedKVCache, sample_tokens
 from verl_omni_b200.utils.dataproto import DataProto
 
 
@@ -37,8 +37,9 @@ def sample_next(logits: torch.Tensor, temperature: float, top_k: int, top_p: flo
 
 class LLMRolloutEngine:
     def __init__(self, module: MoELLM, *, max_new_tokens: int = 256, temperature: float = 1.0, top_k: int = 0,
-                 top_p: float = 1.0, eos_id: Optional[int] = None, device=None):
+                 top_p: float = 1.0, eos_id: Optional[int] = None, device=None, kv_block_size: int = 0):
         self.module = module
+        self.kv_block_size = kv_block_size  # > 0: paged KV cache with blocks of this many positions
         self.max_new_tokens = max_new_tokens
         self.temperature, self.top_k, self.top_p = temperature, top_k, top_p
         self.eos_id = eos_id
@@ -51,8 +52,17 @@ class LLMRolloutEngine:
         dev = ids.device
         g = torch.Generator(device=dev).manual_seed(int(seed))  # sampling stays on the device
         cfg = self.module.cfg
-        caches = [KVCache(B, cfg.kv_heads, P + self.max_new_tokens, cfg.head_dim, dev, self.module.embed.dtype)
-                  for _ in self.module.layers]
+        if self.kv_block_size > 0:
+            bs = self.kv_block_size
+            per_seq = -(-(P + self.max_new_tokens) // bs)
+            caches = []
+            for _ in self.module.layers:
+                pool = PagedKVCache(B * per_seq, cfg.kv_heads, bs, cfg.head_dim, dev, self.module.embed.dtype,
+                                    max_blocks_per_seq=per_seq)
+                caches.append(pool.view([pool.add_sequence() for _ in range(B)]))
+        else:
+            caches = [KVCache(B, cfg.kv_heads, P + self.max_new_tokens, cfg.head_dim, dev, self.module.embed.dtype)
+                      for _ in self.module.layers]
         logits = self.module(ids, caches=caches, pos0=0, audio_feats=batch.batch.get("audio_feats"),
                              image_patches=batch.batch.get("image_patches"))[:, -1]
         out_ids, out_lp = [], []
