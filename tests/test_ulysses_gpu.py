@@ -55,6 +55,41 @@ def test_qwen_image_ulysses_sp2_nccl():
     run_ranks(_run, 2, device="cuda")
 
 
+def _run_masked(rank, world):
+    """Right-padded prompts under SP: gathered keys reordered image-first, native key-count attention."""
+    import torch.distributed as dist
+
+    from verl_omni_b200.models.qwen_image import QwenImageConfig, QwenImageDiT
+
+    torch.manual_seed(0)
+    m = QwenImageDiT(QwenImageConfig(in_channels=4, hidden=256, heads=4, depth=2, joint_attention_dim=64,
+                                     axes_dim=(8, 28, 28))).cuda().bfloat16()
+    g = torch.Generator().manual_seed(1)
+    x, c = torch.randn(2, 4, 32, 32, generator=g).cuda(), torch.randn(2, 256, 64, generator=g).cuda()
+    t = torch.tensor([900.0, 300.0]).cuda()
+    mask = torch.ones(2, 256, device="cuda")
+    mask[0, 150:] = 0
+    mask[1, 40:] = 0
+    gy = torch.randn(x.shape, generator=torch.Generator().manual_seed(2)).cuda()
+    outs, grads = [], []
+    for sp in (None, dist.group.WORLD):
+        m.sp_group = sp
+        out = m(x, t, c, mask)
+        (out.float() * gy).sum().backward()
+        outs.append(out.float().detach())
+        grads.append({n: p.grad.float().clone() for n, p in m.named_parameters() if p.grad is not None})
+        m.zero_grad(set_to_none=True)
+    torch.testing.assert_close(outs[1], outs[0], rtol=3e-2, atol=3e-2)
+    rel = lambda a, b: float((a - b).norm() / (b.norm() + 1e-6))  # noqa: E731
+    for n, gs in grads[1].items():
+        dist.all_reduce(gs)
+        assert rel(gs, grads[0][n]) < 5e-2, (n, rel(gs, grads[0][n]))
+
+
+def test_qwen_image_ulysses_sp2_padded_prompts_nccl():
+    run_ranks(_run_masked, 2, device="cuda")
+
+
 def _fused(rank, world):
     import os
 

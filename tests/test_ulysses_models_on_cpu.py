@@ -10,7 +10,8 @@ CASES = {
     "sd35_tiny": {"St": 12},
     "sd35_tiny_pad": {"St": 13},   # text not divisible by sp: zero-padded and masked
     "flux_tiny": {"St": 12},
-    "qwen_image_tiny": {"St": 12, "mask": True},
+    "qwen_image_tiny": {"St": 12, "mask": True},   # right-padded prompt: segment-major keys + key counts
+    "qwen_image_tiny_holes": {"St": 12, "mask": "holes"},  # interleaved valid keys: boolean key mask
     "wan_tiny": {"St": 12},
 }
 
@@ -18,7 +19,7 @@ CASES = {
 def _inputs(name, St, mask):
     from verl_omni_b200.models.registry import get_arch
 
-    spec = get_arch(name.replace("_pad", ""))
+    spec = get_arch(name.replace("_pad", "").replace("_holes", ""))
     g = torch.Generator().manual_seed(1)
     B = 2
     x = torch.randn(B, *spec.latent_shape, generator=g)
@@ -27,7 +28,9 @@ def _inputs(name, St, mask):
     for k, s in spec.cond_shapes.items():
         if k.endswith("_mask"):
             m = torch.ones(B, St)
-            if mask:
+            if mask == "holes":
+                m[0, 3:6] = 0
+            elif mask:
                 m[0, St - 5:] = 0
             cond[k] = m
         elif k == "prompt_embeds":

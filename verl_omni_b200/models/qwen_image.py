@@ -123,16 +123,22 @@ class QwenImageDiT(nn.Module):
         rope = rope_full = self._rope(Hh // p, Ww // p, n_ref, St, x.device)
         sp = getattr(self, "sp_group", None)
         kv_len = key_mask = None
+        pm = prompt_mask.to(x.device).bool() if masked else None
+        # right-padded prompts (valid text tokens form a prefix): keys past the image tokens + valid text
+        # tokens are masked by a per-sequence key count on the tcgen05 kernels; other masks use a key mask
+        padded = masked and bool((pm.int().cumprod(1).bool() == pm).all())
+        if padded:
+            kv_len = (Si + pm.sum(1)).to(torch.int32)
         if sp is not None:  # Ulysses: this rank keeps 1/sp of the image tokens and of the text tokens
             x, c = shard_sequence(x, sp), shard_sequence(c, sp)
             rope = (local_rows(rope[0], [Si, St], sp), local_rows(rope[1], [Si, St], sp))
-            if masked:  # valid keys in the gathered order [img_0 txt_0 img_1 txt_1 ...]
+            # key counts: the gathered keys are reordered image-first, text in prompt order
+            if masked and not padded:  # valid keys in the gathered order [img_0 txt_0 img_1 txt_1 ...]
                 local = torch.cat([torch.ones(B, x.shape[1], dtype=torch.bool, device=x.device),
-                                   shard_sequence(prompt_mask.to(x.device).bool(), sp)], 1)
+                                   shard_sequence(pm, sp)], 1)
                 key_mask = gather_key_mask(local, sp)
-        elif masked:
-            # right-padded prompts: keys past image tokens + valid text tokens are masked in every block
-            kv_len = (Si + prompt_mask.to(torch.int64).sum(1)).to(torch.int32)
+        elif masked and not padded:
+            key_mask = torch.cat([torch.ones(B, Si, dtype=torch.bool, device=x.device), pm], 1)
         for blk in self.transformer_blocks:
             x, c = blk(x, c, ta, rope, kv_len, sp_group=sp, key_mask=key_mask, rope_full=rope_full)
         x = adaln_layernorm(x, self.norm_out_linear(ta), 1, 0, 2, cfg.eps)

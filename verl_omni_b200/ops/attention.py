@@ -31,9 +31,13 @@ def _native() -> bool:
 
 class _FMHA(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, causal, scale):
-        o, lse = ext().fmha_fwd(q, k, v, causal, scale, _FWD_VERSION)
+    def forward(ctx, q, k, v, causal, scale, kv_len=None):
+        if kv_len is not None:  # keys at positions >= kv_len[b] masked (forward v3)
+            o, lse = ext().fmha_fwd(q, k, v, False, scale, 3, 0, kv_len=kv_len)
+        else:
+            o, lse = ext().fmha_fwd(q, k, v, causal, scale, _FWD_VERSION)
         ctx.save_for_backward(q, k, v, o, lse)
+        ctx.kv_len = kv_len
         ctx.meta = (causal, scale)
         return o
 
@@ -41,18 +45,19 @@ class _FMHA(torch.autograd.Function):
     def backward(ctx, do):
         q, k, v, o, lse = ctx.saved_tensors
         causal, scale = ctx.meta
-        if os.environ.get("VO_ATTN_BWD", "native") != "torch" and hasattr(ext(), "fmha_bwd"):
+        if ctx.kv_len is not None or (os.environ.get("VO_ATTN_BWD", "native") != "torch"
+                                      and hasattr(ext(), "fmha_bwd")):
             B, S, H, D = o.shape
             dq, dk, dv = ext().fmha_bwd(q, k, v, o, lse, do.contiguous().view(B, S, H, D), causal, scale,
-                                        _BWD_VERSION)
-            return dq, dk, dv, None, None
+                                        _BWD_VERSION, kv_len=ctx.kv_len)
+            return dq, dk, dv, None, None, None
         # backward kernel not built: recompute through SDPA autograd
         B, S, H, D = o.shape
         with torch.enable_grad():
             qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
             oo = F.scaled_dot_product_attention(qq, kk, vv, is_causal=causal, scale=scale)
             dq, dk, dv = torch.autograd.grad(oo, (qq, kk, vv), do.view(B, S, H, D).transpose(1, 2))
-        return dq, dk, dv, None, None
+        return dq, dk, dv, None, None, None
 
 
 class _FMHASplit(torch.autograd.Function):
@@ -113,6 +118,10 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = 
     same padding after a sequence-parallel gather interleaved it).  Masked cases run on SDPA."""
     B, H, S, Dh = q.shape
     scale = scale if scale is not None else 1.0 / math.sqrt(Dh)
+    if (kv_len is not None and key_mask is None and not causal and q.is_cuda and _native() and Dh in (64, 128)
+            and q.dtype == torch.bfloat16 and _FWD_VERSION >= 2):
+        o = _FMHA.apply(q, k, v, False, scale, kv_len.to(torch.int32).contiguous())  # [B, S, H, Dh]
+        return o.view(B, S, H * Dh)
     if kv_len is not None or key_mask is not None:
         keep = key_mask.to(q.device, torch.bool) if key_mask is not None else (
             torch.arange(k.shape[2], device=q.device)[None, :] < kv_len.to(q.device)[:, None])

@@ -89,19 +89,44 @@ def head_to_seq(o: torch.Tensor, group, head_dim: int) -> torch.Tensor:
     return _HeadToSeq.apply(o, group, head_dim)
 
 
+_ORDERS: dict = {}
+
+
+def segment_major_order(segments: list[int], world: int, device) -> torch.Tensor:
+    """Key permutation of a gathered sequence ``[seg0_r0 seg1_r0 .. seg0_r1 seg1_r1 ..]`` (each rank holds
+    ``segments[i]`` rows of segment i) into segment-major order ``[seg0_r0 seg0_r1 .. seg1_r0 seg1_r1 ..]``:
+    the original token order of every segment, segments one after the other."""
+    key = (tuple(segments), world, str(device))
+    if key not in _ORDERS:
+        sl, idx, off = sum(segments), [], 0
+        for n in segments:
+            for r in range(world):
+                idx.append(torch.arange(r * sl + off, r * sl + off + n))
+            off += n
+        _ORDERS[key] = torch.cat(idx).to(device)
+    return _ORDERS[key]
+
+
 def ulysses_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, group, causal: bool = False,
-                      scale: Optional[float] = None, key_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+                      scale: Optional[float] = None, key_mask: Optional[torch.Tensor] = None,
+                      kv_len: Optional[torch.Tensor] = None, key_segments: Optional[list] = None) -> torch.Tensor:
     """q/k/v [B, H, S/sp, D] (local tokens, all heads) -> token-major output [B, S/sp, H*D].
 
     ``key_mask`` [B, S] (optional) marks valid keys in the gathered order (rank-major concatenation of the
-    local sequences, see :func:`gather_key_mask`)."""
+    local sequences, see :func:`gather_key_mask`).  ``kv_len`` [B] with ``key_segments`` (rows per rank of
+    each segment, e.g. [image, text]) instead counts the valid keys in segment-major order: the gathered
+    keys and values are permuted into that order (attention is invariant to a joint key / value
+    permutation), which turns right-padded text into a key-count mask the tcgen05 kernels take natively."""
     from verl_omni_b200.ops.attention import attention
 
     if group is None or D.world_size(group) == 1:
-        return attention(q, k, v, causal=causal, scale=scale, key_mask=key_mask)
+        return attention(q, k, v, causal=causal, scale=scale, key_mask=key_mask, kv_len=kv_len)
     Dh = q.shape[-1]
-    o = attention(seq_to_head(q, group), seq_to_head(k, group), seq_to_head(v, group), causal=causal, scale=scale,
-                  key_mask=key_mask)
+    kg, vg = seq_to_head(k, group), seq_to_head(v, group)
+    if kv_len is not None:
+        order = segment_major_order(list(key_segments), D.world_size(group), k.device)
+        kg, vg = kg.index_select(2, order), vg.index_select(2, order)
+    o = attention(seq_to_head(q, group), kg, vg, causal=causal, scale=scale, key_mask=key_mask, kv_len=kv_len)
     return head_to_seq(o, group, Dh)
 
 
@@ -120,7 +145,10 @@ def joint_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, split: in
             o = attention(q, k, v, key_mask=key_mask)
             return o[:, :split].contiguous(), o[:, split:].contiguous()
         return attention_split(q, k, v, split, kv_len=kv_len)
-    o = ulysses_attention(q, k, v, sp_group, key_mask=key_mask)
+    if kv_len is not None and key_mask is None:  # valid keys: every image token, then a prefix of the text
+        o = ulysses_attention(q, k, v, sp_group, kv_len=kv_len, key_segments=[split, q.shape[2] - split])
+    else:
+        o = ulysses_attention(q, k, v, sp_group, key_mask=key_mask)
     return o[:, :split].contiguous(), o[:, split:].contiguous()
 
 
