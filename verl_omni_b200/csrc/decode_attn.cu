@@ -23,6 +23,24 @@ namespace {
 constexpr int kTile = 64;
 constexpr int kDecThreads = 128;
 
+// N consecutive bf16 values (N in {1, 2, 4, 8}, N-element aligned) -> fp32
+template <int N>
+__device__ __forceinline__ void load_row(const __nv_bfloat16* p, float* f) {
+  if constexpr (N == 8) {
+    unpack8(*reinterpret_cast<const bf16x8*>(p), f);
+  } else if constexpr (N == 4) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    f[0] = a.x, f[1] = a.y, f[2] = b.x, f[3] = b.y;
+  } else if constexpr (N == 2) {
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+    f[0] = a.x, f[1] = a.y;
+  } else {
+    f[0] = bf2f(*p);
+  }
+}
+
 struct PageTable {
   const int* table;  // [B, stride] block ids, null: contiguous [B, Hk, Lmax, HD] cache
   int stride;
@@ -41,7 +59,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
   constexpr int ROW = HD + 8;  // padded smem row (bf16 elements)
   __shared__ __align__(16) __nv_bfloat16 ks[kTile * ROW];
   __shared__ __align__(16) __nv_bfloat16 vs[kTile * HD];
-  __shared__ float qs[REP * HD];
+  __shared__ __align__(16) float qs[REP * HD];
   __shared__ float ps[REP * kTile];
   __shared__ float mrow[REP], lrow[REP], alpha_s[REP];
 
@@ -57,8 +75,12 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
     mrow[tid] = -INFINITY;
     lrow[tid] = 0.f;
   }
-  // this thread's output columns: d = tid % HD for heads h = tid / HD + k (HD / kDecThreads ...)
-  constexpr int OUT_PER = (REP * HD + kDecThreads - 1) / kDecThreads;  // outputs owned per thread
+  // this thread's outputs: OUT_PER consecutive head-dim columns [o0, o0 + OUT_PER) of the flattened
+  // (head, dim) space, so each V row read is one vector load
+  constexpr int OUT_PER = (REP * HD) / kDecThreads > 0 ? (REP * HD) / kDecThreads : 1;
+  const int o0 = tid * OUT_PER;
+  const bool o_ok = o0 < REP * HD;
+  const int oh = o_ok ? o0 / HD : 0, od = o0 % HD;
   float acc[OUT_PER];
 #pragma unroll
   for (int i = 0; i < OUT_PER; ++i) acc[i] = 0.f;
@@ -85,22 +107,45 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
       *reinterpret_cast<bf16x8*>(vs + r * HD + c * 8) = vv;
     }
     __syncthreads();
-    // scores (log2 domain)
-    for (int i = tid; i < REP * kTile; i += kDecThreads) {
-      const int h = i / kTile, k = i % kTile;
-      float s = -INFINITY;
+    // scores (log2 domain): thread -> key k, heads h0, h0 + HSTEP, ...; each K chunk is read once for
+    // all of the thread's heads
+    {
+      constexpr int HSTEP = kDecThreads / kTile;
+      constexpr int HPT = (REP + HSTEP - 1) / HSTEP;
+      const int k = tid % kTile, h0 = tid / kTile;
+      float sc[HPT];
+#pragma unroll
+      for (int j = 0; j < HPT; ++j) sc[j] = 0.f;
       if (k < nk) {
-        s = 0.f;
-        const float* qh = qs + h * HD;
-#pragma unroll 4
+#pragma unroll 2
         for (int c = 0; c < HD / 8; ++c) {
           float f[8];
           unpack8(*reinterpret_cast<const bf16x8*>(ks + k * ROW + c * 8), f);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) s = fmaf(qh[c * 8 + j], f[j], s);
+          for (int j = 0; j < HPT; ++j) {
+            const int h = h0 + j * HSTEP;
+            if (h < REP) {
+              const float4 qa = *reinterpret_cast<const float4*>(qs + h * HD + c * 8);
+              const float4 qb = *reinterpret_cast<const float4*>(qs + h * HD + c * 8 + 4);
+              float t = sc[j];
+              t = fmaf(qa.x, f[0], t);
+              t = fmaf(qa.y, f[1], t);
+              t = fmaf(qa.z, f[2], t);
+              t = fmaf(qa.w, f[3], t);
+              t = fmaf(qb.x, f[4], t);
+              t = fmaf(qb.y, f[5], t);
+              t = fmaf(qb.z, f[6], t);
+              t = fmaf(qb.w, f[7], t);
+              sc[j] = t;
+            }
+          }
         }
       }
-      ps[i] = s;
+#pragma unroll
+      for (int j = 0; j < HPT; ++j) {
+        const int h = h0 + j * HSTEP;
+        if (h < REP) ps[h * kTile + k] = k < nk ? sc[j] : -INFINITY;
+      }
     }
     __syncthreads();
     // per-head running max / sum (one warp per head, heads strided over the 4 warps)
@@ -123,35 +168,35 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
       }
     }
     __syncthreads();
-    // O = O * alpha + P V
+    // O = O * alpha + P V (OUT_PER consecutive columns of one head per thread)
+    if (o_ok) {
+      const float al = alpha_s[oh];
 #pragma unroll
-    for (int i = 0; i < OUT_PER; ++i) {
-      const int o = tid + i * kDecThreads;
-      if (o >= REP * HD) break;
-      const int h = o / HD, d = o % HD;
-      float a = acc[i] * alpha_s[h];
-      const float* ph = ps + h * kTile;
-      for (int k = 0; k < nk; ++k) a = fmaf(ph[k], bf2f(vs[k * HD + d]), a);
-      acc[i] = a;
+      for (int i = 0; i < OUT_PER; ++i) acc[i] *= al;
+      const float* ph = ps + oh * kTile;
+      for (int k = 0; k < nk; ++k) {
+        const float p = ph[k];
+        float f[OUT_PER];
+        load_row<OUT_PER>(vs + k * HD + od, f);
+#pragma unroll
+        for (int i = 0; i < OUT_PER; ++i) acc[i] = fmaf(p, f[i], acc[i]);
+      }
     }
     __syncthreads();
   }
   if (splits == 1) {
+    if (o_ok) {
+      const float l = lrow[oh];
 #pragma unroll
-    for (int i = 0; i < OUT_PER; ++i) {
-      const int o = tid + i * kDecThreads;
-      if (o >= REP * HD) break;
-      const int h = o / HD, d = o % HD;
-      const float l = lrow[h];
-      out[((int64_t)b * Hk * REP + (int64_t)kh * REP + h) * HD + d] = f2bf(l > 0.f ? acc[i] / l : 0.f);
+      for (int i = 0; i < OUT_PER; ++i)
+        out[((int64_t)b * Hk * REP + (int64_t)kh * REP + oh) * HD + od + i] = f2bf(l > 0.f ? acc[i] / l : 0.f);
     }
     return;
   }
   const int64_t pbase = (((int64_t)b * Hk + kh) * splits + split) * REP;
+  if (o_ok) {
 #pragma unroll
-  for (int i = 0; i < OUT_PER; ++i) {
-    const int o = tid + i * kDecThreads;
-    if (o < REP * HD) part_o[pbase * HD + o] = acc[i];
+    for (int i = 0; i < OUT_PER; ++i) part_o[pbase * HD + o0 + i] = acc[i];
   }
   if (tid < REP) {
     part_ml[(pbase + tid) * 2] = mrow[tid];

@@ -385,6 +385,39 @@ def bench_moe(a) -> list[dict]:
              "cublas_per_expert_loop_ms": round(ms_loop, 4)}]
 
 
+def bench_decode(a) -> list[dict]:
+    """Grouped-query decode attention, Qwen3-Omni-30B-A3B thinker heads (32 query / 4 KV heads, head_dim 128):
+    ``--B`` sequences with ``--S`` cached positions each, contiguous cache vs paged cache (16-row blocks,
+    blocks shuffled across the pool).  Bandwidth counts the K and V bytes read once (the cache is larger
+    than L2 at the default sizes)."""
+    from verl_omni_b200.ops.decode import decode_attention
+
+    B, L, Hk, rep, hd, bs = a.B, a.S, 4, 8, 128, 16
+    q = torch.randn(B, Hk * rep, hd, device="cuda").bfloat16()
+    kc = torch.randn(B, Hk, L, hd, device="cuda").bfloat16()
+    vc = torch.randn(B, Hk, L, hd, device="cuda").bfloat16()
+    lens = torch.full((B,), L, dtype=torch.int32, device="cuda")
+    nb = B * L // bs
+    perm = torch.randperm(nb, device="cuda")
+    # the same rows scattered over a shuffled block pool [blocks, Hk, 16, hd]
+    kp = torch.empty(nb, Hk, bs, hd, device="cuda", dtype=torch.bfloat16)
+    vp = torch.empty_like(kp)
+    kp[perm] = kc.view(B, Hk, L // bs, bs, hd).permute(0, 2, 1, 3, 4).reshape(nb, Hk, bs, hd)
+    vp[perm] = vc.view(B, Hk, L // bs, bs, hd).permute(0, 2, 1, 3, 4).reshape(nb, Hk, bs, hd)
+    table = perm.view(B, L // bs).to(torch.int32)
+    nbytes = 2 * B * Hk * L * hd * 2
+    out = []
+    for name, fn in (("contiguous", lambda sp: decode_attention(q, kc, vc, lens, splits=sp)),
+                     ("paged16", lambda sp: decode_attention(q, kp, vp, lens, splits=sp, block_table=table))):
+        if a.only and name not in a.only.split(","):
+            continue
+        for sp in ([0] if not a.compare else [0, 2, 4, 8, 16]):  # 0: the default split heuristic
+            ms = timeit(lambda: fn(sp), a.iters)
+            out.append({"op": f"decode_attn_{name}", "splits": sp or "auto", "B": B, "ctx": L, "q_heads": Hk * rep,
+                        "kv_heads": Hk, "hd": hd, "ms": round(ms, 4), "gbs": round(nbytes / ms / 1e6, 1)})
+    return out
+
+
 def bench_groupnorm(a) -> list[dict]:
     """VAE-decoder GroupNorm(32)+SiLU on channels-last [8, 128, 512, 512] bf16 (one read + one write pass
     after the statistics pass)."""
@@ -402,7 +435,7 @@ def bench_groupnorm(a) -> list[dict]:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "gemm_sweep", "gemm_pair", "ulysses", "tp", "fmha", "sde", "adaln", "optstep", "moe", "groupnorm"])
+    ap.add_argument("op", choices=["gemm", "gemm_sweep", "gemm_pair", "ulysses", "tp", "fmha", "sde", "adaln", "optstep", "moe", "groupnorm", "decode"])
     ap.add_argument("--numel", type=int, default=2_240_000_000)
     ap.add_argument("--M", type=int, default=21712)
     ap.add_argument("--N", type=int, default=6144)
@@ -416,7 +449,7 @@ def main() -> None:
     ap.add_argument("--compare", action="store_true")
     a = ap.parse_args()
     pk = _peaks()
-    rows = {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "gemm_pair": bench_gemm_pair, "ulysses": bench_ulysses, "tp": bench_tp, "fmha": bench_fmha, "optstep": bench_optstep, "sde": bench_sde, "adaln": bench_adaln, "moe": bench_moe, "groupnorm": bench_groupnorm}[a.op](a)
+    rows = {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "gemm_pair": bench_gemm_pair, "ulysses": bench_ulysses, "tp": bench_tp, "fmha": bench_fmha, "optstep": bench_optstep, "sde": bench_sde, "adaln": bench_adaln, "moe": bench_moe, "groupnorm": bench_groupnorm, "decode": bench_decode}[a.op](a)
     for r in rows:
         if "tflops" in r:
             r[f"frac_of_{pk['src']}_gemm_peak"] = round(r["tflops"] / pk["tflops"], 3)

@@ -176,10 +176,10 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
         if block_table is not None:
             k_cache, v_cache = gather_paged(k_cache, block_table, lens), gather_paged(v_cache, block_table, lens)
         return decode_attention_reference(q, k_cache, v_cache, lens, scale)
-    if splits <= 0:  # enough CTAs to cover the SMs a few times over
+    if splits <= 0:  # about 16 CTAs per SM (5 are resident at once): memory parallelism for the cache reads
         n = q.shape[0] * k_cache.shape[1]
         span = k_cache.shape[2] * (block_table.shape[1] if block_table is not None else 1)
-        splits = max(1, min(16, (4 * torch.cuda.get_device_properties(q.device).multi_processor_count) // max(n, 1)))
+        splits = max(1, min(16, (16 * torch.cuda.get_device_properties(q.device).multi_processor_count) // max(n, 1)))
         splits = min(splits, max(1, int(span) // 256))
     bt = block_table.to(torch.int32).contiguous() if block_table is not None else None
     return _ext().decode_attention(q.contiguous(), k_cache, v_cache, lens.to(torch.int32).contiguous(), float(scale),
