@@ -2,9 +2,9 @@
 //
 // Decode is bound by reading the cache, so each CTA owns one (sequence, KV head) pair and a slice of the
 // keys, and serves every query head of that group from one read of each K / V tile:
-//   * K and V tiles of 64 keys are staged in shared memory with 16-byte loads (rows padded by 16 bytes so
-//     the per-key row reads of the score phase do not collide in banks);
-//   * scores: the REP x 64 scores of a tile are spread over the 128 threads (consecutive threads take
+//   * K and V tiles of 32 keys are staged in shared memory with 16-byte asynchronous copies, two tiles in
+//     flight (rows padded by 16 bytes so the per-key row reads of the score phase do not collide in banks);
+//   * scores: the REP x kTile scores of a tile are spread over the 128 threads (consecutive threads take
 //     consecutive keys of one query head; REP <= 8 heads per group);
 //   * online softmax per head over the CTA's keys; P V with each thread owning one head-dim column for
 //     all heads of the group;
@@ -20,8 +20,16 @@
 namespace vo {
 namespace {
 
-constexpr int kTile = 64;
+constexpr int kTile = 32;  // keys per tile; tiles are double-buffered
 constexpr int kDecThreads = 128;
+
+// 16-byte asynchronous global -> shared copy; valid == false fills the 16 bytes with zeros
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(valid ? 16 : 0));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
 
 // N consecutive bf16 values (N in {1, 2, 4, 8}, N-element aligned) -> fp32
 template <int N>
@@ -57,8 +65,8 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
     float* __restrict__ part_o,               // [B, Hk, splits, REP, HD]
     float* __restrict__ part_ml) {            // [B, Hk, splits, REP, 2]
   constexpr int ROW = HD + 8;  // padded smem row (bf16 elements)
-  __shared__ __align__(16) __nv_bfloat16 ks[kTile * ROW];
-  __shared__ __align__(16) __nv_bfloat16 vs[kTile * HD];
+  __shared__ __align__(16) __nv_bfloat16 ks_buf[2][kTile * ROW];
+  __shared__ __align__(16) __nv_bfloat16 vs_buf[2][kTile * HD];
   __shared__ __align__(16) float qs[REP * HD];
   __shared__ float ps[REP * kTile];
   __shared__ float mrow[REP], lrow[REP], alpha_s[REP];
@@ -87,26 +95,36 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
   const int64_t kvbase = ((int64_t)b * Hk + kh) * Lmax * HD;
   __syncthreads();
 
-  for (int t0 = s0; t0 < s1; t0 += kTile) {
+  // stage K (padded rows) and V of the tile at t0 into buffer buf: asynchronous copies, zero-filled past
+  // the slice end, so the next tile's loads are in flight while the current tile is consumed
+  auto stage = [&](int t0, int buf) {
     const int nk = min(kTile, s1 - t0);
-    // stage K (padded rows) and V
     for (int i = tid; i < kTile * (HD / 8); i += kDecThreads) {
       const int r = i / (HD / 8), c = i % (HD / 8);
-      bf16x8 kv = {}, vv = {};
+      int64_t off = 0;  // rows past the slice: zero fill, the source address is only a valid placeholder
       if (r < nk) {
         const int t = t0 + r;
-        int64_t off = kvbase + (int64_t)t * HD;
+        off = kvbase + (int64_t)t * HD;
         if (pt.table) {
           const int blk = __ldg(pt.table + (int64_t)b * pt.stride + t / pt.block);
           off = (((int64_t)blk * Hk + kh) * pt.block + t % pt.block) * HD;
         }
-        kv = reinterpret_cast<const bf16x8*>(kc + off)[c];
-        vv = reinterpret_cast<const bf16x8*>(vc + off)[c];
       }
-      *reinterpret_cast<bf16x8*>(ks + r * ROW + c * 8) = kv;
-      *reinterpret_cast<bf16x8*>(vs + r * HD + c * 8) = vv;
+      cp_async16(ks_buf[buf] + r * ROW + c * 8, kc + off + c * 8, r < nk);
+      cp_async16(vs_buf[buf] + r * HD + c * 8, vc + off + c * 8, r < nk);
     }
-    __syncthreads();
+  };
+  if (s0 < s1) stage(s0, 0);
+  cp_async_commit();
+
+  for (int t0 = s0, it = 0; t0 < s1; t0 += kTile, ++it) {
+    const int nk = min(kTile, s1 - t0);
+    const __nv_bfloat16* ks = ks_buf[it & 1];
+    const __nv_bfloat16* vs = vs_buf[it & 1];
+    if (t0 + kTile < s1) stage(t0 + kTile, (it + 1) & 1);  // that buffer was released by the last barrier
+    cp_async_commit();
+    cp_async_wait1();  // this thread's copies of the current tile have landed
+    __syncthreads();   // ... and every other thread's
     // scores (log2 domain): thread -> key k, heads h0, h0 + HSTEP, ...; each K chunk is read once for
     // all of the thread's heads
     {
@@ -151,14 +169,14 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
     // per-head running max / sum (one warp per head, heads strided over the 4 warps)
     const int warp = tid >> 5, lane = tid & 31;
     for (int h = warp; h < REP; h += kDecThreads / 32) {
-      const float a = ps[h * kTile + lane], c2 = ps[h * kTile + 32 + lane];
+      const float a = ps[h * kTile + lane], c2 = kTile > 32 ? ps[h * kTile + 32 + lane] : -INFINITY;
       const float mx = warp_max(fmaxf(a, c2));
       const float m_old = mrow[h];
       const float m_new = fmaxf(m_old, mx);
       const float e0 = (a == -INFINITY) ? 0.f : exp2f(a - m_new);
       const float e1 = (c2 == -INFINITY) ? 0.f : exp2f(c2 - m_new);
       ps[h * kTile + lane] = e0;
-      ps[h * kTile + 32 + lane] = e1;
+      if (kTile > 32) ps[h * kTile + 32 + lane] = e1;
       const float sum = warp_sum(e0 + e1);
       if (lane == 0) {
         const float al = (m_old == -INFINITY) ? 0.f : exp2f(m_old - m_new);
