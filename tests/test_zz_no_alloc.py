@@ -1,7 +1,7 @@
 """Allocation-free SDE-step entry point, called through its exported C symbol.
 
-Some callers of this library cannot allocate device memory (a CUDA graph being captured, an
-allocator callback, a host with a fixed memory budget, a plain C program without PyTorch's
+Some callers of this library cannot allocate device memory (an allocator callback, which would
+re-enter the allocator; a host with a fixed memory budget; a plain C program without PyTorch's
 allocator).  ``vo_sde_step_fwd_noalloc`` serves them with a fixed device array for its partial sums.
 This test checks it against the allocating entry point on two consecutive calls.  The file name
 makes pytest collect it last.
@@ -59,7 +59,10 @@ def test_noalloc_matches_allocating_entry_point(mode):
         torch.testing.assert_close(mean, ref_mean, rtol=1e-5, atol=1e-5)
         torch.testing.assert_close(lp, ref_lp, rtol=1e-4, atol=1e-3)
         torch.testing.assert_close(std, ref_std, rtol=1e-5, atol=1e-6)
-        if mode != "prev":
+        if mode == "prev":
+            # a distinct prev_out receives a copy of the caller's sample
+            torch.testing.assert_close(out_prev, prev, rtol=0, atol=0)
+        else:
             torch.testing.assert_close(out_prev, ref_prev, rtol=1e-4, atol=1e-4)
 
 
@@ -69,6 +72,20 @@ def test_noalloc_rejects_oversized_problem():
     # 100000 rows need at least 100000 partial-sum slots, more than the fixed scratch holds; every buffer
     # is still sized for the request so nothing could be touched out of bounds
     B, n = 100_000, 4
+    x = torch.zeros(B, n, device="cuda")
+    outs = [torch.empty(B, n, device="cuda") for _ in range(2)]
+    sig = torch.full((B,), 0.5, device="cuda")
+    vec = [torch.empty(B, device="cuda") for _ in range(2)]
+    rc = f(_ptr(x), _ptr(x), _ptr(sig), _ptr(sig * 0.5), None, None, _ptr(outs[0]), _ptr(outs[1]), _ptr(vec[0]),
+           _ptr(vec[1]), B, n, 0.95, 0.7, 0, 1, 0, 1, 1, stream)
+    assert rc == -2
+
+
+def test_noalloc_rejects_too_many_rows_for_the_grid():
+    f = _fn()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    # 65536 rows with one chunk each fit the scratch but not the grid's row dimension
+    B, n = 65536, 1
     x = torch.zeros(B, n, device="cuda")
     outs = [torch.empty(B, n, device="cuda") for _ in range(2)]
     sig = torch.full((B,), 0.5, device="cuda")

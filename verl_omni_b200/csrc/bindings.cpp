@@ -73,7 +73,7 @@ int64_t fmha_error(bool reset);
 void peer_copy(torch::Tensor dst, int64_t src_ptr, int64_t nbytes);
 torch::Tensor slot_sum(torch::Tensor slots, int64_t W, c10::optional<torch::Tensor> bias);
 void peer_row_copy(torch::Tensor src, torch::Tensor src_idx, torch::Tensor dst_rank, torch::Tensor dst_row,
-                   std::vector<int64_t> peers);
+                   std::vector<int64_t> peers, int64_t dst_rows, c10::optional<torch::Tensor> err);
 torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor lens,
                                double scale, int64_t splits, c10::optional<torch::Tensor> block_table);
 void fmha_fwd_peer(torch::Tensor q, torch::Tensor k, torch::Tensor v, std::vector<int64_t> peer_o,
@@ -142,7 +142,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_copy", &vo::peer_copy, "copy-engine read of a peer buffer into a local tensor");
   m.def("slot_sum", &vo::slot_sum, "sum of W bf16 partial-sum slots (+ bias), fp32 accumulation",
         py::arg("slots"), py::arg("W"), py::arg("bias") = py::none());
-  m.def("peer_row_copy", &vo::peer_row_copy, "row copies into peer GPUs' buffers (expert-parallel exchange)");
+  m.def("peer_row_copy", &vo::peer_row_copy, "row copies into peer GPUs' buffers (expert-parallel exchange)",
+        py::arg("src"), py::arg("src_idx"), py::arg("dst_rank"), py::arg("dst_row"), py::arg("peers"),
+        py::arg("dst_rows"), py::arg("err") = py::none());
   m.def("decode_attention", &vo::decode_attention,
         "grouped-query decode attention over a contiguous or paged (block table) KV cache", py::arg("q"),
         py::arg("k_cache"), py::arg("v_cache"), py::arg("lens"), py::arg("scale"), py::arg("splits"),

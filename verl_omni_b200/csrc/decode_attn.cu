@@ -52,7 +52,8 @@ __device__ __forceinline__ void load_row(const __nv_bfloat16* p, float* f) {
 struct PageTable {
   const int* table;  // [B, stride] block ids, null: contiguous [B, Hk, Lmax, HD] cache
   int stride;
-  int block;  // rows per block
+  int block;    // rows per block
+  int nblocks;  // blocks in the pool: a table entry outside [0, nblocks) reads as zeros
 };
 
 template <int HD, int REP>
@@ -73,7 +74,9 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
 
   const int bk = blockIdx.x, split = blockIdx.y;
   const int b = bk / Hk, kh = bk % Hk;
-  const int L = lens[b];
+  // lengths beyond the cache (or beyond the block table's reach) are clamped, so a bad length never reads
+  // past the cache
+  const int L = max(0, min(lens[b], pt.table ? pt.stride * pt.block : Lmax));
   const int per = (L + splits - 1) / splits;
   const int s0 = split * per, s1 = min(L, s0 + per);
   const int tid = threadIdx.x;
@@ -102,16 +105,18 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
     for (int i = tid; i < kTile * (HD / 8); i += kDecThreads) {
       const int r = i / (HD / 8), c = i % (HD / 8);
       int64_t off = 0;  // rows past the slice: zero fill, the source address is only a valid placeholder
-      if (r < nk) {
+      bool ok = r < nk;
+      if (ok) {
         const int t = t0 + r;
         off = kvbase + (int64_t)t * HD;
         if (pt.table) {
           const int blk = __ldg(pt.table + (int64_t)b * pt.stride + t / pt.block);
-          off = (((int64_t)blk * Hk + kh) * pt.block + t % pt.block) * HD;
+          ok = blk >= 0 && blk < pt.nblocks;  // out-of-pool block ids read as zeros
+          off = ok ? (((int64_t)blk * Hk + kh) * pt.block + t % pt.block) * HD : 0;
         }
       }
-      cp_async16(ks_buf[buf] + r * ROW + c * 8, kc + off + c * 8, r < nk);
-      cp_async16(vs_buf[buf] + r * HD + c * 8, vc + off + c * 8, r < nk);
+      cp_async16(ks_buf[buf] + r * ROW + c * 8, kc + off + c * 8, ok);
+      cp_async16(vs_buf[buf] + r * HD + c * 8, vc + off + c * 8, ok);
     }
   };
   if (s0 < s1) stage(s0, 0);
@@ -279,7 +284,8 @@ void launch_decode(const torch::Tensor& q, const torch::Tensor& kc, const torch:
 
 // q [B, Hq, HD] bf16; k_cache / v_cache [B, Hk, Lmax, HD] bf16 -- or, with block_table [B, max_blocks]
 // int32, block pools [blocks, Hk, block, HD]; lens [B] int32 (valid rows, >= 1; with a table at most
-// max_blocks x block).  Returns o [B, Hq, HD].  Hq = Hk x rep with rep in {1, 2, 4, 8}; HD in {64, 128}.
+// max_blocks x block; longer lengths are clamped to the cache, table ids outside the pool read as zeros).
+// Returns o [B, Hq, HD].  Hq = Hk x rep with rep in {1, 2, 4, 8}; HD in {64, 128}.
 torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor lens,
                                double scale, int64_t splits, c10::optional<torch::Tensor> block_table) {
   VO_CHECK_INPUT(q);
@@ -287,10 +293,10 @@ torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Te
   VO_CHECK_INPUT(v_cache);
   VO_CHECK_INPUT(lens);
   TORCH_CHECK(q.scalar_type() == torch::kBFloat16 && k_cache.scalar_type() == torch::kBFloat16 &&
-                  lens.scalar_type() == torch::kInt32,
+                  v_cache.scalar_type() == torch::kBFloat16 && lens.scalar_type() == torch::kInt32,
               "bf16 q / cache, int32 lengths");
   const int64_t B = q.size(0), Hq = q.size(1), HD = q.size(2), Hk = k_cache.size(1);
-  PageTable pt{nullptr, 0, 0};
+  PageTable pt{nullptr, 0, 0, 0};
   if (block_table.has_value() && block_table->defined()) {
     VO_CHECK_INPUT(*block_table);
     TORCH_CHECK(block_table->scalar_type() == torch::kInt32 && block_table->dim() == 2 && block_table->size(0) == B,
@@ -298,6 +304,7 @@ torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Te
     pt.table = block_table->data_ptr<int>();
     pt.stride = (int)block_table->size(1);
     pt.block = (int)k_cache.size(2);
+    pt.nblocks = (int)k_cache.size(0);
     TORCH_CHECK(pt.block > 0, "empty blocks");
   } else {
     TORCH_CHECK(k_cache.size(0) == B, "one cache row per sequence");

@@ -17,14 +17,23 @@ struct PeerTable {
   __nv_bfloat16* ptr[kMaxRanks];
 };
 
+// A map entry whose source row, destination rank or destination row is out of range is skipped (never
+// stored through) and counted in *err, which the host checks after the exchange.
 __global__ void peer_row_copy_kernel(const __nv_bfloat16* __restrict__ src, const int64_t* __restrict__ src_idx,
                                      const int* __restrict__ dst_rank, const int64_t* __restrict__ dst_row,
-                                     PeerTable peers, int64_t n, int vecs) {
+                                     PeerTable peers, int npeers, int64_t src_rows, int64_t dst_rows, int64_t n,
+                                     int vecs, int* __restrict__ err) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   for (int64_t i = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < n; i += warps) {
-    const bf16x8* s = reinterpret_cast<const bf16x8*>(src) + src_idx[i] * vecs;
-    bf16x8* d = reinterpret_cast<bf16x8*>(peers.ptr[dst_rank[i]]) + dst_row[i] * vecs;
+    const int64_t si = src_idx[i], di = dst_row[i];
+    const int dr = dst_rank[i];
+    if (si < 0 || si >= src_rows || dr < 0 || dr >= npeers || di < 0 || di >= dst_rows) {
+      if (lane == 0 && err) atomicAdd(err, 1);
+      continue;
+    }
+    const bf16x8* s = reinterpret_cast<const bf16x8*>(src) + si * vecs;
+    bf16x8* d = reinterpret_cast<bf16x8*>(peers.ptr[dr]) + di * vecs;
     for (int v = lane; v < vecs; v += 32) d[v] = s[v];
   }
 }
@@ -91,9 +100,10 @@ void peer_copy(torch::Tensor dst, int64_t src_ptr, int64_t nbytes) {
 }
 
 // src [N, D] bf16; src_idx int64 [n]; dst_rank int32 [n] (< number of peers); dst_row int64 [n];
-// peers: data pointers of each rank's [rows, D] bf16 buffer (this rank's own included).
+// peers: data pointers of each rank's [dst_rows, D] bf16 buffer (this rank's own included).  Entries out of
+// range are skipped and counted into err (int32 [1] on the device) when it is given.
 void peer_row_copy(torch::Tensor src, torch::Tensor src_idx, torch::Tensor dst_rank, torch::Tensor dst_row,
-                   std::vector<int64_t> peers) {
+                   std::vector<int64_t> peers, int64_t dst_rows, c10::optional<torch::Tensor> err) {
   VO_CHECK_INPUT(src);
   VO_CHECK_INPUT(src_idx);
   VO_CHECK_INPUT(dst_rank);
@@ -104,19 +114,27 @@ void peer_row_copy(torch::Tensor src, torch::Tensor src_idx, torch::Tensor dst_r
                   dst_rank.numel() == dst_row.numel(),
               "row maps: int64 source rows, int32 ranks, int64 destination rows of one length");
   TORCH_CHECK(!peers.empty() && peers.size() <= (size_t)kMaxRanks, "1..8 destination buffers");
+  TORCH_CHECK(dst_rows >= 0, "destination capacity in rows");
+  int* errp = nullptr;
+  if (err.has_value() && err->defined()) {
+    VO_CHECK_INPUT(*err);
+    TORCH_CHECK(err->scalar_type() == torch::kInt32 && err->numel() >= 1, "int32 error counter");
+    errp = err->data_ptr<int>();
+  }
   const int64_t n = src_idx.numel();
   if (n == 0) return;
   c10::cuda::CUDAGuard g(src.device());
   PeerTable t{};
   for (size_t i = 0; i < peers.size(); ++i) {
-    TORCH_CHECK(peers[i] % 16 == 0, "destination buffers must be 16-byte aligned");
+    TORCH_CHECK(peers[i] != 0 && peers[i] % 16 == 0, "destination buffers must be non-null and 16-byte aligned");
     t.ptr[i] = reinterpret_cast<__nv_bfloat16*>(peers[i]);
   }
   const int vecs = (int)(src.size(1) / 8);
   const int grid = (int)std::min<int64_t>((n + 7) / 8, 8LL * num_sms());
   peer_row_copy_kernel<<<grid, 256, 0, stream()>>>(reinterpret_cast<const __nv_bfloat16*>(src.data_ptr<at::BFloat16>()),
                                                   src_idx.data_ptr<int64_t>(), dst_rank.data_ptr<int>(),
-                                                  dst_row.data_ptr<int64_t>(), t, n, vecs);
+                                                  dst_row.data_ptr<int64_t>(), t, (int)peers.size(), src.size(0),
+                                                  dst_rows, n, vecs, errp);
   count_launch();
   VO_CUDA_OK(cudaGetLastError());
 }

@@ -12,6 +12,9 @@
 #include "common.cuh"
 #include "sde_noalloc.h"
 
+#include <atomic>
+#include <mutex>
+
 namespace vo {
 namespace {
 
@@ -237,6 +240,7 @@ std::vector<torch::Tensor> sde_step_fwd(torch::Tensor x, torch::Tensor v, torch:
   TORCH_CHECK(x.sizes() == v.sizes(), "sample/model_output shape mismatch");
   c10::cuda::CUDAGuard g(x.device());
   const int B = x.size(0);
+  TORCH_CHECK(B >= 1 && B <= 65535, "sde_step_fwd: 1..65535 rows (one grid row per sample)");
   const int64_t n = x.numel() / B;
   auto mean = torch::empty_like(x);
   torch::Tensor prev_out;
@@ -319,8 +323,11 @@ static __device__ __align__(256) float g_sde_noalloc_partials[VO_SDE_NOALLOC_MAX
 
 namespace {
 constexpr int kMaxDevices = 64;
-float* g_sde_noalloc_ptr[kMaxDevices] = {nullptr};
+// per-device scratch address and SM count; the set-up runs once per device under a mutex and publishes
+// the pointer (release) only after the SM count is stored
+std::atomic<float*> g_sde_noalloc_ptr[kMaxDevices];
 int g_sde_noalloc_sms[kMaxDevices] = {0};
+std::mutex g_sde_noalloc_mu;
 }  // namespace
 
 extern "C" __attribute__((visibility("default"))) int vo_sde_step_fwd_noalloc(
@@ -331,21 +338,25 @@ extern "C" __attribute__((visibility("default"))) int vo_sde_step_fwd_noalloc(
   if (!x || !v || !sigma || !sigma_prev || !mean_out || !std_out || B <= 0 || n <= 0 || sde_type < 0 ||
       sde_type > 2 || (want_logp && !logp_out) || (!prev_in && !prev_out))
     return -1;
+  if (B > 65535) return -2;  // one grid row per sample
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return (int)e;
   if (dev < 0 || dev >= kMaxDevices) return -1;
-  if (!g_sde_noalloc_ptr[dev]) {  // one-time set-up per device, with that device current
-    void* ptr = nullptr;
-    e = cudaGetSymbolAddress(&ptr, g_sde_noalloc_partials);
-    if (e != cudaSuccess) return (int)e;
-    int sms = 0;
-    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return (int)e;
-    g_sde_noalloc_sms[dev] = sms;
-    g_sde_noalloc_ptr[dev] = static_cast<float*>(ptr);
+  if (!g_sde_noalloc_ptr[dev].load(std::memory_order_acquire)) {  // one-time set-up, this device current
+    std::lock_guard<std::mutex> lock(g_sde_noalloc_mu);
+    if (!g_sde_noalloc_ptr[dev].load(std::memory_order_relaxed)) {
+      void* ptr = nullptr;
+      e = cudaGetSymbolAddress(&ptr, g_sde_noalloc_partials);
+      if (e != cudaSuccess) return (int)e;
+      int sms = 0;
+      e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (e != cudaSuccess) return (int)e;
+      g_sde_noalloc_sms[dev] = sms;
+      g_sde_noalloc_ptr[dev].store(static_cast<float*>(ptr), std::memory_order_release);
+    }
   }
-  float* partial = g_sde_noalloc_ptr[dev];
+  float* partial = g_sde_noalloc_ptr[dev].load(std::memory_order_acquire);
   // same chunking as the allocating entry point: ~4 blocks per SM, chunks of multiples of 1024
   const int target = 4 * g_sde_noalloc_sms[dev];
   int nchunks = (int)std::max<int64_t>(1, std::min<int64_t>((n + 1023) / 1024, (target + B - 1) / B));
@@ -369,5 +380,12 @@ extern "C" __attribute__((visibility("default"))) int vo_sde_step_fwd_noalloc(
   vo::sde_finalize_kernel<<<(B + 7) / 8, 256, 0, stream>>>(partial, sigma, sigma_prev, want_logp ? logp_out : nullptr,
                                                            std_out, B, nchunks, n, sigma_max, eta, sde_type,
                                                            norm != 0);
-  return (int)cudaGetLastError();
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return (int)e;
+  // a caller-provided sample is also copied to a distinct prev_out (a device-to-device copy allocates nothing)
+  if (prev_in && prev_out && prev_out != prev_in) {
+    e = cudaMemcpyAsync(prev_out, prev_in, (size_t)B * (size_t)n * sizeof(float), cudaMemcpyDeviceToDevice, stream);
+    if (e != cudaSuccess) return (int)e;
+  }
+  return 0;
 }

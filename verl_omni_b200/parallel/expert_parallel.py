@@ -161,7 +161,7 @@ class _FusedEP(torch.autograd.Function):
         xv = xd.tensor.view(cap, D)
         if plan["pad_rows"].numel():
             xv.index_fill_(0, plan["pad_rows"], 0)
-        e_.peer_row_copy(h.contiguous(), tok_s, dst_rank, dst_row, xd.peer_ptrs)
+        e_.peer_row_copy(h.contiguous(), tok_s, dst_rank, dst_row, xd.peer_ptrs, cap)
         ep.barrier(dev)
         R = L.R
         wgu_l, wd_l = w_gate_up[r * El:(r + 1) * El], w_down[r * El:(r + 1) * El]
@@ -176,7 +176,7 @@ class _FusedEP(torch.autograd.Function):
         # combine: every expert output row back to the slot of the rank that routed it
         yc = ep.buf("y", pcap * D, dev)
         if R:
-            e_.peer_row_copy(y, plan["own_rows"], plan["own_rank"], plan["own_slot"], yc.peer_ptrs)
+            e_.peer_row_copy(y, plan["own_rows"], plan["own_rank"], plan["own_slot"], yc.peer_ptrs, pcap)
         ep.barrier(dev)
         P = order.numel()
         ys = yc.tensor.view(pcap, D)[:P].clone()
@@ -208,7 +208,7 @@ class _FusedEP(torch.autograd.Function):
         if plan["pad_rows"].numel():
             dv.index_fill_(0, plan["pad_rows"], 0)
         e_.peer_row_copy(dy_slot, torch.arange(order.numel(), device=dev), plan["dst_rank"], plan["dst_row"],
-                         db.peer_ptrs)
+                         db.peer_ptrs, cap)
         ep.barrier(dev)
         gwgu = torch.zeros(w_gate_up.shape, device=dev, dtype=torch.float32)
         gwd = torch.zeros(w_down.shape, device=dev, dtype=torch.float32)
@@ -224,7 +224,7 @@ class _FusedEP(torch.autograd.Function):
             e_.moe_gemm_wgrad(dgu, x_own, plan["seg"], gwgu[r * El:(r + 1) * El], True)
         xb = ep.buf("y", pcap * D, dev)
         if R:
-            e_.peer_row_copy(dx, plan["own_rows"], plan["own_rank"], plan["own_slot"], xb.peer_ptrs)
+            e_.peer_row_copy(dx, plan["own_rows"], plan["own_rank"], plan["own_slot"], xb.peer_ptrs, pcap)
         ep.barrier(dev)
         dxs = xb.tensor.view(pcap, D)[:order.numel()]
         dh = torch.zeros(T, D, device=dev, dtype=dout.dtype).index_add(0, tok_s, dxs)
