@@ -58,3 +58,31 @@ def test_device_sampler_distribution_and_logprobs():
     ids, _ = sample_tokens(logits, 1.0, 5, 1.0, g)  # top-k keeps the 5 largest
     top5 = torch.topk(logits, 5, -1).indices
     assert bool((top5 == ids[:, None]).any(-1).all())
+
+
+def test_decode_attention_clamps_lengths_and_block_ids():
+    """A length beyond the cache reads as the full cache; a paged table id outside the pool reads zeros."""
+    from verl_omni_b200.ops._ext import ext
+    from verl_omni_b200.ops.decode import decode_attention_reference
+
+    torch.manual_seed(0)
+    B, Hk, rep, hd, Lmax = 2, 2, 4, 64, 96
+    q = torch.randn(B, Hk * rep, hd, device="cuda").bfloat16()
+    kc = torch.randn(B, Hk, Lmax, hd, device="cuda").bfloat16()
+    vc = torch.randn(B, Hk, Lmax, hd, device="cuda").bfloat16()
+    too_long = torch.tensor([Lmax + 50, 10 ** 6], dtype=torch.int32, device="cuda")
+    full = torch.full((B,), Lmax, dtype=torch.int32, device="cuda")
+    out = ext().decode_attention(q, kc, vc, too_long, hd ** -0.5, 2, None)
+    ref = decode_attention_reference(q, kc, vc, full, hd ** -0.5)
+    torch.testing.assert_close(out.float(), ref.float(), rtol=2e-2, atol=2e-2)
+    # paged: block 1 of sequence 0 names a block past the pool -> its keys score 0 and its values are 0
+    bs, nb = 16, 4
+    kp = torch.randn(nb, Hk, bs, hd, device="cuda").bfloat16()
+    vp = torch.randn(nb, Hk, bs, hd, device="cuda").bfloat16()
+    table = torch.tensor([[0, 999], [2, 3]], dtype=torch.int32, device="cuda")
+    lens = torch.tensor([2 * bs, 2 * bs], dtype=torch.int32, device="cuda")
+    out = ext().decode_attention(q, kp, vp, lens, hd ** -0.5, 1, table)
+    k0 = torch.cat([kp[0], torch.zeros_like(kp[0])], 1)[None]
+    v0 = torch.cat([vp[0], torch.zeros_like(vp[0])], 1)[None]
+    ref0 = decode_attention_reference(q[:1], k0, v0, lens[:1], hd ** -0.5)
+    torch.testing.assert_close(out[:1].float(), ref0.float(), rtol=2e-2, atol=2e-2)

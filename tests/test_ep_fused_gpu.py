@@ -47,3 +47,4 @@ def _run(rank, world):
 
 def test_fused_expert_parallel_matches_nccl_ep2():
     run_ranks(_run, 2, device="cuda")
+

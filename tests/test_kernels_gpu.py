@@ -304,3 +304,108 @@ def test_wan_dit_gpu_matches_cpu():
     torch.testing.assert_close(out.float().cpu(), ref, rtol=5e-2, atol=5e-2)
     out.float().square().mean().backward()
     assert all(torch.isfinite(p.grad).all() for p in mg.parameters() if p.grad is not None)
+
+
+def test_peer_row_copy_skips_out_of_range_rows():
+    """One GPU, this rank's own buffer as the only peer: rows whose destination rank, destination row or
+    source row is out of range are skipped and counted; the others land."""
+    from verl_omni_b200.ops._ext import ext
+
+    D, R = 64, 8
+    src = torch.randn(5, D, device="cuda").bfloat16()
+    dst = torch.zeros(R, D, device="cuda").bfloat16()
+    src_idx = torch.tensor([0, 1, 2, 3, 7], dtype=torch.int64, device="cuda")
+    dst_rank = torch.tensor([0, 1, 0, 0, 0], dtype=torch.int32, device="cuda")
+    dst_row = torch.tensor([2, 3, 5, R + 4, 1], dtype=torch.int64, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ext().peer_row_copy(src, src_idx, dst_rank, dst_row, [dst.data_ptr()], R, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 3  # rank 1 absent, row R + 4 past the buffer, source row 7 past src
+    exp = torch.zeros_like(dst)
+    exp[2], exp[5] = src[0], src[2]
+    assert torch.equal(dst, exp)
+
+
+@pytest.mark.parametrize("V,chunk", [(151936, 32768), (5000, 1024)])
+def test_chunked_vocab_logprob_matches_fp32(V, chunk):
+    """tcgen05 GEMM chunks + online log-sum-exp kernel against an fp32 log_softmax over bf16 logits; the
+    backward's hidden-state gradient and the weight gradient accumulated into main_grad."""
+    from verl_omni_b200.ops.vocab_logprob import token_logprobs_from_hidden
+
+    torch.manual_seed(0)
+    N, D, T = 384, 256, 0.9
+    h = (torch.randn(N, D, device="cuda") * 0.5).bfloat16().requires_grad_(True)
+    w = (torch.randn(V, D, device="cuda") * 0.05).bfloat16().requires_grad_(True)
+    w.main_grad = torch.zeros(V, D, device="cuda")
+    t = torch.randint(0, V, (N,), device="cuda")
+    lp = token_logprobs_from_hidden(h, w, t, T, chunk=chunk)
+    z = (h.float() @ w.float().t()).bfloat16().float() / T
+    ref = torch.log_softmax(z, -1).gather(1, t[:, None])[:, 0]
+    torch.testing.assert_close(lp, ref, rtol=1e-3, atol=2e-3)
+    g = torch.randn(N, device="cuda")
+    (lp * g).sum().backward()
+    hr = h.detach().float().requires_grad_(True)
+    wr = w.detach().float().requires_grad_(True)
+    rr = torch.log_softmax((hr @ wr.t()) / T, -1).gather(1, t[:, None])[:, 0]
+    (rr * g).sum().backward()
+    rel = lambda a, b: float((a.float() - b).norm() / (b.norm() + 1e-12))  # noqa: E731
+    assert rel(h.grad, hr.grad) < 2e-2
+    assert rel(w.main_grad, wr.grad) < 2e-2
+
+
+def test_llm_row_ops_match_fp32():
+    """RMSNorm, SwiGLU, router top-k and per-head q/k RMSNorm + RoPE kernels (forward and backward) against
+    fp32 torch."""
+    from verl_omni_b200.models.layers import rope_table
+    from verl_omni_b200.ops import llm
+
+    torch.manual_seed(0)
+    rel = lambda a, b: float((a.float() - b.float()).norm() / (b.float().norm() + 1e-12))  # noqa: E731
+    # RMSNorm
+    x = torch.randn(300, 2048, device="cuda").bfloat16().requires_grad_(True)
+    w = (1 + 0.1 * torch.randn(2048, device="cuda")).bfloat16().requires_grad_(True)
+    y = llm.rms_norm(x, w, 1e-6)
+    xr, wr = x.detach().float().requires_grad_(True), w.detach().float().requires_grad_(True)
+    yr = xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + 1e-6) * wr
+    assert rel(y, yr) < 1e-2
+    g = torch.randn_like(yr)
+    y.backward(g.bfloat16())
+    yr.backward(g)
+    assert rel(x.grad, xr.grad) < 2e-2 and rel(w.grad, wr.grad) < 2e-2
+    # SwiGLU
+    gu = torch.randn(257, 2 * 768, device="cuda").bfloat16().requires_grad_(True)
+    a = llm.swiglu(gu)
+    gr = gu.detach().float().requires_grad_(True)
+    g_, u_ = gr.chunk(2, -1)
+    ar = torch.nn.functional.silu(g_) * u_
+    assert rel(a, ar) < 1e-2
+    da = torch.randn_like(ar)
+    a.backward(da.bfloat16())
+    ar.backward(da)
+    assert rel(gu.grad, gr.grad) < 2e-2
+    # router
+    logits = torch.randn(1000, 128, device="cuda", requires_grad=True)
+    gates, idx, probs = llm.router_topk(logits, 8)
+    lr = logits.detach().clone().requires_grad_(True)
+    pr = torch.softmax(lr, -1)
+    gv, ir = torch.topk(pr, 8, -1)
+    gvr = gv / gv.sum(-1, keepdim=True)
+    assert torch.equal(idx, ir)
+    torch.testing.assert_close(gates, gvr, rtol=1e-5, atol=1e-6)
+    dg = torch.randn_like(gvr)
+    gates.backward(dg)
+    gvr.backward(dg)
+    torch.testing.assert_close(logits.grad, lr.grad, rtol=1e-4, atol=1e-6)
+    # per-head norm + RoPE over a column slice of a projection output
+    B, S, H, Dh = 2, 77, 4, 128
+    proj = torch.randn(B, S, (H + 2) * Dh, device="cuda").bfloat16().requires_grad_(True)
+    wn = (1 + 0.1 * torch.randn(Dh, device="cuda")).bfloat16().requires_grad_(True)
+    cos, sin = (t.cuda() for t in rope_table(torch.arange(S), Dh, 1e6))
+    out = llm.head_norm_rope(proj, Dh, H, wn, cos, sin)
+    pr2, wr2 = proj.detach().float().requires_grad_(True), wn.detach().float().requires_grad_(True)
+    ref = llm.head_norm_rope_reference(pr2[..., Dh:Dh + H * Dh].reshape(B, S, H, Dh), wr2, cos, sin, 1e-6)
+    assert rel(out, ref) < 1e-2
+    go = torch.randn_like(ref)
+    out.backward(go.bfloat16())
+    ref.backward(go)
+    assert rel(proj.grad, pr2.grad) < 2e-2 and rel(wn.grad, wr2.grad) < 2e-2

@@ -124,3 +124,56 @@ def _ep_check(rank, world):
 
 def test_expert_parallel_ep2_gloo():
     run_ranks(_ep_check, 2)
+
+
+def test_chunked_vocab_logprob_matches_full_log_softmax():
+    """Chunked log-sum-exp over the vocabulary (chunk not dividing V) equals log_softmax().gather, values and
+    gradients of the hidden states and head weight."""
+    from verl_omni_b200.ops.vocab_logprob import token_logprobs_from_hidden
+
+    torch.manual_seed(0)
+    N, D, V, T = 37, 16, 1000, 0.7
+    h = torch.randn(N, D, requires_grad=True)
+    w = torch.randn(V, D, requires_grad=True)
+    t = torch.randint(0, V, (N,))
+    lp = token_logprobs_from_hidden(h, w, t, T, chunk=96)
+    ref = torch.log_softmax((h @ w.t()) / T, -1).gather(1, t[:, None])[:, 0]
+    torch.testing.assert_close(lp, ref, rtol=1e-5, atol=1e-5)
+    g = torch.randn(N)
+    gh, gw = torch.autograd.grad((lp * g).sum(), (h, w))
+    rh, rw = torch.autograd.grad((ref * g).sum(), (h, w))
+    torch.testing.assert_close(gh, rh, rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(gw, rw, rtol=1e-4, atol=1e-5)
+
+
+def _omni_ep_step(rank, world, outdir, ep):
+    import torch.distributed as dist
+
+    from verl_omni_b200.models.moe_llm import MoEConfig
+    from verl_omni_b200.trainer.omni.omni_trainer import OmniGRPOTrainer
+    from verl_omni_b200.workers.config.diffusion import DiffusionActorConfig
+
+    ac = DiffusionActorConfig()
+    ac.optim.lr = 1e-3
+    t = OmniGRPOTrainer(MoEConfig.tiny(), ac, device=torch.device("cpu"), n=4,
+                        ep_group=dist.group.WORLD if ep > 1 else None)
+    blk = t.model.layers[0]
+    m = t.step(num_prompts=2)
+    torch.save({"wgu": blk.w_gate_up.detach().clone(), "e0": blk.e0, "loss": m["actor/pg_loss"],
+                "n_expert_params": sum(p.numel() for p in t.model.parameters() if getattr(p, "_vo_expert", False)),
+                "gn": m["actor/grad_norm"]}, f"{outdir}/ep{ep}_r{rank}.pt")
+
+
+def test_expert_sharded_grpo_step_matches_unsharded(tmp_path):
+    """Two gloo ranks, same data: with EP=2 each rank holds half of every layer's experts (weights, grads,
+    optimizer state) and one GRPO step leaves them equal to the matching slices of the replicated-expert
+    (data-parallel only) step."""
+    run_ranks(_omni_ep_step, 2, (str(tmp_path), 1))
+    run_ranks(_omni_ep_step, 2, (str(tmp_path), 2))
+    full = torch.load(tmp_path / "ep1_r0.pt")
+    E = full["wgu"].shape[0]
+    for r in range(2):
+        part = torch.load(tmp_path / f"ep2_r{r}.pt")
+        assert part["wgu"].shape[0] == E // 2 and part["e0"] == r * E // 2
+        assert part["n_expert_params"] > 0
+        torch.testing.assert_close(part["wgu"], full["wgu"][r * E // 2:(r + 1) * E // 2], rtol=1e-3, atol=5e-5)

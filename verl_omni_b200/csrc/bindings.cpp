@@ -74,10 +74,25 @@ void peer_copy(torch::Tensor dst, int64_t src_ptr, int64_t nbytes);
 torch::Tensor slot_sum(torch::Tensor slots, int64_t W, c10::optional<torch::Tensor> bias);
 void peer_row_copy(torch::Tensor src, torch::Tensor src_idx, torch::Tensor dst_rank, torch::Tensor dst_row,
                    std::vector<int64_t> peers, int64_t dst_rows, c10::optional<torch::Tensor> err);
+void vocab_lse_update(torch::Tensor logits, int64_t lo, torch::Tensor targets, double inv_t, torch::Tensor m,
+                      torch::Tensor s, torch::Tensor t);
+void vocab_lse_grad(torch::Tensor logits, int64_t lo, torch::Tensor targets, double inv_t, torch::Tensor lse,
+                    torch::Tensor g);
+std::vector<torch::Tensor> rms_norm_fwd(torch::Tensor x, torch::Tensor w, double eps);
+torch::Tensor rms_norm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw,
+                           bool accumulate);
+torch::Tensor swiglu_fwd(torch::Tensor gu);
+torch::Tensor swiglu_bwd(torch::Tensor da, torch::Tensor gu);
+std::vector<torch::Tensor> router_topk(torch::Tensor logits, int64_t K);
+torch::Tensor head_rmsnorm_rope(torch::Tensor x, int64_t col0, int64_t H, torch::Tensor w, torch::Tensor cos_t,
+                                torch::Tensor sin_t, double eps);
+torch::Tensor head_rmsnorm_rope_bwd(torch::Tensor dy, torch::Tensor x, int64_t col0, int64_t H, torch::Tensor w,
+                                    torch::Tensor cos_t, torch::Tensor sin_t, double eps, torch::Tensor dw);
 torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor lens,
                                double scale, int64_t splits, c10::optional<torch::Tensor> block_table);
 void fmha_fwd_peer(torch::Tensor q, torch::Tensor k, torch::Tensor v, std::vector<int64_t> peer_o,
-                   std::vector<int64_t> peer_o2, int64_t sl, int64_t si, int64_t htot, int64_t h0, double scale);
+                   std::vector<int64_t> peer_o2, int64_t sl, int64_t si, int64_t htot, int64_t h0, double scale,
+                   int64_t version);
 std::vector<torch::Tensor> linear_bwd_prep(torch::Tensor dy, c10::optional<torch::Tensor> saved,
                                            c10::optional<torch::Tensor> gate, int64_t S, int64_t mode,
                                            c10::optional<torch::Tensor> db, bool db_accumulate);
@@ -145,11 +160,22 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_row_copy", &vo::peer_row_copy, "row copies into peer GPUs' buffers (expert-parallel exchange)",
         py::arg("src"), py::arg("src_idx"), py::arg("dst_rank"), py::arg("dst_row"), py::arg("peers"),
         py::arg("dst_rows"), py::arg("err") = py::none());
+  m.def("vocab_lse_update", &vo::vocab_lse_update, "online log-sum-exp + target logit over one vocabulary chunk");
+  m.def("vocab_lse_grad", &vo::vocab_lse_grad, "in-place d(log p(target)) / d(logits) over one vocabulary chunk");
+  m.def("rms_norm_fwd", &vo::rms_norm_fwd, "row RMSNorm (bf16), returns (y, rstd)");
+  m.def("rms_norm_bwd", &vo::rms_norm_bwd, "row RMSNorm backward: dx, weight grad into fp32 dw");
+  m.def("swiglu_fwd", &vo::swiglu_fwd, "silu(gate) * up over [M, 2F] (gate | up)");
+  m.def("swiglu_bwd", &vo::swiglu_bwd, "SwiGLU backward -> d(gate | up)");
+  m.def("router_topk", &vo::router_topk, "softmax router + top-k with renormalised gates");
+  m.def("head_rmsnorm_rope", &vo::head_rmsnorm_rope, "per-head RMSNorm + rotate-half RoPE, [B,S,H*Dh] -> [B,H,S,Dh]");
+  m.def("head_rmsnorm_rope_bwd", &vo::head_rmsnorm_rope_bwd, "backward of head_rmsnorm_rope");
   m.def("decode_attention", &vo::decode_attention,
         "grouped-query decode attention over a contiguous or paged (block table) KV cache", py::arg("q"),
         py::arg("k_cache"), py::arg("v_cache"), py::arg("lens"), py::arg("scale"), py::arg("splits"),
         py::arg("block_table") = py::none());
-  m.def("fmha_fwd_peer", &vo::fmha_fwd_peer, "Ulysses attention writing each output row to its owner rank");
+  m.def("fmha_fwd_peer", &vo::fmha_fwd_peer, "Ulysses attention writing each output row to its owner rank",
+        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("peer_o"), py::arg("peer_o2"), py::arg("sl"), py::arg("si"),
+        py::arg("htot"), py::arg("h0"), py::arg("scale"), py::arg("version") = 3);
   m.def("fmha_bwd", &vo::fmha_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
         py::arg("dO"), py::arg("causal"), py::arg("scale"), py::arg("version") = 1, py::arg("o2") = py::none(),
         py::arg("dO2") = py::none(), py::arg("split") = 0, py::arg("kv_len") = py::none());

@@ -15,6 +15,12 @@ extern "C" int vo_fmha_fwd3_kvlen(const void* q, const void* k, const void* v, v
 extern "C" int vo_fmha_fwd_peer(const void* q, const void* k, const void* v, void* const* peer_o,
                                 void* const* peer_o2, int nranks, int sl, int si, int htot, int h0, float* lse, int B,
                                 int H, int Sq, int Skv, int D, float scale, cudaStream_t stream);
+extern "C" int vo_fmha_fwd4(const void* q, const void* k, const void* v, void* o, void* o2, int out_split, float* lse,
+                            const int* kv_len, int B, int H, int Sq, int Skv, int D, float scale, int causal,
+                            cudaStream_t stream);
+extern "C" int vo_fmha_fwd4_peer(const void* q, const void* k, const void* v, void* const* peer_o,
+                                 void* const* peer_o2, int nranks, int sl, int si, int htot, int h0, float* lse, int B,
+                                 int H, int Sq, int Skv, int D, float scale, cudaStream_t stream);
 extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const void* o, const void* dO,
                            const void* o2, const void* dO2, int split, const float* lse, void* dq, void* dk, void* dv,
                            float* delta, float* dq_acc, int B, int H, int Sq, int Skv, int D, float scale, int causal,
@@ -25,7 +31,9 @@ namespace vo {
 
 // q [B, H, Sq, D], k/v [B, H, Skv, D] -> (o [B, Sq, H, D], lse [B, H, Sq] fp32[, o2])
 // version 1: one query tile per CTA, P staged in shared memory; version 2: two query tiles per CTA,
-// P and O resident in tensor memory; version 3: as 2 with two softmax warpgroups per query tile.
+// P and O resident in tensor memory; version 3: as 2 with two softmax warpgroups per query tile;
+// version 4: one query tile per CTA, two CTAs per SM, double-buffered 64-key score blocks (key counts
+// and the causal mask both supported).
 // split > 0 (versions 2 / 3): query rows [0, split) go to o [B, split, H, D] and rows [split, Sq) to a
 // second tensor o2 [B, Sq - split, H, D] (the image / text halves of a joint attention, each feeding
 // its own output projection without a copy).
@@ -39,12 +47,22 @@ std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Ten
   const int B = q.size(0), H = q.size(1), Sq = q.size(2), D = q.size(3), Skv = k.size(2);
   TORCH_CHECK(D == 64 || D == 128, "head_dim must be 64 or 128");
   TORCH_CHECK(split >= 0 && split < Sq, "bad output split");
-  TORCH_CHECK(split == 0 || version >= 2, "split outputs need forward version 2 or 3");
+  TORCH_CHECK(split == 0 || version >= 2, "split outputs need forward version 2, 3 or 4");
   auto o = torch::empty({B, split > 0 ? split : Sq, H, D}, q.options());
   torch::Tensor o2 = split > 0 ? torch::empty({B, Sq - split, H, D}, q.options()) : torch::Tensor();
   auto lse = torch::empty({B, H, Sq}, q.options().dtype(torch::kFloat32));
   int rc;
-  if (kv_len.has_value() && kv_len->defined()) {
+  if (version == 4) {
+    const int* kvp = nullptr;
+    if (kv_len.has_value() && kv_len->defined()) {
+      VO_CHECK_INPUT((*kv_len));
+      TORCH_CHECK(kv_len->scalar_type() == torch::kInt32 && kv_len->numel() == B, "int32 [B] key counts");
+      kvp = kv_len->data_ptr<int>();
+    }
+    rc = vo_fmha_fwd4(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), split > 0 ? o2.data_ptr() : nullptr,
+                      (int)split, lse.data_ptr<float>(), kvp, B, H, Sq, Skv, D, (float)scale, causal ? 1 : 0,
+                      stream());
+  } else if (kv_len.has_value() && kv_len->defined()) {
     // per-sequence key counts (right-padded keys masked); non-causal, forward v3
     VO_CHECK_INPUT((*kv_len));
     TORCH_CHECK(kv_len->scalar_type() == torch::kInt32 && kv_len->numel() == B && !causal, "int32 [B] key counts");
@@ -70,7 +88,8 @@ std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Ten
 // each output row is stored into the owning rank's buffer: peer_o[r] [B, si, htot, D] (image rows) or
 // peer_o2[r] [B, sl - si, htot, D] (text rows), this rank's heads at head offset h0.
 void fmha_fwd_peer(torch::Tensor q, torch::Tensor k, torch::Tensor v, std::vector<int64_t> peer_o,
-                   std::vector<int64_t> peer_o2, int64_t sl, int64_t si, int64_t htot, int64_t h0, double scale) {
+                   std::vector<int64_t> peer_o2, int64_t sl, int64_t si, int64_t htot, int64_t h0, double scale,
+                   int64_t version) {
   VO_CHECK_INPUT(q);
   VO_CHECK_INPUT(k);
   VO_CHECK_INPUT(v);
@@ -86,8 +105,9 @@ void fmha_fwd_peer(torch::Tensor q, torch::Tensor k, torch::Tensor v, std::vecto
     if (!peer_o2.empty()) po2[i] = reinterpret_cast<void*>(peer_o2[i]);
   }
   auto lse = torch::empty({B, H, Sq}, q.options().dtype(torch::kFloat32));
-  const int rc = vo_fmha_fwd_peer(q.data_ptr(), k.data_ptr(), v.data_ptr(), po.data(), po2.data(), n, (int)sl, (int)si,
-                                  (int)htot, (int)h0, lse.data_ptr<float>(), B, H, Sq, Skv, D, (float)scale, stream());
+  auto fn = version == 4 ? vo_fmha_fwd4_peer : vo_fmha_fwd_peer;
+  const int rc = fn(q.data_ptr(), k.data_ptr(), v.data_ptr(), po.data(), po2.data(), n, (int)sl, (int)si, (int)htot,
+                    (int)h0, lse.data_ptr<float>(), B, H, Sq, Skv, D, (float)scale, stream());
   TORCH_CHECK(rc == 0, "tcgen05 FMHA (peer output) launch failed: code ", rc);
   count_launch();
 }

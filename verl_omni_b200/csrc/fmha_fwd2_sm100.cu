@@ -708,6 +708,328 @@ __global__ void __launch_bounds__(fwd_threads<SPLIT>(), 1)
   }
 }
 
+
+// ====================================================================================================
+// Forward v4: one 128-row query tile per CTA, two CTAs per SM, 64-key blocks, double-buffered scores.
+//
+// 192 threads: warps 0..3 softmax (one query row per thread, TMEM lane quarter = warp), warp 4 TMA
+// producer, warp 5 TMEM allocator + single-thread MMA issuer.  Tensor memory (256 columns per CTA, so
+// two CTAs share an SM's 512): S buffers [0, 64) and [64, 128), O [128, 128 + D).  The QK^T of key
+// block j + 2 goes into the buffer the softmax of block j has just turned into P, right behind the PV
+// of block j, so the softmax of block j + 1 never waits for the tensor core: its scores were computed
+// while block j was being exponentiated.  The other CTA on the SM supplies the second query tile that
+// keeps the tensor pipe busy while this CTA's softmax runs, and overlaps this CTA's prologue/epilogue.
+// Barriers: s_full[b] / p_full[b] per score buffer (a buffer's phase j >> 1 is block j), o_ready after
+// every PV (the softmax waits on it only to rescale O, or once before the epilogue).
+// A share (6 of 16 pairs) of the exponentials is evaluated on the FMA pipe: 2^x = 2^round(x) * p(f),
+// f = x - round(x) in [-1/2, 1/2], with round() by the 1.5 * 2^23 magic-number addition and p the
+// degree-3 polynomial minimising the relative error of 2^f on [-1/2, 1/2] (Lawson-weighted least
+// squares, max relative error 8.4e-5, far below the bf16 rounding of P); 2^round(x) is an integer add
+// into the exponent field.  The MUFU pipe alone is the bound of the score path at head_dim 64.
+constexpr int FWD4_THREADS = 192;
+constexpr int BK4 = 64;
+
+template <int D>
+struct Cfg4 {
+  static constexpr int Q_BYTES = 128 * D * 2;
+  static constexpr int KV_BYTES = BK4 * D * 2;
+  static constexpr int ST = D == 64 ? 4 : 2;  // K and V stages
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_BYTES;
+  static constexpr int V_OFF = K_OFF + ST * KV_BYTES;
+  static constexpr int BAR_OFF = V_OFF + ST * KV_BYTES;
+  static constexpr int BYTES = BAR_OFF + 256;
+  static_assert(2 * (BYTES + 1024) <= 232448, "two CTAs per SM must fit in shared memory");
+  static constexpr uint32_t O_COL = 128;
+};
+
+__device__ __forceinline__ void fsub2(float a0, float a1, float b0, float b1, float& r0, float& r1) {
+  asm("{\n\t.reg .b64 x, y, r;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+      "sub.rn.f32x2 r, x, y;\n\tmov.b64 {%0, %1}, r;\n\t}"
+      : "=f"(r0), "=f"(r1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void ffma2v(float a0, float a1, float b0, float b1, float c0, float c1, float& r0,
+                                       float& r1) {
+  asm("{\n\t.reg .b64 x, y, z, r;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\tmov.b64 z, {%6, %7};\n\t"
+      "fma.rn.f32x2 r, x, y, z;\n\tmov.b64 {%0, %1}, r;\n\t}"
+      : "=f"(r0), "=f"(r1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+// 2^x0, 2^x1 on the FMA pipe (x <= 2^22; inputs below -126 are clamped: the result is then ~1e-38)
+__device__ __forceinline__ void ex2_fma2(float x0, float x1, float& y0, float& y1) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: adding it rounds to an integer in the low bits
+  x0 = fmaxf(x0, -126.f);
+  x1 = fmaxf(x1, -126.f);
+  float t0 = x0, t1 = x1, r0, r1, f0, f1;
+  fadd2(t0, t1, kMagic, kMagic);            // t = x + magic
+  fsub2(t0, t1, kMagic, kMagic, r0, r1);    // r = round(x)
+  fsub2(x0, x1, r0, r1, f0, f1);            // f in [-1/2, 1/2]
+  float p0, p1;
+  ffma2v(f0, f1, 0.05521300435066223f, 0.05521300435066223f, 0.24271394312381744f, 0.24271394312381744f, p0, p1);
+  ffma2v(p0, p1, f0, f1, 0.6932621598243713f, 0.6932621598243713f, p0, p1);
+  ffma2v(p0, p1, f0, f1, 0.999919593334198f, 0.999919593334198f, p0, p1);
+  // the low 23 bits of t hold round(x) + 2^22 (the magic's mantissa); shifted into the exponent field the
+  // 2^22 part leaves 32 bits, so the integer add scales p by 2^round(x)
+  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+}
+
+template <int D>
+__global__ void __launch_bounds__(FWD4_THREADS, 2)
+    fmha_fwd4_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+                     const __grid_constant__ CUtensorMap mv, const __grid_constant__ Params p) {
+  using C = Cfg4<D>;
+  extern __shared__ __align__(1024) uint8_t raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;           // [ST]
+  uint64_t* k_empty = k_full + C::ST;    // [ST]
+  uint64_t* v_full = k_empty + C::ST;    // [ST]
+  uint64_t* v_empty = v_full + C::ST;    // [ST]
+  uint64_t* s_full = v_empty + C::ST;    // [2] per score buffer
+  uint64_t* p_full = s_full + 2;         // [2]
+  uint64_t* o_ready = p_full + 2;        // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_ready + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // heavier (later) query tiles first under a causal mask
+  const int tile = p.npairs - 1 - (int)(blockIdx.x % p.npairs);
+  const int bh = blockIdx.x / p.npairs;
+  const int q0 = tile * BQ;
+  int kv_end = kv_limit(p, bh);
+  if (p.causal) kv_end = min(kv_end, q0 + BQ);
+  const int nkv = (kv_end + BK4 - 1) / BK4;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < C::ST; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 4);
+    }
+    mbar_init(o_ready, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 5) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(256));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0 && nkv > 0) {
+      mbar_expect_tx(q_full, C::Q_BYTES);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) tma_load_3d(sm + C::Q_OFF + c * 16384, &mq, q_full, c * 64, q0, bh);
+      for (int j = 0; j < nkv; ++j) {
+        const int s = j % C::ST, ph = ((j / C::ST) & 1) ^ 1;
+        if (!mbar_wait(&k_empty[s], ph, abort_flag, 61)) break;
+        mbar_expect_tx(&k_full[s], C::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_3d(sm + C::K_OFF + s * C::KV_BYTES + c * 8192, &mk, &k_full[s], c * 64, j * BK4, bh);
+        if (!mbar_wait(&v_empty[s], ph, abort_flag, 62)) break;
+        mbar_expect_tx(&v_full[s], C::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_3d(sm + C::V_OFF + s * C::KV_BYTES + c * 8192, &mv, &v_full[s], c * 64, j * BK4, bh);
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0 && nkv > 0) {
+      const uint32_t id_s = idesc(128, BK4, 0, 0);
+      const uint32_t id_o = idesc(128, D, 0, 1);
+      const uint32_t O = tmem + C::O_COL;
+      const uint32_t qa = smem_u32(sm + C::Q_OFF);
+      auto issue_s = [&](int j) {
+        const uint32_t ka = smem_u32(sm + C::K_OFF + (j % C::ST) * C::KV_BYTES);
+        const uint32_t Sb = tmem + (j & 1) * BK4;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t in = (kk & 3) * 32;
+          mma_ss(Sb, desc(qa + (kk >> 2) * 16384 + in, 16, 1024), desc(ka + (kk >> 2) * 8192 + in, 16, 1024), id_s,
+                 kk > 0);
+        }
+        commit(&s_full[j & 1]);
+        commit(&k_empty[j % C::ST]);
+      };
+      auto issue_pv = [&](int j) {
+        const uint32_t va = smem_u32(sm + C::V_OFF + (j % C::ST) * C::KV_BYTES);
+        const uint32_t Sb = tmem + (j & 1) * BK4;
+#pragma unroll
+        for (int kk = 0; kk < BK4 / 16; ++kk)
+          mma_ts(O, Sb + kk * 8, desc(va + kk * 2048, 8192, 1024), id_o, (j > 0 || kk > 0) ? 1u : 0u);
+        commit(o_ready);
+        commit(&v_empty[j % C::ST]);
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag, 63);
+      for (int j = 0; ok && j < 2 && j < nkv; ++j) {
+        if (!(ok = mbar_wait(&k_full[j % C::ST], (j / C::ST) & 1, abort_flag, 64))) break;
+        fence_after();
+        issue_s(j);
+      }
+      for (int j = 0; ok && j < nkv; ++j) {
+        if (!mbar_wait(&v_full[j % C::ST], (j / C::ST) & 1, abort_flag, 65)) break;
+        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, abort_flag, 66)) break;
+        fence_after();
+        issue_pv(j);
+        if (j + 2 < nkv) {
+          const int jn = j + 2;
+          if (!mbar_wait(&k_full[jn % C::ST], (jn / C::ST) & 1, abort_flag, 67)) break;
+          fence_after();
+          issue_s(jn);
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax (warps 0..3)
+    const int row = 32 * warp + lane;
+    const int q = q0 + row;
+    const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
+    const uint32_t O_t = tmem + C::O_COL + lane_off;
+    const float sl2 = p.scale_log2;
+    const int kvl = kv_limit(p, bh);
+    float m = -INFINITY, l = 0.f;
+    bool ok = nkv > 0;
+    for (int j = 0; ok && j < nkv; ++j) {
+      const int b = j & 1;
+      if (!mbar_wait(&s_full[b], (j >> 1) & 1, abort_flag, 68)) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      const uint32_t S_b = tmem + b * BK4 + lane_off;
+      const int kv0 = j * BK4;
+      int lim = kvl - kv0;
+      if (p.causal) lim = min(lim, q - kv0 + 1);
+      lim = max(0, min(BK4, lim));
+      uint32_t a[32], c[32];
+      ld32_nowait(S_b, a);
+      ld32_nowait(S_b + 32, c);
+      wait_ld();
+      float mx = -INFINITY;
+      if (lim == BK4) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mx = max3(mx, __uint_as_float(a[i]), __uint_as_float(c[i]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (i < lim) mx = fmaxf(mx, __uint_as_float(a[i]));
+          if (32 + i < lim) mx = fmaxf(mx, __uint_as_float(c[i]));
+        }
+      }
+      const float m_blk = mx * sl2;
+      float alpha = 1.f;
+      const bool move = m_blk > m + RESCALE_THRESHOLD || (m == -INFINITY && m_blk != -INFINITY);
+      if (move) {
+        alpha = (m == -INFINITY) ? 0.f : ex2(m - m_blk);
+        m = m_blk;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, move)) {
+        // O holds blocks < j once PV(j - 1) has completed; PV(j) waits for this block's P
+        if (!mbar_wait(o_ready, (j - 1) & 1, abort_flag, 69)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+#pragma unroll
+        for (int cc = 0; cc < D / 32; ++cc) {
+          uint32_t o[32];
+          ld32_nowait(O_t + cc * 32, o);
+          wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          st32(O_t + cc * 32, o);
+        }
+      }
+      const float nmb = (m == -INFINITY) ? 0.f : -m;
+      uint32_t w[32];
+      float rs0 = 0.f, rs1 = 0.f;
+      if (lim == BK4) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const uint32_t* v = i < 16 ? a : c;
+          const int ii = i & 15;
+          float x0, x1, e0, e1;
+          ffma2(__uint_as_float(v[2 * ii]), __uint_as_float(v[2 * ii + 1]), sl2, nmb, x0, x1);
+          if ((ii & 7) >= 5) {
+            ex2_fma2(x0, x1, e0, e1);
+          } else {
+            e0 = ex2(x0);
+            e1 = ex2(x1);
+          }
+          fadd2(rs0, rs1, e0, e1);
+          w[i] = pack_bf16(e0, e1);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const uint32_t* v = i < 16 ? a : c;
+          const int ii = i & 15, k = 2 * i;
+          const float e0 = k < lim ? ex2(fmaf(__uint_as_float(v[2 * ii]), sl2, nmb)) : 0.f;
+          const float e1 = k + 1 < lim ? ex2(fmaf(__uint_as_float(v[2 * ii + 1]), sl2, nmb)) : 0.f;
+          rs0 += e0;
+          rs1 += e1;
+          w[i] = pack_bf16(e0, e1);
+        }
+      }
+      st32(S_b, w);  // P (bf16 pairs) over the first 32 columns of this score buffer
+      wait_st();
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[b]);
+      l = l * alpha + (rs0 + rs1);
+    }
+    if (ok && mbar_wait(o_ready, (nkv - 1) & 1, abort_flag, 70)) {
+      fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int bb = bh / p.H, h = bh % p.H;
+      const bool row_ok = q < p.Sq;
+      __nv_bfloat16* dst = row_ok ? out_row(p, bb, q, h, D) : nullptr;
+#pragma unroll
+      for (int cc = 0; cc < D / 32; ++cc) {
+        uint32_t o[32];
+        ld32_nowait(O_t + cc * 32, o);
+        wait_ld();
+        if (row_ok) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            uint4 pk;
+            pk.x = pack_bf16(__uint_as_float(o[g * 8 + 0]) * inv, __uint_as_float(o[g * 8 + 1]) * inv);
+            pk.y = pack_bf16(__uint_as_float(o[g * 8 + 2]) * inv, __uint_as_float(o[g * 8 + 3]) * inv);
+            pk.z = pack_bf16(__uint_as_float(o[g * 8 + 4]) * inv, __uint_as_float(o[g * 8 + 5]) * inv);
+            pk.w = pack_bf16(__uint_as_float(o[g * 8 + 6]) * inv, __uint_as_float(o[g * 8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + cc * 32 + g * 8) = pk;
+          }
+        }
+      }
+      if (row_ok) p.lse[(int64_t)bh * p.Sq + q] = (m + __log2f(l)) * 0.69314718055994531f;
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256));
+  }
+}
+
 typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -722,11 +1044,11 @@ static EncodeFn encode() {
   return fn;
 }
 
-// 3D map over [BH, S, D] bf16 with box {64, 128, 1}, 128B swizzle.
-static int map3(CUtensorMap* m, const void* ptr, int BH, int S, int D) {
+// 3D map over [BH, S, D] bf16 with box {64, rows, 1}, 128B swizzle.
+static int map3(CUtensorMap* m, const void* ptr, int BH, int S, int D, int rows = 128) {
   cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)BH};
   cuuint64_t str[2] = {(cuuint64_t)D * 2, (cuuint64_t)S * D * 2};
-  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t box[3] = {64, (cuuint32_t)rows, 1};
   cuuint32_t es[3] = {1, 1, 1};
   return (int)encode()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, str, box, es,
                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -748,6 +1070,21 @@ static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMa
   return (int)cudaGetLastError();
 }
 
+template <int D>
+static int launch4(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const Params& p,
+                   unsigned grid, cudaStream_t stream) {
+  static bool set = false;
+  const int bytes = Cfg4<D>::BYTES + 1024;
+  if (!set) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(fmha_fwd4_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return (int)e;
+    set = true;
+  }
+  fmha_fwd4_kernel<D><<<grid, FWD4_THREADS, bytes, stream>>>(mq, mk, mv, p);
+  return (int)cudaGetLastError();
+}
+
 struct PeerOut {
   void* const* o;   // per rank: image-row output [B, si, htot, D]
   void* const* o2;  // per rank: text-row output [B, sl - si, htot, D] (null entries when sl == si)
@@ -761,9 +1098,10 @@ static int fwd2_impl(const void* q, const void* k, const void* v, void* o, void*
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15)
     return -2;
   CUtensorMap mq, mk, mv;
+  const int kv_rows = split == 4 ? BK4 : 128;
   int r = map3(&mq, q, B * H, Sq, D);
-  if (!r) r = map3(&mk, k, B * H, Skv, D);
-  if (!r) r = map3(&mv, v, B * H, Skv, D);
+  if (!r) r = map3(&mk, k, B * H, Skv, D, kv_rows);
+  if (!r) r = map3(&mv, v, B * H, Skv, D, kv_rows);
   if (r) return r;
   Params p;
   memset(&p, 0, sizeof(p));
@@ -785,7 +1123,8 @@ static int fwd2_impl(const void* q, const void* k, const void* v, void* o, void*
   p.Sq = Sq;
   p.Skv = Skv;
   p.H = H;
-  p.npairs = (Sq + 2 * BQ - 1) / (2 * BQ);
+  // v4: one query tile per CTA (npairs counts tiles); v1-v3: pairs of tiles
+  p.npairs = split == 4 ? (Sq + BQ - 1) / BQ : (Sq + 2 * BQ - 1) / (2 * BQ);
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal;
   p.o = reinterpret_cast<__nv_bfloat16*>(o);
@@ -795,6 +1134,8 @@ static int fwd2_impl(const void* q, const void* k, const void* v, void* o, void*
   p.lse = lse;
   const long long grid = (long long)p.npairs * B * H;
   if (grid == 0) return 0;
+  if (split == 4)
+    return D == 64 ? launch4<64>(mq, mk, mv, p, (unsigned)grid, stream) : launch4<128>(mq, mk, mv, p, (unsigned)grid, stream);
   if (D == 64)
     return split == 3 ? launch<64, 3>(mq, mk, mv, p, (unsigned)grid, stream)
            : split == 2 ? launch<64, 2>(mq, mk, mv, p, (unsigned)grid, stream)
@@ -844,4 +1185,21 @@ extern "C" int vo_fmha_fwd2_error(int reset) {
     cudaMemcpyToSymbol(vo_fmha2::g_error, &z, sizeof(int));
   }
   return e;
+}
+
+// forward v4 (one query tile per CTA, two CTAs per SM, double-buffered 64-key score blocks); optional
+// per-sequence key count (int32 [B] in device memory, or null) and causal mask
+extern "C" int vo_fmha_fwd4(const void* q, const void* k, const void* v, void* o, void* o2, int out_split, float* lse,
+                            const int* kv_len, int B, int H, int Sq, int Skv, int D, float scale, int causal,
+                            cudaStream_t stream) {
+  return vo_fmha2::fwd2_impl(q, k, v, o, o2, out_split, lse, B, H, Sq, Skv, D, scale, causal, stream, 4, nullptr,
+                             kv_len);
+}
+
+// Ulysses attention (peer output rows) on forward v4
+extern "C" int vo_fmha_fwd4_peer(const void* q, const void* k, const void* v, void* const* peer_o,
+                                 void* const* peer_o2, int nranks, int sl, int si, int htot, int h0, float* lse, int B,
+                                 int H, int Sq, int Skv, int D, float scale, cudaStream_t stream) {
+  vo_fmha2::PeerOut po{peer_o, peer_o2, nranks, sl, si, htot, h0};
+  return vo_fmha2::fwd2_impl(q, k, v, nullptr, nullptr, 0, lse, B, H, Sq, Skv, D, scale, 0, stream, 4, &po);
 }

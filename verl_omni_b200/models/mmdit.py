@@ -53,6 +53,13 @@ class MMDiTConfig:
         return MMDiTConfig()
 
     @staticmethod
+    def small() -> "MMDiTConfig":
+        """Miniature with the full-size head width (64) and GEMMs of >= 128 rows: the smallest shape that
+        runs every hot op of the full model on its native kernel (32x32 latents -> 256 image tokens)."""
+        return MMDiTConfig(hidden=256, heads=4, depth=2, joint_attention_dim=256, pooled_projection_dim=128,
+                           dual_attention_layers=1, sample_size=32, pos_embed_max_size=32)
+
+    @staticmethod
     def tiny(hidden: int = 64, heads: int = 2, depth: int = 2) -> "MMDiTConfig":
         return MMDiTConfig(hidden=hidden, heads=heads, depth=depth, joint_attention_dim=48,
                            pooled_projection_dim=32, dual_attention_layers=1, sample_size=8, in_channels=4,

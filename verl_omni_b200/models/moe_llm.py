@@ -24,6 +24,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from verl_omni_b200.models.layers import Linear, rope_table
+from verl_omni_b200.ops import llm as LO
 from verl_omni_b200.ops.attention import attention
 from verl_omni_b200.ops import linear as L
 from verl_omni_b200.ops.decode import KVCache, PagedView, decode_attention
@@ -63,8 +64,8 @@ class MoEConfig:
 
 
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    xf = x.float()
-    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype)
+    """Row RMSNorm: the fused kernel on bf16 CUDA tensors, the fp32 oracle otherwise."""
+    return LO.rms_norm(x.contiguous(), w, eps)
 
 
 def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
@@ -76,7 +77,7 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
 
 
 class MoEBlock(nn.Module):
-    def __init__(self, cfg: MoEConfig):
+    def __init__(self, cfg: MoEConfig, ep=None):
         super().__init__()
         self.cfg = cfg
         D, hd = cfg.hidden, cfg.head_dim
@@ -89,8 +90,21 @@ class MoEBlock(nn.Module):
         self.ln2 = nn.Parameter(torch.ones(D))
         self.router = Linear(D, cfg.experts, bias=False)
         E, F_ = cfg.experts, cfg.expert_ffn
-        self.w_gate_up = nn.Parameter(torch.randn(E, 2 * F_, D) * 0.02)  # [E, 2F, D]
-        self.w_down = nn.Parameter(torch.randn(E, D, F_) * 0.02)  # [E, D, F]
+        # expert parallelism: this rank holds experts [e0, e0 + El) only; each expert's initial weights come
+        # from its own seeded generator, so a sharded model equals the slices of the unsharded one
+        El = E if ep is None else ep.per_rank
+        self.e0 = 0 if ep is None else ep.rank * ep.per_rank
+        base = int(torch.randint(0, 2 ** 31 - E, (1,)))
+        self.w_gate_up = nn.Parameter(torch.empty(El, 2 * F_, D))  # [El, 2F, D]
+        self.w_down = nn.Parameter(torch.empty(El, D, F_))  # [El, D, F]
+        with torch.no_grad():
+            for j in range(El):
+                g = torch.Generator(device=self.w_gate_up.device).manual_seed(base + self.e0 + j)
+                self.w_gate_up[j].normal_(0.0, 0.02, generator=g)
+                self.w_down[j].normal_(0.0, 0.02, generator=g)
+        if ep is not None and ep.ep > 1:
+            self.w_gate_up._vo_expert = True  # sharded over the EP group: the engine's expert parameter set
+            self.w_down._vo_expert = True
 
     def attn_tp(self, x, cos, sin, tp):
         """Tensor + sequence parallel attention: ``x`` [B, S_l, D] holds this rank's tokens (rank r: positions
@@ -110,11 +124,10 @@ class MoEBlock(nn.Module):
                        kvw[0, r * Hk * hd:(r + 1) * Hk * hd], kvw[1, r * Hk * hd:(r + 1) * Hk * hd]], 0)
         y = column_parallel_linear(h, w, None, tp)  # [W*B*Sl, (Hq + 2Hk) hd], rank-major rows
         y = y.view(W, B, Sl, -1).permute(1, 0, 2, 3).reshape(B, S, -1)
-        q = y[..., :Hq * hd].view(B, S, Hq, hd)
-        k = y[..., Hq * hd:(Hq + Hk) * hd].view(B, S, Hk, hd)
         v = y[..., (Hq + Hk) * hd:].view(B, S, Hk, hd).transpose(1, 2)
-        q = apply_rope(rms_norm(q.transpose(1, 2), self.q_norm, cfg.eps), cos, sin)
-        k = apply_rope(rms_norm(k.transpose(1, 2), self.k_norm, cfg.eps), cos, sin)
+        # per-head q/k RMSNorm + RoPE straight from the projection output (one kernel each)
+        q = LO.head_norm_rope(y, 0, Hq, self.q_norm, cos, sin, cfg.eps)
+        k = LO.head_norm_rope(y, Hq * hd, Hk, self.k_norm, cos, sin, cfg.eps)
         rep = Hq // Hk
         o = attention(q.contiguous(), k.repeat_interleave(rep, 1).contiguous(),
                       v.repeat_interleave(rep, 1).contiguous(), causal=True)  # [B, S, Hq hd]
@@ -127,11 +140,11 @@ class MoEBlock(nn.Module):
         B, S, D = x.shape
         hd = cfg.head_dim
         h = rms_norm(x, self.ln1, cfg.eps)
-        q = self.q_proj(h).view(B, S, cfg.q_heads, hd).transpose(1, 2)
-        kv = self.kv_proj(h).view(B, S, 2, cfg.kv_heads, hd)
-        k, v = kv[:, :, 0].transpose(1, 2), kv[:, :, 1].transpose(1, 2)
-        q = apply_rope(rms_norm(q, self.q_norm, cfg.eps), cos, sin)
-        k = apply_rope(rms_norm(k, self.k_norm, cfg.eps), cos, sin)
+        qp = self.q_proj(h)  # [B, S, Hq hd]
+        kvp = self.kv_proj(h)  # [B, S, 2 Hk hd]: k heads, then v heads
+        q = LO.head_norm_rope(qp, 0, cfg.q_heads, self.q_norm, cos, sin, cfg.eps)  # [B, Hq, S, hd]
+        k = LO.head_norm_rope(kvp, 0, cfg.kv_heads, self.k_norm, cos, sin, cfg.eps)  # [B, Hk, S, hd]
+        v = kvp[..., cfg.kv_heads * hd:].view(B, S, cfg.kv_heads, hd).transpose(1, 2)
         if isinstance(cache, KVCache):
             # preallocated cache: in-place append; one-token steps use the grouped-query decode kernel
             first = cache.len == 0
@@ -168,10 +181,9 @@ class MoEBlock(nn.Module):
         cfg = self.cfg
         B, S, D = x.shape
         h = rms_norm(x, self.ln2, cfg.eps).reshape(B * S, D)
-        logits = self.router(h).float()
-        probs = torch.softmax(logits, -1)
-        gates, idx = torch.topk(probs, cfg.top_k, dim=-1)
-        gates = (gates / gates.sum(-1, keepdim=True)).to(x.dtype)
+        # softmax + top-k + renormalised gates on the device (one kernel, no host sync)
+        gates, idx, probs = LO.router_topk(self.router(h).float(), cfg.top_k)
+        gates = gates.to(x.dtype)
         self.last_router = (probs, idx)
         if ep is not None and hasattr(ep, "fused_ok") and ep.fused_ok(h, self.w_gate_up, self.w_down):
             out = ep.dispatch_combine_fused(h, idx, gates, self.w_gate_up, self.w_down)  # peer-memory exchange
@@ -182,8 +194,8 @@ class MoEBlock(nn.Module):
         return x + out.view(B, S, D)
 
     def expert_ffn(self, tokens: torch.Tensor, expert_ids: torch.Tensor) -> torch.Tensor:
-        """SwiGLU of locally-owned experts for tokens already grouped by expert."""
-        return _ffn_grouped(tokens, expert_ids, self.w_gate_up, self.w_down)
+        """SwiGLU of locally-owned experts for tokens already grouped by (global) expert id."""
+        return _ffn_grouped(tokens, expert_ids - self.e0, self.w_gate_up, self.w_down)
 
     def forward(self, x, cos, sin, cache=None, pos0: int = 0, ep=None, tp=None):
         if tp is not None:
@@ -252,17 +264,31 @@ class _Encoder(nn.Module):
 
 
 class MoELLM(nn.Module):
-    def __init__(self, cfg: MoEConfig):
+    def __init__(self, cfg: MoEConfig, ep=None):
+        """``ep``: an :class:`~verl_omni_b200.parallel.expert_parallel.ExpertParallel` context; its rank then
+        holds only its own experts' weights (``experts / ep`` per layer)."""
         super().__init__()
         self.cfg = cfg
         self.embed = nn.Parameter(torch.randn(cfg.vocab, cfg.hidden) * 0.02)
-        self.layers = nn.ModuleList([MoEBlock(cfg) for _ in range(cfg.layers)])
+        self.layers = nn.ModuleList([MoEBlock(cfg, ep) for _ in range(cfg.layers)])
         self.norm = nn.Parameter(torch.ones(cfg.hidden))
         self.lm_head = Linear(cfg.hidden, cfg.vocab, bias=False)
         self.audio_tower = _Encoder(cfg.audio_mel, cfg.audio_dim, cfg.audio_layers, cfg.hidden)
         self.visual = _Encoder(cfg.vision_patch_dim, cfg.vision_dim, cfg.vision_layers, cfg.hidden)
-        self.ep = None
+        self.ep = ep
         self.tp = None  # TPContext: tensor + sequence parallel training forwards (no KV cache)
+        self._rope_cache = None  # (cos, sin) fp32 [n, head_dim / 2] on the model's device, grown on demand
+
+    def rope(self, pos0: int, S: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+        """cos / sin rows for positions [pos0, pos0 + S) from a device-resident table (built once, grown
+        to the next power of two when a longer position is asked for)."""
+        need = pos0 + S
+        c = self._rope_cache
+        if c is None or c[0].shape[0] < need or c[0].device != torch.device(device):
+            n = 1 << max(12, (need - 1).bit_length())
+            cos, sin = rope_table(torch.arange(n), self.cfg.head_dim, self.cfg.rope_theta)
+            c = self._rope_cache = (cos.to(device), sin.to(device))
+        return c[0][pos0:need], c[1][pos0:need]
 
     def embed_tokens(self, ids, audio_feats=None, image_patches=None):
         x = F.embedding(ids, self.embed)
@@ -277,13 +303,16 @@ class MoELLM(nn.Module):
         return x
 
     def forward(self, ids, positions=None, caches=None, pos0: int = 0, audio_feats=None, image_patches=None,
-                return_hidden: bool = False):
+                return_hidden: bool = False, targets: Optional[torch.Tensor] = None, temperature: float = 1.0):
+        """Logits [B, S, V] (fp32); ``return_hidden``: the final hidden states; ``targets`` [B, S] (next-token
+        ids per position): log p(target) [B, S] through the chunked vocabulary kernel, with no logits tensor
+        (under tensor parallelism each rank scores its own tokens and the log-probs are gathered)."""
+        from verl_omni_b200.ops.vocab_logprob import token_logprobs_from_hidden
+
         cfg = self.cfg
         B, S = ids.shape
         x = self.embed_tokens(ids, audio_feats, image_patches) if pos0 == 0 else F.embedding(ids, self.embed)
-        pos = torch.arange(pos0, pos0 + S, device=ids.device)
-        cos, sin = rope_table(pos.cpu(), cfg.head_dim, cfg.rope_theta)
-        cos, sin = cos.to(ids.device), sin.to(ids.device)
+        cos, sin = self.rope(pos0, S, ids.device)
         tp = self.tp if (self.tp is not None and caches is None and pos0 == 0 and self.tp.world > 1) else None
         if tp is not None:
             from verl_omni_b200.parallel.ulysses import gather_sequence
@@ -292,14 +321,16 @@ class MoELLM(nn.Module):
             pad = (-S) % W  # causal: zero tokens appended at the end change no earlier position
             if pad:
                 x = torch.cat([x, x.new_zeros(B, pad, x.shape[-1])], 1)
-                pos = torch.arange(S + pad, device=ids.device)
-                cos, sin = rope_table(pos.cpu(), cfg.head_dim, cfg.rope_theta)
-                cos, sin = cos.to(ids.device), sin.to(ids.device)
+                cos, sin = self.rope(0, S + pad, ids.device)
             Sl = x.shape[1] // W
             x = x[:, tp.rank * Sl:(tp.rank + 1) * Sl]
             for blk in self.layers:
                 x = blk(x, cos, sin, None, 0, self.ep, tp)
             h = rms_norm(x, self.norm, cfg.eps)
+            if targets is not None:
+                tl = F.pad(targets, (0, pad))[:, tp.rank * Sl:(tp.rank + 1) * Sl]
+                lp = token_logprobs_from_hidden(h, self.lm_head.weight, tl, temperature)
+                return gather_sequence(lp.unsqueeze(-1), tp.group)[:, :S, 0]
             if return_hidden:
                 return gather_sequence(h, tp.group)[:, :S]
             # the vocabulary projection stays partitioned by tokens; the logits are gathered
@@ -307,6 +338,8 @@ class MoELLM(nn.Module):
         for i, blk in enumerate(self.layers):
             x = blk(x, cos, sin, None if caches is None else caches[i], pos0, self.ep)
         h = rms_norm(x, self.norm, cfg.eps)
+        if targets is not None:
+            return token_logprobs_from_hidden(h, self.lm_head.weight, targets, temperature)
         if return_hidden:
             return h
         return self.lm_head(h).float()

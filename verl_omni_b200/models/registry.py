@@ -66,6 +66,10 @@ ARCHS: dict[str, ArchSpec] = {
         "sd35_medium", "SD3MMDiT", lambda: MMDiT(MMDiTConfig.sd35_medium()), (16, 64, 64),
         {"prompt_embeds": (333, 4096), "pooled_prompt_embeds": (2048,)}, reward="vit", image_size=512,
         notes="24 joint blocks, hidden 1536, 24 heads, patch 2, 16-ch latents; 256 T5 + 77 CLIP tokens"),
+    "sd35_small": ArchSpec(
+        "sd35_small", "SD3MMDiT", lambda: MMDiT(MMDiTConfig.small()), (16, 32, 32),
+        {"prompt_embeds": (77, 256), "pooled_prompt_embeds": (128,)}, reward="mlp", image_size=64,
+        notes="2 joint blocks, hidden 256, 4 heads of 64, 256 image + 77 text tokens"),
     "sd35_tiny": ArchSpec(
         "sd35_tiny", "SD3MMDiT", lambda: MMDiT(MMDiTConfig.tiny()), (4, 8, 8),
         {"prompt_embeds": (12, 48), "pooled_prompt_embeds": (32,)}, reward="mlp", image_size=64),

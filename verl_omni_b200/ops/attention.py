@@ -18,9 +18,15 @@ import torch.nn.functional as F
 from verl_omni_b200.ops._ext import ext
 
 
-# forward kernel generation: 3 = two query tiles per CTA, P/O in tensor memory, two softmax warpgroups per
-# tile (default); 2 = one softmax warpgroup per tile; 1 = one query tile per CTA
+# forward kernel generation: 4 = one query tile per CTA, two CTAs per SM, double-buffered 64-key score
+# blocks; 3 = two query tiles per CTA, P/O in tensor memory, two softmax warpgroups per tile; 2 = one
+# softmax warpgroup per tile; 1 = one query tile per CTA
 _FWD_VERSION = int(os.environ.get("VO_FMHA_FWD", "3"))
+
+
+def _kv_version() -> int:
+    """Forward generation for per-sequence key counts (versions 3 and 4 support them)."""
+    return 4 if _FWD_VERSION >= 4 else 3
 # backward kernel generation: 2 = pipelined (P^T/dS^T in tensor memory, concurrent dQ drain), 1 = serial
 _BWD_VERSION = int(os.environ.get("VO_FMHA_BWD", "2"))
 
@@ -32,8 +38,8 @@ def _native() -> bool:
 class _FMHA(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, causal, scale, kv_len=None):
-        if kv_len is not None:  # keys at positions >= kv_len[b] masked (forward v3)
-            o, lse = ext().fmha_fwd(q, k, v, False, scale, 3, 0, kv_len=kv_len)
+        if kv_len is not None:  # keys at positions >= kv_len[b] masked (forward v3 / v4)
+            o, lse = ext().fmha_fwd(q, k, v, False, scale, _kv_version(), 0, kv_len=kv_len)
         else:
             o, lse = ext().fmha_fwd(q, k, v, causal, scale, _FWD_VERSION)
         ctx.save_for_backward(q, k, v, o, lse)
@@ -65,8 +71,8 @@ class _FMHASplit(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, q, k, v, causal, scale, split, kv_len=None):
-        if kv_len is not None:  # right-padded keys: per-sequence key counts (forward v3)
-            o_a, lse, o_b = ext().fmha_fwd(q, k, v, causal, scale, 3, split, kv_len=kv_len)
+        if kv_len is not None:  # right-padded keys: per-sequence key counts (forward v3 / v4)
+            o_a, lse, o_b = ext().fmha_fwd(q, k, v, causal, scale, _kv_version(), split, kv_len=kv_len)
         else:
             o_a, lse, o_b = ext().fmha_fwd(q, k, v, causal, scale, _FWD_VERSION, split)
         ctx.save_for_backward(q, k, v, o_a, o_b, lse)

@@ -317,12 +317,18 @@ def bench_fmha(a) -> list[dict]:
     flops_f = 4.0 * B * H * S * S * D
     cases = {"fwd": (lambda: e.fmha_fwd(q, k, v, False, scale, 1), flops_f),
              "fwd2": (lambda: e.fmha_fwd(q, k, v, False, scale, 2), flops_f),
-             "fwd3": (lambda: e.fmha_fwd(q, k, v, False, scale, 3), flops_f)}
+             "fwd3": (lambda: e.fmha_fwd(q, k, v, False, scale, 3), flops_f),
+             "fwd4": (lambda: e.fmha_fwd(q, k, v, False, scale, 4), flops_f)}
     if hasattr(e, "fmha_bwd"):
         cases["bwd"] = (lambda: e.fmha_bwd(q, k, v, o, lse, do, False, scale, 1), 2.5 * flops_f)
         cases["bwd2"] = (lambda: e.fmha_bwd(q, k, v, o, lse, do, False, scale, 2), 2.5 * flops_f)
     if a.compare:
         cases["sdpa_fwd"] = (lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v), flops_f)
+        qg, kg, vg = (t.detach().clone().requires_grad_(True) for t in (q, k, v))
+        og = torch.nn.functional.scaled_dot_product_attention(qg, kg, vg)
+        gdo = torch.randn_like(og)
+        # backward only: one autograd.grad through the retained SDPA graph per call
+        cases["sdpa_bwd"] = (lambda: torch.autograd.grad(og, (qg, kg, vg), gdo, retain_graph=True), 2.5 * flops_f)
     if a.only:
         cases = {k: cases[k] for k in a.only.split(",")}
     out = []

@@ -78,8 +78,7 @@ class _ExpertFFN(torch.autograd.Function):
     def forward(ctx, xs, w_gate_up, w_down, tile_expert, seg):
         e = _ext()
         gu = e.moe_gemm_fwd(xs, w_gate_up, tile_expert)  # [Mp, 2F]
-        g, u = gu.chunk(2, -1)
-        a = (F.silu(g.float()) * u.float()).to(xs.dtype)
+        a = e.swiglu_fwd(gu)  # silu(gate) * up, bf16 (one pass)
         y = e.moe_gemm_fwd(a, w_down, tile_expert)  # [Mp, D]
         ctx.save_for_backward(xs, gu, a, w_gate_up, w_down, tile_expert, seg)
         return y
@@ -89,7 +88,7 @@ class _ExpertFFN(torch.autograd.Function):
         xs, gu, a, w_gate_up, w_down, tile_expert, seg = ctx.saved_tensors
         e = _ext()
         dy = dy.contiguous()
-        da = e.moe_gemm_dgrad(dy, w_down, tile_expert).float()  # [Mp, F]
+        da = e.moe_gemm_dgrad(dy, w_down, tile_expert)  # [Mp, F]
         gd = None
         mg = getattr(w_down, "main_grad", None)
         if mg is not None:
@@ -98,11 +97,7 @@ class _ExpertFFN(torch.autograd.Function):
             buf = torch.zeros(w_down.shape, device=dy.device, dtype=torch.float32)
             e.moe_gemm_wgrad(dy, a, seg, buf, True)
             gd = buf.to(w_down.dtype)
-        g, u = gu.float().chunk(2, -1)
-        sg = torch.sigmoid(g)
-        dg = da * u * sg * (1.0 + g * (1.0 - sg))
-        du = da * g * sg
-        dgu = torch.cat([dg, du], -1).to(xs.dtype).contiguous()
+        dgu = e.swiglu_bwd(da, gu)  # d(gate | up) in one pass
         dxs = e.moe_gemm_dgrad(dgu, w_gate_up, tile_expert)
         ggu = None
         mg = getattr(w_gate_up, "main_grad", None)

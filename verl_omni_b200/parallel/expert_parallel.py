@@ -134,7 +134,7 @@ class _FusedEP(torch.autograd.Function):
         e_ = ext()
         dev = h.device
         T, K = idx.shape
-        E, D = w_gate_up.shape[0], h.shape[1]
+        E, D = ep.per_rank * ep.ep, h.shape[1]
         W, r, El = ep.ep, ep.rank, ep.per_rank
         flat_e = idx.reshape(-1)
         order = torch.argsort(flat_e, stable=True)
@@ -164,12 +164,11 @@ class _FusedEP(torch.autograd.Function):
         e_.peer_row_copy(h.contiguous(), tok_s, dst_rank, dst_row, xd.peer_ptrs, cap)
         ep.barrier(dev)
         R = L.R
-        wgu_l, wd_l = w_gate_up[r * El:(r + 1) * El], w_down[r * El:(r + 1) * El]
+        wgu_l, wd_l = _local(w_gate_up, r, El), _local(w_down, r, El)
         x_own = xv[:R].clone()
         if R:
             gu = e_.moe_gemm_fwd(x_own, wgu_l, plan["tile"])
-            g, u = gu.chunk(2, -1)
-            a = (F_silu(g.float()) * u.float()).to(h.dtype)
+            a = e_.swiglu_fwd(gu)
             y = e_.moe_gemm_fwd(a, wd_l, plan["tile"])
         else:
             gu = a = y = h.new_zeros(0, D)
@@ -210,29 +209,32 @@ class _FusedEP(torch.autograd.Function):
         e_.peer_row_copy(dy_slot, torch.arange(order.numel(), device=dev), plan["dst_rank"], plan["dst_row"],
                          db.peer_ptrs, cap)
         ep.barrier(dev)
-        gwgu = torch.zeros(w_gate_up.shape, device=dev, dtype=torch.float32)
-        gwd = torch.zeros(w_down.shape, device=dev, dtype=torch.float32)
-        wgu_l, wd_l = w_gate_up[r * El:(r + 1) * El], w_down[r * El:(r + 1) * El]
+        # weight gradients go straight into the (local) experts' fp32 main_grad when the engine owns one
+        mg_gu, mg_d = getattr(w_gate_up, "main_grad", None), getattr(w_down, "main_grad", None)
+        gwgu = mg_gu if mg_gu is not None else torch.zeros(w_gate_up.shape, device=dev, dtype=torch.float32)
+        gwd = mg_d if mg_d is not None else torch.zeros(w_down.shape, device=dev, dtype=torch.float32)
+        wgu_l, wd_l = _local(w_gate_up, r, El), _local(w_down, r, El)
         if R:
             dyo = dv[:R].clone()
-            da = e_.moe_gemm_dgrad(dyo, wd_l, plan["tile"]).float()
-            e_.moe_gemm_wgrad(dyo, a, plan["seg"], gwd[r * El:(r + 1) * El], True)
-            g, u = gu.float().chunk(2, -1)
-            sg = torch.sigmoid(g)
-            dgu = torch.cat([da * u * sg * (1.0 + g * (1.0 - sg)), da * g * sg], -1).to(dout.dtype).contiguous()
+            da = e_.moe_gemm_dgrad(dyo, wd_l, plan["tile"])
+            e_.moe_gemm_wgrad(dyo, a, plan["seg"], _local(gwd, r, El), True)
+            dgu = e_.swiglu_bwd(da, gu)
             dx = e_.moe_gemm_dgrad(dgu, wgu_l, plan["tile"])
-            e_.moe_gemm_wgrad(dgu, x_own, plan["seg"], gwgu[r * El:(r + 1) * El], True)
+            e_.moe_gemm_wgrad(dgu, x_own, plan["seg"], _local(gwgu, r, El), True)
         xb = ep.buf("y", pcap * D, dev)
         if R:
             e_.peer_row_copy(dx, plan["own_rows"], plan["own_rank"], plan["own_slot"], xb.peer_ptrs, pcap)
         ep.barrier(dev)
         dxs = xb.tensor.view(pcap, D)[:order.numel()]
         dh = torch.zeros(T, D, device=dev, dtype=dout.dtype).index_add(0, tok_s, dxs)
-        return (dh, dgates.view(T, K).to(dout.dtype), gwgu.to(w_gate_up.dtype), gwd.to(w_down.dtype), None, None)
+        return (dh, dgates.view(T, K).to(dout.dtype), None if mg_gu is not None else gwgu.to(w_gate_up.dtype),
+                None if mg_d is not None else gwd.to(w_down.dtype), None, None)
 
 
-def F_silu(x: torch.Tensor) -> torch.Tensor:
-    return torch.nn.functional.silu(x)
+def _local(w: torch.Tensor, r: int, El: int) -> torch.Tensor:
+    """This rank's experts of a stacked expert tensor: the whole tensor when it holds only the local experts
+    (expert-sharded model), else slice [r El, (r + 1) El)."""
+    return w if w.shape[0] == El else w[r * El:(r + 1) * El]
 
 
 class FusedExpertParallel(ExpertParallel):

@@ -153,6 +153,9 @@ class PolicyGradientTrainer:
                                         shuffle=bool(config.data.get("shuffle", True)))
         self.loss_fn = lambda model_output, data: diffusion_loss(self.actor_cfg, model_output, data)
         self.ckpt_dir = config.trainer.default_local_dir
+        from verl_omni_b200.utils.mfu import DiffusionFlopsCounter
+
+        self.flops_counter = DiffusionFlopsCounter(module, getattr(module, "family", ""))
 
     # ------------------------------------------------------------------ pieces
     @torch.no_grad()
@@ -290,7 +293,29 @@ class PolicyGradientTrainer:
         metrics.update(rmetrics)
         metrics.update(M.compute_timing_metrics_diffusion(timer.timing, len(out)))
         metrics.update(M.compute_throughput_metrics_diffusion(step_time, len(out) * self.dp, self.world))
+        metrics.update(self._mfu_metrics(out, timer.timing, step_time))
         return metrics
+
+    def _mfu_metrics(self, out: DataProto, timing: dict, step_time: float) -> dict:
+        """``perf/mfu/*`` from the architecture's FLOPs formula and the phase timings."""
+        from verl_omni_b200.utils.mfu import step_mfu_metrics
+
+        shape = self.spec.latent_shape
+        image_tokens = self.spec.sched_seq_len or int(np.prod(shape[1:])) // 4
+        pe = self.spec.cond_shapes.get("prompt_embeds")
+        text_tokens = int(pe[0]) if pe else int(self.spec.prompt_len if self.spec.text_encoder else 0)
+        gs = self.model_cfg.pipeline.guidance_scale
+        cfg_passes = 2 if (gs is not None and gs > 1.0 and "negative_prompt_embeds" in out.batch) else 1
+        bypass = self.algo_cfg.rollout_correction.bypass_mode or self.actor_cfg.rollout_correction.bypass_mode
+        ref_passes = 1 if self.actor_cfg.use_kl_loss else 0
+        try:
+            return step_mfu_metrics(self.flops_counter, samples=len(out),
+                                    rollout_steps=int(self.rollout_cfg.pipeline.num_inference_steps),
+                                    train_steps=int(out.batch["step_index"].shape[1]), image_tokens=image_tokens,
+                                    text_tokens=text_tokens, cfg_passes=cfg_passes, timing=timing,
+                                    step_time=step_time, recompute_old=not bypass, ref_passes=ref_passes, sp=self.sp)
+        except Exception:  # noqa: BLE001 - a missing config field must not break a training step
+            return {}
 
     def _esi_close_to_expiration(self) -> bool:
         """Capacity-block expiration rule, agreed by every rank (one flag all-reduce, MAX)."""

@@ -16,7 +16,7 @@ from typing import Optional
 import numpy as np
 import torch
 
-from verl_omni_b200.models.moe_llm import MoEConfig, MoELLM, token_logprobs
+from verl_omni_b200.models.moe_llm import MoEConfig, MoELLM
 from verl_omni_b200.parallel import dist as D
 from verl_omni_b200.trainer.diffusion.diffusion_algos import group_normalize
 from verl_omni_b200.trainer.omni.omni_algos import get_omni_loss_fn, omni_dpo_loss, sequence_logps
@@ -35,12 +35,20 @@ class OmniGRPOTrainer:
         torch.manual_seed(seed)
         self.cfg, self.actor_cfg, self.device, self.n = cfg, actor_cfg, device, n
         self.prompt_text, self.audio_tokens, self.image_tokens = prompt_text, audio_tokens, image_tokens
-        self.model = MoELLM(cfg).to(device)
+        ep = None
+        self.expert_dp_group = None
         if ep_group is not None and D.world_size(ep_group) > 1:
             from verl_omni_b200.parallel.expert_parallel import FusedExpertParallel
 
-            # peer-memory dispatch / combine where it applies (CUDA, one node), NCCL all-to-all otherwise
-            self.model.ep = FusedExpertParallel(cfg.experts, ep_group)
+            # expert parallelism over consecutive blocks of ranks: each rank holds experts / ep of every layer
+            # (weights, fp32 main grads and optimizer state); the ranks holding the same experts form the
+            # expert data-parallel group.  Peer-memory dispatch / combine where it applies (CUDA, one node),
+            # NCCL all-to-all otherwise.
+            ep_size = D.world_size(ep_group)
+            ep_group, self.expert_dp_group = D.make_hsdp_groups(ep_size)
+            ep = FusedExpertParallel(cfg.experts, ep_group)
+        with torch.device(device):
+            self.model = MoELLM(cfg, ep)
         # tensor + sequence parallelism (Megatron layout): ranks of a TP group share their samples and split each
         # sequence and the attention heads; weights stay replicated, so every rank's gradient is its share and
         # the loss is scaled by tp for the world-averaged gradient (groups of consecutive ranks)
@@ -49,7 +57,8 @@ class OmniGRPOTrainer:
             from verl_omni_b200.parallel.tensor_parallel import TPContext
 
             self.model.tp = TPContext(tp_group)
-        self.engine = ShardedEngine(self.model, actor_cfg, device=device, total_steps=1000)
+        self.engine = ShardedEngine(self.model, actor_cfg, device=device, total_steps=1000,
+                                    expert_group=self.expert_dp_group)
         self.rollout = LLMRolloutEngine(self.model, max_new_tokens=response_len, device=device)
         self.loss_fn = get_omni_loss_fn(loss_mode)
         self.loss_mode = loss_mode
@@ -71,9 +80,12 @@ class OmniGRPOTrainer:
     def _resp_logprobs(self, data: DataProto) -> torch.Tensor:
         ids = data.batch["input_ids"].to(self.device)
         P = data.batch["prompts"].shape[1]
-        logits = self.model(ids[:, :-1], audio_feats=data.batch["audio_feats"].to(self.device),
-                            image_patches=data.batch["image_patches"].to(self.device))
-        return token_logprobs(logits[:, P - 1:], ids[:, P:])
+        # the vocabulary projection and log-softmax run chunked inside the model (no [B, S, V] logits)
+        tgt = torch.zeros_like(ids[:, :-1])
+        tgt[:, P - 1:] = ids[:, P:]
+        lp = self.model(ids[:, :-1], audio_feats=data.batch["audio_feats"].to(self.device),
+                        image_patches=data.batch["image_patches"].to(self.device), targets=tgt)
+        return lp[:, P - 1:]
 
     def step(self, num_prompts: int = 2) -> dict:
         self.step_count += 1
@@ -104,9 +116,11 @@ class OmniGRPOTrainer:
         def seqlp(model, d):
             ids = d.batch["input_ids"].to(self.device)
             P = d.batch["prompts"].shape[1]
-            lg = model(ids[:, :-1], audio_feats=d.batch["audio_feats"].to(self.device),
-                       image_patches=d.batch["image_patches"].to(self.device))
-            return sequence_logps(token_logprobs(lg[:, P - 1:], ids[:, P:]), d.batch["response_mask"].to(self.device))
+            tgt = torch.zeros_like(ids[:, :-1])
+            tgt[:, P - 1:] = ids[:, P:]
+            lp = model(ids[:, :-1], audio_feats=d.batch["audio_feats"].to(self.device),
+                       image_patches=d.batch["image_patches"].to(self.device), targets=tgt)[:, P - 1:]
+            return sequence_logps(lp, d.batch["response_mask"].to(self.device))
 
         with torch.no_grad():
             rc, rr = seqlp(ref_model, chosen), seqlp(ref_model, rejected)

@@ -77,14 +77,44 @@ def dit_forward_flops(module, image_tokens: int, text_tokens: int) -> float:
     return flops
 
 
+@register_flops("flux")
+def flux_forward_flops(module, image_tokens: int, text_tokens: int) -> float:
+    cfg = module.cfg
+    D = cfg.hidden
+    mlp = int(D * cfg.mlp_ratio)
+    S = image_tokens + text_tokens
+    double = 2 * (4 * D * D + 2 * D * mlp) * S + 4 * S * S * D      # per-stream weights, joint attention
+    single = 2 * (3 * D * D + D * mlp + (D + mlp) * D) * S + 4 * S * S * D  # fused qkv+mlp-in, out over [attn|mlp]
+    return cfg.depth_double * double + cfg.depth_single * single + 2 * cfg.joint_attention_dim * D * text_tokens
+
+
+@register_flops("qwen_image")
+def qwen_image_forward_flops(module, image_tokens: int, text_tokens: int) -> float:
+    cfg = module.cfg
+    D = cfg.hidden
+    mlp = int(D * getattr(cfg, "mlp_ratio", 4.0))
+    S = image_tokens + text_tokens
+    return cfg.depth * (2 * (4 * D * D + 2 * D * mlp) * S + 4 * S * S * D)
+
+
+def generic_forward_flops(module, image_tokens: int, text_tokens: int) -> float:
+    """Fallback: every 2-D weight applied to every token, full attention over all tokens (upper bound for
+    families without a formula of their own)."""
+    S = image_tokens + text_tokens
+    dense = 2.0 * _linear_params(module, lambda n: "embed" not in n) * S
+    cfg = getattr(module, "cfg", None)
+    depth = getattr(cfg, "depth", 0) or getattr(cfg, "layers", 0) or 0
+    hidden = getattr(cfg, "hidden", 0) or 0
+    return dense + 4.0 * depth * S * S * hidden
+
+
 class DiffusionFlopsCounter:
     def __init__(self, module, family: str):
-        if family not in FLOPS_REGISTRY:
-            raise KeyError(f"no FLOPs formula for {family!r}")
         self.module, self.family = module, family
+        self._fn = FLOPS_REGISTRY.get(family, generic_forward_flops)
 
     def forward_flops(self, image_tokens: int, text_tokens: int) -> float:
-        return FLOPS_REGISTRY[self.family](self.module, image_tokens, text_tokens)
+        return float(self._fn(self.module, image_tokens, text_tokens))
 
     def estimate_flops(self, num_samples: int, steps: int, image_tokens: int, text_tokens: int, *,
                        cfg_passes: int = 1, train: bool = True) -> float:
@@ -92,4 +122,27 @@ class DiffusionFlopsCounter:
         return self.forward_flops(image_tokens, text_tokens) * num_samples * steps * cfg_passes * passes
 
     def mfu(self, flops: float, seconds: float, n_gpus: int = 1) -> float:
-        return flops / (seconds * n_gpus * device_peak_tflops() * 1e12)
+        return flops / (max(seconds, 1e-9) * n_gpus * device_peak_tflops() * 1e12)
+
+
+def step_mfu_metrics(counter: "DiffusionFlopsCounter", *, samples: int, rollout_steps: int, train_steps: int,
+                     image_tokens: int, text_tokens: int, cfg_passes: int, timing: dict, step_time: float,
+                     recompute_old: bool, ref_passes: int = 0, sp: int = 1) -> dict:
+    """Per-rank model-FLOPs utilisation of one FlowGRPO step, by phase, against the measured bf16 GEMM
+    peak (the reference reports ``perf/mfu/actor`` for the update and ``perf/mfu/actor_infer`` for the
+    old-log-prob recompute).  ``samples`` are this rank's trajectories; under sequence parallelism each of
+    the ``sp`` ranks of a group runs 1/sp of every sequence."""
+    f = counter.forward_flops(image_tokens, text_tokens) / max(1, sp)
+    gen = f * samples * rollout_steps * cfg_passes
+    old = f * samples * train_steps if recompute_old else 0.0
+    ref = f * samples * train_steps * ref_passes
+    upd = 3.0 * f * samples * train_steps
+    out = {"perf/flops_per_step_tflop": (gen + old + ref + upd) / 1e12,
+           "perf/mfu/step": counter.mfu(gen + old + ref + upd, step_time)}
+    if timing.get("update_actor"):
+        out["perf/mfu/actor"] = counter.mfu(upd, timing["update_actor"])
+    if recompute_old and timing.get("old_log_prob"):
+        out["perf/mfu/actor_infer"] = counter.mfu(old, timing["old_log_prob"])
+    if timing.get("gen"):
+        out["perf/mfu/rollout"] = counter.mfu(gen, timing["gen"])
+    return out

@@ -48,13 +48,13 @@ class FlatParams:
     """Packs the trainable parameters of ``module`` into one flat buffer + fp32 grad buffer."""
 
     def __init__(self, module: nn.Module, dtype: torch.dtype, device: torch.device, world: int, rank: int,
-                 group=None, symmetric: bool = False):
+                 group=None, symmetric: bool = False, select=None, owns_module: bool = True):
         self.module = module
         self.group = group
         self.world, self.rank = world, rank
         self.names, self.params = [], []
         for n, p in module.named_parameters():
-            if p.requires_grad:
+            if p.requires_grad and (select is None or select(n, p)):
                 self.names.append(n)
                 self.params.append(p)
         self.shapes = [tuple(p.shape) for p in self.params]
@@ -94,6 +94,8 @@ class FlatParams:
             p.data = self.flat[o:o + n].view(s)
             p.main_grad = self.main_grad[o:o + n].view(s)
             p.register_post_accumulate_grad_hook(self._accumulate)
+        if not owns_module:
+            return
         # non-trainable parameters and buffers follow the compute dtype/device
         for m in module.modules():
             for k, p in list(m._parameters.items()):
@@ -189,9 +191,13 @@ class ShardedEngine:
     """Owns a module, its flat parameters and the sharded AdamW state."""
 
     def __init__(self, module: nn.Module, actor_cfg, *, device: torch.device, group=None, total_steps: int = 1,
-                 trainable: bool = True):
+                 trainable: bool = True, expert_group=None):
         self.cfg = actor_cfg
         self.group = group
+        # expert-parallel parameters (marked ``_vo_expert``: each rank holds only its experts' slices) live in
+        # a second flat set sharded over ``expert_group`` -- the ranks that hold the same experts
+        self.expert_group = expert_group
+        self.eflat = None
         self.replica_group = None
         self.n_replicas = 1
         fs = int(getattr(actor_cfg.fsdp_config, "fsdp_size", -1) or -1)
@@ -211,9 +217,18 @@ class ShardedEngine:
             module.to(device=device, dtype=self.dtype)
             self.flat = None
         else:
+            has_experts = any(getattr(p, "_vo_expert", False) for p in module.parameters())
+            if has_experts and self.replica_group is not None:
+                raise ValueError("expert-parallel parameters with HSDP replicas are not supported")
+            not_expert = (lambda n, p: not getattr(p, "_vo_expert", False)) if has_experts else None
             self.flat = FlatParams(module, self.dtype, device, self.world, self.rank, self.group,
-                                   symmetric=self.replica_group is None and self._want_symmetric(actor_cfg, device,
-                                                                                                 self.group))
+                                   symmetric=(not has_experts and self.replica_group is None
+                                              and self._want_symmetric(actor_cfg, device, self.group)),
+                                   select=not_expert)
+            if has_experts:
+                eg = expert_group
+                self.eflat = FlatParams(module, self.dtype, device, D.world_size(eg), D.rank(eg), eg,
+                                        select=lambda n, p: getattr(p, "_vo_expert", False), owns_module=False)
         self.opt_step = 0
         self.sched = LRSchedule(actor_cfg.optim, total_steps) if trainable else None
         self.last_grad_norm = None
@@ -242,6 +257,8 @@ class ShardedEngine:
     def zero_grad(self) -> None:
         if self.flat is not None:
             self.flat.zero_grad()
+        if self.eflat is not None:
+            self.eflat.zero_grad()
 
     # ------------------------------------------------------------------ optimizer
     def optimizer_step(self) -> torch.Tensor:
@@ -270,27 +287,44 @@ class ShardedEngine:
             D.all_reduce(fp.grad_shard, group=self.replica_group)
         if self.world * self.n_replicas > 1:
             fp.grad_shard.mul_(1.0 / (self.world * self.n_replicas))
+        flats = [fp]
+        ef = self.eflat
+        if ef is not None:
+            # an expert's gradient already sums the contributions of every rank of its EP group (the exchange
+            # backward); summing over the ranks holding the same experts and dividing by the world size gives
+            # the same data-parallel mean as the dense parameters
+            D.reduce_scatter_into(ef.grad_shard, ef.main_grad, ef.group)
+            ef.grad_shard.mul_(1.0 / D.world_size())
+            flats.append(ef)
         self.opt_step += 1
         lr = self.sched.lr()
         b1, b2 = float(oc.betas[0]), float(oc.betas[1])
         max_norm = float(self.cfg.grad_clip if self.cfg.grad_clip is not None else oc.clip_grad)
+        # the dense and expert shards partition the parameters over the world: one all-reduce of the local
+        # squared norms gives the global norm
+        norm_group = self.group if ef is None else None
         if fp.master.is_cuda:
             sq = ext().sq_norm(fp.grad_shard)
-            D.all_reduce(sq, group=self.group)
-            ext().adamw_flat(fp.master, fp.grad_shard, fp.exp_avg, fp.exp_avg_sq, fp.shard_view(), lr, b1, b2,
-                             float(oc.eps), float(oc.weight_decay), self.opt_step, max_norm, sq, 1.0)
+            if ef is not None:
+                sq = sq + ext().sq_norm(ef.grad_shard)
+            D.all_reduce(sq, group=norm_group)
+            for f in flats:
+                ext().adamw_flat(f.master, f.grad_shard, f.exp_avg, f.exp_avg_sq, f.shard_view(), lr, b1, b2,
+                                 float(oc.eps), float(oc.weight_decay), self.opt_step, max_norm, sq, 1.0)
         else:
-            sq = (fp.grad_shard.double() ** 2).sum().float().reshape(1)
-            D.all_reduce(sq, group=self.group)
+            sq = sum((f.grad_shard.double() ** 2).sum() for f in flats).float().reshape(1)
+            D.all_reduce(sq, group=norm_group)
             norm = float(sq.sqrt())
             if math.isfinite(norm):
                 coef = min(1.0, max_norm / (norm + 1e-6)) if max_norm > 0 else 1.0
-                _adamw_torch(fp.master, fp.grad_shard * coef, fp.exp_avg, fp.exp_avg_sq, lr, b1, b2, float(oc.eps),
-                             float(oc.weight_decay), self.opt_step)
-                fp.shard_view().copy_(fp.master.to(fp.dtype))
-        D.all_gather_into(fp.flat, fp.shard_view().clone() if self.world > 1 else fp.shard_view(), self.group)
+                for f in flats:
+                    _adamw_torch(f.master, f.grad_shard * coef, f.exp_avg, f.exp_avg_sq, lr, b1, b2, float(oc.eps),
+                                 float(oc.weight_decay), self.opt_step)
+                    f.shard_view().copy_(f.master.to(f.dtype))
+        for f in flats:
+            D.all_gather_into(f.flat, f.shard_view().clone() if f.world > 1 else f.shard_view(), f.group)
+            f.zero_grad()
         self.sched.step()
-        fp.zero_grad()
         self.last_grad_norm = sq.sqrt()
         return self.last_grad_norm
 
@@ -348,6 +382,13 @@ class ShardedEngine:
                         "rng": torch.get_rng_state(),
                         "cuda_rng": torch.cuda.get_rng_state() if torch.cuda.is_available() else None},
                        os.path.join(local_path, f"extra_state_world_size_{W}_rank_{r}.pt"))
+        if self.eflat is not None:
+            # expert-parallel slices: every rank writes its own experts' master shard and moments (reloaded at
+            # the same world size and expert layout)
+            ef = self.eflat
+            torch.save({"names": ef.names, "shapes": ef.shapes, "master": ef.master.cpu(), "exp_avg": ef.exp_avg.cpu(),
+                        "exp_avg_sq": ef.exp_avg_sq.cpu(), "group_world": ef.world, "group_rank": ef.rank},
+                       os.path.join(local_path, f"expert_world_size_{D.world_size()}_rank_{D.rank()}.pt"))
         if r == 0 and writer:
             with open(os.path.join(local_path, "fsdp_config.json"), "w") as f:
                 json.dump({"FSDP_version": 2, "world_size": W, "layout": "flat-shard-adamw",
@@ -391,6 +432,21 @@ class ShardedEngine:
                 if k > 0:
                     fp.exp_avg[:k].copy_(m[lo:lo + k].to(self.device))
                     fp.exp_avg_sq[:k].copy_(v[lo:lo + k].to(self.device))
+        if self.eflat is not None:
+            ef = self.eflat
+            path = os.path.join(local_path, f"expert_world_size_{D.world_size()}_rank_{D.rank()}.pt")
+            if not os.path.exists(path):
+                raise FileNotFoundError(f"expert-parallel checkpoint {path} (expert slices reload at the same "
+                                        "world size and expert layout)")
+            e = torch.load(path, map_location="cpu")
+            if list(e["names"]) != list(ef.names) or e["group_world"] != ef.world:
+                raise ValueError("expert-parallel checkpoint layout differs from this run's")
+            ef.master.copy_(e["master"].to(self.device))
+            ef.exp_avg.copy_(e["exp_avg"].to(self.device))
+            ef.exp_avg_sq.copy_(e["exp_avg_sq"].to(self.device))
+            full = torch.empty(ef.padded, dtype=torch.float32, device=self.device)
+            D.all_gather_into(full, ef.master, ef.group)
+            ef.flat.copy_(full.to(ef.dtype))
         if "extra" in load_contents:
             r = self.rank if Wsaved == self.world else 0
             e = torch.load(os.path.join(local_path, f"extra_state_world_size_{Wsaved}_rank_{r}.pt"),
