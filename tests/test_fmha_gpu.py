@@ -32,7 +32,7 @@ def _ref(q, k, v, causal, scale):
     return o, lse
 
 
-@pytest.mark.parametrize("version", [1, 2, 3, 4])
+@pytest.mark.parametrize("version", [1, 2, 3, 4, 5])
 @pytest.mark.parametrize("B,H,Sq,Skv,D,causal", CASES)
 def test_fmha_fwd(E, B, H, Sq, Skv, D, causal, version):
     torch.manual_seed(0)
@@ -46,7 +46,7 @@ def test_fmha_fwd(E, B, H, Sq, Skv, D, causal, version):
     torch.testing.assert_close(lse, rlse, rtol=1e-3, atol=1e-3)
 
 
-@pytest.mark.parametrize("version", [1, 2, 3, 4])
+@pytest.mark.parametrize("version", [1, 2, 3, 4, 5])
 @pytest.mark.parametrize("D", [64, 128])
 def test_fmha_fwd_growing_max(E, D, version):
     """Later key blocks carry far larger scores: exercises the running-max rescale of O."""
@@ -101,7 +101,7 @@ def test_fmha_bwd(E, B, H, Sq, Skv, D, causal, version):
         assert rel < 2e-2, rel
 
 
-@pytest.mark.parametrize("fwd,bwd", [(2, 1), (3, 2), (4, 2)])
+@pytest.mark.parametrize("fwd,bwd", [(2, 1), (3, 2), (4, 2), (5, 2)])
 @pytest.mark.parametrize("D", [64, 128])
 def test_attention_split_matches_joint(E, fwd, bwd, D, monkeypatch):
     """Split outputs (image rows / text rows in separate tensors) equal slices of the joint output,
@@ -169,9 +169,10 @@ def test_split_attention_with_key_counts_backward():
     assert float(k.grad[1, :, Si + 40:].abs().max()) == 0.0 and float(v.grad[1, :, Si + 40:].abs().max()) == 0.0
 
 
+@pytest.mark.parametrize("version", [4, 5])
 @pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("causal", [False, True])
-def test_fmha_fwd4_key_counts_and_wide_scores(E, D, causal):
+def test_fmha_fwd4_key_counts_and_wide_scores(E, D, causal, version):
     """Forward v4 with per-sequence key counts (and the causal mask), scores spanning a wide range so the
     FMA-pipe exponentials see large negative arguments, against the fp32 reference."""
     torch.manual_seed(7)
@@ -182,12 +183,12 @@ def test_fmha_fwd4_key_counts_and_wide_scores(E, D, causal):
     kv_len = torch.tensor([S, 300, 65], dtype=torch.int32, device="cuda")
     scale = 1 / math.sqrt(D)
     if causal:
-        o, lse = E.fmha_fwd(q, k, v, True, scale, 4)
+        o, lse = E.fmha_fwd(q, k, v, True, scale, version)
         ro, rlse = _ref(q, k, v, True, scale)
         torch.testing.assert_close(o.float(), ro.transpose(1, 2), rtol=2e-2, atol=2e-2)
         torch.testing.assert_close(lse, rlse, rtol=1e-3, atol=1e-3)
         return
-    o, lse = E.fmha_fwd(q, k, v, False, scale, 4, 0, kv_len=kv_len)
+    o, lse = E.fmha_fwd(q, k, v, False, scale, version, 0, kv_len=kv_len)
     for b in range(B):
         n = int(kv_len[b])
         ro, rlse = _ref(q[b:b + 1], k[b:b + 1, :, :n], v[b:b + 1, :, :n], False, scale)

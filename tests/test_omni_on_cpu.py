@@ -177,3 +177,36 @@ def test_expert_sharded_grpo_step_matches_unsharded(tmp_path):
         assert part["wgu"].shape[0] == E // 2 and part["e0"] == r * E // 2
         assert part["n_expert_params"] > 0
         torch.testing.assert_close(part["wgu"], full["wgu"][r * E // 2:(r + 1) * E // 2], rtol=1e-3, atol=5e-5)
+
+
+def _main_omni(rank, world, ckpt, steps):
+    from verl_omni_b200.trainer.main_omni import run_omni
+    from verl_omni_b200.utils.config import load_config
+
+    cfg = load_config("omni_trainer", [
+        "trainer.device=cpu", "actor_rollout_ref.model.architecture=qwen3_omni_tiny", "data.train_batch_size=2",
+        "actor_rollout_ref.rollout.n=4", "actor_rollout_ref.rollout.response_length=6",
+        "data.prompt_text_tokens=5", "data.prompt_audio_tokens=3", "data.prompt_image_tokens=3",
+        "actor_rollout_ref.actor.ppo_micro_batch_size_per_gpu=3",
+        "actor_rollout_ref.actor.megatron.expert_model_parallel_size=2", f"trainer.total_training_steps={steps}",
+        "trainer.save_freq=1", f"trainer.default_local_dir={ckpt}", "trainer.logger=[]"])
+    hist = run_omni(cfg)
+    if rank == 0:
+        import json
+
+        with open(f"{ckpt}/hist_{steps}.json", "w") as f:
+            json.dump([{k: v for k, v in m.items() if isinstance(v, (int, float))} for m in hist], f)
+
+
+def test_main_omni_ep2_checkpoint_resume(tmp_path):
+    """The omni entry point from its config tree on two gloo ranks with EP=2 and micro-batches: one step,
+    a checkpoint (dense shards + expert slices), then a resumed run that continues at step 2."""
+    import json
+
+    run_ranks(_main_omni, 2, (str(tmp_path), 1))
+    assert (tmp_path / "global_step_1" / "actor" / "expert_world_size_2_rank_1.pt").exists()
+    run_ranks(_main_omni, 2, (str(tmp_path), 2))
+    h1 = json.load(open(tmp_path / "hist_1.json"))
+    h2 = json.load(open(tmp_path / "hist_2.json"))
+    assert len(h1) == 1 and len(h2) == 1 and h2[0]["training/global_step"] == 2
+    assert all(abs(v) < 1e6 for v in h2[0].values())

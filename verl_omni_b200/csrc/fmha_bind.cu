@@ -21,6 +21,15 @@ extern "C" int vo_fmha_fwd4(const void* q, const void* k, const void* v, void* o
 extern "C" int vo_fmha_fwd4_peer(const void* q, const void* k, const void* v, void* const* peer_o,
                                  void* const* peer_o2, int nranks, int sl, int si, int htot, int h0, float* lse, int B,
                                  int H, int Sq, int Skv, int D, float scale, cudaStream_t stream);
+extern "C" int vo_fmha_fwd5(const void* q, const void* k, const void* v, void* o, void* o2, int out_split, float* lse,
+                            const int* kv_len, int B, int H, int Sq, int Skv, int D, float scale, int causal,
+                            cudaStream_t stream);
+extern "C" int vo_fmha_fwd5_peer(const void* q, const void* k, const void* v, void* const* peer_o,
+                                 void* const* peer_o2, int nranks, int sl, int si, int htot, int h0, float* lse, int B,
+                                 int H, int Sq, int Skv, int D, float scale, cudaStream_t stream);
+extern "C" int vo_fmha_fwd4v(const void* q, const void* k, const void* v, void* o, void* o2, int out_split, float* lse,
+                             const int* kv_len, int B, int H, int Sq, int Skv, int D, float scale, int causal,
+                             cudaStream_t stream, int variant);
 extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const void* o, const void* dO,
                            const void* o2, const void* dO2, int split, const float* lse, void* dq, void* dk, void* dv,
                            float* delta, float* dq_acc, int B, int H, int Sq, int Skv, int D, float scale, int causal,
@@ -33,7 +42,8 @@ namespace vo {
 // version 1: one query tile per CTA, P staged in shared memory; version 2: two query tiles per CTA,
 // P and O resident in tensor memory; version 3: as 2 with two softmax warpgroups per query tile;
 // version 4: one query tile per CTA, two CTAs per SM, double-buffered 64-key score blocks (key counts
-// and the causal mask both supported).
+// and the causal mask both supported); version 5: as 4 with two independent softmax halves per tile at
+// head_dim 64 (other widths run version 4).
 // split > 0 (versions 2 / 3): query rows [0, split) go to o [B, split, H, D] and rows [split, Sq) to a
 // second tensor o2 [B, Sq - split, H, D] (the image / text halves of a joint attention, each feeding
 // its own output projection without a copy).
@@ -52,16 +62,22 @@ std::vector<torch::Tensor> fmha_fwd(torch::Tensor q, torch::Tensor k, torch::Ten
   torch::Tensor o2 = split > 0 ? torch::empty({B, Sq - split, H, D}, q.options()) : torch::Tensor();
   auto lse = torch::empty({B, H, Sq}, q.options().dtype(torch::kFloat32));
   int rc;
-  if (version == 4) {
+  if (version >= 4) {
     const int* kvp = nullptr;
     if (kv_len.has_value() && kv_len->defined()) {
       VO_CHECK_INPUT((*kv_len));
       TORCH_CHECK(kv_len->scalar_type() == torch::kInt32 && kv_len->numel() == B, "int32 [B] key counts");
       kvp = kv_len->data_ptr<int>();
     }
-    rc = vo_fmha_fwd4(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), split > 0 ? o2.data_ptr() : nullptr,
-                      (int)split, lse.data_ptr<float>(), kvp, B, H, Sq, Skv, D, (float)scale, causal ? 1 : 0,
-                      stream());
+    if (version >= 40) {  // version 4 with an explicit exponential split (measurements)
+      rc = vo_fmha_fwd4v(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), split > 0 ? o2.data_ptr() : nullptr,
+                         (int)split, lse.data_ptr<float>(), kvp, B, H, Sq, Skv, D, (float)scale, causal ? 1 : 0,
+                         stream(), (int)version);
+    } else {
+      auto fn = version >= 5 ? vo_fmha_fwd5 : vo_fmha_fwd4;
+      rc = fn(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), split > 0 ? o2.data_ptr() : nullptr, (int)split,
+              lse.data_ptr<float>(), kvp, B, H, Sq, Skv, D, (float)scale, causal ? 1 : 0, stream());
+    }
   } else if (kv_len.has_value() && kv_len->defined()) {
     // per-sequence key counts (right-padded keys masked); non-causal, forward v3
     VO_CHECK_INPUT((*kv_len));
@@ -105,7 +121,7 @@ void fmha_fwd_peer(torch::Tensor q, torch::Tensor k, torch::Tensor v, std::vecto
     if (!peer_o2.empty()) po2[i] = reinterpret_cast<void*>(peer_o2[i]);
   }
   auto lse = torch::empty({B, H, Sq}, q.options().dtype(torch::kFloat32));
-  auto fn = version == 4 ? vo_fmha_fwd4_peer : vo_fmha_fwd_peer;
+  auto fn = version >= 5 ? vo_fmha_fwd5_peer : version == 4 ? vo_fmha_fwd4_peer : vo_fmha_fwd_peer;
   const int rc = fn(q.data_ptr(), k.data_ptr(), v.data_ptr(), po.data(), po2.data(), n, (int)sl, (int)si, (int)htot,
                     (int)h0, lse.data_ptr<float>(), B, H, Sq, Skv, D, (float)scale, stream());
   TORCH_CHECK(rc == 0, "tcgen05 FMHA (peer output) launch failed: code ", rc);

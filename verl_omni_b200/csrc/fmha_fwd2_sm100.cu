@@ -35,6 +35,9 @@ constexpr unsigned long long WAIT_BUDGET = 8ull * 1000 * 1000 * 1000;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
 
 __device__ int g_error = 0;
+// mbarrier waits suspend the waiting thread for up to this long (it wakes early when the phase completes),
+// so spinning producer / issuer / softmax warps do not take issue slots from the working ones
+constexpr uint32_t kSuspendNs = 200000;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -51,9 +54,9 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t par) {
   uint32_t ok;
   asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(b)), "r"(par)
+      : "r"(smem_u32(b)), "r"(par), "r"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
@@ -107,6 +110,15 @@ __device__ __forceinline__ void ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
         "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+// 32 lanes x 16 columns; no wait
+__device__ __forceinline__ void ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
 __device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -720,13 +732,15 @@ __global__ void __launch_bounds__(fwd_threads<SPLIT>(), 1)
 // while block j was being exponentiated.  The other CTA on the SM supplies the second query tile that
 // keeps the tensor pipe busy while this CTA's softmax runs, and overlaps this CTA's prologue/epilogue.
 // Barriers: s_full[b] / p_full[b] per score buffer (a buffer's phase j >> 1 is block j), o_ready after
-// every PV (the softmax waits on it only to rescale O, or once before the epilogue).
+// every PV (the softmax waits on it only to rescale O: at block j, PV(j - 2) is known complete, so
+// phases j - 1 and j are the only candidates and parity tells them apart), o_final after the last PV.
 // A share (6 of 16 pairs) of the exponentials is evaluated on the FMA pipe: 2^x = 2^round(x) * p(f),
 // f = x - round(x) in [-1/2, 1/2], with round() by the 1.5 * 2^23 magic-number addition and p the
 // degree-3 polynomial minimising the relative error of 2^f on [-1/2, 1/2] (Lawson-weighted least
 // squares, max relative error 8.4e-5, far below the bf16 rounding of P); 2^round(x) is an integer add
 // into the exponent field.  The MUFU pipe alone is the bound of the score path at head_dim 64.
 constexpr int FWD4_THREADS = 192;
+constexpr int kFwd4Emu64 = 3;  // of every 8 exponential pairs, this many on the FMA pipe at head_dim 64
 constexpr int BK4 = 64;
 
 template <int D>
@@ -775,7 +789,7 @@ __device__ __forceinline__ void ex2_fma2(float x0, float x1, float& y0, float& y
   y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
-template <int D>
+template <int D, int EMU>
 __global__ void __launch_bounds__(FWD4_THREADS, 2)
     fmha_fwd4_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                      const __grid_constant__ CUtensorMap mv, const __grid_constant__ Params p) {
@@ -790,8 +804,9 @@ __global__ void __launch_bounds__(FWD4_THREADS, 2)
   uint64_t* v_empty = v_full + C::ST;    // [ST]
   uint64_t* s_full = v_empty + C::ST;    // [2] per score buffer
   uint64_t* p_full = s_full + 2;         // [2]
-  uint64_t* o_ready = p_full + 2;        // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_ready + 1);
+  uint64_t* o_ready = p_full + 2;        // [1] after every PV
+  uint64_t* o_final = o_ready + 1;       // [1] after the last PV
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -816,6 +831,7 @@ __global__ void __launch_bounds__(FWD4_THREADS, 2)
       mbar_init(&p_full[b], 4);
     }
     mbar_init(o_ready, 1);
+    mbar_init(o_final, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -888,6 +904,7 @@ __global__ void __launch_bounds__(FWD4_THREADS, 2)
         if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, abort_flag, 66)) break;
         fence_after();
         issue_pv(j);
+        if (j + 1 == nkv) commit(o_final);
         if (j + 2 < nkv) {
           const int jn = j + 2;
           if (!mbar_wait(&k_full[jn % C::ST], (jn / C::ST) & 1, abort_flag, 67)) break;
@@ -924,8 +941,11 @@ __global__ void __launch_bounds__(FWD4_THREADS, 2)
       wait_ld();
       float mx = -INFINITY;
       if (lim == BK4) {
+        // four independent max chains (short dependency chains), combined at the end
+        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int i = 0; i < 32; ++i) mx = max3(mx, __uint_as_float(a[i]), __uint_as_float(c[i]));
+        for (int i = 0; i < 32; ++i) mq[i & 3] = max3(mq[i & 3], __uint_as_float(a[i]), __uint_as_float(c[i]));
+        mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
@@ -961,21 +981,24 @@ __global__ void __launch_bounds__(FWD4_THREADS, 2)
       uint32_t w[32];
       float rs0 = 0.f, rs1 = 0.f;
       if (lim == BK4) {
+        float ra[4] = {0.f, 0.f, 0.f, 0.f}, rb[4] = {0.f, 0.f, 0.f, 0.f};  // four independent sum chains
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const uint32_t* v = i < 16 ? a : c;
           const int ii = i & 15;
           float x0, x1, e0, e1;
           ffma2(__uint_as_float(v[2 * ii]), __uint_as_float(v[2 * ii + 1]), sl2, nmb, x0, x1);
-          if ((ii & 7) >= 5) {
+          if ((ii & 7) >= 8 - EMU) {  // EMU of every 8 pairs on the FMA pipe
             ex2_fma2(x0, x1, e0, e1);
           } else {
             e0 = ex2(x0);
             e1 = ex2(x1);
           }
-          fadd2(rs0, rs1, e0, e1);
+          fadd2(ra[i & 3], rb[i & 3], e0, e1);
           w[i] = pack_bf16(e0, e1);
         }
+        rs0 = (ra[0] + ra[1]) + (ra[2] + ra[3]);
+        rs1 = (rb[0] + rb[1]) + (rb[2] + rb[3]);
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
@@ -995,7 +1018,8 @@ __global__ void __launch_bounds__(FWD4_THREADS, 2)
       if (lane == 0) mbar_arrive(&p_full[b]);
       l = l * alpha + (rs0 + rs1);
     }
-    if (ok && mbar_wait(o_ready, (nkv - 1) & 1, abort_flag, 70)) {
+    // o_ready could not tell the last PV from the one two blocks earlier (equal parity): a barrier of its own
+    if (ok && mbar_wait(o_final, 0, abort_flag, 70)) {
       fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const int bb = bh / p.H, h = bh % p.H;
@@ -1024,6 +1048,300 @@ __global__ void __launch_bounds__(FWD4_THREADS, 2)
   fence_before();
   __syncthreads();
   if (warp == 5) {
+    __syncwarp();
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256));
+  }
+}
+
+
+// ====================================================================================================
+// Forward v5 (head_dim 64): v4 with two softmax warpgroups per query tile.  Warpgroup h (warps 4h..4h+3)
+// owns keys [32 h, 32 h + 32) of every 64-key block with its own running max, row sum and accumulator
+// O_h (tensor-memory columns [128 + 64 h, 192 + 64 h)); the halves never synchronise inside the key loop
+// and are combined once in the epilogue.  Twice the softmax warps per SM sub-partition hide the
+// tensor-memory and MUFU latencies that bound v4 at this head width.  P of half h is packed into
+// columns [32 h, 32 h + 16) of the score buffer (half 0's P lands on its own, already-read columns).
+// 320 threads: warps 0..7 softmax, warp 8 TMA producer, warp 9 MMA issuer + TMEM allocator.
+constexpr int FWD5_THREADS = 320;
+
+__global__ void __launch_bounds__(FWD5_THREADS, 2)
+    fmha_fwd5_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+                     const __grid_constant__ CUtensorMap mv, const __grid_constant__ Params p) {
+  constexpr int D = 64;
+  using C = Cfg4<D>;
+  extern __shared__ __align__(1024) uint8_t raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;           // [ST]
+  uint64_t* k_empty = k_full + C::ST;    // [ST]
+  uint64_t* v_full = k_empty + C::ST;    // [ST]
+  uint64_t* v_empty = v_full + C::ST;    // [ST]
+  uint64_t* s_full = v_empty + C::ST;    // [2] per score buffer
+  uint64_t* p_full = s_full + 2;         // [2]: 8 warps arrive
+  uint64_t* o_ready = p_full + 2;        // [1] after every pair of PVs
+  uint64_t* o_final = o_ready + 1;       // [1] after the last pair
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // epilogue exchange of the halves' (max, sum) per row: [half][2][128], then a per-half count of warps
+  // that have written theirs (a bounded wait on it, never an unbounded barrier)
+  float* xch = reinterpret_cast<float*>(sm + C::BAR_OFF + 256);
+  int* xcnt = reinterpret_cast<int*>(xch + 512);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = p.npairs - 1 - (int)(blockIdx.x % p.npairs);
+  const int bh = blockIdx.x / p.npairs;
+  const int q0 = tile * BQ;
+  int kv_end = kv_limit(p, bh);
+  if (p.causal) kv_end = min(kv_end, q0 + BQ);
+  const int nkv = (kv_end + BK4 - 1) / BK4;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < C::ST; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 8);
+    }
+    mbar_init(o_ready, 1);
+    mbar_init(o_final, 1);
+    *abort_flag = 0;
+    xcnt[0] = xcnt[1] = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 9) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(256));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    if (lane == 0 && nkv > 0) {
+      mbar_expect_tx(q_full, C::Q_BYTES);
+      tma_load_3d(sm + C::Q_OFF, &mq, q_full, 0, q0, bh);
+      for (int j = 0; j < nkv; ++j) {
+        const int s = j % C::ST, ph = ((j / C::ST) & 1) ^ 1;
+        if (!mbar_wait(&k_empty[s], ph, abort_flag, 71)) break;
+        mbar_expect_tx(&k_full[s], C::KV_BYTES);
+        tma_load_3d(sm + C::K_OFF + s * C::KV_BYTES, &mk, &k_full[s], 0, j * BK4, bh);
+        if (!mbar_wait(&v_empty[s], ph, abort_flag, 72)) break;
+        mbar_expect_tx(&v_full[s], C::KV_BYTES);
+        tma_load_3d(sm + C::V_OFF + s * C::KV_BYTES, &mv, &v_full[s], 0, j * BK4, bh);
+      }
+    }
+  } else if (warp == 9) {
+    if (lane == 0 && nkv > 0) {
+      const uint32_t id_s = idesc(128, BK4, 0, 0);
+      const uint32_t id_o = idesc(128, D, 0, 1);
+      const uint32_t qa = smem_u32(sm + C::Q_OFF);
+      auto issue_s = [&](int j) {
+        const uint32_t ka = smem_u32(sm + C::K_OFF + (j % C::ST) * C::KV_BYTES);
+        const uint32_t Sb = tmem + (j & 1) * BK4;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) mma_ss(Sb, desc(qa + kk * 32, 16, 1024), desc(ka + kk * 32, 16, 1024), id_s, kk > 0);
+        commit(&s_full[j & 1]);
+        commit(&k_empty[j % C::ST]);
+      };
+      auto issue_pv = [&](int j) {
+        const uint32_t va = smem_u32(sm + C::V_OFF + (j % C::ST) * C::KV_BYTES);
+        const uint32_t Sb = tmem + (j & 1) * BK4;
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk)
+            mma_ts(tmem + C::O_COL + 64 * h, Sb + 32 * h + kk * 8, desc(va + (2 * h + kk) * 2048, 8192, 1024), id_o,
+                   (j > 0 || kk > 0) ? 1u : 0u);
+        commit(o_ready);
+        commit(&v_empty[j % C::ST]);
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag, 73);
+      for (int j = 0; ok && j < 2 && j < nkv; ++j) {
+        if (!(ok = mbar_wait(&k_full[j % C::ST], (j / C::ST) & 1, abort_flag, 74))) break;
+        fence_after();
+        issue_s(j);
+      }
+      for (int j = 0; ok && j < nkv; ++j) {
+        if (!mbar_wait(&v_full[j % C::ST], (j / C::ST) & 1, abort_flag, 75)) break;
+        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, abort_flag, 76)) break;
+        fence_after();
+        issue_pv(j);
+        if (j + 1 == nkv) commit(o_final);
+        if (j + 2 < nkv) {
+          const int jn = j + 2;
+          if (!mbar_wait(&k_full[jn % C::ST], (jn / C::ST) & 1, abort_flag, 77)) break;
+          fence_after();
+          issue_s(jn);
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax halves (warps 0..7)
+    const int hf = warp >> 2, quarter = warp & 3;
+    const int row = 32 * quarter + lane;
+    const int q = q0 + row;
+    const uint32_t lane_off = (uint32_t)(32 * quarter) << 16;
+    const uint32_t O_h = tmem + C::O_COL + 64 * hf + lane_off;
+    const float sl2 = p.scale_log2;
+    const int kvl = kv_limit(p, bh);
+    float m = -INFINITY, l = 0.f;
+    bool ok = nkv > 0;
+    for (int j = 0; ok && j < nkv; ++j) {
+      const int b = j & 1;
+      if (!mbar_wait(&s_full[b], (j >> 1) & 1, abort_flag, 78)) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      const uint32_t S_h = tmem + b * BK4 + 32 * hf + lane_off;
+      const int kv0 = j * BK4 + 32 * hf;
+      int lim = kvl - kv0;
+      if (p.causal) lim = min(lim, q - kv0 + 1);
+      lim = max(0, min(32, lim));
+      uint32_t a[32];
+      ld32_nowait(S_h, a);
+      wait_ld();
+      float mx = -INFINITY;
+      if (lim == 32) {
+        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int i = 0; i < 16; ++i) mq[i & 3] = max3(mq[i & 3], __uint_as_float(a[2 * i]), __uint_as_float(a[2 * i + 1]));
+        mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < lim) mx = fmaxf(mx, __uint_as_float(a[i]));
+      }
+      const float m_blk = mx * sl2;
+      float alpha = 1.f;
+      const bool move = m_blk > m + RESCALE_THRESHOLD || (m == -INFINITY && m_blk != -INFINITY);
+      if (move) {
+        alpha = (m == -INFINITY) ? 0.f : ex2(m - m_blk);
+        m = m_blk;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, move)) {
+        if (!mbar_wait(o_ready, (j - 1) & 1, abort_flag, 79)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {  // 16 columns at a time: the scores stay in registers
+          uint32_t o[16];
+          ld16_nowait(O_h + cc * 16, o);
+          wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          st16(O_h + cc * 16, o);
+        }
+      }
+      const float nmb = (m == -INFINITY) ? 0.f : -m;
+      uint32_t w[16];
+      float rs0 = 0.f, rs1 = 0.f;
+      if (lim == 32) {
+        float ra[4] = {0.f, 0.f, 0.f, 0.f}, rb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float x0, x1, e0, e1;
+          ffma2(__uint_as_float(a[2 * i]), __uint_as_float(a[2 * i + 1]), sl2, nmb, x0, x1);
+          if ((i & 7) >= 8 - kFwd4Emu64) {
+            ex2_fma2(x0, x1, e0, e1);
+          } else {
+            e0 = ex2(x0);
+            e1 = ex2(x1);
+          }
+          fadd2(ra[i & 3], rb[i & 3], e0, e1);
+          w[i] = pack_bf16(e0, e1);
+        }
+        rs0 = (ra[0] + ra[1]) + (ra[2] + ra[3]);
+        rs1 = (rb[0] + rb[1]) + (rb[2] + rb[3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int k = 2 * i;
+          const float e0 = k < lim ? ex2(fmaf(__uint_as_float(a[k]), sl2, nmb)) : 0.f;
+          const float e1 = k + 1 < lim ? ex2(fmaf(__uint_as_float(a[k + 1]), sl2, nmb)) : 0.f;
+          rs0 += e0;
+          rs1 += e1;
+          w[i] = pack_bf16(e0, e1);
+        }
+      }
+      st16(S_h, w);
+      wait_st();
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[b]);
+      l = l * alpha + (rs0 + rs1);
+    }
+    if (ok && mbar_wait(o_final, 0, abort_flag, 80)) {
+      fence_after();
+      xch[(hf * 2 + 0) * 128 + row] = m;
+      xch[(hf * 2 + 1) * 128 + row] = l;
+      __threadfence_block();
+      __syncwarp();
+      if (lane == 0) atomicAdd(&xcnt[hf], 1);
+      bool seen = false;
+      const unsigned long long t0 = clock64();
+      while (!(seen = (*reinterpret_cast<volatile int*>(&xcnt[hf ^ 1]) >= 4))) {
+        if (*abort_flag) break;
+        if (clock64() - t0 > WAIT_BUDGET) {
+          atomicCAS(&g_error, 0, 81);
+          *abort_flag = 1;
+          break;
+        }
+      }
+      __threadfence_block();
+      if (seen) {
+      const float m_o = xch[((hf ^ 1) * 2 + 0) * 128 + row], l_o = xch[((hf ^ 1) * 2 + 1) * 128 + row];
+      const float m_out = fmaxf(m, m_o);
+      const float c_me = (m == -INFINITY) ? 0.f : ex2(m - m_out);
+      const float c_ot = (m_o == -INFINITY) ? 0.f : ex2(m_o - m_out);
+      const float lt = l * c_me + l_o * c_ot;
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      // this half writes output columns [32 hf, 32 hf + 32): O_0 and O_1 combined with their weights
+      const float c0 = (hf == 0 ? c_me : c_ot) * inv, c1 = (hf == 0 ? c_ot : c_me) * inv;
+      const bool row_ok = q < p.Sq;
+      __nv_bfloat16* dst = row_ok ? out_row(p, bh / p.H, q, bh % p.H, D) + 32 * hf : nullptr;
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch) {  // 16 output columns at a time
+        uint32_t o0[16], o1[16];
+        ld16_nowait(tmem + C::O_COL + 32 * hf + 16 * ch + lane_off, o0);
+        ld16_nowait(tmem + C::O_COL + 64 + 32 * hf + 16 * ch + lane_off, o1);
+        wait_ld();
+        if (row_ok) {
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              v[i] = __uint_as_float(o0[g * 8 + i]) * c0 + __uint_as_float(o1[g * 8 + i]) * c1;
+            uint4 pk;
+            pk.x = pack_bf16(v[0], v[1]);
+            pk.y = pack_bf16(v[2], v[3]);
+            pk.z = pack_bf16(v[4], v[5]);
+            pk.w = pack_bf16(v[6], v[7]);
+            *reinterpret_cast<uint4*>(dst + 16 * ch + g * 8) = pk;
+          }
+        }
+      }
+      if (row_ok) {
+        if (hf == 0) p.lse[(int64_t)bh * p.Sq + q] = (m_out + __log2f(lt)) * 0.69314718055994531f;
+      }
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 9) {
     __syncwarp();
     fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256));
@@ -1070,18 +1388,31 @@ static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMa
   return (int)cudaGetLastError();
 }
 
-template <int D>
+template <int D, int EMU>
 static int launch4(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const Params& p,
                    unsigned grid, cudaStream_t stream) {
   static bool set = false;
   const int bytes = Cfg4<D>::BYTES + 1024;
   if (!set) {
     const cudaError_t e =
-        cudaFuncSetAttribute(fmha_fwd4_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        cudaFuncSetAttribute(fmha_fwd4_kernel<D, EMU>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e != cudaSuccess) return (int)e;
     set = true;
   }
-  fmha_fwd4_kernel<D><<<grid, FWD4_THREADS, bytes, stream>>>(mq, mk, mv, p);
+  fmha_fwd4_kernel<D, EMU><<<grid, FWD4_THREADS, bytes, stream>>>(mq, mk, mv, p);
+  return (int)cudaGetLastError();
+}
+
+static int launch5(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const Params& p,
+                   unsigned grid, cudaStream_t stream) {
+  static bool set = false;
+  const int bytes = Cfg4<64>::BYTES + 1024 + 3072;  // + the epilogue's (max, sum) exchange and counters
+  if (!set) {
+    const cudaError_t e = cudaFuncSetAttribute(fmha_fwd5_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return (int)e;
+    set = true;
+  }
+  fmha_fwd5_kernel<<<grid, FWD5_THREADS, bytes, stream>>>(mq, mk, mv, p);
   return (int)cudaGetLastError();
 }
 
@@ -1098,7 +1429,7 @@ static int fwd2_impl(const void* q, const void* k, const void* v, void* o, void*
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15)
     return -2;
   CUtensorMap mq, mk, mv;
-  const int kv_rows = split == 4 ? BK4 : 128;
+  const int kv_rows = split >= 4 ? BK4 : 128;
   int r = map3(&mq, q, B * H, Sq, D);
   if (!r) r = map3(&mk, k, B * H, Skv, D, kv_rows);
   if (!r) r = map3(&mv, v, B * H, Skv, D, kv_rows);
@@ -1124,7 +1455,7 @@ static int fwd2_impl(const void* q, const void* k, const void* v, void* o, void*
   p.Skv = Skv;
   p.H = H;
   // v4: one query tile per CTA (npairs counts tiles); v1-v3: pairs of tiles
-  p.npairs = split == 4 ? (Sq + BQ - 1) / BQ : (Sq + 2 * BQ - 1) / (2 * BQ);
+  p.npairs = split >= 4 ? (Sq + BQ - 1) / BQ : (Sq + 2 * BQ - 1) / (2 * BQ);  // 40..48 count as 4
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal;
   p.o = reinterpret_cast<__nv_bfloat16*>(o);
@@ -1134,8 +1465,26 @@ static int fwd2_impl(const void* q, const void* k, const void* v, void* o, void*
   p.lse = lse;
   const long long grid = (long long)p.npairs * B * H;
   if (grid == 0) return 0;
-  if (split == 4)
-    return D == 64 ? launch4<64>(mq, mk, mv, p, (unsigned)grid, stream) : launch4<128>(mq, mk, mv, p, (unsigned)grid, stream);
+  if (split == 5 && D == 64) return launch5(mq, mk, mv, p, (unsigned)grid, stream);
+  // exponentials on the FMA pipe per 8 pairs: kFwd4Emu (head_dim 64, where MUFU bounds the score path),
+  // none at head_dim 128 (tensor-bound); versions 40..48 select 0..8 of 8 for measurements
+  if (split >= 40 && split <= 48) {
+    const int emu = split - 40;
+    if (D == 64) {
+      switch (emu) {
+        case 0: return launch4<64, 0>(mq, mk, mv, p, (unsigned)grid, stream);
+        case 1: return launch4<64, 1>(mq, mk, mv, p, (unsigned)grid, stream);
+        case 2: return launch4<64, 2>(mq, mk, mv, p, (unsigned)grid, stream);
+        case 4: return launch4<64, 4>(mq, mk, mv, p, (unsigned)grid, stream);
+        default: return launch4<64, 3>(mq, mk, mv, p, (unsigned)grid, stream);
+      }
+    }
+    return emu == 0 ? launch4<128, 0>(mq, mk, mv, p, (unsigned)grid, stream)
+                    : launch4<128, 2>(mq, mk, mv, p, (unsigned)grid, stream);
+  }
+  if (split >= 4)
+    return D == 64 ? launch4<64, kFwd4Emu64>(mq, mk, mv, p, (unsigned)grid, stream)
+                   : launch4<128, 0>(mq, mk, mv, p, (unsigned)grid, stream);
   if (D == 64)
     return split == 3 ? launch<64, 3>(mq, mk, mv, p, (unsigned)grid, stream)
            : split == 2 ? launch<64, 2>(mq, mk, mv, p, (unsigned)grid, stream)
@@ -1202,4 +1551,28 @@ extern "C" int vo_fmha_fwd4_peer(const void* q, const void* k, const void* v, vo
                                  int H, int Sq, int Skv, int D, float scale, cudaStream_t stream) {
   vo_fmha2::PeerOut po{peer_o, peer_o2, nranks, sl, si, htot, h0};
   return vo_fmha2::fwd2_impl(q, k, v, nullptr, nullptr, 0, lse, B, H, Sq, Skv, D, scale, 0, stream, 4, &po);
+}
+
+// forward v5: head_dim 64 with two independent softmax halves per query tile (other widths run v4)
+extern "C" int vo_fmha_fwd5(const void* q, const void* k, const void* v, void* o, void* o2, int out_split, float* lse,
+                            const int* kv_len, int B, int H, int Sq, int Skv, int D, float scale, int causal,
+                            cudaStream_t stream) {
+  return vo_fmha2::fwd2_impl(q, k, v, o, o2, out_split, lse, B, H, Sq, Skv, D, scale, causal, stream, 5, nullptr,
+                             kv_len);
+}
+
+extern "C" int vo_fmha_fwd5_peer(const void* q, const void* k, const void* v, void* const* peer_o,
+                                 void* const* peer_o2, int nranks, int sl, int si, int htot, int h0, float* lse, int B,
+                                 int H, int Sq, int Skv, int D, float scale, cudaStream_t stream) {
+  vo_fmha2::PeerOut po{peer_o, peer_o2, nranks, sl, si, htot, h0};
+  return vo_fmha2::fwd2_impl(q, k, v, nullptr, nullptr, 0, lse, B, H, Sq, Skv, D, scale, 0, stream, 5, &po);
+}
+
+// forward v4 with an explicit exponential split (variant 40..48: 0..8 of every 8 pairs on the FMA pipe)
+extern "C" int vo_fmha_fwd4v(const void* q, const void* k, const void* v, void* o, void* o2, int out_split, float* lse,
+                             const int* kv_len, int B, int H, int Sq, int Skv, int D, float scale, int causal,
+                             cudaStream_t stream, int variant) {
+  if (variant < 40 || variant > 48) return -1;
+  return vo_fmha2::fwd2_impl(q, k, v, o, o2, out_split, lse, B, H, Sq, Skv, D, scale, causal, stream, variant,
+                             nullptr, kv_len);
 }

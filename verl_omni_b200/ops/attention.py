@@ -18,7 +18,8 @@ import torch.nn.functional as F
 from verl_omni_b200.ops._ext import ext
 
 
-# forward kernel generation: 4 = one query tile per CTA, two CTAs per SM, double-buffered 64-key score
+# forward kernel generation: 5 = as 4 with two independent softmax halves per tile at head_dim 64 (other
+# widths run 4); 4 = one query tile per CTA, two CTAs per SM, double-buffered 64-key score
 # blocks; 3 = two query tiles per CTA, P/O in tensor memory, two softmax warpgroups per tile; 2 = one
 # softmax warpgroup per tile; 1 = one query tile per CTA
 _FWD_VERSION = int(os.environ.get("VO_FMHA_FWD", "3"))
@@ -26,7 +27,7 @@ _FWD_VERSION = int(os.environ.get("VO_FMHA_FWD", "3"))
 
 def _kv_version() -> int:
     """Forward generation for per-sequence key counts (versions 3 and 4 support them)."""
-    return 4 if _FWD_VERSION >= 4 else 3
+    return min(_FWD_VERSION, 5) if _FWD_VERSION >= 4 else 3
 # backward kernel generation: 2 = pipelined (P^T/dS^T in tensor memory, concurrent dQ drain), 1 = serial
 _BWD_VERSION = int(os.environ.get("VO_FMHA_BWD", "2"))
 

@@ -318,7 +318,10 @@ def bench_fmha(a) -> list[dict]:
     cases = {"fwd": (lambda: e.fmha_fwd(q, k, v, False, scale, 1), flops_f),
              "fwd2": (lambda: e.fmha_fwd(q, k, v, False, scale, 2), flops_f),
              "fwd3": (lambda: e.fmha_fwd(q, k, v, False, scale, 3), flops_f),
-             "fwd4": (lambda: e.fmha_fwd(q, k, v, False, scale, 4), flops_f)}
+             "fwd4": (lambda: e.fmha_fwd(q, k, v, False, scale, 4), flops_f),
+             "fwd5": (lambda: e.fmha_fwd(q, k, v, False, scale, 5), flops_f)}
+    for emu in (0, 1, 2, 3, 4):  # version 4 with emu of every 8 exponential pairs on the FMA pipe
+        cases[f"fwd4e{emu}"] = (lambda emu=emu: e.fmha_fwd(q, k, v, False, scale, 40 + emu), flops_f)
     if hasattr(e, "fmha_bwd"):
         cases["bwd"] = (lambda: e.fmha_bwd(q, k, v, o, lse, do, False, scale, 1), 2.5 * flops_f)
         cases["bwd2"] = (lambda: e.fmha_bwd(q, k, v, o, lse, do, False, scale, 2), 2.5 * flops_f)

@@ -145,7 +145,7 @@ def joint_attention_fused(h_img: torch.Tensor, h_txt: Optional[torch.Tensor], qk
     # 3. attention; every output row goes to its token's owner
     sc = scale if scale is not None else dh ** -0.5
     e.fmha_fwd_peer(q, k, v, ws.o_img.peer_ptrs, ws.o_txt.peer_ptrs if St else [], Sl, Si, heads, r * Hg, sc,
-                    4 if A._FWD_VERSION >= 4 else 3)
+                    A._kv_version())
     stream_barrier(group, h_img.device)
     o_img = ws.o_img.tensor.view(B, Si, Dm)
     o_txt = ws.o_txt.tensor.view(B, St, Dm) if St else None

@@ -270,19 +270,19 @@ class FlowDPPOLoss(DiffusionLossFn):
         loss = per.mean()
         with torch.no_grad():
             m = {
-                "actor/ppo_kl": torch.mean(-log_ratio).item(),
-                "actor/approx_kl": (0.5 * log_ratio.pow(2)).mean().item(),
-                "actor/ratio_mean": ratio.mean().item(),
-                "actor/ratio_std": ratio.std(unbiased=False).item(),
-                "actor/ratio_min": ratio.min().item(),
-                "actor/ratio_max": ratio.max().item(),
-                "actor/kl_new_old_mean": kl.mean().item(),
-                "actor/kl_new_old_max": kl.max().item(),
-                "actor/kl_mask_fraction": high.float().mean().item(),
-                "actor/pos_rm_fraction": pos.float().mean().item(),
-                "actor/neg_rm_fraction": neg.float().mean().item(),
-                "actor/masked_fraction": rm.float().mean().item(),
-                "actor/unmasked_fraction": keep.float().mean().item(),
+                "actor/ppo_kl": torch.mean(-log_ratio).detach(),
+                "actor/approx_kl": (0.5 * log_ratio.pow(2)).mean().detach(),
+                "actor/ratio_mean": ratio.mean().detach(),
+                "actor/ratio_std": ratio.std(unbiased=False).detach(),
+                "actor/ratio_min": ratio.min().detach(),
+                "actor/ratio_max": ratio.max().detach(),
+                "actor/kl_new_old_mean": kl.mean().detach(),
+                "actor/kl_new_old_max": kl.max().detach(),
+                "actor/kl_mask_fraction": high.float().mean().detach(),
+                "actor/pos_rm_fraction": pos.float().mean().detach(),
+                "actor/neg_rm_fraction": neg.float().mean().detach(),
+                "actor/masked_fraction": rm.float().mean().detach(),
+                "actor/unmasked_fraction": keep.float().mean().detach(),
             }
         return loss, m
 
@@ -319,12 +319,12 @@ class GRPOGuardLoss(DiffusionLossFn):
         loss = per.mean() / (sqrt_dt_mean ** 2)
         with torch.no_grad():
             m = {
-                "actor/ppo_kl": torch.mean(-log_ratio).item(),
-                "actor/pg_clipfrac": torch.mean((torch.abs(ratio - 1.0) > lc.clip_ratio).float()).item(),
-                "actor/pg_clipfrac_higher": torch.mean((ratio - 1.0 > lc.clip_ratio).float()).item(),
-                "actor/pg_clipfrac_lower": torch.mean((1.0 - ratio > lc.clip_ratio).float()).item(),
-                "actor/ratio_mean": ratio.mean().item(),
-                "actor/ratio_std": ratio.std().item() if ratio.numel() > 1 else 0.0,
+                "actor/ppo_kl": torch.mean(-log_ratio).detach(),
+                "actor/pg_clipfrac": torch.mean((torch.abs(ratio - 1.0) > lc.clip_ratio).float()).detach(),
+                "actor/pg_clipfrac_higher": torch.mean((ratio - 1.0 > lc.clip_ratio).float()).detach(),
+                "actor/pg_clipfrac_lower": torch.mean((1.0 - ratio > lc.clip_ratio).float()).detach(),
+                "actor/ratio_mean": ratio.mean().detach(),
+                "actor/ratio_std": ratio.std() if ratio.numel() > 1 else torch.zeros((), device=ratio.device),
             }
         return loss, m
 
@@ -403,11 +403,11 @@ class DPOLoss(DiffusionLossFn):
         with torch.no_grad():
             rc, rr = -0.5 * beta * w_diff, -0.5 * beta * l_diff
             m = {
-                "actor/dpo_loss": loss.item(),
-                "actor/implicit_acc": ((inside > 0).sum().float() / inside.numel()).item(),
-                "rewards/chosen": rc.mean().item(),
-                "rewards/rejected": rr.mean().item(),
-                "rewards/margins": (rc - rr).mean().item(),
+                "actor/dpo_loss": loss.detach(),
+                "actor/implicit_acc": ((inside > 0).sum().float() / inside.numel()).detach(),
+                "rewards/chosen": rc.mean().detach(),
+                "rewards/rejected": rr.mean().detach(),
+                "rewards/margins": (rc - rr).mean().detach(),
             }
         return loss, m
 
@@ -452,13 +452,13 @@ class DiffusionNFTLoss(DiffusionLossFn):
         loss = policy_loss + lc.ref_kl_coef * ref_kl
         with torch.no_grad():
             m = {
-                "actor/policy_loss": policy_loss.item(),
-                "actor/positive_loss": pos_loss.mean().item(),
-                "actor/negative_loss": neg_loss.mean().item(),
-                "actor/ref_kl_loss": ref_kl.item(),
-                "actor/old_deviate": ((forward_prediction - old) ** 2).mean().item(),
-                "actor/reward_prob_mean": w.mean().item(),
-                "actor/total_loss": loss.item(),
+                "actor/policy_loss": policy_loss.detach(),
+                "actor/positive_loss": pos_loss.mean().detach(),
+                "actor/negative_loss": neg_loss.mean().detach(),
+                "actor/ref_kl_loss": ref_kl.detach(),
+                "actor/old_deviate": ((forward_prediction - old) ** 2).mean().detach(),
+                "actor/reward_prob_mean": w.mean().detach(),
+                "actor/total_loss": loss.detach(),
             }
         return loss, m
 
@@ -537,7 +537,7 @@ class _MeanKL(DiffusionLossFn):
 
     def __call__(self, *, config, model_output, data):
         kl = self._kl(model_output["prev_sample_mean"], data[self.target_key], model_output["std_dev_t"])
-        return DiffusionLossResult(kl.mean(), {self.metric: kl.mean().item()})
+        return DiffusionLossResult(kl.mean(), {self.metric: kl.mean().detach()})
 
 
 @register_diffusion_loss("kl")
@@ -549,7 +549,7 @@ class KLLoss(_MeanKL):
     @classmethod
     def compute_loss(cls, *, prev_sample_mean, ref_prev_sample_mean, std_dev_t):
         kl = cls._kl(prev_sample_mean, ref_prev_sample_mean, std_dev_t)
-        return kl.mean(), {cls.metric: kl.mean().item()}
+        return kl.mean(), {cls.metric: kl.mean().detach()}
 
 
 @register_diffusion_loss("distill_kl")
@@ -561,7 +561,7 @@ class DistillKLLoss(_MeanKL):
     @classmethod
     def compute_loss(cls, *, prev_sample_mean, teacher_prev_sample_mean, std_dev_t):
         kl = cls._kl(prev_sample_mean, teacher_prev_sample_mean, std_dev_t)
-        return kl.mean(), {cls.metric: kl.mean().item()}
+        return kl.mean(), {cls.metric: kl.mean().detach()}
 
 
 @register_diffusion_loss("distill_fm_mse")
@@ -572,7 +572,7 @@ class DistillFlowMatchingMSELoss(DiffusionLossFn):
     @classmethod
     def compute_loss(cls, *, noise_pred, teacher_noise_pred):
         mse = ((noise_pred - teacher_noise_pred) ** 2).mean()
-        return mse, {"actor/distill_fm_mse_loss": mse.item()}
+        return mse, {"actor/distill_fm_mse_loss": mse.detach()}
 
     def __call__(self, *, config, model_output, data):
         loss, m = self.compute_loss(noise_pred=model_output["noise_pred"], teacher_noise_pred=data["teacher_noise_pred"])

@@ -31,8 +31,11 @@ from verl_omni_b200.workers.rollout.llm_rollout import LLMRolloutEngine
 class OmniGRPOTrainer:
     def __init__(self, cfg: MoEConfig, actor_cfg: DiffusionActorConfig, *, device, n: int = 8,
                  prompt_text: int = 16, audio_tokens: int = 4, image_tokens: int = 4, response_len: int = 8,
-                 loss_mode: str = "grpo", ep_group=None, tp_group=None, seed: int = 0):
+                 loss_mode: str = "grpo", ep_group=None, tp_group=None, seed: int = 0,
+                 micro_batch_size: Optional[int] = None, temperature: float = 1.0, kv_block_size: int = 0,
+                 total_steps: int = 1000):
         torch.manual_seed(seed)
+        self.micro_batch_size = micro_batch_size  # sequences per forward/backward (None: the whole batch)
         self.cfg, self.actor_cfg, self.device, self.n = cfg, actor_cfg, device, n
         self.prompt_text, self.audio_tokens, self.image_tokens = prompt_text, audio_tokens, image_tokens
         ep = None
@@ -57,9 +60,11 @@ class OmniGRPOTrainer:
             from verl_omni_b200.parallel.tensor_parallel import TPContext
 
             self.model.tp = TPContext(tp_group)
-        self.engine = ShardedEngine(self.model, actor_cfg, device=device, total_steps=1000,
+        self.engine = ShardedEngine(self.model, actor_cfg, device=device, total_steps=total_steps,
                                     expert_group=self.expert_dp_group)
-        self.rollout = LLMRolloutEngine(self.model, max_new_tokens=response_len, device=device)
+        self.rollout = LLMRolloutEngine(self.model, max_new_tokens=response_len, device=device,
+                                        temperature=temperature, kv_block_size=kv_block_size)
+        self.temperature = temperature
         self.loss_fn = get_omni_loss_fn(loss_mode)
         self.loss_mode = loss_mode
         self.step_count = 0
@@ -84,32 +89,96 @@ class OmniGRPOTrainer:
         tgt = torch.zeros_like(ids[:, :-1])
         tgt[:, P - 1:] = ids[:, P:]
         lp = self.model(ids[:, :-1], audio_feats=data.batch["audio_feats"].to(self.device),
-                        image_patches=data.batch["image_patches"].to(self.device), targets=tgt)
+                        image_patches=data.batch["image_patches"].to(self.device), targets=tgt,
+                        temperature=self.temperature)
         return lp[:, P - 1:]
 
+    def _micro(self, data: DataProto) -> list[slice]:
+        n = len(data)
+        mb = self.micro_batch_size or n
+        return [slice(i, min(n, i + mb)) for i in range(0, n, mb)]
+
     def step(self, num_prompts: int = 2) -> dict:
+        """One GRPO / GSPO step on ``num_prompts`` prompts x ``n`` responses of this data-parallel rank:
+        rollout -> rule reward -> group advantage -> old log-probs -> micro-batched update -> optimizer."""
         self.step_count += 1
         t0 = time.perf_counter()
+        timing = {}
         prompts = self.make_prompts(num_prompts, seed=1000 * self.step_count + self.dp_rank).repeat(self.n)
+        tg = time.perf_counter()
         out = self.rollout.generate(prompts, seed=self.step_count)
         rewards = hash_token_reward(out, seed=7).to(self.device)
         adv = group_normalize(rewards, out.non_tensor_batch["uid"], global_std=False)
         mask = out.batch["response_mask"].to(self.device)
+        self._sync()
+        timing["gen"] = time.perf_counter() - tg
+        tg = time.perf_counter()
+        slices = self._micro(out)
         with torch.no_grad():
-            old = self._resp_logprobs(out)
+            old = torch.cat([self._resp_logprobs(out.select_idxs(sl)) for sl in slices], 0)
+        self._sync()
+        timing["old_log_prob"] = time.perf_counter() - tg
+        tg = time.perf_counter()
         self.engine.train_mode()
         self.engine.zero_grad()
-        logp = self._resp_logprobs(out)
-        loss, m = self.loss_fn(logp, old, adv, mask)
-        (loss * self.tp_size).backward()
+        # each micro-batch's token-mean (sequence-mean for GSPO) is weighted by its share of the batch, so the
+        # accumulated gradient is that of the whole batch's mean
+        seq_level = self.loss_mode == "gspo"
+        total = float(mask.shape[0]) if seq_level else float(mask.sum().clamp_min(1))
+        losses, ms = [], []
+        for sl in slices:
+            logp = self._resp_logprobs(out.select_idxs(sl))
+            mk = mask[sl]
+            loss, m = self.loss_fn(logp, old[sl], adv[sl], mk)
+            w = (mk.shape[0] if seq_level else float(mk.sum().clamp_min(1))) / total
+            (loss * (w * self.tp_size)).backward()
+            losses.append(loss.detach() * w)
+            ms.append(m)
         norm = self.engine.optimizer_step()
-        m.update({"actor/pg_loss": float(loss.detach()), "actor/grad_norm": float(norm.reshape(())),
-                  "critic/rewards/mean": float(rewards.mean()),
+        self._sync()
+        timing["update_actor"] = time.perf_counter() - tg
+        m = {k: float(np.mean([x[k] for x in ms])) for k in ms[0]}
+        m.update({"actor/pg_loss": float(torch.stack(losses).sum()), "actor/grad_norm": float(norm.reshape(())),
+                  "actor/lr": self.engine.lr(), "critic/rewards/mean": float(rewards.mean()),
+                  "training/global_step": self.step_count,
+                  "response_length/mean": float(mask.sum(-1).mean()),
                   "rollout_corr/logprob_abs_diff_mean": float(((old - out.batch["rollout_log_probs"].to(self.device))
                                                                .abs() * mask).sum() / mask.sum())})
+        m.update(M.compute_timing_metrics_diffusion(timing, len(out)))
         m.update(M.compute_throughput_metrics_diffusion(time.perf_counter() - t0, len(out) * self.dp,
                                                          D.world_size()))
         return m
+
+    def _sync(self) -> None:
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+
+    # ------------------------------------------------------------------ checkpoint / resume
+    def save_checkpoint(self, root_dir: str) -> str:
+        """``{root_dir}/global_step_{N}/actor`` (engine shards, expert slices) + ``data.pt`` +
+        ``latest_checkpointed_iteration.txt`` -- the diffusion trainers' layout."""
+        import os
+
+        root = os.path.join(root_dir, f"global_step_{self.step_count}")
+        self.engine.save_checkpoint(os.path.join(root, "actor"), self.step_count)
+        if D.rank() == 0:
+            torch.save({"global_step": self.step_count}, os.path.join(root, "data.pt"))
+            with open(os.path.join(root_dir, "latest_checkpointed_iteration.txt"), "w") as f:
+                f.write(str(self.step_count))
+        D.barrier()
+        return root
+
+    def load_checkpoint(self, root_dir: str) -> bool:
+        import os
+
+        marker = os.path.join(root_dir, "latest_checkpointed_iteration.txt")
+        if not os.path.exists(marker):
+            return False
+        with open(marker) as f:
+            root = os.path.join(root_dir, f"global_step_{int(f.read().strip())}")
+        self.engine.load_checkpoint(os.path.join(root, "actor"))
+        self.step_count = int(torch.load(os.path.join(root, "data.pt"))["global_step"])
+        return True
 
     def dpo_step(self, chosen: DataProto, rejected: DataProto, ref_model: MoELLM, beta: float = 0.1) -> dict:
         """Offline omni DPO on (chosen, rejected) response pairs against a frozen reference."""

@@ -40,18 +40,26 @@ def new_engine(model_type: str, backend: str, *args, **kwargs):
 
 
 def _mean_metrics(ms: list[dict]) -> dict:
+    """Means of per-micro-step metrics.  Device tensors are stacked on the device and read back with one
+    copy; host floats are averaged on the host."""
     acc: dict = defaultdict(list)
     for m in ms:
         for k, v in m.items():
-            acc[k].append(v if isinstance(v, torch.Tensor) else torch.tensor(float(v)))
-    out = {}
-    if not acc:
-        return out
-    keys = list(acc.keys())
-    stacked = torch.stack([torch.stack([t.detach().float().reshape(()).cpu() if t.device.type != "cpu" else
-                                        t.detach().float().reshape(()) for t in acc[k]]).mean() for k in keys])
-    for k, v in zip(keys, stacked.tolist()):
-        out[k] = v
+            acc[k].append(v)
+    out, dev_keys, dev_vals = {}, [], []
+    for k, vs in acc.items():
+        if all(isinstance(v, torch.Tensor) for v in vs):
+            dev_keys.append(k)
+            dev_vals.append(torch.stack([v.detach().float().reshape(()) for v in vs]).mean())
+        else:
+            out[k] = float(sum(float(v) for v in vs) / len(vs))
+    if dev_keys:
+        by_dev: dict = defaultdict(list)
+        for k, v in zip(dev_keys, dev_vals):
+            by_dev[v.device].append((k, v))
+        for items in by_dev.values():
+            vals = torch.stack([v for _, v in items]).cpu().tolist()
+            out.update({k: x for (k, _), x in zip(items, vals)})
     return out
 
 
@@ -143,8 +151,7 @@ class PPODiffusionEngine:
                 losses.append(loss.detach() * gas)
                 metrics.append(m)
         grad_norm = eng.optimizer_step()
+        metrics.append({"actor/pg_loss": torch.stack(losses).float().mean(), "actor/grad_norm": grad_norm.reshape(())})
         res = _mean_metrics(metrics)
-        res["actor/pg_loss"] = float(torch.stack(losses).float().mean())
-        res["actor/grad_norm"] = float(grad_norm.reshape(()))
         res["actor/lr"] = eng.lr()
         return res

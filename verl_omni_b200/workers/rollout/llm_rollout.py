@@ -63,8 +63,10 @@ class LLMRolloutEngine:
         else:
             caches = [KVCache(B, cfg.kv_heads, P + self.max_new_tokens, cfg.head_dim, dev, self.module.embed.dtype)
                       for _ in self.module.layers]
-        logits = self.module(ids, caches=caches, pos0=0, audio_feats=batch.batch.get("audio_feats"),
-                             image_patches=batch.batch.get("image_patches"))[:, -1]
+        # prefill: the vocabulary projection of the last prompt position only
+        h = self.module(ids, caches=caches, pos0=0, audio_feats=batch.batch.get("audio_feats"),
+                        image_patches=batch.batch.get("image_patches"), return_hidden=True)
+        logits = self.module.lm_head(h[:, -1:].contiguous()).float()[:, -1]
         out_ids, out_lp = [], []
         done = torch.zeros(B, dtype=torch.bool, device=ids.device)
         mask = []
