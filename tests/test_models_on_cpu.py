@@ -70,3 +70,32 @@ def test_flowgrpo_step_new_families(arch):
     from tests._dist_util import run_ranks
 
     run_ranks(_one_step, 1, (arch,))
+
+
+def test_sd3_diffusers_export_import_round_trip(tmp_path):
+    """The fused MMDiT exports diffusers SD3Transformer2DModel names (to_qkv split into to_q/k/v, the patch
+    linear as a [D, C, p, p] convolution) and a fresh model loaded from that directory computes the same
+    output."""
+    import json
+
+    from safetensors.torch import load_file
+
+    from verl_omni_b200.models import hf_io
+    from verl_omni_b200.models.mmdit import MMDiT, MMDiTConfig
+
+    torch.manual_seed(0)
+    m = MMDiT(MMDiTConfig.tiny())
+    named = dict(m.named_parameters())
+    hf_io.save_diffusers(named, m, str(tmp_path))
+    sd = load_file(str(tmp_path / "diffusion_pytorch_model.safetensors"))
+    assert "transformer_blocks.0.attn.to_q.weight" in sd and "transformer_blocks.0.attn2.to_k.weight" in sd
+    assert sd["pos_embed.proj.weight"].shape == (64, 4, 2, 2)
+    assert "transformer_blocks.1.ff_context.net.2.weight" not in sd  # context-pre-only last block
+    assert json.load(open(tmp_path / "config.json"))["num_layers"] == 2
+    torch.manual_seed(1)
+    m2 = MMDiT(MMDiTConfig.tiny())
+    assert hf_io.load_diffusers(m2, str(tmp_path)) == len(named)
+    x = torch.randn(2, 4, 8, 8)
+    t = torch.tensor([100.0, 700.0])
+    ctx, pooled = torch.randn(2, 12, 48), torch.randn(2, 32)
+    torch.testing.assert_close(m2(x, t, ctx, pooled), m.to(torch.bfloat16).float()(x, t, ctx, pooled), rtol=2e-2, atol=2e-2)

@@ -103,7 +103,8 @@ class JointBlock(nn.Module):
         # chunk order: 0 shift_msa, 1 scale_msa, 2 gate_msa, 3 shift_mlp, 4 scale_mlp, 5 gate_mlp,
         #              6 shift_msa2, 7 scale_msa2, 8 gate_msa2
         h = adaln_layernorm(x, mod, 0, 1, self.n_mod, self.eps)
-        hc = adaln_layernorm(c, modc, 0, 1, self.n_mod_c, self.eps)
+        # AdaLayerNormZero chunks: shift, scale, ...; the context-pre-only block's AdaLayerNormContinuous: scale, shift
+        hc = adaln_layernorm(c, modc, 1 if self.cpo else 0, 0 if self.cpo else 1, self.n_mod_c, self.eps)
         S = Si + St
         dev, dt = x.device, x.dtype
         if (key_mask is None and type(self.to_qkv) is Linear and type(self.add_qkv) is Linear

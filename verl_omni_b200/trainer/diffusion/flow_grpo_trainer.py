@@ -45,6 +45,18 @@ from verl_omni_b200.workers.utils_losses import diffusion_loss
 _log = logging.getLogger(__name__)
 
 
+def load_pretrained(module, path) -> int:
+    """``actor_rollout_ref.model.path``: ``random-init`` (or empty) keeps the random weights; a diffusers
+    pipeline / transformer directory (or a safetensors file) loads through the diffusers name mapping."""
+    if not path or str(path) in ("random-init", "null", "None"):
+        return 0
+    from verl_omni_b200.models import hf_io
+
+    if not hf_io.supported(module):
+        raise NotImplementedError(f"loading pretrained weights for the {getattr(module, 'family', '?')!r} family")
+    return hf_io.load_diffusers(module, str(path))
+
+
 class PolicyGradientTrainer:
     def __init__(self, config, *, arch: Optional[str] = None, device: Optional[torch.device] = None):
         self.config = config
@@ -81,6 +93,7 @@ class PolicyGradientTrainer:
         cuda = self.device.type == "cuda"
         # ---------------------------------------------------------------- models
         module = self.spec.build()
+        load_pretrained(module, self.model_cfg.path)
         if self.model_cfg.enable_gradient_checkpointing and hasattr(module, "gradient_checkpointing"):
             module.gradient_checkpointing = True
         module.to(self.device)
@@ -102,6 +115,20 @@ class PolicyGradientTrainer:
         self.scheduler = self.adapter.build_scheduler(T, image_seq_len=seq, device=self.device)
         self.actor = PPODiffusionEngine(module, self.adapter, self.scheduler, self.actor_cfg, self.model_cfg,
                                         device=self.device, total_steps=self.total_steps)
+        # on-policy distillation: a frozen teacher of the same family scores the rollout trajectories
+        self.teacher = None
+        dist_cfg = config.get("distillation", {}) or {}
+        if bool(dist_cfg.get("enabled", dist_cfg.get("enable", False))):
+            tcfg = (dist_cfg.get("teacher_models", {}) or {}).get("teacher_model", {}) or {}
+            torch.manual_seed(int(tcfg.get("seed", 1234)))
+            teacher_module = self.spec.build()
+            load_pretrained(teacher_module, tcfg.get("model_path"))
+            teacher_module.to(self.device)
+            if self.sp_group is not None:
+                teacher_module.sp_group = self.sp_group
+            self.teacher = PPODiffusionEngine(teacher_module, self.adapter, self.scheduler, self.actor_cfg,
+                                              self.model_cfg, device=self.device, trainable=False)
+            torch.manual_seed(seed)
         self.ref = None
         if ref_module is not None:
             self.ref = PPODiffusionEngine(ref_module, self.adapter, self.scheduler, self.actor_cfg, self.model_cfg,
@@ -235,6 +262,14 @@ class PolicyGradientTrainer:
                     with use_adapter(self.actor.module, None):
                         r = self.actor.infer_batch(out, keys=("prev_sample_mean",))
                 out.batch["ref_prev_sample_mean"] = r.batch["prev_sample_mean"]
+        if self.teacher is not None:
+            with timer("teacher"):
+                fm = self.actor_cfg.distill_loss_mode == "distill_fm_mse"
+                tm = self.teacher.infer_batch(out, keys=("prev_sample_mean", "noise_pred") if fm else
+                                              ("prev_sample_mean",))
+                out.batch["teacher_prev_sample_mean"] = tm.batch["prev_sample_mean"]
+                if fm:
+                    out.batch["teacher_noise_pred"] = tm.batch["noise_pred"]
         if self.actor_cfg.diffusion_loss.loss_mode in ("flow_dppo", "grpo_guard"):
             with timer("old_mean"):
                 om = self.actor.infer_batch(out, keys=("prev_sample_mean",))
@@ -253,6 +288,53 @@ class PolicyGradientTrainer:
         metrics.update(corr_metrics)
         metrics.update(M.compute_data_metrics_diffusion(scores, adv[:, 0], out.non_tensor_batch["uid"]))
         return metrics
+
+    # ------------------------------------------------------------------ validation
+    @torch.no_grad()
+    def validate(self) -> dict:
+        """Validation generations (reference ``_validate``, ``ray_diffusion_trainer.py:508-641``): a fixed
+        prompt set (``data.val_num_prompts``, seeded apart from the training prompts), ``val_kwargs.n``
+        samples each with the ``val_kwargs`` sampling settings (steps, noise level, seed), scored by the
+        reward manager.  Returns ``val-core/<data_source>/reward/mean@n`` plus ``val-aux`` spread metrics, all
+        reduced over the data-parallel ranks."""
+        vk = self.config.actor_rollout_ref.rollout.get("val_kwargs", {}) or {}
+        n = int(vk.get("n", 1))
+        nval = int(self.config.data.get("val_num_prompts", 0) or 0) or max(self.dp, self.prompts_per_rank)
+        if not hasattr(self, "_val_dataset"):
+            self._val_dataset = SyntheticPromptDataset(
+                nval, seed=int(self.config.data.get("seed", 0) or 0) + 7919,
+                token_len=self.spec.prompt_len if self.spec.text_encoder else 0, vocab=self.spec.vocab,
+                cond_shapes=self.spec.cond_shapes)
+        per = -(-nval // self.dp)
+        ids = list(range(self.dp_rank * per, min(nval, (self.dp_rank + 1) * per)))
+        scores = torch.zeros(0, device=self.device)
+        if ids:
+            cond = self.encode_prompts(self._val_dataset.get_batch(ids))
+            cond.non_tensor_batch["uid"] = np.array([f"val-{i}" for i in ids], dtype=object)
+            gen = cond.repeat(n, interleave=True)
+            algo = vk.get("algo", {}) or {}
+            steps = (vk.get("pipeline", {}) or {}).get("num_inference_steps")
+            out = self.rollout.generate(gen, seed=int(vk.get("seed", 42)), global_step=0, record_logprobs=False,
+                                        window=(0, int(steps or self.rollout_cfg.pipeline.num_inference_steps)),
+                                        noise_level=float(algo.get("noise_level", 0.0)),
+                                        sde_type=algo.get("sde_type"), num_inference_steps=steps)
+            out.non_tensor_batch.update({k: v[:len(out)] for k, v in gen.non_tensor_batch.items()})
+            scores, _ = self.reward_fn(out)
+            scores = scores.to(self.device).float()
+        # mean / std / best-of-n over every rank's samples
+        stats = torch.tensor([float(scores.sum()), float((scores ** 2).sum()), float(scores.numel()),
+                              float(scores.view(-1, n).max(-1).values.sum()) if scores.numel() else 0.0],
+                             dtype=torch.float64, device=self.device)
+        if self.world > 1:
+            D.all_reduce(stats)
+        if self.sp > 1:
+            stats /= self.sp  # the ranks of a sequence-parallel group score the same samples
+        cnt = max(1.0, float(stats[2]))
+        mean = float(stats[0]) / cnt
+        var = max(0.0, float(stats[1]) / cnt - mean * mean)
+        src = str(self.config.data.get("data_source", "synthetic"))
+        return {f"val-core/{src}/reward/mean@{n}": mean, f"val-aux/{src}/reward/std@{n}": var ** 0.5,
+                f"val-core/{src}/reward/best@{n}/mean": float(stats[3]) / max(1.0, cnt / n)}
 
     # ------------------------------------------------------------------ one step
     def step(self, global_ids: Optional[list[int]] = None) -> dict:
@@ -345,8 +427,18 @@ class PolicyGradientTrainer:
         if self.config.trainer.resume_mode == "auto":
             self.maybe_resume()
         hist = []
+        test_freq = int(self.config.trainer.get("test_freq", -1) or -1)
+        if self.config.trainer.get("val_before_train", False):
+            v = self.validate()
+            hist.append(dict(v, **{"training/global_step": self.global_step}))
+            if log_fn is not None and self.rank == 0:
+                log_fn(hist[-1])
         while self.global_step < steps:
             m = self.step()
+            if test_freq > 0 and (self.global_step % test_freq == 0 or self.global_step >= steps):
+                t0 = time.perf_counter()
+                m.update(self.validate())
+                m["timing_s/testing"] = time.perf_counter() - t0
             hist.append(m)
             if log_fn is not None and self.rank == 0:
                 log_fn(m)

@@ -369,9 +369,16 @@ class ShardedEngine:
             if hf_export and r == 0 and writer:
                 from safetensors.torch import save_file
 
-                os.makedirs(os.path.join(local_path, "huggingface"), exist_ok=True)
-                save_file({n: v.to(torch.bfloat16).contiguous().cpu() for n, v in fp.param_views(full)},
-                          os.path.join(local_path, "huggingface", "diffusion_pytorch_model.safetensors"))
+                from verl_omni_b200.models import hf_io
+
+                hf_dir = os.path.join(local_path, "huggingface")
+                named = dict(fp.param_views(full))
+                if hf_io.supported(self.module):  # diffusers parameter names and layouts
+                    hf_io.save_diffusers(named, self.module, hf_dir)
+                else:
+                    os.makedirs(hf_dir, exist_ok=True)
+                    save_file({n: v.to(torch.bfloat16).contiguous().cpu() for n, v in named.items()},
+                              os.path.join(hf_dir, "diffusion_pytorch_model.safetensors"))
             del full
         if "optimizer" in save_contents and writer:
             torch.save({"exp_avg": fp.exp_avg.cpu(), "exp_avg_sq": fp.exp_avg_sq.cpu(), "step": self.opt_step,

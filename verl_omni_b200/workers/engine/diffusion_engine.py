@@ -141,7 +141,7 @@ class PPODiffusionEngine:
                      "advantages": mb.batch["advantages"][:, t].to(self.device),
                      "gradient_accumulation_steps": gas, "sp_size": self.sp}
                 for k in ("ref_prev_sample_mean", "old_prev_sample_mean", "teacher_prev_sample_mean",
-                          "rollout_is_weights"):
+                          "teacher_noise_pred", "rollout_is_weights"):
                     if k in mb.batch:
                         d[k] = mb.batch[k][:, t].to(self.device)
                 if "uid" in mb.non_tensor_batch:

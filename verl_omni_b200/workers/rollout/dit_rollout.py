@@ -74,7 +74,9 @@ class DiTRolloutEngine:
         self.decoder = decoder
         T = rollout_cfg.pipeline.num_inference_steps
         seq = sched_seq_len or int(np.prod(self.latent_shape[-2:])) // 4
+        self._sched_seq = seq
         self.scheduler = adapter.build_scheduler(T, image_seq_len=seq, device=device)
+        self._schedulers = {T: self.scheduler}
         self._abort = threading.Event()
         self.sleeping = False
 
@@ -111,19 +113,22 @@ class DiTRolloutEngine:
     def generate(self, batch: DataProto, *, seed: int = 0, global_step: int = 0, record_logprobs: bool = True,
                  decode: bool = True, row_seeds: Optional[torch.Tensor] = None,
                  window: Optional[tuple[int, int]] = None, noise_level: Optional[float] = None,
-                 sde_type: Optional[str] = None, guidance_scale: Optional[float] = None) -> DataProto:
+                 sde_type: Optional[str] = None, guidance_scale: Optional[float] = None,
+                 num_inference_steps: Optional[int] = None) -> DataProto:
         """``batch`` holds the conditioning tensors (adapter ``cond_keys``, optional ``negative_*``).
 
         ``row_seeds`` (int64 [B]) keys each sample's initial noise and SDE noise by its own seed, so
         a sample's trajectory does not depend on how requests were packed into device batches.
         ``window`` / ``noise_level`` / ``sde_type`` / ``guidance_scale`` override the configured
-        values for this call (validation sampling, request-level parameters).
+        values for this call (validation sampling, request-level parameters); ``num_inference_steps``
+        samples with a schedule of that many steps (built once per length).
         """
         if self.sleeping:
             self.wake_up()
         self._abort.clear()
         cfg, algo = self.cfg, self.cfg.algo
-        T = cfg.pipeline.num_inference_steps
+        T = int(num_inference_steps or cfg.pipeline.num_inference_steps)
+        sched_T = self._scheduler_for(T)
         w0, W = window if window is not None else select_sde_window(algo, T, global_step, seed)
         B = len(batch)
         guidance = cfg.pipeline.guidance_scale if guidance_scale is None else guidance_scale
@@ -139,7 +144,8 @@ class DiTRolloutEngine:
                 break
             mb = batch.select_idxs(slice(s, min(B, s + mbs)))
             rs = row_seeds[s:min(B, s + mbs)] if row_seeds is not None else None
-            chunks.append(self._run_chunk(mb, T, w0, W, seed * 1_000_003 + s, guidance, record_logprobs, rs, nl, st))
+            chunks.append(self._run_chunk(mb, T, w0, W, seed * 1_000_003 + s, guidance, record_logprobs, rs, nl, st,
+                                          sched_T))
         done = sum(len(c) for c in chunks)
         out = DataProto.concat(chunks) if chunks else DataProto()
         if done < B:  # aborted: synthesize aborted outputs for the unfinished requests
@@ -157,8 +163,13 @@ class DiTRolloutEngine:
         imgs = [self.decoder(latents[i:i + chunk]) for i in range(0, latents.shape[0], chunk)]
         return torch.cat(imgs, 0)
 
+    def _scheduler_for(self, T: int):
+        if T not in self._schedulers:
+            self._schedulers[T] = self.adapter.build_scheduler(T, image_seq_len=self._sched_seq, device=self.device)
+        return self._schedulers[T]
+
     def _run_chunk(self, mb: DataProto, T: int, w0: int, W: int, seed: int, guidance, record: bool,
-                   row_seeds: Optional[torch.Tensor], noise_level: float, sde_type: str) -> DataProto:
+                   row_seeds: Optional[torch.Tensor], noise_level: float, sde_type: str, sched=None) -> DataProto:
         keys = self.adapter.cond_keys()
         cond = {k: mb.batch[k].to(self.device) for k in keys}
         neg = None
@@ -170,7 +181,7 @@ class DiTRolloutEngine:
             x = normal_rows(row_seeds, self.latent_shape, _INIT_NOISE_OFFSET, self.device)
         else:
             x = self._initial_noise(b, seed)
-        sched = self.scheduler
+        sched = sched or self.scheduler
         traj = [x] if w0 == 0 else []
         logps, steps = [], []
         for t in range(T):
