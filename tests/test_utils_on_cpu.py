@@ -2,6 +2,8 @@
 
 import json
 
+import numpy as np
+
 import pytest
 import torch
 
@@ -117,3 +119,59 @@ def test_non_diffusers_model_base_roundtrip(tmp_path):
     m2.enable_gradient_checkpointing()
     m2(x).sum().backward()
     assert x.grad is not None
+
+
+def test_parquet_datasets(tmp_path):
+    """Prompt / offline-DPO / MLLM-DPO parquet datasets: tensors and prompts round-trip through pyarrow."""
+    import pandas as pd
+
+    from verl_omni_b200.utils.datasets_parquet import (ParquetMLLMDPODataset, ParquetOfflineDPODataset,
+                                                       ParquetPromptDataset)
+
+    rng = np.random.default_rng(0)
+    emb = [rng.standard_normal((5, 8)).astype("float32") for _ in range(3)]
+    msgs = lambda t: [{"role": "user", "content": t}]  # noqa: E731  (chat-message prompts, verl's format)
+    pd.DataFrame({"prompt": [msgs("a cat"), msgs("a dog"), msgs("hi")],
+                  "negative_prompt": ["", "blurry", ""], "data_source": ["ocr"] * 3,
+                  "reward_model": [{"ground_truth": "CAT"}, {"ground_truth": "DOG"}, {"ground_truth": None}],
+                  "prompt_embeds": [e.reshape(-1).tolist() for e in emb], "prompt_embeds_shape": [[5, 8]] * 3}
+                 ).to_parquet(tmp_path / "p.parquet")
+    ds = ParquetPromptDataset(str(tmp_path / "p.parquet"), cond_keys=("prompt_embeds",), token_len=6, vocab=100)
+    b = ds.get_batch([2, 0])
+    assert b.batch["input_ids"].shape == (2, 6) and b.batch["prompt_embeds"].shape == (2, 5, 8)
+    assert torch.allclose(b.batch["prompt_embeds"][1], torch.tensor(emb[0]))
+    assert list(b.non_tensor_batch["ground_truth"]) == [None, "CAT"] and b.non_tensor_batch["raw_prompt"][0] == "hi"
+    lat = rng.standard_normal((2, 4, 4, 4)).astype("float32")
+    pd.DataFrame({"img_win_latents": [lat[0].reshape(-1).tolist()], "img_win_latents_shape": [[4, 4, 4]],
+                  "img_lose_latents": [lat[1].reshape(-1).tolist()], "img_lose_latents_shape": [[4, 4, 4]],
+                  "prompt_embeds": [emb[0].reshape(-1).tolist()], "prompt_embeds_shape": [[5, 8]],
+                  "win_score": [0.9], "lose_score": [0.1]}).to_parquet(tmp_path / "d.parquet")
+    d = ParquetOfflineDPODataset(str(tmp_path / "d.parquet"), cond_keys=("prompt_embeds",)).get_batch([0])
+    assert d.batch["latents_clean"].shape == (2, 4, 4, 4)
+    torch.testing.assert_close(d.batch["rm_scores"], torch.tensor([0.9, 0.1]))
+    pd.DataFrame({"prompt_ids": [[5, 6, 7], [8]], "chosen_ids": [[1, 2], [3]], "rejected_ids": [[4], [5, 6, 7]]}
+                 ).to_parquet(tmp_path / "m.parquet")
+    ch, rj = ParquetMLLMDPODataset(str(tmp_path / "m.parquet")).get_pairs([0, 1])
+    assert ch.batch["input_ids"].shape == (2, 5) and rj.batch["response_mask"].sum().item() == 4
+
+
+def test_trainer_reads_parquet_prompts(tmp_path):
+    """data.train_files pointing at a parquet file feeds the trainer's prompts (text-encoder model)."""
+    import pandas as pd
+
+    from verl_omni_b200.parallel import dist as D
+    from verl_omni_b200.trainer.diffusion.flow_grpo_trainer import PolicyGradientTrainer
+
+    pd.DataFrame({"prompt": [[{"role": "user", "content": f"prompt number {i}"}] for i in range(6)],
+                  "data_source": ["toy"] * 6}).to_parquet(tmp_path / "train.parquet")
+    cfg = load_config("diffusion_trainer", [
+        "trainer.device=cpu", "actor_rollout_ref.model.architecture=tiny_dit", "data.train_batch_size=2",
+        f"data.train_files={tmp_path / 'train.parquet'}", "actor_rollout_ref.rollout.n=2",
+        "actor_rollout_ref.rollout.pipeline.num_inference_steps=2", "actor_rollout_ref.actor.ppo_mini_batch_size=2",
+        "actor_rollout_ref.actor.ppo_micro_batch_size_per_gpu=4", "trainer.resume_mode=disable", "trainer.logger=[]",
+        "trainer.total_training_steps=1"])
+    D.init_distributed(device="cpu")
+    t = PolicyGradientTrainer(cfg)
+    assert len(t.dataset) == 6
+    m = t.step()
+    assert m["actor/grad_norm"] == m["actor/grad_norm"]

@@ -740,7 +740,7 @@ __global__ void __launch_bounds__(fwd_threads<SPLIT>(), 1)
 // squares, max relative error 8.4e-5, far below the bf16 rounding of P); 2^round(x) is an integer add
 // into the exponent field.  The MUFU pipe alone is the bound of the score path at head_dim 64.
 constexpr int FWD4_THREADS = 192;
-constexpr int kFwd4Emu64 = 3;  // of every 8 exponential pairs, this many on the FMA pipe at head_dim 64
+constexpr int kFwd4Emu64 = 0;  // of every 8 exponential pairs, this many on the FMA pipe at head_dim 64 (0 measured fastest)
 constexpr int BK4 = 64;
 
 template <int D>

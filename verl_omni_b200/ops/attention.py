@@ -22,7 +22,7 @@ from verl_omni_b200.ops._ext import ext
 # widths run 4); 4 = one query tile per CTA, two CTAs per SM, double-buffered 64-key score
 # blocks; 3 = two query tiles per CTA, P/O in tensor memory, two softmax warpgroups per tile; 2 = one
 # softmax warpgroup per tile; 1 = one query tile per CTA
-_FWD_VERSION = int(os.environ.get("VO_FMHA_FWD", "3"))
+_FWD_VERSION = int(os.environ.get("VO_FMHA_FWD", "4"))
 
 
 def _kv_version() -> int:

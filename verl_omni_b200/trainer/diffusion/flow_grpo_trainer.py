@@ -172,10 +172,22 @@ class PolicyGradientTrainer:
                 cond_keys=tuple(self.adapter.cond_keys()), num_workers=int(agent_cfg.get("num_workers", 8)),
                 default_agent_loop=str(agent_cfg.get("default_agent_loop", "diffusion_single_turn_agent")))
         # ---------------------------------------------------------------- data
-        n_prompts = int(config.data.get("synthetic", {}).get("num_prompts", 1024))
-        self.dataset = SyntheticPromptDataset(n_prompts, seed=int(config.data.get("seed", 0) or 0),
-                                              token_len=self.spec.prompt_len if self.spec.text_encoder else 0,
-                                              vocab=self.spec.vocab, cond_shapes=self.spec.cond_shapes)
+        train_files = config.data.get("train_files", "synthetic")
+        if train_files and str(train_files) != "synthetic":
+            # parquet prompts (verl RLHF layout): precomputed conditioning columns, or text for the text encoder
+            from verl_omni_b200.utils.datasets_parquet import ParquetPromptDataset
+
+            self.dataset = ParquetPromptDataset(
+                train_files, cond_keys=tuple(self.spec.cond_shapes),
+                token_len=self.spec.prompt_len if self.spec.text_encoder else 0, vocab=self.spec.vocab,
+                prompt_key=str(config.data.get("prompt_key", "prompt")),
+                max_samples=int(config.data.get("train_max_samples", -1) or -1))
+            n_prompts = len(self.dataset)
+        else:
+            n_prompts = int(config.data.get("synthetic", {}).get("num_prompts", 1024))
+            self.dataset = SyntheticPromptDataset(n_prompts, seed=int(config.data.get("seed", 0) or 0),
+                                                  token_len=self.spec.prompt_len if self.spec.text_encoder else 0,
+                                                  vocab=self.spec.vocab, cond_shapes=self.spec.cond_shapes)
         self.sampler = ResumableSampler(n_prompts, gbs, seed=int(config.data.get("seed", 0) or 0),
                                         shuffle=bool(config.data.get("shuffle", True)))
         self.loss_fn = lambda model_output, data: diffusion_loss(self.actor_cfg, model_output, data)
