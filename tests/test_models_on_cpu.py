@@ -99,3 +99,61 @@ def test_sd3_diffusers_export_import_round_trip(tmp_path):
     t = torch.tensor([100.0, 700.0])
     ctx, pooled = torch.randn(2, 12, 48), torch.randn(2, 32)
     torch.testing.assert_close(m2(x, t, ctx, pooled), m.to(torch.bfloat16).float()(x, t, ctx, pooled), rtol=2e-2, atol=2e-2)
+
+
+def test_reference_family_scorers_through_multi_manager():
+    """PickScore / HPSv3 / OCR judge / UnifiedReward / CLAP / ImageBind-shaped scorers (tiny sizes) and the
+    MMK12 / choice rules, combined by the multi reward manager."""
+    import numpy as np
+
+    from verl_omni_b200.models.scorers import choice_reward, mmk12_reward
+    from verl_omni_b200.utils.dataproto import DataProto
+    from verl_omni_b200.workers.reward.reward_manager import (MultiVisualRewardManager, VisualRewardManager,
+                                                              build_model_scorer)
+
+    torch.manual_seed(0)
+    dev = torch.device("cpu")
+    vit = dict(image_size=32, patch=8, vision_dim=32, vision_depth=1, vision_heads=2)
+    vlm = dict(vit, lm_dim=32, lm_depth=1, lm_heads=2, vocab=300, text_len=8)
+    subs = [("pickscore", build_model_scorer("pickscore", dev, torch.float32, **vit, text_dim=32, text_depth=1,
+                                             text_heads=2, embed_dim=16, vocab=300, text_len=8)),
+            ("hpsv3", build_model_scorer("hpsv3", dev, torch.float32, **vlm)),
+            ("ocr", build_model_scorer("ocr", dev, torch.float32, new_tokens=3, **vlm)),
+            ("unified_reward", build_model_scorer("unified_reward", dev, torch.float32, new_tokens=3, **vlm)),
+            ("clap", build_model_scorer("clap", dev, torch.float32, n_mels=8, audio_dim=32, audio_depth=1,
+                                        audio_heads=2, text_dim=32, text_depth=1, text_heads=2, embed_dim=16,
+                                        vocab=300, text_len=8)),
+            ("imagebind", build_model_scorer("imagebind", dev, torch.float32, image_size=32, patch=8, dim=32,
+                                             depth=2, heads=2, n_mels=8, embed_dim=16, vocab=300, text_len=8))]
+    batch = DataProto({"images": torch.rand(3, 3, 64, 64) * 2 - 1, "audio_mels": torch.randn(3, 10, 8)},
+                      {"raw_prompt": np.array(["a red cat", "SALE", "two dogs"], dtype=object),
+                       "ground_truth": np.array([None, "SALE", None], dtype=object)})
+    mgr = MultiVisualRewardManager([(n, VisualRewardManager(s, name=n), 1.0, True) for n, s in subs])
+    total, metrics = mgr(batch)
+    assert total.shape == (3,) and torch.isfinite(total).all()
+    assert all(f"reward/{n}_mean" in metrics for n, _ in subs)
+    assert mmk12_reward(["so x = \\boxed{42}", "41"], ["42", "42"]).tolist() == [1.0, 0.0]
+    assert choice_reward(["I pick (B)", "answer: C"], ["B", "D"]).tolist() == [1.0, 0.0]
+
+
+def test_trainer_multi_reward_config():
+    """reward.sub_rewards builds the weighted multi-reward manager inside the trainer (default scorer + a
+    tiny PickScore-shaped model)."""
+    from verl_omni_b200.parallel import dist as D
+    from verl_omni_b200.trainer.diffusion.flow_grpo_trainer import PolicyGradientTrainer
+    from verl_omni_b200.utils.config import load_config
+
+    cfg = load_config("diffusion_trainer", [
+        "trainer.device=cpu", "actor_rollout_ref.model.architecture=tiny_dit", "data.train_batch_size=2",
+        "actor_rollout_ref.rollout.n=2", "actor_rollout_ref.rollout.pipeline.num_inference_steps=2",
+        "actor_rollout_ref.actor.ppo_mini_batch_size=2", "actor_rollout_ref.actor.ppo_micro_batch_size_per_gpu=4",
+        "trainer.resume_mode=disable", "trainer.logger=[]", "trainer.total_training_steps=1"])
+    cfg.reward.sub_rewards = [{"name": "latent", "scorer": "default", "weight": 0.5},
+                              {"name": "hps", "scorer": "hpsv3", "weight": 1.0, "required": False,
+                               "sizes": {"image_size": 32, "patch": 8, "vision_dim": 32, "vision_depth": 1,
+                                         "vision_heads": 2, "lm_dim": 32, "lm_depth": 1, "lm_heads": 2,
+                                         "vocab": 300, "text_len": 8}}]
+    D.init_distributed(device="cpu")
+    t = PolicyGradientTrainer(cfg)
+    m = t.step()
+    assert "reward/latent_mean" in m and ("reward/hps_mean" in m or "reward/hps_failed" in m)

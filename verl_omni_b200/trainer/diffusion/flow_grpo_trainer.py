@@ -45,6 +45,30 @@ from verl_omni_b200.workers.utils_losses import diffusion_loss
 _log = logging.getLogger(__name__)
 
 
+def build_multi_reward(subs: list, device, dtype, default=None):
+    """``reward.sub_rewards`` -> a weighted multi-reward manager (reference ``reward_manager/multi.py``)."""
+    from verl_omni_b200.workers.reward.reward_manager import (SCORERS, MultiVisualRewardManager,
+                                                              build_model_scorer)
+
+    model_kinds = ("pickscore", "hpsv3", "ocr", "unified_reward", "clap", "imagebind")
+    entries = []
+    for sub in subs:
+        sub = dict(sub)
+        kind = str(sub.get("scorer", sub.get("name")))
+        name = str(sub.get("name", kind))
+        if kind == "default" and default is not None:
+            mgr = default[0]
+        elif kind in model_kinds:
+            mgr = VisualRewardManager(build_model_scorer(kind, device, dtype, **dict(sub.get("sizes", {}) or {})),
+                                      name=name)
+        elif kind in SCORERS:
+            mgr = VisualRewardManager(SCORERS[kind], name=name, **dict(sub.get("kwargs", {}) or {}))
+        else:
+            raise KeyError(f"unknown reward scorer {kind!r}")
+        entries.append((name, mgr, float(sub.get("weight", 1.0)), bool(sub.get("required", True))))
+    return MultiVisualRewardManager(entries)
+
+
 def load_pretrained(module, path) -> int:
     """``actor_rollout_ref.model.path``: ``random-init`` (or empty) keeps the random weights; a diffusers
     pipeline / transformer directory (or a safetensors file) loads through the diffusers name mapping."""
@@ -153,6 +177,9 @@ class PolicyGradientTrainer:
             decoder = vae.decode_video if self.spec.reward == "vit_video" else vae
             scorer = ModelScorer(ViTScorer(image_size=self.spec.image_size).to(self.device, dt), "images", self.device)
         self.reward_fn = VisualRewardManager(scorer, name="score")
+        subs = list(config.get("reward", {}).get("sub_rewards", []) or [])
+        if subs:
+            self.reward_fn = build_multi_reward(subs, self.device, dt, default=(self.reward_fn, "score"))
         self.rollout = DiTRolloutEngine(module, self.adapter, self.rollout_cfg, self.model_cfg, device=self.device,
                                         latent_shape=self.spec.latent_shape, decoder=decoder,
                                         sched_seq_len=self.spec.sched_seq_len)

@@ -100,6 +100,87 @@ def http_scorer(batch: DataProto, url: str = "", timeout: float = 60.0, **_) -> 
     return torch.tensor(pickle.loads(r.content), dtype=torch.float32)
 
 
+# ------------------------------------------------------------------ model-based scorers of the reference family
+class _ModuleScorer:
+    """A frozen scorer module called on the batch's images / audio and prompts (``models/scorers.py``)."""
+
+    def __init__(self, kind: str, module: torch.nn.Module, device, micro_batch: int = 8):
+        self.kind, self.module, self.device, self.mb = kind, module.eval(), device, micro_batch
+        for p in self.module.parameters():
+            p.requires_grad_(False)
+
+    @torch.no_grad()
+    def __call__(self, batch: DataProto, **_) -> torch.Tensor:
+        from verl_omni_b200.models.scorers import _texts
+
+        n = len(batch)
+        texts = _texts(batch, n)
+        truths = list(batch.non_tensor_batch.get("ground_truth", [None] * n))
+        out = []
+        for i in range(0, n, self.mb):
+            sl = slice(i, min(n, i + self.mb))
+            imgs = batch.batch["images"][sl].to(self.device) if "images" in batch.batch else None
+            mels = batch.batch["audio_mels"][sl].to(self.device) if "audio_mels" in batch.batch else None
+            if imgs is not None and imgs.ndim == 5:  # video: score the middle frame
+                imgs = imgs[:, :, imgs.shape[2] // 2]
+            if self.kind in ("pickscore", "hpsv3"):
+                s = self.module.score(imgs, texts[sl])
+            elif self.kind in ("ocr", "unified_reward"):
+                s = self.module.score(imgs, texts[sl], truths[sl])
+            elif self.kind == "clap":
+                s = self.module.score(mels, texts[sl])
+            else:  # imagebind
+                s = self.module.score(texts[sl], images=imgs, mels=mels)
+            out.append(s.float().cpu())
+        return torch.cat(out, 0)
+
+
+def build_model_scorer(kind: str, device, dtype=torch.bfloat16, **sizes) -> _ModuleScorer:
+    """``pickscore`` | ``hpsv3`` | ``ocr`` | ``unified_reward`` | ``clap`` | ``imagebind`` at their reference
+    shapes (or ``sizes`` overrides for small runs), random-init and frozen."""
+    from verl_omni_b200.models import scorers as S
+
+    if kind == "pickscore":
+        m = S.PickScoreScorer(**sizes)
+    elif kind == "hpsv3":
+        m = S.HPSv3Scorer(**sizes)
+    elif kind == "ocr":
+        m = S.VLMJudge("ocr", **sizes)
+    elif kind == "unified_reward":
+        m = S.VLMJudge("unified", **sizes)
+    elif kind == "clap":
+        m = S.CLAPScorer(**sizes)
+    elif kind == "imagebind":
+        m = S.ImageBindScorer(**sizes)
+    else:
+        raise KeyError(f"unknown model scorer {kind!r}")
+    return _ModuleScorer(kind, m.to(device=device, dtype=dtype), device)
+
+
+def _decoded_responses(batch: DataProto) -> list[str]:
+    from verl_omni_b200.models.scorers import byte_text
+
+    if "response_text" in batch.non_tensor_batch:
+        return [str(x) for x in batch.non_tensor_batch["response_text"]]
+    return byte_text(batch.batch["responses"].cpu())
+
+
+@register_scorer("mmk12")
+def mmk12_scorer(batch: DataProto, **_) -> torch.Tensor:
+    from verl_omni_b200.models.scorers import mmk12_reward
+
+    return mmk12_reward(_decoded_responses(batch), list(batch.non_tensor_batch.get("ground_truth",
+                                                                                    [None] * len(batch))))
+
+
+@register_scorer("choice")
+def choice_scorer(batch: DataProto, **_) -> torch.Tensor:
+    from verl_omni_b200.models.scorers import choice_reward
+
+    return choice_reward(_decoded_responses(batch), list(batch.non_tensor_batch.get("ground_truth",
+                                                                                     [None] * len(batch))))
+
+
 @register_reward_manager("visual")
 class VisualRewardManager:
     def __init__(self, scorer: Callable, name: str = "reward", **kwargs):
