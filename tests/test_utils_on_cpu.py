@@ -175,3 +175,20 @@ def test_trainer_reads_parquet_prompts(tmp_path):
     assert len(t.dataset) == 6
     m = t.step()
     assert m["actor/grad_norm"] == m["actor/grad_norm"]
+
+
+def test_media_dump_video_and_wav(tmp_path):
+    """Video frames (mp4 when an ffmpeg writer exists, else an animated gif) and 16-bit WAV audio are written
+    beside the JSONL record."""
+    import wave
+
+    from verl_omni_b200.utils.tracking import dump_media_generations
+
+    vids = torch.rand(2, 3, 4, 16, 16) * 2 - 1
+    aud = [torch.sin(torch.linspace(0, 100, 800)), None]
+    fn = dump_media_generations(str(tmp_path), 3, ["a", "b"], [0.1, 0.2], videos=vids, audios=aud,
+                                sample_rates=[8000, 8000])
+    rows = [json.loads(ln) for ln in open(fn)]
+    assert rows[0]["video"].split(".")[-1] in ("mp4", "gif", "npy") and "audio" not in rows[1]
+    with wave.open(rows[0]["audio"]) as w:
+        assert w.getframerate() == 8000 and w.getnframes() == 800 and w.getsampwidth() == 2
