@@ -201,3 +201,47 @@ def load_peft_adapter(module: nn.Module, path: str, adapter: str = "default") ->
                 m.lora_B[adapter].copy_(sd[kb])
                 n += 1
     return n
+
+
+def export_peft_from_checkpoint(actor_dir: str, out_dir: str, adapter: str = "default", lora_alpha: Optional[float] = None,
+                                base_model: str = "") -> int:
+    """PEFT adapter directory from a sharded engine checkpoint, without building the model (reference
+    ``verl_omni/utils/fsdp_utils.py:218-274``, which gathers the LoRA tensors of FSDP shards).
+
+    ``actor_dir`` holds ``model_world_size_{W}_rank_{r}.pt`` (every parameter's dim-0 shard per rank); the
+    adapter's ``lora_A`` / ``lora_B`` tensors are re-assembled across ranks and written with PEFT keys
+    (``base_model.model.<module>.lora_{A,B}.weight``) plus ``adapter_config.json``.  ``lora_alpha`` defaults
+    to the rank (scaling 1) when the checkpoint does not record it.  Returns the number of adapted modules."""
+    import glob
+    import re
+
+    from safetensors.torch import save_file
+
+    files = glob.glob(os.path.join(actor_dir, "model_world_size_*_rank_*.pt"))
+    if not files:
+        raise FileNotFoundError(f"no model_world_size_*_rank_*.pt under {actor_dir}")
+    W = int(re.search(r"model_world_size_(\d+)_rank_", os.path.basename(files[0])).group(1))
+    parts = [torch.load(os.path.join(actor_dir, f"model_world_size_{W}_rank_{r}.pt"), map_location="cpu")["params"]
+             for r in range(W)]
+    pat = re.compile(rf"^(.*)\.lora_([AB])\.{re.escape(adapter)}$")
+    tensors, mods, rank = {}, set(), None
+    for name in parts[0]:
+        m = pat.match(name)
+        if not m:
+            continue
+        full = torch.cat([p[name] for p in parts], 0) if parts[0][name].ndim else parts[0][name]
+        mod, ab = m.group(1), m.group(2)
+        mods.add(mod)
+        tensors[f"base_model.model.{mod}.lora_{ab}.weight"] = full.float().contiguous()
+        if ab == "A":
+            rank = full.shape[0]
+    if not tensors:
+        raise ValueError(f"checkpoint has no LoRA tensors for adapter {adapter!r}")
+    os.makedirs(out_dir, exist_ok=True)
+    cfg = {"peft_type": "LORA", "r": rank, "lora_alpha": float(lora_alpha if lora_alpha is not None else rank),
+           "target_modules": sorted({m.split(".")[-1] for m in mods}), "lora_dropout": 0.0, "bias": "none",
+           "base_model_name_or_path": base_model, "task_type": None}
+    with open(os.path.join(out_dir, "adapter_config.json"), "w") as f:
+        json.dump(cfg, f, indent=2)
+    save_file(tensors, os.path.join(out_dir, "adapter_model.safetensors"))
+    return len(mods)
