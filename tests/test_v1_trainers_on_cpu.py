@@ -84,3 +84,48 @@ def test_v1_trainer_modes(mode, extra):
         # the replica received the trainer's weights
         for (n1, p1), (n2, p2) in zip(t.core.actor.module.named_parameters(), t.rollout.module.named_parameters()):
             assert torch.equal(p1.detach(), p2.detach()), n1
+
+
+def _standalone(rank, world, outdir):
+    import json
+
+    from verl_omni_b200.trainer.diffusion.v1.trainer import build_v1_trainer
+    from verl_omni_b200.utils.config import load_config
+
+    cfg = load_config("diffusion_trainer", [
+        "trainer.device=cpu", "actor_rollout_ref.model.architecture=tiny_dit", "data.train_batch_size=4",
+        "actor_rollout_ref.rollout.n=2", "actor_rollout_ref.rollout.pipeline.num_inference_steps=2",
+        "actor_rollout_ref.actor.ppo_mini_batch_size=4", "actor_rollout_ref.actor.ppo_micro_batch_size_per_gpu=4",
+        "trainer.resume_mode=disable", "trainer.logger=[]", "trainer.total_training_steps=4", "trainer.use_v1=true",
+        "trainer.v1.trainer_mode=separate_async", "trainer.v1.standalone_rollout_ranks=2",
+        "trainer.v1.parameter_sync_step=1", "actor_rollout_ref.actor.optim.lr=1e-3"])
+    role = build_v1_trainer(cfg)
+    hist = role.fit()
+    from verl_omni_b200.trainer.diffusion.v1.standalone import RolloutRank
+
+    if isinstance(role, RolloutRank):
+        # after the run the rollout's weights are a pushed version: compare with the trainer's final push
+        torch.save(role.channel.buf.clone(), f"{outdir}/rollout_{rank}.pt")
+    else:
+        json.dump([{k: v for k, v in m.items() if isinstance(v, (int, float))} for m in hist],
+                  open(f"{outdir}/trainer_{rank}.json", "w"))
+        if rank == 0:
+            torch.save(role.last_pushed.clone(), f"{outdir}/pushed.pt")
+
+
+def test_standalone_rollout_ranks_gloo(tmp_path):
+    """4 gloo ranks: 2 trainers + 2 standalone rollout ranks.  Batches travel rollout -> trainer, weights
+    trainer 0 -> both rollout ranks after every step (one-step off-policy): each rollout rank ends up holding
+    exactly the last pushed flat buffer, and the trainers see samples one version behind their policy."""
+    import json
+
+    from tests._dist_util import run_ranks
+
+    run_ranks(_standalone, 4, (str(tmp_path),))
+    pushed = torch.load(tmp_path / "pushed.pt")
+    for r in (2, 3):
+        assert torch.equal(torch.load(tmp_path / f"rollout_{r}.pt"), pushed)
+    h0 = json.load(open(tmp_path / "trainer_0.json"))
+    assert [m["training/global_step"] for m in h0] == [1, 2, 3, 4]
+    assert h0[0]["training/staleness/mean"] == 0.0 and h0[2]["training/staleness/mean"] == 1.0
+    assert all(m["actor/grad_norm"] == m["actor/grad_norm"] for m in h0)

@@ -68,12 +68,31 @@ def set_info(i: DistInfo) -> None:
     _INFO = i
 
 
+# group that ``group=None`` resolves to (None: the world).  A process subset that runs a trainer of its own --
+# the trainer ranks of a standalone-rollout topology -- sets its group here so the trainer, its engine and
+# every collective helper operate on that subset without threading the group through each call.
+_DEFAULT_GROUP = None
+
+
+def set_default_group(group) -> None:
+    global _DEFAULT_GROUP
+    _DEFAULT_GROUP = group
+
+
+def default_group():
+    return _DEFAULT_GROUP
+
+
+def _g(group):
+    return group if group is not None else _DEFAULT_GROUP
+
+
 def world_size(group=None) -> int:
-    return dist.get_world_size(group) if dist.is_initialized() else 1
+    return dist.get_world_size(_g(group)) if dist.is_initialized() else 1
 
 
 def rank(group=None) -> int:
-    return dist.get_rank(group) if dist.is_initialized() else 0
+    return dist.get_rank(_g(group)) if dist.is_initialized() else 0
 
 
 _HSDP_CACHE: dict = {}
@@ -85,6 +104,9 @@ def make_hsdp_groups(fsdp_size: int):
     collective contract of ``new_group``); results are cached per size."""
     if fsdp_size in _HSDP_CACHE:
         return _HSDP_CACHE[fsdp_size]
+    if _DEFAULT_GROUP is not None:
+        # new_group is collective over the world: a process subset cannot create sub-groups on its own
+        raise NotImplementedError("HSDP / EP / TP sub-groups inside a trainer that runs on a subset of the ranks")
     ws, r = world_size(), rank()
     if ws % fsdp_size:
         raise ValueError(f"world size {ws} not divisible by fsdp_size {fsdp_size}")
@@ -95,6 +117,7 @@ def make_hsdp_groups(fsdp_size: int):
 
 
 def barrier(group=None) -> None:
+    group = _g(group)
     if dist.is_initialized():
         if dist.get_backend(group) == "nccl":
             dist.barrier(group, device_ids=[torch.cuda.current_device()])
@@ -103,12 +126,14 @@ def barrier(group=None) -> None:
 
 
 def all_reduce(t: torch.Tensor, op=dist.ReduceOp.SUM, group=None) -> torch.Tensor:
+    group = _g(group)
     if dist.is_initialized() and world_size(group) > 1:
         dist.all_reduce(t, op=op, group=group)
     return t
 
 
 def all_reduce_max(x: float, group=None, device=None) -> float:
+    group = _g(group)
     if not dist.is_initialized() or world_size(group) == 1:
         return x
     t = torch.tensor([x], dtype=torch.float64, device=device or "cpu")
@@ -118,6 +143,7 @@ def all_reduce_max(x: float, group=None, device=None) -> float:
 
 def all_gather_into(out: torch.Tensor, shard: torch.Tensor, group=None) -> None:
     """``out`` (flat, world*shard elements) <- concat of every rank's ``shard``."""
+    group = _g(group)
     ws = world_size(group)
     if ws == 1:
         if out.data_ptr() != shard.data_ptr():
@@ -132,6 +158,7 @@ def all_gather_into(out: torch.Tensor, shard: torch.Tensor, group=None) -> None:
 
 def reduce_scatter_into(shard: torch.Tensor, full: torch.Tensor, group=None, op=dist.ReduceOp.SUM) -> None:
     """``shard`` <- this rank's slice of the element-wise reduction of every rank's ``full``."""
+    group = _g(group)
     ws = world_size(group)
     if ws == 1:
         if shard.data_ptr() != full.data_ptr():
@@ -146,6 +173,7 @@ def reduce_scatter_into(shard: torch.Tensor, full: torch.Tensor, group=None, op=
 
 
 def all_gather_object(obj, group=None) -> list:
+    group = _g(group)
     if not dist.is_initialized() or world_size(group) == 1:
         return [obj]
     out = [None] * world_size(group)
@@ -154,6 +182,7 @@ def all_gather_object(obj, group=None) -> list:
 
 
 def broadcast_object(obj, src: int = 0, group=None):
+    group = _g(group)
     if not dist.is_initialized() or world_size(group) == 1:
         return obj
     lst = [obj]

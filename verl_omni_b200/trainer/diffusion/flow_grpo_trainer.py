@@ -82,8 +82,13 @@ def load_pretrained(module, path) -> int:
 
 
 class PolicyGradientTrainer:
-    def __init__(self, config, *, arch: Optional[str] = None, device: Optional[torch.device] = None):
+    def __init__(self, config, *, arch: Optional[str] = None, device: Optional[torch.device] = None,
+                 rollout_only: bool = False, dp_override: Optional[int] = None):
+        """``rollout_only`` (a standalone rollout rank): the policy module, rollout engine, reward and prompt
+        stream without optimizer state or collectives; ``dp_override`` sets the data-parallel size whose
+        prompt shares this rank produces (the trainer ranks' count)."""
         self.config = config
+        self.rollout_only = rollout_only
         di = D.info()
         self.device = device or di.device
         self.rank, self.world = D.rank(), D.world_size()
@@ -101,6 +106,8 @@ class PolicyGradientTrainer:
         if self.world % self.sp:
             raise ValueError(f"world size {self.world} not divisible by ulysses_sequence_parallel_size={self.sp}")
         self.dp, self.dp_rank = self.world // self.sp, self.rank // self.sp
+        if dp_override is not None:
+            self.dp, self.dp_rank = int(dp_override), 0
         self.sp_group = None
         if self.sp > 1:
             from verl_omni_b200.parallel.ulysses import make_sp_groups
@@ -129,7 +136,10 @@ class PolicyGradientTrainer:
                         self.model_cfg.exclude_modules, adapters=tuple(self.model_cfg.policy_state_adapters),
                         init=self.model_cfg.lora_init_weights)
         # with LoRA the reference policy is the base model (adapters disabled): no second copy
-        ref_module = copy.deepcopy(module) if (self.actor_cfg.use_kl_loss and not self.lora) else None
+        ref_module = (copy.deepcopy(module) if (self.actor_cfg.use_kl_loss and not self.lora and not rollout_only)
+                      else None)
+        # the trainer's flat-buffer parameter set (a standalone rollout rank lays its push buffer out the same way)
+        self.trainable_names = [n for n, p in module.named_parameters() if p.requires_grad]
         if self.sp_group is not None:
             module.sp_group = self.sp_group
             if ref_module is not None:
@@ -138,11 +148,12 @@ class PolicyGradientTrainer:
         seq = self.spec.sched_seq_len or int(np.prod(self.spec.latent_shape[-2:])) // 4
         self.scheduler = self.adapter.build_scheduler(T, image_seq_len=seq, device=self.device)
         self.actor = PPODiffusionEngine(module, self.adapter, self.scheduler, self.actor_cfg, self.model_cfg,
-                                        device=self.device, total_steps=self.total_steps)
+                                        device=self.device, total_steps=self.total_steps,
+                                        trainable=not rollout_only)
         # on-policy distillation: a frozen teacher of the same family scores the rollout trajectories
         self.teacher = None
         dist_cfg = config.get("distillation", {}) or {}
-        if bool(dist_cfg.get("enabled", dist_cfg.get("enable", False))):
+        if bool(dist_cfg.get("enabled", dist_cfg.get("enable", False))) and not rollout_only:
             tcfg = (dist_cfg.get("teacher_models", {}) or {}).get("teacher_model", {}) or {}
             torch.manual_seed(int(tcfg.get("seed", 1234)))
             teacher_module = self.spec.build()

@@ -12,10 +12,12 @@ Counterparts of ``verl_omni/trainer/diffusion/v1/trainer_base.py:104-386``,
 * ``sync``: the rollout engine is colocated and shares the trainer's weights; generation for a step
   happens when it is sampled, so every batch is on-policy;
 * ``separate_async``: a standalone rollout replica (its own weight copy) runs on a background thread
-  and CUDA stream, kept ``warmup_batches + 1`` batches ahead; weight pushes every
-  ``parameter_sync_step`` updates (copy in-process; the NCCL checkpoint engine when the replica lives
-  on other ranks); in-flight generations are aborted at a push unless ``partial_rollout`` is set and
-  the whole-sample retry client regenerates them on the new weights; staleness is tracked per group.
+  and CUDA stream of the same rank, kept ``warmup_batches + 1`` batches ahead; weight pushes every
+  ``parameter_sync_step`` updates (an in-process copy); in-flight generations are aborted at a push unless
+  ``partial_rollout`` is set and the whole-sample retry client regenerates them on the new weights;
+  staleness is tracked per group;
+* ``trainer.v1.standalone_rollout_ranks = R > 0``: rollout on the last R ranks of the job instead, weights
+  pushed across GPUs by one peer-store kernel (``trainer/diffusion/v1/standalone.py``).
 """
 
 from __future__ import annotations
@@ -55,6 +57,11 @@ def get_diffusion_trainer_cls(name: str) -> type:
 
 
 def build_v1_trainer(config):
+    if int(config.trainer.v1.get("standalone_rollout_ranks", 0) or 0) > 0:
+        # rollout on dedicated ranks of the job (trainer ranks + rollout ranks, weights pushed across GPUs)
+        from verl_omni_b200.trainer.diffusion.v1.standalone import build_standalone
+
+        return build_standalone(config)
     return get_diffusion_trainer_cls(config.trainer.v1.trainer_mode)(config)
 
 

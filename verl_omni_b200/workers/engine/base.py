@@ -193,7 +193,7 @@ class ShardedEngine:
     def __init__(self, module: nn.Module, actor_cfg, *, device: torch.device, group=None, total_steps: int = 1,
                  trainable: bool = True, expert_group=None):
         self.cfg = actor_cfg
-        self.group = group
+        self.group = group if group is not None else D.default_group()
         # expert-parallel parameters (marked ``_vo_expert``: each rank holds only its experts' slices) live in
         # a second flat set sharded over ``expert_group`` -- the ranks that hold the same experts
         self.expert_group = expert_group
