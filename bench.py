@@ -33,6 +33,23 @@ METRIC = "FlowGRPO step time & samples/sec (rollout+train) at 1/2/4/8 B200, max 
 PROMPTS_PER_GPU = 6
 GROUP = 16
 
+# Workloads of the headline metric (global batch at 8 GPUs / 8 = the per-GPU share under weak scaling; with
+# sequence parallelism a group of `sp` GPUs shares its samples, so prompts are counted per data-parallel group).
+CONFIGS = {
+    "sd35": dict(arch="sd35_medium", prompts_per_dp=6, group=16, sde_steps=10, sp=1, micro=16, max_num_seqs=48,
+                 model="SD3.5-Medium-shaped MMDiT (2.24B params, 24 joint blocks, hidden 1536, 24 heads, patch 2, "
+                       "16-ch latents)", seq_len=1024 + 333,
+                 reward="random-init VAE decoder 512^2 + ViT-B/16 scorer"),
+    "flux_sp2": dict(arch="flux1_dev", prompts_per_dp=6, group=12, sde_steps=16, sp=2, micro=4, max_num_seqs=12,
+                     model="FLUX.1-dev-shaped rectified-flow transformer (~12B, 19 double + 38 single blocks, hidden "
+                           "3072, 24 heads, 2D RoPE), full fine-tune, guidance embedding 3.5", seq_len=4096 + 512,
+                     reward="random-init VAE decoder 1024^2 + ViT-B/16 scorer"),
+    "wan_sp8_async": dict(arch="wan21_14b", prompts_per_dp=8, group=8, sde_steps=20, sp=8, micro=1, max_num_seqs=4,
+                          model="Wan2.1-14B-shaped video DiT (40 blocks, hidden 5120, 40 heads, FFN 13824, 3D RoPE), "
+                                "81 frames 480x832", seq_len=32760 + 512, v1="separate_async",
+                          reward="random-init VAE decoder + 12-layer ViT per frame, mean-pooled"),
+}
+
 
 def _clock_sampler(path: str):
     try:
@@ -106,11 +123,15 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
-    ap.add_argument("--arch", default="sd35_medium")
-    ap.add_argument("--prompts-per-gpu", type=int, default=PROMPTS_PER_GPU)
-    ap.add_argument("--group", type=int, default=GROUP)
-    ap.add_argument("--sde-steps", type=int, default=10)
-    ap.add_argument("--micro", type=int, default=16)
+    ap.add_argument("--config", default="sd35", choices=list(CONFIGS) + ["omni_moe"],
+                    help="sd35 (default): SD3.5-Medium FSDP-style DP; flux_sp2: FLUX-12B full FT with Ulysses SP=2; "
+                         "wan_sp8_async: Wan-14B video with SP=8 and the async trainer; omni_moe: Qwen3-Omni-30B-A3B "
+                         "MoE GRPO with EP and TP=2")
+    ap.add_argument("--arch", default=None)
+    ap.add_argument("--prompts-per-gpu", type=int, default=None, help="prompts per data-parallel group")
+    ap.add_argument("--group", type=int, default=None)
+    ap.add_argument("--sde-steps", type=int, default=None)
+    ap.add_argument("--micro", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile-step", action="store_true",
                     help="after warm-up, run one step under torch.profiler and print the top CUDA kernels (no bench line)")
@@ -118,6 +139,13 @@ def main() -> None:
     if args.impl == "reference":
         reference_arm(args)
         return
+    if args.config == "omni_moe":
+        return bench_omni(args)
+    C = dict(CONFIGS[args.config])
+    for k, a in (("arch", "arch"), ("prompts_per_dp", "prompts_per_gpu"), ("group", "group"),
+                 ("sde_steps", "sde_steps"), ("micro", "micro")):
+        if getattr(args, a) is not None:
+            C[k] = getattr(args, a)
 
     import torch
     import torch.distributed as dist
@@ -130,21 +158,34 @@ def main() -> None:
     info = D.init_distributed(device="cuda", timeout_s=1800)
     N = D.world_size()
     assert N == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={N}"
-    prompts = args.prompts_per_gpu * N
+    sp = min(int(C["sp"]), N)
+    dp = N // sp
+    prompts = int(C["prompts_per_dp"]) * dp
     ov = [
-        "trainer.device=cuda", f"actor_rollout_ref.model.architecture={args.arch}",
-        f"data.train_batch_size={prompts}", f"actor_rollout_ref.rollout.n={args.group}",
-        f"actor_rollout_ref.rollout.pipeline.num_inference_steps={args.sde_steps}",
+        "trainer.device=cuda", f"actor_rollout_ref.model.architecture={C['arch']}",
+        f"data.train_batch_size={prompts}", f"actor_rollout_ref.rollout.n={C['group']}",
+        f"actor_rollout_ref.rollout.pipeline.num_inference_steps={C['sde_steps']}",
         "actor_rollout_ref.rollout.algo.noise_level=0.7", "actor_rollout_ref.rollout.algo.sde_type=sde",
-        "actor_rollout_ref.rollout.max_num_seqs=48",
+        f"actor_rollout_ref.rollout.max_num_seqs={C['max_num_seqs']}",
+        f"actor_rollout_ref.actor.fsdp_config.ulysses_sequence_parallel_size={sp}",
         f"actor_rollout_ref.actor.ppo_mini_batch_size={prompts}",
-        f"actor_rollout_ref.actor.ppo_micro_batch_size_per_gpu={args.micro}",
+        f"actor_rollout_ref.actor.ppo_micro_batch_size_per_gpu={C['micro']}",
         "actor_rollout_ref.actor.optim.lr=1e-5", "actor_rollout_ref.actor.optim.weight_decay=0.0",
         "trainer.total_training_steps=1000", "trainer.resume_mode=disable", "trainer.logger=[]",
         "trainer.save_freq=-1",
     ]
+    if C.get("v1"):
+        ov += ["trainer.use_v1=true", f"trainer.v1.trainer_mode={C['v1']}"]
     cfg = load_config("diffusion_trainer", ov)
-    trainer = PolicyGradientTrainer(cfg)
+    if C.get("v1"):
+        from verl_omni_b200.trainer.diffusion.v1.trainer import build_v1_trainer
+
+        v1 = build_v1_trainer(cfg)
+        trainer = v1.core
+        v1.on_train_begin()
+        trainer.step = lambda ids=None: v1.step()  # the async trainer's step through the same driver loop
+    else:
+        trainer = PolicyGradientTrainer(cfg)
     dev = info.device
     n_params = sum(p.numel() for p in trainer.actor.module.parameters())
 
@@ -197,7 +238,7 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     dev_ms = float(t.item())
     ms_per_step = dev_ms / args.steps
-    samples_per_step = prompts * args.group
+    samples_per_step = prompts * int(C["group"])
     value = samples_per_step / (ms_per_step / 1000.0)
     timing = {k: round(v, 3) for k, v in m.items() if k.startswith("timing_s/")}
     mfu = {k.split("perf/mfu/")[1]: round(v, 4) for k, v in m.items() if k.startswith("perf/mfu/")}
@@ -235,15 +276,77 @@ def main() -> None:
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 2), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random prompt embeddings / latents, random-init weights)",
-            "config": {"model": f"SD3.5-Medium-shaped MMDiT ({n_params / 1e9:.2f}B params, 24 joint blocks, "
-                                "hidden 1536, 24 heads, patch 2, 16-ch latents)",
-                       "global_batch": samples_per_step, "prompts": prompts, "group": args.group,
-                       "seq_len": 1024 + 333, "sde_steps": args.sde_steps, "parallelism": f"dp{N}",
-                       "reward": "random-init VAE decoder 512^2 + ViT-B/16 scorer",
-                       "l2": "inputs larger than L2 (no flush)"},
+            "config": {"model": C["model"] + f" [{n_params / 1e9:.2f}B params]", "name": args.config,
+                       "global_batch": samples_per_step, "prompts": prompts, "group": int(C["group"]),
+                       "seq_len": C["seq_len"], "sde_steps": int(C["sde_steps"]),
+                       "parallelism": f"dp{dp}" + (f"_sp{sp}" if sp > 1 else ""), "reward": C["reward"],
+                       "trainer": C.get("v1", "sync"), "l2": "inputs larger than L2 (no flush)"},
             "impl": "native", "gpu_launches": launches, "clocks": clocks, "e2e": e2e, "phase_s": timing, "mfu": mfu,
         }
         print(json.dumps(out), flush=True)
+    D.destroy()
+
+
+def bench_omni(args) -> None:
+    """Qwen3-Omni-30B-A3B-shaped MoE thinker GRPO (48 layers, hidden 2048, 128 experts top-8, vocab 151936):
+    512-token multimodal prompts (256 audio frames through the audio tower + 256 image patches through the
+    vision tower), 1024-token responses, group 8; EP over all GPUs (experts sharded), TP=2 attention when
+    N >= 2; per-GPU share of 64 prompts at 8 GPUs.  Same timing rules and JSON line as the diffusion configs."""
+    import torch
+    import torch.distributed as dist
+
+    from verl_omni_b200.ops._ext import ext
+    from verl_omni_b200.parallel import dist as D
+    from verl_omni_b200.trainer.main_omni import build_omni_trainer
+    from verl_omni_b200.utils.config import load_config
+
+    info = D.init_distributed(device="cuda", timeout_s=1800)
+    N = D.world_size()
+    assert N == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={N}"
+    tp = 2 if N >= 2 else 1
+    dp = N // tp
+    per_dp = args.prompts_per_gpu or 16
+    group = args.group or 8
+    cfg = load_config("omni_trainer", [
+        "trainer.device=cuda", f"data.train_batch_size={per_dp * dp}", f"actor_rollout_ref.rollout.n={group}",
+        "actor_rollout_ref.rollout.response_length=1024", f"actor_rollout_ref.actor.megatron.expert_model_parallel_size={N}",
+        f"actor_rollout_ref.actor.megatron.tensor_model_parallel_size={tp}",
+        f"actor_rollout_ref.actor.ppo_micro_batch_size_per_gpu={args.micro or 8}", "trainer.logger=[]",
+        "trainer.total_training_steps=1000", "trainer.resume_mode=disable"])
+    tr = build_omni_trainer(cfg)
+
+    def sync():
+        D.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        m = tr.step(tr.prompts_per_rank)
+    sync()
+    launches0 = ext().launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        m = tr.step(tr.prompts_per_rank)
+    e1.record()
+    sync()
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=info.device)
+    if N > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item()) / args.steps
+    samples = per_dp * dp * group
+    if info.rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": round(samples / (ms / 1000.0), 4), "unit": "samples/s", "n_gpus": N,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random text ids, log-mel frames, image patches; random-init weights)",
+            "config": {"model": "Qwen3-Omni-30B-A3B-shaped MoE thinker (48 layers, hidden 2048, 32 q / 4 kv heads, "
+                                "128 experts top-8, expert FFN 768, vocab 151936) + 32-layer audio / 27-layer vision towers",
+                       "name": "omni_moe", "global_batch": samples, "prompts": per_dp * dp, "group": group,
+                       "seq_len": 512 + 1024, "parallelism": f"ep{N}_tp{tp}_dp{dp}", "reward": "seeded hash of the "
+                       "response tokens", "l2": "inputs larger than L2 (no flush)"},
+            "impl": "native", "gpu_launches": ext().launch_count() - launches0,
+            "phase_s": {k: round(v, 3) for k, v in m.items() if k.startswith("timing_s/")}}), flush=True)
     D.destroy()
 
 
