@@ -223,3 +223,100 @@ class DiTRolloutEngine:
         g = torch.Generator(device="cpu")
         g.manual_seed(int(seed) & 0x7FFFFFFFFFFFFFFF)
         return torch.randn((b,) + self.latent_shape, generator=g).to(self.device)
+
+
+class StepwiseBatcher:
+    """Step-level continuous batching over a :class:`DiTRolloutEngine` (the step-exec interface of the
+    reference's vLLM-Omni adapters, ``pipelines/qwen_image_flow_grpo/vllm_omni_rollout_adapter.py:199-594``:
+    ``prepare_encode`` / ``step_scheduler`` / ``denoise_step`` / ``post_decode``).
+
+    Requests join a pool as they are submitted and each carries its own step counter; every iteration runs
+    ONE denoising step for up to ``max_num_seqs`` pooled requests in a single forward (rows at different
+    timesteps: the models take per-row timesteps), then the SDE update per distinct step (each row's noise
+    is keyed by its own seed and its step, so a request's trajectory does not depend on who shared its
+    batches).  A request that finishes its ``T`` steps leaves at once and a waiting one takes its slot, so
+    the device batch stays full while requests arrive and finish at different times.
+    """
+
+    def __init__(self, engine: "DiTRolloutEngine", max_num_seqs: Optional[int] = None, noise_level: Optional[float] = None,
+                 sde_type: Optional[str] = None, guidance_scale: Optional[float] = None):
+        self.e = engine
+        self.max = int(max_num_seqs or engine.cfg.max_num_seqs)
+        algo = engine.cfg.algo
+        self.nl = algo.noise_level if noise_level is None else float(noise_level)
+        self.st = algo.sde_type if sde_type is None else sde_type
+        self.guidance = engine.cfg.pipeline.guidance_scale if guidance_scale is None else guidance_scale
+        self.T = int(engine.cfg.pipeline.num_inference_steps)
+        self.waiting: list = []
+        self.active: list = []
+        self.finished: dict = {}
+        self.iterations = 0
+        self.rows_per_iteration: list = []
+
+    def submit(self, request_id, cond: dict, seed: int) -> None:
+        """``cond``: one request's conditioning tensors (leading dim 1)."""
+        self.waiting.append({"id": request_id, "cond": cond, "seed": int(seed)})
+
+    def _admit(self) -> None:
+        e = self.e
+        while self.waiting and len(self.active) < self.max:
+            r = self.waiting.pop(0)
+            rs = torch.tensor([r["seed"]], dtype=torch.int64, device=e.device)
+            r["row_seed"] = rs
+            r["x"] = normal_rows(rs, e.latent_shape, _INIT_NOISE_OFFSET, e.device)
+            r["t"] = 0
+            r["traj"], r["logps"] = [r["x"]], []
+            self.active.append(r)
+
+    @torch.no_grad()
+    def step(self) -> int:
+        """One iteration; returns the number of requests that finished in it."""
+        self._admit()
+        if not self.active:
+            return 0
+        e, sched = self.e, self.e.scheduler
+        rows = self.active[:self.max]
+        keys = e.adapter.cond_keys()
+        x = torch.cat([r["x"] for r in rows], 0)
+        cond = {k: torch.cat([r["cond"][k].to(e.device) for r in rows], 0) for k in keys}
+        tvec = torch.tensor([r["t"] for r in rows], device=e.device)
+        tt = sched.timesteps.to(e.device)[tvec]
+        v = e.adapter.predict(e.module, x, tt, cond, None, self.guidance)
+        self.iterations += 1
+        self.rows_per_iteration.append(len(rows))
+        done = 0
+        steps_now = [r["t"] for r in rows]  # grouped before any row advances
+        for t in sorted(set(steps_now)):
+            idx = [i for i, ti in enumerate(steps_now) if ti == t]
+            sel = torch.tensor(idx, device=e.device)
+            rs = torch.cat([rows[i]["row_seed"] for i in idx], 0)
+            out = sched.sample_previous_step(x[sel].float(), v[sel].float(), step_index=t, noise_level=self.nl,
+                                             sde_type=self.st, noise_offset=t, return_logprobs=True, row_seeds=rs)
+            for j, i in enumerate(idx):
+                r = rows[i]
+                r["x"] = out.prev_sample[j:j + 1]
+                r["traj"].append(r["x"])
+                r["logps"].append(out.log_prob[j:j + 1])
+                r["t"] += 1
+        for r in list(rows):
+            if r["t"] >= self.T:
+                self.active.remove(r)
+                self.finished[r["id"]] = self._result(r)
+                done += 1
+        return done
+
+    def _result(self, r) -> DataProto:
+        e = self.e
+        T = self.T
+        res = {"latents": torch.stack(r["traj"], 1)[0:1].reshape((1, T + 1) + tuple(e.latent_shape)),
+               "step_index": torch.arange(T, device=e.device)[None],
+               "timesteps": e.scheduler.timesteps.to(e.device)[:T][None],
+               "final_latents": r["x"], "rollout_log_probs": torch.cat(r["logps"], 0).reshape(1, T)}
+        res.update({k: v.to(e.device) for k, v in r["cond"].items()})
+        return DataProto(res)
+
+    def run(self) -> dict:
+        """Steps until every submitted request has finished; returns ``{request_id: DataProto row}``."""
+        while self.waiting or self.active:
+            self.step()
+        return self.finished
