@@ -160,14 +160,14 @@ class PushChannel:
         t0 = time.perf_counter()
         if self.symm is not None:
             from verl_omni_b200.parallel import weight_sync
+            from verl_omni_b200.parallel.symm_mem import stream_barrier
 
+            # every rollout rank has finished the work that reads its weights before the peer stores land
+            stream_barrier(self.topo.push_group, self.device)
             if self.topo.rank == 0:
-                weight_sync.push(src[:self.numel].contiguous(), self.symm.peer_ptrs, self.plan.to(self.device),
-                                 self.topo.push_group)
+                weight_sync.push(src[:self.numel].contiguous(), self.symm.peer_ptrs, self.plan, self.topo.push_group)
             else:
-                from verl_omni_b200.parallel.symm_mem import stream_barrier
-
-                stream_barrier(self.topo.push_group, self.device)
+                stream_barrier(self.topo.push_group, self.device)  # ... and they start after the stores
         else:
             t = src[:self.numel] if self.topo.rank == 0 else self.buf
             if self.device.type == "cuda" or dist.get_backend() == "gloo":
