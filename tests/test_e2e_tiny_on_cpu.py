@@ -56,6 +56,20 @@ def test_tiny_flowgrpo_gloo_world2(tmp_path):
     assert os.path.exists(tmp_path / "global_step_2" / "actor" / "model_world_size_2_rank_1.pt")
     assert os.path.exists(tmp_path / "global_step_2" / "actor" / "fsdp_config.json")
     assert (tmp_path / "latest_checkpointed_iteration.txt").read_text() == "2"
+    # the world-2 checkpoint (flat master slices, no gather at save) re-shards into a world-1 engine
+    from verl_omni_b200.trainer.diffusion.flow_grpo_trainer import PolicyGradientTrainer
+    from verl_omni_b200.utils.config import load_config
+    from verl_omni_b200.workers.engine.base import read_full_state
+
+    state = read_full_state(str(tmp_path / "global_step_2" / "actor"))
+    cfg = load_config("diffusion_trainer", OVR + [f"trainer.default_local_dir={tmp_path}", "trainer.resume_mode=auto",
+                                                  "trainer.total_training_steps=3"])
+    t = PolicyGradientTrainer(cfg)
+    assert t.maybe_resume() and t.global_step == 2
+    fp = t.actor.engine.flat
+    for n, view in fp.param_views(fp.master):
+        torch.testing.assert_close(view, state[n].float(), rtol=0, atol=0)
+    assert abs(float(fp.flat.double().sum()) - d["sum"]) < 1e-3 * max(1.0, abs(d["sum"]))
 
 
 def _hsdp(rank, world, outdir):

@@ -88,6 +88,45 @@ def test_ppo_clip_fwd_bwd():
     torch.testing.assert_close(lp.grad, lp2.grad, rtol=1e-5, atol=1e-7)
 
 
+@pytest.mark.parametrize("shape", [(3, 16, 128, 128), (7, 4), (2, 1 << 20)])
+def test_sq_dist_fwd_bwd(shape):
+    from verl_omni_b200.ops.losses import _SqDist
+
+    torch.manual_seed(0)
+    a = torch.randn(*shape, device="cuda").requires_grad_(True)
+    b = torch.randn(*shape, device="cuda").requires_grad_(True)
+    d = _SqDist.apply(a, b)
+    g = torch.randn_like(d)
+    (d * g).sum().backward()
+    a2 = a.detach().double().requires_grad_(True)
+    b2 = b.detach().double().requires_grad_(True)
+    rd = ((a2 - b2) ** 2).flatten(1).mean(1)
+    (rd * g.double()).sum().backward()
+    torch.testing.assert_close(d.double(), rd, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(a.grad.double(), a2.grad, rtol=1e-5, atol=1e-7)
+    torch.testing.assert_close(b.grad.double(), b2.grad, rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("D", [128, 1536])
+def test_affine_layernorm_fwd_bwd(D):
+    from verl_omni_b200.ops.norm import layer_norm
+
+    torch.manual_seed(0)
+    x = torch.randn(2, 333, D, device="cuda").bfloat16().requires_grad_(True)
+    w = (1 + 0.1 * torch.randn(D, device="cuda")).bfloat16().requires_grad_(True)
+    b = (0.1 * torch.randn(D, device="cuda")).bfloat16().requires_grad_(True)
+    y = layer_norm(x, w, b, 1e-6)
+    gy = torch.randn_like(y)
+    (y.float() * gy.float()).sum().backward()
+    x2, w2, b2 = (t.detach().float().requires_grad_(True) for t in (x, w, b))
+    y2 = torch.nn.functional.layer_norm(x2, (D,), w2, b2, 1e-6)
+    (y2 * gy.float()).sum().backward()
+    torch.testing.assert_close(y.float(), y2, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(x.grad.float(), x2.grad, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(w.grad.float(), w2.grad, rtol=2e-2, atol=0.5)
+    torch.testing.assert_close(b.grad.float(), b2.grad, rtol=2e-2, atol=0.5)
+
+
 @pytest.mark.parametrize("D", [256, 1536])
 def test_adaln_layernorm_fwd_bwd(D):
     from verl_omni_b200.ops.norm import adaln_layernorm

@@ -88,6 +88,8 @@ torch::Tensor head_rmsnorm_rope(torch::Tensor x, int64_t col0, int64_t H, torch:
                                 torch::Tensor sin_t, double eps);
 torch::Tensor head_rmsnorm_rope_bwd(torch::Tensor dy, torch::Tensor x, int64_t col0, int64_t H, torch::Tensor w,
                                     torch::Tensor cos_t, torch::Tensor sin_t, double eps, torch::Tensor dw);
+torch::Tensor sq_dist_fwd(torch::Tensor a, torch::Tensor b);
+std::vector<torch::Tensor> sq_dist_bwd(torch::Tensor a, torch::Tensor b, torch::Tensor g, bool want_gb);
 torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor lens,
                                double scale, int64_t splits, c10::optional<torch::Tensor> block_table);
 void fmha_fwd_peer(torch::Tensor q, torch::Tensor k, torch::Tensor v, std::vector<int64_t> peer_o,
@@ -126,6 +128,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sde_step_bwd", &vo::sde_step_bwd);
   m.def("ppo_clip_fwd", &vo::ppo_clip_fwd);
   m.def("ppo_clip_bwd", &vo::ppo_clip_bwd);
+  m.def("sq_dist_fwd", &vo::sq_dist_fwd, "per-sample mean squared distance of two fp32 [B, ...] tensors");
+  m.def("sq_dist_bwd", &vo::sq_dist_bwd, "backward of sq_dist_fwd");
   m.def("adaln_ln_fwd", &vo::adaln_ln_fwd);
   m.def("adaln_ln_bwd", &vo::adaln_ln_bwd);
   m.def("qk_rmsnorm_fwd", &vo::qk_rmsnorm_fwd);

@@ -20,10 +20,10 @@ from dataclasses import dataclass
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 
 from verl_omni_b200.models.layers import (Linear, TimestepMLP, linear_pair, patchify, rope_nd, timestep_embedding,
                                          unpatchify)
+from verl_omni_b200.ops import llm as LO
 from verl_omni_b200.ops.attention import attention
 
 
@@ -52,13 +52,7 @@ class BagelConfig:
 
 
 def _rms(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    xf = x.float()
-    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype)
-
-
-def _rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    x1, x2 = x.float().chunk(2, -1)
-    return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], -1).to(x.dtype)
+    return LO.rms_norm(x.contiguous(), w, eps)  # one fused kernel per row on CUDA
 
 
 class _Expert(nn.Module):
@@ -84,9 +78,12 @@ class MoTLayer(nn.Module):
     def _heads(self, qkv, e: _Expert, B, S, cos, sin):
         cfg = self.cfg
         hd, Hq, Hk = cfg.head_dim, cfg.q_heads, cfg.kv_heads
-        q, k, v = qkv.view(B, S, Hq + 2 * Hk, hd).split([Hq, Hk, Hk], 2)
-        q = _rope(_rms(q, e.q_norm, cfg.eps), cos, sin).transpose(1, 2)
-        k = _rope(_rms(k, e.k_norm, cfg.eps), cos, sin).transpose(1, 2)
+        # per-head RMSNorm + rotate-half RoPE read straight out of the QKV projection (one kernel each)
+        x3 = qkv.view(B, S, (Hq + 2 * Hk) * hd)
+        c2, s2 = cos.reshape(S, hd // 2), sin.reshape(S, hd // 2)
+        q = LO.head_norm_rope(x3, 0, Hq, e.q_norm, c2, s2, cfg.eps)
+        k = LO.head_norm_rope(x3, Hq * hd, Hk, e.k_norm, c2, s2, cfg.eps)
+        v = qkv.view(B, S, Hq + 2 * Hk, hd)[:, :, Hq + Hk:]
         return q, k, v.transpose(1, 2)
 
     def forward(self, xt, xl, rope_t, rope_l):
@@ -106,8 +103,7 @@ class MoTLayer(nn.Module):
         xt, xl = self._out(ot, ol, xt, xl)
         gu_t, gu_l = linear_pair(self.und.gate_up, _rms(xt, self.und.ln2, cfg.eps), self.gen.gate_up,
                                  _rms(xl, self.gen.ln2, cfg.eps))
-        at = F.silu(gu_t[..., :cfg.ffn]) * gu_t[..., cfg.ffn:]
-        al = F.silu(gu_l[..., :cfg.ffn]) * gu_l[..., cfg.ffn:]
+        at, al = LO.swiglu(gu_t.contiguous()), LO.swiglu(gu_l.contiguous())
         dt_, dl_ = linear_pair(self.und.down, at, self.gen.down, al)
         return xt + dt_, xl + dl_
 

@@ -88,7 +88,7 @@ class DiTBlock(nn.Module):
             o = ulysses_attention(q, k, v, sp_group)  # local queries; keys over the whole sequence
         x = self.o(o, epilogue="gate_res", gate=mod.view(B, 6, D)[:, 2], res=x, S=S)
         # cross attention (no gate)
-        hn = F.layer_norm(x, (D,), self.norm3_w.to(x.dtype), self.norm3_b.to(x.dtype), self.eps)
+        hn = layer_norm(x, self.norm3_w.to(x.dtype), self.norm3_b.to(x.dtype), self.eps)
         qc = self.cross_q(hn).reshape(B * S, D)
         kv = self.cross_kv(ctx).reshape(B * St, 2 * D)
         qc, _, _ = qk_norm_split_into(mk(S), None, None, qc, self.cross_norm_q.weight, self.cross_norm_k.weight, S, 0,

@@ -208,28 +208,23 @@ def export_peft_from_checkpoint(actor_dir: str, out_dir: str, adapter: str = "de
     """PEFT adapter directory from a sharded engine checkpoint, without building the model (reference
     ``verl_omni/utils/fsdp_utils.py:218-274``, which gathers the LoRA tensors of FSDP shards).
 
-    ``actor_dir`` holds ``model_world_size_{W}_rank_{r}.pt`` (every parameter's dim-0 shard per rank); the
+    ``actor_dir`` holds ``model_world_size_{W}_rank_{r}.pt`` (each rank's slice of the flat master); the
     adapter's ``lora_A`` / ``lora_B`` tensors are re-assembled across ranks and written with PEFT keys
     (``base_model.model.<module>.lora_{A,B}.weight``) plus ``adapter_config.json``.  ``lora_alpha`` defaults
     to the rank (scaling 1) when the checkpoint does not record it.  Returns the number of adapted modules."""
-    import glob
     import re
 
     from safetensors.torch import save_file
 
-    files = glob.glob(os.path.join(actor_dir, "model_world_size_*_rank_*.pt"))
-    if not files:
-        raise FileNotFoundError(f"no model_world_size_*_rank_*.pt under {actor_dir}")
-    W = int(re.search(r"model_world_size_(\d+)_rank_", os.path.basename(files[0])).group(1))
-    parts = [torch.load(os.path.join(actor_dir, f"model_world_size_{W}_rank_{r}.pt"), map_location="cpu")["params"]
-             for r in range(W)]
+    from verl_omni_b200.workers.engine.base import read_full_state
+
+    state = read_full_state(actor_dir)
     pat = re.compile(rf"^(.*)\.lora_([AB])\.{re.escape(adapter)}$")
     tensors, mods, rank = {}, set(), None
-    for name in parts[0]:
+    for name, full in state.items():
         m = pat.match(name)
         if not m:
             continue
-        full = torch.cat([p[name] for p in parts], 0) if parts[0][name].ndim else parts[0][name]
         mod, ab = m.group(1), m.group(2)
         mods.add(mod)
         tensors[f"base_model.model.{mod}.lora_{ab}.weight"] = full.float().contiguous()

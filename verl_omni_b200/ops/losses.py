@@ -67,3 +67,38 @@ def ppo_clip_loss(logp: torch.Tensor, old: torch.Tensor, adv: torch.Tensor, clip
     else:
         loss, stats = ppo_clip_reference(logp, old, adv, clip, weights)
     return loss, {k: stats[i] for i, k in enumerate(STAT_NAMES)}
+
+
+def sq_dist_reference(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    d = (a.float() - b.float()).pow(2)
+    return d.flatten(1).mean(1) if d.ndim > 1 else d
+
+
+class _SqDist(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a, b):
+        ctx.save_for_backward(a, b)
+        return ext().sq_dist_fwd(a, b)
+
+    @staticmethod
+    def backward(ctx, g):
+        a, b = ctx.saved_tensors
+        need_b = ctx.needs_input_grad[1]
+        grads = ext().sq_dist_bwd(a, b, g.float().contiguous(), need_b)
+        return grads[0], (grads[1] if need_b else None)
+
+
+def sq_dist(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """Per-sample ``mean((a - b)^2)`` over every non-batch dim -> ``[B]`` fp32.
+
+    The squared distance between two reverse-SDE means behind the Flow-DPPO KL mask
+    (``verl_omni/trainer/diffusion/diffusion_algos.py:361-463``), the GRPO-Guard bias term (``:466-587``)
+    and the reference / distillation KLs (``:1013-1094``).  On CUDA (fp32, contiguous, per-sample size a
+    multiple of 4) one read of both operands in a chunked block reduction replaces the
+    sub / pow / mean chain and its two full-size temporaries; backward writes ``2 (a - b) g / n`` once.
+    """
+    if (a.is_cuda and a.dtype == torch.float32 and b.dtype == torch.float32 and a.shape == b.shape
+            and a.ndim > 1 and a.is_contiguous() and b.is_contiguous() and (a.numel() // a.shape[0]) % 4 == 0
+            and a.shape[0] <= 65535):
+        return _SqDist.apply(a, b)
+    return sq_dist_reference(a, b)

@@ -52,16 +52,25 @@ class _AffineLN(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, b, eps):
         D = x.shape[-1]
-        y, _, _ = ext().adaln_ln_fwd(x.reshape(-1, D), None, 0, 0, w, b, 1, eps)
+        y, mean, rstd = ext().adaln_ln_fwd(x.reshape(-1, D), None, 0, 0, w, b, 1, eps)
+        ctx.save_for_backward(x, w, b, mean, rstd)
         return y.view_as(x)
 
     @staticmethod
-    def backward(ctx, dy):  # frozen encoders only (reward / text encoders run without grad)
-        raise RuntimeError("affine LayerNorm kernel is forward-only (frozen encoders)")
+    def backward(ctx, dy):
+        # y = xhat * w + b is the modulated form xhat * (1 + scale) + shift of one sample whose sequence is
+        # every row: the AdaLN backward kernel gives dx and the column sums db = sum dy, dw = sum dy * xhat
+        x, w, b, mean, rstd = ctx.saved_tensors
+        D = x.shape[-1]
+        N = x.numel() // D
+        mod = torch.cat([b.float(), w.float() - 1.0]).to(torch.bfloat16).reshape(1, 2 * D)
+        dx, db, dw = ext().adaln_ln_bwd(dy.contiguous().reshape(1, N, D), x.reshape(1, N, D), mean, rstd, mod, 0, D, N)
+        return dx.view_as(x), dw.reshape(D).to(w.dtype), db.reshape(D).to(b.dtype), None
 
 
 def layer_norm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
-    if x.is_cuda and not torch.is_grad_enabled() and x.dtype == torch.bfloat16:
+    if (x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and b.dtype == torch.bfloat16
+            and x.shape[-1] % 8 == 0):
         return _AffineLN.apply(x.contiguous(), w.contiguous(), b.contiguous(), eps)
     return F.layer_norm(x, (x.shape[-1],), w, b, eps)
 

@@ -235,6 +235,15 @@ def _bcast_like(v: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
     return v.reshape(v.shape[0], *([1] * (target.ndim - 1)))
 
 
+def _per_sample(v: torch.Tensor, batch: int):
+    """``v`` as a ``[B]`` (or 0-d) tensor when it is constant over every non-batch dim, else None."""
+    if v.numel() == 1:
+        return v.reshape(())
+    if v.numel() == batch and v.shape[0] == batch:
+        return v.reshape(batch)
+    return None
+
+
 def _mean_nonbatch(x: torch.Tensor) -> torch.Tensor:
     return x.mean(dim=tuple(range(1, x.ndim))) if x.ndim > 1 else x
 
@@ -252,13 +261,15 @@ class FlowDPPOLoss(DiffusionLossFn):
         log_ratio = log_prob - old_log_prob
         ratio = torch.exp(log_ratio)
         unclipped = -adv * ratio
-        d2 = (prev_sample_mean - old_prev_sample_mean).pow(2)
         if getattr(lc, "add_kl_coefficient", True):
             sig = std_dev_t * _bcast_like(sqrt_dt, std_dev_t)
-            kl_elem = d2 / (2 * sig.pow(2))
         else:
-            kl_elem = d2 / 2
-        kl = _mean_nonbatch(kl_elem)
+            sig = torch.ones((), device=prev_sample_mean.device)
+        sig_b = _per_sample(sig, prev_sample_mean.shape[0])
+        if sig_b is not None:
+            kl = loss_ops.sq_dist(prev_sample_mean, old_prev_sample_mean) / (2 * sig_b.pow(2))
+        else:
+            kl = _mean_nonbatch((prev_sample_mean - old_prev_sample_mean).pow(2) / (2 * sig.pow(2)))
         high = kl >= lc.kl_mask_threshold
         pos = high & (ratio > 1.0) & (adv > 0)
         neg = high & (ratio < 1.0) & (adv < 0)
@@ -308,7 +319,7 @@ class GRPOGuardLoss(DiffusionLossFn):
         sigma_t = std_dev_t.mean()
         sqrt_dt_mean = sqrt_dt.mean()
         scale = sqrt_dt_mean * sigma_t
-        bias = _mean_nonbatch((prev_sample_mean - old_prev_sample_mean).pow(2)) / (2 * scale ** 2)
+        bias = loss_ops.sq_dist(prev_sample_mean, old_prev_sample_mean) / (2 * scale ** 2)
         log_ratio = log_prob - old_log_prob
         ratio = torch.exp((log_ratio + bias) * scale)
         unc = -adv * ratio
@@ -530,6 +541,11 @@ class _MeanKL(DiffusionLossFn):
 
     @classmethod
     def _kl(cls, prev_sample_mean, other, std_dev_t):
+        if prev_sample_mean.ndim > 1:
+            std_b = _per_sample(std_dev_t, prev_sample_mean.shape[0])
+            if std_b is not None:
+                d2 = loss_ops.sq_dist(prev_sample_mean, other)
+                return (d2 / (2 * std_b ** 2)).reshape(-1, *([1] * (prev_sample_mean.ndim - 1)))
         d2 = ((prev_sample_mean - other) ** 2)
         d2 = d2.mean(dim=tuple(range(1, d2.ndim)), keepdim=True)
         std = std_dev_t.reshape(std_dev_t.shape[0], *([1] * (d2.ndim - 1))) if std_dev_t.ndim else std_dev_t

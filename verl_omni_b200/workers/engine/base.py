@@ -357,29 +357,30 @@ class ShardedEngine:
         # HSDP: every replica holds the same shards; replica 0 writes them
         writer = self.replica_group is None or D.rank() // self.world == 0
         if "model" in save_contents:
-            full = fp.full_master()
-            shards = {}
-            for n, view in fp.param_views(full):
-                rows = view.shape[0] if view.ndim else 1
-                per = (rows + W - 1) // W
-                shards[n] = view[r * per:(r + 1) * per].detach().cpu().clone() if view.ndim else view.detach().cpu()
+            # each rank writes its own slice of the flat fp32 master as it lies in memory (no gather); the
+            # per-parameter layout travels with it so any world size can re-shard on load
             if writer:
-                torch.save({"params": shards, "placements": {"type": "Shard", "dim": 0}, "world_size": W},
+                torch.save({"layout": "flat", "master": fp.master.detach().cpu(), "shard_lo": fp.shard_lo,
+                            "numel": fp.numel, "padded": fp.padded, "names": list(fp.names),
+                            "offsets": list(fp.offsets), "numels": list(fp.numels),
+                            "shapes": [tuple(sh) for sh in fp.shapes], "world_size": W},
                            os.path.join(local_path, f"model_world_size_{W}_rank_{r}.pt"))
-            if hf_export and r == 0 and writer:
-                from safetensors.torch import save_file
+            if hf_export:
+                full = fp.full_master()  # the only gather: the exported file holds every parameter
+                if r == 0 and writer:
+                    from safetensors.torch import save_file
 
-                from verl_omni_b200.models import hf_io
+                    from verl_omni_b200.models import hf_io
 
-                hf_dir = os.path.join(local_path, "huggingface")
-                named = dict(fp.param_views(full))
-                if hf_io.supported(self.module):  # diffusers parameter names and layouts
-                    hf_io.save_diffusers(named, self.module, hf_dir)
-                else:
-                    os.makedirs(hf_dir, exist_ok=True)
-                    save_file({n: v.to(torch.bfloat16).contiguous().cpu() for n, v in named.items()},
-                              os.path.join(hf_dir, "diffusion_pytorch_model.safetensors"))
-            del full
+                    hf_dir = os.path.join(local_path, "huggingface")
+                    named = dict(fp.param_views(full))
+                    if hf_io.supported(self.module):  # diffusers parameter names and layouts
+                        hf_io.save_diffusers(named, self.module, hf_dir)
+                    else:
+                        os.makedirs(hf_dir, exist_ok=True)
+                        save_file({n: v.to(torch.bfloat16).contiguous().cpu() for n, v in named.items()},
+                                  os.path.join(hf_dir, "diffusion_pytorch_model.safetensors"))
+                del full
         if "optimizer" in save_contents and writer:
             torch.save({"exp_avg": fp.exp_avg.cpu(), "exp_avg_sq": fp.exp_avg_sq.cpu(), "step": self.opt_step,
                         "padded": fp.padded, "world_size": W},
@@ -409,13 +410,15 @@ class ShardedEngine:
         fp = self.flat
         info: dict = {}
         if "model" in load_contents:
-            parts = [torch.load(os.path.join(local_path, f"model_world_size_{Wsaved}_rank_{i}.pt"), map_location="cpu")
-                     for i in range(Wsaved)]
-            state = {}
-            for n in fp.names:
-                pieces = [p["params"][n] for p in parts]
-                state[n] = torch.cat(pieces, 0) if pieces[0].ndim else pieces[0]
-            self.load_full_state(state)
+            own = torch.load(os.path.join(local_path, f"model_world_size_{Wsaved}_rank_{self.rank}.pt"),
+                             map_location="cpu") if self.rank < Wsaved else None
+            if (Wsaved == self.world and own is not None and own.get("layout") == "flat"
+                    and own["names"] == list(fp.names) and own["padded"] == fp.padded):
+                # same world size and layout: the shard goes straight back; compute weights are re-gathered
+                fp.master.copy_(own["master"].to(self.device))
+                D.all_gather_into(fp.flat, fp.master.to(fp.dtype), self.group)
+            else:
+                self.load_full_state(read_full_state(local_path, Wsaved))
         if "optimizer" in load_contents:
             if Wsaved == self.world:
                 o = torch.load(os.path.join(local_path, f"optim_world_size_{Wsaved}_rank_{self.rank}.pt"),
@@ -462,6 +465,34 @@ class ShardedEngine:
             info["global_step"] = e.get("global_step", 0)
         D.barrier(self.group)
         return info
+
+
+def read_full_state(ckpt_dir: str, world_size: Optional[int] = None) -> dict:
+    """Every parameter of a sharded actor checkpoint as a full CPU tensor, by name.
+
+    Reads ``model_world_size_{W}_rank_{r}.pt`` for all ``r``: the flat layout (each rank's slice of the
+    flat fp32 master plus the name / offset / shape table) or per-parameter dim-0 shards.
+    """
+    import glob
+    import re
+
+    if world_size is None:
+        files = glob.glob(os.path.join(ckpt_dir, "model_world_size_*_rank_*.pt"))
+        if not files:
+            raise FileNotFoundError(f"no model_world_size_*_rank_*.pt under {ckpt_dir}")
+        world_size = int(re.search(r"model_world_size_(\d+)_rank_", os.path.basename(files[0])).group(1))
+    parts = [torch.load(os.path.join(ckpt_dir, f"model_world_size_{world_size}_rank_{i}.pt"), map_location="cpu")
+             for i in range(world_size)]
+    if parts[0].get("layout") == "flat":
+        flat = torch.cat([p["master"] for p in parts])
+        meta = parts[0]
+        return {n: flat[o:o + k].view(sh).clone()
+                for n, o, k, sh in zip(meta["names"], meta["offsets"], meta["numels"], meta["shapes"])}
+    out = {}
+    for n in parts[0]["params"]:
+        pieces = [p["params"][n] for p in parts]
+        out[n] = torch.cat(pieces, 0) if pieces[0].ndim else pieces[0]
+    return out
 
 
 def _adamw_torch(p, g, m, v, lr, b1, b2, eps, wd, step):
