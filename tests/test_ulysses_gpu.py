@@ -49,6 +49,9 @@ def _run(rank, world):
         e16, esp = rel(g16[n], g32[n]), rel(gs, g32[n])
         # the SP gradient is as close to the fp32 oracle as the one-rank bf16 gradient is
         assert esp <= max(5e-2, 1.5 * e16 + 2e-2), (n, esp, e16)
+    from verl_omni_b200.parallel import peer_a2a as PA
+
+    PA.release_all()
 
 
 def test_qwen_image_ulysses_sp2_nccl():
@@ -140,3 +143,42 @@ def _fused(rank, world):
 def test_ulysses_fused_exchange_matches_nccl_sp2():
     """QKV-GEMM scatter + attention peer output (both exchanges inside kernels) == NCCL all-to-all path."""
     run_ranks(_fused, 2, device="cuda")
+
+
+def _peer_exchange(rank, world):
+    import os
+
+    from verl_omni_b200.parallel import peer_a2a as PA
+    from verl_omni_b200.parallel import ulysses as U
+
+    import torch.distributed as dist
+
+    grp = dist.group.WORLD
+    torch.manual_seed(10 + rank)
+    B, H, Sl, Dh = 2, 8, 40, 64
+    xs = [torch.randn(B, H, Sl, Dh, device="cuda").bfloat16().requires_grad_(True) for _ in range(3)]
+    o = torch.randn(B, world * Sl, (H // world) * Dh, device="cuda").bfloat16().requires_grad_(True)
+    gh = [torch.randn(B, H // world, world * Sl, Dh, device="cuda").bfloat16() for _ in range(3)]
+    gt = torch.randn(B, Sl, H * Dh, device="cuda").bfloat16()
+
+    def run(peer: bool):
+        os.environ["VO_ULYSSES_PEER"] = "1" if peer else "0"
+        assert PA.applies(grp, xs) == peer
+        hs = U.seq_to_head_many(xs, grp)
+        t = U.head_to_seq(o, grp, Dh)
+        loss = sum((h.float() * g.float()).sum() for h, g in zip(hs, gh)) + (t.float() * gt.float()).sum()
+        grads = torch.autograd.grad(loss, xs + [o])
+        return [h.detach() for h in hs] + [t.detach()] + list(grads)
+
+    ref = run(False)
+    for _ in range(3):  # both receive slots, reused
+        got = run(True)
+        for a, b in zip(got, ref):
+            assert torch.equal(a, b)  # pure data movement: bit-exact
+    os.environ["VO_ULYSSES_PEER"] = "1"
+    PA.release_all()
+
+
+def test_ulysses_peer_exchange_matches_nccl_sp2():
+    """Sequence <-> head exchanges as one peer-memory kernel each == NCCL all-to-all, forward and backward."""
+    run_ranks(_peer_exchange, 2, device="cuda")

@@ -108,6 +108,7 @@ torch::Tensor ipc_get_handle(int64_t ptr);
 int64_t ipc_open(torch::Tensor handle);
 void ipc_close(int64_t ptr);
 torch::Tensor tensor_from_ptr(int64_t ptr, int64_t numel, int64_t dtype_code, int64_t device);
+void peer_a2a(torch::Tensor jobs, std::vector<int64_t> src_numel, std::vector<int64_t> dst_ptrs, int64_t dst_cap);
 torch::Tensor peer_grad_reduce(std::vector<int64_t> grad_ptrs, int64_t lo, int64_t n, double scale, torch::Tensor out);
 void peer_adamw_bcast(std::vector<int64_t> flat_ptrs, int64_t lo, int64_t n, torch::Tensor p, torch::Tensor grad,
                       torch::Tensor m, torch::Tensor v, double lr, double b1, double b2, double eps, double wd,
@@ -194,5 +195,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", &vo::ipc_close);
   m.def("tensor_from_ptr", &vo::tensor_from_ptr);
   m.def("peer_grad_reduce", &vo::peer_grad_reduce);
+  m.def("peer_a2a", &vo::peer_a2a, "all-to-all with layout change over peer memory (Ulysses exchanges)");
   m.def("peer_adamw_bcast", &vo::peer_adamw_bcast);
 }

@@ -29,7 +29,7 @@ def _kv_version() -> int:
     """Forward generation for per-sequence key counts (versions 3 and 4 support them)."""
     return min(_FWD_VERSION, 5) if _FWD_VERSION >= 4 else 3
 # backward kernel generation: 2 = pipelined (P^T/dS^T in tensor memory, concurrent dQ drain), 1 = serial
-_BWD_VERSION = int(os.environ.get("VO_FMHA_BWD", "2"))
+_BWD_VERSION = int(os.environ.get("VO_FMHA_BWD", "3"))
 
 
 def _native() -> bool:

@@ -191,6 +191,44 @@ def bench_ulysses(a) -> list[dict]:
                          "ms": round(float(ms), 4), "tflops": round(flops / float(ms) / 1e9, 1),
                          "nvlink_gb": round(xbytes / 1e9, 3), "roofline_ms": round(t_roof, 4),
                          "frac_of_roofline": round(t_roof / float(ms), 3)})
+    # training: forward + backward of the same layer; the exchanges as NCCL all-to-alls with permute copies
+    # vs one peer-memory kernel each (sequence -> heads for q/k/v, heads -> sequence, and their inverses)
+    from verl_omni_b200.parallel import peer_a2a as PA
+
+    hig, htg = hi.clone().requires_grad_(True), ht.clone().requires_grad_(True)
+    goi = torch.randn(B, si, Dm, device=dev, dtype=torch.bfloat16)
+    got = torch.randn(B, st, Dm, device=dev, dtype=torch.bfloat16)
+
+    def train():
+        a0, a1 = qi(hig).reshape(B * si, 3 * Dm), qt(htg).reshape(B * st, 3 * Dm)
+        mk = lambda: torch.empty(B, H, si + st, dh, device=dev, dtype=torch.bfloat16)  # noqa: E731
+        q, k, v = qk_norm_split_into(mk(), mk(), mk(), a0, wn[0], wn[1], si, 0)
+        q, k, v = qk_norm_split_into(q, k, v, a1, wn[2], wn[3], st, si)
+        oi, ot = joint_attention(q, k, v, si, sp_group=grp)
+        torch.autograd.backward([oi, ot], [goi, got])
+
+    for name, peer in (("train_nccl_all_to_all", "0"), ("train_peer_a2a", "1")):
+        os.environ["VO_ULYSSES_PEER"] = peer
+        for _ in range(3):
+            train()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.iters):
+            train()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([e0.elapsed_time(e1) / a.iters], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        S = Si + St
+        flops = 3 * 2.0 * B * (si + st) * Dm * 3 * Dm + 3.5 * 4.0 * B * (H // W) * S * S * dh
+        xbytes = 2 * 2.0 * B * (si + st) * (3 * Dm + Dm) * (W - 1) / W
+        rows.append({"op": f"ulysses_{name}", "world": W, "B": B, "S_img": Si, "S_txt": St, "hidden": Dm,
+                     "ms": round(float(ms), 4), "tflops": round(flops / float(ms) / 1e9, 1),
+                     "nvlink_gb": round(xbytes / 1e9, 3)})
+    os.environ["VO_ULYSSES_PEER"] = "1"
+    PA.release_all()
     UF.release_all()
     if D.rank() != 0:
         return []

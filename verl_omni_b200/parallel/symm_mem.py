@@ -112,9 +112,13 @@ def fused_optimizer_step(flat16: SymmetricBuffer, grad: SymmetricBuffer, lo: int
     """Reduce-scatter + clip + AdamW + all-gather over peer memory; returns the global grad norm."""
     W = grad.world
     stream_barrier(group, master.device)  # every rank's main_grad is final
-    sq = _ext().peer_grad_reduce(grad.peer_ptrs, lo, n, 1.0 / W, grad_shard)
+    # peer lists start at this rank: at any moment the W ranks read (and write) W different peers
+    r = grad.rank
+    gptrs = grad.peer_ptrs[r:] + grad.peer_ptrs[:r]
+    fptrs = flat16.peer_ptrs[r:] + flat16.peer_ptrs[:r]
+    sq = _ext().peer_grad_reduce(gptrs, lo, n, 1.0 / W, grad_shard)
     dist.all_reduce(sq, group=group)  # also orders: every rank finished reading main_grad
-    _ext().peer_adamw_bcast(flat16.peer_ptrs, lo, n, master, grad_shard, exp_avg, exp_avg_sq, lr,
+    _ext().peer_adamw_bcast(fptrs, lo, n, master, grad_shard, exp_avg, exp_avg_sq, lr,
                             float(betas[0]), float(betas[1]), eps, weight_decay, step, max_norm, sq)
     stream_barrier(group, master.device)  # every peer's weights written before anyone reads them
     return sq.sqrt()

@@ -8,8 +8,10 @@ token-major output goes back from ``[B, S, H/sp*D]`` to ``[B, S/sp, H*D]``.  The
 ordered by source rank; full (non-causal) attention is invariant to key order and the inverse exchange
 restores each rank's queries.
 
-The exchanges are autograd functions (backward = the inverse exchange).  On NCCL they are
-``all_to_all_single``; gloo has no all-to-all, so CPU ranks emulate it with an all-gather.
+The exchanges are autograd functions (backward = the inverse exchange).  On one node with symmetric
+memory each is a single peer-memory kernel that writes the destination layout directly
+(``parallel/peer_a2a.py``); otherwise NCCL ``all_to_all_single`` with permute copies around it; gloo has no
+all-to-all, so CPU ranks emulate it with an all-gather.
 """
 
 from __future__ import annotations
@@ -82,10 +84,27 @@ class _HeadToSeq(torch.autograd.Function):
 
 
 def seq_to_head(x: torch.Tensor, group) -> torch.Tensor:
+    from verl_omni_b200.parallel import peer_a2a as PA
+
+    if PA.applies(group, [x]):  # one peer-memory kernel: layout change + NVLink transfer
+        return PA.seq_to_head(group, x)[0]
     return _SeqToHead.apply(x, group)
 
 
+def seq_to_head_many(xs: list, group) -> list:
+    """Several [B, H, S/sp, D] tensors through one exchange (q, k and v of one attention)."""
+    from verl_omni_b200.parallel import peer_a2a as PA
+
+    if PA.applies(group, xs):
+        return list(PA.seq_to_head(group, *xs))
+    return [_SeqToHead.apply(x, group) for x in xs]
+
+
 def head_to_seq(o: torch.Tensor, group, head_dim: int) -> torch.Tensor:
+    from verl_omni_b200.parallel import peer_a2a as PA
+
+    if PA.applies(group, [o]):
+        return PA.head_to_seq(o, group)
     return _HeadToSeq.apply(o, group, head_dim)
 
 
@@ -122,11 +141,11 @@ def ulysses_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, group, 
     if group is None or D.world_size(group) == 1:
         return attention(q, k, v, causal=causal, scale=scale, key_mask=key_mask, kv_len=kv_len)
     Dh = q.shape[-1]
-    kg, vg = seq_to_head(k, group), seq_to_head(v, group)
+    qg, kg, vg = seq_to_head_many([q, k, v], group)
     if kv_len is not None:
         order = segment_major_order(list(key_segments), D.world_size(group), k.device)
         kg, vg = kg.index_select(2, order), vg.index_select(2, order)
-    o = attention(seq_to_head(q, group), kg, vg, causal=causal, scale=scale, key_mask=key_mask, kv_len=kv_len)
+    o = attention(qg, kg, vg, causal=causal, scale=scale, key_mask=key_mask, kv_len=kv_len)
     return head_to_seq(o, group, Dh)
 
 
