@@ -41,10 +41,12 @@ CONFIGS = {
                        "16-ch latents)", seq_len=1024 + 333,
                  reward="random-init VAE decoder 512^2 + ViT-B/16 scorer"),
     "flux_sp2": dict(arch="flux1_dev", prompts_per_dp=6, group=12, sde_steps=16, sp=2, micro=4, max_num_seqs=12,
+                     grad_ckpt=True,
                      model="FLUX.1-dev-shaped rectified-flow transformer (~12B, 19 double + 38 single blocks, hidden "
                            "3072, 24 heads, 2D RoPE), full fine-tune, guidance embedding 3.5", seq_len=4096 + 512,
                      reward="random-init VAE decoder 1024^2 + ViT-B/16 scorer"),
     "wan_sp8_async": dict(arch="wan21_14b", prompts_per_dp=8, group=8, sde_steps=20, sp=8, micro=1, max_num_seqs=4,
+                          grad_ckpt=True,
                           model="Wan2.1-14B-shaped video DiT (40 blocks, hidden 5120, 40 heads, FFN 13824, 3D RoPE), "
                                 "81 frames 480x832", seq_len=32760 + 512, v1="separate_async",
                           reward="random-init VAE decoder + 12-layer ViT per frame, mean-pooled"),
@@ -86,20 +88,30 @@ def _clock_summary(path: str) -> dict:
     return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons)}
 
 
+_REF_INSTALL = ("python -m pip install --no-index --no-build-isolation --find-links /opt/wheelhouse --target "
+                "baseline/_ref <reference source>")
+
+
 def reference_arm(args) -> None:
+    """The reference's own trainer through its public entry point, or one line saying why it cannot run.
+
+    The offline install with dependencies stops at resolution (``accelerate>=1.14.0`` is not in the
+    wheelhouse); with ``--no-deps`` it installs, and the import of its trainer names the first missing
+    runtime dependency, which is reported here as found on this machine."""
     ref = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
-    why = None
     if not os.path.isdir(os.path.join(ref, "verl_omni")):
-        why = "reference not installed under baseline/_ref"
+        why = (f"not installed under baseline/_ref: `{_REF_INSTALL}` fails offline (accelerate>=1.14.0 not in "
+               "the wheelhouse); the --no-deps install imports without diffusers/verl/ray/vllm_omni")
     else:
         sys.path.insert(0, ref)
         try:
             import verl_omni.trainer.main_diffusion  # noqa: F401
+
+            why = ("reference imports, but its trainer needs a Ray cluster and vLLM-Omni rollout servers, "
+                   "neither installable offline")
         except Exception as e:  # noqa: BLE001
-            why = (f"reference installed (pip --no-deps) but its runtime dependencies are absent offline: "
+            why = (f"`{_REF_INSTALL} --no-deps` installed it; importing verl_omni.trainer.main_diffusion fails: "
                    f"{type(e).__name__}: {e}".replace("\n", " "))
-    if why is None:
-        why = "reference importable but its trainer needs Ray + vLLM-Omni servers, unavailable offline"
     if int(os.environ.get("RANK", "0")) == 0:
         print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
 
@@ -174,6 +186,8 @@ def main() -> None:
         "trainer.total_training_steps=1000", "trainer.resume_mode=disable", "trainer.logger=[]",
         "trainer.save_freq=-1",
     ]
+    if C.get("grad_ckpt"):  # multi-billion-parameter models at 4-32k tokens: recompute block activations
+        ov.append("actor_rollout_ref.model.enable_gradient_checkpointing=true")
     if C.get("v1"):
         ov += ["trainer.use_v1=true", f"trainer.v1.trainer_mode={C['v1']}"]
     cfg = load_config("diffusion_trainer", ov)

@@ -86,3 +86,59 @@ def test_decode_attention_clamps_lengths_and_block_ids():
     v0 = torch.cat([vp[0], torch.zeros_like(vp[0])], 1)[None]
     ref0 = decode_attention_reference(q[:1], k0, v0, lens[:1], hd ** -0.5)
     torch.testing.assert_close(out[:1].float(), ref0.float(), rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("rep,Hk", [(8, 4), (16, 2), (1, 8), (4, 1)])
+@pytest.mark.parametrize("splits", [0, 1, 3])
+@pytest.mark.parametrize("block", [0, 8, 32, 128])
+def test_decode_tcgen05_matches_reference(rep, Hk, splits, block):
+    """head_dim 128 runs the tcgen05 kernel (TMA tiles, tensor-core QK^T / PV): contiguous and paged caches,
+    partial last tiles, empty key splits, zero-length sequences."""
+    from verl_omni_b200.ops._ext import ext
+    from verl_omni_b200.ops.decode import decode_attention, decode_attention_reference, gather_paged
+
+    torch.manual_seed(0)
+    hd, B = 128, 4
+    lens = torch.tensor([1, 129, 700, 0], dtype=torch.int32, device="cuda")
+    q = torch.randn(B, Hk * rep, hd, device="cuda").bfloat16()
+    if block == 0:
+        Lmax = 768
+        kc = torch.randn(B, Hk, Lmax, hd, device="cuda").bfloat16()
+        vc = torch.randn(B, Hk, Lmax, hd, device="cuda").bfloat16()
+        # rows past each length hold non-finite garbage: they must not leak into the result
+        for bi, L in enumerate(lens.tolist()):
+            vc[bi, :, L:] = float("nan")
+            kc[bi, :, L:] = float("inf")
+        out = decode_attention(q, kc, vc, lens, splits=splits)
+        ref = decode_attention_reference(q, kc, vc, lens, hd ** -0.5)
+    else:
+        width = (int(lens.max()) + block - 1) // block
+        nb = B * width + 3
+        table = torch.randperm(nb)[:B * width].view(B, width).to(torch.int32).cuda()
+        kp = torch.randn(nb, Hk, block, hd, device="cuda").bfloat16()
+        vp = torch.randn(nb, Hk, block, hd, device="cuda").bfloat16()
+        out = decode_attention(q, kp, vp, lens, splits=splits, block_table=table)
+        ref = decode_attention_reference(q, gather_paged(kp, table, lens), gather_paged(vp, table, lens), lens,
+                                         hd ** -0.5)
+    assert ext().decode_tc_error(True) == 0
+    ref = torch.where(lens[:, None, None] > 0, ref.float(), torch.zeros_like(ref.float()))
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+
+
+def test_decode_tcgen05_equals_cuda_core_path(monkeypatch):
+    """The tensor-core kernel and the CUDA-core kernel agree, including out-of-pool block ids (zero rows)."""
+    from verl_omni_b200.ops._ext import ext
+
+    torch.manual_seed(1)
+    B, Hk, rep, hd, bs, nb = 3, 4, 8, 128, 16, 40
+    q = torch.randn(B, Hk * rep, hd, device="cuda").bfloat16()
+    kp = torch.randn(nb, Hk, bs, hd, device="cuda").bfloat16()
+    vp = torch.randn(nb, Hk, bs, hd, device="cuda").bfloat16()
+    table = torch.randint(0, nb, (B, 12), dtype=torch.int32, device="cuda")
+    table[0, 3] = 9999  # outside the pool: reads as zero keys and values on both paths
+    lens = torch.tensor([100, 192, 37], dtype=torch.int32, device="cuda")
+    tc = ext().decode_attention(q, kp, vp, lens, hd ** -0.5, 0, table)
+    monkeypatch.setenv("VO_DECODE_TC", "0")
+    cc = ext().decode_attention(q, kp, vp, lens, hd ** -0.5, 0, table)
+    assert ext().decode_tc_error(True) == 0
+    torch.testing.assert_close(tc.float(), cc.float(), rtol=2e-2, atol=2e-2)

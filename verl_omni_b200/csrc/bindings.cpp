@@ -90,6 +90,7 @@ torch::Tensor head_rmsnorm_rope_bwd(torch::Tensor dy, torch::Tensor x, int64_t c
                                     torch::Tensor cos_t, torch::Tensor sin_t, double eps, torch::Tensor dw);
 torch::Tensor sq_dist_fwd(torch::Tensor a, torch::Tensor b);
 std::vector<torch::Tensor> sq_dist_bwd(torch::Tensor a, torch::Tensor b, torch::Tensor g, bool want_gb);
+int64_t decode_tc_error(bool reset);
 torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor lens,
                                double scale, int64_t splits, c10::optional<torch::Tensor> block_table);
 void fmha_fwd_peer(torch::Tensor q, torch::Tensor k, torch::Tensor v, std::vector<int64_t> peer_o,
@@ -174,6 +175,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("router_topk", &vo::router_topk, "softmax router + top-k with renormalised gates");
   m.def("head_rmsnorm_rope", &vo::head_rmsnorm_rope, "per-head RMSNorm + rotate-half RoPE, [B,S,H*Dh] -> [B,H,S,Dh]");
   m.def("head_rmsnorm_rope_bwd", &vo::head_rmsnorm_rope_bwd, "backward of head_rmsnorm_rope");
+  m.def("decode_tc_error", &vo::decode_tc_error, "first error code of a bounded wait in the tcgen05 decode kernel");
   m.def("decode_attention", &vo::decode_attention,
         "grouped-query decode attention over a contiguous or paged (block table) KV cache", py::arg("q"),
         py::arg("k_cache"), py::arg("v_cache"), py::arg("lens"), py::arg("scale"), py::arg("splits"),

@@ -15,7 +15,15 @@
 // Paged mode (vLLM-style block tables): the cache is a pool of fixed-size blocks [blocks, Hk, block, HD] and
 // row t of sequence b lives in block table[b][t / block] at offset t % block; the staging loads resolve
 // every row through the table, the rest of the kernel is unchanged.
+#include <cstdlib>
+
 #include "common.cuh"
+
+extern "C" int vo_decode_tc(const void* q, const void* kc, const void* vc, const int* lens, const int* table,
+                            int stride, int block, int nblocks, int B, int Hk, int Lmax, int rep, int hd,
+                            float scale_log2, int splits, void* out, float* part_o, float* part_ml,
+                            cudaStream_t stream);
+extern "C" int vo_decode_tc_error(int reset);
 
 namespace vo {
 namespace {
@@ -280,12 +288,62 @@ void launch_decode(const torch::Tensor& q, const torch::Tensor& kc, const torch:
   VO_CUDA_OK(cudaGetLastError());
 }
 
+// key splits: enough CTAs to cover the SMs `per_sm` times over, at least `min_keys` keys per split
+int pick_splits(int64_t pairs, int64_t span, int per_sm, int64_t min_keys, int cap) {
+  const int64_t want = (per_sm * (int64_t)num_sms() + pairs - 1) / std::max<int64_t>(pairs, 1);
+  return (int)std::max<int64_t>(1, std::min<int64_t>({want, (int64_t)cap, std::max<int64_t>(1, span / min_keys)}));
+}
+
 }  // namespace
+
+// q [B, Hk * rep, 128] against the cache on the tcgen05 kernel (csrc/decode_attn_sm100.cu); false when the
+// shape is outside it (the CUDA-core kernel runs instead)
+static bool decode_tc(const torch::Tensor& q, const torch::Tensor& kc, const torch::Tensor& vc, const torch::Tensor& lens,
+                      float scale_log2, int64_t splits, const PageTable& pt, torch::Tensor& out) {
+  const char* env = std::getenv("VO_DECODE_TC");
+  if (env && env[0] == '0') return false;
+  const int B = (int)q.size(0), Hk = (int)kc.size(1), HD = (int)q.size(2), rep = (int)(q.size(1) / Hk);
+  if (HD != 128 || (rep != 1 && rep != 2 && rep != 4 && rep != 8 && rep != 16)) return false;
+  if (pt.table && (pt.block % 8 || 128 % pt.block)) return false;
+  const int Lmax = pt.table ? 0 : (int)kc.size(2);
+  const int64_t span = pt.table ? (int64_t)pt.stride * pt.block : Lmax;
+  // one CTA per SM (two 64 KB K / V stages): about two CTAs per SM, at least four 128-key tiles each
+  const int sp = splits > 0 ? (int)splits : pick_splits((int64_t)B * Hk, span, 2, 512, 64);
+  auto fo = q.options().dtype(torch::kFloat32);
+  torch::Tensor po, pml;
+  if (sp > 1) {
+    po = torch::empty({B, Hk, sp, rep, HD}, fo);
+    pml = torch::empty({B, Hk, sp, rep, 2}, fo);
+  }
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int rc = vo_decode_tc(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), lens.data_ptr<int>(), pt.table, pt.stride,
+                              pt.block, pt.nblocks, B, Hk, Lmax, rep, HD, scale_log2, sp, out.data_ptr(),
+                              sp > 1 ? po.data_ptr<float>() : nullptr, sp > 1 ? pml.data_ptr<float>() : nullptr, st);
+  if (rc == -1) return false;
+  TORCH_CHECK(rc == 0, "tcgen05 decode attention launch failed: ", rc);
+  count_launch();
+  if (sp > 1) {
+    const int64_t total = (int64_t)B * Hk * rep * HD;
+    const int grid = (int)std::min<int64_t>((total + 255) / 256, 4096);
+    auto* o = reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>());
+#define VO_COMB(R) \
+  if (rep == R) decode_combine_kernel<128, R><<<grid, 256, 0, st>>>(po.data_ptr<float>(), pml.data_ptr<float>(), Hk, sp, total, o);
+    VO_COMB(1) VO_COMB(2) VO_COMB(4) VO_COMB(8) VO_COMB(16)
+#undef VO_COMB
+    count_launch();
+  }
+  VO_CUDA_OK(cudaGetLastError());
+  return true;
+}
+
+int64_t decode_tc_error(bool reset) { return vo_decode_tc_error(reset ? 1 : 0); }
 
 // q [B, Hq, HD] bf16; k_cache / v_cache [B, Hk, Lmax, HD] bf16 -- or, with block_table [B, max_blocks]
 // int32, block pools [blocks, Hk, block, HD]; lens [B] int32 (valid rows, >= 1; with a table at most
 // max_blocks x block; longer lengths are clamped to the cache, table ids outside the pool read as zeros).
-// Returns o [B, Hq, HD].  Hq = Hk x rep with rep in {1, 2, 4, 8}; HD in {64, 128}.
+// Returns o [B, Hq, HD].  Hq = Hk x rep with rep in {1, 2, 4, 8} (16 as well at HD 128); HD in {64, 128}.
+// splits <= 0 picks the key split count for the kernel that runs.  head_dim 128 runs the tcgen05 kernel
+// (paged blocks of a multiple of 8 rows dividing 128); the rest the CUDA-core kernel above.
 torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor lens,
                                double scale, int64_t splits, c10::optional<torch::Tensor> block_table) {
   VO_CHECK_INPUT(q);
@@ -315,7 +373,10 @@ torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Te
   auto out = torch::empty_like(q);
   const int rep = (int)(Hq / Hk);
   const float sl2 = (float)scale * 1.4426950408889634f;
-  const int sp = (int)std::max<int64_t>(1, splits);
+  if (decode_tc(q, k_cache, v_cache, lens, sl2, splits, pt, out)) return out;
+  // CUDA-core kernel: about 16 CTAs per SM (5 resident at once) for memory parallelism, >= 256 keys each
+  const int64_t span = pt.table ? (int64_t)pt.stride * pt.block : k_cache.size(2);
+  const int sp = splits > 0 ? (int)splits : pick_splits(B * Hk, span, 16, 256, 16);
 #define VO_DEC(HDV, REPV) \
   if (HD == HDV && rep == REPV) return launch_decode<HDV, REPV>(q, k_cache, v_cache, lens, sl2, sp, pt, out), out;
   VO_DEC(128, 8) VO_DEC(128, 4) VO_DEC(128, 2) VO_DEC(128, 1) VO_DEC(64, 8) VO_DEC(64, 4) VO_DEC(64, 2) VO_DEC(64, 1)

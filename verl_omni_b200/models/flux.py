@@ -173,11 +173,19 @@ class FluxDiT(nn.Module):
             x, c = shard_sequence(x, sp), shard_sequence(c, sp)
             rope = (local_rows(rope[0], [Si, St], sp), local_rows(rope[1], [Si, St], sp))
         Sl = x.shape[1]
+        ckpt = self.gradient_checkpointing and torch.is_grad_enabled()
         for blk in self.transformer_blocks:
-            x, c = blk(x, c, ta, rope, sp_group=sp, rope_full=rope_full)
+            if ckpt:  # keep only block inputs; the block's activations are recomputed in backward
+                x, c = torch.utils.checkpoint.checkpoint(blk, x, c, ta, rope, None, sp, None, rope_full,
+                                                         use_reentrant=False)
+            else:
+                x, c = blk(x, c, ta, rope, sp_group=sp, rope_full=rope_full)
         xs = torch.cat([x, c], 1)
         for blk in self.single_transformer_blocks:
-            xs = blk(xs, ta, rope, sp_group=sp)
+            if ckpt:
+                xs = torch.utils.checkpoint.checkpoint(blk, xs, ta, rope, sp, use_reentrant=False)
+            else:
+                xs = blk(xs, ta, rope, sp_group=sp)
         x = xs[:, :Sl].contiguous()
         x = adaln_layernorm(x, self.norm_out_linear(ta), 1, 0, 2, cfg.eps)
         y = self.proj_out(x)

@@ -453,16 +453,22 @@ def bench_decode(a) -> list[dict]:
     kp[perm] = kc.view(B, Hk, L // bs, bs, hd).permute(0, 2, 1, 3, 4).reshape(nb, Hk, bs, hd)
     vp[perm] = vc.view(B, Hk, L // bs, bs, hd).permute(0, 2, 1, 3, 4).reshape(nb, Hk, bs, hd)
     table = perm.view(B, L // bs).to(torch.int32)
+    import os
+
     nbytes = 2 * B * Hk * L * hd * 2
     out = []
-    for name, fn in (("contiguous", lambda sp: decode_attention(q, kc, vc, lens, splits=sp)),
-                     ("paged16", lambda sp: decode_attention(q, kp, vp, lens, splits=sp, block_table=table))):
-        if a.only and name not in a.only.split(","):
-            continue
-        for sp in ([0] if not a.compare else [0, 2, 4, 8, 16]):  # 0: the default split heuristic
-            ms = timeit(lambda: fn(sp), a.iters)
-            out.append({"op": f"decode_attn_{name}", "splits": sp or "auto", "B": B, "ctx": L, "q_heads": Hk * rep,
-                        "kv_heads": Hk, "hd": hd, "ms": round(ms, 4), "gbs": round(nbytes / ms / 1e6, 1)})
+    for kernel in ("tcgen05", "cuda_core"):  # VO_DECODE_TC=0 selects the CUDA-core kernel
+        os.environ["VO_DECODE_TC"] = "1" if kernel == "tcgen05" else "0"
+        for name, fn in (("contiguous", lambda sp: decode_attention(q, kc, vc, lens, splits=sp)),
+                         ("paged16", lambda sp: decode_attention(q, kp, vp, lens, splits=sp, block_table=table))):
+            if a.only and name not in a.only.split(","):
+                continue
+            for sp in ([0] if not a.compare else [0, 1, 2, 4, 8]):  # 0: the default split heuristic
+                ms = timeit(lambda: fn(sp), a.iters)
+                out.append({"op": f"decode_attn_{name}", "kernel": kernel, "splits": sp or "auto", "B": B, "ctx": L,
+                            "q_heads": Hk * rep, "kv_heads": Hk, "hd": hd, "ms": round(ms, 4),
+                            "gbs": round(nbytes / ms / 1e6, 1)})
+    os.environ["VO_DECODE_TC"] = "1"
     return out
 
 

@@ -5,9 +5,11 @@
 * :class:`PagedKVCache` -- a pool of fixed-size blocks ``[blocks, Hk, block, hd]`` shared by sequences of
   different lengths, a free list and one block table per sequence (vLLM's paged layout): sequences that
   finish return their blocks at once, memory follows the tokens actually cached;
-* :func:`decode_attention` -- one new query token per sequence against the cache (``csrc/decode_attn.cu``:
+* :func:`decode_attention` -- one new query token per sequence against the cache: at head_dim 128 a tcgen05
+  kernel (``csrc/decode_attn_sm100.cu``: TMA-staged 128-key tiles, S^T = K Q^T and O^T = V^T P^T on the
+  tensor cores with the query heads of a KV group as N), else the CUDA-core kernel (``csrc/decode_attn.cu``);
   each CTA reads a (sequence, KV head) slice of the cache once for all query heads of its group,
-  flash-decoding splits for long caches); fp32 torch oracle on CPU;
+  flash-decoding splits for long caches; fp32 torch oracle on CPU;
 * :func:`sample_tokens` -- temperature / top-k / top-p sampling and the sampled tokens' log-probs on the
   device (Gumbel-max over the filtered logits with a seeded device generator): no host round trip per token.
 
@@ -172,15 +174,12 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     hd = q.shape[-1]
     scale = scale if scale is not None else 1.0 / math.sqrt(hd)
     rep = q.shape[1] // k_cache.shape[1]
-    if not q.is_cuda or hd not in (64, 128) or rep not in (1, 2, 4, 8) or q.dtype != torch.bfloat16:
+    reps = (1, 2, 4, 8, 16) if hd == 128 else (1, 2, 4, 8)
+    if not q.is_cuda or hd not in (64, 128) or rep not in reps or q.dtype != torch.bfloat16:
         if block_table is not None:
             k_cache, v_cache = gather_paged(k_cache, block_table, lens), gather_paged(v_cache, block_table, lens)
         return decode_attention_reference(q, k_cache, v_cache, lens, scale)
-    if splits <= 0:  # about 16 CTAs per SM (5 are resident at once): memory parallelism for the cache reads
-        n = q.shape[0] * k_cache.shape[1]
-        span = k_cache.shape[2] * (block_table.shape[1] if block_table is not None else 1)
-        splits = max(1, min(16, (16 * torch.cuda.get_device_properties(q.device).multi_processor_count) // max(n, 1)))
-        splits = min(splits, max(1, int(span) // 256))
+    # splits <= 0: the extension picks the key split count for the kernel that runs (tcgen05 at head_dim 128)
     bt = block_table.to(torch.int32).contiguous() if block_table is not None else None
     return _ext().decode_attention(q.contiguous(), k_cache, v_cache, lens.to(torch.int32).contiguous(), float(scale),
                                    int(splits), bt)

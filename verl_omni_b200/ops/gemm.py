@@ -72,9 +72,13 @@ def matmul_nn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
 
 
 def wgrad(dy: torch.Tensor, x: torch.Tensor, main_grad: Optional[torch.Tensor]):
-    """``dy[M,N]^T @ x[M,K]``; accumulated (fp32) into ``main_grad`` when given (returns None)."""
+    """``dy[M,N]^T @ x[M,K]``; accumulated (fp32) into ``main_grad`` when given (returns None).
+
+    The output is ``[N, K]``: the tile count depends on N and K only, so a short reduction (the AdaLN
+    modulation linear, M = one row per sample) still fills the tensor-core tiles, and the fused fp32
+    accumulation into ``main_grad`` replaces a bf16 GEMM plus a separate add."""
     if dy.dtype == x.dtype == torch.bfloat16 and _use_native(dy.shape[1], x.shape[1],
-                                                             rows=min(dy.shape[0], dy.shape[1])):
+                                                             rows=min(dy.shape[1], x.shape[1])):
         if main_grad is not None:
             ext().gemm_wgrad(dy, x, main_grad, True)
             return None

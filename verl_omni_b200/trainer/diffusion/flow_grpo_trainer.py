@@ -123,7 +123,13 @@ class PolicyGradientTrainer:
         torch.manual_seed(seed)
         cuda = self.device.type == "cuda"
         # ---------------------------------------------------------------- models
-        module = self.spec.build()
+        if cuda and self.spec.init_on_device:
+            # multi-billion-parameter presets: built (and randomly initialised) on the device, no fp32 host copy
+            # per rank; the engine then moves each parameter into its flat buffers and frees it one by one
+            with torch.device(self.device):
+                module = self.spec.build()
+        else:
+            module = self.spec.build()
         load_pretrained(module, self.model_cfg.path)
         if self.model_cfg.enable_gradient_checkpointing and hasattr(module, "gradient_checkpointing"):
             module.gradient_checkpointing = True

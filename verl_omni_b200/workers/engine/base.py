@@ -80,20 +80,24 @@ class FlatParams:
         else:
             self.flat = torch.zeros(self.padded, dtype=dtype, device=device)
             self.main_grad = torch.zeros(self.padded, dtype=torch.float32, device=device)
-        master_full = torch.zeros(self.padded, dtype=torch.float32, device=device)
-        for p, o, n in zip(self.params, self.offsets, self.numels):
-            src = p.detach().reshape(-1).to(device=device, dtype=torch.float32)
-            master_full[o:o + n].copy_(src)
-        self.flat.copy_(master_full.to(dtype))
-        self.master = master_full[self.shard_lo:self.shard_lo + self.shard_size].clone()
-        del master_full
-        self.exp_avg = torch.zeros_like(self.master)
-        self.exp_avg_sq = torch.zeros_like(self.master)
-        self.grad_shard = torch.zeros_like(self.master)
+        # parameter by parameter: the compute copy into the flat buffer, this rank's slice into the fp32
+        # master, then the parameter is rebound to its flat view (its own storage is released at once), so
+        # no full-size fp32 temporary exists and peak memory stays near one model copy
+        self.flat.zero_()
+        self.master = torch.zeros(self.shard_size, dtype=torch.float32, device=device)
+        lo, hi = self.shard_lo, self.shard_lo + self.shard_size
         for p, o, n, s in zip(self.params, self.offsets, self.numels, self.shapes):
+            src = p.detach().reshape(-1)
+            self.flat[o:o + n].copy_(src)
+            a, b = max(o, lo), min(o + n, hi)
+            if a < b:
+                self.master[a - lo:b - lo].copy_(src[a - o:b - o])
             p.data = self.flat[o:o + n].view(s)
             p.main_grad = self.main_grad[o:o + n].view(s)
             p.register_post_accumulate_grad_hook(self._accumulate)
+        self.exp_avg = torch.zeros_like(self.master)
+        self.exp_avg_sq = torch.zeros_like(self.master)
+        self.grad_shard = torch.zeros_like(self.master)
         if not owns_module:
             return
         # non-trainable parameters and buffers follow the compute dtype/device
