@@ -116,6 +116,17 @@ def reference_arm(args) -> None:
         print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
 
 
+def _max_mem_gb(dev, n: int) -> float:
+    """Peak bytes held by the caching allocator on any rank (GB), symmetric buffers excluded."""
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([torch.cuda.max_memory_allocated(dev) / 1e9], dtype=torch.float64, device=dev)
+    if n > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return round(float(t.item()), 2)
+
+
 class _PinnedOnce:
     """Serves one pre-pinned host batch through the dataset interface (end-to-end input path)."""
 
@@ -284,6 +295,7 @@ def main() -> None:
                "h2d_bytes_per_step": h2d // e2e_steps, "d2h_bytes_per_step": d2h // e2e_steps,
                "ms_per_step": round(1000.0 * wall / e2e_steps, 2), "steps": e2e_steps}
     clocks = _clock_summary(clock_path) if info.local_rank == 0 else None
+    mem_gb = _max_mem_gb(dev, N)
     if info.rank == 0:
         out = {
             "metric": METRIC, "value": round(value, 4), "unit": "samples/s", "n_gpus": N, "steps": args.steps,
@@ -296,6 +308,7 @@ def main() -> None:
                        "parallelism": f"dp{dp}" + (f"_sp{sp}" if sp > 1 else ""), "reward": C["reward"],
                        "trainer": C.get("v1", "sync"), "l2": "inputs larger than L2 (no flush)"},
             "impl": "native", "gpu_launches": launches, "clocks": clocks, "e2e": e2e, "phase_s": timing, "mfu": mfu,
+            "max_memory_allocated_gb": mem_gb,
         }
         print(json.dumps(out), flush=True)
     D.destroy()
@@ -348,6 +361,7 @@ def bench_omni(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item()) / args.steps
     samples = per_dp * dp * group
+    mem_gb = _max_mem_gb(info.device, N)
     if info.rank == 0:
         print(json.dumps({
             "metric": METRIC, "value": round(samples / (ms / 1000.0), 4), "unit": "samples/s", "n_gpus": N,
@@ -359,7 +373,7 @@ def bench_omni(args) -> None:
                        "name": "omni_moe", "global_batch": samples, "prompts": per_dp * dp, "group": group,
                        "seq_len": 512 + 1024, "parallelism": f"ep{N}_tp{tp}_dp{dp}", "reward": "seeded hash of the "
                        "response tokens", "l2": "inputs larger than L2 (no flush)"},
-            "impl": "native", "gpu_launches": ext().launch_count() - launches0,
+            "impl": "native", "gpu_launches": ext().launch_count() - launches0, "max_memory_allocated_gb": mem_gb,
             "phase_s": {k: round(v, 3) for k, v in m.items() if k.startswith("timing_s/")}}), flush=True)
     D.destroy()
 

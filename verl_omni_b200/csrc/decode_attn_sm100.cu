@@ -4,7 +4,8 @@
 // Decode reads every cached K / V row once; the work per row is tiny, so the kernel is built to keep the
 // copy engine (TMA) streaming and the issue slots free:
 //   * one CTA per (sequence, KV head, key split); tiles of 128 keys, K and V staged by TMA (128B swizzle)
-//     in a two-stage ring, paged caches resolved block by block through the block table;
+//     in a three-stage ring, paged caches resolved block by block through the block table (one warp reads
+//     a tile's block ids in parallel, a tile ahead);
 //   * S^T = K Q^T on the tensor core with the keys as M (128) and the query heads of the group as N (16,
 //     zero-padded): 8 MMAs per tile, the 128 x 16 fp32 scores land in tensor memory, one key per lane;
 //   * softmax warps (4 x 32 = 128 threads, thread = key) take per-head tile maxima with warp shuffles,
@@ -27,7 +28,7 @@ constexpr int TK = 128;        // keys per tile (MMA M of S^T, K of O^T)
 constexpr int HD = 128;        // head dim (MMA M of O^T)
 constexpr int NH = 16;         // MMA N: query heads of one group, zero-padded
 constexpr int NTHREADS = 192;  // warps 0-3 compute, 4 producer, 5 MMA
-constexpr int STAGES = 2;
+constexpr int STAGES = 3;     // K / V ring: three 64 KB tiles in flight per SM
 constexpr int KV_BYTES = TK * HD * 2;  // K or V of one tile: 32 KB (two 16 KB swizzle atoms of 64 columns)
 constexpr int STAGE_BYTES = 2 * KV_BYTES;
 constexpr int Q_OFF = STAGES * STAGE_BYTES;      // Q: 16 rows x 128, K-major, two 2 KB atoms
@@ -35,7 +36,7 @@ constexpr int P_OFF = Q_OFF + 2 * 2048;          // P^T: two buffers of 16 rows 
 constexpr int RED_OFF = P_OFF + 2 * 4096;        // per-warp head maxima, two tile parities: 2 x 4 x 16 floats
 constexpr int MASK_OFF = RED_OFF + 2 * 4 * NH * 4;  // per stage: valid-row bitmask (4 words), zero-row bitmask (4)
 constexpr int BAR_OFF = MASK_OFF + STAGES * 32;
-constexpr int NBARS = 14;
+constexpr int NBARS = 2 * STAGES + 10;
 constexpr int SMEM_BYTES = BAR_OFF + NBARS * 8 + 16;
 constexpr int S_COL = 0, O_COL = 32, TMEM_COLS = 64;
 constexpr unsigned long long WAIT_BUDGET = 4ull * 1000 * 1000 * 1000;
@@ -150,13 +151,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   extern __shared__ __align__(1024) uint8_t raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BAR_OFF);
-  uint64_t* full = bars;          // [2] TMA landed (count 1 + tx)
-  uint64_t* kv_empty = bars + 2;  // [2] PV of the stage's tile done (commit)
-  uint64_t* s_full = bars + 4;    // [2] scores in tensor memory (commit)
-  uint64_t* s_empty = bars + 6;   // [2] scores read (128 arrivals)
-  uint64_t* p_full = bars + 8;    // [2] P^T written (128 arrivals)
-  uint64_t* o_full = bars + 10;   // [2] tile output in tensor memory (commit)
-  uint64_t* o_empty = bars + 12;  // [2] tile output read (128 arrivals)
+  uint64_t* full = bars;                   // [STAGES] K / V of a tile landed (count 1 + tx)
+  uint64_t* kv_empty = full + STAGES;      // [STAGES] PV of the stage's tile done (commit)
+  uint64_t* s_full = kv_empty + STAGES;    // [2] scores in tensor memory (commit)
+  uint64_t* s_empty = s_full + 2;          // [2] scores read (128 arrivals)
+  uint64_t* p_full = s_empty + 2;          // [2] P^T written (128 arrivals)
+  uint64_t* o_full = p_full + 2;           // [2] tile output in tensor memory (commit)
+  uint64_t* o_empty = o_full + 2;          // [2] tile output read (128 arrivals)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint32_t* mask = reinterpret_cast<uint32_t*>(sm + MASK_OFF);
@@ -166,14 +167,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int bk = blockIdx.x, split = blockIdx.y;
   const int b = bk / p.Hk, kh = bk % p.Hk;
   const int L = max(0, min(p.lens[b], p.table ? p.stride * p.block : p.Lmax));
-  const int per = (L + p.splits - 1) / p.splits;
+  // splits cover whole 128-key tiles: every tile starts on a block boundary of a paged cache
+  const int per = ((L + p.splits - 1) / p.splits + TK - 1) / TK * TK;
   const int s0 = min(L, split * per), s1 = min(L, s0 + per);
   const int ntiles = (s1 - s0 + TK - 1) / TK;
 
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < STAGES; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 128);
       mbar_init(&p_full[i], 128);
@@ -209,69 +213,78 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 4) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      int issued = 0;
-      for (int i = 0; i < ntiles; ++i) {
-        const int st = i & 1;
-        if (!mbar_wait(&kv_empty[st], ((i >> 1) & 1) ^ 1, abort_flag, 1)) break;
-        const int t0 = s0 + i * TK;
-        const int nvalid = min(TK, s1 - t0);
-        uint8_t* sk = sm + st * STAGE_BYTES;
-        uint8_t* sv = sk + KV_BYTES;
-        uint32_t m[4] = {0u, 0u, 0u, 0u}, z[4] = {0u, 0u, 0u, 0u};
-        if (!p.table) {
-          for (int r = 0; r < nvalid; ++r) m[r >> 5] |= 1u << (r & 31);
+    // ------------------------------------------------------------------ TMA producer (one warp)
+    // Paged caches: lane j resolves block j of a tile (one table read per lane, all in flight at once) and,
+    // once lane 0 has armed the stage's barrier, issues that block's copies; the next tile's ids are read
+    // before the wait for its stage, so the table latency hides behind the ring.
+    const int blk = p.table ? p.block : TK;
+    const int nblk = TK / blk;
+    auto read_id = [&](int i) {
+      const int t = s0 + i * TK + lane * blk;
+      if (i >= ntiles || lane >= nblk || t >= s1) return -2;  // no keys here
+      return __ldg(p.table + (int64_t)b * p.stride + t / blk);
+    };
+    int id_next = p.table ? read_id(0) : -2;
+    int issued = 0;
+    for (int i = 0; i < ntiles; ++i) {
+      const int kv = i % STAGES;
+      const int id = id_next;
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(&kv_empty[kv], ((i / STAGES) & 1) ^ 1, abort_flag, 1);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) break;
+      if (p.table) id_next = read_id(i + 1);
+      const int t0 = s0 + i * TK;
+      const int nvalid = min(TK, s1 - t0);
+      uint8_t* sk = sm + kv * STAGE_BYTES;
+      uint8_t* sv = sk + KV_BYTES;
+      if (!p.table) {
+        if (lane == 0) {
           for (int w = 0; w < 4; ++w) {
-            mask[st * 8 + w] = m[w];
-            mask[st * 8 + 4 + w] = 0u;
+            const int lo = w * 32;
+            mask[kv * 8 + w] = nvalid >= lo + 32 ? 0xffffffffu : nvalid <= lo ? 0u : (1u << (nvalid - lo)) - 1u;
+            mask[kv * 8 + 4 + w] = 0u;
           }
-          mbar_expect_tx(&full[st], 2 * KV_BYTES);
+          mbar_expect_tx(&full[kv], 2 * KV_BYTES);
           const int row = bk * p.Lmax + t0;
           for (int a = 0; a < HD / 64; ++a) {
-            tma_load_2d(sk + a * (TK * 128), &mk, &full[st], a * 64, row);
-            tma_load_2d(sv + a * (TK * 128), &mv, &full[st], a * 64, row);
-          }
-        } else {
-          const int blk = p.block;
-          int ids[TK / 8];
-          uint32_t bytes = 0;
-          for (int j = 0; j < TK / blk; ++j) {
-            ids[j] = -1;
-            const int t = t0 + j * blk;
-            if (t >= s1) continue;
-            const int id = __ldg(p.table + (int64_t)b * p.stride + t / blk);
-            const bool in_pool = id >= 0 && id < p.nblocks;
-            for (int r = j * blk; r < min((j + 1) * blk, nvalid); ++r) {
-              m[r >> 5] |= 1u << (r & 31);
-              if (!in_pool) z[r >> 5] |= 1u << (r & 31);  // out-of-pool ids read as zero keys and values
-            }
-            if (!in_pool) continue;
-            ids[j] = id;
-            bytes += 2u * blk * HD * 2;
-          }
-          for (int w = 0; w < 4; ++w) {
-            mask[st * 8 + w] = m[w];
-            mask[st * 8 + 4 + w] = z[w];
-          }
-          mbar_expect_tx(&full[st], bytes);
-          for (int j = 0; j < TK / blk; ++j) {
-            if (ids[j] < 0) continue;
-            const int row = (ids[j] * p.Hk + kh) * blk;
-            for (int a = 0; a < HD / 64; ++a) {
-              tma_load_2d(sk + a * (TK * 128) + j * blk * 128, &mk, &full[st], a * 64, row);
-              tma_load_2d(sv + a * (TK * 128) + j * blk * 128, &mv, &full[st], a * 64, row);
-            }
+            tma_load_2d(sk + a * (TK * 128), &mk, &full[kv], a * 64, row);
+            tma_load_2d(sv + a * (TK * 128), &mv, &full[kv], a * 64, row);
           }
         }
-        issued = i + 1;
-      }
-      // after an abort, let this producer's copies land before the CTA leaves (bounded)
-      if (*abort_flag) {
-        for (int i = max(0, issued - 2); i < issued; ++i) {
-          const unsigned long long t0 = clock64();
-          while (!mbar_try_wait(&full[i & 1], (i >> 1) & 1) && clock64() - t0 < WAIT_BUDGET) {
+      } else {
+        const bool has = id != -2;                           // block holds keys of this split
+        const bool in_pool = has && id >= 0 && id < p.nblocks;  // out-of-pool ids read as zero keys and values
+        const unsigned load_mask = __ballot_sync(0xffffffffu, in_pool);
+        const unsigned zero_mask = __ballot_sync(0xffffffffu, has && !in_pool);
+        if (lane == 0) {
+          uint32_t m[4] = {0u, 0u, 0u, 0u}, z[4] = {0u, 0u, 0u, 0u};
+          for (int r = 0; r < nvalid; ++r) {
+            m[r >> 5] |= 1u << (r & 31);
+            if ((zero_mask >> (r / blk)) & 1u) z[r >> 5] |= 1u << (r & 31);
           }
+          for (int w = 0; w < 4; ++w) {
+            mask[kv * 8 + w] = m[w];
+            mask[kv * 8 + 4 + w] = z[w];
+          }
+          mbar_expect_tx(&full[kv], (uint32_t)__popc(load_mask) * 2u * blk * HD * 2u);
+        }
+        __syncwarp();
+        if (in_pool) {
+          const int row = (id * p.Hk + kh) * blk;
+          for (int a = 0; a < HD / 64; ++a) {
+            tma_load_2d(sk + a * (TK * 128) + lane * blk * 128, &mk, &full[kv], a * 64, row);
+            tma_load_2d(sv + a * (TK * 128) + lane * blk * 128, &mv, &full[kv], a * 64, row);
+          }
+        }
+      }
+      issued = i + 1;
+    }
+    // after an abort, let this producer's copies land before the CTA leaves (bounded)
+    if (lane == 0 && *abort_flag) {
+      for (int i = max(0, issued - STAGES); i < issued; ++i) {
+        const unsigned long long t0 = clock64();
+        while (!mbar_try_wait(&full[i % STAGES], (i / STAGES) & 1) && clock64() - t0 < WAIT_BUDGET) {
         }
       }
     }
@@ -286,34 +299,37 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       uint64_t* last_bar = nullptr;  // barrier of the latest commit: its completion covers every MMA issued
       uint32_t last_par = 0;
       auto issue_s = [&](int i) {
-        const int st = i & 1;
-        const uint32_t ph = (i >> 1) & 1;
-        if (!mbar_wait(&full[st], ph, abort_flag, 2) || !mbar_wait(&s_empty[st], ph ^ 1, abort_flag, 3)) return false;
+        const int kv = i % STAGES, sb = i & 1;
+        const uint32_t sph = (i >> 1) & 1;
+        if (!mbar_wait(&full[kv], (i / STAGES) & 1, abort_flag, 2) ||
+            !mbar_wait(&s_empty[sb], sph ^ 1, abort_flag, 3))
+          return false;
         fence_after();
-        const uint32_t ka = sbase + st * STAGE_BYTES, qa = sbase + Q_OFF;
+        const uint32_t ka = sbase + kv * STAGE_BYTES, qa = sbase + Q_OFF;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk)
-          mma_ss(tmem + S_COL + st * NH, desc(ka + (kk >> 2) * (TK * 128) + (kk & 3) * 32, 16, 1024),
+          mma_ss(tmem + S_COL + sb * NH, desc(ka + (kk >> 2) * (TK * 128) + (kk & 3) * 32, 16, 1024),
                  desc(qa + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), id_s, kk > 0 ? 1u : 0u);
-        commit(&s_full[st]);
-        last_bar = &s_full[st];
-        last_par = ph;
+        commit(&s_full[sb]);
+        last_bar = &s_full[sb];
+        last_par = sph;
         return true;
       };
       auto issue_pv = [&](int i) {
-        const int st = i & 1;
-        const uint32_t ph = (i >> 1) & 1;
-        if (!mbar_wait(&p_full[st], ph, abort_flag, 4) || !mbar_wait(&o_empty[st], ph ^ 1, abort_flag, 5)) return false;
+        const int kv = i % STAGES, sb = i & 1;
+        const uint32_t sph = (i >> 1) & 1;
+        if (!mbar_wait(&p_full[sb], sph, abort_flag, 4) || !mbar_wait(&o_empty[sb], sph ^ 1, abort_flag, 5))
+          return false;
         fence_after();
-        const uint32_t va = sbase + st * STAGE_BYTES + KV_BYTES, pa = sbase + P_OFF + st * 4096;
+        const uint32_t va = sbase + kv * STAGE_BYTES + KV_BYTES, pa = sbase + P_OFF + sb * 4096;
 #pragma unroll
         for (int kk = 0; kk < TK / 16; ++kk)
-          mma_ss(tmem + O_COL + st * NH, desc(va + kk * 2048, TK * 128, 1024),
+          mma_ss(tmem + O_COL + sb * NH, desc(va + kk * 2048, TK * 128, 1024),
                  desc(pa + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), id_o, kk > 0 ? 1u : 0u);
-        commit(&o_full[st]);
-        commit(&kv_empty[st]);
-        last_bar = &kv_empty[st];
-        last_par = ph;
+        commit(&o_full[sb]);
+        commit(&kv_empty[kv]);
+        last_bar = &kv_empty[kv];
+        last_par = (i / STAGES) & 1;
         return true;
       };
       if (ntiles > 0) ok = issue_s(0);
@@ -355,20 +371,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     };
     bool ok = true;
     for (int i = 0; i < ntiles && ok; ++i) {
-      const int st = i & 1;
-      const uint32_t ph = (i >> 1) & 1;
-      ok = mbar_wait(&full[st], ph, abort_flag, 7) && mbar_wait(&s_full[st], ph, abort_flag, 8);
+      const int kv = i % STAGES, sb = i & 1;
+      ok = mbar_wait(&full[kv], (i / STAGES) & 1, abort_flag, 7) && mbar_wait(&s_full[sb], (i >> 1) & 1, abort_flag, 8);
       if (!all_compute(ok)) {
         ok = false;
         break;
       }
       fence_after();
       uint32_t r[16];
-      ld16(trow + S_COL + st * NH, r);
+      ld16(trow + S_COL + sb * NH, r);
       fence_before();
-      mbar_arrive(&s_empty[st]);
-      const bool valid = (mask[st * 8 + (tid >> 5)] >> (tid & 31)) & 1u;
-      const bool zero = (mask[st * 8 + 4 + (tid >> 5)] >> (tid & 31)) & 1u;
+      mbar_arrive(&s_empty[sb]);
+      const bool valid = (mask[kv * 8 + (tid >> 5)] >> (tid & 31)) & 1u;
+      const bool zero = (mask[kv * 8 + 4 + (tid >> 5)] >> (tid & 31)) & 1u;
       float s[REP];
 #pragma unroll
       for (int h = 0; h < REP; ++h) {
@@ -376,15 +391,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         float v = s[h];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-        if (lane == 0) red[(st * 4 + warp) * NH + h] = v;
+        if (lane == 0) red[(sb * 4 + warp) * NH + h] = v;
       }
       compute_sync();
-      __nv_bfloat16* pt = reinterpret_cast<__nv_bfloat16*>(sm + P_OFF + st * 4096);
+      __nv_bfloat16* pt = reinterpret_cast<__nv_bfloat16*>(sm + P_OFF + sb * 4096);
       const int kc = (tid & 63) >> 3, ke = tid & 7, katom = tid >> 6;
       float alpha_cur[REP];
 #pragma unroll
       for (int h = 0; h < REP; ++h) {
-        const float* rr = red + st * 4 * NH + h;
+        const float* rr = red + sb * 4 * NH + h;
         const float tmax = fmaxf(fmaxf(rr[0], rr[NH]), fmaxf(rr[2 * NH], rr[3 * NH]));
         const float mn = fmaxf(m[h], tmax);
         alpha_cur[h] = mn == -INFINITY ? 1.f : ex2(m[h] - mn);
@@ -394,14 +409,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         pt[(katom * 2048 + h * 128 + ((kc ^ (h & 7)) << 4)) / 2 + ke] = __float2bfloat16_rn(pv);
       }
       if (!valid || zero) {  // rows past the range or of out-of-pool blocks: zero V (0 * garbage stays 0)
-        uint4* vrow = reinterpret_cast<uint4*>(sm + st * STAGE_BYTES + KV_BYTES + tid * 128);
+        uint4* vrow = reinterpret_cast<uint4*>(sm + kv * STAGE_BYTES + KV_BYTES + tid * 128);
 #pragma unroll
         for (int a = 0; a < HD / 64; ++a)
 #pragma unroll
           for (int c = 0; c < 8; ++c) vrow[a * (TK * 128 / 16) + c] = make_uint4(0, 0, 0, 0);
       }
       fence_async_smem();
-      mbar_arrive(&p_full[st]);
+      mbar_arrive(&p_full[sb]);
       if (i > 0 && !fold_o(i - 1)) {
         ok = false;
         break;

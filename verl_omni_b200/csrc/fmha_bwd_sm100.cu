@@ -1158,6 +1158,346 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 }  // namespace v3
 
+// ------------------------------------------------------------------------------------ version 4
+// Version 3 with the gradient math of a block split over two warpgroups (512 threads): warps 4-7 and 8-11
+// each take 32 of the block's 64 query columns for the same 128 key rows (both warpgroups cover the four
+// TMEM lane quadrants), so the exp2 / dS work per block runs on twice the warps; warps 12-15 drain dQ
+// and store dK / dV.  Each warpgroup packs its bf16 P^T / dS^T into the first half of its own 32 fp32
+// columns ([0, 16) and [32, 48)), never into columns the other warpgroup still reads; the dV / dK MMAs
+// take their A operand from those two column ranges.  Shared-memory layout is version 3's.
+namespace v4 {
+using v3::Lay3;
+using v2::ld32_nowait;
+using v2::mma_ts;
+using v2::pack_bf16;
+using v2::st16;
+using v2::wait_ld;
+using v2::wait_st;
+
+constexpr int BQ = 64;
+constexpr int THREADS = 512;
+constexpr int ST = 3;  // Q / dO stages
+
+
+__global__ void __launch_bounds__(THREADS, 1)
+    fmha_bwd4_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+                     const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
+                     const __grid_constant__ CUtensorMap mdo2, const __grid_constant__ CUtensorMap mdq, Params p) {
+  using L = Lay3;
+  constexpr int D = L::D;
+  extern __shared__ __align__(1024) uint8_t raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR_OFF);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qdo_full = bars + 1;           // [ST]
+  uint64_t* qdo_empty = qdo_full + ST;     // [ST]
+  uint64_t* sdp_full = qdo_empty + ST;     // [2] S^T / dP^T of a block computed
+  uint64_t* ds_full = sdp_full + 2;        // [2] P^T / dS^T of a block written (4 gradient warps)
+  uint64_t* ls_full = ds_full + 2;         // [2] the block's lse / Delta staged (TMA warp)
+  uint64_t* dsfree = ls_full + 2;          // [2] the dQ MMA of a pair has read its dS^T slots
+  uint64_t* dq_full = dsfree + 2;          // [2] dQ of a pair computed
+  uint64_t* dq_free = dq_full + 2;         // [2] dQ of a pair drained (4 drain warps)
+  uint64_t* kv_done = dq_free + 2;         // every MMA issued and complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(kv_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float4* lsm = reinterpret_cast<float4*>(sm + L::LS_OFF);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x % p.nkv_tiles;
+  const int bh = blockIdx.x / p.nkv_tiles;
+  const int b = bh / p.H, h = bh % p.H;
+  const int kv0 = kt * 128;
+  const int j0 = p.causal ? kv0 / BQ : 0;  // even: kv0 is a multiple of 128
+  const int nqb = (p.Sq + BQ - 1) / BQ;
+  const int nblk = max(0, nqb - j0);
+  const int npair = (nblk + 1) / 2;
+  const int kvl = p.kv_len ? min(p.Skv, max(0, __ldg(p.kv_len + b))) : p.Skv;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < ST; ++i) {
+      mbar_init(&qdo_full[i], 1);
+      mbar_init(&qdo_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sdp_full[i], 1);
+      mbar_init(&ds_full[i], 8);
+      mbar_init(&ls_full[i], 1);
+      mbar_init(&dsfree[i], 1);
+      mbar_init(&dq_full[i], 1);
+      mbar_init(&dq_free[i], 4);
+    }
+    mbar_init(kv_done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer + lse / Delta staging
+    if (nblk > 0) {
+      if (lane == 0) {
+        mbar_expect_tx(kv_full, 2 * L::KV_TILE);
+        tma3(sm + L::K_OFF, &mk, kv_full, 0, kv0, bh);
+        tma3(sm + L::V_OFF, &mv, kv_full, 0, kv0, bh);
+      }
+      for (int i = 0; i < nblk; ++i) {
+        const int j = j0 + i, st = i % ST;
+        const bool ok1 = mbar_wait(&qdo_empty[st], ((i / ST) & 1) ^ 1, abort_flag, 81);
+        if (!ok1) break;
+        if (lane == 0) {
+          mbar_expect_tx(&qdo_full[st], 2 * L::QB);
+          tma3(sm + L::Q_OFF + st * L::QB, &mq, &qdo_full[st], 0, j * BQ, bh);
+          if (p.split > 0 && j * BQ >= p.split)
+            tma4(sm + L::DO_OFF + st * L::QB, &mdo2, &qdo_full[st], 0, h, j * BQ - p.split, b);
+          else
+            tma4(sm + L::DO_OFF + st * L::QB, &mdo, &qdo_full[st], 0, h, j * BQ, b);
+        }
+        // slot i & 1 was last read by the gradient warps for block i - 2
+        if (i >= 2 && !mbar_wait(&ds_full[i & 1], ((i >> 1) & 1) ^ 1, abort_flag, 82)) break;
+        const int q = j * BQ + 2 * lane;
+        float4 v;
+        v.x = q < p.Sq ? -p.lse[(int64_t)bh * p.Sq + q] * 1.4426950408889634f : -INFINITY;
+        v.y = q + 1 < p.Sq ? -p.lse[(int64_t)bh * p.Sq + q + 1] * 1.4426950408889634f : -INFINITY;
+        v.z = q < p.Sq ? p.delta[(int64_t)bh * p.Sq + q] : 0.f;
+        v.w = q + 1 < p.Sq ? p.delta[(int64_t)bh * p.Sq + q + 1] : 0.f;
+        lsm[(i & 1) * 32 + lane] = v;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ls_full[i & 1]);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0 && nblk > 0) {
+      const uint32_t id_kq = idesc(128, BQ, 0, 0);  // S^T = K Q^T, dP^T = V dO^T  (M keys, N queries)
+      const uint32_t id_kn = idesc(128, D, 0, 1);   // dV += P^T dO, dK += dS^T Q (A from tensor memory)
+      const uint32_t id_nn = idesc(128, D, 1, 1);   // dQ = dS K (A = dS^T in SMEM read MN-major)
+      const uint32_t ka = smem_u32(sm + L::K_OFF), va = smem_u32(sm + L::V_OFF);
+      auto issue_sdp = [&](int i) {
+        const uint32_t qa = smem_u32(sm + L::Q_OFF + (i % ST) * L::QB);
+        const uint32_t oa = smem_u32(sm + L::DO_OFF + (i % ST) * L::QB);
+        const uint32_t cs = tmem + L::C_S + 64 * (i & 1), cdp = tmem + L::C_DP + 64 * (i & 1);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) mma(cs, desc(ka + kk * 32, 16, 1024), desc(qa + kk * 32, 16, 1024), id_kq, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) mma(cdp, desc(va + kk * 32, 16, 1024), desc(oa + kk * 32, 16, 1024), id_kq, kk > 0);
+        commit(&sdp_full[i & 1]);
+      };
+      bool ok = mbar_wait(kv_full, 0, abort_flag, 83);
+      for (int i = 0; ok && i < 2 && i < nblk; ++i) {
+        if (!(ok = mbar_wait(&qdo_full[i % ST], (i / ST) & 1, abort_flag, 84))) break;
+        fence_after();
+        issue_sdp(i);
+      }
+      for (int i = 0; ok && i < nblk; ++i) {
+        const int st = i % ST;
+        if (!mbar_wait(&ds_full[i & 1], (i >> 1) & 1, abort_flag, 85)) break;
+        fence_after();
+        const uint32_t qa = smem_u32(sm + L::Q_OFF + st * L::QB);
+        const uint32_t oa = smem_u32(sm + L::DO_OFF + st * L::QB);
+        const uint32_t cs = tmem + L::C_S + 64 * (i & 1), cdp = tmem + L::C_DP + 64 * (i & 1);
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk)  // dV += P^T dO over the block's 64 queries (8 packed columns / step)
+          mma_ts(tmem + L::C_DV, cs + kk * 8 + (kk >> 1) * 16, desc(oa + kk * 2048, 8192, 1024), id_kn,
+                 (i > 0 || kk > 0));
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk)  // dK += dS^T Q
+          mma_ts(tmem + L::C_DK, cdp + kk * 8 + (kk >> 1) * 16, desc(qa + kk * 2048, 8192, 1024), id_kn,
+                 (i > 0 || kk > 0));
+        commit(&qdo_empty[st]);
+        if ((i & 1) || i + 1 == nblk) {  // dQ of the pair (blocks 2q, 2q + 1) over the 128 keys
+          const int q = i >> 1, c = q & 1;
+          if (q >= 2 && !mbar_wait(&dq_free[c], ((q >> 1) & 1) ^ 1, abort_flag, 86)) break;
+          fence_after();
+          const uint32_t da = smem_u32(sm + L::DS_OFF + c * 32768);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma(tmem + L::C_DQ + 64 * c, desc(da + kk * 2048, 16384, 1024), desc(ka + kk * 2048, 8192, 1024), id_nn,
+                kk > 0);
+          commit(&dq_full[c]);
+          commit(&dsfree[c]);
+        }
+        if (i + 2 < nblk) {
+          if (!mbar_wait(&qdo_full[(i + 2) % ST], ((i + 2) / ST) & 1, abort_flag, 87)) break;
+          fence_after();
+          issue_sdp(i + 2);
+        }
+      }
+      if (ok) commit(kv_done);
+    }
+  } else if (warp >= 4 && warp < 12) {
+    // ---------------------------------------------------------------- gradient warps: one key row per thread,
+    // warps 4-7 take query columns [0, 32) of each block and warps 8-11 columns [32, 64)
+    const int hf = (warp - 4) >> 2;
+    const int lane_base = 32 * (warp & 3);
+    const int r = lane_base + lane;
+    const int kv = kv0 + r;
+    const uint32_t lane_off = (uint32_t)lane_base << 16;
+    const float sl2 = p.scale_log2;
+    bool ok = nblk > 0;
+    for (int i = 0; ok && i < nblk; ++i) {
+      const int j = j0 + i;
+      const int q0 = j * BQ;
+      const int q = i >> 1, c = q & 1;
+      // the pair's dS^T slots were last read by the dQ MMA of pair q - 2
+      if (!(i & 1) && q >= 2 && !mbar_wait(&dsfree[c], ((q >> 1) & 1) ^ 1, abort_flag, 88)) {
+        ok = false;
+        break;
+      }
+      if (!mbar_wait(&ls_full[i & 1], (i >> 1) & 1, abort_flag, 89) ||
+          !mbar_wait(&sdp_full[i & 1], (i >> 1) & 1, abort_flag, 90)) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      // visible query columns of this key row within the block: [qlo, qhi)
+      int qhi = kv < kvl ? min(BQ, p.Sq - q0) : 0;
+      int qlo = p.causal ? max(0, kv - q0) : 0;
+      qhi = max(qhi, 0);
+      if (qlo > qhi) qlo = qhi;
+      const bool full = qlo == 0 && qhi == BQ;
+      const uint32_t S_t = tmem + L::C_S + 64 * (i & 1) + lane_off;
+      const uint32_t DP_t = tmem + L::C_DP + 64 * (i & 1) + lane_off;
+      const float4* ls = lsm + (i & 1) * 32;
+      uint8_t* ds = sm + L::DS_OFF + c * 32768 + (i & 1) * 16384;
+      {  // this warpgroup's 32 query columns
+        uint32_t sa[32], pa[32];
+        ld32_nowait(S_t + hf * 32, sa);
+        ld32_nowait(DP_t + hf * 32, pa);
+        wait_ld();
+        uint32_t wp[16], wd[16];
+#pragma unroll
+        for (int jj = 0; jj < 32; jj += 2) {
+          const int qc = hf * 32 + jj;
+          const float4 l4 = ls[qc >> 1];  // broadcast
+          float x0, x1;
+          v2::ffma2p(__uint_as_float(sa[jj]), __uint_as_float(sa[jj + 1]), sl2, l4.x, l4.y, x0, x1);
+          float e0 = ex2(x0), e1 = ex2(x1);
+          if (!full) {
+            if (qc < qlo || qc >= qhi) e0 = 0.f;
+            if (qc + 1 < qlo || qc + 1 >= qhi) e1 = 0.f;
+          }
+          float d0, d1;
+          v2::sub_mul2(__uint_as_float(pa[jj]), __uint_as_float(pa[jj + 1]), l4.z, l4.w, e0, e1, d0, d1);
+          wp[jj >> 1] = pack_bf16(e0, e1);
+          wd[jj >> 1] = pack_bf16(d0, d1);
+        }
+        // packed bf16 P^T / dS^T into columns [16 hf, 16 hf + 16) of this block's buffers (already read)
+        st16(S_t + hf * 32, wp);
+        st16(DP_t + hf * 32, wd);
+        // dS^T row r, query columns [32 hf, 32 hf + 32) of the block -> swizzled slot for the dQ MMA
+#pragma unroll
+        for (int u4 = 0; u4 < 4; ++u4) {
+          const int unit = hf * 4 + u4;
+          *reinterpret_cast<uint4*>(ds + r * 128 + ((unit ^ (r & 7)) << 4)) =
+              make_uint4(wd[4 * u4], wd[4 * u4 + 1], wd[4 * u4 + 2], wd[4 * u4 + 3]);
+        }
+      }
+      wait_st();
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ds_full[i & 1]);
+    }
+  } else if (warp >= 12) {
+    // ---------------------------------------------------------------- dQ drain, then the dK / dV store
+    const int lane_base = 32 * (warp & 3);
+    const int r = lane_base + lane;
+    const uint32_t lane_off = (uint32_t)lane_base << 16;
+    uint8_t* stage = sm + L::DQST_OFF + (warp - 12) * 8192;
+    int nchunk = 0;
+    bool ok = nblk > 0;
+    for (int q = 0; ok && q < npair; ++q) {
+      const int c = q & 1;
+      if (!mbar_wait(&dq_full[c], (q >> 1) & 1, abort_flag, 91)) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      const int qrow0 = (j0 + 2 * q) * BQ;  // first query row of the pair
+#pragma unroll
+      for (int cc = 0; cc < D / 32; ++cc) {
+        uint32_t v[32];
+        ld32_nowait(tmem + L::C_DQ + 64 * c + lane_off + cc * 32, v);
+        wait_ld();
+        uint8_t* buf = stage + (nchunk & 1) * 4096;
+        ++nchunk;
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+        __syncwarp();
+        uint8_t* rowp = buf + lane * 128;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<float4*>(rowp + 16 * (u ^ (lane & 7))) =
+              make_float4(__uint_as_float(v[4 * u]), __uint_as_float(v[4 * u + 1]), __uint_as_float(v[4 * u + 2]),
+                          __uint_as_float(v[4 * u + 3]));
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          // rows past Sq (the unused half of an odd last pair) are clipped by the tensor map
+          asm volatile(
+              "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(&mdq),
+              "r"(smem_u32(buf)), "r"(cc * 32), "r"(qrow0 + lane_base), "r"(bh)
+              : "memory");
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&dq_free[c]);
+    }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
+    const int kv = kv0 + r;
+    if (ok && nblk > 0 && mbar_wait(kv_done, 0, abort_flag, 92)) {
+      fence_after();
+#pragma unroll
+      for (int cc = 0; cc < D / 32; ++cc) {
+        float vv[32], kk[32];
+        ld32(tmem + L::C_DV + lane_off + cc * 32, vv);
+        ld32(tmem + L::C_DK + lane_off + cc * 32, kk);
+        if (kv < p.Skv) {
+          __nv_bfloat16* dvp = p.dv + ((int64_t)bh * p.Skv + kv) * D + cc * 32;
+          __nv_bfloat16* dkp = p.dk + ((int64_t)bh * p.Skv + kv) * D + cc * 32;
+#pragma unroll
+          for (int jj = 0; jj < 32; jj += 8) {
+            uint4 a, bq;
+            a.x = pack_bf16(vv[jj], vv[jj + 1]);
+            a.y = pack_bf16(vv[jj + 2], vv[jj + 3]);
+            a.z = pack_bf16(vv[jj + 4], vv[jj + 5]);
+            a.w = pack_bf16(vv[jj + 6], vv[jj + 7]);
+            bq.x = pack_bf16(kk[jj] * p.scale, kk[jj + 1] * p.scale);
+            bq.y = pack_bf16(kk[jj + 2] * p.scale, kk[jj + 3] * p.scale);
+            bq.z = pack_bf16(kk[jj + 4] * p.scale, kk[jj + 5] * p.scale);
+            bq.w = pack_bf16(kk[jj + 6] * p.scale, kk[jj + 7] * p.scale);
+            *reinterpret_cast<uint4*>(dvp + jj) = a;
+            *reinterpret_cast<uint4*>(dkp + jj) = bq;
+          }
+        }
+      }
+    } else if (nblk == 0 && kv < p.Skv) {  // causal key tile past every query: zero gradients
+      for (int jj = 0; jj < D; ++jj) {
+        p.dv[((int64_t)bh * p.Skv + kv) * D + jj] = __float2bfloat16_rn(0.f);
+        p.dk[((int64_t)bh * p.Skv + kv) * D + jj] = __float2bfloat16_rn(0.f);
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+  }
+}
+}  // namespace v4
+
 // Delta[bh, q] = sum_d dO[b, q, h, d] * O[b, q, h, d]
 template <int D>
 __global__ void delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dO,
@@ -1297,6 +1637,20 @@ static int launch3(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
   return (int)cudaGetLastError();
 }
 
+static int launch4(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
+                   const CUtensorMap& mdo2, const CUtensorMap& mdq, Params p, int grid, cudaStream_t st) {
+  using L = v3::Lay3;
+  static bool set = false;
+  if (!set) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(v4::fmha_bwd4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES + 1024);
+    if (e != cudaSuccess) return (int)e;
+    set = true;
+  }
+  v4::fmha_bwd4_kernel<<<grid, v4::THREADS, L::BYTES + 1024, st>>>(mq, mk, mv, mdo, mdo2, mdq, p);
+  return (int)cudaGetLastError();
+}
+
 }  // namespace vo_fbwd
 
 // q [B,H,Sq,D], k/v [B,H,Skv,D], o/do [B,Sq,H,D], lse [B,H,Sq]; outputs dq [B,H,Sq,D], dk/dv [B,H,Skv,D].
@@ -1319,9 +1673,9 @@ extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const vo
     delta_kernel<128><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
         (const __nv_bfloat16*)o, (const __nv_bfloat16*)dO, (const __nv_bfloat16*)o2, (const __nv_bfloat16*)dO2, split,
         delta, B, Sq, H);
-  // version 3 (head_dim 64): 64-query blocks; other head widths run version 2
-  if (version == 3 && D != 64) version = 2;
-  const int qrows = version == 3 ? 64 : 128;
+  // versions 3 and 4 (head_dim 64): 64-query blocks; other head widths run version 2
+  if ((version == 3 || version == 4) && D != 64) version = 2;
+  const int qrows = (version == 3 || version == 4) ? 64 : 128;
   CUtensorMap mq, mk, mv, mdo;
   int r = map3(&mq, q, B * H, Sq, D, qrows);
   if (!r) r = map3(&mk, k, B * H, Skv, D);
@@ -1347,10 +1701,11 @@ extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const vo
   p.dv = (__nv_bfloat16*)dv;
   p.split = split;
   const int grid = p.nkv_tiles * B * H;
-  if (version == 3) {
+  if (version == 3 || version == 4) {
     CUtensorMap mdq;
     if ((r = map3_f32(&mdq, dq_acc, B * H, Sq, D))) return r;
-    r = launch3(mq, mk, mv, mdo, mdo2, mdq, p, grid, stream);
+    r = version == 4 ? launch4(mq, mk, mv, mdo, mdo2, mdq, p, grid, stream)
+                     : launch3(mq, mk, mv, mdo, mdo2, mdq, p, grid, stream);
   } else if (version == 2) {
     CUtensorMap mdq;
     if ((r = map3_f32(&mdq, dq_acc, B * H, Sq, D))) return r;
