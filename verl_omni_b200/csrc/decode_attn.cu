@@ -42,7 +42,10 @@ __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_g
 // N consecutive bf16 values (N in {1, 2, 4, 8}, N-element aligned) -> fp32
 template <int N>
 __device__ __forceinline__ void load_row(const __nv_bfloat16* p, float* f) {
-  if constexpr (N == 8) {
+  if constexpr (N == 16) {
+    unpack8(*reinterpret_cast<const bf16x8*>(p), f);
+    unpack8(*reinterpret_cast<const bf16x8*>(p + 8), f + 8);
+  } else if constexpr (N == 8) {
     unpack8(*reinterpret_cast<const bf16x8*>(p), f);
   } else if constexpr (N == 4) {
     const uint2 u = *reinterpret_cast<const uint2*>(p);
@@ -307,8 +310,12 @@ static bool decode_tc(const torch::Tensor& q, const torch::Tensor& kc, const tor
   if (pt.table && (pt.block % 8 || 128 % pt.block)) return false;
   const int Lmax = pt.table ? 0 : (int)kc.size(2);
   const int64_t span = pt.table ? (int64_t)pt.stride * pt.block : Lmax;
-  // one CTA per SM (two 64 KB K / V stages): about two CTAs per SM, at least four 128-key tiles each
-  const int sp = splits > 0 ? (int)splits : pick_splits((int64_t)B * Hk, span, 2, 512, 64);
+  // one CTA per SM (three 64 KB K / V stages): split the keys only while every CTA still gets an SM in the
+  // first wave (a second partial wave costs more than the longer key range), >= four 128-key tiles each
+  const int64_t pairs = (int64_t)B * Hk;
+  const int sp = splits > 0 ? (int)splits
+                            : (int)std::max<int64_t>(1, std::min<int64_t>({num_sms() / std::max<int64_t>(pairs, 1), 64,
+                                                                           std::max<int64_t>(1, span / 512)}));
   auto fo = q.options().dtype(torch::kFloat32);
   torch::Tensor po, pml;
   if (sp > 1) {
@@ -343,7 +350,7 @@ int64_t decode_tc_error(bool reset) { return vo_decode_tc_error(reset ? 1 : 0); 
 // max_blocks x block; longer lengths are clamped to the cache, table ids outside the pool read as zeros).
 // Returns o [B, Hq, HD].  Hq = Hk x rep with rep in {1, 2, 4, 8} (16 as well at HD 128); HD in {64, 128}.
 // splits <= 0 picks the key split count for the kernel that runs.  head_dim 128 runs the tcgen05 kernel
-// (paged blocks of a multiple of 8 rows dividing 128); the rest the CUDA-core kernel above.
+// (contiguous caches and paged blocks of 64 or 128 rows); the rest the CUDA-core kernel above.
 torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor lens,
                                double scale, int64_t splits, c10::optional<torch::Tensor> block_table) {
   VO_CHECK_INPUT(q);
@@ -379,9 +386,10 @@ torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Te
   const int sp = splits > 0 ? (int)splits : pick_splits(B * Hk, span, 16, 256, 16);
 #define VO_DEC(HDV, REPV) \
   if (HD == HDV && rep == REPV) return launch_decode<HDV, REPV>(q, k_cache, v_cache, lens, sl2, sp, pt, out), out;
-  VO_DEC(128, 8) VO_DEC(128, 4) VO_DEC(128, 2) VO_DEC(128, 1) VO_DEC(64, 8) VO_DEC(64, 4) VO_DEC(64, 2) VO_DEC(64, 1)
+  VO_DEC(128, 16) VO_DEC(128, 8) VO_DEC(128, 4) VO_DEC(128, 2) VO_DEC(128, 1) VO_DEC(64, 8) VO_DEC(64, 4) VO_DEC(64, 2)
+  VO_DEC(64, 1)
 #undef VO_DEC
-  TORCH_CHECK(false, "decode attention: head_dim 64 / 128 and 1, 2, 4 or 8 query heads per KV head");
+  TORCH_CHECK(false, "decode attention: head_dim 64 / 128 and 1, 2, 4 or 8 query heads per KV head (16 at 128)");
   return out;
 }
 

@@ -258,14 +258,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const unsigned load_mask = __ballot_sync(0xffffffffu, in_pool);
         const unsigned zero_mask = __ballot_sync(0xffffffffu, has && !in_pool);
         if (lane == 0) {
-          uint32_t m[4] = {0u, 0u, 0u, 0u}, z[4] = {0u, 0u, 0u, 0u};
-          for (int r = 0; r < nvalid; ++r) {
-            m[r >> 5] |= 1u << (r & 31);
-            if ((zero_mask >> (r / blk)) & 1u) z[r >> 5] |= 1u << (r & 31);
-          }
+          // row bitmaps in closed form: valid = the first nvalid rows, zero = rows of out-of-pool blocks
+          const uint32_t bmask = blk >= 32 ? 0xffffffffu : (1u << blk) - 1u;
           for (int w = 0; w < 4; ++w) {
-            mask[kv * 8 + w] = m[w];
-            mask[kv * 8 + 4 + w] = z[w];
+            const int lo = w * 32;
+            const uint32_t m = nvalid >= lo + 32 ? 0xffffffffu : nvalid <= lo ? 0u : (1u << (nvalid - lo)) - 1u;
+            uint32_t z = 0u;
+            for (int r = lo; r < lo + 32; r += blk < 32 ? blk : 32)
+              if ((zero_mask >> (r / blk)) & 1u) z |= bmask << (r - lo);
+            mask[kv * 8 + w] = m;
+            mask[kv * 8 + 4 + w] = z & m;
           }
           mbar_expect_tx(&full[kv], (uint32_t)__popc(load_mask) * 2u * blk * HD * 2u);
         }

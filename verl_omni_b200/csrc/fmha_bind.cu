@@ -169,14 +169,15 @@ std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Ten
   auto dk = torch::empty_like(k);
   auto dv = torch::empty_like(v);
   auto fo = q.options().dtype(torch::kFloat32);
-  auto delta = torch::empty({B, H, Sq}, fo);
+  // Delta [B, H, Sq], then (16-byte aligned) the per-64-query-block lse / Delta records of version 4
+  auto delta = torch::empty({B * H * Sq + B * H * ((Sq + 63) / 64) * 128 + 4}, fo);
   auto dq_acc = torch::zeros({B, H, Sq, D}, fo);
   int rc = vo_fmha_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dO.data_ptr(), po2, pdo2, (int)split,
                        lse.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), delta.data_ptr<float>(),
                        dq_acc.data_ptr<float>(), B, H, Sq, Skv, D, (float)scale, causal ? 1 : 0, stream(),
                        (int)version, kvp);
   TORCH_CHECK(rc == 0, "tcgen05 FMHA backward launch failed: code ", rc);
-  count_launch(3);
+  count_launch(version == 4 ? 4 : 3);
   return {dq, dk, dv};
 }
 

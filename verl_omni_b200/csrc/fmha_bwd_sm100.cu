@@ -42,12 +42,16 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t n) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
 }
+// a waiting thread is suspended for up to this long (it wakes as soon as the phase completes), so warps
+// that wait -- the drain, producer and issuer warps most of the time -- do not spin on issue slots and ALU
+// cycles the gradient warps need
+constexpr uint32_t kSuspendNs = 200000;
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t par) {
   uint32_t ok;
   asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(b)), "r"(par)
+      : "r"(smem_u32(b)), "r"(par), "r"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
@@ -134,6 +138,7 @@ struct Params {
   __nv_bfloat16* dk;   // [BH, Skv, D]
   __nv_bfloat16* dv;   // [BH, Skv, D]
   int split;           // > 0: dO rows q >= split come from the second dO tensor map (split % 128 == 0)
+  const float4* ls_rec = nullptr;  // version 4: [BH, ceil(Sq / 64), 32] {-lse q log2e, -lse q+1 log2e, Delta q, Delta q+1}
 };
 
 template <int D>
@@ -814,6 +819,27 @@ __global__ void __launch_bounds__(512, 1)
 // Barrier parities: ds_full[b] / sdp_full[b] carry block j at phase j >> 1 of buffer j & 1 (the producer of
 // block j + 2 needs the consumer of block j first, so no barrier runs two phases ahead); dsfree / dq_full /
 // dq_free carry pair q at phase q >> 1 of slot q & 1 under the same argument.
+// version 4's per-block lse / Delta records: pair u of block j of row bh -> {-lse log2e, -lse log2e, Delta, Delta}
+// for queries 64 j + 2u, + 1 (-inf / 0 past Sq)
+__global__ void ls_record_kernel(const float* __restrict__ lse, const float* __restrict__ delta,
+                                 float4* __restrict__ rec, int Sq, int nqb, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int u = (int)(i % 32);
+  const int64_t bj = i / 32;
+  const int j = (int)(bj % nqb);
+  const int64_t bh = bj / nqb;
+  const int q = j * 64 + 2 * u;
+  const float* l = lse + bh * Sq;
+  const float* d = delta + bh * Sq;
+  float4 v;
+  v.x = q < Sq ? -l[q] * 1.4426950408889634f : -INFINITY;
+  v.y = q + 1 < Sq ? -l[q + 1] * 1.4426950408889634f : -INFINITY;
+  v.z = q < Sq ? d[q] : 0.f;
+  v.w = q + 1 < Sq ? d[q + 1] : 0.f;
+  rec[i] = v;
+}
+
 namespace v3 {
 using v2::ld32_nowait;
 using v2::mma_ts;
@@ -856,7 +882,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* qdo_empty = qdo_full + ST;     // [ST]
   uint64_t* sdp_full = qdo_empty + ST;     // [2] S^T / dP^T of a block computed
   uint64_t* ds_full = sdp_full + 2;        // [2] P^T / dS^T of a block written (4 gradient warps)
-  uint64_t* ls_full = ds_full + 2;         // [2] the block's lse / Delta staged (TMA warp)
+  uint64_t* ls_full = ds_full + 2;         // [2] unused here: lse / Delta arrive with Q / dO
   uint64_t* dsfree = ls_full + 2;          // [2] the dQ MMA of a pair has read its dS^T slots
   uint64_t* dq_full = dsfree + 2;          // [2] dQ of a pair computed
   uint64_t* dq_free = dq_full + 2;         // [2] dQ of a pair drained (4 drain warps)
@@ -1167,6 +1193,24 @@ __global__ void __launch_bounds__(THREADS, 1)
 // take their A operand from those two column ranges.  Shared-memory layout is version 3's.
 namespace v4 {
 using v3::Lay3;
+// version 3's layout with one 512-byte lse / Delta record per Q / dO stage
+struct Lay4 {
+  static constexpr int D = 64;
+  static constexpr int KV_TILE = Lay3::KV_TILE, QB = Lay3::QB;
+  static constexpr int K_OFF = Lay3::K_OFF, V_OFF = Lay3::V_OFF, Q_OFF = Lay3::Q_OFF, DO_OFF = Lay3::DO_OFF;
+  static constexpr int DS_OFF = Lay3::DS_OFF, DQST_OFF = Lay3::DQST_OFF, LS_OFF = Lay3::LS_OFF;
+  static constexpr int BAR_OFF = LS_OFF + 3 * 512;
+  static constexpr int BYTES = BAR_OFF + 256;
+  static_assert(BYTES + 1024 <= 232448, "shared memory above the 227 KB per-block limit");
+  static constexpr uint32_t C_S = Lay3::C_S, C_DP = Lay3::C_DP, C_DV = Lay3::C_DV, C_DK = Lay3::C_DK,
+                            C_DQ = Lay3::C_DQ;
+};
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
 using v2::ld32_nowait;
 using v2::mma_ts;
 using v2::pack_bf16;
@@ -1183,7 +1227,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     fmha_bwd4_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                      const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
                      const __grid_constant__ CUtensorMap mdo2, const __grid_constant__ CUtensorMap mdq, Params p) {
-  using L = Lay3;
+  using L = Lay4;
   constexpr int D = L::D;
   extern __shared__ __align__(1024) uint8_t raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
@@ -1193,7 +1237,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* qdo_empty = qdo_full + ST;     // [ST]
   uint64_t* sdp_full = qdo_empty + ST;     // [2] S^T / dP^T of a block computed
   uint64_t* ds_full = sdp_full + 2;        // [2] P^T / dS^T of a block written (4 gradient warps)
-  uint64_t* ls_full = ds_full + 2;         // [2] the block's lse / Delta staged (TMA warp)
+  uint64_t* ls_full = ds_full + 2;         // [2] unused here: lse / Delta arrive with Q / dO
   uint64_t* dsfree = ls_full + 2;          // [2] the dQ MMA of a pair has read its dS^T slots
   uint64_t* dq_full = dsfree + 2;          // [2] dQ of a pair computed
   uint64_t* dq_free = dq_full + 2;         // [2] dQ of a pair drained (4 drain warps)
@@ -1248,29 +1292,21 @@ __global__ void __launch_bounds__(THREADS, 1)
         tma3(sm + L::K_OFF, &mk, kv_full, 0, kv0, bh);
         tma3(sm + L::V_OFF, &mv, kv_full, 0, kv0, bh);
       }
-      for (int i = 0; i < nblk; ++i) {
-        const int j = j0 + i, st = i % ST;
-        const bool ok1 = mbar_wait(&qdo_empty[st], ((i / ST) & 1) ^ 1, abort_flag, 81);
-        if (!ok1) break;
-        if (lane == 0) {
-          mbar_expect_tx(&qdo_full[st], 2 * L::QB);
+      // Q, dO and the block's lse / Delta record arrive on one barrier per stage; the TMA warp never waits
+      // on the gradient warps, so it runs up to three blocks ahead
+      if (lane == 0) {
+        const int nqb_all = (p.Sq + BQ - 1) / BQ;
+        for (int i = 0; i < nblk; ++i) {
+          const int j = j0 + i, st = i % ST;
+          if (!mbar_wait(&qdo_empty[st], ((i / ST) & 1) ^ 1, abort_flag, 81)) break;
+          mbar_expect_tx(&qdo_full[st], 2 * L::QB + 512);
           tma3(sm + L::Q_OFF + st * L::QB, &mq, &qdo_full[st], 0, j * BQ, bh);
           if (p.split > 0 && j * BQ >= p.split)
             tma4(sm + L::DO_OFF + st * L::QB, &mdo2, &qdo_full[st], 0, h, j * BQ - p.split, b);
           else
             tma4(sm + L::DO_OFF + st * L::QB, &mdo, &qdo_full[st], 0, h, j * BQ, b);
+          bulk_load(sm + L::LS_OFF + st * 512, p.ls_rec + ((int64_t)bh * nqb_all + j) * 32, 512, &qdo_full[st]);
         }
-        // slot i & 1 was last read by the gradient warps for block i - 2
-        if (i >= 2 && !mbar_wait(&ds_full[i & 1], ((i >> 1) & 1) ^ 1, abort_flag, 82)) break;
-        const int q = j * BQ + 2 * lane;
-        float4 v;
-        v.x = q < p.Sq ? -p.lse[(int64_t)bh * p.Sq + q] * 1.4426950408889634f : -INFINITY;
-        v.y = q + 1 < p.Sq ? -p.lse[(int64_t)bh * p.Sq + q + 1] * 1.4426950408889634f : -INFINITY;
-        v.z = q < p.Sq ? p.delta[(int64_t)bh * p.Sq + q] : 0.f;
-        v.w = q + 1 < p.Sq ? p.delta[(int64_t)bh * p.Sq + q + 1] : 0.f;
-        lsm[(i & 1) * 32 + lane] = v;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ls_full[i & 1]);
       }
     }
   } else if (warp == 1) {
@@ -1351,7 +1387,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         ok = false;
         break;
       }
-      if (!mbar_wait(&ls_full[i & 1], (i >> 1) & 1, abort_flag, 89) ||
+      if (!mbar_wait(&qdo_full[i % ST], (i / ST) & 1, abort_flag, 89) ||
           !mbar_wait(&sdp_full[i & 1], (i >> 1) & 1, abort_flag, 90)) {
         ok = false;
         break;
@@ -1365,7 +1401,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const bool full = qlo == 0 && qhi == BQ;
       const uint32_t S_t = tmem + L::C_S + 64 * (i & 1) + lane_off;
       const uint32_t DP_t = tmem + L::C_DP + 64 * (i & 1) + lane_off;
-      const float4* ls = lsm + (i & 1) * 32;
+      const float4* ls = lsm + (i % ST) * 32;
       uint8_t* ds = sm + L::DS_OFF + c * 32768 + (i & 1) * 16384;
       {  // this warpgroup's 32 query columns
         uint32_t sa[32], pa[32];
@@ -1639,7 +1675,7 @@ static int launch3(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
 
 static int launch4(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
                    const CUtensorMap& mdo2, const CUtensorMap& mdq, Params p, int grid, cudaStream_t st) {
-  using L = v3::Lay3;
+  using L = v4::Lay4;
   static bool set = false;
   if (!set) {
     const cudaError_t e =
@@ -1701,6 +1737,15 @@ extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const vo
   p.dv = (__nv_bfloat16*)dv;
   p.split = split;
   const int grid = p.nkv_tiles * B * H;
+  if (version == 4) {
+    // records follow Delta in the caller's scratch, rounded up to 16 bytes
+    float4* rec = reinterpret_cast<float4*>((reinterpret_cast<uintptr_t>(delta + (int64_t)B * H * Sq) + 15) &
+                                            ~uintptr_t(15));
+    const int nqb = (Sq + 63) / 64;
+    const int64_t n = (int64_t)B * H * nqb * 32;
+    ls_record_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(lse, delta, rec, Sq, nqb, n);
+    p.ls_rec = rec;
+  }
   if (version == 3 || version == 4) {
     CUtensorMap mdq;
     if ((r = map3_f32(&mdq, dq_acc, B * H, Sq, D))) return r;

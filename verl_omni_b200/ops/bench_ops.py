@@ -460,8 +460,12 @@ def bench_decode(a) -> list[dict]:
     out = []
     for kernel in ("tcgen05", "cuda_core"):  # VO_DECODE_TC=0 selects the CUDA-core kernel
         os.environ["VO_DECODE_TC"] = "1" if kernel == "tcgen05" else "0"
+        kp128 = kc.view(B, Hk, L // 128, 128, hd).permute(0, 2, 1, 3, 4).reshape(B * L // 128, Hk, 128, hd)
+        vp128 = vc.view(B, Hk, L // 128, 128, hd).permute(0, 2, 1, 3, 4).reshape(B * L // 128, Hk, 128, hd)
+        t128 = torch.arange(B * L // 128, device="cuda", dtype=torch.int32).view(B, L // 128)
         for name, fn in (("contiguous", lambda sp: decode_attention(q, kc, vc, lens, splits=sp)),
-                         ("paged16", lambda sp: decode_attention(q, kp, vp, lens, splits=sp, block_table=table))):
+                         ("paged16", lambda sp: decode_attention(q, kp, vp, lens, splits=sp, block_table=table)),
+                         ("paged128", lambda sp: decode_attention(q, kp128, vp128, lens, splits=sp, block_table=t128))):
             if a.only and name not in a.only.split(","):
                 continue
             for sp in ([0] if not a.compare else [0, 1, 2, 4, 8]):  # 0: the default split heuristic
