@@ -179,6 +179,9 @@ def _peer_exchange(rank, world):
     PA.release_all()
 
 
-def test_ulysses_peer_exchange_matches_nccl_sp2():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ulysses_peer_exchange_matches_nccl(world):
     """Sequence <-> head exchanges as one peer-memory kernel each == NCCL all-to-all, forward and backward."""
-    run_ranks(_peer_exchange, 2, device="cuda")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    run_ranks(_peer_exchange, world, device="cuda")
