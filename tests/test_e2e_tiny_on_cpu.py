@@ -147,3 +147,23 @@ def test_on_policy_distillation_teacher(mode):
     m = t.step()
     key = "actor/distill_kl_loss" if mode == "distill_kl" else "actor/distill_fm_mse_loss"
     assert m[key] > 0 and "timing_s/teacher" in m
+
+
+def _veomni(rank, world, outdir):
+    from verl_omni_b200.trainer.diffusion.flow_grpo_trainer import PolicyGradientTrainer
+    from verl_omni_b200.utils.config import load_config
+
+    cfg = load_config("diffusion_trainer", ["diffusion/model_engine=veomni_diffusion"] + OVR + [
+        f"trainer.default_local_dir={outdir}", "trainer.total_training_steps=1", "trainer.resume_mode=disable",
+        "actor_rollout_ref.actor.veomni_config.fsdp_size=2"])
+    assert cfg.model_engine == "veomni_diffusion" and cfg.actor_rollout_ref.actor.strategy == "veomni"
+    t = PolicyGradientTrainer(cfg)
+    eng = t.actor.engine
+    assert eng.world == 2 and eng.n_replicas == 2  # dp_shard 2 x dp_replicate 2
+    t.fit()
+
+
+def test_veomni_engine_selection_world4(tmp_path):
+    """``diffusion/model_engine=veomni_diffusion`` picks the VeOmni actor config; its fsdp_size sets the
+    dp_shard x dp_replicate layout of the sharded engine."""
+    run_ranks(_veomni, world=4, args=(str(tmp_path),))

@@ -22,7 +22,7 @@ import copy
 import os
 import re
 from pathlib import Path
-from typing import Any, Iterable
+from typing import Optional, Any, Iterable
 
 import yaml
 
@@ -126,9 +126,10 @@ def _load_yaml(path: Path) -> dict:
     return data
 
 
-def compose(name: str, root: Path = CONFIG_ROOT) -> Cfg:
-    """Compose the config ``<root>/<name>.yaml`` with its defaults list (recursively)."""
-    return to_cfg(_compose_file(root / f"{name}.yaml", root, selections={}))
+def compose(name: str, root: Path = CONFIG_ROOT, choices: Optional[dict] = None) -> Cfg:
+    """Compose the config ``<root>/<name>.yaml`` with its defaults list (recursively); ``choices`` replaces
+    the option a defaults entry selects for a group (Hydra's ``group=option`` overrides)."""
+    return to_cfg(_compose_file(root / f"{name}.yaml", root, selections={"__choices__": dict(choices or {})}))
 
 
 def _compose_file(path: Path, root: Path, selections: dict) -> dict:
@@ -150,6 +151,7 @@ def _compose_file(path: Path, root: Path, selections: dict) -> dict:
             continue
         val = re.sub(r"\$\{([^}]+)\}", lambda m: str(selections.get(m.group(1), m.group(0))), str(val))
         group, _, target = key.partition("@")
+        val = selections.get("__choices__", {}).get(group, val)
         selections[group] = val
         group_dir = root / group
         sub = _compose_file(group_dir / f"{val}.yaml", root, selections)
@@ -273,7 +275,17 @@ def resolve(cfg: Cfg, max_passes: int = 16) -> Cfg:
 
 
 def load_config(name: str = "diffusion_trainer", overrides: Iterable[str] = (), root: Path = CONFIG_ROOT) -> Cfg:
-    """Compose + override + resolve: the equivalent of ``@hydra.main`` followed by ``OmegaConf.resolve``."""
-    cfg = compose(name, root)
-    apply_overrides(cfg, overrides)
+    """Compose + override + resolve: the equivalent of ``@hydra.main`` followed by ``OmegaConf.resolve``.
+
+    An override whose key names a config group directory (``diffusion/model_engine=veomni_diffusion``)
+    selects that group's option in the defaults lists; every other override sets a value."""
+    choices, rest = {}, []
+    for ov in overrides:
+        key, sep, val = ov.strip().partition("=")
+        if sep and "/" in key and "." not in key and (root / key).is_dir():
+            choices[key] = val
+        else:
+            rest.append(ov)
+    cfg = compose(name, root, choices)
+    apply_overrides(cfg, rest)
     return resolve(cfg)

@@ -78,6 +78,23 @@ class FSDPEngineConfig(BaseConfig):
 
 
 @dataclass
+class VeOmniEngineConfig(BaseConfig):
+    """The VeOmni engine's layout knobs (reference ``VeOmniDiffusionEngineConfig``,
+    ``trainer/config/diffusion/engine/diffusion_veomni.yaml``), read by the sharded engine when
+    ``strategy == "veomni"``: ``fsdp_size`` ranks per dp_shard group, replicated across the rest."""
+
+    fsdp_size: int = -1
+    ulysses_parallel_size: int = 1
+    expert_parallel_size: int = 1
+    init_device: str = "cuda"
+    reshard_after_forward: bool = False
+    model_dtype: str = "bfloat16"
+    mixed_precision: bool = True
+    mixed_precision_param_dtype: str = "bfloat16"
+    mixed_precision_reduce_dtype: str = "float32"
+
+
+@dataclass
 class CheckpointConfig(BaseConfig):
     save_contents: list = field(default_factory=lambda: ["model", "optimizer", "extra"])
     load_contents: list = field(default_factory=lambda: ["model", "optimizer", "extra"])
@@ -104,10 +121,13 @@ class DiffusionActorConfig(BaseConfig):
     checkpoint: CheckpointConfig = field(default_factory=CheckpointConfig)
     optim: OptimConfig = field(default_factory=OptimConfig)
     fsdp_config: FSDPEngineConfig = field(default_factory=FSDPEngineConfig)
+    veomni_config: VeOmniEngineConfig = field(default_factory=VeOmniEngineConfig)
     rollout_correction: RolloutCorrectionConfig = field(default_factory=RolloutCorrectionConfig)
     global_batch_info: dict = field(default_factory=dict)
 
     def __post_init__(self):
+        if self.strategy not in ("fsdp", "fsdp2", "veomni", "b200"):
+            raise ValueError(f"Unknown actor strategy: {self.strategy!r}")
         if self.distill_loss_mode not in ("distill_kl", "distill_fm_mse"):
             raise ValueError(f"Invalid distill_loss_mode: {self.distill_loss_mode}")
         if self.ppo_epochs < 1:

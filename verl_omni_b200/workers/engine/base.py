@@ -205,6 +205,11 @@ class ShardedEngine:
         self.replica_group = None
         self.n_replicas = 1
         fs = int(getattr(actor_cfg.fsdp_config, "fsdp_size", -1) or -1)
+        vc = getattr(actor_cfg, "veomni_config", None) if getattr(actor_cfg, "strategy", "") == "veomni" else None
+        if vc is not None and fs <= 0:
+            # VeOmni layout (reference workers/engine/veomni/diffusion_impl.py:97-132): dp_shard groups of
+            # veomni_config.fsdp_size ranks, replicated across dp_replicate = world / fsdp_size
+            fs = int(getattr(vc, "fsdp_size", -1) or -1)
         if group is None and 0 < fs < D.world_size() and trainable:
             # HSDP: shard within groups of fsdp_size consecutive ranks (one node), replicate across them
             self.group, self.replica_group = D.make_hsdp_groups(fs)

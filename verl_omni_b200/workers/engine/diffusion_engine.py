@@ -63,7 +63,7 @@ def _mean_metrics(ms: list[dict]) -> dict:
     return out
 
 
-@register_engine("diffusion_model", ("fsdp", "fsdp2", "b200"))
+@register_engine("diffusion_model", ("fsdp", "fsdp2", "veomni", "b200"))
 class PPODiffusionEngine:
     """Actor (or frozen ref) DiT with the PPO-style per-timestep training loop."""
 
