@@ -177,7 +177,7 @@ std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Ten
                        dq_acc.data_ptr<float>(), B, H, Sq, Skv, D, (float)scale, causal ? 1 : 0, stream(),
                        (int)version, kvp);
   TORCH_CHECK(rc == 0, "tcgen05 FMHA backward launch failed: code ", rc);
-  count_launch(version == 4 ? 4 : 3);
+  count_launch(version == 4 || version == 5 ? 4 : 3);
   return {dq, dk, dv};
 }
 

@@ -1193,13 +1193,17 @@ __global__ void __launch_bounds__(THREADS, 1)
 // take their A operand from those two column ranges.  Shared-memory layout is version 3's.
 namespace v4 {
 using v3::Lay3;
-// version 3's layout with one 512-byte lse / Delta record per Q / dO stage
+// version 3's layout with ST Q / dO stages (three or five) and one 512-byte lse / Delta record per stage
+template <int ST>
 struct Lay4 {
   static constexpr int D = 64;
   static constexpr int KV_TILE = Lay3::KV_TILE, QB = Lay3::QB;
-  static constexpr int K_OFF = Lay3::K_OFF, V_OFF = Lay3::V_OFF, Q_OFF = Lay3::Q_OFF, DO_OFF = Lay3::DO_OFF;
-  static constexpr int DS_OFF = Lay3::DS_OFF, DQST_OFF = Lay3::DQST_OFF, LS_OFF = Lay3::LS_OFF;
-  static constexpr int BAR_OFF = LS_OFF + 3 * 512;
+  static constexpr int K_OFF = 0, V_OFF = KV_TILE, Q_OFF = 2 * KV_TILE;
+  static constexpr int DO_OFF = Q_OFF + ST * QB;
+  static constexpr int DS_OFF = DO_OFF + ST * QB;      // 4 slots of dS^T [128 keys x 64 q] bf16
+  static constexpr int DQST_OFF = DS_OFF + 4 * 16384;  // dQ drain staging: 4 warps x 2 x 4 KB
+  static constexpr int LS_OFF = DQST_OFF + 32768;
+  static constexpr int BAR_OFF = LS_OFF + ST * 512;
   static constexpr int BYTES = BAR_OFF + 256;
   static_assert(BYTES + 1024 <= 232448, "shared memory above the 227 KB per-block limit");
   static constexpr uint32_t C_S = Lay3::C_S, C_DP = Lay3::C_DP, C_DV = Lay3::C_DV, C_DK = Lay3::C_DK,
@@ -1220,14 +1224,14 @@ using v2::wait_st;
 
 constexpr int BQ = 64;
 constexpr int THREADS = 512;
-constexpr int ST = 3;  // Q / dO stages
 
 
+template <int ST>
 __global__ void __launch_bounds__(THREADS, 1)
     fmha_bwd4_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                      const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
                      const __grid_constant__ CUtensorMap mdo2, const __grid_constant__ CUtensorMap mdq, Params p) {
-  using L = Lay4;
+  using L = Lay4<ST>;
   constexpr int D = L::D;
   extern __shared__ __align__(1024) uint8_t raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
@@ -1673,17 +1677,18 @@ static int launch3(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
   return (int)cudaGetLastError();
 }
 
+template <int ST>
 static int launch4(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
                    const CUtensorMap& mdo2, const CUtensorMap& mdq, Params p, int grid, cudaStream_t st) {
-  using L = v4::Lay4;
+  using L = v4::Lay4<ST>;
   static bool set = false;
   if (!set) {
     const cudaError_t e =
-        cudaFuncSetAttribute(v4::fmha_bwd4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES + 1024);
+        cudaFuncSetAttribute(v4::fmha_bwd4_kernel<ST>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES + 1024);
     if (e != cudaSuccess) return (int)e;
     set = true;
   }
-  v4::fmha_bwd4_kernel<<<grid, v4::THREADS, L::BYTES + 1024, st>>>(mq, mk, mv, mdo, mdo2, mdq, p);
+  v4::fmha_bwd4_kernel<ST><<<grid, v4::THREADS, L::BYTES + 1024, st>>>(mq, mk, mv, mdo, mdo2, mdq, p);
   return (int)cudaGetLastError();
 }
 
@@ -1709,9 +1714,10 @@ extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const vo
     delta_kernel<128><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
         (const __nv_bfloat16*)o, (const __nv_bfloat16*)dO, (const __nv_bfloat16*)o2, (const __nv_bfloat16*)dO2, split,
         delta, B, Sq, H);
-  // versions 3 and 4 (head_dim 64): 64-query blocks; other head widths run version 2
-  if ((version == 3 || version == 4) && D != 64) version = 2;
-  const int qrows = (version == 3 || version == 4) ? 64 : 128;
+  // versions 3, 4 and 5 (head_dim 64): 64-query blocks (5 = 4 with a five-deep Q / dO ring); other head
+  // widths run version 2
+  if (version >= 3 && version <= 5 && D != 64) version = 2;
+  const int qrows = (version >= 3 && version <= 5) ? 64 : 128;
   CUtensorMap mq, mk, mv, mdo;
   int r = map3(&mq, q, B * H, Sq, D, qrows);
   if (!r) r = map3(&mk, k, B * H, Skv, D);
@@ -1737,7 +1743,7 @@ extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const vo
   p.dv = (__nv_bfloat16*)dv;
   p.split = split;
   const int grid = p.nkv_tiles * B * H;
-  if (version == 4) {
+  if (version == 4 || version == 5) {
     // records follow Delta in the caller's scratch, rounded up to 16 bytes
     float4* rec = reinterpret_cast<float4*>((reinterpret_cast<uintptr_t>(delta + (int64_t)B * H * Sq) + 15) &
                                             ~uintptr_t(15));
@@ -1746,11 +1752,12 @@ extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const vo
     ls_record_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(lse, delta, rec, Sq, nqb, n);
     p.ls_rec = rec;
   }
-  if (version == 3 || version == 4) {
+  if (version >= 3 && version <= 5) {
     CUtensorMap mdq;
     if ((r = map3_f32(&mdq, dq_acc, B * H, Sq, D))) return r;
-    r = version == 4 ? launch4(mq, mk, mv, mdo, mdo2, mdq, p, grid, stream)
-                     : launch3(mq, mk, mv, mdo, mdo2, mdq, p, grid, stream);
+    r = version == 5   ? launch4<5>(mq, mk, mv, mdo, mdo2, mdq, p, grid, stream)
+        : version == 4 ? launch4<3>(mq, mk, mv, mdo, mdo2, mdq, p, grid, stream)
+                       : launch3(mq, mk, mv, mdo, mdo2, mdq, p, grid, stream);
   } else if (version == 2) {
     CUtensorMap mdq;
     if ((r = map3_f32(&mdq, dq_acc, B * H, Sq, D))) return r;
