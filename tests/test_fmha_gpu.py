@@ -32,7 +32,7 @@ def _ref(q, k, v, causal, scale):
     return o, lse
 
 
-@pytest.mark.parametrize("version", [1, 2, 3, 4, 5])
+@pytest.mark.parametrize("version", [1, 2, 3, 4, 5, 7])
 @pytest.mark.parametrize("B,H,Sq,Skv,D,causal", CASES)
 def test_fmha_fwd(E, B, H, Sq, Skv, D, causal, version):
     torch.manual_seed(0)
@@ -46,7 +46,7 @@ def test_fmha_fwd(E, B, H, Sq, Skv, D, causal, version):
     torch.testing.assert_close(lse, rlse, rtol=1e-3, atol=1e-3)
 
 
-@pytest.mark.parametrize("version", [1, 2, 3, 4, 5])
+@pytest.mark.parametrize("version", [1, 2, 3, 4, 5, 7])
 @pytest.mark.parametrize("D", [64, 128])
 def test_fmha_fwd_growing_max(E, D, version):
     """Later key blocks carry far larger scores: exercises the running-max rescale of O."""
@@ -82,7 +82,7 @@ def test_attention_op_autograd():
         torch.testing.assert_close(a.grad.float(), b.grad, rtol=5e-2, atol=5e-2)
 
 
-@pytest.mark.parametrize("version", [1, 2, 3, 4, 5])
+@pytest.mark.parametrize("version", [1, 2, 3, 4, 5, 7])
 @pytest.mark.parametrize("B,H,Sq,Skv,D,causal", CASES)
 def test_fmha_bwd(E, B, H, Sq, Skv, D, causal, version):
     torch.manual_seed(2)
@@ -101,7 +101,7 @@ def test_fmha_bwd(E, B, H, Sq, Skv, D, causal, version):
         assert rel < 2e-2, rel
 
 
-@pytest.mark.parametrize("fwd,bwd", [(2, 1), (3, 2), (4, 2), (5, 2), (4, 3), (4, 4), (4, 5)])
+@pytest.mark.parametrize("fwd,bwd", [(2, 1), (3, 2), (4, 2), (5, 2), (4, 3), (4, 4), (4, 5), (4, 7)])
 @pytest.mark.parametrize("D", [64, 128])
 def test_attention_split_matches_joint(E, fwd, bwd, D, monkeypatch):
     """Split outputs (image rows / text rows in separate tensors) equal slices of the joint output,

@@ -114,6 +114,7 @@ torch::Tensor peer_grad_reduce(std::vector<int64_t> grad_ptrs, int64_t lo, int64
 void peer_adamw_bcast(std::vector<int64_t> flat_ptrs, int64_t lo, int64_t n, torch::Tensor p, torch::Tensor grad,
                       torch::Tensor m, torch::Tensor v, double lr, double b1, double b2, double eps, double wd,
                       int64_t step, double max_norm, torch::Tensor sq_norm);
+torch::Tensor fmha_bwd_trace();
 std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
                                     torch::Tensor lse, torch::Tensor dO, bool causal, double scale, int64_t version,
                                     c10::optional<torch::Tensor> o2, c10::optional<torch::Tensor> dO2, int64_t split,
@@ -183,6 +184,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fmha_fwd_peer", &vo::fmha_fwd_peer, "Ulysses attention writing each output row to its owner rank",
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("peer_o"), py::arg("peer_o2"), py::arg("sl"), py::arg("si"),
         py::arg("htot"), py::arg("h0"), py::arg("scale"), py::arg("version") = 3);
+  m.def("fmha_bwd_trace", &vo::fmha_bwd_trace, "event stamps of the last traced FMHA backward (version 6)");
   m.def("fmha_bwd", &vo::fmha_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
         py::arg("dO"), py::arg("causal"), py::arg("scale"), py::arg("version") = 1, py::arg("o2") = py::none(),
         py::arg("dO2") = py::none(), py::arg("split") = 0, py::arg("kv_len") = py::none());

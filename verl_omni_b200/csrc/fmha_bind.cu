@@ -30,6 +30,7 @@ extern "C" int vo_fmha_fwd5_peer(const void* q, const void* k, const void* v, vo
 extern "C" int vo_fmha_fwd4v(const void* q, const void* k, const void* v, void* o, void* o2, int out_split, float* lse,
                              const int* kv_len, int B, int H, int Sq, int Skv, int D, float scale, int causal,
                              cudaStream_t stream, int variant);
+extern "C" int vo_fmha_bwd_trace(long long* host);
 extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const void* o, const void* dO,
                            const void* o2, const void* dO2, int split, const float* lse, void* dq, void* dk, void* dv,
                            float* delta, float* dq_acc, int B, int H, int Sq, int Skv, int D, float scale, int causal,
@@ -177,8 +178,20 @@ std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Ten
                        dq_acc.data_ptr<float>(), B, H, Sq, Skv, D, (float)scale, causal ? 1 : 0, stream(),
                        (int)version, kvp);
   TORCH_CHECK(rc == 0, "tcgen05 FMHA backward launch failed: code ", rc);
-  count_launch(version == 4 || version == 5 ? 4 : 3);
+  count_launch(version >= 4 && version <= 8 ? 4 : 3);
   return {dq, dk, dv};
+}
+
+// Event stamps of the last traced backward launch (version 6): int64 [32 CTAs, 64 blocks, 16 slots] of
+// SM clocks (0 = not reached).  Events: 0 Q/dO load issued, 1 MMA sees dS ready, 2 dV/dK/dQ issued,
+// 3 next S/dP inputs ready, 4 gradient block start, 5 dS slots free, 6 S/dP ready, 7 dS written,
+// 8 dQ ready at the drain, 9 dQ drained, 10 scores loaded from tensor memory, 11 exp / dS math done,
+// 12 tensor-memory and shared stores issued, 13 tensor-memory stores complete.
+torch::Tensor fmha_bwd_trace() {
+  auto out = torch::zeros({32, 64, 16}, torch::dtype(torch::kInt64));
+  const int rc = vo_fmha_bwd_trace(reinterpret_cast<long long*>(out.data_ptr<int64_t>()));
+  TORCH_CHECK(rc == 0, "no traced FMHA backward launch to read (run version 6 first): ", rc);
+  return out;
 }
 
 }  // namespace vo

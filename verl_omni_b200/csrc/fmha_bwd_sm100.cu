@@ -139,6 +139,7 @@ struct Params {
   __nv_bfloat16* dv;   // [BH, Skv, D]
   int split;           // > 0: dO rows q >= split come from the second dO tensor map (split % 128 == 0)
   const float4* ls_rec = nullptr;  // version 4: [BH, ceil(Sq / 64), 32] {-lse q log2e, -lse q+1 log2e, Delta q, Delta q+1}
+  long long* trace = nullptr;      // traced launches: SM clock stamps [32 CTAs][64 blocks][10 events]
 };
 
 template <int D>
@@ -466,6 +467,62 @@ __device__ __forceinline__ void sub_mul2(float p0, float p1, float d0, float d1,
       "sub.rn.f32x2 t, x, y;\n\tmul.rn.f32x2 t, t, e;\n\tmov.b64 {%0, %1}, t;\n\t}"
       : "=f"(r0), "=f"(r1)
       : "f"(p0), "f"(p1), "f"(d0), "f"(d1), "f"(e0), "f"(e1));
+}
+
+// 16 query columns [c0, c0 + 16) of one key row (one thread): P^T = exp2(S^T scale_log2 - lse log2e) and
+// dS^T = P^T (dP^T - Delta).  Written phase by phase over the 16 columns (all loads, all FMAs, all
+// exponentials, all dS, all packs), so every phase is 8-16 independent instructions the scheduler can
+// overlap instead of one dependent chain per column pair.  The packed bf16 P^T / dS^T go into tensor-memory
+// columns [c0 / 2, c0 / 2 + 8) of the two score buffers: with the chunks of a row run in order c0 = 0, 16,
+// 32, 48 by one thread, those columns have been read already.  dS^T also goes to the swizzled shared-memory
+// row for the dQ MMA.  `ls` holds {-lse log2e, -lse log2e, Delta, Delta} per query pair.
+__device__ __forceinline__ void grad_chunk16(uint32_t S_t, uint32_t DP_t, int c0, const float4* __restrict__ ls,
+                                             float sl2, bool full, int qlo, int qhi, uint8_t* ds, int r) {
+  uint32_t sa[16], pa[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(sa[0]), "=r"(sa[1]), "=r"(sa[2]), "=r"(sa[3]), "=r"(sa[4]), "=r"(sa[5]), "=r"(sa[6]), "=r"(sa[7]),
+        "=r"(sa[8]), "=r"(sa[9]), "=r"(sa[10]), "=r"(sa[11]), "=r"(sa[12]), "=r"(sa[13]), "=r"(sa[14]), "=r"(sa[15])
+      : "r"(S_t + c0));
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(pa[0]), "=r"(pa[1]), "=r"(pa[2]), "=r"(pa[3]), "=r"(pa[4]), "=r"(pa[5]), "=r"(pa[6]), "=r"(pa[7]),
+        "=r"(pa[8]), "=r"(pa[9]), "=r"(pa[10]), "=r"(pa[11]), "=r"(pa[12]), "=r"(pa[13]), "=r"(pa[14]), "=r"(pa[15])
+      : "r"(DP_t + c0));
+  float4 l4[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) l4[u] = ls[(c0 >> 1) + u];  // broadcast reads, in flight with the tensor-memory loads
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  float x[16], d[16];
+#pragma unroll
+  for (int u = 0; u < 8; ++u)
+    ffma2p(__uint_as_float(sa[2 * u]), __uint_as_float(sa[2 * u + 1]), sl2, l4[u].x, l4[u].y, x[2 * u], x[2 * u + 1]);
+#pragma unroll
+  for (int u = 0; u < 16; ++u) x[u] = ex2(x[u]);
+  if (!full) {
+#pragma unroll
+    for (int u = 0; u < 16; ++u)
+      if (c0 + u < qlo || c0 + u >= qhi) x[u] = 0.f;
+  }
+#pragma unroll
+  for (int u = 0; u < 8; ++u)
+    sub_mul2(__uint_as_float(pa[2 * u]), __uint_as_float(pa[2 * u + 1]), l4[u].z, l4[u].w, x[2 * u], x[2 * u + 1],
+             d[2 * u], d[2 * u + 1]);
+  uint32_t wp[8], wd[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    wp[u] = pack_bf16(x[2 * u], x[2 * u + 1]);
+    wd[u] = pack_bf16(d[2 * u], d[2 * u + 1]);
+  }
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(S_t + (c0 >> 1)),
+               "r"(wp[0]), "r"(wp[1]), "r"(wp[2]), "r"(wp[3]), "r"(wp[4]), "r"(wp[5]), "r"(wp[6]), "r"(wp[7])
+               : "memory");
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(DP_t + (c0 >> 1)),
+               "r"(wd[0]), "r"(wd[1]), "r"(wd[2]), "r"(wd[3]), "r"(wd[4]), "r"(wd[5]), "r"(wd[6]), "r"(wd[7])
+               : "memory");
+  const int unit = c0 >> 3;  // 16-byte units of the 128-byte dS^T row
+  *reinterpret_cast<uint4*>(ds + r * 128 + ((unit ^ (r & 7)) << 4)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+  *reinterpret_cast<uint4*>(ds + r * 128 + (((unit + 1) ^ (r & 7)) << 4)) = make_uint4(wd[4], wd[5], wd[6], wd[7]);
 }
 
 template <int D>
@@ -1053,39 +1110,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float4* ls = lsm + (i & 1) * 32;
       uint8_t* ds = sm + L::DS_OFF + c * 32768 + (i & 1) * 16384;
 #pragma unroll 1
-      for (int hf = 0; hf < 2; ++hf) {  // 32 query columns at a time
-        uint32_t sa[32], pa[32];
-        ld32_nowait(S_t + hf * 32, sa);
-        ld32_nowait(DP_t + hf * 32, pa);
-        wait_ld();
-        uint32_t wp[16], wd[16];
-#pragma unroll
-        for (int jj = 0; jj < 32; jj += 2) {
-          const int qc = hf * 32 + jj;
-          const float4 l4 = ls[qc >> 1];  // broadcast
-          float x0, x1;
-          v2::ffma2p(__uint_as_float(sa[jj]), __uint_as_float(sa[jj + 1]), sl2, l4.x, l4.y, x0, x1);
-          float e0 = ex2(x0), e1 = ex2(x1);
-          if (!full) {
-            if (qc < qlo || qc >= qhi) e0 = 0.f;
-            if (qc + 1 < qlo || qc + 1 >= qhi) e1 = 0.f;
-          }
-          float d0, d1;
-          v2::sub_mul2(__uint_as_float(pa[jj]), __uint_as_float(pa[jj + 1]), l4.z, l4.w, e0, e1, d0, d1);
-          wp[jj >> 1] = pack_bf16(e0, e1);
-          wd[jj >> 1] = pack_bf16(d0, d1);
-        }
-        // packed bf16 P^T / dS^T into columns [16 hf, 16 hf + 16) of this block's buffers (already read)
-        st16(S_t + hf * 16, wp);
-        st16(DP_t + hf * 16, wd);
-        // dS^T row r, query columns [32 hf, 32 hf + 32) of the block -> swizzled slot for the dQ MMA
-#pragma unroll
-        for (int u4 = 0; u4 < 4; ++u4) {
-          const int unit = hf * 4 + u4;
-          *reinterpret_cast<uint4*>(ds + r * 128 + ((unit ^ (r & 7)) << 4)) =
-              make_uint4(wd[4 * u4], wd[4 * u4 + 1], wd[4 * u4 + 2], wd[4 * u4 + 3]);
-        }
-      }
+      for (int c0 = 0; c0 < BQ; c0 += 16) v2::grad_chunk16(S_t, DP_t, c0, ls, sl2, full, qlo, qhi, ds, r);
       wait_st();
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       fence_before();
@@ -1226,7 +1251,17 @@ constexpr int BQ = 64;
 constexpr int THREADS = 512;
 
 
-template <int ST>
+// event stamps of a traced launch (first 32 CTAs, first 64 query blocks, 16 event slots): SM clock per stamp
+#define VO_TR(ev, blk)                                                                     \
+  do {                                                                                      \
+    if constexpr (TRACE) {                                                                  \
+      if (blockIdx.x < 32 && (blk) < 64) p.trace[(blockIdx.x * 64 + (blk)) * 16 + (ev)] = clock64(); \
+    }                                                                                       \
+  } while (0)
+
+// ALT: the two gradient warpgroups take alternate blocks (warps 4-7 even, 8-11 odd), all 64 columns each,
+// so one warpgroup's exponential burst overlaps the other's wait for its next scores
+template <int ST, bool TRACE = false, bool ALT = false>
 __global__ void __launch_bounds__(THREADS, 1)
     fmha_bwd4_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                      const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
@@ -1269,7 +1304,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sdp_full[i], 1);
-      mbar_init(&ds_full[i], 8);
+      mbar_init(&ds_full[i], ALT ? 4 : 8);
       mbar_init(&ls_full[i], 1);
       mbar_init(&dsfree[i], 1);
       mbar_init(&dq_full[i], 1);
@@ -1303,6 +1338,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int i = 0; i < nblk; ++i) {
           const int j = j0 + i, st = i % ST;
           if (!mbar_wait(&qdo_empty[st], ((i / ST) & 1) ^ 1, abort_flag, 81)) break;
+          VO_TR(0, i);
           mbar_expect_tx(&qdo_full[st], 2 * L::QB + 512);
           tma3(sm + L::Q_OFF + st * L::QB, &mq, &qdo_full[st], 0, j * BQ, bh);
           if (p.split > 0 && j * BQ >= p.split)
@@ -1339,19 +1375,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int i = 0; ok && i < nblk; ++i) {
         const int st = i % ST;
         if (!mbar_wait(&ds_full[i & 1], (i >> 1) & 1, abort_flag, 85)) break;
+        VO_TR(1, i);
         fence_after();
         const uint32_t qa = smem_u32(sm + L::Q_OFF + st * L::QB);
         const uint32_t oa = smem_u32(sm + L::DO_OFF + st * L::QB);
         const uint32_t cs = tmem + L::C_S + 64 * (i & 1), cdp = tmem + L::C_DP + 64 * (i & 1);
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk)  // dV += P^T dO over the block's 64 queries (8 packed columns / step)
-          mma_ts(tmem + L::C_DV, cs + kk * 8 + (kk >> 1) * 16, desc(oa + kk * 2048, 8192, 1024), id_kn,
+          mma_ts(tmem + L::C_DV, cs + kk * 8 + (ALT ? 0 : (kk >> 1) * 16), desc(oa + kk * 2048, 8192, 1024), id_kn,
                  (i > 0 || kk > 0));
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk)  // dK += dS^T Q
-          mma_ts(tmem + L::C_DK, cdp + kk * 8 + (kk >> 1) * 16, desc(qa + kk * 2048, 8192, 1024), id_kn,
+          mma_ts(tmem + L::C_DK, cdp + kk * 8 + (ALT ? 0 : (kk >> 1) * 16), desc(qa + kk * 2048, 8192, 1024), id_kn,
                  (i > 0 || kk > 0));
         commit(&qdo_empty[st]);
+        VO_TR(2, i);
         if ((i & 1) || i + 1 == nblk) {  // dQ of the pair (blocks 2q, 2q + 1) over the 128 keys
           const int q = i >> 1, c = q & 1;
           if (q >= 2 && !mbar_wait(&dq_free[c], ((q >> 1) & 1) ^ 1, abort_flag, 86)) break;
@@ -1366,6 +1404,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (i + 2 < nblk) {
           if (!mbar_wait(&qdo_full[(i + 2) % ST], ((i + 2) / ST) & 1, abort_flag, 87)) break;
+          VO_TR(3, i);
           fence_after();
           issue_sdp(i + 2);
         }
@@ -1375,27 +1414,30 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp >= 4 && warp < 12) {
     // ---------------------------------------------------------------- gradient warps: one key row per thread,
     // warps 4-7 take query columns [0, 32) of each block and warps 8-11 columns [32, 64)
-    const int hf = (warp - 4) >> 2;
+    const int wg = (warp - 4) >> 2;
     const int lane_base = 32 * (warp & 3);
     const int r = lane_base + lane;
     const int kv = kv0 + r;
     const uint32_t lane_off = (uint32_t)lane_base << 16;
     const float sl2 = p.scale_log2;
     bool ok = nblk > 0;
-    for (int i = 0; ok && i < nblk; ++i) {
+    for (int i = ALT ? wg : 0; ok && i < nblk; i += ALT ? 2 : 1) {
       const int j = j0 + i;
       const int q0 = j * BQ;
       const int q = i >> 1, c = q & 1;
+      if (warp == 4 && lane == 0) VO_TR(4, i);
       // the pair's dS^T slots were last read by the dQ MMA of pair q - 2
-      if (!(i & 1) && q >= 2 && !mbar_wait(&dsfree[c], ((q >> 1) & 1) ^ 1, abort_flag, 88)) {
+      if ((ALT || !(i & 1)) && q >= 2 && !mbar_wait(&dsfree[c], ((q >> 1) & 1) ^ 1, abort_flag, 88)) {
         ok = false;
         break;
       }
+      if (warp == 4 && lane == 0) VO_TR(5, i);
       if (!mbar_wait(&qdo_full[i % ST], (i / ST) & 1, abort_flag, 89) ||
           !mbar_wait(&sdp_full[i & 1], (i >> 1) & 1, abort_flag, 90)) {
         ok = false;
         break;
       }
+      if (warp == 4 && lane == 0) VO_TR(6, i);
       fence_after();
       // visible query columns of this key row within the block: [qlo, qhi)
       int qhi = kv < kvl ? min(BQ, p.Sq - q0) : 0;
@@ -1407,11 +1449,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t DP_t = tmem + L::C_DP + 64 * (i & 1) + lane_off;
       const float4* ls = lsm + (i % ST) * 32;
       uint8_t* ds = sm + L::DS_OFF + c * 32768 + (i & 1) * 16384;
-      {  // this warpgroup's 32 query columns
+if constexpr (ALT) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BQ; c0 += 16) v2::grad_chunk16(S_t, DP_t, c0, ls, sl2, full, qlo, qhi, ds, r);
+      } else {  // this warpgroup's 32 query columns
+        const int hf = wg;
         uint32_t sa[32], pa[32];
         ld32_nowait(S_t + hf * 32, sa);
         ld32_nowait(DP_t + hf * 32, pa);
         wait_ld();
+        if (warp == 4 && lane == 0) VO_TR(10, i);
         uint32_t wp[16], wd[16];
 #pragma unroll
         for (int jj = 0; jj < 32; jj += 2) {
@@ -1429,7 +1476,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           wp[jj >> 1] = pack_bf16(e0, e1);
           wd[jj >> 1] = pack_bf16(d0, d1);
         }
-        // packed bf16 P^T / dS^T into columns [16 hf, 16 hf + 16) of this block's buffers (already read)
+        if (warp == 4 && lane == 0) VO_TR(11, i);
+        // packed bf16 P^T / dS^T into the first half of this warpgroup's own 32 columns (already read)
         st16(S_t + hf * 32, wp);
         st16(DP_t + hf * 32, wd);
         // dS^T row r, query columns [32 hf, 32 hf + 32) of the block -> swizzled slot for the dQ MMA
@@ -1440,11 +1488,14 @@ __global__ void __launch_bounds__(THREADS, 1)
               make_uint4(wd[4 * u4], wd[4 * u4 + 1], wd[4 * u4 + 2], wd[4 * u4 + 3]);
         }
       }
+      if (warp == 4 && lane == 0) VO_TR(12, i);
       wait_st();
+      if (warp == 4 && lane == 0) VO_TR(13, i);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ds_full[i & 1]);
+      if (warp == 4 && lane == 0) VO_TR(7, i);
     }
   } else if (warp >= 12) {
     // ---------------------------------------------------------------- dQ drain, then the dK / dV store
@@ -1460,6 +1511,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         ok = false;
         break;
       }
+      if (warp == 12 && lane == 0) VO_TR(8, 2 * q);
       fence_after();
       const int qrow0 = (j0 + 2 * q) * BQ;  // first query row of the pair
 #pragma unroll
@@ -1491,6 +1543,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&dq_free[c]);
+      if (warp == 12 && lane == 0) VO_TR(9, 2 * q);
     }
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     __syncwarp();
@@ -1536,6 +1589,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
   }
 }
+#undef VO_TR
 }  // namespace v4
 
 // Delta[bh, q] = sum_d dO[b, q, h, d] * O[b, q, h, d]
@@ -1677,20 +1731,24 @@ static int launch3(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
   return (int)cudaGetLastError();
 }
 
-template <int ST>
+template <int ST, bool TRACE = false, bool ALT = false>
 static int launch4(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
                    const CUtensorMap& mdo2, const CUtensorMap& mdq, Params p, int grid, cudaStream_t st) {
   using L = v4::Lay4<ST>;
   static bool set = false;
   if (!set) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(v4::fmha_bwd4_kernel<ST>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES + 1024);
+    const cudaError_t e = cudaFuncSetAttribute(v4::fmha_bwd4_kernel<ST, TRACE, ALT>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES + 1024);
     if (e != cudaSuccess) return (int)e;
     set = true;
   }
-  v4::fmha_bwd4_kernel<ST><<<grid, v4::THREADS, L::BYTES + 1024, st>>>(mq, mk, mv, mdo, mdo2, mdq, p);
+  v4::fmha_bwd4_kernel<ST, TRACE, ALT><<<grid, v4::THREADS, L::BYTES + 1024, st>>>(mq, mk, mv, mdo, mdo2, mdq, p);
   return (int)cudaGetLastError();
 }
+
+// traced launches (version 6) write their event stamps here
+static long long* g_trace_buf = nullptr;
+static constexpr size_t kTraceElems = 32 * 64 * 16;
 
 }  // namespace vo_fbwd
 
@@ -1714,10 +1772,11 @@ extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const vo
     delta_kernel<128><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
         (const __nv_bfloat16*)o, (const __nv_bfloat16*)dO, (const __nv_bfloat16*)o2, (const __nv_bfloat16*)dO2, split,
         delta, B, Sq, H);
-  // versions 3, 4 and 5 (head_dim 64): 64-query blocks (5 = 4 with a five-deep Q / dO ring); other head
-  // widths run version 2
-  if (version >= 3 && version <= 5 && D != 64) version = 2;
-  const int qrows = (version >= 3 && version <= 5) ? 64 : 128;
+  // versions 3-8 (head_dim 64): 64-query blocks (5 = 4 with a five-deep Q / dO ring; 6 = 4 traced: SM clock
+  // stamps of the pipeline events, read back with vo_fmha_bwd_trace; 7 = gradient warpgroups on alternate
+  // blocks; 8 = 7 traced); other widths run version 2
+  if (version >= 3 && version <= 8 && D != 64) version = 2;
+  const int qrows = (version >= 3 && version <= 8) ? 64 : 128;
   CUtensorMap mq, mk, mv, mdo;
   int r = map3(&mq, q, B * H, Sq, D, qrows);
   if (!r) r = map3(&mk, k, B * H, Skv, D);
@@ -1743,7 +1802,7 @@ extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const vo
   p.dv = (__nv_bfloat16*)dv;
   p.split = split;
   const int grid = p.nkv_tiles * B * H;
-  if (version == 4 || version == 5) {
+  if (version >= 4 && version <= 8) {
     // records follow Delta in the caller's scratch, rounded up to 16 bytes
     float4* rec = reinterpret_cast<float4*>((reinterpret_cast<uintptr_t>(delta + (int64_t)B * H * Sq) + 15) &
                                             ~uintptr_t(15));
@@ -1752,10 +1811,18 @@ extern "C" int vo_fmha_bwd(const void* q, const void* k, const void* v, const vo
     ls_record_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(lse, delta, rec, Sq, nqb, n);
     p.ls_rec = rec;
   }
-  if (version >= 3 && version <= 5) {
+  if (version >= 3 && version <= 8) {
     CUtensorMap mdq;
     if ((r = map3_f32(&mdq, dq_acc, B * H, Sq, D))) return r;
-    r = version == 5   ? launch4<5>(mq, mk, mv, mdo, mdo2, mdq, p, grid, stream)
+    if (version == 6 || version == 8) {
+      if (!g_trace_buf && cudaMalloc(&g_trace_buf, kTraceElems * sizeof(long long)) != cudaSuccess) return -4;
+      cudaMemsetAsync(g_trace_buf, 0, kTraceElems * sizeof(long long), stream);
+      p.trace = g_trace_buf;
+    }
+    r = version == 8   ? launch4<3, true, true>(mq, mk, mv, mdo, mdo2, mdq, p, grid, stream)
+        : version == 7 ? launch4<3, false, true>(mq, mk, mv, mdo, mdo2, mdq, p, grid, stream)
+        : version == 6 ? launch4<3, true>(mq, mk, mv, mdo, mdo2, mdq, p, grid, stream)
+        : version == 5 ? launch4<5>(mq, mk, mv, mdo, mdo2, mdq, p, grid, stream)
         : version == 4 ? launch4<3>(mq, mk, mv, mdo, mdo2, mdq, p, grid, stream)
                        : launch3(mq, mk, mv, mdo, mdo2, mdq, p, grid, stream);
   } else if (version == 2) {
@@ -1783,4 +1850,11 @@ extern "C" int vo_fmha_bwd_error(int reset) {
     cudaMemcpyToSymbol(vo_fbwd::g_error, &z, sizeof(int));
   }
   return e;
+}
+
+// Copies the event stamps of the last traced backward launch ([32][64][16] SM clocks; 0 = not reached).
+extern "C" int vo_fmha_bwd_trace(long long* host) {
+  using namespace vo_fbwd;
+  if (!g_trace_buf) return -1;
+  return (int)cudaMemcpy(host, g_trace_buf, kTraceElems * sizeof(long long), cudaMemcpyDeviceToHost);
 }

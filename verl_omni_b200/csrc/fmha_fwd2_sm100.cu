@@ -980,7 +980,35 @@ __global__ void __launch_bounds__(FWD4_THREADS, 2)
       const float nmb = (m == -INFINITY) ? 0.f : -m;
       uint32_t w[32];
       float rs0 = 0.f, rs1 = 0.f;
-      if (lim == BK4) {
+      if (lim == BK4 && EMU == 0) {
+        // phase by phase over the 64 scores (all FMAs, all exponentials, all sums, all packs): each phase is
+        // 32-64 independent instructions, so the scheduler overlaps their latencies instead of running one
+        // dependent chain per pair
+        float fa[32], fc[32];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          ffma2(__uint_as_float(a[2 * i]), __uint_as_float(a[2 * i + 1]), sl2, nmb, fa[2 * i], fa[2 * i + 1]);
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          ffma2(__uint_as_float(c[2 * i]), __uint_as_float(c[2 * i + 1]), sl2, nmb, fc[2 * i], fc[2 * i + 1]);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) fa[i] = ex2(fa[i]);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) fc[i] = ex2(fc[i]);
+        float ra[4] = {0.f, 0.f, 0.f, 0.f}, rb[4] = {0.f, 0.f, 0.f, 0.f};  // four independent sum chains
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          fadd2(ra[i & 3], rb[i & 3], fa[2 * i], fa[2 * i + 1]);
+          w[i] = pack_bf16(fa[2 * i], fa[2 * i + 1]);
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          fadd2(ra[i & 3], rb[i & 3], fc[2 * i], fc[2 * i + 1]);
+          w[16 + i] = pack_bf16(fc[2 * i], fc[2 * i + 1]);
+        }
+        rs0 = (ra[0] + ra[1]) + (ra[2] + ra[3]);
+        rs1 = (rb[0] + rb[1]) + (rb[2] + rb[3]);
+      } else if (lim == BK4) {
         float ra[4] = {0.f, 0.f, 0.f, 0.f}, rb[4] = {0.f, 0.f, 0.f, 0.f};  // four independent sum chains
 #pragma unroll
         for (int i = 0; i < 32; ++i) {

@@ -366,6 +366,7 @@ def bench_fmha(a) -> list[dict]:
         cases["bwd3"] = (lambda: e.fmha_bwd(q, k, v, o, lse, do, False, scale, 3), 2.5 * flops_f)
         cases["bwd4"] = (lambda: e.fmha_bwd(q, k, v, o, lse, do, False, scale, 4), 2.5 * flops_f)
         cases["bwd5"] = (lambda: e.fmha_bwd(q, k, v, o, lse, do, False, scale, 5), 2.5 * flops_f)
+        cases["bwd7"] = (lambda: e.fmha_bwd(q, k, v, o, lse, do, False, scale, 7), 2.5 * flops_f)
     if a.compare:
         cases["sdpa_fwd"] = (lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v), flops_f)
         qg, kg, vg = (t.detach().clone().requires_grad_(True) for t in (q, k, v))
