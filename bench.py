@@ -155,6 +155,7 @@ def main() -> None:
     ap.add_argument("--group", type=int, default=None)
     ap.add_argument("--sde-steps", type=int, default=None)
     ap.add_argument("--micro", type=int, default=None)
+    ap.add_argument("--layers", type=int, default=None, help="omni_moe: decoder layers (default: the full 48)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile-step", action="store_true",
                     help="after warm-up, run one step under torch.profiler and print the top CUDA kernels (no bench line)")
@@ -334,7 +335,10 @@ def bench_omni(args) -> None:
     dp = N // tp
     per_dp = args.prompts_per_gpu or 16
     group = args.group or 8
-    cfg = load_config("omni_trainer", [
+    ov = []
+    if args.layers:  # full width, fewer decoder layers (a smoke run on few GPUs; named in the config below)
+        ov.append(f"actor_rollout_ref.model.num_layers={args.layers}")
+    cfg = load_config("omni_trainer", ov + [
         "trainer.device=cuda", f"data.train_batch_size={per_dp * dp}", f"actor_rollout_ref.rollout.n={group}",
         "actor_rollout_ref.rollout.response_length=1024", f"actor_rollout_ref.actor.megatron.expert_model_parallel_size={N}",
         f"actor_rollout_ref.actor.megatron.tensor_model_parallel_size={tp}",
@@ -371,6 +375,7 @@ def bench_omni(args) -> None:
             "config": {"model": "Qwen3-Omni-30B-A3B-shaped MoE thinker (48 layers, hidden 2048, 32 q / 4 kv heads, "
                                 "128 experts top-8, expert FFN 768, vocab 151936) + 32-layer audio / 27-layer vision towers",
                        "name": "omni_moe", "global_batch": samples, "prompts": per_dp * dp, "group": group,
+                       "layers": args.layers or 48,
                        "seq_len": 512 + 1024, "parallelism": f"ep{N}_tp{tp}_dp{dp}", "reward": "seeded hash of the "
                        "response tokens", "l2": "inputs larger than L2 (no flush)"},
             "impl": "native", "gpu_launches": ext().launch_count() - launches0, "max_memory_allocated_gb": mem_gb,

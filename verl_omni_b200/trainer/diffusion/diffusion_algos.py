@@ -405,8 +405,9 @@ class DPOLoss(DiffusionLossFn):
             raise ValueError("DPO loss expects each chosen sample reward to be >= its rejected pair reward.")
         beta = config.diffusion_loss.dpo_beta
         target = noise.float() - latent.float()
-        model_err = ((model_noise_pred.float() - target) ** 2).flatten(1).mean(1)
-        ref_err = ((ref_noise_pred.float() - target) ** 2).flatten(1).mean(1)
+        model_err = loss_ops.sq_dist(model_noise_pred.float().contiguous(), target.contiguous())
+        with torch.no_grad():
+            ref_err = loss_ops.sq_dist(ref_noise_pred.float().contiguous(), target.contiguous())
         w_diff = model_err[0::2] - ref_err[0::2]
         l_diff = model_err[1::2] - ref_err[1::2]
         inside = -0.5 * beta * (w_diff - l_diff)
@@ -455,11 +456,13 @@ class DiffusionNFTLoss(DiffusionLossFn):
                 min=lc.adaptive_weight_min).to(x0_pos.dtype)
             nw = torch.abs(x0_neg.double() - x0.double()).mean(dim=dims, keepdim=True).clip(
                 min=lc.adaptive_weight_min).to(x0_neg.dtype)
-        pos_loss = ((x0_pos - x0) ** 2 / pw).mean(dim=dims)
-        neg_loss = ((x0_neg - x0) ** 2 / nw).mean(dim=dims)
+        # per-sample squared distances (one fused pass each on CUDA fp32), divided by the per-sample weights
+        x0c = x0.contiguous()
+        pos_loss = loss_ops.sq_dist(x0_pos.contiguous(), x0c) / pw.reshape(-1).float()
+        neg_loss = loss_ops.sq_dist(x0_neg.contiguous(), x0c) / nw.reshape(-1).float()
         per = w * pos_loss / beta + (1.0 - w) * neg_loss / beta
         policy_loss = (per * lc.adv_clip_max).mean()
-        ref_kl = ((forward_prediction - ref) ** 2).mean(dim=dims).mean()
+        ref_kl = loss_ops.sq_dist(forward_prediction.contiguous(), ref.contiguous()).mean()
         loss = policy_loss + lc.ref_kl_coef * ref_kl
         with torch.no_grad():
             m = {
@@ -467,7 +470,7 @@ class DiffusionNFTLoss(DiffusionLossFn):
                 "actor/positive_loss": pos_loss.mean().detach(),
                 "actor/negative_loss": neg_loss.mean().detach(),
                 "actor/ref_kl_loss": ref_kl.detach(),
-                "actor/old_deviate": ((forward_prediction - old) ** 2).mean().detach(),
+                "actor/old_deviate": loss_ops.sq_dist(forward_prediction.detach().contiguous(), old.contiguous()).mean(),
                 "actor/reward_prob_mean": w.mean().detach(),
                 "actor/total_loss": loss.detach(),
             }

@@ -32,6 +32,10 @@ def build_omni_trainer(config):
     if arch not in ARCHS:
         raise KeyError(f"unknown omni architecture {arch!r}; known: {sorted(ARCHS)}")
     mcfg = getattr(MoEConfig, ARCHS[arch])()
+    # optional depth override (full width, fewer layers): smoke runs of the full-width model on few GPUs
+    nl = arc.model.get("num_layers", None) if hasattr(arc.model, "get") else None
+    if nl:
+        mcfg.layers = int(nl)
     act = arc.actor
     ac = DiffusionActorConfig()
     ac.grad_clip = float(act.grad_clip)

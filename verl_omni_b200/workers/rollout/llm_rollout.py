@@ -64,8 +64,9 @@ class LLMRolloutEngine:
             caches = [KVCache(B, cfg.kv_heads, P + self.max_new_tokens, cfg.head_dim, dev, self.module.embed.dtype)
                       for _ in self.module.layers]
         # prefill: the vocabulary projection of the last prompt position only
-        h = self.module(ids, caches=caches, pos0=0, audio_feats=batch.batch.get("audio_feats"),
-                        image_patches=batch.batch.get("image_patches"), return_hidden=True)
+        af, ip = batch.batch.get("audio_feats"), batch.batch.get("image_patches")
+        h = self.module(ids, caches=caches, pos0=0, audio_feats=af.to(dev) if af is not None else None,
+                        image_patches=ip.to(dev) if ip is not None else None, return_hidden=True)
         logits = self.module.lm_head(h[:, -1:].contiguous()).float()[:, -1]
         out_ids, out_lp = [], []
         done = torch.zeros(B, dtype=torch.bool, device=ids.device)
