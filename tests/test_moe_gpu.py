@@ -84,3 +84,22 @@ def test_moe_layer_forward_backward_matches_loop(E_):
     g_ref = torch.autograd.grad((ref * gy).sum(), leaves)
     for a, b, name in zip(g_nat, g_ref, ("h", "gates", "w_gate_up", "w_down")):
         assert _rel(a, b) < 3e-2, name
+
+
+def test_moe_ffn_local_experts_only(E_):
+    """This rank's experts' contribution with the other slots dropped on the device (sink tiles skipped by the
+    grouped GEMM) equals the fp32 oracle restricted to those experts."""
+    from verl_omni_b200.ops.moe import moe_ffn_local, moe_ffn_local_reference
+
+    torch.manual_seed(0)
+    E, El, e0, D, F, T, K = 16, 4, 8, 256, 128, 96, 4
+    h = (torch.randn(T, D, device="cuda") * 0.5).bfloat16()
+    idx = torch.randint(0, E, (T, K), device="cuda")
+    gates = torch.rand(T, K, device="cuda")
+    wgu = (torch.randn(El, 2 * F, D, device="cuda") * 0.05).bfloat16()
+    wd = (torch.randn(El, D, F, device="cuda") * 0.05).bfloat16()
+    with torch.no_grad():
+        out = moe_ffn_local(h, idx, gates, wgu, wd, e0)
+    ref = moe_ffn_local_reference(h, idx, gates, wgu, wd, e0)
+    assert torch.isfinite(out).all()
+    assert _rel(out, ref) < 2e-2

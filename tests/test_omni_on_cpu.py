@@ -126,6 +126,35 @@ def test_expert_parallel_ep2_gloo():
     run_ranks(_ep_check, 2)
 
 
+def _ep_decode_check(rank, world):
+    from verl_omni_b200.parallel.expert_parallel import ExpertParallel
+    import torch.distributed as dist
+
+    torch.manual_seed(0)
+    E, D, F = 4, 8, 6
+    wgu, wd = torch.randn(E, 2 * F, D), torch.randn(E, D, F)
+    torch.manual_seed(10 + rank)
+    h = torch.randn(5, D)
+    idx = torch.randint(0, E, (5, 2))
+    gates = torch.rand(5, 2)
+    ref = grouped_expert_ffn(h, idx, gates, wgu, wd)
+    ep = ExpertParallel(E, dist.group.WORLD)
+    El = E // world
+    lo = rank * El
+    with torch.no_grad():
+        out = ep.decode_combine(h, idx, gates, wgu[lo:lo + El], wd[lo:lo + El], lo)
+    # tokens / gates travel as bf16 through the gather: compare with the oracle on the rounded inputs
+    ref16 = grouped_expert_ffn(h.bfloat16().float(), idx, gates.bfloat16().float(), wgu, wd)
+    torch.testing.assert_close(out, ref16, rtol=1e-4, atol=1e-4)
+    assert float((out - ref).abs().max()) < 0.1 * float(ref.abs().max()) + 1e-3
+
+
+def test_expert_parallel_decode_gather_ep2_gloo():
+    """One-token decode steps: tokens all-gathered, local experts, reduce-scatter (no host-synchronised
+    variable all-to-all) equals the unsharded expert layer."""
+    run_ranks(_ep_decode_check, 2)
+
+
 def test_chunked_vocab_logprob_matches_full_log_softmax():
     """Chunked log-sum-exp over the vocabulary (chunk not dividing V) equals log_softmax().gather, values and
     gradients of the hidden states and head weight."""

@@ -185,7 +185,11 @@ class MoEBlock(nn.Module):
         gates, idx, probs = LO.router_topk(self.router(h).float(), cfg.top_k)
         gates = gates.to(x.dtype)
         self.last_router = (probs, idx)
-        if ep is not None and hasattr(ep, "fused_ok") and ep.fused_ok(h, self.w_gate_up, self.w_down):
+        if (ep is not None and ep.ep > 1 and not torch.is_grad_enabled() and S == 1
+                and getattr(ep, "decode_combine", None) is not None):
+            # one-token decode steps: fixed-size gather / reduce-scatter, no host synchronisation per layer
+            out = ep.decode_combine(h, idx, gates, self.w_gate_up, self.w_down, self.e0)
+        elif ep is not None and hasattr(ep, "fused_ok") and ep.fused_ok(h, self.w_gate_up, self.w_down):
             out = ep.dispatch_combine_fused(h, idx, gates, self.w_gate_up, self.w_down)  # peer-memory exchange
         elif ep is not None:
             out = ep.dispatch_combine(h, idx, gates, self.expert_ffn)

@@ -132,6 +132,34 @@ def moe_ffn(h: torch.Tensor, idx: torch.Tensor, gates: torch.Tensor, w_gate_up: 
     return out.index_add(0, plan.tok, (y.index_select(0, plan.dst) * w).to(h.dtype))
 
 
+def moe_ffn_local(h: torch.Tensor, idx: torch.Tensor, gates: torch.Tensor, w_gate_up: torch.Tensor,
+                  w_down: torch.Tensor, e0: int) -> torch.Tensor:
+    """The contribution of this rank's experts [e0, e0 + El) to ``sum_k gates[:, k] expert_{idx[:, k]}(h)``,
+    with every other slot dropped on the device (no host synchronisation).
+
+    Slots of other ranks' experts are sorted into a sink segment whose tiles are marked -1, which the
+    grouped GEMM skips; their rows are excluded with ``where`` (the skipped rows hold no values)."""
+    El = w_gate_up.shape[0]
+    loc = (idx >= e0) & (idx < e0 + El)
+    lidx = torch.where(loc, idx - e0, torch.full_like(idx, El))
+    plan = plan_dispatch(lidx, El + 1)
+    tile_expert = torch.where(plan.tile_expert >= El, torch.full_like(plan.tile_expert, -1), plan.tile_expert)
+    xs = h.new_zeros(plan.rows, h.shape[1])
+    xs = xs.index_copy(0, plan.dst, h.index_select(0, plan.tok))
+    y = _ExpertFFN.apply(xs, w_gate_up, w_down, tile_expert, plan.seg)
+    keep = loc.reshape(-1)[plan.order].unsqueeze(-1)
+    w = gates.reshape(-1)[plan.order].unsqueeze(-1).float()
+    contrib = torch.where(keep, y.index_select(0, plan.dst).float() * w, torch.zeros((), device=h.device))
+    return torch.zeros(h.shape, dtype=torch.float32, device=h.device).index_add(0, plan.tok, contrib)
+
+
+def moe_ffn_local_reference(h, idx, gates, w_gate_up, w_down, e0: int) -> torch.Tensor:
+    El = w_gate_up.shape[0]
+    loc = (idx >= e0) & (idx < e0 + El)
+    return moe_ffn_reference(h, torch.where(loc, idx - e0, 0), torch.where(loc, gates, torch.zeros_like(gates)),
+                             w_gate_up, w_down)
+
+
 def moe_ffn_reference(h, idx, gates, w_gate_up, w_down) -> torch.Tensor:
     """fp32 per-expert loop (oracle)."""
     out = torch.zeros(h.shape, dtype=torch.float32, device=h.device)

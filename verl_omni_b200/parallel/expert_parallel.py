@@ -87,6 +87,34 @@ class ExpertParallel:
         return out.index_add(0, tok[order], y_back * w)
 
 
+    def decode_combine(self, h: torch.Tensor, idx: torch.Tensor, gates: torch.Tensor, w_gate_up, w_down,
+                       e0: int) -> torch.Tensor:
+        """Expert layer for a gradient-free step of a few tokens per rank (decode): every rank's tokens, expert
+        ids and gates are all-gathered (one packed buffer), each rank applies its own experts to all of them,
+        and a reduce-scatter sums the contributions back to the tokens' owners.  Every message has a fixed size,
+        so nothing waits on the host (the variable all-to-all reads its split sizes on the host every layer).
+        All ranks must call it with the same token count."""
+        from verl_omni_b200.ops import moe as MO
+
+        T, K = idx.shape
+        Dm = h.shape[1]
+        W = self.ep
+        # idx travels as bf16: expert ids < 256 are exact
+        pack = torch.cat([h.to(torch.bfloat16), gates.to(torch.bfloat16), idx.to(torch.bfloat16)], 1)
+        allp = torch.empty(W * T, pack.shape[1], dtype=pack.dtype, device=h.device)
+        D.all_gather_into(allp.view(-1), pack.contiguous().view(-1), self.group)
+        hg = allp[:, :Dm].contiguous()
+        gg = allp[:, Dm:Dm + K].float()
+        ig = allp[:, Dm + K:].float().round().to(torch.int64)
+        if MO.native_ok(hg, w_gate_up, w_down):
+            part = MO.moe_ffn_local(hg, ig, gg, w_gate_up, w_down, e0)
+        else:
+            part = MO.moe_ffn_local_reference(hg, ig, gg, w_gate_up, w_down, e0)
+        out = torch.empty(T, Dm, dtype=torch.float32, device=h.device)
+        D.reduce_scatter_into(out.view(-1), part.contiguous().view(-1), self.group)
+        return out.to(h.dtype)
+
+
 # ---------------------------------------------------------------- fused exchange over peer memory
 class _Layout:
     """Host plan of one fused exchange (computed from the all-gathered per-expert counts)."""
