@@ -48,7 +48,8 @@ def plan_dispatch(idx: torch.Tensor, n_experts: int) -> DispatchPlan:
     flat_e = idx.reshape(-1)
     order = torch.argsort(flat_e, stable=True)
     sorted_e = flat_e[order]
-    counts = torch.bincount(flat_e, minlength=n_experts)
+    # scatter-add count (bincount reads the maximum id back to the host to size its output)
+    counts = torch.zeros(n_experts, dtype=torch.int64, device=dev).scatter_add_(0, flat_e, torch.ones_like(flat_e))
     padded = (counts + TILE - 1) // TILE * TILE
     seg = torch.zeros(n_experts + 1, dtype=torch.int64, device=dev)
     seg[1:] = torch.cumsum(padded, 0)
