@@ -729,39 +729,8 @@ __global__ void __launch_bounds__(512, 1)
       const uint32_t S_t = tmem + L::C_S + lane_off + 64 * g;
       const uint32_t DP_t = tmem + L::C_DP + lane_off + 64 * g;
 #pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t sa[32], pa[32];
-        ld32_nowait(S_t + c * 32, sa);
-        ld32_nowait(DP_t + c * 32, pa);
-        wait_ld();
-        uint32_t wp[16], wd[16];
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const int qc = c * 32 + j;
-          const float4 l4 = *reinterpret_cast<const float4*>(lsm + (qc >> 1) * 4);  // broadcast
-          float x0, x1;
-          ffma2p(__uint_as_float(sa[j]), __uint_as_float(sa[j + 1]), sl2, l4.x, l4.y, x0, x1);
-          float e0 = ex2(x0), e1 = ex2(x1);
-          if (!full) {
-            if (qc < qlo || qc >= qhi) e0 = 0.f;
-            if (qc + 1 < qlo || qc + 1 >= qhi) e1 = 0.f;
-          }
-          float d0, d1;
-          sub_mul2(__uint_as_float(pa[j]), __uint_as_float(pa[j + 1]), l4.z, l4.w, e0, e1, d0, d1);
-          wp[j >> 1] = pack_bf16(e0, e1);
-          wd[j >> 1] = pack_bf16(d0, d1);
-        }
-        st16(S_t + c * 16, wp);
-        st16(DP_t + c * 16, wd);
-        // dS^T row r, query columns 64 g + 32 c .. +31 -> 128B-swizzled tile for the dQ MMA
-        const int chunk = g;  // 64-column chunk of the 128-query tile
-#pragma unroll
-        for (int u4 = 0; u4 < 4; ++u4) {
-          const int unit = c * 4 + u4;  // 16-byte unit (8 queries) within the 128-byte row
-          *reinterpret_cast<uint4*>(ds + chunk * 16384 + r * 128 + ((unit ^ (r & 7)) << 4)) =
-              make_uint4(wd[4 * u4], wd[4 * u4 + 1], wd[4 * u4 + 2], wd[4 * u4 + 3]);
-        }
-      }
+      for (int c0 = 0; c0 < 64; c0 += 16)  // 16 query columns at a time, phase by phase
+        grad_chunk16(S_t, DP_t, c0, reinterpret_cast<const float4*>(lsm), sl2, full, qlo, qhi, ds + g * 16384, r);
       wait_st();
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       fence_before();
