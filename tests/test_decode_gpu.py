@@ -142,3 +142,32 @@ def test_decode_tcgen05_equals_cuda_core_path(monkeypatch):
     cc = ext().decode_attention(q, kp, vp, lens, hd ** -0.5, 0, table)
     assert ext().decode_tc_error(True) == 0
     torch.testing.assert_close(tc.float(), cc.float(), rtol=2e-2, atol=2e-2)
+
+
+def test_llm_rollout_cuda_graph_decode_matches_eager(monkeypatch):
+    """The thinker's decode step captured once as a CUDA graph and replayed at every position produces the
+    same greedy tokens and log-probs as eager steps, and the launch counter advances on replays."""
+    from verl_omni_b200.models.moe_llm import MoEConfig, MoELLM
+    from verl_omni_b200.ops._ext import ext
+    from verl_omni_b200.utils.dataproto import DataProto
+    from verl_omni_b200.workers.rollout.llm_rollout import LLMRolloutEngine
+
+    torch.manual_seed(0)
+    cfg = MoEConfig(vocab=2048, hidden=512, layers=2, q_heads=16, kv_heads=2, head_dim=128, experts=8, top_k=2,
+                    expert_ffn=256, audio_layers=1, audio_dim=128, audio_mel=16, vision_layers=1, vision_dim=128,
+                    vision_patch_dim=48, audio_token=2046, image_token=2047)
+    m = MoELLM(cfg).to("cuda", torch.bfloat16).eval()
+    ids = torch.randint(0, 2000, (4, 37))
+    batch = DataProto({"input_ids": ids}, {})
+    eng = LLMRolloutEngine(m, max_new_tokens=12, temperature=0.0, device=torch.device("cuda"))
+    monkeypatch.setenv("VO_DECODE_GRAPH", "0")
+    n0 = ext().launch_count()
+    a = eng.generate(batch, seed=0)
+    n_eager = ext().launch_count() - n0
+    monkeypatch.setenv("VO_DECODE_GRAPH", "1")
+    n0 = ext().launch_count()
+    b = eng.generate(batch, seed=0)
+    torch.cuda.synchronize()
+    assert n_eager > 10 * cfg.layers and ext().launch_count() - n0 == n_eager
+    assert torch.equal(a.batch["responses"], b.batch["responses"])
+    torch.testing.assert_close(b.batch["rollout_log_probs"], a.batch["rollout_log_probs"], rtol=1e-4, atol=1e-4)

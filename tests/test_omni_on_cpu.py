@@ -45,6 +45,33 @@ def test_paged_cache_decode_matches_full_forward():
     torch.testing.assert_close(c[:, 0], full[:, 6], rtol=1e-4, atol=1e-4)
 
 
+def test_device_position_decode_matches_host_position():
+    """One-token steps with the position held in a device tensor (the CUDA-graph decode form) give the same
+    logits as steps with the host position."""
+    from verl_omni_b200.ops.decode import KVCache
+
+    torch.manual_seed(0)
+    m = MoELLM(MoEConfig.tiny())
+    cfg = m.cfg
+    ids = torch.randint(0, 500, (2, 8))
+    mk = lambda: [KVCache(2, cfg.kv_heads, 8, cfg.head_dim, "cpu", torch.float32) for _ in m.layers]
+    ca, cb = mk(), mk()
+    m(ids[:, :5], caches=ca, pos0=0)
+    m(ids[:, :5], caches=cb, pos0=0)
+    m.rope(0, 8, "cpu")
+    pos = torch.zeros(1, dtype=torch.long)
+    for t in range(5, 8):
+        a = m(ids[:, t:t + 1], caches=ca, pos0=t)[:, -1]
+        pos.fill_(t)
+        b = m(ids[:, t:t + 1], caches=cb, pos_t=pos)[:, -1]
+        for c in cb:
+            c.len = t + 1
+        torch.testing.assert_close(b, a, rtol=1e-5, atol=1e-5)
+    for x, y in zip(ca, cb):
+        torch.testing.assert_close(y.k, x.k)
+        torch.testing.assert_close(y.v, x.v)
+
+
 def test_rollout_paged_cache_same_tokens():
     from verl_omni_b200.trainer.omni.omni_trainer import OmniGRPOTrainer
 
@@ -208,7 +235,7 @@ def test_expert_sharded_grpo_step_matches_unsharded(tmp_path):
         torch.testing.assert_close(part["wgu"], full["wgu"][r * E // 2:(r + 1) * E // 2], rtol=1e-3, atol=5e-5)
 
 
-def _main_omni(rank, world, ckpt, steps):
+def _main_omni(rank, world, ckpt, steps, par="actor_rollout_ref.actor.megatron.expert_model_parallel_size=2"):
     from verl_omni_b200.trainer.main_omni import run_omni
     from verl_omni_b200.utils.config import load_config
 
@@ -217,7 +244,7 @@ def _main_omni(rank, world, ckpt, steps):
         "actor_rollout_ref.rollout.n=4", "actor_rollout_ref.rollout.response_length=6",
         "data.prompt_text_tokens=5", "data.prompt_audio_tokens=3", "data.prompt_image_tokens=3",
         "actor_rollout_ref.actor.ppo_micro_batch_size_per_gpu=3",
-        "actor_rollout_ref.actor.megatron.expert_model_parallel_size=2", f"trainer.total_training_steps={steps}",
+        par, f"trainer.total_training_steps={steps}",
         "trainer.save_freq=1", f"trainer.default_local_dir={ckpt}", "trainer.logger=[]"])
     hist = run_omni(cfg)
     if rank == 0:
@@ -238,6 +265,21 @@ def test_main_omni_ep2_checkpoint_resume(tmp_path):
     h1 = json.load(open(tmp_path / "hist_1.json"))
     h2 = json.load(open(tmp_path / "hist_2.json"))
     assert len(h1) == 1 and len(h2) == 1 and h2[0]["training/global_step"] == 2
+    assert all(abs(v) < 1e6 for v in h2[0].values())
+
+
+def test_main_omni_pp2_checkpoint_resume(tmp_path):
+    """The omni entry point with pipeline_model_parallel_size=2: each stage writes its shards under
+    ``actor/pp_rank_XX`` and a resumed run continues at step 2."""
+    import json
+
+    pp = "actor_rollout_ref.actor.megatron.pipeline_model_parallel_size=2"
+    run_ranks(_main_omni, 2, (str(tmp_path), 1, pp))
+    for s in range(2):
+        assert (tmp_path / "global_step_1" / "actor" / f"pp_rank_{s:02d}" / "model_world_size_1_rank_0.pt").exists()
+    run_ranks(_main_omni, 2, (str(tmp_path), 2, pp))
+    h2 = json.load(open(tmp_path / "hist_2.json"))
+    assert len(h2) == 1 and h2[0]["training/global_step"] == 2
     assert all(abs(v) < 1e6 for v in h2[0].values())
 
 
@@ -293,3 +335,48 @@ def _pp_check(rank, world, outdir):
 def test_pipeline_1f1b_two_stages_match_single_rank():
     """1F1B over 2 gloo stages (4 micro-batches) gives the single-rank loss and every parameter's gradient."""
     run_ranks(_pp_check, 2, ("",))
+
+
+def _omni_pp_step(rank, world, outdir, pp):
+    from verl_omni_b200.models.moe_llm import MoEConfig
+    from verl_omni_b200.trainer.omni.omni_trainer import OmniGRPOTrainer
+    from verl_omni_b200.workers.config.diffusion import DiffusionActorConfig
+
+    ac = DiffusionActorConfig()
+    ac.optim.lr = 1e-3
+    cfg = MoEConfig.tiny()
+    cfg.layers = 3
+    t = OmniGRPOTrainer(cfg, ac, device=torch.device("cpu"), n=4, response_len=5, micro_batch_size=3,
+                        pp_size=pp)
+    m = t.step(num_prompts=2)
+    out = {"m": {k: m[k] for k in ("actor/pg_loss", "actor/grad_norm", "critic/rewards/mean",
+                                   "rollout_corr/logprob_abs_diff_mean")},
+           "params": {f"{n}" if pp == 1 else _full_name(n, t.model): p.detach().clone()
+                      for n, p in t.model.named_parameters()}}
+    torch.save(out, f"{outdir}/pp{pp}_r{rank}.pt")
+
+
+def _full_name(n, stage):
+    if n.startswith("layers."):
+        i, rest = n.split(".", 2)[1:]
+        return f"layers.{int(i) + stage.lo}.{rest}"
+    return n
+
+
+def test_pipeline_parallel_grpo_step_matches_single_rank(tmp_path):
+    """The omni GRPO step with the model split into 2 pipeline stages (gloo ranks: layers [0, 2) + embedding
+    and towers, layer 2 + head): pipelined decode, forward-only old log-probs, 1F1B update over uneven
+    micro-batches (3 + 3 + 2 sequences) and the cross-stage gradient norm give the single-rank step's
+    losses, norm and updated parameters."""
+    run_ranks(_omni_pp_step, 1, (str(tmp_path), 1))
+    run_ranks(_omni_pp_step, 2, (str(tmp_path), 2))
+    ref = torch.load(tmp_path / "pp1_r0.pt")
+    seen = set()
+    for r in range(2):
+        part = torch.load(tmp_path / f"pp2_r{r}.pt")
+        for k, v in ref["m"].items():
+            assert abs(part["m"][k] - v) <= 1e-5 * max(1.0, abs(v)), (k, part["m"][k], v)
+        for n, p in part["params"].items():
+            torch.testing.assert_close(p, ref["params"][n], rtol=1e-4, atol=1e-6, msg=lambda s: f"{n}: {s}")
+            seen.add(n)
+    assert seen == set(ref["params"])

@@ -124,6 +124,7 @@ std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Ten
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "verl_omni_b200 sm_100a kernels";
   m.def("launch_count", &vo::launch_count);
+  m.def("count_launches", &vo::count_launch, "adds n to the launch counter (replayed CUDA graphs of counted kernels)");
   m.def("sde_step_fwd", &vo::sde_step_fwd, py::arg("x"), py::arg("v"), py::arg("sigma"), py::arg("sigma_prev"),
         py::arg("prev"), py::arg("noise"), py::arg("sigma_max"), py::arg("eta"), py::arg("type"), py::arg("seed"),
         py::arg("offset"), py::arg("want_logp"), py::arg("norm"), py::arg("row_seeds") = py::none());

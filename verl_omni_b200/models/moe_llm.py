@@ -135,7 +135,9 @@ class MoEBlock(nn.Module):
         wo = self.o_proj.weight[:, r * Hq * hd:(r + 1) * Hq * hd]
         return x + row_parallel_linear(o, wo, None, tp).view(B, Sl, D)
 
-    def attn(self, x, cos, sin, cache: Optional[dict], pos0: int):
+    def attn(self, x, cos, sin, cache: Optional[dict], pos0: int, pos_t: Optional[torch.Tensor] = None):
+        """``pos_t`` (int64 ``[1]`` on the device, one-token steps on a :class:`KVCache`): the position comes
+        from the device, nothing is read on the host (a step that can be captured in a CUDA graph)."""
         cfg = self.cfg
         B, S, D = x.shape
         hd = cfg.head_dim
@@ -145,6 +147,12 @@ class MoEBlock(nn.Module):
         q = LO.head_norm_rope(qp, 0, cfg.q_heads, self.q_norm, cos, sin, cfg.eps)  # [B, Hq, S, hd]
         k = LO.head_norm_rope(kvp, 0, cfg.kv_heads, self.k_norm, cos, sin, cfg.eps)  # [B, Hk, S, hd]
         v = kvp[..., cfg.kv_heads * hd:].view(B, S, cfg.kv_heads, hd).transpose(1, 2)
+        if pos_t is not None:
+            if not isinstance(cache, KVCache) or S != 1:
+                raise ValueError("device-position steps take one token against a contiguous KVCache")
+            cache.append_at(k, v, pos_t)
+            o = decode_attention(q[:, :, 0], cache.k, cache.v, cache.lens_at(pos_t))  # [B, Hq, hd]
+            return x + self.o_proj(o.reshape(B, 1, cfg.q_heads * hd))
         if isinstance(cache, KVCache):
             # preallocated cache: in-place append; one-token steps use the grouped-query decode kernel
             first = cache.len == 0
@@ -201,10 +209,10 @@ class MoEBlock(nn.Module):
         """SwiGLU of locally-owned experts for tokens already grouped by (global) expert id."""
         return _ffn_grouped(tokens, expert_ids - self.e0, self.w_gate_up, self.w_down)
 
-    def forward(self, x, cos, sin, cache=None, pos0: int = 0, ep=None, tp=None):
+    def forward(self, x, cos, sin, cache=None, pos0: int = 0, ep=None, tp=None, pos_t=None):
         if tp is not None:
             return self.moe(self.attn_tp(x, cos, sin, tp), ep)
-        return self.moe(self.attn(x, cos, sin, cache, pos0), ep)
+        return self.moe(self.attn(x, cos, sin, cache, pos0, pos_t), ep)
 
 
 def _ffn_grouped(tokens, expert_ids, w_gate_up, w_down):
@@ -307,14 +315,28 @@ class MoELLM(nn.Module):
         return x
 
     def forward(self, ids, positions=None, caches=None, pos0: int = 0, audio_feats=None, image_patches=None,
-                return_hidden: bool = False, targets: Optional[torch.Tensor] = None, temperature: float = 1.0):
+                return_hidden: bool = False, targets: Optional[torch.Tensor] = None, temperature: float = 1.0,
+                pos_t: Optional[torch.Tensor] = None):
         """Logits [B, S, V] (fp32); ``return_hidden``: the final hidden states; ``targets`` [B, S] (next-token
         ids per position): log p(target) [B, S] through the chunked vocabulary kernel, with no logits tensor
-        (under tensor parallelism each rank scores its own tokens and the log-probs are gathered)."""
+        (under tensor parallelism each rank scores its own tokens and the log-probs are gathered).
+
+        ``pos_t`` (int64 ``[1]`` on the device): a one-token decode step at that position against contiguous
+        caches, with the RoPE rows and the KV write position taken on the device (``rope`` must already
+        cover the position: the caller sizes the table before the step is captured)."""
         from verl_omni_b200.ops.vocab_logprob import token_logprobs_from_hidden
 
         cfg = self.cfg
         B, S = ids.shape
+        if pos_t is not None:
+            if caches is None or S != 1 or self._rope_cache is None:
+                raise ValueError("device-position steps need caches, one token and a sized RoPE table")
+            x = F.embedding(ids, self.embed)
+            cos, sin = self._rope_cache[0].index_select(0, pos_t), self._rope_cache[1].index_select(0, pos_t)
+            for i, blk in enumerate(self.layers):
+                x = blk(x, cos, sin, caches[i], 0, self.ep, pos_t=pos_t)
+            h = rms_norm(x, self.norm, cfg.eps)
+            return h if return_hidden else self.lm_head(h).float()
         x = self.embed_tokens(ids, audio_feats, image_patches) if pos0 == 0 else F.embedding(ids, self.embed)
         cos, sin = self.rope(pos0, S, ids.device)
         tp = self.tp if (self.tp is not None and caches is None and pos0 == 0 and self.tp.world > 1) else None
@@ -346,6 +368,52 @@ class MoELLM(nn.Module):
             return token_logprobs_from_hidden(h, self.lm_head.weight, targets, temperature)
         if return_hidden:
             return h
+        return self.lm_head(h).float()
+
+
+class MoEStage(nn.Module):
+    """One pipeline stage of a :class:`MoELLM`: layers ``[lo, hi)``; the first stage also holds the token
+    embedding and the audio / vision towers, the last the final norm and the vocabulary head.
+
+    Built from a whole model (the stages then hold exactly the parameters of the unsplit model, initialised
+    from the same generator state) whose other parts are dropped.  Counterpart of Megatron's
+    ``pipeline_model_parallel_size`` layer split used by the reference's omni Megatron trainer
+    (``trainer/config/_generated_omni_megatron_trainer.yaml:34-67``)."""
+
+    def __init__(self, full: MoELLM, lo: int, hi: int, first: bool, last: bool):
+        super().__init__()
+        self.cfg, self.lo, self.hi, self.first, self.last = full.cfg, int(lo), int(hi), bool(first), bool(last)
+        self.layers = nn.ModuleList(list(full.layers[lo:hi]))
+        if first:
+            self.embed, self.audio_tower, self.visual = full.embed, full.audio_tower, full.visual
+        if last:
+            self.norm, self.lm_head = full.norm, full.lm_head
+        self.ep, self.tp, self._rope_cache = full.ep, None, None
+
+    rope = MoELLM.rope
+    embed_tokens = MoELLM.embed_tokens
+
+    def forward(self, x, pos0: int = 0, caches=None, audio_feats=None, image_patches=None,
+                targets: Optional[torch.Tensor] = None, temperature: float = 1.0, last_only: bool = False):
+        """``x``: token ids ``[B, S]`` on the first stage, the previous stage's hidden states ``[B, S, D]``
+        otherwise.  Returns the hidden states on every stage but the last; there: log p(``targets``) when
+        given, else fp32 logits (of the last position only with ``last_only``)."""
+        from verl_omni_b200.ops.vocab_logprob import token_logprobs_from_hidden
+
+        cfg = self.cfg
+        if self.first:
+            ids = x
+            x = self.embed_tokens(ids, audio_feats, image_patches) if pos0 == 0 else F.embedding(ids, self.embed)
+        cos, sin = self.rope(pos0, x.shape[1], x.device)
+        for i, blk in enumerate(self.layers):
+            x = blk(x, cos, sin, None if caches is None else caches[i], pos0, self.ep)
+        if not self.last:
+            return x
+        h = rms_norm(x, self.norm, cfg.eps)
+        if targets is not None:
+            return token_logprobs_from_hidden(h, self.lm_head.weight, targets, temperature)
+        if last_only:
+            h = h[:, -1:].contiguous()
         return self.lm_head(h).float()
 
 

@@ -479,6 +479,36 @@ def bench_decode(a) -> list[dict]:
     return out
 
 
+def bench_rollout_decode(a) -> list[dict]:
+    """Thinker decode steps at full Qwen3-Omni-30B-A3B width (hidden 2048, 32 / 4 heads of 128, 128 experts,
+    top-8, vocab 151936) with ``--layers`` layers: ``--B`` sequences, ``--S``-token prompts, greedy.  The time
+    per decode step is (generate with ``--new`` tokens - generate with 1 token) / (``--new`` - 1), eager steps
+    vs the step captured as one CUDA graph (``VO_DECODE_GRAPH``)."""
+    import os
+
+    from verl_omni_b200.models.moe_llm import MoEConfig, MoELLM
+    from verl_omni_b200.utils.dataproto import DataProto
+    from verl_omni_b200.workers.rollout.llm_rollout import LLMRolloutEngine
+
+    cfg = MoEConfig(layers=a.layers, audio_layers=1, vision_layers=1)
+    torch.manual_seed(0)
+    with torch.device("cuda"):
+        m = MoELLM(cfg).to(torch.bfloat16).eval()
+    batch = DataProto({"input_ids": torch.randint(0, 150000, (a.B, a.S))}, {})
+    out = []
+    for mode in ("0", "1"):
+        os.environ["VO_DECODE_GRAPH"] = mode
+        t = {}
+        for n in (1, a.new):
+            eng = LLMRolloutEngine(m, max_new_tokens=n, temperature=0.0, device=torch.device("cuda"))
+            t[n] = timeit(lambda: eng.generate(batch, seed=0), max(2, a.iters // 4), warmup=1)
+        step = (t[a.new] - t[1]) / (a.new - 1)
+        out.append({"op": "rollout_decode_step", "graph": mode == "1", "layers": a.layers, "B": a.B, "prompt": a.S,
+                    "new_tokens": a.new, "ms_per_step": round(step, 3), "ms_per_layer": round(step / a.layers, 4)})
+    os.environ["VO_DECODE_GRAPH"] = "1"
+    return out
+
+
 def bench_groupnorm(a) -> list[dict]:
     """VAE-decoder GroupNorm(32)+SiLU on channels-last [8, 128, 512, 512] bf16 (one read + one write pass
     after the statistics pass)."""
@@ -496,7 +526,7 @@ def bench_groupnorm(a) -> list[dict]:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "gemm_sweep", "gemm_pair", "ulysses", "tp", "fmha", "sde", "adaln", "optstep", "moe", "groupnorm", "decode"])
+    ap.add_argument("op", choices=["gemm", "gemm_sweep", "gemm_pair", "ulysses", "tp", "fmha", "sde", "adaln", "optstep", "moe", "groupnorm", "decode", "rollout_decode"])
     ap.add_argument("--numel", type=int, default=2_240_000_000)
     ap.add_argument("--M", type=int, default=21712)
     ap.add_argument("--N", type=int, default=6144)
@@ -508,9 +538,11 @@ def main() -> None:
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--only", default="")
     ap.add_argument("--compare", action="store_true")
+    ap.add_argument("--layers", type=int, default=8)
+    ap.add_argument("--new", type=int, default=64)
     a = ap.parse_args()
     pk = _peaks()
-    rows = {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "gemm_pair": bench_gemm_pair, "ulysses": bench_ulysses, "tp": bench_tp, "fmha": bench_fmha, "optstep": bench_optstep, "sde": bench_sde, "adaln": bench_adaln, "moe": bench_moe, "groupnorm": bench_groupnorm, "decode": bench_decode}[a.op](a)
+    rows = {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "gemm_pair": bench_gemm_pair, "ulysses": bench_ulysses, "tp": bench_tp, "fmha": bench_fmha, "optstep": bench_optstep, "sde": bench_sde, "adaln": bench_adaln, "moe": bench_moe, "groupnorm": bench_groupnorm, "decode": bench_decode, "rollout_decode": bench_rollout_decode}[a.op](a)
     for r in rows:
         if "tflops" in r:
             r[f"frac_of_{pk['src']}_gemm_peak"] = round(r["tflops"] / pk["tflops"], 3)

@@ -52,6 +52,18 @@ class KVCache:
     def lens(self) -> torch.Tensor:
         return torch.full((self.k.shape[0],), self.len, dtype=torch.int32, device=self.k.device)
 
+    def append_at(self, k: torch.Tensor, v: torch.Tensor, pos_t: torch.Tensor) -> None:
+        """One-token step written at the position held on the device (``pos_t`` int64 ``[1]``): k / v
+        ``[B, Hk, 1, hd]``.  Neither the host counter nor any host value is read, so the step can be captured
+        in a CUDA graph once and replayed at every later position; the caller keeps ``len`` in step and keeps
+        the position below ``max_len``."""
+        self.k.index_copy_(2, pos_t, k)
+        self.v.index_copy_(2, pos_t, v)
+
+    def lens_at(self, pos_t: torch.Tensor) -> torch.Tensor:
+        """Valid rows after a step at ``pos_t``: ``pos_t + 1`` for every sequence, int32 ``[B]`` (device)."""
+        return (pos_t + 1).to(torch.int32).expand(self.k.shape[0]).contiguous()
+
 
 class PagedKVCache:
     """Paged K / V storage of one layer: pools ``[num_blocks, Hk, block_size, hd]``, a host-side free list and

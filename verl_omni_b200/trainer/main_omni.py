@@ -2,8 +2,9 @@
 
 Counterpart of ``verl_omni/trainer/main_omni.py:57-360`` (Hydra config ``omni_trainer``): the config tree
 ``trainer/config/omni_trainer.yaml`` with the same override syntax; one process per GPU under ``torchrun``
-instead of Ray workers.  ``actor_rollout_ref.actor.megatron.{tensor,expert}_model_parallel_size`` set the
-TP (attention heads + sequence, consecutive ranks) and EP (experts sharded, consecutive ranks) sizes;
+instead of Ray workers.  ``actor_rollout_ref.actor.megatron.{tensor,expert,pipeline}_model_parallel_size`` set the
+TP (attention heads + sequence, consecutive ranks), EP (experts sharded, consecutive ranks) and PP (layer
+stages; stage s on ranks [s W / pp, (s + 1) W / pp)) sizes;
 checkpoints use the diffusion trainers' layout (``global_step_{N}/actor`` + expert slices) and resume with
 ``trainer.resume_mode=auto``.
 """
@@ -50,12 +51,13 @@ def build_omni_trainer(config):
     W = D.world_size()
     tp = int(act.megatron.tensor_model_parallel_size)
     ep = int(act.megatron.expert_model_parallel_size)
-    for name, n in (("tensor", tp), ("expert", ep)):
+    pp = int(act.megatron.pipeline_model_parallel_size)
+    for name, n in (("tensor", tp), ("expert", ep), ("pipeline", pp)):
         if n < 1 or W % n:
             raise ValueError(f"{name}_model_parallel_size={n} must divide the world size {W}")
     tp_group = D.make_hsdp_groups(tp)[0] if tp > 1 else None
     ep_group = D.make_hsdp_groups(ep)[0] if ep > 1 else None
-    dp = W // tp
+    dp = W // tp // pp
     gbs = int(config.data.train_batch_size)
     if gbs % dp:
         raise ValueError(f"data.train_batch_size={gbs} must be divisible by the data-parallel size {dp}")
@@ -68,7 +70,7 @@ def build_omni_trainer(config):
         response_len=int(ro.response_length), loss_mode=str(act.policy_loss.loss_mode), ep_group=ep_group,
         tp_group=tp_group, seed=int(config.data.seed), micro_batch_size=int(act.ppo_micro_batch_size_per_gpu),
         temperature=float(ro.temperature), kv_block_size=int(ro.kv_block_size),
-        total_steps=int(config.trainer.total_training_steps))
+        total_steps=int(config.trainer.total_training_steps), pp_size=pp)
     trainer.prompts_per_rank = gbs // dp
     return trainer
 

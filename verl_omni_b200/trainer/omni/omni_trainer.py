@@ -33,8 +33,15 @@ class OmniGRPOTrainer:
                  prompt_text: int = 16, audio_tokens: int = 4, image_tokens: int = 4, response_len: int = 8,
                  loss_mode: str = "grpo", ep_group=None, tp_group=None, seed: int = 0,
                  micro_batch_size: Optional[int] = None, temperature: float = 1.0, kv_block_size: int = 0,
-                 total_steps: int = 1000):
+                 total_steps: int = 1000, pp_size: int = 1):
+        """``pp_size > 1``: pipeline parallelism over ``pp_size`` stages (rank r is stage r // (world / pp) of
+        data-parallel rank r % (world / pp)); each stage holds a contiguous slice of the layers, the rollout
+        decodes through the stages and the update runs the 1F1B schedule over the micro-batches."""
         torch.manual_seed(seed)
+        self.pp_size = int(pp_size)
+        if self.pp_size > 1 and ((ep_group is not None and D.world_size(ep_group) > 1)
+                                 or (tp_group is not None and D.world_size(tp_group) > 1)):
+            raise ValueError("pipeline parallelism is combined with data parallelism only (no EP / TP groups)")
         self.micro_batch_size = micro_batch_size  # sequences per forward/backward (None: the whole batch)
         self.cfg, self.actor_cfg, self.device, self.n = cfg, actor_cfg, device, n
         self.prompt_text, self.audio_tokens, self.image_tokens = prompt_text, audio_tokens, image_tokens
@@ -60,16 +67,36 @@ class OmniGRPOTrainer:
             from verl_omni_b200.parallel.tensor_parallel import TPContext
 
             self.model.tp = TPContext(tp_group)
+        self.pp = None
+        dp_group = None
+        if self.pp_size > 1:
+            from verl_omni_b200.models.moe_llm import MoEStage
+            from verl_omni_b200.parallel.pipeline import PipeLink, stage_layers
+
+            W = D.world_size()
+            if W % self.pp_size or cfg.layers < self.pp_size:
+                raise ValueError(f"pipeline_model_parallel_size={self.pp_size} must divide the world size {W} "
+                                 f"and not exceed the layer count {cfg.layers}")
+            dpn = W // self.pp_size
+            dp_group, pp_group = D.make_hsdp_groups(dpn)  # same-stage ranks, and the ranks of one pipeline
+            s_idx = D.rank() // dpn
+            lo, hi = stage_layers(cfg.layers, self.pp_size, s_idx)
+            self.model = MoEStage(self.model, lo, hi, s_idx == 0, s_idx == self.pp_size - 1)
+            self.pp = PipeLink(s_idx, self.pp_size, [D.rank() % dpn + k * dpn for k in range(self.pp_size)],
+                               pp_group, device)
         self.engine = ShardedEngine(self.model, actor_cfg, device=device, total_steps=total_steps,
-                                    expert_group=self.expert_dp_group)
+                                    expert_group=self.expert_dp_group, group=dp_group, pp_size=self.pp_size)
         self.rollout = LLMRolloutEngine(self.model, max_new_tokens=response_len, device=device,
-                                        temperature=temperature, kv_block_size=kv_block_size)
+                                        temperature=temperature, kv_block_size=kv_block_size, pp=self.pp)
         self.temperature = temperature
         self.loss_fn = get_omni_loss_fn(loss_mode)
         self.loss_mode = loss_mode
         self.step_count = 0
         self.rank = D.rank()
         self.dp_rank, self.dp = self.rank // self.tp_size, D.world_size() // self.tp_size
+        if self.pp is not None:
+            self.dp = D.world_size() // self.pp_size
+            self.dp_rank = self.rank % self.dp
 
     def make_prompts(self, num: int, seed: int) -> DataProto:
         g = torch.Generator().manual_seed(seed)
@@ -101,6 +128,8 @@ class OmniGRPOTrainer:
     def step(self, num_prompts: int = 2) -> dict:
         """One GRPO / GSPO step on ``num_prompts`` prompts x ``n`` responses of this data-parallel rank:
         rollout -> rule reward -> group advantage -> old log-probs -> micro-batched update -> optimizer."""
+        if self.pp is not None:
+            return self._step_pp(num_prompts)
         self.step_count += 1
         t0 = time.perf_counter()
         timing = {}
@@ -149,6 +178,94 @@ class OmniGRPOTrainer:
                                                          D.world_size()))
         return m
 
+    # ------------------------------------------------------------------ pipeline parallel step
+    def _stage_fn(self, data: DataProto, slices, with_loss: bool, old=None, adv=None, mask=None, total=None,
+                  store=None):
+        """This stage's computation of micro-batch ``i``: the first stage embeds the prompt + response ids
+        (and the multimodal features), every stage runs its layers, the last computes the response
+        log-probs (and, ``with_loss``, the weighted policy loss)."""
+        st = self.model
+        ids = data.batch["input_ids"].to(self.device)
+        P = data.batch["prompts"].shape[1]
+        af, ip = data.batch["audio_feats"].to(self.device), data.batch["image_patches"].to(self.device)
+        seq_level = self.loss_mode == "gspo"
+
+        def fn(x, i):
+            sl = slices[i]
+            tgt = None
+            if st.last:
+                tgt = torch.zeros_like(ids[sl, :-1])
+                tgt[:, P - 1:] = ids[sl, P:]
+            if st.first:
+                x = ids[sl, :-1]
+            y = st(x, audio_feats=af[sl] if st.first else None, image_patches=ip[sl] if st.first else None,
+                   targets=tgt, temperature=self.temperature)
+            if not st.last:
+                return y
+            lp = y[:, P - 1:]
+            if not with_loss:
+                return lp
+            mk = mask[sl]
+            loss, m = self.loss_fn(lp, old[i], adv[sl], mk)
+            w = (mk.shape[0] if seq_level else float(mk.sum().clamp_min(1))) / total
+            store.append(m)
+            return loss * w
+
+        return fn
+
+    def _step_pp(self, num_prompts: int) -> dict:
+        """The GRPO / GSPO step with the model split into pipeline stages: pipelined decode, forward-only
+        old log-probs over the stages, 1F1B update, one optimizer step per stage with the gradient norm of the
+        whole model; the last stage's metrics are broadcast to the pipeline."""
+        from verl_omni_b200.parallel.pipeline import PipelineStage
+
+        self.step_count += 1
+        t0 = time.perf_counter()
+        timing = {}
+        link = self.pp
+        prompts = self.make_prompts(num_prompts, seed=1000 * self.step_count + self.dp_rank).repeat(self.n)
+        tg = time.perf_counter()
+        out = self.rollout.generate(prompts, seed=self.step_count)
+        rewards = hash_token_reward(out, seed=7).to(self.device)
+        adv = group_normalize(rewards, out.non_tensor_batch["uid"], global_std=False)
+        mask = out.batch["response_mask"].to(self.device)
+        self._sync()
+        timing["gen"] = time.perf_counter() - tg
+        slices = self._micro(out)
+        Lm1 = out.batch["input_ids"].shape[1] - 1
+        shape = lambda i: (slices[i].stop - slices[i].start, Lm1, self.cfg.hidden)
+        stage = PipelineStage(None, link.s, link.S, link.ranks, shape, shape, self.engine.dtype, self.device)
+        tg = time.perf_counter()
+        old = stage.forward_only(len(slices), self._stage_fn(out, slices, False))
+        self._sync()
+        timing["old_log_prob"] = time.perf_counter() - tg
+        tg = time.perf_counter()
+        self.engine.train_mode()
+        self.engine.zero_grad()
+        seq_level = self.loss_mode == "gspo"
+        total = float(mask.shape[0]) if seq_level else float(mask.sum().clamp_min(1))
+        ms: list = []
+        stage.fn = self._stage_fn(out, slices, True, old, adv, mask, total, ms)
+        losses = stage.run(len(slices))
+        norm = self.engine.optimizer_step()
+        self._sync()
+        timing["update_actor"] = time.perf_counter() - tg
+        m = {}
+        if link.last:
+            m = {k: float(np.mean([x[k] for x in ms])) for k in ms[0]}
+            oldc = torch.cat(old, 0)
+            m.update({"actor/pg_loss": float(torch.stack(losses).sum()),
+                      "rollout_corr/logprob_abs_diff_mean": float(
+                          ((oldc - out.batch["rollout_log_probs"].to(self.device)).abs() * mask).sum() / mask.sum())})
+        m = D.broadcast_object(m, src=link.ranks[-1], group=link.group)
+        m.update({"actor/grad_norm": float(norm.reshape(())), "actor/lr": self.engine.lr(),
+                  "critic/rewards/mean": float(rewards.mean()), "training/global_step": self.step_count,
+                  "response_length/mean": float(mask.sum(-1).mean())})
+        m.update(M.compute_timing_metrics_diffusion(timing, len(out)))
+        m.update(M.compute_throughput_metrics_diffusion(time.perf_counter() - t0, len(out) * self.dp,
+                                                         D.world_size()))
+        return m
+
     def _sync(self) -> None:
         if self.device.type == "cuda":
             torch.cuda.synchronize(self.device)
@@ -160,13 +277,20 @@ class OmniGRPOTrainer:
         import os
 
         root = os.path.join(root_dir, f"global_step_{self.step_count}")
-        self.engine.save_checkpoint(os.path.join(root, "actor"), self.step_count)
+        self.engine.save_checkpoint(self._actor_dir(root), self.step_count)
         if D.rank() == 0:
             torch.save({"global_step": self.step_count}, os.path.join(root, "data.pt"))
             with open(os.path.join(root_dir, "latest_checkpointed_iteration.txt"), "w") as f:
                 f.write(str(self.step_count))
         D.barrier()
         return root
+
+    def _actor_dir(self, root: str) -> str:
+        """``actor`` (``actor/pp_rank_{s:02d}`` per stage under pipeline parallelism: each stage's shards)."""
+        import os
+
+        d = os.path.join(root, "actor")
+        return d if self.pp is None else os.path.join(d, f"pp_rank_{self.pp.s:02d}")
 
     def load_checkpoint(self, root_dir: str) -> bool:
         import os
@@ -176,7 +300,7 @@ class OmniGRPOTrainer:
             return False
         with open(marker) as f:
             root = os.path.join(root_dir, f"global_step_{int(f.read().strip())}")
-        self.engine.load_checkpoint(os.path.join(root, "actor"))
+        self.engine.load_checkpoint(self._actor_dir(root))
         self.step_count = int(torch.load(os.path.join(root, "data.pt"))["global_step"])
         return True
 

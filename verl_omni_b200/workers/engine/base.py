@@ -195,8 +195,11 @@ class ShardedEngine:
     """Owns a module, its flat parameters and the sharded AdamW state."""
 
     def __init__(self, module: nn.Module, actor_cfg, *, device: torch.device, group=None, total_steps: int = 1,
-                 trainable: bool = True, expert_group=None):
+                 trainable: bool = True, expert_group=None, pp_size: int = 1):
+        """``pp_size > 1``: ``module`` is one pipeline stage and ``group`` the ranks holding the same stage; the
+        gradient norm for clipping is then reduced over every rank (all stages)."""
         self.cfg = actor_cfg
+        self.pp_size = int(pp_size)
         self.group = group if group is not None else D.default_group()
         # expert-parallel parameters (marked ``_vo_expert``: each rank holds only its experts' slices) live in
         # a second flat set sharded over ``expert_group`` -- the ranks that hold the same experts
@@ -231,7 +234,7 @@ class ShardedEngine:
                 raise ValueError("expert-parallel parameters with HSDP replicas are not supported")
             not_expert = (lambda n, p: not getattr(p, "_vo_expert", False)) if has_experts else None
             self.flat = FlatParams(module, self.dtype, device, self.world, self.rank, self.group,
-                                   symmetric=(not has_experts and self.replica_group is None
+                                   symmetric=(not has_experts and self.replica_group is None and self.pp_size == 1
                                               and self._want_symmetric(actor_cfg, device, self.group)),
                                    select=not_expert)
             if has_experts:
@@ -311,7 +314,7 @@ class ShardedEngine:
         max_norm = float(self.cfg.grad_clip if self.cfg.grad_clip is not None else oc.clip_grad)
         # the dense and expert shards partition the parameters over the world: one all-reduce of the local
         # squared norms gives the global norm
-        norm_group = self.group if ef is None else None
+        norm_group = self.group if (ef is None and self.pp_size == 1) else None
         if fp.master.is_cuda:
             sq = ext().sq_norm(fp.grad_shard)
             if ef is not None:
