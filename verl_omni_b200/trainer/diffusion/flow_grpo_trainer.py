@@ -172,8 +172,11 @@ class PolicyGradientTrainer:
             torch.manual_seed(seed)
         self.ref = None
         if ref_module is not None:
+            # ref.fsdp_config.param_offload (or the actor's): the frozen reference waits on the host between uses
+            rfc = ((config.actor_rollout_ref.get("ref", {}) or {}).get("fsdp_config", {}) or {})
+            ref_off = bool(rfc.get("param_offload", False)) or bool(self.actor_cfg.fsdp_config.param_offload)
             self.ref = PPODiffusionEngine(ref_module, self.adapter, self.scheduler, self.actor_cfg, self.model_cfg,
-                                          device=self.device, trainable=False)
+                                          device=self.device, trainable=False, param_offload=ref_off)
         dt = self.actor.engine.dtype
         self.text_encoder = None
         if self.spec.text_encoder is not None:

@@ -136,11 +136,49 @@ class FlatParams:
     @staticmethod
     def _accumulate(p: torch.Tensor) -> None:
         if p.grad is not None:
+            if p.main_grad is None:
+                raise RuntimeError("backward after the gradient buffer was released: call the engine's zero_grad "
+                                   "before the update's first backward")
             p.main_grad.add_(p.grad.view_as(p.main_grad))
             p.grad = None
 
     def zero_grad(self) -> None:
+        if self.main_grad is None:  # released by ``release_grads``: re-created zeroed and re-bound
+            self.main_grad = torch.zeros(self.padded, dtype=torch.float32, device=self.device)
+            for p, o, n, s in zip(self.params, self.offsets, self.numels, self.shapes):
+                p.main_grad = self.main_grad[o:o + n].view(s)
+            return
         self.main_grad.zero_()
+
+    # ------------------------------------------------------------------ host offload
+    def release_grads(self) -> None:
+        """Drops the full-size fp32 gradient buffer (between updates it holds nothing: every update starts
+        with ``zero_grad``, which re-creates it).  Peer-mapped gradient buffers stay."""
+        if self.symm_grad is not None or self.main_grad is None:
+            return
+        self.main_grad = None
+        for p in self.params:
+            p.main_grad = None
+
+    _OPT_STATE = ("master", "exp_avg", "exp_avg_sq", "grad_shard")
+
+    def offload_optimizer(self) -> None:
+        """fp32 master shard, AdamW moments and the gradient shard to pinned host memory (the device copies
+        are released); ``load_optimizer`` brings them back."""
+        if self.device.type != "cuda" or not self.master.is_cuda:
+            return
+        for k in self._OPT_STATE:
+            t = getattr(self, k)
+            h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+            h.copy_(t, non_blocking=True)
+            setattr(self, k, h)
+        torch.cuda.current_stream(self.device).synchronize()  # host copies complete before anyone reads them
+
+    def load_optimizer(self) -> None:
+        if self.device.type != "cuda" or self.master.is_cuda:
+            return
+        for k in self._OPT_STATE:
+            setattr(self, k, getattr(self, k).to(self.device, non_blocking=True))
 
     def shard_view(self) -> torch.Tensor:
         return self.flat[self.shard_lo:self.shard_lo + self.shard_size]
@@ -195,7 +233,7 @@ class ShardedEngine:
     """Owns a module, its flat parameters and the sharded AdamW state."""
 
     def __init__(self, module: nn.Module, actor_cfg, *, device: torch.device, group=None, total_steps: int = 1,
-                 trainable: bool = True, expert_group=None, pp_size: int = 1):
+                 trainable: bool = True, expert_group=None, pp_size: int = 1, param_offload: Optional[bool] = None):
         """``pp_size > 1``: ``module`` is one pipeline stage and ``group`` the ranks holding the same stage; the
         gradient norm for clipping is then reduced over every rank (all stages)."""
         self.cfg = actor_cfg
@@ -244,6 +282,50 @@ class ShardedEngine:
         self.opt_step = 0
         self.sched = LRSchedule(actor_cfg.optim, total_steps) if trainable else None
         self.last_grad_norm = None
+        fc = actor_cfg.fsdp_config
+        self.optimizer_offload = bool(getattr(fc, "optimizer_offload", False)) and device.type == "cuda"
+        po = getattr(fc, "param_offload", False) if param_offload is None else param_offload
+        self.param_offload = bool(po) and device.type == "cuda"
+        self._host_params = None
+        if trainable:
+            self._after_update()
+
+    def _flats(self) -> list:
+        return [f for f in (self.flat, self.eflat) if f is not None]
+
+    def _after_update(self) -> None:
+        """Between updates: optimizer state to the host (``optimizer_offload``), gradient buffers released
+        (``param_offload``; the bf16 weights stay, the colocated rollout reads them in place)."""
+        for f in self._flats():
+            if self.optimizer_offload:
+                f.offload_optimizer()
+            if self.param_offload:
+                f.release_grads()
+
+    def _before_update(self) -> None:
+        for f in self._flats():
+            f.load_optimizer()
+
+    # frozen engines (reference policy, distillation teacher): weights on the host while idle
+    def offload_params(self) -> None:
+        """``param_offload`` on a frozen engine: its weights move to pinned host memory until ``load_params``
+        (reference / teacher models are read in one phase of the step and idle in the others)."""
+        if self.trainable or not self.param_offload or self._host_params is not None:
+            return
+        self._host_params = []
+        for p in self.module.parameters():
+            h = torch.empty(p.shape, dtype=p.dtype, pin_memory=True)
+            h.copy_(p.data, non_blocking=True)
+            self._host_params.append((p, h))
+            p.data = h
+        torch.cuda.current_stream(self.device).synchronize()
+
+    def load_params(self) -> None:
+        if self._host_params is None:
+            return
+        for p, h in self._host_params:
+            p.data = h.to(self.device, non_blocking=True)
+        self._host_params = None
 
     def _want_symmetric(self, actor_cfg, device, group) -> bool:
         """``fsdp_config.fused_collectives``: "auto" (on for NCCL ranks of one node), "on", "off"."""
@@ -267,10 +349,8 @@ class ShardedEngine:
         return self
 
     def zero_grad(self) -> None:
-        if self.flat is not None:
-            self.flat.zero_grad()
-        if self.eflat is not None:
-            self.eflat.zero_grad()
+        for f in self._flats():
+            f.zero_grad()
 
     # ------------------------------------------------------------------ optimizer
     def optimizer_step(self) -> torch.Tensor:
@@ -278,6 +358,13 @@ class ShardedEngine:
 
         Returns the global grad norm as a device scalar (non-finite -> the update is skipped on device).
         """
+        self._before_update()
+        try:
+            return self._optimizer_step()
+        finally:
+            self._after_update()
+
+    def _optimizer_step(self) -> torch.Tensor:
         fp = self.flat
         oc = self.cfg.optim
         if fp.symm_grad is not None:
@@ -363,6 +450,20 @@ class ShardedEngine:
     # ------------------------------------------------------------------ checkpoints
     def save_checkpoint(self, local_path: str, global_step: int = 0, save_contents=("model", "optimizer", "extra"),
                         hf_export: bool = False) -> None:
+        self._before_update()  # offloaded optimizer state back on the device for the collectives below
+        try:
+            self._save_checkpoint(local_path, global_step, save_contents, hf_export)
+        finally:
+            self._after_update()
+
+    def load_checkpoint(self, local_path: str, load_contents=("model", "optimizer", "extra")) -> dict:
+        self._before_update()
+        try:
+            return self._load_checkpoint(local_path, load_contents)
+        finally:
+            self._after_update()
+
+    def _save_checkpoint(self, local_path: str, global_step: int, save_contents, hf_export: bool) -> None:
         os.makedirs(local_path, exist_ok=True)
         W, r = self.world, self.rank
         fp = self.flat
@@ -415,7 +516,7 @@ class ShardedEngine:
                            "replicas": self.n_replicas}, f)
         D.barrier()
 
-    def load_checkpoint(self, local_path: str, load_contents=("model", "optimizer", "extra")) -> dict:
+    def _load_checkpoint(self, local_path: str, load_contents) -> dict:
         with open(os.path.join(local_path, "fsdp_config.json")) as f:
             meta = json.load(f)
         Wsaved = int(meta["world_size"])

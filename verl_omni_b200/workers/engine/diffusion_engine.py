@@ -68,9 +68,9 @@ class PPODiffusionEngine:
     """Actor (or frozen ref) DiT with the PPO-style per-timestep training loop."""
 
     def __init__(self, module, adapter: type[DiffusionModelBase], scheduler, actor_cfg, model_cfg, *, device,
-                 group=None, total_steps: int = 1, trainable: bool = True):
+                 group=None, total_steps: int = 1, trainable: bool = True, param_offload: Optional[bool] = None):
         self.engine = ShardedEngine(module, actor_cfg, device=device, group=group, total_steps=total_steps,
-                                    trainable=trainable)
+                                    trainable=trainable, param_offload=param_offload)
         self.module = module
         self.adapter = adapter
         self.scheduler = scheduler
@@ -80,6 +80,7 @@ class PPODiffusionEngine:
         # sequence-parallel ranks each back-propagate their own tokens' share: the loss is scaled by sp so the
         # world-averaged gradient equals the data-parallel average
         self.sp = int(getattr(actor_cfg.fsdp_config, "ulysses_sequence_parallel_size", 1) or 1)
+        self.engine.offload_params()  # frozen engine with param_offload: on the host until its phase runs
 
     # ------------------------------------------------------------------ helpers
     def _micro_batches(self, data: DataProto, mbs: Optional[int]) -> list[DataProto]:
@@ -112,6 +113,13 @@ class PPODiffusionEngine:
         """Per-step outputs for every trajectory: ``log_probs`` [B, T] and optionally
         ``prev_sample_mean`` [B, T, ...] (reference/old means for KL, DPPO, GRPO-Guard)."""
         self.engine.eval_mode()
+        self.engine.load_params()
+        try:
+            return self._infer(data, keys, micro_batch_size)
+        finally:
+            self.engine.offload_params()
+
+    def _infer(self, data: DataProto, keys, micro_batch_size: Optional[int]) -> DataProto:
         T = data.batch["step_index"].shape[1]
         outs = defaultdict(list)
         for mb in self._micro_batches(data, micro_batch_size or self.cfg.ppo_micro_batch_size_per_gpu):
