@@ -268,6 +268,17 @@ def test_main_omni_ep2_checkpoint_resume(tmp_path):
     assert all(abs(v) < 1e6 for v in h2[0].values())
 
 
+def test_main_omni_rollout_tp2(tmp_path):
+    """The omni entry point with the rollout decoding tensor-parallel over both ranks: the rollout's log-probs
+    agree with the trainer's (replicated-weight) recompute."""
+    import json
+
+    run_ranks(_main_omni, 2, (str(tmp_path), 1, "actor_rollout_ref.rollout.tensor_model_parallel_size=2"))
+    h1 = json.load(open(tmp_path / "hist_1.json"))
+    assert len(h1) == 1 and all(abs(v) < 1e6 for v in h1[0].values())
+    assert h1[0]["rollout_corr/logprob_abs_diff_mean"] < 1e-4
+
+
 def test_main_omni_pp2_checkpoint_resume(tmp_path):
     """The omni entry point with pipeline_model_parallel_size=2: each stage writes its shards under
     ``actor/pp_rank_XX`` and a resumed run continues at step 2."""
@@ -380,3 +391,54 @@ def test_pipeline_parallel_grpo_step_matches_single_rank(tmp_path):
             torch.testing.assert_close(p, ref["params"][n], rtol=1e-4, atol=1e-6, msg=lambda s: f"{n}: {s}")
             seen.add(n)
     assert seen == set(ref["params"])
+
+
+def _tp_rollout_check(rank, world):
+    import torch.distributed as dist
+
+    from verl_omni_b200.parallel.tensor_parallel import TPContext
+    from verl_omni_b200.utils.dataproto import DataProto
+    from verl_omni_b200.workers.rollout.llm_rollout import LLMRolloutEngine
+
+    torch.manual_seed(0)
+    cfg = MoEConfig.tiny()
+    m = MoELLM(cfg)
+    g = torch.Generator().manual_seed(100 + rank)
+    n, P = 3, 6
+    ids = torch.cat([torch.randint(0, 500, (n, P - 2), generator=g), torch.full((n, 1), cfg.audio_token),
+                     torch.full((n, 1), cfg.image_token)], 1)
+    batch = DataProto({"input_ids": ids, "audio_feats": torch.randn(n, 1, cfg.audio_mel, generator=g),
+                       "image_patches": torch.randn(n, 1, cfg.vision_patch_dim, generator=g)}, {})
+    tp = LLMRolloutEngine(m, max_new_tokens=5, temperature=0.0, device=torch.device("cpu"),
+                          tp=TPContext(dist.group.WORLD))
+    ref = LLMRolloutEngine(m, max_new_tokens=5, temperature=0.0, device=torch.device("cpu"))
+    a, b = tp.generate(batch, seed=1), ref.generate(batch, seed=1)
+    assert torch.equal(a.batch["responses"], b.batch["responses"])
+    assert torch.equal(a.batch["prompts"], ids)
+    torch.testing.assert_close(a.batch["rollout_log_probs"], b.batch["rollout_log_probs"], rtol=1e-4, atol=1e-5)
+    # sampled decode: both ranks of the group draw the same tokens for the group's whole batch
+    import verl_omni_b200.workers.rollout.llm_rollout as LR
+
+    drawn, orig = [], LR.sample_tokens
+
+    def rec(*a, **k):
+        out = orig(*a, **k)
+        drawn.append(out[0].clone())
+        return out
+
+    LR.sample_tokens = rec
+    try:
+        tp.temperature = 1.0
+        tp.generate(batch, seed=3)
+    finally:
+        LR.sample_tokens = orig
+    mine = torch.stack(drawn)  # [steps, group batch]
+    both = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(both, mine)
+    assert mine.shape[1] == world * n and torch.equal(both[0], both[1])
+
+
+def test_tensor_parallel_rollout_tp2_gloo():
+    """Rollout decode with attention heads (and KV caches) split over a TP=2 group: greedy tokens and log-probs
+    equal the replicated-weight decode of the same prompts."""
+    run_ranks(_tp_rollout_check, 2)

@@ -28,6 +28,7 @@ from verl_omni_b200.ops import llm as LO
 from verl_omni_b200.ops.attention import attention
 from verl_omni_b200.ops import linear as L
 from verl_omni_b200.ops.decode import KVCache, PagedView, decode_attention
+from verl_omni_b200.parallel import dist as D_
 
 
 @dataclass
@@ -135,6 +136,54 @@ class MoEBlock(nn.Module):
         wo = self.o_proj.weight[:, r * Hq * hd:(r + 1) * Hq * hd]
         return x + row_parallel_linear(o, wo, None, tp).view(B, Sl, D)
 
+    def _tp_weights(self, tp):
+        """This rank's slices of the attention weights (q / k / v rows of its heads, o_proj columns),
+        contiguous copies kept until the weights change (their version counter, shared with the flat
+        parameter buffer, moves on every optimizer step)."""
+        cfg = self.cfg
+        hd, W, r = cfg.head_dim, tp.world, tp.rank
+        Hq, Hk = cfg.q_heads // W, cfg.kv_heads // W
+        key = (W, r, self.q_proj.weight._version, self.kv_proj.weight._version, self.o_proj.weight._version,
+               self.q_proj.weight.data_ptr())
+        c = getattr(self, "_tp_w", None)
+        if c is None or c[0] != key:
+            kvw = self.kv_proj.weight.detach().view(2, cfg.kv_heads * hd, -1)
+            qkv = torch.cat([self.q_proj.weight.detach()[r * Hq * hd:(r + 1) * Hq * hd],
+                             kvw[0, r * Hk * hd:(r + 1) * Hk * hd], kvw[1, r * Hk * hd:(r + 1) * Hk * hd]], 0)
+            wo = self.o_proj.weight.detach()[:, r * Hq * hd:(r + 1) * Hq * hd].contiguous()
+            c = self._tp_w = (key, qkv, wo)
+        return c[1], c[2]
+
+    def attn_tp_decode(self, x, cos, sin, cache: KVCache, tp):
+        """Tensor-parallel attention for the rollout (no autograd): every rank of the TP group holds the
+        group's whole batch; rank r projects q / k / v for its ``q_heads / W`` and ``kv_heads / W`` heads, keeps
+        only those KV heads in its cache and attends over them; the output projection's partial sums (its
+        columns of ``o_proj``) are summed over the group by one all-reduce, so every rank continues with the
+        same hidden states (vLLM's tensor-parallel attention)."""
+        cfg = self.cfg
+        B, S, D = x.shape
+        hd, W = cfg.head_dim, tp.world
+        Hq, Hk = cfg.q_heads // W, cfg.kv_heads // W
+        wqkv, wo = self._tp_weights(tp)
+        h = rms_norm(x, self.ln1, cfg.eps)
+        y = L.linear(h, wqkv)  # [B, S, (Hq + 2 Hk) hd]
+        q = LO.head_norm_rope(y, 0, Hq, self.q_norm, cos, sin, cfg.eps)
+        k = LO.head_norm_rope(y, Hq * hd, Hk, self.k_norm, cos, sin, cfg.eps)
+        v = y[..., (Hq + Hk) * hd:].reshape(B, S, Hk, hd).transpose(1, 2)
+        first = cache.len == 0
+        cache.append(k, v)
+        if S == 1 and not first:
+            o = decode_attention(q[:, :, 0], cache.k, cache.v, cache.lens()).reshape(B, 1, Hq * hd)
+        else:
+            if not first:
+                k, v = cache.k[:, :, :cache.len], cache.v[:, :, :cache.len]
+            rep = Hq // Hk
+            o = attention(q.contiguous(), k.repeat_interleave(rep, 1).contiguous(),
+                          v.repeat_interleave(rep, 1).contiguous(), causal=first and S > 1)
+        part = L.linear(o.reshape(B, S, Hq * hd), wo)
+        D_.all_reduce(part, group=tp.group)
+        return x + part
+
     def attn(self, x, cos, sin, cache: Optional[dict], pos0: int, pos_t: Optional[torch.Tensor] = None):
         """``pos_t`` (int64 ``[1]`` on the device, one-token steps on a :class:`KVCache`): the position comes
         from the device, nothing is read on the host (a step that can be captured in a CUDA graph)."""
@@ -209,7 +258,9 @@ class MoEBlock(nn.Module):
         """SwiGLU of locally-owned experts for tokens already grouped by (global) expert id."""
         return _ffn_grouped(tokens, expert_ids - self.e0, self.w_gate_up, self.w_down)
 
-    def forward(self, x, cos, sin, cache=None, pos0: int = 0, ep=None, tp=None, pos_t=None):
+    def forward(self, x, cos, sin, cache=None, pos0: int = 0, ep=None, tp=None, pos_t=None, tp_decode=None):
+        if tp_decode is not None:
+            return self.moe(self.attn_tp_decode(x, cos, sin, cache, tp_decode), ep)
         if tp is not None:
             return self.moe(self.attn_tp(x, cos, sin, tp), ep)
         return self.moe(self.attn(x, cos, sin, cache, pos0, pos_t), ep)
@@ -316,7 +367,7 @@ class MoELLM(nn.Module):
 
     def forward(self, ids, positions=None, caches=None, pos0: int = 0, audio_feats=None, image_patches=None,
                 return_hidden: bool = False, targets: Optional[torch.Tensor] = None, temperature: float = 1.0,
-                pos_t: Optional[torch.Tensor] = None):
+                pos_t: Optional[torch.Tensor] = None, tp_decode=None):
         """Logits [B, S, V] (fp32); ``return_hidden``: the final hidden states; ``targets`` [B, S] (next-token
         ids per position): log p(target) [B, S] through the chunked vocabulary kernel, with no logits tensor
         (under tensor parallelism each rank scores its own tokens and the log-probs are gathered).
@@ -328,6 +379,16 @@ class MoELLM(nn.Module):
 
         cfg = self.cfg
         B, S = ids.shape
+        if tp_decode is not None:
+            # tensor-parallel rollout: heads split over the group, KV caches of this rank's heads only
+            if caches is None:
+                raise ValueError("tensor-parallel decode runs against KV caches")
+            x = self.embed_tokens(ids, audio_feats, image_patches) if pos0 == 0 else F.embedding(ids, self.embed)
+            cos, sin = self.rope(pos0, S, ids.device)
+            for i, blk in enumerate(self.layers):
+                x = blk(x, cos, sin, caches[i], pos0, self.ep, tp_decode=tp_decode)
+            h = rms_norm(x, self.norm, cfg.eps)
+            return h if return_hidden else self.lm_head(h).float()
         if pos_t is not None:
             if caches is None or S != 1 or self._rope_cache is None:
                 raise ValueError("device-position steps need caches, one token and a sized RoPE table")

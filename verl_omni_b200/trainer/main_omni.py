@@ -4,7 +4,8 @@ Counterpart of ``verl_omni/trainer/main_omni.py:57-360`` (Hydra config ``omni_tr
 ``trainer/config/omni_trainer.yaml`` with the same override syntax; one process per GPU under ``torchrun``
 instead of Ray workers.  ``actor_rollout_ref.actor.megatron.{tensor,expert,pipeline}_model_parallel_size`` set the
 TP (attention heads + sequence, consecutive ranks), EP (experts sharded, consecutive ranks) and PP (layer
-stages; stage s on ranks [s W / pp, (s + 1) W / pp)) sizes;
+stages; stage s on ranks [s W / pp, (s + 1) W / pp)) sizes, ``actor_rollout_ref.rollout.tensor_model_parallel_size``
+the rollout's (heads and KV caches split over groups of consecutive ranks);
 checkpoints use the diffusion trainers' layout (``global_step_{N}/actor`` + expert slices) and resume with
 ``trainer.resume_mode=auto``.
 """
@@ -56,6 +57,10 @@ def build_omni_trainer(config):
         if n < 1 or W % n:
             raise ValueError(f"{name}_model_parallel_size={n} must divide the world size {W}")
     tp_group = D.make_hsdp_groups(tp)[0] if tp > 1 else None
+    rtp = int(arc.rollout.tensor_model_parallel_size)
+    if rtp < 1 or W % rtp:
+        raise ValueError(f"rollout.tensor_model_parallel_size={rtp} must divide the world size {W}")
+    rollout_tp_group = D.make_hsdp_groups(rtp)[0] if rtp > 1 else None
     ep_group = D.make_hsdp_groups(ep)[0] if ep > 1 else None
     dp = W // tp // pp
     gbs = int(config.data.train_batch_size)
@@ -70,7 +75,7 @@ def build_omni_trainer(config):
         response_len=int(ro.response_length), loss_mode=str(act.policy_loss.loss_mode), ep_group=ep_group,
         tp_group=tp_group, seed=int(config.data.seed), micro_batch_size=int(act.ppo_micro_batch_size_per_gpu),
         temperature=float(ro.temperature), kv_block_size=int(ro.kv_block_size),
-        total_steps=int(config.trainer.total_training_steps), pp_size=pp)
+        total_steps=int(config.trainer.total_training_steps), pp_size=pp, rollout_tp_group=rollout_tp_group)
     trainer.prompts_per_rank = gbs // dp
     return trainer
 

@@ -33,7 +33,7 @@ class OmniGRPOTrainer:
                  prompt_text: int = 16, audio_tokens: int = 4, image_tokens: int = 4, response_len: int = 8,
                  loss_mode: str = "grpo", ep_group=None, tp_group=None, seed: int = 0,
                  micro_batch_size: Optional[int] = None, temperature: float = 1.0, kv_block_size: int = 0,
-                 total_steps: int = 1000, pp_size: int = 1):
+                 total_steps: int = 1000, pp_size: int = 1, rollout_tp_group=None):
         """``pp_size > 1``: pipeline parallelism over ``pp_size`` stages (rank r is stage r // (world / pp) of
         data-parallel rank r % (world / pp)); each stage holds a contiguous slice of the layers, the rollout
         decodes through the stages and the update runs the 1F1B schedule over the micro-batches."""
@@ -86,8 +86,17 @@ class OmniGRPOTrainer:
                                pp_group, device)
         self.engine = ShardedEngine(self.model, actor_cfg, device=device, total_steps=total_steps,
                                     expert_group=self.expert_dp_group, group=dp_group, pp_size=self.pp_size)
+        rtp = None
+        if rollout_tp_group is not None and D.world_size(rollout_tp_group) > 1:
+            from verl_omni_b200.parallel.tensor_parallel import TPContext
+
+            if self.pp is not None:
+                raise ValueError("a tensor-parallel rollout is not combined with pipeline stages")
+            rtp = self.model.tp if (self.model.tp is not None and self.model.tp.group is rollout_tp_group) \
+                else TPContext(rollout_tp_group)
         self.rollout = LLMRolloutEngine(self.model, max_new_tokens=response_len, device=device,
-                                        temperature=temperature, kv_block_size=kv_block_size, pp=self.pp)
+                                        temperature=temperature, kv_block_size=kv_block_size, pp=self.pp,
+                                        tp=rtp)
         self.temperature = temperature
         self.loss_fn = get_omni_loss_fn(loss_mode)
         self.loss_mode = loss_mode

@@ -100,12 +100,15 @@ class _DecodeStep:
 class LLMRolloutEngine:
     def __init__(self, module: MoELLM, *, max_new_tokens: int = 256, temperature: float = 1.0, top_k: int = 0,
                  top_p: float = 1.0, eos_id: Optional[int] = None, device=None, kv_block_size: int = 0,
-                 pp=None):
+                 pp=None, tp=None):
         """``pp``: a :class:`~verl_omni_b200.parallel.pipeline.PipeLink` when ``module`` is one pipeline stage
         (:class:`~verl_omni_b200.models.moe_llm.MoEStage`): every step's hidden states travel down the stages
         and the last stage's sampled tokens are broadcast back."""
         self.module = module
         self.pp = pp
+        # ``tp``: a TPContext -- tensor-parallel decode (vLLM's rollout tensor_model_parallel_size): the ranks of
+        # the group decode their prompts together, heads (and KV caches) split over the group
+        self.tp = tp if tp is not None and tp.world > 1 else None
         self.kv_block_size = kv_block_size  # > 0: paged KV cache with blocks of this many positions
         self.max_new_tokens = max_new_tokens
         self.temperature, self.top_k, self.top_p = temperature, top_k, top_p
@@ -116,12 +119,24 @@ class LLMRolloutEngine:
     def generate(self, batch: DataProto, seed: int = 0) -> DataProto:
         if self.pp is not None:
             return self._generate_pp(batch, seed)
+        tp = self.tp
         ids = batch.batch["input_ids"].to(self.device)
+        af, ip = batch.batch.get("audio_feats"), batch.batch.get("image_patches")
+        af = af.to(ids.device) if af is not None else None
+        ip = ip.to(ids.device) if ip is not None else None
+        B_own = ids.shape[0]
+        if tp is not None:
+            # the group's prompts in group-rank order; every rank decodes all of them (same seed on every rank,
+            # identical logits after the all-reduces, so the same draws) and keeps its own rows at the end
+            ids, af, ip = (self._gather(t, tp) if t is not None else None for t in (ids, af, ip))
         B, P = ids.shape
         dev = ids.device
         g = torch.Generator(device=dev).manual_seed(int(seed))  # sampling stays on the device
         cfg = self.module.cfg
-        if self.kv_block_size > 0:
+        if tp is not None:
+            caches = [KVCache(B, cfg.kv_heads // tp.world, P + self.max_new_tokens, cfg.head_dim, dev,
+                              self.module.embed.dtype) for _ in self.module.layers]
+        elif self.kv_block_size > 0:
             bs = self.kv_block_size
             per_seq = -(-(P + self.max_new_tokens) // bs)
             caches = []
@@ -133,15 +148,14 @@ class LLMRolloutEngine:
             caches = [KVCache(B, cfg.kv_heads, P + self.max_new_tokens, cfg.head_dim, dev, self.module.embed.dtype)
                       for _ in self.module.layers]
         # prefill: the vocabulary projection of the last prompt position only
-        af, ip = batch.batch.get("audio_feats"), batch.batch.get("image_patches")
-        h = self.module(ids, caches=caches, pos0=0, audio_feats=af.to(dev) if af is not None else None,
-                        image_patches=ip.to(dev) if ip is not None else None, return_hidden=True)
+        h = self.module(ids, caches=caches, pos0=0, audio_feats=af, image_patches=ip, return_hidden=True,
+                        **({"tp_decode": tp} if tp is not None else {}))
         logits = self.module.lm_head(h[:, -1:].contiguous()).float()[:, -1]
         out_ids, out_lp = [], []
         done = torch.zeros(B, dtype=torch.bool, device=ids.device)
         mask = []
         step = None
-        if self.max_new_tokens > 1 and _graph_ok(self.module, caches, dev):
+        if self.max_new_tokens > 1 and tp is None and _graph_ok(self.module, caches, dev):
             self.module.rope(0, P + self.max_new_tokens, dev)  # the table covers every decode position
             step = _DecodeStep(self.module, caches, B, dev)
         for t in range(self.max_new_tokens):
@@ -156,9 +170,25 @@ class LLMRolloutEngine:
             if t + 1 < self.max_new_tokens:
                 if step is not None:
                     logits = step(nxt, P + t)
+                elif tp is not None:
+                    logits = self.module(nxt[:, None], caches=caches, pos0=P + t, tp_decode=tp)[:, -1]
                 else:
                     logits = self.module(nxt[:, None], caches=caches, pos0=P + t)[:, -1]
-        return self._pack(batch, ids, out_ids, torch.stack(out_lp, 1), mask)
+        lp = torch.stack(out_lp, 1)
+        if tp is not None:
+            own = slice(tp.rank * B_own, (tp.rank + 1) * B_own)
+            ids, lp = ids[own], lp[own]
+            out_ids, mask = [t[own] for t in out_ids], [t[own] for t in mask]
+        return self._pack(batch, ids, out_ids, lp, mask)
+
+    @staticmethod
+    def _gather(t: torch.Tensor, tp) -> torch.Tensor:
+        from verl_omni_b200.parallel import dist as D
+
+        t = t.contiguous()
+        out = torch.empty((tp.world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        D.all_gather_into(out, t, tp.group)
+        return out
 
     @staticmethod
     def _pack(batch: DataProto, ids, out_ids, lp, mask) -> DataProto:
