@@ -283,6 +283,12 @@ class ShardedEngine:
         self.sched = LRSchedule(actor_cfg.optim, total_steps) if trainable else None
         self.last_grad_norm = None
         fc = actor_cfg.fsdp_config
+        if trainable and bool(getattr(fc, "reshard_after_forward", False)):
+            import warnings
+
+            warnings.warn("fsdp_config.reshard_after_forward=true: the bf16 weights stay whole on every rank (only "
+                          "the fp32 master, moments and gradient shards are sharded); use param_offload / "
+                          "optimizer_offload to reduce device memory")
         self.optimizer_offload = bool(getattr(fc, "optimizer_offload", False)) and device.type == "cuda"
         po = getattr(fc, "param_offload", False) if param_offload is None else param_offload
         self.param_offload = bool(po) and device.type == "cuda"
