@@ -268,6 +268,21 @@ def test_main_omni_ep2_checkpoint_resume(tmp_path):
     assert all(abs(v) < 1e6 for v in h2[0].values())
 
 
+def test_pipeline_with_expert_parallel_matches_ep_only(tmp_path):
+    """4 gloo ranks as 2 pipeline stages x EP=2 (experts sharded inside each stage, expert data-parallel groups
+    stage-local): the step equals the 2-rank EP=2 step without stages (losses, norm, every parameter of each
+    stage against the same expert shard)."""
+    run_ranks(_omni_pp_step, 2, (str(tmp_path), 1, 2))
+    run_ranks(_omni_pp_step, 4, (str(tmp_path), 2, 2))
+    for r in range(4):
+        ref = torch.load(tmp_path / f"pp1_ep2_r{r % 2}.pt")
+        part = torch.load(tmp_path / f"pp2_ep2_r{r}.pt")
+        for k, v in ref["m"].items():
+            assert abs(part["m"][k] - v) <= 1e-5 * max(1.0, abs(v)), (r, k, part["m"][k], v)
+        for n, p in part["params"].items():
+            torch.testing.assert_close(p, ref["params"][n], rtol=1e-4, atol=1e-6, msg=lambda s: f"{r} {n}: {s}")
+
+
 def test_main_omni_rollout_tp2(tmp_path):
     """The omni entry point with the rollout decoding tensor-parallel over both ranks: the rollout's log-probs
     agree with the trainer's (replicated-weight) recompute."""
@@ -348,7 +363,9 @@ def test_pipeline_1f1b_two_stages_match_single_rank():
     run_ranks(_pp_check, 2, ("",))
 
 
-def _omni_pp_step(rank, world, outdir, pp):
+def _omni_pp_step(rank, world, outdir, pp, ep=1):
+    import torch.distributed as dist
+
     from verl_omni_b200.models.moe_llm import MoEConfig
     from verl_omni_b200.trainer.omni.omni_trainer import OmniGRPOTrainer
     from verl_omni_b200.workers.config.diffusion import DiffusionActorConfig
@@ -357,14 +374,19 @@ def _omni_pp_step(rank, world, outdir, pp):
     ac.optim.lr = 1e-3
     cfg = MoEConfig.tiny()
     cfg.layers = 3
+    ep_group = None
+    if ep > 1:
+        from verl_omni_b200.parallel import dist as D
+
+        ep_group = D.make_hsdp_groups(ep)[0]
     t = OmniGRPOTrainer(cfg, ac, device=torch.device("cpu"), n=4, response_len=5, micro_batch_size=3,
-                        pp_size=pp)
+                        pp_size=pp, ep_group=ep_group)
     m = t.step(num_prompts=2)
     out = {"m": {k: m[k] for k in ("actor/pg_loss", "actor/grad_norm", "critic/rewards/mean",
                                    "rollout_corr/logprob_abs_diff_mean")},
            "params": {f"{n}" if pp == 1 else _full_name(n, t.model): p.detach().clone()
                       for n, p in t.model.named_parameters()}}
-    torch.save(out, f"{outdir}/pp{pp}_r{rank}.pt")
+    torch.save(out, f"{outdir}/pp{pp}_ep{ep}_r{rank}.pt")
 
 
 def _full_name(n, stage):
@@ -381,10 +403,10 @@ def test_pipeline_parallel_grpo_step_matches_single_rank(tmp_path):
     losses, norm and updated parameters."""
     run_ranks(_omni_pp_step, 1, (str(tmp_path), 1))
     run_ranks(_omni_pp_step, 2, (str(tmp_path), 2))
-    ref = torch.load(tmp_path / "pp1_r0.pt")
+    ref = torch.load(tmp_path / "pp1_ep1_r0.pt")
     seen = set()
     for r in range(2):
-        part = torch.load(tmp_path / f"pp2_r{r}.pt")
+        part = torch.load(tmp_path / f"pp2_ep1_r{r}.pt")
         for k, v in ref["m"].items():
             assert abs(part["m"][k] - v) <= 1e-5 * max(1.0, abs(v)), (k, part["m"][k], v)
         for n, p in part["params"].items():

@@ -116,6 +116,25 @@ def make_hsdp_groups(fsdp_size: int):
     return _HSDP_CACHE[fsdp_size]
 
 
+def make_partition_groups(rank_lists) -> object:
+    """The group of this rank among a partition of the world into ``rank_lists`` (every rank creates every
+    group in the same order, the collective contract of ``new_group``; cached per partition)."""
+    key = ("partition", tuple(tuple(int(x) for x in l) for l in rank_lists))
+    if key in _HSDP_CACHE:
+        return _HSDP_CACHE[key]
+    if _DEFAULT_GROUP is not None:
+        raise NotImplementedError("sub-groups inside a trainer that runs on a subset of the ranks")
+    r, mine = rank(), None
+    for l in key[1]:
+        g = dist.new_group(list(l))
+        if r in l:
+            mine = g
+    if mine is None:
+        raise ValueError(f"rank {r} is in no group of {key[1]}")
+    _HSDP_CACHE[key] = mine
+    return mine
+
+
 def barrier(group=None) -> None:
     group = _g(group)
     if dist.is_initialized():

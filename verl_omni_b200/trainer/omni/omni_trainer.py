@@ -39,9 +39,8 @@ class OmniGRPOTrainer:
         decodes through the stages and the update runs the 1F1B schedule over the micro-batches."""
         torch.manual_seed(seed)
         self.pp_size = int(pp_size)
-        if self.pp_size > 1 and ((ep_group is not None and D.world_size(ep_group) > 1)
-                                 or (tp_group is not None and D.world_size(tp_group) > 1)):
-            raise ValueError("pipeline parallelism is combined with data parallelism only (no EP / TP groups)")
+        if self.pp_size > 1 and tp_group is not None and D.world_size(tp_group) > 1:
+            raise ValueError("pipeline parallelism is combined with data and expert parallelism (no TP groups)")
         self.micro_batch_size = micro_batch_size  # sequences per forward/backward (None: the whole batch)
         self.cfg, self.actor_cfg, self.device, self.n = cfg, actor_cfg, device, n
         self.prompt_text, self.audio_tokens, self.image_tokens = prompt_text, audio_tokens, image_tokens
@@ -56,6 +55,16 @@ class OmniGRPOTrainer:
             # NCCL all-to-all otherwise.
             ep_size = D.world_size(ep_group)
             ep_group, self.expert_dp_group = D.make_hsdp_groups(ep_size)
+            if self.pp_size > 1:
+                # EP groups of consecutive ranks lie inside one stage (ep divides the ranks per stage); the
+                # ranks holding the same experts are those of the same EP position within the same stage
+                W = D.world_size()
+                dpn = W // self.pp_size
+                if dpn % ep_size:
+                    raise ValueError(f"expert_model_parallel_size={ep_size} must divide the {dpn} ranks per stage")
+                self.expert_dp_group = D.make_partition_groups(
+                    [[s * dpn + j + k * ep_size for k in range(dpn // ep_size)]
+                     for s in range(self.pp_size) for j in range(ep_size)])
             ep = FusedExpertParallel(cfg.experts, ep_group)
         with torch.device(device):
             self.model = MoELLM(cfg, ep)

@@ -396,10 +396,10 @@ class ShardedEngine:
         ef = self.eflat
         if ef is not None:
             # an expert's gradient already sums the contributions of every rank of its EP group (the exchange
-            # backward); summing over the ranks holding the same experts and dividing by the world size gives
-            # the same data-parallel mean as the dense parameters
+            # backward); summing over the ranks holding the same experts and dividing by the data-parallel size
+            # (the world, or the ranks of one pipeline stage) gives the same mean as the dense parameters
             D.reduce_scatter_into(ef.grad_shard, ef.main_grad, ef.group)
-            ef.grad_shard.mul_(1.0 / D.world_size())
+            ef.grad_shard.mul_(1.0 / (D.world_size() // self.pp_size))
             flats.append(ef)
         self.opt_step += 1
         lr = self.sched.lr()
