@@ -67,6 +67,14 @@ def test_adapters_registered():
     assert DiffusionModelBase.get("QwenImage", "dpo") is a
     e = DiffusionModelBase.get("QwenImageEdit", "flow_grpo")
     assert "image_latents" in e.cond_keys()
+    # the reference's pipeline-class keys select the same adapters
+    assert DiffusionModelBase.get("QwenImagePipeline", "flow_grpo") is a
+    assert DiffusionModelBase.get("QwenImageEditPlusPipeline", "flow_grpo") is e
+    for cls_name, algo in (("StableDiffusion3Pipeline", "flow_grpo"), ("StableDiffusion3Pipeline", "dpo"),
+                           ("WanPipeline", "dance_grpo"), ("LTX2Pipeline", "flow_grpo"),
+                           ("MiniMaxH3Pipeline", "diffusion_nft"), ("OmniBagelForConditionalGeneration", "flow_grpo"),
+                           ("QwenImagePipeline", "mix_grpo"), ("QwenImagePipeline", "diffusion_nft")):
+        assert DiffusionModelBase.get(cls_name, algo) is not None
     m = QwenImageDiT(QwenImageConfig.tiny()).eval()
     lat, t, emb = _inputs()
     cond = {"prompt_embeds": emb, "prompt_embeds_mask": torch.ones(2, 12)}

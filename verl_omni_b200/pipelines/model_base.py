@@ -24,6 +24,21 @@ from verl_omni_b200.pipelines.schedulers.flow_match_sde import FlowMatchSDEDiscr
 
 _REGISTRY: dict[tuple[str, str], type] = {}
 
+# the reference keys its adapters by the diffusers / transformers pipeline class (``model_index.json``
+# ``_class_name``); those names select the same adapters here (reference ``pipelines/*/__init__.py``
+# registrations: ``("StableDiffusion3Pipeline", "flow_grpo")`` and so on)
+PIPELINE_CLASS_ALIASES = {
+    "StableDiffusion3Pipeline": "SD3MMDiT",
+    "FluxPipeline": "FluxDiT",
+    "QwenImagePipeline": "QwenImage",
+    "QwenImageEditPlusPipeline": "QwenImageEdit",
+    "QwenImageEditPipeline": "QwenImageEdit",
+    "WanPipeline": "WanDiT",
+    "LTX2Pipeline": "LTX2",
+    "MiniMaxH3Pipeline": "MiniMaxH3",
+    "OmniBagelForConditionalGeneration": "Bagel",
+}
+
 
 class DiffusionModelBase:
     """Adapter base; subclasses are stateless (classmethods), selected by (architecture, algorithm)."""
@@ -44,6 +59,7 @@ class DiffusionModelBase:
 
     @classmethod
     def get(cls, arch: str, algorithm: str) -> type:
+        arch = PIPELINE_CLASS_ALIASES.get(arch, arch)
         if (arch, algorithm) in _REGISTRY:
             return _REGISTRY[(arch, algorithm)]
         if (arch, "flow_grpo") in _REGISTRY and algorithm in ("dance_grpo", "mix_grpo", "flow_dppo", "grpo_guard",
