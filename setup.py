@@ -26,6 +26,11 @@ nvcc_flags = [
 ]
 if os.environ.get("VO_PTXAS_VERBOSE"):
     nvcc_flags.append("-Xptxas=-v")
+cxx_flags = ["-O3", "-std=c++17"]
+if os.environ.get("VO_DEVICE_CHECKS", "0") == "1":
+    # device-side bounds / range checks that record the failing line and skip the access (debug builds)
+    nvcc_flags.append("-DVO_DEVICE_CHECKS")
+    cxx_flags.append("-DVO_DEVICE_CHECKS")
 
 setup(
     name="verl_omni_b200",
@@ -36,7 +41,7 @@ setup(
             name="verl_omni_b200._C",
             sources=sources,
             include_dirs=[os.path.join(ROOT, CSRC)],
-            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": nvcc_flags},
+            extra_compile_args={"cxx": cxx_flags, "nvcc": nvcc_flags},
             libraries=["cuda"],
         )
     ],

@@ -2,9 +2,34 @@
 #include <torch/extension.h>
 
 #include <atomic>
+#include <string>
+#include <utility>
 #include <vector>
 
 namespace vo {
+using DcheckReader = unsigned long long (*)(bool reset);
+static std::vector<std::pair<std::string, DcheckReader>>& dcheck_table() {
+  static std::vector<std::pair<std::string, DcheckReader>> t;
+  return t;
+}
+void dcheck_register(const char* file, DcheckReader fn) { dcheck_table().emplace_back(file, fn); }
+
+// {"enabled": built with VO_DEVICE_CHECKS, "sites": {source file: first failing line}} (cleared with reset)
+py::dict device_check_status(bool reset) {
+  py::dict out, sites;
+#ifdef VO_DEVICE_CHECKS
+  out["enabled"] = true;
+#else
+  out["enabled"] = false;
+#endif
+  for (auto& e : dcheck_table()) {
+    const unsigned long long v = e.second(reset);
+    if (v) sites[py::str(e.first)] = (int64_t)v;
+  }
+  out["sites"] = sites;
+  return out;
+}
+
 static std::atomic<int64_t> g_launches{0};
 void count_launch(int64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 int64_t launch_count() { return g_launches.load(); }
@@ -124,6 +149,8 @@ std::vector<torch::Tensor> fmha_bwd(torch::Tensor q, torch::Tensor k, torch::Ten
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "verl_omni_b200 sm_100a kernels";
   m.def("launch_count", &vo::launch_count);
+  m.def("device_check_status", &vo::device_check_status, py::arg("reset") = false,
+        "first failing VO_DCHECK site per source file (builds with VO_DEVICE_CHECKS=1)");
   m.def("count_launches", &vo::count_launch, "adds n to the launch counter (replayed CUDA graphs of counted kernels)");
   m.def("sde_step_fwd", &vo::sde_step_fwd, py::arg("x"), py::arg("v"), py::arg("sigma"), py::arg("sigma_prev"),
         py::arg("prev"), py::arg("noise"), py::arg("sigma_max"), py::arg("eta"), py::arg("type"), py::arg("seed"),

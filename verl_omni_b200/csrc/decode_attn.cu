@@ -87,7 +87,9 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
   const int b = bk / Hk, kh = bk % Hk;
   // lengths beyond the cache (or beyond the block table's reach) are clamped, so a bad length never reads
   // past the cache
-  const int L = max(0, min(lens[b], pt.table ? pt.stride * pt.block : Lmax));
+  const int cap = pt.table ? pt.stride * pt.block : Lmax;
+  VO_DCHECK(lens[b] >= 0 && lens[b] <= cap);  // checked builds record a clamped length
+  const int L = max(0, min(lens[b], cap));
   const int per = (L + splits - 1) / splits;
   const int s0 = split * per, s1 = min(L, s0 + per);
   const int tid = threadIdx.x;
@@ -122,7 +124,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
         off = kvbase + (int64_t)t * HD;
         if (pt.table) {
           const int blk = __ldg(pt.table + (int64_t)b * pt.stride + t / pt.block);
-          ok = blk >= 0 && blk < pt.nblocks;  // out-of-pool block ids read as zeros
+          ok = VO_DCHECK(blk >= 0 && blk < pt.nblocks);  // out-of-pool block ids read as zeros
           off = ok ? (((int64_t)blk * Hk + kh) * pt.block + t % pt.block) * HD : 0;
         }
       }

@@ -22,6 +22,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "dcheck.cuh"
+
 namespace vo_dec {
 
 constexpr int TK = 128;        // keys per tile (MMA M of S^T, K of O^T)
@@ -166,7 +168,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int bk = blockIdx.x, split = blockIdx.y;
   const int b = bk / p.Hk, kh = bk % p.Hk;
-  const int L = max(0, min(p.lens[b], p.table ? p.stride * p.block : p.Lmax));
+  const int cap = p.table ? p.stride * p.block : p.Lmax;
+  VO_DCHECK(p.lens[b] >= 0 && p.lens[b] <= cap);  // checked builds record a clamped length
+  const int L = max(0, min(p.lens[b], cap));
   // splits cover whole 128-key tiles: every tile starts on a block boundary of a paged cache
   const int per = ((L + p.splits - 1) / p.splits + TK - 1) / TK * TK;
   const int s0 = min(L, split * per), s1 = min(L, s0 + per);
@@ -254,7 +258,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
       } else {
         const bool has = id != -2;                           // block holds keys of this split
-        const bool in_pool = has && id >= 0 && id < p.nblocks;  // out-of-pool ids read as zero keys and values
+        const bool in_pool = has && VO_DCHECK(id >= 0 && id < p.nblocks);  // out-of-pool ids read as zeros
         const unsigned load_mask = __ballot_sync(0xffffffffu, in_pool);
         const unsigned zero_mask = __ballot_sync(0xffffffffu, has && !in_pool);
         if (lane == 0) {

@@ -28,7 +28,7 @@ __global__ void peer_row_copy_kernel(const __nv_bfloat16* __restrict__ src, cons
   for (int64_t i = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < n; i += warps) {
     const int64_t si = src_idx[i], di = dst_row[i];
     const int dr = dst_rank[i];
-    if (si < 0 || si >= src_rows || dr < 0 || dr >= npeers || di < 0 || di >= dst_rows) {
+    if (!VO_DCHECK(si >= 0 && si < src_rows && dr >= 0 && dr < npeers && di >= 0 && di < dst_rows)) {
       if (lane == 0 && err) atomicAdd(err, 1);
       continue;
     }
