@@ -244,7 +244,7 @@ def _main_omni(rank, world, ckpt, steps, par="actor_rollout_ref.actor.megatron.e
         "actor_rollout_ref.rollout.n=4", "actor_rollout_ref.rollout.response_length=6",
         "data.prompt_text_tokens=5", "data.prompt_audio_tokens=3", "data.prompt_image_tokens=3",
         "actor_rollout_ref.actor.ppo_micro_batch_size_per_gpu=3",
-        par, f"trainer.total_training_steps={steps}",
+        *((par,) if isinstance(par, str) else tuple(par)), f"trainer.total_training_steps={steps}",
         "trainer.save_freq=1", f"trainer.default_local_dir={ckpt}", "trainer.logger=[]"])
     hist = run_omni(cfg)
     if rank == 0:
@@ -292,6 +292,28 @@ def test_main_omni_rollout_tp2(tmp_path):
     h1 = json.load(open(tmp_path / "hist_1.json"))
     assert len(h1) == 1 and all(abs(v) < 1e6 for v in h1[0].values())
     assert h1[0]["rollout_corr/logprob_abs_diff_mean"] < 1e-4
+
+
+def test_main_omni_ep2_hf_export_loads_into_unsharded_thinker(tmp_path):
+    """save_contents with hf_model: the EP ranks write disjoint safetensors files (dense tensors once, each
+    rank its experts) in the hub layout; together they load strictly into an unsharded thinker and equal the
+    trained ranks' weights."""
+    from verl_omni_b200.models.hf_omni_io import load_thinker
+
+    run_ranks(_main_omni, 2, (str(tmp_path), 1, ("actor_rollout_ref.actor.megatron.expert_model_parallel_size=2",
+                                                 "actor_rollout_ref.actor.checkpoint.save_contents=[model,optimizer,extra,hf_model]")))
+    hf_dir = tmp_path / "global_step_1" / "actor" / "huggingface"
+    files = sorted(p.name for p in hf_dir.glob("*.safetensors"))
+    assert len(files) == 2, files
+    m = MoELLM(MoEConfig.tiny())
+    n = load_thinker(m, str(hf_dir))
+    assert n == len([k for k, _ in m.named_parameters() if not k.startswith(("audio_tower.", "visual."))])
+    from safetensors import safe_open
+
+    with safe_open(str(hf_dir / files[1]), framework="pt") as h:  # rank 1: experts 4..7 of every layer
+        assert "thinker.model.layers.0.mlp.experts.7.down_proj.weight" in h.keys()
+        torch.testing.assert_close(h.get_tensor("thinker.model.layers.0.mlp.experts.7.down_proj.weight").float(),
+                                   m.layers[0].w_down[7].float())
 
 
 def test_main_omni_pp2_checkpoint_resume(tmp_path):

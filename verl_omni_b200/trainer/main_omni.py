@@ -75,7 +75,8 @@ def build_omni_trainer(config):
         response_len=int(ro.response_length), loss_mode=str(act.policy_loss.loss_mode), ep_group=ep_group,
         tp_group=tp_group, seed=int(config.data.seed), micro_batch_size=int(act.ppo_micro_batch_size_per_gpu),
         temperature=float(ro.temperature), kv_block_size=int(ro.kv_block_size),
-        total_steps=int(config.trainer.total_training_steps), pp_size=pp, rollout_tp_group=rollout_tp_group)
+        total_steps=int(config.trainer.total_training_steps), pp_size=pp, rollout_tp_group=rollout_tp_group,
+        model_path=arc.model.get("path", None))
     trainer.prompts_per_rank = gbs // dp
     return trainer
 

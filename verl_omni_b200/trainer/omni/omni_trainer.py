@@ -33,7 +33,7 @@ class OmniGRPOTrainer:
                  prompt_text: int = 16, audio_tokens: int = 4, image_tokens: int = 4, response_len: int = 8,
                  loss_mode: str = "grpo", ep_group=None, tp_group=None, seed: int = 0,
                  micro_batch_size: Optional[int] = None, temperature: float = 1.0, kv_block_size: int = 0,
-                 total_steps: int = 1000, pp_size: int = 1, rollout_tp_group=None):
+                 total_steps: int = 1000, pp_size: int = 1, rollout_tp_group=None, model_path: Optional[str] = None):
         """``pp_size > 1``: pipeline parallelism over ``pp_size`` stages (rank r is stage r // (world / pp) of
         data-parallel rank r % (world / pp)); each stage holds a contiguous slice of the layers, the rollout
         decodes through the stages and the update runs the 1F1B schedule over the micro-batches."""
@@ -68,6 +68,12 @@ class OmniGRPOTrainer:
             ep = FusedExpertParallel(cfg.experts, ep_group)
         with torch.device(device):
             self.model = MoELLM(cfg, ep)
+        if model_path:
+            # HF checkpoint of the thinker (hub or fused expert layout): the language model's weights; each EP
+            # rank reads its own experts (the towers keep their initialisation)
+            from verl_omni_b200.models.hf_omni_io import load_thinker
+
+            load_thinker(self.model, model_path)
         # tensor + sequence parallelism (Megatron layout): ranks of a TP group share their samples and split each
         # sequence and the attention heads; weights stay replicated, so every rank's gradient is its share and
         # the loss is scaled by tp for the world-averaged gradient (groups of consecutive ranks)
@@ -295,13 +301,44 @@ class OmniGRPOTrainer:
         import os
 
         root = os.path.join(root_dir, f"global_step_{self.step_count}")
-        self.engine.save_checkpoint(self._actor_dir(root), self.step_count)
+        contents = tuple(self.actor_cfg.checkpoint.save_contents)
+        self.engine.save_checkpoint(self._actor_dir(root), self.step_count,
+                                    tuple(c for c in contents if c != "hf_model"))
+        if "hf_model" in contents:
+            self.export_hf(os.path.join(root, "actor", "huggingface"))
         if D.rank() == 0:
             torch.save({"global_step": self.step_count}, os.path.join(root, "data.pt"))
             with open(os.path.join(root_dir, "latest_checkpointed_iteration.txt"), "w") as f:
                 f.write(str(self.step_count))
         D.barrier()
         return root
+
+    def export_hf(self, directory: str) -> None:
+        """The thinker's language model in the HF hub layout (bf16 safetensors, ``thinker.`` names, one tensor
+        per expert).  Ranks write disjoint files: the first rank of each pipeline stage its dense tensors,
+        the first rank of each expert data-parallel group its experts; together they form one checkpoint."""
+        import os
+
+        from safetensors.torch import save_file
+
+        from verl_omni_b200.models.hf_omni_io import thinker_to_hf
+
+        os.makedirs(directory, exist_ok=True)
+        stage = self.pp.s if self.pp is not None else 0
+        off = self.model.lo if self.pp is not None else 0
+        first_of_stage = D.rank() % self.dp == 0 if self.pp is not None else D.rank() == 0
+        first_expert_holder = self.expert_dp_group is None and first_of_stage or (
+            self.expert_dp_group is not None and D.rank(self.expert_dp_group) == 0)
+        named = {}
+        for n, p in self.model.named_parameters():
+            is_expert = n.endswith(("w_gate_up", "w_down"))
+            if (first_expert_holder if is_expert else first_of_stage):
+                named[n] = p
+        state = {k: v.detach().to(torch.bfloat16).cpu().contiguous()
+                 for k, v in thinker_to_hf(named, self.model, off).items()}
+        if state:
+            save_file(state, os.path.join(directory, f"model-stage{stage:02d}-rank{D.rank():05d}.safetensors"))
+        D.barrier()
 
     def _actor_dir(self, root: str) -> str:
         """``actor`` (``actor/pp_rank_{s:02d}`` per stage under pipeline parallelism: each stage's shards)."""

@@ -471,6 +471,7 @@ class ShardedEngine:
 
     def _save_checkpoint(self, local_path: str, global_step: int, save_contents, hf_export: bool) -> None:
         os.makedirs(local_path, exist_ok=True)
+        hf_export = hf_export or "hf_model" in save_contents  # verl's checkpoint-contents name for the HF export
         W, r = self.world, self.rank
         fp = self.flat
         # HSDP: every replica holds the same shards; replica 0 writes them
