@@ -448,3 +448,31 @@ def test_llm_row_ops_match_fp32():
     out.backward(go.bfloat16())
     ref.backward(go)
     assert rel(proj.grad, pr2.grad) < 2e-2 and rel(wn.grad, wr2.grad) < 2e-2
+
+
+@pytest.mark.parametrize("Dh,H,S", [(64, 3, 45), (128, 5, 33), (256, 2, 19)])
+def test_head_norm_rope_vector_kernel_widths(Dh, H, S):
+    """The vectorised per-head RMSNorm + RoPE (16-byte lanes, rotate-half partner one shuffle away) at each
+    head width, with a head count that leaves the last CTA partly empty; and RMSNorm on the warp-per-row widths
+    and the CTA-per-row fallback."""
+    from verl_omni_b200.models.layers import rope_table
+    from verl_omni_b200.ops import llm
+
+    torch.manual_seed(1)
+    rel = lambda a, b: float((a.float() - b.float()).norm() / (b.float().norm() + 1e-12))  # noqa: E731
+    B = 3
+    proj = torch.randn(B, S, (H + 3) * Dh, device="cuda").bfloat16()
+    wn = (1 + 0.1 * torch.randn(Dh, device="cuda")).bfloat16()
+    cos, sin = (t.cuda() for t in rope_table(torch.arange(S) + 5, Dh, 1e6))
+    with torch.no_grad():
+        out = llm.head_norm_rope(proj, 2 * Dh, H, wn, cos, sin)
+    ref = llm.head_norm_rope_reference(proj.float()[..., 2 * Dh:(2 + H) * Dh].reshape(B, S, H, Dh), wn.float(), cos,
+                                       sin, 1e-6)
+    assert out.shape == (B, H, S, Dh) and rel(out, ref) < 1e-2
+    for D in (1024, 1536, 2048, 1000):
+        x = torch.randn(37, D, device="cuda").bfloat16()
+        w = (1 + 0.1 * torch.randn(D, device="cuda")).bfloat16()
+        with torch.no_grad():
+            y = llm.rms_norm(x, w, 1e-6)
+        yr = x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+        assert rel(y, yr) < 1e-2, D

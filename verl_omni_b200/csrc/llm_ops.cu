@@ -34,6 +34,42 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const bf16x8* __restri
   }
 }
 
+// Warp-per-row variant for D = 256 * NV (NV in 4, 6, 8): the row stays in registers as packed bf16 vectors (NV per
+// lane), read from memory once and unpacked per pass; eight rows per 256-thread CTA keep many rows' loads in
+// flight (the CTA-per-row form above waits on a block-wide reduction between its two passes).
+template <int NV>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_warp_kernel(const bf16x8* __restrict__ x,
+                                                               const bf16x8* __restrict__ w, bf16x8* __restrict__ y,
+                                                               float* __restrict__ rstd, int64_t rows, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const bf16x8* xr = x + row * (NV * 32);
+  bf16x8 raw[NV];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) raw[v] = xr[v * 32 + lane];
+  float ss = 0.f;
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    float f[8];
+    unpack8(raw[v], f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
+  }
+  const float r = rsqrtf(warp_sum(ss) * (1.f / (NV * 256)) + eps);
+  if (lane == 0) rstd[row] = r;
+  bf16x8* yr = y + row * (NV * 32);
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    float f[8], g[8];
+    unpack8(raw[v], f);
+    unpack8(w[v * 32 + lane], g);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = f[j] * r * g[j];
+    yr[v * 32 + lane] = pack8(f);
+  }
+}
+
 // dx = rstd * (w dy - x rstd^2 mean(x w dy)); dw partials per CTA row-chunk: dw[c] = sum_rows dy x rstd
 __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const bf16x8* __restrict__ dy, const bf16x8* __restrict__ x,
                                                           const bf16x8* __restrict__ w, const float* __restrict__ rstd,
@@ -234,6 +270,55 @@ __global__ void head_rmsnorm_rope_kernel(const __nv_bfloat16* __restrict__ x, in
   }
 }
 
+// Vectorised form for Dh in {64, 128, 256}: a head's Dh elements are Dh / 8 16-byte vectors held by LPH = Dh / 8
+// consecutive lanes (32 / LPH heads per warp).  Lanes [0, LPH/2) of a head hold the first half (d < Dh/2), lanes
+// [LPH/2, LPH) the second; the rotate-half partner of lane p is lane p ^ (LPH/2), one shuffle away.  Requires
+// 16-byte aligned rows (ld, the column offset and the base a multiple of 8 elements).
+template <int DH>
+__global__ void __launch_bounds__(256) head_rmsnorm_rope_vec_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld,
+                                                                    const __nv_bfloat16* __restrict__ w,
+                                                                    const float* __restrict__ cos_t,
+                                                                    const float* __restrict__ sin_t,
+                                                                    __nv_bfloat16* __restrict__ y, int B, int S, int H,
+                                                                    float eps) {
+  constexpr int LPH = DH / 8, HALF = DH / 2, PART = LPH / 2;
+  const int lane = threadIdx.x & 31;
+  const int p = lane % LPH;  // vector index within the head
+  const int64_t item = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * (32 / LPH) + lane / LPH;
+  const bool live = item < (int64_t)B * S * H;
+  const int64_t it = live ? item : 0;
+  const int h = (int)(it % H);
+  const int64_t bs = it / H;
+  const int s = (int)(bs % S);
+  const int b = (int)(bs / S);
+  float f[8];
+  unpack8(*reinterpret_cast<const bf16x8*>(x + bs * ld + (int64_t)h * DH + p * 8), f);
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
+#pragma unroll
+  for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);  // within the head's lanes
+  const float r = rsqrtf(ss * (1.f / DH) + eps);
+  float g[8];
+  unpack8(reinterpret_cast<const bf16x8*>(w)[p], g);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) f[j] *= r * g[j];
+  float o2[8];  // the partner's normalised values: x2 for a first-half lane, x1 for a second-half lane
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o2[j] = __shfl_xor_sync(0xffffffffu, f[j], PART);
+  const bool first = p < PART;
+  const int d0 = (first ? p : p - PART) * 8;  // index into the half-width tables
+  const float4* cp = reinterpret_cast<const float4*>(cos_t + (int64_t)s * HALF + d0);
+  const float4* sp = reinterpret_cast<const float4*>(sin_t + (int64_t)s * HALF + d0);
+  const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
+  const float co[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  const float si[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+  float out[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) out[j] = first ? f[j] * co[j] - o2[j] * si[j] : o2[j] * si[j] + f[j] * co[j];
+  if (live) *reinterpret_cast<bf16x8*>(y + (((int64_t)b * H + h) * S + s) * DH + p * 8) = pack8(out);
+}
+
 // backward of the above: dy [B, H, S, Dh] -> dx [B, S, H, Dh] (contiguous), dw partial sums per item block
 __global__ void head_rmsnorm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
                                              int64_t ld, const __nv_bfloat16* __restrict__ w,
@@ -308,9 +393,21 @@ std::vector<torch::Tensor> rms_norm_fwd(torch::Tensor x, torch::Tensor w, double
   auto y = torch::empty_like(x);
   auto rstd = torch::empty({rows}, x.options().dtype(torch::kFloat32));
   if (rows == 0) return {y, rstd};
-  rmsnorm_fwd_kernel<<<(unsigned)rows, 256, 0, stream()>>>(
-      reinterpret_cast<const bf16x8*>(x.data_ptr<at::BFloat16>()), reinterpret_cast<const bf16x8*>(w.data_ptr<at::BFloat16>()),
-      reinterpret_cast<bf16x8*>(y.data_ptr<at::BFloat16>()), rstd.data_ptr<float>(), (int)(D / 8), (float)eps);
+  const auto* xp = reinterpret_cast<const bf16x8*>(x.data_ptr<at::BFloat16>());
+  const auto* wp = reinterpret_cast<const bf16x8*>(w.data_ptr<at::BFloat16>());
+  auto* yp = reinterpret_cast<bf16x8*>(y.data_ptr<at::BFloat16>());
+  const unsigned wgrid = (unsigned)((rows + 7) / 8);
+  switch (D) {  // warp per row for the model zoo's widths; a CTA per row otherwise
+#define VO_RMS_WARP(NV) \
+  case NV * 256:        \
+    rmsnorm_fwd_warp_kernel<NV><<<wgrid, 256, 0, stream()>>>(xp, wp, yp, rstd.data_ptr<float>(), rows, (float)eps); \
+    break;
+    VO_RMS_WARP(4) VO_RMS_WARP(6) VO_RMS_WARP(8)
+#undef VO_RMS_WARP
+    default:
+      rmsnorm_fwd_kernel<<<(unsigned)rows, 256, 0, stream()>>>(xp, wp, yp, rstd.data_ptr<float>(), (int)(D / 8),
+                                                               (float)eps);
+  }
   count_launch();
   VO_CUDA_OK(cudaGetLastError());
   return {y, rstd};
@@ -426,11 +523,28 @@ torch::Tensor head_rmsnorm_rope(torch::Tensor x, int64_t col0, int64_t H, torch:
   auto y = torch::empty({B, H, S, Dh}, x.options());
   const int64_t items = B * S * H;
   if (items == 0) return y;
-  head_rmsnorm_rope_kernel<<<(unsigned)((items + 7) / 8), 256, 0, stream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr<at::BFloat16>()) + col0, x.stride(1),
-      reinterpret_cast<const __nv_bfloat16*>(w.data_ptr<at::BFloat16>()), cos_t.data_ptr<float>(),
-      sin_t.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(y.data_ptr<at::BFloat16>()), (int)B, (int)S, (int)H,
-      (int)Dh, (float)eps);
+  const auto* xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr<at::BFloat16>()) + col0;
+  const auto* wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr<at::BFloat16>());
+  auto* yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr<at::BFloat16>());
+  const bool vec = (Dh == 64 || Dh == 128 || Dh == 256) && x.stride(1) % 8 == 0 &&
+                   reinterpret_cast<uintptr_t>(xp) % 16 == 0 && reinterpret_cast<uintptr_t>(wp) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(cos_t.data_ptr<float>()) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(sin_t.data_ptr<float>()) % 16 == 0;
+  if (vec) {
+    const int64_t heads_per_cta = 8 * (32 / (Dh / 8));
+    const unsigned grid = (unsigned)((items + heads_per_cta - 1) / heads_per_cta);
+#define VO_HNR(DH)                                                                                                  \
+  if (Dh == DH)                                                                                                      \
+    head_rmsnorm_rope_vec_kernel<DH><<<grid, 256, 0, stream()>>>(xp, x.stride(1), wp, cos_t.data_ptr<float>(),       \
+                                                                 sin_t.data_ptr<float>(), yp, (int)B, (int)S, (int)H, \
+                                                                 (float)eps);
+    VO_HNR(64) VO_HNR(128) VO_HNR(256)
+#undef VO_HNR
+  } else {
+    head_rmsnorm_rope_kernel<<<(unsigned)((items + 7) / 8), 256, 0, stream()>>>(
+        xp, x.stride(1), wp, cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), yp, (int)B, (int)S, (int)H, (int)Dh,
+        (float)eps);
+  }
   count_launch();
   VO_CUDA_OK(cudaGetLastError());
   return y;

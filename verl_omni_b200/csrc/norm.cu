@@ -23,10 +23,10 @@ struct ModPtr {
 };
 
 // Register-resident variant: one warp per row, the row's D = 256 * NV bf16 values stay in registers
-// (NV 16-byte vectors per lane), so x is read from memory once; mean and variance are two passes
-// over registers.
+// (NV 16-byte vectors per lane, packed), so x is read from memory once; mean and variance are two passes
+// over registers; at D = 1536 at most 64 registers, so four 256-thread CTAs fit on an SM.
 template <int NV>
-__global__ void __launch_bounds__(256) adaln_ln_fwd_reg_kernel(const __nv_bfloat16* __restrict__ x,
+__global__ void __launch_bounds__(256, (NV <= 6 ? 4 : 1)) adaln_ln_fwd_reg_kernel(const __nv_bfloat16* __restrict__ x,
                                                                __nv_bfloat16* __restrict__ y,
                                                                float* __restrict__ mean_out,
                                                                float* __restrict__ rstd_out, ModPtr mod,
@@ -38,23 +38,31 @@ __global__ void __launch_bounds__(256) adaln_ln_fwd_reg_kernel(const __nv_bfloat
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
   const bf16x8* xr = reinterpret_cast<const bf16x8*>(x + row * D);
-  float f[NV][8];
+  // the row stays packed (4 registers per 8 values) and is unpacked in each pass: fewer registers, more
+  // rows resident per SM, more loads in flight
+  bf16x8 raw[NV];
 #pragma unroll
-  for (int v = 0; v < NV; ++v) unpack8(xr[v * 32 + lane], f[v]);
+  for (int v = 0; v < NV; ++v) raw[v] = xr[v * 32 + lane];
   float s = 0.f;
 #pragma unroll
-  for (int v = 0; v < NV; ++v)
+  for (int v = 0; v < NV; ++v) {
+    float t[8];
+    unpack8(raw[v], t);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) s += f[v][j];
+    for (int j = 0; j < 8; ++j) s += t[j];
+  }
   const float mu = warp_sum(s) * (1.f / D);
   float ss = 0.f;
 #pragma unroll
-  for (int v = 0; v < NV; ++v)
+  for (int v = 0; v < NV; ++v) {
+    float t[8];
+    unpack8(raw[v], t);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float d = f[v][j] - mu;
+      const float d = t[j] - mu;
       ss += d * d;
     }
+  }
   const float rstd = rsqrtf(warp_sum(ss) * (1.f / D) + eps);
   if (lane == 0) {
     mean_out[row] = mu;
@@ -65,17 +73,18 @@ __global__ void __launch_bounds__(256) adaln_ln_fwd_reg_kernel(const __nv_bfloat
 #pragma unroll
   for (int v = 0; v < NV; ++v) {
     const int i = v * 32 + lane;
-    float a[8], c[8], o[8];
+    float a[8], c[8], o[8], fv[8];
+    unpack8(raw[v], fv);
     if (aff_w) {
       unpack8(reinterpret_cast<const bf16x8*>(aff_w)[i], a);
       unpack8(reinterpret_cast<const bf16x8*>(aff_b)[i], c);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = (f[v][j] - mu) * rstd * a[j] + c[j];
+      for (int j = 0; j < 8; ++j) o[j] = (fv[j] - mu) * rstd * a[j] + c[j];
     } else {
       unpack8(reinterpret_cast<const bf16x8*>(mod.scale + b * mod.stride)[i], a);
       unpack8(reinterpret_cast<const bf16x8*>(mod.shift + b * mod.stride)[i], c);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = (f[v][j] - mu) * rstd * (1.f + a[j]) + c[j];
+      for (int j = 0; j < 8; ++j) o[j] = (fv[j] - mu) * rstd * (1.f + a[j]) + c[j];
     }
     yr[i] = pack8(o);
   }

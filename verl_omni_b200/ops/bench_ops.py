@@ -509,6 +509,62 @@ def bench_rollout_decode(a) -> list[dict]:
     return out
 
 
+def bench_rowops(a) -> list[dict]:
+    """The memory-bound kernels of a training step, each on inputs larger than L2 (126 MB), bytes counted as
+    the algorithmic reads + writes: AdaLN LayerNorm forward (D 1536), fused q/k RMSNorm + RoPE + QKV split
+    (joint-attention buffers, head_dim 64), flow-matching SDE step with log-prob, RMSNorm (D 2048), SwiGLU,
+    per-head RMSNorm + RoPE of the thinker, sharded AdamW over a flat fp32 buffer.  ``--iters 1`` for one
+    launch of each (ncu captures)."""
+    from verl_omni_b200.ops import llm as LO
+    from verl_omni_b200.ops._ext import ext
+    from verl_omni_b200.ops.norm import qk_norm_split_into
+    from verl_omni_b200.ops.sde import sde_step
+
+    out = []
+    dev = "cuda"
+
+    def add(op, nbytes, fn, **kw):
+        with torch.no_grad():
+            ms = timeit(fn, a.iters, warmup=0 if a.iters == 1 else 3)  # --iters 1: one launch (ncu)
+        out.append({"op": op, **kw, "ms": round(ms, 4), "gbs": round(nbytes / ms / 1e6, 1)})
+
+    rows, D = 65536, 1536
+    x = torch.randn(rows // 16, 16, D, device=dev).bfloat16().view(16, rows // 16, D)
+    mod = torch.randn(16, 6 * D, device=dev).bfloat16()
+    add("adaln_ln_fwd", 2 * 2 * x.numel(), lambda: ext().adaln_ln_fwd(x, mod, 0, D, None, None, rows // 16, 1e-6),
+        rows=rows, D=D)
+    B, S, H, Dh = 16, 2048, 24, 64
+    x2d = torch.randn(B * S, 3 * H * Dh, device=dev).bfloat16()
+    q, k, v = (torch.empty(B, H, S, Dh, device=dev, dtype=torch.bfloat16) for _ in range(3))
+    wq, wk = torch.ones(Dh, device=dev).bfloat16(), torch.ones(Dh, device=dev).bfloat16()
+    cos, sin = torch.rand(S, Dh // 2, device=dev), torch.rand(S, Dh // 2, device=dev)
+    add("qk_rmsnorm_rope_split", 2 * 2 * x2d.numel(),
+        lambda: qk_norm_split_into(q, k, v, x2d, wq, wk, S, 0, rope=(cos, sin)), rows=B * S, heads=H, hd=Dh)
+    lat = torch.randn(512, 16, 64, 64, device=dev)
+    vel = torch.randn_like(lat)
+    sig = torch.full((512,), 0.6, device=dev)
+    add("sde_step_logprob", 4 * 4 * lat.numel(),
+        lambda: sde_step(lat, vel, sig, sig - 0.1, sigma_max=0.95, noise_level=0.7, seed=1), B=512)
+    xr = torch.randn(65536, 2048, device=dev).bfloat16()
+    w = torch.ones(2048, device=dev).bfloat16()
+    add("rms_norm_fwd", 2 * 2 * xr.numel(), lambda: LO.rms_norm(xr, w, 1e-6), rows=65536, D=2048)
+    gu = torch.randn(65536, 2 * 768, device=dev).bfloat16()
+    add("swiglu_fwd", 2 * gu.numel() + gu.numel(), lambda: LO.swiglu(gu), rows=65536, F=768)
+    y = torch.randn(32, 2048, (32 + 4) * 128, device=dev).bfloat16()
+    wh = torch.ones(128, device=dev).bfloat16()
+    c2, s2 = torch.rand(2048, 64, device=dev), torch.rand(2048, 64, device=dev)
+    add("head_rmsnorm_rope", 2 * 2 * 32 * 2048 * 32 * 128, lambda: LO.head_norm_rope(y, 0, 32, wh, c2, s2, 1e-6),
+        B=32, S=2048, heads=32, hd=128)
+    n = 64 << 20
+    p32, g32, m32, v32 = (torch.randn(n, device=dev) for _ in range(4))
+    v32.abs_()
+    p16 = torch.empty(n, device=dev, dtype=torch.bfloat16)
+    sq = torch.ones(1, device=dev)
+    add("adamw_flat", n * (4 * 4 + 3 * 4 + 2),
+        lambda: ext().adamw_flat(p32, g32, m32, v32, p16, 1e-6, 0.9, 0.999, 1e-8, 0.0, 1, 1.0, sq, 1.0), numel=n)
+    return out
+
+
 def bench_groupnorm(a) -> list[dict]:
     """VAE-decoder GroupNorm(32)+SiLU on channels-last [8, 128, 512, 512] bf16 (one read + one write pass
     after the statistics pass)."""
@@ -526,7 +582,7 @@ def bench_groupnorm(a) -> list[dict]:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "gemm_sweep", "gemm_pair", "ulysses", "tp", "fmha", "sde", "adaln", "optstep", "moe", "groupnorm", "decode", "rollout_decode"])
+    ap.add_argument("op", choices=["gemm", "gemm_sweep", "gemm_pair", "ulysses", "tp", "fmha", "sde", "adaln", "optstep", "moe", "groupnorm", "decode", "rollout_decode", "rowops"])
     ap.add_argument("--numel", type=int, default=2_240_000_000)
     ap.add_argument("--M", type=int, default=21712)
     ap.add_argument("--N", type=int, default=6144)
@@ -542,7 +598,7 @@ def main() -> None:
     ap.add_argument("--new", type=int, default=64)
     a = ap.parse_args()
     pk = _peaks()
-    rows = {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "gemm_pair": bench_gemm_pair, "ulysses": bench_ulysses, "tp": bench_tp, "fmha": bench_fmha, "optstep": bench_optstep, "sde": bench_sde, "adaln": bench_adaln, "moe": bench_moe, "groupnorm": bench_groupnorm, "decode": bench_decode, "rollout_decode": bench_rollout_decode}[a.op](a)
+    rows = {"gemm": bench_gemm, "gemm_sweep": bench_gemm_sweep, "gemm_pair": bench_gemm_pair, "ulysses": bench_ulysses, "tp": bench_tp, "fmha": bench_fmha, "optstep": bench_optstep, "sde": bench_sde, "adaln": bench_adaln, "moe": bench_moe, "groupnorm": bench_groupnorm, "decode": bench_decode, "rollout_decode": bench_rollout_decode, "rowops": bench_rowops}[a.op](a)
     for r in rows:
         if "tflops" in r:
             r[f"frac_of_{pk['src']}_gemm_peak"] = round(r["tflops"] / pk["tflops"], 3)
