@@ -461,14 +461,17 @@ def test_head_norm_rope_vector_kernel_widths(Dh, H, S):
     torch.manual_seed(1)
     rel = lambda a, b: float((a.float() - b.float()).norm() / (b.float().norm() + 1e-12))  # noqa: E731
     B = 3
-    proj = torch.randn(B, S, (H + 3) * Dh, device="cuda").bfloat16()
-    wn = (1 + 0.1 * torch.randn(Dh, device="cuda")).bfloat16()
+    proj = torch.randn(B, S, (H + 3) * Dh, device="cuda").bfloat16().requires_grad_(True)
+    wn = (1 + 0.1 * torch.randn(Dh, device="cuda")).bfloat16().requires_grad_(True)
     cos, sin = (t.cuda() for t in rope_table(torch.arange(S) + 5, Dh, 1e6))
-    with torch.no_grad():
-        out = llm.head_norm_rope(proj, 2 * Dh, H, wn, cos, sin)
-    ref = llm.head_norm_rope_reference(proj.float()[..., 2 * Dh:(2 + H) * Dh].reshape(B, S, H, Dh), wn.float(), cos,
-                                       sin, 1e-6)
+    out = llm.head_norm_rope(proj, 2 * Dh, H, wn, cos, sin)
+    pr, wr = proj.detach().float().requires_grad_(True), wn.detach().float().requires_grad_(True)
+    ref = llm.head_norm_rope_reference(pr[..., 2 * Dh:(2 + H) * Dh].reshape(B, S, H, Dh), wr, cos, sin, 1e-6)
     assert out.shape == (B, H, S, Dh) and rel(out, ref) < 1e-2
+    go = torch.randn_like(ref)
+    out.backward(go.bfloat16())
+    ref.backward(go)
+    assert rel(proj.grad, pr.grad) < 2e-2 and rel(wn.grad, wr.grad) < 2e-2
     for D in (1024, 1536, 2048, 1000):
         x = torch.randn(37, D, device="cuda").bfloat16()
         w = (1 + 0.1 * torch.randn(D, device="cuda")).bfloat16()

@@ -286,11 +286,12 @@ __global__ void __launch_bounds__(256) head_rmsnorm_rope_vec_kernel(const __nv_b
   const int p = lane % LPH;  // vector index within the head
   const int64_t item = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * (32 / LPH) + lane / LPH;
   const bool live = item < (int64_t)B * S * H;
-  const int64_t it = live ? item : 0;
-  const int h = (int)(it % H);
-  const int64_t bs = it / H;
-  const int s = (int)(bs % S);
-  const int b = (int)(bs / S);
+  const uint32_t it = live ? (uint32_t)item : 0u;  // the host launches this form for B S H < 2^31 only
+  const int h = (int)(it % (uint32_t)H);
+  const uint32_t bs32 = it / (uint32_t)H;
+  const int s = (int)(bs32 % (uint32_t)S);
+  const int b = (int)(bs32 / (uint32_t)S);
+  const int64_t bs = bs32;
   float f[8];
   unpack8(*reinterpret_cast<const bf16x8*>(x + bs * ld + (int64_t)h * DH + p * 8), f);
   float ss = 0.f;
@@ -374,6 +375,104 @@ __global__ void head_rmsnorm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ d
       atomicAdd(dw + d, g1[k] * n1);
       atomicAdd(dw + d + half, g2[k] * n2);
     }
+  }
+}
+
+// Vectorised backward for Dh in {64, 128, 256} (same lane layout as the forward vector kernel): each warp walks
+// groups of 32 / LPH heads with a grid stride, un-rotates the gradient with the partner lane's values, and keeps
+// the weight-gradient partial sums of its 8 columns in registers; one atomic add per column per warp at the end
+// (the per-element form above adds B S H Dh times into Dh addresses).
+template <int DH>
+__global__ void __launch_bounds__(256) head_rmsnorm_rope_bwd_vec_kernel(
+    const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x, int64_t ld,
+    const __nv_bfloat16* __restrict__ w, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+    __nv_bfloat16* __restrict__ dx, float* __restrict__ dw, int B, int S, int H, float eps) {
+  constexpr int LPH = DH / 8, HALF = DH / 2, PART = LPH / 2, HPW = 32 / LPH;
+  const int lane = threadIdx.x & 31;
+  const int p = lane % LPH;
+  const bool first = p < PART;
+  const int d0 = (first ? p : p - PART) * 8;
+  const uint32_t items = (uint32_t)B * S * H;
+  const uint32_t groups = (items + HPW - 1) / HPW;
+  const uint32_t warps = gridDim.x * (blockDim.x >> 5);
+  float wv[8], acc[8];
+  unpack8(reinterpret_cast<const bf16x8*>(w)[p], wv);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  // one group ahead: the next group's x / dy vectors are loaded before this group's math, so two groups'
+  // loads are in flight per warp
+  auto locate = [&](uint32_t grp, bool& live, int& h, uint32_t& bs, int& s, int& b) {
+    const uint32_t item = grp * HPW + lane / LPH;
+    live = item < items;  // uniform per head: its lanes skip together, shuffles stay in their head
+    const uint32_t it = live ? item : 0u;
+    h = (int)(it % (uint32_t)H);
+    bs = it / (uint32_t)H;
+    s = (int)(bs % (uint32_t)S);
+    b = (int)(bs / (uint32_t)S);
+  };
+  uint32_t grp = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  bool nlive;
+  int nh, ns, nb;
+  uint32_t nbs;
+  bf16x8 xn, dn;
+  if (grp < groups) {
+    locate(grp, nlive, nh, nbs, ns, nb);
+    xn = *reinterpret_cast<const bf16x8*>(x + (int64_t)nbs * ld + (int64_t)nh * DH + p * 8);
+    dn = *reinterpret_cast<const bf16x8*>(dy + (((int64_t)nb * H + nh) * S + ns) * DH + p * 8);
+  }
+  for (; grp < groups; grp += warps) {
+    const bool live = nlive;
+    const int h = nh, s = ns;
+    const uint32_t bs = nbs;
+    float xv[8], gv[8], gp[8];
+    unpack8(xn, xv);
+    unpack8(dn, gv);
+    if (grp + warps < groups) {
+      locate(grp + warps, nlive, nh, nbs, ns, nb);
+      xn = *reinterpret_cast<const bf16x8*>(x + (int64_t)nbs * ld + (int64_t)nh * DH + p * 8);
+      dn = *reinterpret_cast<const bf16x8*>(dy + (((int64_t)nb * H + nh) * S + ns) * DH + p * 8);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) gp[j] = __shfl_xor_sync(0xffffffffu, gv[j], PART);
+    const float4* cp = reinterpret_cast<const float4*>(cos_t + (int64_t)s * HALF + d0);
+    const float4* sp = reinterpret_cast<const float4*>(sin_t + (int64_t)s * HALF + d0);
+    const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
+    const float co[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float si[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      // gradient w.r.t. the normalised, scaled value of this lane's element (rotation undone):
+      // first half  g1 = d1 cos + d2 sin;  second half g2 = -d1 sin + d2 cos
+      gv[j] = first ? gv[j] * co[j] + gp[j] * si[j] : -gp[j] * si[j] + gv[j] * co[j];
+      ss += xv[j] * xv[j];
+    }
+#pragma unroll
+    for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float r = rsqrtf(ss * (1.f / DH) + eps);
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dot += gv[j] * wv[j] * xv[j] * r;
+#pragma unroll
+    for (int o = LPH / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    dot *= 1.f / DH;
+    float out[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float n = xv[j] * r;
+      out[j] = r * (gv[j] * wv[j] - n * dot);
+      if (live) acc[j] += gv[j] * n;
+    }
+    if (live) *reinterpret_cast<bf16x8*>(dx + ((int64_t)bs * H + h) * DH + p * 8) = pack8(out);
+  }
+  // lanes holding the same columns (one per head of the warp) combine, then one lane adds them
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int o = LPH; o < 32; o <<= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+  if (lane < LPH) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) atomicAdd(dw + p * 8 + j, acc[j]);
   }
 }
 
@@ -526,7 +625,7 @@ torch::Tensor head_rmsnorm_rope(torch::Tensor x, int64_t col0, int64_t H, torch:
   const auto* xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr<at::BFloat16>()) + col0;
   const auto* wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr<at::BFloat16>());
   auto* yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr<at::BFloat16>());
-  const bool vec = (Dh == 64 || Dh == 128 || Dh == 256) && x.stride(1) % 8 == 0 &&
+  const bool vec = (Dh == 64 || Dh == 128 || Dh == 256) && items < (int64_t(1) << 31) && x.stride(1) % 8 == 0 &&
                    reinterpret_cast<uintptr_t>(xp) % 16 == 0 && reinterpret_cast<uintptr_t>(wp) % 16 == 0 &&
                    reinterpret_cast<uintptr_t>(cos_t.data_ptr<float>()) % 16 == 0 &&
                    reinterpret_cast<uintptr_t>(sin_t.data_ptr<float>()) % 16 == 0;
@@ -563,6 +662,32 @@ torch::Tensor head_rmsnorm_rope_bwd(torch::Tensor dy, torch::Tensor x, int64_t c
   auto dx = torch::empty({B, S, H, Dh}, x.options());
   const int64_t items = B * S * H;
   if (items == 0) return dx;
+  {
+    const auto* xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr<at::BFloat16>()) + col0;
+    const bool vec = (Dh == 64 || Dh == 128 || Dh == 256) && items < (int64_t(1) << 31) && x.stride(1) % 8 == 0 &&
+                     dy.is_contiguous() && reinterpret_cast<uintptr_t>(xp) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(dy.data_ptr()) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(cos_t.data_ptr<float>()) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(sin_t.data_ptr<float>()) % 16 == 0;
+    if (vec) {
+      const int64_t groups = (items + 32 / (Dh / 8) - 1) / (32 / (Dh / 8));
+      const unsigned grid = (unsigned)std::min<int64_t>((groups + 7) / 8, 8LL * num_sms());
+      const auto* dyp = reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr<at::BFloat16>());
+      const auto* wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr<at::BFloat16>());
+      auto* dxp = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr<at::BFloat16>());
+#define VO_HNRB(DH)                                                                                                  \
+  if (Dh == DH)                                                                                                      \
+    head_rmsnorm_rope_bwd_vec_kernel<DH><<<grid, 256, 0, stream()>>>(dyp, xp, x.stride(1), wp, cos_t.data_ptr<float>(), \
+                                                                     sin_t.data_ptr<float>(), dxp, dw.data_ptr<float>(), \
+                                                                     (int)B, (int)S, (int)H, (float)eps);
+      VO_HNRB(64) VO_HNRB(128) VO_HNRB(256)
+#undef VO_HNRB
+      count_launch();
+      VO_CUDA_OK(cudaGetLastError());
+      return dx;
+    }
+  }
   head_rmsnorm_rope_bwd_kernel<<<(unsigned)((items + 7) / 8), 256, 0, stream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr<at::BFloat16>()),
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr<at::BFloat16>()) + col0, x.stride(1),

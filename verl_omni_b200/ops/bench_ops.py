@@ -513,7 +513,7 @@ def bench_rowops(a) -> list[dict]:
     """The memory-bound kernels of a training step, each on inputs larger than L2 (126 MB), bytes counted as
     the algorithmic reads + writes: AdaLN LayerNorm forward (D 1536), fused q/k RMSNorm + RoPE + QKV split
     (joint-attention buffers, head_dim 64), flow-matching SDE step with log-prob, RMSNorm (D 2048), SwiGLU,
-    per-head RMSNorm + RoPE of the thinker, sharded AdamW over a flat fp32 buffer.  ``--iters 1`` for one
+    per-head RMSNorm + RoPE of the thinker (forward and backward), sharded AdamW over a flat fp32 buffer.  ``--iters 1`` for one
     launch of each (ncu captures)."""
     from verl_omni_b200.ops import llm as LO
     from verl_omni_b200.ops._ext import ext
@@ -555,6 +555,10 @@ def bench_rowops(a) -> list[dict]:
     c2, s2 = torch.rand(2048, 64, device=dev), torch.rand(2048, 64, device=dev)
     add("head_rmsnorm_rope", 2 * 2 * 32 * 2048 * 32 * 128, lambda: LO.head_norm_rope(y, 0, 32, wh, c2, s2, 1e-6),
         B=32, S=2048, heads=32, hd=128)
+    dyh = torch.randn(32, 32, 2048, 128, device=dev).bfloat16()
+    dwh = torch.zeros(128, device=dev)
+    add("head_rmsnorm_rope_bwd", 3 * 2 * 32 * 2048 * 32 * 128,
+        lambda: ext().head_rmsnorm_rope_bwd(dyh, y, 0, 32, wh, c2, s2, 1e-6, dwh), B=32, S=2048, heads=32, hd=128)
     n = 64 << 20
     p32, g32, m32, v32 = (torch.randn(n, device=dev) for _ in range(4))
     v32.abs_()
