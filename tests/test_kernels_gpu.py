@@ -210,6 +210,13 @@ def test_adamw_matches_torch():
     bad = torch.tensor([float("inf")], device="cuda")
     ext().adamw_flat(p, g, m, v, p16, 1e-3, 0.9, 0.999, 1e-8, 0.01, 8, 1.0, bad, 1.0)
     assert torch.equal(p, before)
+    # views starting one element in (not 16-byte aligned): the scalar kernel takes the whole range
+    p3, m3, v3 = p2.clone(), m2.clone(), v2.clone()
+    p4, m4, v4 = p2.clone(), m2.clone(), v2.clone()
+    ext().adamw_flat(p3[1:], g[1:], m3[1:], v3[1:], p16[1:], 1e-3, 0.9, 0.999, 1e-8, 0.01, 9, 1.0, None, 1.0)
+    _adamw_torch(p4[1:], g[1:], m4[1:], v4[1:], 1e-3, 0.9, 0.999, 1e-8, 0.01, 9)
+    torch.testing.assert_close(p3, p4, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(v3, v4, rtol=1e-4, atol=1e-6)  # fused multiply-add vs addcmul_ rounding
 
 
 def test_tiny_mmdit_gpu_matches_cpu():

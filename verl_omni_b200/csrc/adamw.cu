@@ -60,6 +60,47 @@ __global__ void adamw_flat_kernel(float* __restrict__ p, const float* __restrict
   }
 }
 
+// Same update on 4-element vectors (16-byte loads / stores of p, g, m, v; 8-byte bf16 stores): identical
+// arithmetic per element, four times fewer memory instructions.  n4 = n / 4 vectors; the host runs the
+// scalar kernel on the tail and whenever a pointer is not 16-byte aligned.
+__global__ void __launch_bounds__(256) adamw_flat_vec_kernel(float4* __restrict__ p, const float4* __restrict__ g,
+                                                             float4* __restrict__ m, float4* __restrict__ v,
+                                                             uint2* __restrict__ p16, int64_t n4, float lr, float b1,
+                                                             float b2, float eps, float wd, float bc1, float bc2_sqrt,
+                                                             float max_norm, const float* __restrict__ sq_norm,
+                                                             float grad_scale) {
+  float coef = grad_scale;
+  if (sq_norm) {
+    const float norm = sqrtf(sq_norm[0]);
+    if (!isfinite(norm)) return;
+    if (max_norm > 0.f) coef *= fminf(1.f, max_norm / (norm + 1e-6f));
+  }
+  const float step = lr / bc1;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 g4 = g[i], p4 = p[i], m4 = m[i], v4 = v[i];
+    float gi[4] = {g4.x, g4.y, g4.z, g4.w}, pi[4] = {p4.x, p4.y, p4.z, p4.w};
+    float mi[4] = {m4.x, m4.y, m4.z, m4.w}, vi[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float gk = gi[k] * coef;
+      float pk = pi[k] * (1.f - lr * wd);
+      const float mk = b1 * mi[k] + (1.f - b1) * gk;
+      const float vk = b2 * vi[k] + (1.f - b2) * gk * gk;
+      pk -= step * mk / (sqrtf(vk) / bc2_sqrt + eps);
+      pi[k] = pk;
+      mi[k] = mk;
+      vi[k] = vk;
+    }
+    p[i] = make_float4(pi[0], pi[1], pi[2], pi[3]);
+    m[i] = make_float4(mi[0], mi[1], mi[2], mi[3]);
+    v[i] = make_float4(vi[0], vi[1], vi[2], vi[3]);
+    if (p16) {
+      __nv_bfloat162 lo = __floats2bfloat162_rn(pi[0], pi[1]), hi = __floats2bfloat162_rn(pi[2], pi[3]);
+      p16[i] = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+    }
+  }
+}
+
 }  // namespace
 
 // returns the [1] fp32 sum of squares of g (deterministic two-stage reduction)
@@ -94,11 +135,29 @@ void adamw_flat(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor
   }
   const float* sn = (sq_norm_t.has_value() && sq_norm_t->defined()) ? sq_norm_t->data_ptr<float>() : nullptr;
   const int64_t n = p.numel();
-  const int nb = (int)std::min<int64_t>((n + 255) / 256, 8LL * num_sms());
-  adamw_flat_kernel<<<nb, 256, 0, stream()>>>(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(),
-                                              v.data_ptr<float>(), p16p, n, (float)lr, (float)b1, (float)b2,
-                                              (float)eps, (float)wd, (float)bc1, (float)std::sqrt(bc2),
-                                              (float)max_norm, sn, (float)grad_scale); vo::count_launch();
+  auto a16 = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+  const bool vec = a16(p.data_ptr()) && a16(g.data_ptr()) && a16(m.data_ptr()) && a16(v.data_ptr()) &&
+                   (p16p == nullptr || reinterpret_cast<uintptr_t>(p16p) % 8 == 0);
+  const int64_t n4 = vec ? n / 4 : 0, head = n4 * 4;
+  if (n4 > 0) {
+    const int nb = (int)std::min<int64_t>((n4 + 255) / 256, 8LL * num_sms());
+    adamw_flat_vec_kernel<<<nb, 256, 0, stream()>>>(
+        reinterpret_cast<float4*>(p.data_ptr<float>()), reinterpret_cast<const float4*>(g.data_ptr<float>()),
+        reinterpret_cast<float4*>(m.data_ptr<float>()), reinterpret_cast<float4*>(v.data_ptr<float>()),
+        reinterpret_cast<uint2*>(p16p), n4, (float)lr, (float)b1, (float)b2, (float)eps, (float)wd, (float)bc1,
+        (float)std::sqrt(bc2), (float)max_norm, sn, (float)grad_scale);
+    vo::count_launch();
+  }
+  if (n > head) {  // tail (or everything, when not 16-byte aligned)
+    const int64_t rest = n - head;
+    const int nb = (int)std::min<int64_t>((rest + 255) / 256, 8LL * num_sms());
+    adamw_flat_kernel<<<nb, 256, 0, stream()>>>(p.data_ptr<float>() + head, g.data_ptr<float>() + head,
+                                                m.data_ptr<float>() + head, v.data_ptr<float>() + head,
+                                                p16p ? p16p + head : nullptr, rest, (float)lr, (float)b1, (float)b2,
+                                                (float)eps, (float)wd, (float)bc1, (float)std::sqrt(bc2),
+                                                (float)max_norm, sn, (float)grad_scale);
+    vo::count_launch();
+  }
   VO_CUDA_OK(cudaGetLastError());
 }
 

@@ -45,6 +45,8 @@ __global__ void __launch_bounds__(kThreads) bwd_prep_kernel(const __nv_bfloat16*
   float db[8], dg[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) db[i] = dg[i] = 0.f;
+  // unrolled so that several rows' loads are in flight per thread (the sums still run in row order)
+#pragma unroll 4
   for (int64_t r = r0; r < r1; ++r) {
     const int64_t off = r * N + col;
     float d[8];

@@ -34,15 +34,32 @@ __global__ void __launch_bounds__(256, (NV <= 6 ? 4 : 1)) adaln_ln_fwd_reg_kerne
                                                                const __nv_bfloat16* __restrict__ aff_b, int64_t rows,
                                                                int S, float eps) {
   constexpr int D = NV * 256;
+  // the modulation (scale, shift) of the CTA's first row's sample -- or the affine weight and bias -- staged
+  // once per CTA in shared memory while the rows' loads are in flight; rows of another sample (a CTA that
+  // straddles a sample boundary) read theirs from global memory
+  __shared__ bf16x8 sm_a[NV * 32], sm_c[NV * 32];
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const bf16x8* xr = reinterpret_cast<const bf16x8*>(x + row * D);
+  const bool active = row < rows;
+  const bf16x8* xr = reinterpret_cast<const bf16x8*>(x + (active ? row : 0) * D);
   // the row stays packed (4 registers per 8 values) and is unpacked in each pass: fewer registers, more
   // rows resident per SM, more loads in flight
   bf16x8 raw[NV];
 #pragma unroll
   for (int v = 0; v < NV; ++v) raw[v] = xr[v * 32 + lane];
+  const int64_t b0 = ((int64_t)blockIdx.x * (blockDim.x >> 5)) / S;
+  {
+    const bf16x8* sa = aff_w ? reinterpret_cast<const bf16x8*>(aff_w)
+                             : reinterpret_cast<const bf16x8*>(mod.scale + b0 * mod.stride);
+    const bf16x8* sc = aff_w ? reinterpret_cast<const bf16x8*>(aff_b)
+                             : reinterpret_cast<const bf16x8*>(mod.shift + b0 * mod.stride);
+    for (int i = threadIdx.x; i < NV * 32; i += blockDim.x) {
+      sm_a[i] = sa[i];
+      sm_c[i] = sc[i];
+    }
+  }
+  __syncthreads();
+  if (!active) return;
   float s = 0.f;
 #pragma unroll
   for (int v = 0; v < NV; ++v) {
@@ -75,14 +92,17 @@ __global__ void __launch_bounds__(256, (NV <= 6 ? 4 : 1)) adaln_ln_fwd_reg_kerne
     const int i = v * 32 + lane;
     float a[8], c[8], o[8], fv[8];
     unpack8(raw[v], fv);
-    if (aff_w) {
-      unpack8(reinterpret_cast<const bf16x8*>(aff_w)[i], a);
-      unpack8(reinterpret_cast<const bf16x8*>(aff_b)[i], c);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = (fv[j] - mu) * rstd * a[j] + c[j];
+    if (aff_w || b == b0) {
+      unpack8(sm_a[i], a);
+      unpack8(sm_c[i], c);
     } else {
       unpack8(reinterpret_cast<const bf16x8*>(mod.scale + b * mod.stride)[i], a);
       unpack8(reinterpret_cast<const bf16x8*>(mod.shift + b * mod.stride)[i], c);
+    }
+    if (aff_w) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = (fv[j] - mu) * rstd * a[j] + c[j];
+    } else {
 #pragma unroll
       for (int j = 0; j < 8; ++j) o[j] = (fv[j] - mu) * rstd * (1.f + a[j]) + c[j];
     }

@@ -513,7 +513,8 @@ def bench_rowops(a) -> list[dict]:
     """The memory-bound kernels of a training step, each on inputs larger than L2 (126 MB), bytes counted as
     the algorithmic reads + writes: AdaLN LayerNorm forward (D 1536), fused q/k RMSNorm + RoPE + QKV split
     (joint-attention buffers, head_dim 64), flow-matching SDE step with log-prob, RMSNorm (D 2048), SwiGLU,
-    per-head RMSNorm + RoPE of the thinker (forward and backward), sharded AdamW over a flat fp32 buffer.  ``--iters 1`` for one
+    per-head RMSNorm + RoPE of the thinker (forward and backward), the linear-backward prologue (GELU' scaling
+    + bias-gradient sums over 32768 x 6144), sharded AdamW over a flat fp32 buffer.  ``--iters 1`` for one
     launch of each (ncu captures)."""
     from verl_omni_b200.ops import llm as LO
     from verl_omni_b200.ops._ext import ext
@@ -559,6 +560,12 @@ def bench_rowops(a) -> list[dict]:
     dwh = torch.zeros(128, device=dev)
     add("head_rmsnorm_rope_bwd", 3 * 2 * 32 * 2048 * 32 * 128,
         lambda: ext().head_rmsnorm_rope_bwd(dyh, y, 0, 32, wh, c2, s2, 1e-6, dwh), B=32, S=2048, heads=32, hd=128)
+    dyl = torch.randn(32768, 6144, device=dev).bfloat16()
+    pre = torch.randn_like(dyl)
+    dbl = torch.zeros(6144, device=dev)
+    add("linear_bwd_prep_gelu", 3 * 2 * dyl.numel(),
+        lambda: ext().linear_bwd_prep(dyl, pre, None, 32768, 1, dbl, True), rows=32768, N=6144)
+    del dyl, pre
     n = 64 << 20
     p32, g32, m32, v32 = (torch.randn(n, device=dev) for _ in range(4))
     v32.abs_()
