@@ -441,10 +441,9 @@ class PolicyGradientTrainer:
         """``perf/mfu/*`` from the architecture's FLOPs formula and the phase timings."""
         from verl_omni_b200.utils.mfu import step_mfu_metrics
 
-        shape = self.spec.latent_shape
-        image_tokens = self.spec.sched_seq_len or int(np.prod(shape[1:])) // 4
-        pe = self.spec.cond_shapes.get("prompt_embeds")
-        text_tokens = int(pe[0]) if pe else int(self.spec.prompt_len if self.spec.text_encoder else 0)
+        from verl_omni_b200.utils.mfu import token_counts
+
+        image_tokens, text_tokens = token_counts(self.spec)
         gs = self.model_cfg.pipeline.guidance_scale
         cfg_passes = 2 if (gs is not None and gs > 1.0 and "negative_prompt_embeds" in out.batch) else 1
         bypass = self.algo_cfg.rollout_correction.bypass_mode or self.actor_cfg.rollout_correction.bypass_mode

@@ -200,6 +200,7 @@ class OmniGRPOTrainer:
         m.update(M.compute_timing_metrics_diffusion(timing, len(out)))
         m.update(M.compute_throughput_metrics_diffusion(time.perf_counter() - t0, len(out) * self.dp,
                                                          D.world_size()))
+        m.update(self._mfu(out, timing))
         return m
 
     # ------------------------------------------------------------------ pipeline parallel step
@@ -288,7 +289,15 @@ class OmniGRPOTrainer:
         m.update(M.compute_timing_metrics_diffusion(timing, len(out)))
         m.update(M.compute_throughput_metrics_diffusion(time.perf_counter() - t0, len(out) * self.dp,
                                                          D.world_size()))
+        m.update(self._mfu(out, timing))
         return m
+
+    def _mfu(self, out: DataProto, timing: dict) -> dict:
+        """``perf/mfu/*`` of the step: the language model's FLOPs over every data-parallel rank's sequences."""
+        from verl_omni_b200.utils.mfu import omni_step_mfu_metrics
+
+        return omni_step_mfu_metrics(self.cfg, batch=len(out) * self.dp, seq=int(out.batch["input_ids"].shape[1]),
+                                     timing=timing, n_gpus=D.world_size())
 
     def _sync(self) -> None:
         if self.device.type == "cuda":

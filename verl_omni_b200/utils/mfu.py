@@ -97,6 +97,49 @@ def qwen_image_forward_flops(module, image_tokens: int, text_tokens: int) -> flo
     return cfg.depth * (2 * (4 * D * D + 2 * D * mlp) * S + 4 * S * S * D)
 
 
+@register_flops("minimax_h3")
+def h3_forward_flops(module, image_tokens: int, text_tokens: int) -> float:
+    """Single stream over packed [text | audio | video] rows; the modulation linear runs once per sample."""
+    cfg = module.cfg
+    D = cfg.hidden
+    hid = int(D * cfg.mlp_ratio)
+    S = cfg.video_rows + cfg.audio_rows + text_tokens  # the packed rows are fixed by the model's layout
+    return cfg.depth * (2 * (4 * D * D + 2 * D * hid) * S + 4 * S * S * D) + 2 * cfg.text_dim * D * text_tokens
+
+
+@register_flops("ltx2")
+def ltx2_forward_flops(module, image_tokens: int, text_tokens: int) -> float:
+    """Video and audio streams per layer: self-attention, text cross-attention, cross-modal attention
+    (queries of one stream, keys / values projected from the other), MLP.  The video and audio token counts
+    are fixed by the model's latent layout."""
+    cfg = module.cfg
+    f, h, w = cfg.video_grid
+    nv, na = f * h * w, cfg.audio_tokens
+    T = text_tokens
+    Dv, Da = cfg.video_hidden, cfg.audio_hidden
+
+    def stream(D, N, Do, M):
+        hid = int(D * cfg.mlp_ratio)
+        lin = 2 * (4 * D * D + 2 * D * D + 2 * D * D + 2 * D * hid) * N  # qkv+o, text q+o, av q+o, mlp
+        lin += 2 * (2 * D * D) * T + 2 * (2 * Do * D) * M  # text k/v, cross-modal k/v
+        return lin + 4 * N * N * D + 4 * N * T * D + 4 * N * M * D
+
+    per_layer = stream(Dv, nv, Da, na) + stream(Da, na, Dv, nv)
+    return cfg.depth * per_layer + 2 * cfg.text_dim * (Dv + Da) * T
+
+
+@register_flops("bagel")
+def bagel_forward_flops(module, image_tokens: int, text_tokens: int) -> float:
+    """Mixture-of-Transformers: prompt tokens through the understanding weights (causal attention), latent
+    tokens through the generation weights attending to every token."""
+    cfg = module.cfg
+    D, hd = cfg.hidden, cfg.head_dim
+    per_tok = (D * (cfg.q_heads + 2 * cfg.kv_heads) * hd + cfg.q_heads * hd * D + 3 * D * cfg.ffn)
+    P, L = text_tokens, image_tokens
+    attn = 2 * P * P * cfg.q_heads * hd + 4 * L * (P + L) * cfg.q_heads * hd
+    return cfg.layers * (2 * per_tok * (P + L) + attn)
+
+
 def generic_forward_flops(module, image_tokens: int, text_tokens: int) -> float:
     """Fallback: every 2-D weight applied to every token, full attention over all tokens (upper bound for
     families without a formula of their own)."""
@@ -106,6 +149,46 @@ def generic_forward_flops(module, image_tokens: int, text_tokens: int) -> float:
     depth = getattr(cfg, "depth", 0) or getattr(cfg, "layers", 0) or 0
     hidden = getattr(cfg, "hidden", 0) or 0
     return dense + 4.0 * depth * S * S * hidden
+
+
+def moe_llm_forward_flops(cfg, batch: int, seq: int) -> float:
+    """Forward FLOPs of the MoE thinker's language model over ``batch`` sequences of ``seq`` tokens: the active
+    parameters per token (q / k / v / o projections, router, ``top_k`` SwiGLU experts, vocabulary head) twice
+    each, plus causal attention (half of 4 S^2 d per layer).  The audio / vision towers are not counted."""
+    D, hd = cfg.hidden, cfg.head_dim
+    attn_proj = D * (cfg.q_heads + 2 * cfg.kv_heads) * hd + cfg.q_heads * hd * D
+    per_token = cfg.layers * (attn_proj + D * cfg.experts + cfg.top_k * 3 * D * cfg.expert_ffn) + D * cfg.vocab
+    return 2.0 * per_token * batch * seq + cfg.layers * 2.0 * batch * seq * seq * cfg.q_heads * hd
+
+
+def omni_step_mfu_metrics(cfg, *, batch: int, seq: int, timing: dict, n_gpus: int) -> dict:
+    """``perf/mfu/{rollout,actor_infer,actor}`` of one omni GRPO step from its phase times: generation as one
+    forward over the full sequences (prefill + cached decode), the old-log-prob forward, and the update
+    (forward + backward = 3 forwards); ``batch`` counts the sequences of all ranks."""
+    f = moe_llm_forward_flops(cfg, batch, seq)
+    peak = device_peak_tflops() * 1e12 * max(1, n_gpus)
+    out = {}
+    for key, phase, mult in (("rollout", "gen", 1.0), ("actor_infer", "old_log_prob", 1.0),
+                             ("actor", "update_actor", 3.0)):
+        t = timing.get(phase)
+        if t:
+            out[f"perf/mfu/{key}"] = mult * f / (t * peak)
+    return out
+
+
+def token_counts(spec) -> tuple[int, int]:
+    """(image-side, text-side) tokens of one sample of an architecture: the scheduler's sequence length or the
+    2 x 2-patched latent, plus the reference-image latents of edit models; prompt embeddings, prompt ids or
+    the text encoder's prompt length."""
+    import numpy as np
+
+    image = spec.sched_seq_len or int(np.prod(spec.latent_shape[1:])) // 4
+    ref = spec.cond_shapes.get("image_latents")
+    if ref is not None:
+        image += int(np.prod(ref[1:])) // 4
+    pe = spec.cond_shapes.get("prompt_embeds") or spec.cond_shapes.get("prompt_ids")
+    text = int(pe[0]) if pe else int(spec.prompt_len if spec.text_encoder else 0)
+    return image, text
 
 
 class DiffusionFlopsCounter:
