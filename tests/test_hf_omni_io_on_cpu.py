@@ -97,3 +97,21 @@ def test_expert_parallel_rank_and_pipeline_stage_take_their_slices():
     gs = H.thinker_from_hf(sd, st, layer_offset=1)
     assert "embed" not in gs and "lm_head.weight" in gs
     torch.testing.assert_close(gs["layers.0.q_proj.weight"], full.layers[1].q_proj.weight)
+
+
+def test_omni_trainer_starts_from_hf_checkpoint(tmp_path):
+    """``OmniGRPOTrainer(model_path=...)`` (``actor_rollout_ref.model.path``) starts from the checkpoint's
+    language-model weights; a step runs from there."""
+    from safetensors.torch import save_file
+
+    from verl_omni_b200.trainer.omni.omni_trainer import OmniGRPOTrainer
+    from verl_omni_b200.workers.config.diffusion import DiffusionActorConfig
+
+    cfg = MoEConfig.tiny()
+    _, sd = _hf_state(cfg, seed=3)
+    save_file({k: v.contiguous() for k, v in sd.items()}, str(tmp_path / "model.safetensors"))
+    t = OmniGRPOTrainer(cfg, DiffusionActorConfig(), device=torch.device("cpu"), n=2, model_path=str(tmp_path))
+    torch.testing.assert_close(t.model.layers[1].router.weight, sd["thinker.model.layers.1.mlp.gate.weight"])
+    torch.testing.assert_close(t.model.embed, sd["thinker.model.embed_tokens.weight"])
+    m = t.step(num_prompts=1)
+    assert m["actor/grad_norm"] == m["actor/grad_norm"]
