@@ -486,3 +486,39 @@ def test_tensor_parallel_rollout_tp2_gloo():
     """Rollout decode with attention heads (and KV caches) split over a TP=2 group: greedy tokens and log-probs
     equal the replicated-weight decode of the same prompts."""
     run_ranks(_tp_rollout_check, 2)
+
+
+def _main_omni_parquet(rank, world, root):
+    from verl_omni_b200.trainer.main_omni import run_omni
+    from verl_omni_b200.utils.config import load_config
+
+    for name in ("with_feats", "text_only"):
+        cfg = load_config("omni_trainer", [
+            "trainer.device=cpu", "actor_rollout_ref.model.architecture=qwen3_omni_tiny", "data.train_batch_size=2",
+            "actor_rollout_ref.rollout.n=2", "actor_rollout_ref.rollout.response_length=4",
+            f"data.train_files={root}/{name}.parquet", "data.max_prompt_length=10", "trainer.total_training_steps=1",
+            "trainer.save_freq=0", f"trainer.default_local_dir={root}/ck_{name}", "trainer.logger=[]"])
+        hist = run_omni(cfg)
+        assert len(hist) == 1 and hist[0]["actor/grad_norm"] == hist[0]["actor/grad_norm"]
+
+
+def test_main_omni_reads_parquet_prompts(tmp_path):
+    """data.train_files: omni prompts from parquet (token ids with audio / image placeholders and their
+    feature arrays, or plain text), left-padded to max_prompt_length, through the entry point on 2 gloo ranks."""
+    import pandas as pd
+
+    from verl_omni_b200.utils.datasets_parquet import ParquetOmniRLDataset
+
+    cfg = MoEConfig.tiny()
+    rows = []
+    for i in range(5):
+        rows.append({"prompt_ids": [3 + i, 7, cfg.audio_token, cfg.audio_token, cfg.image_token],
+                     "audio_feats": torch.randn(2, cfg.audio_mel).tolist(),
+                     "image_patches": torch.randn(1, cfg.vision_patch_dim).tolist(), "data_source": "synthetic"})
+    pd.DataFrame(rows).to_parquet(tmp_path / "with_feats.parquet")
+    pd.DataFrame([{"prompt": f"describe sound number {i}"} for i in range(3)]).to_parquet(tmp_path / "text_only.parquet")
+    ds = ParquetOmniRLDataset(str(tmp_path / "with_feats.parquet"), vocab=cfg.vocab, max_prompt_length=8)
+    b = ds.get_batch([4, 5])  # index 5 wraps to row 0
+    assert b.batch["input_ids"].shape == (2, 8) and b.batch["audio_feats"].shape == (2, 2, cfg.audio_mel)
+    assert b.batch["input_ids"][0, :3].tolist() == [0, 0, 0] and b.batch["input_ids"][1, 3].item() == 3
+    run_ranks(_main_omni_parquet, 2, (str(tmp_path),))

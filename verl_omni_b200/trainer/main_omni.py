@@ -78,6 +78,13 @@ def build_omni_trainer(config):
         total_steps=int(config.trainer.total_training_steps), pp_size=pp, rollout_tp_group=rollout_tp_group,
         model_path=arc.model.get("path", None))
     trainer.prompts_per_rank = gbs // dp
+    files = config.data.get("train_files", None)
+    if files:
+        from verl_omni_b200.utils.datasets_parquet import ParquetOmniRLDataset
+
+        trainer.dataset = ParquetOmniRLDataset(files, vocab=mcfg.vocab,
+                                               max_prompt_length=int(config.data.get("max_prompt_length", 512)),
+                                               max_samples=int(config.data.get("train_max_samples", -1) or -1))
     return trainer
 
 

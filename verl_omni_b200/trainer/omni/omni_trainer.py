@@ -122,7 +122,13 @@ class OmniGRPOTrainer:
             self.dp = D.world_size() // self.pp_size
             self.dp_rank = self.rank % self.dp
 
+    dataset = None  # a ParquetOmniRLDataset: prompts come from it instead of the synthetic generator
+
     def make_prompts(self, num: int, seed: int) -> DataProto:
+        if self.dataset is not None:
+            # step s, data-parallel rank r: rows [((s - 1) dp + r) num, ... + num) of the dataset, cycling
+            start = ((self.step_count - 1) * self.dp + self.dp_rank) * num
+            return self.dataset.get_batch(list(range(start, start + num)), uid_prefix=f"{self.step_count}-")
         g = torch.Generator().manual_seed(seed)
         cfg = self.cfg
         text = torch.randint(0, cfg.vocab - 2, (num, self.prompt_text), generator=g)
@@ -139,10 +145,15 @@ class OmniGRPOTrainer:
         # the vocabulary projection and log-softmax run chunked inside the model (no [B, S, V] logits)
         tgt = torch.zeros_like(ids[:, :-1])
         tgt[:, P - 1:] = ids[:, P:]
-        lp = self.model(ids[:, :-1], audio_feats=data.batch["audio_feats"].to(self.device),
-                        image_patches=data.batch["image_patches"].to(self.device), targets=tgt,
+        af, ip = self._feats(data)
+        lp = self.model(ids[:, :-1], audio_feats=af, image_patches=ip, targets=tgt,
                         temperature=self.temperature)
         return lp[:, P - 1:]
+
+    def _feats(self, data: DataProto):
+        """The prompt's audio frames / image patches on the device (None when the batch has none)."""
+        return tuple(data.batch[k].to(self.device) if k in data.batch else None
+                     for k in ("audio_feats", "image_patches"))
 
     def _micro(self, data: DataProto) -> list[slice]:
         n = len(data)
@@ -212,7 +223,7 @@ class OmniGRPOTrainer:
         st = self.model
         ids = data.batch["input_ids"].to(self.device)
         P = data.batch["prompts"].shape[1]
-        af, ip = data.batch["audio_feats"].to(self.device), data.batch["image_patches"].to(self.device)
+        af, ip = self._feats(data)
         seq_level = self.loss_mode == "gspo"
 
         def fn(x, i):
@@ -223,7 +234,8 @@ class OmniGRPOTrainer:
                 tgt[:, P - 1:] = ids[sl, P:]
             if st.first:
                 x = ids[sl, :-1]
-            y = st(x, audio_feats=af[sl] if st.first else None, image_patches=ip[sl] if st.first else None,
+            y = st(x, audio_feats=af[sl] if (st.first and af is not None) else None,
+                   image_patches=ip[sl] if (st.first and ip is not None) else None,
                    targets=tgt, temperature=self.temperature)
             if not st.last:
                 return y
@@ -375,8 +387,8 @@ class OmniGRPOTrainer:
             P = d.batch["prompts"].shape[1]
             tgt = torch.zeros_like(ids[:, :-1])
             tgt[:, P - 1:] = ids[:, P:]
-            lp = model(ids[:, :-1], audio_feats=d.batch["audio_feats"].to(self.device),
-                       image_patches=d.batch["image_patches"].to(self.device), targets=tgt)[:, P - 1:]
+            af, ip = self._feats(d)
+            lp = model(ids[:, :-1], audio_feats=af, image_patches=ip, targets=tgt)[:, P - 1:]
             return sequence_logps(lp, d.batch["response_mask"].to(self.device))
 
         with torch.no_grad():

@@ -11,6 +11,9 @@
   prompt conditioning; rows come out interleaved ``[chosen, rejected, ...]`` with ``rm_scores`` win / lose.
 * :class:`ParquetMLLMDPODataset` -- offline omni DPO (reference ``utils/dataset/offline_mllm_dpo_dataset.py``):
   ``prompt_ids``, ``chosen_ids``, ``rejected_ids`` (+ optional ``audio_feats`` / ``image_patches``).
+* :class:`ParquetOmniRLDataset` -- online omni RL prompts (reference ``utils/dataset/omni_rl_datasets.py``):
+  ``prompt_ids`` (token ids holding the audio / image placeholder tokens) or ``prompt`` text, with optional
+  ``audio_feats`` / ``image_patches`` arrays, ``data_source`` and ``reward_model.ground_truth``.
 
 Tensor columns hold nested lists (any depth) or flat lists with a ``<col>_shape`` column.
 """
@@ -186,3 +189,48 @@ class ParquetMLLMDPODataset:
                     t[feat] = torch.stack([_tensor(r, feat) for r in rows])
             out.append(DataProto(t, {"uid": np.array([f"pair-{i}" for i in ids], dtype=object)}))
         return out[0], out[1]
+
+
+class ParquetOmniRLDataset:
+    """Prompts for the omni GRPO / GSPO trainer.  Each batch is left-padded to ``max_prompt_length`` with
+    ``pad_id`` (the thinker attends over the padding like any other prompt token, identically in the rollout
+    and the log-prob recompute); longer prompts keep their last ``max_prompt_length`` tokens.  Text prompts
+    without ids are tokenized byte-level.  Feature arrays are stacked per batch (equal counts per row)."""
+
+    def __init__(self, files, *, vocab: int, max_prompt_length: int, pad_id: int = 0, max_samples: int = -1,
+                 tokenizer: Optional[Callable[[str], list[int]]] = None):
+        self.df = _read(files)
+        if max_samples and max_samples > 0:
+            self.df = self.df.iloc[:max_samples]
+        if "prompt_ids" not in self.df.columns and "prompt" not in self.df.columns:
+            raise ValueError("omni RL parquet needs a 'prompt_ids' or a 'prompt' column")
+        self.L, self.pad = int(max_prompt_length), int(pad_id)
+        self.tok = tokenizer or (lambda text: [b % vocab for b in text.encode("utf-8")])
+
+    def __len__(self) -> int:
+        return len(self.df)
+
+    def get_batch(self, ids: list[int], uid_prefix: str = "") -> DataProto:
+        rows = [self.df.iloc[int(i) % len(self.df)].to_dict() for i in ids]
+        out = torch.full((len(rows), self.L), self.pad, dtype=torch.long)
+        for j, r in enumerate(rows):
+            toks = list(r["prompt_ids"]) if r.get("prompt_ids") is not None else self.tok(_prompt_text(r["prompt"]))
+            toks = [int(t) for t in toks][-self.L:]
+            out[j, self.L - len(toks):] = torch.tensor(toks, dtype=torch.long)
+        t = {"input_ids": out}
+        for feat in ("audio_feats", "image_patches"):
+            if feat in self.df.columns:
+                t[feat] = torch.stack([_tensor(r, feat) for r in rows])
+        gts = []
+        for r in rows:
+            rm = r.get("reward_model")
+            if isinstance(rm, str):
+                try:
+                    rm = json.loads(rm)
+                except ValueError:
+                    rm = None
+            gts.append(rm.get("ground_truth") if isinstance(rm, dict) else None)
+        nt = {"uid": np.array([f"{uid_prefix}{i}" for i in ids], dtype=object),
+              "data_source": np.array([r.get("data_source", "unknown") for r in rows], dtype=object),
+              "ground_truth": np.array(gts, dtype=object)}
+        return DataProto(t, nt)
