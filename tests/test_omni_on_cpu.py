@@ -522,3 +522,43 @@ def test_main_omni_reads_parquet_prompts(tmp_path):
     assert b.batch["input_ids"].shape == (2, 8) and b.batch["audio_feats"].shape == (2, 2, cfg.audio_mel)
     assert b.batch["input_ids"][0, :3].tolist() == [0, 0, 0] and b.batch["input_ids"][1, 3].item() == 3
     run_ranks(_main_omni_parquet, 2, (str(tmp_path),))
+
+
+def _main_omni_dpo(rank, world, root, steps):
+    import json
+
+    from verl_omni_b200.trainer.main_omni import run_omni
+    from verl_omni_b200.utils.config import load_config
+
+    cfg = load_config("omni_trainer", [
+        "trainer.device=cpu", "actor_rollout_ref.model.architecture=qwen3_omni_tiny", "data.train_batch_size=4",
+        "algorithm.trainer_type=direct_preference", "algorithm.dpo_beta=0.2", f"data.train_files={root}/pairs.parquet",
+        "actor_rollout_ref.actor.megatron.expert_model_parallel_size=2", "actor_rollout_ref.actor.optim.lr=1e-3",
+        f"trainer.total_training_steps={steps}", "trainer.save_freq=1", f"trainer.default_local_dir={root}/ck",
+        "trainer.logger=[]"])
+    hist = run_omni(cfg)
+    if rank == 0:
+        with open(f"{root}/dpo_{steps}.json", "w") as f:
+            json.dump(hist, f)
+
+
+def test_main_omni_offline_dpo_ep2_and_resume(tmp_path):
+    """algorithm.trainer_type=direct_preference: offline omni DPO from parquet pairs through the entry point on 2
+    gloo ranks with EP=2; the first step sits at log 2 (policy == frozen reference), a resumed run continues."""
+    import json
+
+    import pandas as pd
+
+    cfg = MoEConfig.tiny()
+    g = torch.Generator().manual_seed(0)
+    rows = [{"prompt_ids": torch.randint(0, 500, (6,), generator=g).tolist(),
+             "chosen_ids": torch.randint(0, 500, (4,), generator=g).tolist(),
+             "rejected_ids": torch.randint(0, 500, (3 + i % 2,), generator=g).tolist()} for i in range(8)]
+    pd.DataFrame(rows).to_parquet(tmp_path / "pairs.parquet")
+    run_ranks(_main_omni_dpo, 2, (str(tmp_path), 2))
+    h = json.load(open(tmp_path / "dpo_2.json"))
+    assert len(h) == 2 and abs(h[0]["dpo_loss"] - math.log(2)) < 1e-4
+    assert abs(h[1]["dpo_loss"] - math.log(2)) > 1e-6  # the first update moved the policy off the reference
+    run_ranks(_main_omni_dpo, 2, (str(tmp_path), 3))
+    h3 = json.load(open(tmp_path / "dpo_3.json"))
+    assert len(h3) == 1 and h3[0]["training/global_step"] == 3

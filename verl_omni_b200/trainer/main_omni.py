@@ -90,10 +90,12 @@ def build_omni_trainer(config):
 
 def run_omni(config) -> list[dict]:
     D.init_distributed(device=config.trainer.device, timeout_s=int(config.actor_rollout_ref.nccl_timeout))
-    if config.algorithm.trainer_type != "policy_gradient":
-        raise ValueError("main_omni runs the policy-gradient omni trainer (GRPO / GSPO); offline omni DPO goes "
-                         "through OmniGRPOTrainer.dpo_step")
+    if config.algorithm.trainer_type not in ("policy_gradient", "direct_preference"):
+        raise ValueError(f"unknown algorithm.trainer_type {config.algorithm.trainer_type!r}: policy_gradient "
+                         "(online GRPO / GSPO) or direct_preference (offline DPO on parquet pairs)")
     trainer = build_omni_trainer(config)
+    if config.algorithm.trainer_type == "direct_preference":
+        return _run_dpo(config, trainer)
     ckpt = str(config.trainer.default_local_dir)
     if config.trainer.resume_mode == "auto":
         trainer.load_checkpoint(ckpt)
@@ -103,6 +105,50 @@ def run_omni(config) -> list[dict]:
     hist = []
     while trainer.step_count < total:
         m = trainer.step(trainer.prompts_per_rank)
+        hist.append(m)
+        if log and D.rank() == 0:
+            print(json.dumps({k: (round(v, 6) if isinstance(v, float) else v) for k, v in m.items()}), flush=True)
+        if save_freq > 0 and (trainer.step_count % save_freq == 0 or trainer.step_count >= total):
+            trainer.save_checkpoint(ckpt)
+    return hist
+
+
+def _run_dpo(config, trainer) -> list[dict]:
+    """Offline omni DPO (reference ``OmniDirectPreferenceRayTrainer``, ``trainer/omni/ray_omni_trainer.py``):
+    (chosen, rejected) response pairs from ``data.train_files`` (``prompt_ids`` / ``chosen_ids`` /
+    ``rejected_ids``, optional prompt features) against a frozen reference copy of the initial policy;
+    ``algorithm.dpo_beta``; checkpoints and resume as in the online trainer."""
+    from verl_omni_b200.models.moe_llm import MoELLM
+    from verl_omni_b200.utils.datasets_parquet import ParquetMLLMDPODataset
+
+    files = config.data.get("train_files", None)
+    if not files:
+        raise ValueError("direct_preference needs data.train_files with prompt_ids / chosen_ids / rejected_ids")
+    if trainer.pp is not None:
+        raise ValueError("offline omni DPO runs without pipeline stages")
+    trainer.dataset = None
+    ds = ParquetMLLMDPODataset(files, max_samples=int(config.data.get("train_max_samples", -1) or -1))
+    # the reference: an independent frozen copy of the initial policy (the same expert shard per rank), taken
+    # before a resumed run loads its trained weights
+    with torch.device(trainer.device):
+        ref = MoELLM(trainer.cfg, trainer.model.ep)
+    ref.load_state_dict({k: v.detach() for k, v in trainer.model.state_dict().items()})
+    ref.to(next(trainer.model.parameters()).dtype).eval().requires_grad_(False)
+    ckpt = str(config.trainer.default_local_dir)
+    if config.trainer.resume_mode == "auto":
+        trainer.load_checkpoint(ckpt)
+    beta = float(config.algorithm.get("dpo_beta", 0.1))
+    bs = trainer.prompts_per_rank
+    save_freq, total = int(config.trainer.save_freq), int(config.trainer.total_training_steps)
+    log = "console" in list(config.trainer.logger)
+    hist = []
+    while trainer.step_count < total:
+        trainer.step_count += 1
+        start = ((trainer.step_count - 1) * trainer.dp + trainer.dp_rank) * bs
+        chosen, rejected = ds.get_pairs([(start + j) % len(ds) for j in range(bs)])
+        m = trainer.dpo_step(chosen, rejected, ref, beta=beta)
+        m.update({"training/global_step": trainer.step_count, "actor/lr": trainer.engine.lr(),
+                  "actor/grad_norm": float(trainer.engine.last_grad_norm.reshape(()))})
         hist.append(m)
         if log and D.rank() == 0:
             print(json.dumps({k: (round(v, 6) if isinstance(v, float) else v) for k, v in m.items()}), flush=True)
